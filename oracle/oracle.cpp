@@ -24,6 +24,7 @@
 #ifdef _OPENMP
 #include <omp.h>
 #endif
+#include <immintrin.h>
 
 namespace {
 
@@ -66,6 +67,28 @@ inline float h2f(uint16_t h) { return half_table().v[h]; }
 int g_threads = 1;
 
 // ------------------------------------------------------------ layers -----
+// fp32 dot product with 16 independent partial sums (a SIMD-friendly order, as
+// ncnn's vectorised InnerProduct/Gemm kernels use; fp32 summation order is not
+// specified by the reference).
+inline float dot(const float* a, const float* b, int n) {
+    float acc[16] = {0.f};
+    int k = 0;
+    for (; k + 16 <= n; k += 16)
+        for (int j = 0; j < 16; ++j) acc[j] += a[k + j] * b[k + j];
+    float s = 0.f;
+    for (int j = 0; j < 16; ++j) s += acc[j];
+    for (; k < n; ++k) s += a[k] * b[k];
+    return s;
+}
+
+// widen n fp16 values (F16C)
+inline void widen(const uint16_t* src, int n, float* dst) {
+    int k = 0;
+    for (; k + 8 <= n; k += 8)
+        _mm256_storeu_ps(dst + k, _mm256_cvtph_ps(_mm_loadu_si128(reinterpret_cast<const __m128i*>(src + k))));
+    for (; k < n; ++k) dst[k] = half_table().v[src[k]];
+}
+
 // y[m][n] = sum_k W[n][k] x[m][k] (+ b[n]); nn.Linear / ncnn InnerProduct/Gemm.
 void linear(const uint16_t* w, const uint16_t* b, int n_out, int k_in, const float* x, int m,
             float* y) {
@@ -75,15 +98,11 @@ void linear(const uint16_t* w, const uint16_t* b, int n_out, int k_in, const flo
         std::vector<float> row(static_cast<std::size_t>(k_in));
 #pragma omp for schedule(static)
         for (int n = 0; n < n_out; ++n) {
-            const uint16_t* wr = w + static_cast<std::size_t>(n) * k_in;
-            for (int k = 0; k < k_in; ++k) row[static_cast<std::size_t>(k)] = t.v[wr[k]];
+            widen(w + static_cast<std::size_t>(n) * k_in, k_in, row.data());
             const float bias = b ? t.v[b[n]] : 0.0f;
-            for (int i = 0; i < m; ++i) {
-                const float* xr = x + static_cast<std::size_t>(i) * k_in;
-                float s = 0.0f;
-                for (int k = 0; k < k_in; ++k) s += row[static_cast<std::size_t>(k)] * xr[k];
-                y[static_cast<std::size_t>(i) * n_out + n] = s + bias;
-            }
+            for (int i = 0; i < m; ++i)
+                y[static_cast<std::size_t>(i) * n_out + n] =
+                    dot(row.data(), x + static_cast<std::size_t>(i) * k_in, k_in) + bias;
         }
     }
 }
@@ -455,44 +474,50 @@ void decoder_forward(orc_model* m, int which, const float* embed, int n, const f
     m->tokens[which] = past + n;
 }
 
-// DiT decoder over one 11-token sequence (DitEstimator.decoder,
-// export_components.py:625-659): no mask, no cache, RoPE positions 0..10.
-void dit_decoder(const orc_model* m, float* hidden, int n, float* out) {
+// DiT decoder over the CFG sequences (DitEstimator.decoder,
+// export_components.py:625-659): no mask, no cache, RoPE positions 0..seq-1.
+// The linear layers run over all nseq * seq rows at once (rows are
+// independent); attention stays within each sequence.
+void dit_decoder(const orc_model* m, float* hidden, int nseq, int seq, float* out) {
     const orc_desc& d = m->desc;
     const DecShape s = dit_shape(d);
     const int H = s.h, F = s.f, hq = s.hq, hkv = s.hkv, hd = s.d;
-    std::vector<float> cos(static_cast<std::size_t>(n) * hd), sin(cos.size());
-    rope_cache(hd, d.rope_theta, d.rope_original_max, m->short_factor.data(), nullptr, 0, n,
+    const int n = nseq * seq;
+    std::vector<float> cos(static_cast<std::size_t>(seq) * hd), sin(cos.size());
+    rope_cache(hd, d.rope_theta, d.rope_original_max, m->short_factor.data(), nullptr, 0, seq,
                cos.data(), sin.data());
-    const std::size_t N = n;
+    const std::size_t N = n, S = seq;
     std::vector<float> normed(N * H), q(N * hq * hd), k(N * hkv * hd), v(N * hkv * hd),
-        qh(q.size()), kh(k.size()), vh(v.size()), attn_h(q.size()), attn(q.size()), o(N * H),
-        gate(N * F), up(N * F), down(N * H);
+        qh(S * hq * hd), kh(S * hkv * hd), vh(S * hkv * hd), attn_h(qh.size()), attn(q.size()),
+        o(N * H), gate(N * F), up(N * F), down(N * H);
     for (const DecoderLayerW& L : m->dit.dec.layers) {
         rmsnorm(hidden, L.in_norm, H, d.rms_eps, n, normed.data());
         linear(L.wq, nullptr, hq * hd, H, normed.data(), n, q.data());
         linear(L.wk, nullptr, hkv * hd, H, normed.data(), n, k.data());
         linear(L.wv, nullptr, hkv * hd, H, normed.data(), n, v.data());
-        for (int i = 0; i < n; ++i) {
-            for (int hh = 0; hh < hq; ++hh)
-                std::memcpy(&qh[(static_cast<std::size_t>(hh) * n + i) * hd],
-                            &q[(static_cast<std::size_t>(i) * hq + hh) * hd], sizeof(float) * hd);
-            for (int hh = 0; hh < hkv; ++hh) {
-                std::memcpy(&kh[(static_cast<std::size_t>(hh) * n + i) * hd],
-                            &k[(static_cast<std::size_t>(i) * hkv + hh) * hd], sizeof(float) * hd);
-                std::memcpy(&vh[(static_cast<std::size_t>(hh) * n + i) * hd],
-                            &v[(static_cast<std::size_t>(i) * hkv + hh) * hd], sizeof(float) * hd);
+        for (int b = 0; b < nseq; ++b) {
+            const std::size_t r0 = static_cast<std::size_t>(b) * seq;
+            for (int i = 0; i < seq; ++i) {
+                for (int hh = 0; hh < hq; ++hh)
+                    std::memcpy(&qh[(static_cast<std::size_t>(hh) * seq + i) * hd],
+                                &q[((r0 + i) * hq + hh) * hd], sizeof(float) * hd);
+                for (int hh = 0; hh < hkv; ++hh) {
+                    std::memcpy(&kh[(static_cast<std::size_t>(hh) * seq + i) * hd],
+                                &k[((r0 + i) * hkv + hh) * hd], sizeof(float) * hd);
+                    std::memcpy(&vh[(static_cast<std::size_t>(hh) * seq + i) * hd],
+                                &v[((r0 + i) * hkv + hh) * hd], sizeof(float) * hd);
+                }
             }
+            rope_apply(qh.data(), hq, seq, hd, cos.data(), sin.data());
+            rope_apply(kh.data(), hkv, seq, hd, cos.data(), sin.data());
+            sdpa_impl(qh.data(), hq, seq, hd, kh.data(), vh.data(), hkv, seq, hd, nullptr, 0,
+                      nullptr, nullptr, 0, 0.0f, attn_h.data(), nullptr, nullptr);
+            for (int i = 0; i < seq; ++i)
+                for (int hh = 0; hh < hq; ++hh)
+                    std::memcpy(&attn[((r0 + i) * hq + hh) * hd],
+                                &attn_h[(static_cast<std::size_t>(hh) * seq + i) * hd],
+                                sizeof(float) * hd);
         }
-        rope_apply(qh.data(), hq, n, hd, cos.data(), sin.data());
-        rope_apply(kh.data(), hkv, n, hd, cos.data(), sin.data());
-        sdpa_impl(qh.data(), hq, n, hd, kh.data(), vh.data(), hkv, n, hd, nullptr, 0, nullptr,
-                  nullptr, 0, 0.0f, attn_h.data(), nullptr, nullptr);
-        for (int i = 0; i < n; ++i)
-            for (int hh = 0; hh < hq; ++hh)
-                std::memcpy(&attn[(static_cast<std::size_t>(i) * hq + hh) * hd],
-                            &attn_h[(static_cast<std::size_t>(hh) * n + i) * hd],
-                            sizeof(float) * hd);
         linear(L.wo, nullptr, H, hq * hd, attn.data(), n, o.data());
         const float rs = d.dit_residual_scale;
         for (std::size_t i = 0; i < N * H; ++i) hidden[i] = hidden[i] + (rs == 1.0f ? o[i] : o[i] * rs);
@@ -541,20 +566,21 @@ int dit_estimator(const orc_model* m, const float* x_in, const float* mu_in, con
     time_mlp(w.t1_w, w.t1_b, w.t2_w, w.t2_b, Hd, temb.data(), 2, tt.data());
     time_mlp(w.dt1_w, w.dt1_b, w.dt2_w, w.dt2_b, Hd, dtemb.data(), 2, dtt.data());
     const int seq = 3 + 2 * P;  // [mu0, mu1, time, cond x P, x x P] = 11
-    std::vector<float> hidden(static_cast<std::size_t>(seq) * Hd), normed(hidden.size());
+    std::vector<float> hidden(static_cast<std::size_t>(2) * seq * Hd), normed(hidden.size());
     std::vector<float> rows(static_cast<std::size_t>(2) * P * Hd);
     for (int b = 0; b < 2; ++b) {
-        float* hp = hidden.data();
+        float* hp = hidden.data() + static_cast<std::size_t>(b) * seq * Hd;
         std::memcpy(hp, mu_in + static_cast<std::size_t>(b) * 2 * Hd, sizeof(float) * 2 * Hd);
         for (int e = 0; e < Hd; ++e)
             hp[2 * Hd + e] = tt[static_cast<std::size_t>(b) * Hd + e] + dtt[static_cast<std::size_t>(b) * Hd + e];
         std::memcpy(hp + 3 * Hd, &ch[static_cast<std::size_t>(b) * P * Hd], sizeof(float) * P * Hd);
         std::memcpy(hp + (3 + P) * static_cast<std::size_t>(Hd), &xh[static_cast<std::size_t>(b) * P * Hd],
                     sizeof(float) * P * Hd);
-        dit_decoder(m, hidden.data(), seq, normed.data());
-        std::memcpy(&rows[static_cast<std::size_t>(b) * P * Hd], normed.data() + (3 + P) * static_cast<std::size_t>(Hd),
-                    sizeof(float) * P * Hd);
     }
+    dit_decoder(m, hidden.data(), 2, seq, normed.data());
+    for (int b = 0; b < 2; ++b)
+        std::memcpy(&rows[static_cast<std::size_t>(b) * P * Hd],
+                    normed.data() + (static_cast<std::size_t>(b) * seq + 3 + P) * Hd, sizeof(float) * P * Hd);
     std::vector<float> o(static_cast<std::size_t>(2) * P * D);
     linear(w.out_w, w.out_b, D, Hd, rows.data(), 2 * P, o.data());
     // reshape(batch, 4, -1).transpose(1, 2) -> [2][D][P]
