@@ -1,0 +1,227 @@
+/* C ABI of libvoxcpm2_cuda: the B200 (sm_100a) VoxCPM2 patch loop.
+ *
+ * This is the thin shim the reference's C++ host runtime calls instead of its
+ * ncnn graphs for the autoregressive patch loop. Each entry point names the
+ * reference routine it replaces. Conventions (mirroring include/voxcpm2/c_api.h):
+ *   - every function returning int32_t returns a vxc_status and never throws;
+ *     on failure vxc_last_error() holds this thread's message (valid until the
+ *     thread's next failing call);
+ *   - unless stated otherwise pointers are HOST memory, fp32, C order;
+ *   - calls on one vxc_stream are serialised by the library; distinct streams
+ *     (e.g. one host thread each) run concurrently and share their device's
+ *     read-only weights;
+ *   - nothing falls back to the CPU: without a usable CUDA device calls fail.
+ */
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__) || defined(__clang__)
+#define VXC_API __attribute__((visibility("default")))
+#else
+#define VXC_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VXC_ABI_VERSION 1u
+
+typedef struct vxc_device vxc_device;
+typedef struct vxc_stream vxc_stream;
+
+/* Same values and meaning as voxcpm2_status (include/voxcpm2/c_api.h:37-44). */
+typedef enum vxc_status {
+    VXC_STATUS_OK = 0,
+    VXC_STATUS_INVALID_ARGUMENT = 1,
+    VXC_STATUS_INVALID_STATE = 2,
+    VXC_STATUS_CANCELLED = 3,
+    VXC_STATUS_OUT_OF_MEMORY = 4,
+    VXC_STATUS_RUNTIME_ERROR = 5,
+} vxc_status;
+
+/* Component ids of src/components.h:16-29 (the audio VAE ids 9/10 are not served here). */
+enum {
+    VXC_TEXT_EMBED = 0,
+    VXC_BASE_DECODER = 1,
+    VXC_RESIDUAL_DECODER = 2,
+    VXC_FSQ = 3,
+    VXC_FUSION_PROJ = 4,
+    VXC_DIT_PROJ = 5,
+    VXC_STOP_HEAD = 6,
+    VXC_FEAT_ENCODER = 7,
+    VXC_DIT_ESTIMATOR = 8,
+};
+
+/* Which decoder a KV-cache call addresses. */
+enum { VXC_BASE = 0, VXC_RESIDUAL = 1 };
+
+/* Model dimensions: the fields of model.json's "setting" block
+ * (src/model_manifest.cpp:145-172) plus the per-component sizes the ncnn
+ * graphs carry implicitly. */
+typedef struct vxc_model_desc {
+    int32_t hidden;        /* LM hidden size H */
+    int32_t ffn;           /* LM SwiGLU intermediate size */
+    int32_t q_heads;
+    int32_t kv_heads;
+    int32_t head_dim;      /* 64 */
+    int32_t base_layers;   /* base_attn_cnt */
+    int32_t res_layers;    /* residual_attn_cnt */
+    int32_t dit_hidden;    /* Hd; mu is 2 tokens of Hd */
+    int32_t dit_ffn;
+    int32_t dit_layers;
+    int32_t dit_q_heads;
+    int32_t dit_kv_heads;
+    int32_t feat_dim;      /* D = 64 */
+    int32_t patch_size;    /* P = 4 */
+    int32_t vocab;
+    int32_t fsq_dim;
+    float fsq_scale;
+    float rms_eps;
+    float rope_theta;
+    int32_t rope_original_max;   /* original_max_position_embeddings */
+    float base_residual_scale;   /* muP scale_depth / sqrt(layers), 1 = off */
+    float res_residual_scale;
+    float dit_residual_scale;
+    float embed_scale;           /* text_embed scale_emb, 1 = off */
+    int32_t audio_start_token;
+    int32_t max_generation_patches; /* hard cap, 2000 in the reference */
+} vxc_model_desc;
+
+/* Snapshot of a stream's device control block. */
+typedef struct vxc_stream_state {
+    int32_t kv_len[2];      /* tokens in the base / residual KV caches */
+    int32_t patches;        /* patches generated since the last prefill */
+    int32_t stopped;        /* the last patch step hit the stop rule */
+    float stop_logits[2];   /* the last stop_head logits */
+    int32_t prefix_len;
+    int32_t error;          /* last device-side check code (0 = none) */
+} vxc_stream_state;
+
+/* Progress callback of vxc_generate: return non-zero to continue, zero to cancel
+ * (the same contract as voxcpm2_progress_callback, include/voxcpm2/c_api.h:98-106). */
+typedef int32_t (*vxc_progress_fn)(void* user_data, int32_t completed, int32_t total);
+
+VXC_API uint32_t vxc_abi_version(void);
+VXC_API const char* vxc_last_error(void);
+
+/* Number of fp16 values vxc_load_weights expects for a component. */
+VXC_API size_t vxc_component_weight_count(const vxc_model_desc* desc, int32_t component);
+
+/* Loads the model on one CUDA device (replaces Synthesizer::Impl::load_manifest /
+ * load_net, src/synthesizer.cpp:812-870, for the patch-loop components). */
+VXC_API int32_t vxc_device_create(int32_t device, const vxc_model_desc* desc, vxc_device** out);
+VXC_API void vxc_device_destroy(vxc_device* dev);
+
+/* Copies one component's fp16 weights (IEEE half bits, the tensor order documented
+ * in voxcpm2_b200/config.py) to the device (replaces ncnn::Net::load_model). */
+VXC_API int32_t vxc_load_weights(vxc_device* dev, int32_t component, const void* fp16, size_t count);
+
+/* One synthesis stream: its CUDA stream, KV caches of kv_capacity tokens for both
+ * decoders (replaces HostDecoderKvCache, src/kvcache.h:18-40), scratch and graphs. */
+VXC_API int32_t vxc_stream_create(vxc_device* dev, int32_t kv_capacity, vxc_stream** out);
+VXC_API void vxc_stream_destroy(vxc_stream* s);
+/* Empties both KV caches (a new HostDecoderKvCache pair, synthesizer.cpp:348-350). */
+VXC_API int32_t vxc_stream_reset(vxc_stream* s);
+/* Cancels the active vxc_generate at its next patch boundary (thread-safe;
+ * voxcpm2_operation_cancel, include/voxcpm2/c_api.h:110-114). */
+VXC_API void vxc_stream_cancel(vxc_stream* s);
+
+/* HostDecoderKvCache::token_count (src/kvcache.cpp:55-60). */
+VXC_API int32_t vxc_token_count(vxc_stream* s, int32_t which, int32_t* out);
+/* HostDecoderKvCache::cache_or_empty (src/kvcache.cpp:62-72) as fp32 copies:
+ * k, v [kv_heads][token_count][head_dim]. */
+VXC_API int32_t vxc_read_cache(vxc_stream* s, int32_t which, int32_t layer, float* k, float* v);
+
+/* run_decoder_with_kv (src/kvcache.h:87-94, src/kvcache.cpp:232-279): runs the
+ * base (RoPE) or residual decoder over n new rows embed [n][H], with the causal
+ * mask make_decoder_mask(n, token_count) and, for the base decoder, the RoPE
+ * rows of positions [token_count, token_count + n) -- exactly what every call
+ * site in synthesizer.cpp passes -- appends to the KV cache and writes the
+ * final-norm output out [n][H]. */
+VXC_API int32_t vxc_decoder_step(vxc_stream* s, int32_t which, const float* embed, int32_t n, float* out);
+
+/* text_embed graph (export_components.py:475-482): out [n][H]. */
+VXC_API int32_t vxc_text_embed(vxc_stream* s, const int32_t* ids, int32_t n, float* out);
+
+/* One-row small graphs (run_net_vec in synthesizer.cpp:546-640):
+ *   VXC_FSQ          in0 [H]                 -> out [H]
+ *   VXC_FUSION_PROJ  in0 lm [H], in1 feat [H] -> out [H]
+ *   VXC_DIT_PROJ     in0 lm [H], in1 res [H]  -> out [2*Hd]
+ *   VXC_STOP_HEAD    in0 [H]                 -> out [2]
+ *   VXC_FEAT_ENCODER in0 latent [D][P] d-major -> out [H] */
+VXC_API int32_t vxc_run_component(vxc_stream* s, int32_t component, const float* in0, const float* in1,
+                                  float* out);
+
+/* One dit_estimator call as cfm_sample binds it (synthesizer.cpp:137-145):
+ * x_in [2][D][P], mu_in [2][2*Hd], t_in [2] = {step index, timesteps} (schedule
+ * mode), cond_in [2][D][P], dt_in [2] raw -> out [2][D*P]. */
+VXC_API int32_t vxc_dit_estimator(vxc_stream* s, const float* x_in, const float* mu_in, const float* t_in,
+                                  const float* cond_in, const float* dt_in, float* out);
+
+/* cfm_sample (synthesizer.cpp:86-170) for one patch: mu [2*Hd], cond [D*P],
+ * noise [D*P] (the patch's N(0,1) draws) -> out_latent [D*P]. */
+VXC_API int32_t vxc_cfm_sample(vxc_stream* s, const float* mu, const float* cond, const float* noise,
+                               int32_t timesteps, float cfg_value, float* out_latent);
+
+/* Prefix phase of generate_with_caches for a text-only prompt
+ * (synthesizer.cpp:387-535): prefix = text_ids + audio_start; text_embed, base
+ * prefill, fusion_proj, residual prefill; resets the caches and the patch count. */
+VXC_API int32_t vxc_prefill(vxc_stream* s, const int32_t* text_ids, int32_t n_text);
+
+/* One iteration of the patch loop (synthesizer.cpp:537-659), replayed as one
+ * CUDA graph: dit_proj, cfm_sample (timesteps-1 estimator calls after the
+ * zero-init skip), stop_head, and -- unless the stop rule fires --
+ * feat_encoder, base decode, fsq, fusion_proj and residual decode. 'step' must
+ * equal the number of patches generated since vxc_prefill. noise [D*P] are the
+ * patch's draws (NULL: use the table uploaded with vxc_upload_noise).
+ * out_latent [D*P] (may be NULL); *out_stop = 1 when the loop must break. */
+VXC_API int32_t vxc_patch_step(vxc_stream* s, const float* noise, int32_t min_patches, int32_t step,
+                               float cfg_value, int32_t timesteps, float* out_latent, int32_t* out_stop);
+
+/* generate_with_caches without the audio VAE (synthesizer.cpp:353-659): prefill,
+ * then patch steps with noise from std::mt19937(seed) (:452, :108-112) until the
+ * stop rule or max_patches (max_patches_for_target, :216-220; max_patches_override
+ * > 0 lowers it). out_latents [max][D*P]; optional traces per patch of the hidden
+ * states entering it: lm_trace / res_trace [max][H], stop_trace [max][2]. */
+VXC_API int32_t vxc_generate(vxc_stream* s, const int32_t* text_ids, int32_t n_text, int32_t min_patches,
+                             int32_t timesteps, float cfg_value, int32_t max_patches_override, uint32_t seed,
+                             float* out_latents, int32_t* out_patches, float* lm_trace, float* res_trace,
+                             float* stop_trace, vxc_progress_fn progress, void* progress_user_data);
+
+/* VoxCPM2SDPA::forward (src/ncnn_layers/sdpa/voxcpm2_sdpa.cpp:115-260) on DEVICE
+ * pointers, ncnn layout (w = dim, h = seq, c = heads): q [heads][src][d],
+ * k/v [groups][cur][d|dv], mask [mask_c][src][past+cur] or NULL, past_k/v
+ * [groups][past][d] (past may be 0), out [heads][src][dv], out_k/out_v
+ * [groups][past+cur][d] or NULL. scale 0 -> 1/sqrt(d). cuda_stream is a
+ * cudaStream_t (NULL = legacy default stream); the call is asynchronous. */
+VXC_API int32_t vxc_sdpa(const float* q, int32_t heads, int32_t src, int32_t d, const float* k, const float* v,
+                         int32_t groups, int32_t cur, int32_t dv, const float* mask, int32_t mask_c,
+                         const float* past_k, const float* past_v, int32_t past, float scale, float* out,
+                         float* out_k, float* out_v, void* cuda_stream);
+/* The same on HOST pointers (what the ncnn CPU layer receives); synchronous. */
+VXC_API int32_t vxc_sdpa_host(const float* q, int32_t heads, int32_t src, int32_t d, const float* k,
+                              const float* v, int32_t groups, int32_t cur, int32_t dv, const float* mask,
+                              int32_t mask_c, const float* past_k, const float* past_v, int32_t past,
+                              float scale, float* out, float* out_k, float* out_v);
+
+/* ---- device-resident driving (benchmarks, multi-stream servers) ---------- */
+/* Uploads noise [patches][D*P] into the stream's device noise table. */
+VXC_API int32_t vxc_upload_noise(vxc_stream* s, const float* noise, int32_t patches);
+/* Enqueues one patch-step graph reading the device noise table; no host sync,
+ * no host copies. The caller checks the stop flag later with vxc_read_state. */
+VXC_API int32_t vxc_patch_step_async(vxc_stream* s, int32_t min_patches, float cfg_value, int32_t timesteps);
+VXC_API int32_t vxc_stream_synchronize(vxc_stream* s);
+VXC_API int32_t vxc_read_state(vxc_stream* s, vxc_stream_state* out);
+/* Current hidden states entering the next patch: lm [H], res [H] (either may be NULL). */
+VXC_API int32_t vxc_read_hidden(vxc_stream* s, float* lm, float* res);
+/* Latents of patches [first, first + count) generated since the last prefill. */
+VXC_API int32_t vxc_read_latents(vxc_stream* s, int32_t first, int32_t count, float* out);
+/* The stream's cudaStream_t, for callers timing it with CUDA events. */
+VXC_API int32_t vxc_stream_cuda_handle(vxc_stream* s, void** out);
+
+#ifdef __cplusplus
+}
+#endif

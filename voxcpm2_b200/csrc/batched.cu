@@ -1,0 +1,681 @@
+// Token-batched kernels: prompt prefill rows and the DiT estimator's 2 x 11 tokens.
+//
+// The DiT estimator (tools/export_components.py:602-689) runs its decoder over
+// two 11-token sequences per call: [mu(2), time(1), cond(4), x(4)] for the
+// conditional and the unconditional CFG row. Prefill runs the decoders over
+// the whole prompt (synthesizer.cpp:455-525). Both are weight-streaming
+// products with a handful of token rows; this file holds the CUDA-core version
+// of those products plus the row-wise RMSNorm, RoPE/append and attention
+// kernels around them, and the DiT embedding / output / CFG step.
+#include <algorithm>
+#include <cfloat>
+#include <stdexcept>
+
+#include "kernels.cuh"
+
+namespace vxc {
+namespace {
+
+cudaLaunchConfig_t make_cfg(dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+                            cudaLaunchAttribute* attr) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cfg;
+}
+
+void check_launch(cudaError_t e) {
+    if (e != cudaSuccess) throw std::runtime_error(cudaGetErrorString(e));
+}
+
+__device__ __forceinline__ bool stopped(const StreamCtl* ctl, int skip) { return skip && ctl && ctl->stopped; }
+
+// ------------------------------------------------------- rows linear ------
+constexpr int kRowsWarps = 4;
+constexpr int kRowsTile = 8;  // token rows per CTA
+
+template <int MODE>
+__global__ void __launch_bounds__(kRowsWarps * kWarp) rows_linear_kernel(const RowsArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();
+    if (stopped(a.ctl, a.skip_if_stopped)) return;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int item = blockIdx.x * kRowsWarps + warp;
+    int row[4];
+    bool valid[4];
+    if constexpr (MODE == GEMV_GATEUP) {
+        const int p0 = item * 2;
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            valid[i] = valid[i + 2] = p0 + i < a.rows;
+            row[i] = p0 + i;
+            row[i + 2] = a.rows + p0 + i;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            row[i] = item * 4 + i;
+            valid[i] = row[i] < a.rows;
+        }
+    }
+    if (!valid[0]) return;
+    const int m0 = blockIdx.y * kRowsTile;
+    const int mt = min(kRowsTile, a.M - m0);
+    const int K = a.K;
+    float acc[4][kRowsTile];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < kRowsTile; ++j) acc[i][j] = 0.f;
+
+    for (int e = lane * 8; e < K; e += kWarp * 8) {
+        uint4 w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            w[i] = valid[i] ? __ldg(reinterpret_cast<const uint4*>(a.w + static_cast<size_t>(row[i]) * K + e))
+                            : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int j = 0; j < kRowsTile; ++j) {
+            if (j < mt) {
+                const float* xr = a.x + static_cast<size_t>(m0 + j) * a.ldx + e;
+                const float4 x0 = *reinterpret_cast<const float4*>(xr);
+                const float4 x1 = *reinterpret_cast<const float4*>(xr + 4);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) acc[i][j] = dot8(w[i], x0, x1, acc[i][j]);
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < kRowsTile; ++j) acc[i][j] = warp_sum(acc[i][j]);
+    if (lane != 0) return;
+    for (int j = 0; j < mt; ++j) {
+        float* yr = a.y + static_cast<size_t>(m0 + j) * a.ldy;
+        if constexpr (MODE == GEMV_GATEUP) {
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+                if (valid[i]) yr[row[i]] = silu(acc[i][j]) * acc[i + 2][j];
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                if (!valid[i]) continue;
+                if constexpr (MODE == GEMV_RESID) {
+                    yr[row[i]] = yr[row[i]] + (a.rscale == 1.f ? acc[i][j] : acc[i][j] * a.rscale);
+                } else {
+                    float v = acc[i][j] + (a.bias ? __half2float(a.bias[row[i]]) : 0.f);
+                    if (a.act == ACT_SILU) v = silu(v);
+                    yr[row[i]] = v;
+                }
+            }
+        }
+    }
+}
+
+__global__ void rmsnorm_rows_kernel(const float* x, int ldx, const __half* g, float eps, int K,
+                                    float* out, int ldo, StreamCtl* ctl, int skip) {
+    __shared__ float red[32];
+    pdl_launch_dependents();
+    pdl_wait();
+    if (stopped(ctl, skip)) return;
+    const float* xr = x + static_cast<size_t>(blockIdx.x) * ldx;
+    float ss = 0.f;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) ss += xr[k] * xr[k];
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float t = 0.f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += red[w];
+    const float a = rsqrtf(t / static_cast<float>(K) + eps);
+    float* orow = out + static_cast<size_t>(blockIdx.x) * ldo;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) orow[k] = xr[k] * a * __half2float(g[k]);
+}
+
+__global__ void qkv_rows_post_kernel(float* qkv, int q_heads, int kv_heads, int d, int past,
+                                     int pos_mod, const float* rope_cos, const float* rope_sin,
+                                     __half* k_cache, __half* v_cache, int cap, StreamCtl* ctl) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int m = blockIdx.x;
+    const int width = (q_heads + 2 * kv_heads) * d;
+    float* row = qkv + static_cast<size_t>(m) * width;
+    const int pos = past + (m % pos_mod);
+    const int half = d / 2;
+    const int pairs = (q_heads + 2 * kv_heads) * half;
+    for (int it = threadIdx.x; it < pairs; it += blockDim.x) {
+        const int hh = it / half, j = it - hh * half;
+        float* p = row + hh * d;
+        float a0 = p[j], a1 = p[j + half];
+        const bool is_v = hh >= q_heads + kv_heads;
+        if (!is_v && rope_cos) {
+            const float* c = rope_cos + static_cast<size_t>(pos) * d;
+            const float* s = rope_sin + static_cast<size_t>(pos) * d;
+            const float o0 = a0 * c[j] + (-a1) * s[j];
+            const float o1 = a1 * c[j + half] + a0 * s[j + half];
+            a0 = o0;
+            a1 = o1;
+            p[j] = a0;
+            p[j + half] = a1;
+        }
+        if (k_cache && hh >= q_heads) {
+            const int crow = past + m;
+            if (crow >= cap) {
+                if (ctl) ctl->error = 1;
+                continue;
+            }
+            const int kvh = is_v ? hh - q_heads - kv_heads : hh - q_heads;
+            __half* dst = (is_v ? v_cache : k_cache) + (static_cast<size_t>(kvh) * cap + crow) * d;
+            dst[j] = __float2half_rn(a0);
+            dst[j + half] = __float2half_rn(a1);
+        }
+    }
+}
+
+// One CTA per (head, query row): scores in shared memory, two-pass softmax, P.V.
+// SRC 0: prefill rows over the fp16 cache, keys [0, past + m] (the causal -1e4
+// mask of make_decoder_mask removes later keys exactly: exp underflows to 0).
+// SRC 1: DiT rows over the qkv rows of the same 'seq'-row sequence, no mask.
+template <int SRC>
+__global__ void attn_rows_kernel(const float* qkv, int q_heads, int kv_heads, int d, int past,
+                                 int seq, const __half* k_cache, const __half* v_cache, int cap,
+                                 float scale, float* out, StreamCtl* ctl) {
+    extern __shared__ float sm[];
+    __shared__ float red[32];
+    pdl_launch_dependents();
+    pdl_wait();
+    if (SRC == 1 && ctl && ctl->stopped) return;
+    const int hh = blockIdx.x, m = blockIdx.y;
+    const int G = q_heads / kv_heads, kvh = hh / G;
+    const int width = (q_heads + 2 * kv_heads) * d;
+    float* qs = sm;       // [d]
+    float* sc = sm + d;   // [T]
+    for (int e = threadIdx.x; e < d; e += blockDim.x) qs[e] = qkv[static_cast<size_t>(m) * width + hh * d + e] * scale;
+    __syncthreads();
+    int T, key0;
+    if (SRC == 0) {
+        T = past + m + 1;
+        key0 = 0;
+    } else {
+        T = seq;
+        key0 = (m / seq) * seq;
+    }
+    for (int t = threadIdx.x; t < T; t += blockDim.x) {
+        float s = 0.f;
+        if (SRC == 0) {
+            const __half* kp = k_cache + (static_cast<size_t>(kvh) * cap + t) * d;
+            for (int e = 0; e < d; ++e) s = fmaf(qs[e], __half2float(kp[e]), s);
+        } else {
+            const float* kp = qkv + static_cast<size_t>(key0 + t) * width + q_heads * d + kvh * d;
+            for (int e = 0; e < d; ++e) s = fmaf(qs[e], kp[e], s);
+        }
+        sc[t] = s;
+    }
+    __syncthreads();
+    float mx = -FLT_MAX;
+    for (int t = threadIdx.x; t < T; t += blockDim.x) mx = fmaxf(mx, sc[t]);
+    mx = warp_max(mx);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    mx = -FLT_MAX;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) mx = fmaxf(mx, red[w]);
+    __syncthreads();
+    float l = 0.f;
+    for (int t = threadIdx.x; t < T; t += blockDim.x) {
+        const float p = __expf(sc[t] - mx);
+        sc[t] = p;
+        l += p;
+    }
+    l = warp_sum(l);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = l;
+    __syncthreads();
+    l = 0.f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) l += red[w];
+    const float inv = 1.f / l;
+    for (int e = threadIdx.x; e < d; e += blockDim.x) {
+        float acc = 0.f;
+        if (SRC == 0) {
+            const __half* vp = v_cache + static_cast<size_t>(kvh) * cap * d + e;
+            for (int t = 0; t < T; ++t) acc = fmaf(sc[t], __half2float(vp[static_cast<size_t>(t) * d]), acc);
+        } else {
+            const float* vp = qkv + static_cast<size_t>(key0) * width + (q_heads + kv_heads) * d + kvh * d + e;
+            for (int t = 0; t < T; ++t) acc = fmaf(sc[t], vp[static_cast<size_t>(t) * width], acc);
+        }
+        out[static_cast<size_t>(m) * q_heads * d + hh * d + e] = acc * inv;
+    }
+}
+
+__global__ void embed_gather_kernel(const __half* table, const int32_t* ids, int H, float scale,
+                                    float* out) {
+    const int m = blockIdx.x;
+    const __half* row = table + static_cast<size_t>(ids[m]) * H;
+    for (int k = threadIdx.x; k < H; k += blockDim.x)
+        out[static_cast<size_t>(m) * H + k] = __half2float(row[k]) * scale;
+}
+
+// ------------------------------------------------------------------ DiT ---
+// hidden[b] = [mu_b0, mu_b1, t_b + dt_b, cond_proj(cond_b frames), in_proj(x_b frames)]
+__global__ void dit_embed_kernel(const DitEmbedArgs a) {
+    extern __shared__ float sm[];
+    pdl_launch_dependents();
+    pdl_wait();
+    if (a.ctl && a.ctl->stopped) return;
+    const int DP = a.D * a.P;
+    float* xs = sm;           // [2][D*P]
+    float* cs = sm + 2 * DP;  // [2][D*P]
+    for (int i = threadIdx.x; i < DP; i += blockDim.x) {
+        xs[i] = a.x[i];
+        xs[DP + i] = a.x_uncond ? a.x_uncond[i] : a.x[i];
+        cs[i] = a.cond[i];
+        cs[DP + i] = a.cond_uncond ? a.cond_uncond[i] : a.cond[i];
+    }
+    __syncthreads();
+    const int f = blockIdx.x * blockDim.x + threadIdx.x;
+    if (f >= a.Hd) return;
+    const int seq = 3 + 2 * a.P;
+    const __half* wi = a.in_w + static_cast<size_t>(f) * a.D;
+    const __half* wc = a.cond_w + static_cast<size_t>(f) * a.D;
+    const float bi = __half2float(a.in_b[f]), bc = __half2float(a.cond_b[f]);
+    for (int b = 0; b < 2; ++b) {
+        float* h = a.hidden + static_cast<size_t>(b) * seq * a.Hd;
+        const float* mu = b == 0 ? a.mu : a.mu_uncond;
+        h[f] = mu ? mu[f] : 0.f;
+        h[a.Hd + f] = mu ? mu[a.Hd + f] : 0.f;
+        h[2 * a.Hd + f] = (b == 0 ? a.t_tok0 : a.t_tok1)[f] + (b == 0 ? a.dt_tok0 : a.dt_tok1)[f];
+        for (int p = 0; p < a.P; ++p) {
+            float sx = 0.f, scd = 0.f;
+            for (int e = 0; e < a.D; ++e) {
+                // frame p of a d-major [D][P] patch
+                sx = fmaf(__half2float(wi[e]), xs[b * DP + e * a.P + p], sx);
+                scd = fmaf(__half2float(wc[e]), cs[b * DP + e * a.P + p], scd);
+            }
+            h[static_cast<size_t>(3 + p) * a.Hd + f] = scd + bc;
+            h[static_cast<size_t>(3 + a.P + p) * a.Hd + f] = sx + bi;
+        }
+    }
+}
+
+__global__ void timestep_embedding_kernel(float t_or_step, float timesteps, int schedule,
+                                          int half_dim, float* out, StreamCtl* ctl) {
+    pdl_launch_dependents();
+    pdl_wait();
+    if (ctl && ctl->stopped) return;
+    // VoxCPM2TimestepEmbedding::forward (timestep_embedding.cpp:128-160)
+    constexpr float kPi = 3.14159265358979323846f;
+    float t = t_or_step;
+    if (schedule) {
+        const float u = 1.0f - t_or_step / fmaxf(timesteps, 1.0f);
+        t = u + (cosf(kPi * 0.5f * u) - 1.0f + u);
+    }
+    t *= 1000.0f;
+    const float log_period = logf(10000.0f);
+    for (int i = threadIdx.x; i < half_dim; i += blockDim.x) {
+        const float inv_freq = expf(-log_period * static_cast<float>(i) / static_cast<float>(half_dim - 1));
+        const float phase = t * inv_freq;
+        out[i] = sinf(phase);
+        out[i + half_dim] = cosf(phase);
+    }
+}
+
+// final norm of the x rows, out_proj, then CFG-zero* and the Euler step
+// (synthesizer.cpp:147-161). One CTA.
+__global__ void __launch_bounds__(256) dit_out_kernel(const DitOutArgs a) {
+    extern __shared__ float sm[];
+    __shared__ float red[32];
+    __shared__ double dred[2][8];
+    pdl_launch_dependents();
+    pdl_wait();
+    if (a.ctl && a.ctl->stopped) return;
+    const int R = 2 * a.P;        // rows (b, p)
+    const int L = a.D * a.P;      // latent size
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    float* xn = sm;               // [R][Hd]
+    float* est = sm + R * a.Hd;   // [2][L]
+    for (int r = 0; r < R; ++r) {
+        const int b = r / a.P, p = r - b * a.P;
+        const float* h = a.hidden + (static_cast<size_t>(b) * a.seq + 3 + a.P + p) * a.Hd;
+        float ss = 0.f;
+        for (int k = threadIdx.x; k < a.Hd; k += blockDim.x) ss += h[k] * h[k];
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        float t = 0.f;
+        for (int w = 0; w < nw; ++w) t += red[w];
+        const float inv = rsqrtf(t / static_cast<float>(a.Hd) + a.eps);
+        for (int k = threadIdx.x; k < a.Hd; k += blockDim.x)
+            xn[r * a.Hd + k] = h[k] * inv * __half2float(a.norm_g[k]);
+        __syncthreads();
+    }
+    // out_proj: warp per output feature e, all R rows
+    for (int e = warp; e < a.D; e += nw) {
+        float acc[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) acc[r] = 0.f;
+        const __half* wr = a.out_w + static_cast<size_t>(e) * a.Hd;
+        for (int k = lane * 8; k < a.Hd; k += kWarp * 8) {
+            const uint4 w = __ldg(reinterpret_cast<const uint4*>(wr + k));
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+                if (r < R) {
+                    const float4 x0 = *reinterpret_cast<const float4*>(&xn[r * a.Hd + k]);
+                    const float4 x1 = *reinterpret_cast<const float4*>(&xn[r * a.Hd + k + 4]);
+                    acc[r] = dot8(w, x0, x1, acc[r]);
+                }
+            }
+        }
+        const float bias = __half2float(a.out_b[e]);
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            const float v = warp_sum(acc[r]);
+            if (lane == 0 && r < R) {
+                const int b = r / a.P, p = r - b * a.P;
+                est[b * L + e * a.P + p] = v + bias;  // [2][D][P]
+            }
+        }
+    }
+    __syncthreads();
+    if (a.est_out)
+        for (int i = threadIdx.x; i < 2 * L; i += blockDim.x) a.est_out[i] = est[i];
+    if (!a.x) return;
+    // optimized_scale in double (synthesizer.cpp:76-84) + finiteness check (:150)
+    double dot = 0.0, nrm = 0.0;
+    int bad = 0;
+    for (int i = threadIdx.x; i < L; i += blockDim.x) {
+        const float p = est[i], n = est[L + i];
+        if (!isfinite(p) || !isfinite(n)) bad = 1;
+        dot += static_cast<double>(p) * n;
+        nrm += static_cast<double>(n) * n;
+    }
+    bad = __syncthreads_or(bad);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        nrm += __shfl_xor_sync(0xffffffffu, nrm, o);
+    }
+    if (lane == 0) {
+        dred[0][warp] = dot;
+        dred[1][warp] = nrm;
+    }
+    __syncthreads();
+    if (bad) {
+        if (threadIdx.x == 0 && a.ctl) a.ctl->error = 2;
+        return;
+    }
+    double dt_ = 0.0, nm = 1e-8;
+    for (int w = 0; w < nw; ++w) {
+        dt_ += dred[0][w];
+        nm += dred[1][w];
+    }
+    const float sc = static_cast<float>(dt_ / nm);
+    for (int i = threadIdx.x; i < L; i += blockDim.x) {
+        const float pos = est[i], neg = est[L + i];
+        const float dphi = neg * sc + a.cfg * (pos - neg * sc);
+        a.x[i] -= a.dt * dphi;
+    }
+}
+
+__global__ void stop_decide_kernel(const __half* head_w, const float* mid, int H, StreamCtl* ctl,
+                                   float* logits_out) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __shared__ float lg[2];
+    if (warp < 2) {
+        float s = 0.f;
+        for (int k = lane; k < H; k += kWarp) s = fmaf(__half2float(head_w[static_cast<size_t>(warp) * H + k]), mid[k], s);
+        s = warp_sum(s);
+        if (lane == 0) lg[warp] = s;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (logits_out) {
+            logits_out[0] = lg[0];
+            logits_out[1] = lg[1];
+        }
+        if (ctl) {
+            ctl->stop_logits[0] = lg[0];
+            ctl->stop_logits[1] = lg[1];
+            // synthesizer.cpp:584: step > min_patches and argmax2(logits) == 1
+            ctl->stopped = (ctl->step > ctl->min_patches && lg[1] > lg[0]) ? 1 : 0;
+        }
+    }
+}
+
+__global__ void patch_begin_kernel(const float* noise_table, const float* latents, const float* init_cond,
+                                   int per_patch, float* x, float* cond, StreamCtl* ctl) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int patch = ctl->patch;
+    const float* src = noise_table + static_cast<size_t>(patch) * per_patch;
+    const float* c = patch > 0 ? latents + static_cast<size_t>(patch - 1) * per_patch : init_cond;
+    for (int i = threadIdx.x; i < per_patch; i += blockDim.x) {
+        x[i] = src[i];
+        cond[i] = c[i];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) ctl->stopped = 0;
+}
+
+__global__ void patch_end_kernel(const float* x, float* latents, int per_patch, StreamCtl* ctl) {
+    pdl_launch_dependents();
+    pdl_wait();
+    float* dst = latents + static_cast<size_t>(ctl->patch) * per_patch;
+    for (int i = threadIdx.x; i < per_patch; i += blockDim.x) dst[i] = x[i];
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        ctl->patch += 1;
+        ctl->step += 1;
+    }
+}
+
+// VoxCPM2SDPA CPU forward on the GPU (voxcpm2_sdpa.cpp:187-252): one CTA per (head, row).
+__global__ void sdpa_rows_f32_kernel(const float* q, int heads, int src, int d, const float* k,
+                                     const float* v, int groups, int cur, int dv, const float* mask,
+                                     int mask_c, const float* past_k, const float* past_v,
+                                     int past, float scale, float* out) {
+    extern __shared__ float sc[];
+    __shared__ float red[32];
+    const int h = blockIdx.x, i = blockIdx.y;
+    const int dst = past + cur;
+    const int g = h / (heads / groups);
+    const float* qp = q + (static_cast<size_t>(h) * src + i) * d;
+    for (int j = threadIdx.x; j < dst; j += blockDim.x) {
+        const float* kp = j < past ? past_k + (static_cast<size_t>(g) * past + j) * d
+                                   : k + (static_cast<size_t>(g) * cur + (j - past)) * d;
+        float s = 0.f;
+        for (int e = 0; e < d; ++e) s = fmaf(qp[e], kp[e], s);
+        s *= scale;
+        if (mask) {
+            const float* mp = mask + (mask_c > 1 ? static_cast<size_t>(h) * src * dst : 0);
+            s += mp[static_cast<size_t>(i) * dst + j];
+        }
+        sc[j] = s;
+    }
+    __syncthreads();
+    float mx = -FLT_MAX;
+    for (int j = threadIdx.x; j < dst; j += blockDim.x) mx = fmaxf(mx, sc[j]);
+    mx = warp_max(mx);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    mx = -FLT_MAX;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) mx = fmaxf(mx, red[w]);
+    __syncthreads();
+    float l = 0.f;
+    for (int j = threadIdx.x; j < dst; j += blockDim.x) {
+        const float p = expf(sc[j] - mx);
+        sc[j] = p;
+        l += p;
+    }
+    l = warp_sum(l);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = l;
+    __syncthreads();
+    l = 0.f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) l += red[w];
+    for (int e = threadIdx.x; e < dv; e += blockDim.x) {
+        float acc = 0.f;
+        for (int j = 0; j < dst; ++j) {
+            const float* vp = j < past ? past_v + (static_cast<size_t>(g) * past + j) * dv
+                                       : v + (static_cast<size_t>(g) * cur + (j - past)) * dv;
+            acc = fmaf(sc[j] / l, vp[e], acc);
+        }
+        out[(static_cast<size_t>(h) * src + i) * dv + e] = acc;
+    }
+}
+
+__global__ void concat_kv_kernel(const float* past, const float* cur, int past_len, int cur_len,
+                                 int d, float* out) {
+    const int g = blockIdx.y;
+    const int dst = past_len + cur_len;
+    const size_t n = static_cast<size_t>(dst) * d;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const size_t row = i / d, e = i - row * d;
+        out[static_cast<size_t>(g) * n + i] =
+            row < static_cast<size_t>(past_len) ? past[(static_cast<size_t>(g) * past_len + row) * d + e]
+                                                : cur[(static_cast<size_t>(g) * cur_len + (row - past_len)) * d + e];
+    }
+}
+
+}  // namespace
+
+void init_batched_attributes() {
+    constexpr int kMax = 200 * 1024;
+    check_launch(cudaFuncSetAttribute(attn_rows_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax));
+    check_launch(cudaFuncSetAttribute(dit_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax));
+    check_launch(cudaFuncSetAttribute(sdpa_rows_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax));
+}
+
+void launch_rows_linear(const RowsArgs& a, cudaStream_t s, bool pdl) {
+    if (a.K <= 0 || a.K % 8 != 0 || a.M <= 0 || a.rows <= 0 || a.ldx % 4 != 0)
+        throw std::invalid_argument("rows_linear: bad shape");
+    const int per_warp = a.mode == GEMV_GATEUP ? 2 : 4;
+    const int items = (a.rows + per_warp - 1) / per_warp;
+    const dim3 grid((items + kRowsWarps - 1) / kRowsWarps, (a.M + kRowsTile - 1) / kRowsTile);
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(grid, dim3(kRowsWarps * kWarp), 0, s, pdl, attr);
+    switch (a.mode) {
+        case GEMV_PLAIN: check_launch(cudaLaunchKernelEx(&cfg, rows_linear_kernel<GEMV_PLAIN>, a)); break;
+        case GEMV_RESID: check_launch(cudaLaunchKernelEx(&cfg, rows_linear_kernel<GEMV_RESID>, a)); break;
+        case GEMV_GATEUP: check_launch(cudaLaunchKernelEx(&cfg, rows_linear_kernel<GEMV_GATEUP>, a)); break;
+        default: throw std::invalid_argument("rows_linear: unsupported mode");
+    }
+}
+
+void launch_rmsnorm_rows(const float* x, int ldx, const __half* g, float eps, int K, int M,
+                         float* out, int ldo, StreamCtl* ctl, int skip_if_stopped, cudaStream_t s,
+                         bool pdl) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(dim3(M), dim3(256), 0, s, pdl, attr);
+    check_launch(cudaLaunchKernelEx(&cfg, rmsnorm_rows_kernel, x, ldx, g, eps, K, out, ldo, ctl, skip_if_stopped));
+}
+
+void launch_qkv_rows_post(float* qkv, int M, int q_heads, int kv_heads, int d, int past,
+                          int pos_mod, const float* rope_cos, const float* rope_sin,
+                          __half* k_cache, __half* v_cache, int cap, StreamCtl* ctl,
+                          cudaStream_t s, bool pdl) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(dim3(M), dim3(256), 0, s, pdl, attr);
+    check_launch(cudaLaunchKernelEx(&cfg, qkv_rows_post_kernel, qkv, q_heads, kv_heads, d, past, pos_mod,
+                                    rope_cos, rope_sin, k_cache, v_cache, cap, ctl));
+}
+
+void launch_attn_rows_cache(const float* qkv, int M, int q_heads, int kv_heads, int d, int past,
+                            const __half* k_cache, const __half* v_cache, int cap, float scale,
+                            float* out, cudaStream_t s, bool pdl) {
+    if (past + M > cap) throw std::invalid_argument("prefill attention: rows beyond the cache capacity");
+    const size_t smem = static_cast<size_t>(d + past + M) * sizeof(float);
+    if (smem > 200 * 1024) throw std::invalid_argument("prefill attention: sequence too long");
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(dim3(q_heads, M), dim3(128), smem, s, pdl, attr);
+    check_launch(cudaLaunchKernelEx(&cfg, attn_rows_kernel<0>, qkv, q_heads, kv_heads, d, past, 0, k_cache,
+                                    v_cache, cap, scale, out, static_cast<StreamCtl*>(nullptr)));
+}
+
+void launch_dit_attention(const float* qkv, int nseq, int seq, int q_heads, int kv_heads, int d,
+                          float scale, float* out, StreamCtl* ctl, cudaStream_t s, bool pdl) {
+    const size_t smem = static_cast<size_t>(d + seq) * sizeof(float);
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(dim3(q_heads, nseq * seq), dim3(64), smem, s, pdl, attr);
+    check_launch(cudaLaunchKernelEx(&cfg, attn_rows_kernel<1>, qkv, q_heads, kv_heads, d, 0, seq,
+                                    static_cast<const __half*>(nullptr), static_cast<const __half*>(nullptr), 0,
+                                    scale, out, ctl));
+}
+
+void launch_embed_gather(const __half* table, const int32_t* ids, int M, int H, float scale,
+                         float* out, cudaStream_t s) {
+    embed_gather_kernel<<<M, 256, 0, s>>>(table, ids, H, scale, out);
+    check_launch(cudaGetLastError());
+}
+
+void launch_dit_embed(const DitEmbedArgs& a, cudaStream_t s, bool pdl) {
+    cudaLaunchAttribute attr[1];
+    const size_t smem = static_cast<size_t>(4 * a.D * a.P) * sizeof(float);
+    cudaLaunchConfig_t cfg = make_cfg(dim3((a.Hd + 127) / 128), dim3(128), smem, s, pdl, attr);
+    check_launch(cudaLaunchKernelEx(&cfg, dit_embed_kernel, a));
+}
+
+void launch_timestep_embedding(float t_or_step, float timesteps, int schedule, int half_dim,
+                               float* out, StreamCtl* ctl, cudaStream_t s, bool pdl) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(dim3(1), dim3(256), 0, s, pdl, attr);
+    check_launch(cudaLaunchKernelEx(&cfg, timestep_embedding_kernel, t_or_step, timesteps, schedule,
+                                    half_dim, out, ctl));
+}
+
+void launch_dit_out(const DitOutArgs& a, cudaStream_t s, bool pdl) {
+    if (2 * a.P > 8 || a.Hd % 8 != 0) throw std::invalid_argument("dit_out: unsupported patch shape");
+    const size_t smem = static_cast<size_t>(2 * a.P * a.Hd + 2 * a.D * a.P) * sizeof(float);
+    if (smem > 200 * 1024) throw std::invalid_argument("dit_out: hidden too large");
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(dim3(1), dim3(256), smem, s, pdl, attr);
+    check_launch(cudaLaunchKernelEx(&cfg, dit_out_kernel, a));
+}
+
+void launch_stop_decide(const __half* head_w, const float* mid, int H, StreamCtl* ctl,
+                        float* logits_out, cudaStream_t s, bool pdl) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(dim3(1), dim3(64), 0, s, pdl, attr);
+    check_launch(cudaLaunchKernelEx(&cfg, stop_decide_kernel, head_w, mid, H, ctl, logits_out));
+}
+
+void launch_patch_begin(const float* noise_table, const float* latents, const float* init_cond,
+                        int per_patch, float* x, float* cond, StreamCtl* ctl, cudaStream_t s, bool pdl) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(dim3(1), dim3(256), 0, s, pdl, attr);
+    check_launch(cudaLaunchKernelEx(&cfg, patch_begin_kernel, noise_table, latents, init_cond, per_patch, x,
+                                    cond, ctl));
+}
+
+void launch_patch_end(const float* x, float* latents, int per_patch, StreamCtl* ctl,
+                      cudaStream_t s, bool pdl) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(dim3(1), dim3(256), 0, s, pdl, attr);
+    check_launch(cudaLaunchKernelEx(&cfg, patch_end_kernel, x, latents, per_patch, ctl));
+}
+
+void launch_sdpa_rows_f32(const float* q, int heads, int src, int d, const float* k,
+                          const float* v, int groups, int cur, int dv, const float* mask,
+                          int mask_c, const float* past_k, const float* past_v, int past,
+                          float scale, float* out, cudaStream_t s) {
+    const size_t smem = static_cast<size_t>(past + cur) * sizeof(float);
+    if (smem > 200 * 1024) throw std::invalid_argument("sdpa: key sequence too long");
+    sdpa_rows_f32_kernel<<<dim3(heads, src), dim3(128), smem, s>>>(q, heads, src, d, k, v, groups, cur, dv,
+                                                                   mask, mask_c, past_k, past_v, past,
+                                                                   scale, out);
+    check_launch(cudaGetLastError());
+}
+
+void launch_concat_kv(const float* past, const float* cur, int groups, int past_len, int cur_len,
+                      int d, float* out, cudaStream_t s) {
+    const size_t n = static_cast<size_t>(past_len + cur_len) * d;
+    const int blocks = static_cast<int>(std::min<size_t>((n + 255) / 256, 1024));
+    concat_kv_kernel<<<dim3(blocks, groups), 256, 0, s>>>(past, cur, past_len, cur_len, d, out);
+    check_launch(cudaGetLastError());
+}
+
+}  // namespace vxc

@@ -1,0 +1,381 @@
+// Batch-1 decoder kernels: GEMV family and split-K flash-decode attention.
+//
+// The KV-cache decode step of base_decoder_kv / residual_decoder_kv
+// (tools/export_components.py:496-550, run by src/kvcache.cpp:232-279) is a
+// chain of matrix-vector products over fp16 weights. Each GEMV streams its
+// weight rows into registers with 16-byte no-allocate loads BEFORE waiting on
+// the previous kernel (programmatic dependent launch), so weight streaming of
+// kernel i+1 overlaps kernel i; only the small fp32 input vector is read after
+// the dependency resolves. RMSNorm is folded into the GEMV prologue, RoPE and
+// the fp16 KV append into the q/k/v epilogue.
+#include <cfloat>
+#include <stdexcept>
+
+#include "kernels.cuh"
+
+namespace vxc {
+namespace {
+
+constexpr int kGemvWarps = 4;
+constexpr int kGemvThreads = kGemvWarps * kWarp;
+
+__device__ __forceinline__ float gemv_input(const GemvArgs& a, int k) {
+    if (a.in_mode == IN_CONCAT) return k < a.k1 ? a.x[k] : a.x2[k - a.k1];
+    if (a.in_mode == IN_LATENT_T) {
+        // make_feat_encoder_input: frame-major value[p * D + d] = latent[d * P + p]
+        const int p = k / a.lat_d, d = k - p * a.lat_d;
+        return a.x[d * a.lat_p + p];
+    }
+    return a.x[k];
+}
+
+template <int MODE, int MAXCH, int RPW>
+__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
+    extern __shared__ float xs[];
+    __shared__ float red[kGemvWarps];
+    pdl_launch_dependents();
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int item = blockIdx.x * kGemvWarps + warp;
+    const bool active = item < a.rows;
+    const int K = a.K;
+
+    // rows owned by this warp
+    int row[RPW];
+    if constexpr (MODE == GEMV_GATEUP) {
+        row[0] = item;
+        row[1] = item + a.rows;
+    } else if constexpr (MODE == GEMV_QKV) {
+        const int half = a.head_dim >> 1;
+        const int hh = item / half, j = item - hh * half;
+        row[0] = hh * a.head_dim + j;
+        row[1] = row[0] + half;
+    } else {
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) row[r] = item * RPW + r;
+    }
+
+    // 1) stream this warp's weight rows into registers (independent of inputs)
+    uint4 wr[RPW][MAXCH];
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+        const __half* wrow = a.w + static_cast<size_t>(row[r]) * K;
+#pragma unroll
+        for (int c = 0; c < MAXCH; ++c) {
+            const int e = (c * kWarp + lane) * 8;
+            wr[r][c] = (active && e < K) ? ld_stream(wrow + e) : make_uint4(0, 0, 0, 0);
+        }
+    }
+
+    // 2) wait for the producer of the input vector
+    pdl_wait();
+    if (a.skip_if_stopped && a.ctl && a.ctl->stopped) return;
+
+    // 3) stage the (optionally RMS-normalised) input in shared memory
+    float ss = 0.f;
+    for (int k = threadIdx.x; k < K; k += kGemvThreads) {
+        const float v = gemv_input(a, k);
+        ss += v * v;
+        xs[k] = a.norm_g ? v * __half2float(a.norm_g[k]) : v;
+    }
+    float inv_rms = 1.f;
+    if (a.norm_g) {
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        float t = 0.f;
+#pragma unroll
+        for (int w = 0; w < kGemvWarps; ++w) t += red[w];
+        inv_rms = rsqrtf(t / static_cast<float>(K) + a.eps);
+    } else {
+        __syncthreads();
+    }
+    if (!active) return;
+
+    // 4) dot products
+    float acc[RPW];
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) acc[r] = 0.f;
+#pragma unroll
+    for (int c = 0; c < MAXCH; ++c) {
+        const int e = (c * kWarp + lane) * 8;
+        if (e < K) {
+            const float4 x0 = *reinterpret_cast<const float4*>(&xs[e]);
+            const float4 x1 = *reinterpret_cast<const float4*>(&xs[e + 4]);
+#pragma unroll
+            for (int r = 0; r < RPW; ++r) acc[r] = dot8(wr[r][c], x0, x1, acc[r]);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) acc[r] = warp_sum(acc[r]) * inv_rms;
+    if (lane != 0) return;
+
+    // 5) epilogue
+    if constexpr (MODE == GEMV_PLAIN) {
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) {
+            float v = acc[r] + (a.bias ? __half2float(a.bias[row[r]]) : 0.f);
+            if (a.act == ACT_SILU) v = silu(v);
+            else if (a.act == ACT_FSQ) v = rintf(tanhf(v) * a.act_scale) / a.act_scale;
+            a.y[row[r]] = v;
+            if (a.y2) a.y2[row[r]] = v;
+        }
+    } else if constexpr (MODE == GEMV_RESID) {
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) {
+            const float v = a.resid[row[r]] + (a.rscale == 1.f ? acc[r] : acc[r] * a.rscale);
+            a.resid[row[r]] = v;
+        }
+    } else if constexpr (MODE == GEMV_GATEUP) {
+        a.y[item] = silu(acc[0]) * acc[1];
+    } else {  // GEMV_QKV
+        const int d = a.head_dim, half = d >> 1;
+        const int hh = item / half, j = item - hh * half;
+        const int pos = a.ctl->kv_len[a.which];
+        float o0 = acc[0], o1 = acc[1];
+        const bool is_v = hh >= a.q_heads + a.kv_heads;
+        if (!is_v && a.rope_cos && pos < a.cap) {
+            // apply_rotary_pos_emb with rotate_half: x*cos + rotate_half(x)*sin
+            const float* c = a.rope_cos + static_cast<size_t>(pos) * d;
+            const float* s = a.rope_sin + static_cast<size_t>(pos) * d;
+            o0 = acc[0] * c[j] + (-acc[1]) * s[j];
+            o1 = acc[1] * c[j + half] + acc[0] * s[j + half];
+        }
+        if (hh < a.q_heads) {
+            a.y[hh * d + j] = o0;
+            a.y[hh * d + j + half] = o1;
+        } else if (pos >= a.cap) {
+            a.ctl->error = 1;  // KV capacity exceeded: the host checks before launch
+        } else {
+            const int kvh = is_v ? hh - a.q_heads - a.kv_heads : hh - a.q_heads;
+            __half* dst = (is_v ? a.v_cache : a.k_cache) + (static_cast<size_t>(kvh) * a.cap + pos) * d;
+            dst[j] = __float2half_rn(o0);
+            dst[j + half] = __float2half_rn(o1);
+        }
+    }
+}
+
+cudaLaunchConfig_t make_cfg(dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+                            cudaLaunchAttribute* attr) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cfg;
+}
+
+void check_launch(cudaError_t e) {
+    if (e != cudaSuccess) throw std::runtime_error(cudaGetErrorString(e));
+}
+
+template <int MODE, int RPW>
+void dispatch_gemv(const GemvArgs& a, cudaStream_t s, bool pdl) {
+    const int nch = (a.K + 255) / 256;
+    const int blocks = (a.rows + kGemvWarps - 1) / kGemvWarps;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(dim3(blocks), dim3(kGemvThreads),
+                                      static_cast<size_t>(((a.K + 7) / 8) * 8) * sizeof(float), s, pdl, attr);
+    if (nch <= 1) check_launch(cudaLaunchKernelEx(&cfg, gemv_kernel<MODE, 1, RPW>, a));
+    else if (nch <= 2) check_launch(cudaLaunchKernelEx(&cfg, gemv_kernel<MODE, 2, RPW>, a));
+    else if (nch <= 4) check_launch(cudaLaunchKernelEx(&cfg, gemv_kernel<MODE, 4, RPW>, a));
+    else if (nch <= 8) check_launch(cudaLaunchKernelEx(&cfg, gemv_kernel<MODE, 8, RPW>, a));
+    else if (RPW == 1 && nch <= 16) check_launch(cudaLaunchKernelEx(&cfg, gemv_kernel<MODE, 16, 1>, a));
+    else throw std::invalid_argument("gemv: input dimension too large");
+}
+
+// ------------------------------------------------------------ attention ---
+template <typename KV>
+__device__ __forceinline__ float load_kv(const KV* p, int e);
+template <>
+__device__ __forceinline__ float load_kv<__half>(const __half* p, int e) { return __half2float(p[e]); }
+template <>
+__device__ __forceinline__ float load_kv<float>(const float* p, int e) { return p[e]; }
+
+constexpr int kAttnThreads = 128;
+constexpr int kMaxGroup = 16;
+
+template <typename KV, int D>
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArgs a, int max_chunk) {
+    extern __shared__ float sm[];
+    __shared__ float s_m[kMaxGroup], s_l[kMaxGroup];
+    __shared__ int s_last;
+    pdl_launch_dependents();
+    pdl_wait();
+    if (a.skip_if_stopped && a.ctl && a.ctl->stopped) return;
+
+    const int G = a.q_heads / a.kv_heads;
+    const int split = blockIdx.x, kvh = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int len0 = a.len0, len1 = a.len1;
+    if (a.ctl) {
+        len0 = min(a.ctl->kv_len[a.which] + 1, a.len0);  // len0 holds the capacity here
+        len1 = 0;
+    }
+    const int T = len0 + len1;
+    const int chunk = (T + a.splits - 1) / a.splits;
+    const int t0 = split * chunk;
+    const int n = max(0, min(min(T, t0 + chunk) - t0, max_chunk));
+
+    float* qs = sm;                 // [G][D]
+    float* sc = sm + G * D;         // [G][max_chunk]
+    for (int i = tid; i < G * D; i += kAttnThreads) qs[i] = a.q[kvh * G * D + i] * a.scale;
+    __syncthreads();
+
+    const KV* k0 = static_cast<const KV*>(a.k0) + static_cast<size_t>(kvh) * a.stride0 * D;
+    const KV* v0 = static_cast<const KV*>(a.v0) + static_cast<size_t>(kvh) * a.stride0 * D;
+    const KV* k1 = a.k1 ? static_cast<const KV*>(a.k1) + static_cast<size_t>(kvh) * a.stride1 * D : nullptr;
+    const KV* v1 = a.v1 ? static_cast<const KV*>(a.v1) + static_cast<size_t>(kvh) * a.stride1 * D : nullptr;
+
+    // scores: one key row per thread, all G heads of the group
+    for (int t = tid; t < n; t += kAttnThreads) {
+        const int row = t0 + t;
+        const KV* kp = row < len0 ? k0 + static_cast<size_t>(row) * D : k1 + static_cast<size_t>(row - len0) * D;
+        float kr[D];
+#pragma unroll
+        for (int e = 0; e < D; ++e) kr[e] = load_kv(kp, e);
+        const float madd = a.mask ? a.mask[row] : 0.f;
+        for (int g = 0; g < G; ++g) {
+            float s = 0.f;
+#pragma unroll
+            for (int e = 0; e < D; ++e) s = fmaf(qs[g * D + e], kr[e], s);
+            sc[g * max_chunk + t] = s + madd;
+        }
+    }
+    __syncthreads();
+    // softmax statistics per head (one warp per head)
+    for (int g = warp; g < G; g += kAttnThreads / kWarp) {
+        float m = -1e30f;
+        for (int t = lane; t < n; t += kWarp) m = fmaxf(m, sc[g * max_chunk + t]);
+        m = warp_max(m);
+        float l = 0.f;
+        for (int t = lane; t < n; t += kWarp) {
+            const float p = __expf(sc[g * max_chunk + t] - m);
+            sc[g * max_chunk + t] = p;
+            l += p;
+        }
+        l = warp_sum(l);
+        if (lane == 0) {
+            s_m[g] = n > 0 ? m : -1e30f;
+            s_l[g] = l;
+        }
+    }
+    __syncthreads();
+    // P.V partials
+    float* part = a.partial + (static_cast<size_t>(kvh) * a.splits + split) * G * (D + 2);
+    for (int it = tid; it < G * D; it += kAttnThreads) {
+        const int g = it / D, e = it - g * D;
+        float acc = 0.f;
+        for (int t = 0; t < n; ++t) {
+            const int row = t0 + t;
+            const KV* vp = row < len0 ? v0 + static_cast<size_t>(row) * D : v1 + static_cast<size_t>(row - len0) * D;
+            acc = fmaf(sc[g * max_chunk + t], load_kv(vp, e), acc);
+        }
+        part[g * (D + 2) + e] = acc;
+        if (e == 0) {
+            part[g * (D + 2) + D] = s_m[g];
+            part[g * (D + 2) + D + 1] = s_l[g];
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(&a.counters[kvh], 1) == a.splits - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    // combine the splits of this KV head
+    const float* pk = a.partial + static_cast<size_t>(kvh) * a.splits * G * (D + 2);
+    for (int it = tid; it < G * D; it += kAttnThreads) {
+        const int g = it / D, e = it - g * D;
+        float M = -1e30f;
+        for (int sp = 0; sp < a.splits; ++sp) M = fmaxf(M, __ldcg(pk + (sp * G + g) * (D + 2) + D));
+        float num = 0.f, den = 0.f;
+        for (int sp = 0; sp < a.splits; ++sp) {
+            const float* pp = pk + (sp * G + g) * (D + 2);
+            const float w = __expf(__ldcg(pp + D) - M);
+            num = fmaf(w, __ldcg(pp + e), num);
+            den = fmaf(w, __ldcg(pp + D + 1), den);
+        }
+        a.out[(kvh * G + g) * D + e] = num / den;
+    }
+    if (tid == 0) a.counters[kvh] = 0;
+}
+
+__global__ void final_norm_kernel(const float* h, const __half* g, float eps, int H, float* out,
+                                  float* out2, StreamCtl* ctl, int which, int bump, int skip) {
+    __shared__ float red[32];
+    pdl_launch_dependents();
+    pdl_wait();
+    if (skip && ctl && ctl->stopped) return;
+    float ss = 0.f;
+    for (int k = threadIdx.x; k < H; k += blockDim.x) ss += h[k] * h[k];
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float t = 0.f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += red[w];
+    const float a = rsqrtf(t / static_cast<float>(H) + eps);
+    for (int k = threadIdx.x; k < H; k += blockDim.x) {
+        const float v = h[k] * a * __half2float(g[k]);
+        out[k] = v;
+        if (out2) out2[k] = v;
+    }
+    if (bump && ctl && threadIdx.x == 0) ctl->kv_len[which] += bump;
+}
+
+}  // namespace
+
+void launch_gemv(const GemvArgs& a, cudaStream_t s, bool pdl) {
+    if (a.K <= 0 || a.K % 8 != 0 || a.rows <= 0) throw std::invalid_argument("gemv: bad shape");
+    switch (a.mode) {
+        case GEMV_PLAIN: dispatch_gemv<GEMV_PLAIN, 1>(a, s, pdl); break;
+        case GEMV_RESID: dispatch_gemv<GEMV_RESID, 1>(a, s, pdl); break;
+        case GEMV_GATEUP: dispatch_gemv<GEMV_GATEUP, 2>(a, s, pdl); break;
+        case GEMV_QKV:
+            if (a.head_dim % 2 != 0 || a.ctl == nullptr) throw std::invalid_argument("gemv: bad q/k/v setup");
+            dispatch_gemv<GEMV_QKV, 2>(a, s, pdl);
+            break;
+        default: throw std::invalid_argument("gemv: unknown mode");
+    }
+}
+
+void launch_attn_decode(const AttnArgs& a, bool fp16_kv, cudaStream_t s, bool pdl) {
+    if (a.head_dim != 64) throw std::invalid_argument("attention: head_dim must be 64");
+    if (a.kv_heads <= 0 || a.q_heads % a.kv_heads != 0 || a.splits < 1)
+        throw std::invalid_argument("attention: bad head grouping");
+    const int G = a.q_heads / a.kv_heads;
+    if (G < 1 || G > kMaxGroup) throw std::invalid_argument("attention: more than 16 query heads per KV head");
+    // the longest split any launch of this configuration can see
+    const int t_max = a.ctl ? a.len0 : a.len0 + a.len1;
+    const int max_chunk = (t_max + a.splits - 1) / a.splits;
+    const size_t smem = static_cast<size_t>(G) * (64 + max_chunk) * sizeof(float);
+    if (smem > 200 * 1024) throw std::invalid_argument("attention: sequence too long for one split");
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(dim3(a.splits, a.kv_heads), dim3(kAttnThreads), smem, s, pdl, attr);
+    if (fp16_kv) check_launch(cudaLaunchKernelEx(&cfg, attn_decode_kernel<__half, 64>, a, max_chunk));
+    else check_launch(cudaLaunchKernelEx(&cfg, attn_decode_kernel<float, 64>, a, max_chunk));
+}
+
+void init_batched_attributes();
+
+void init_kernel_attributes() {
+    constexpr int kMax = 200 * 1024;
+    check_launch(cudaFuncSetAttribute(attn_decode_kernel<__half, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax));
+    check_launch(cudaFuncSetAttribute(attn_decode_kernel<float, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax));
+    init_batched_attributes();
+}
+
+void launch_final_norm(const float* h, const __half* g, float eps, int H, float* out, float* out2,
+                       StreamCtl* ctl, int which, int bump, int skip_if_stopped, cudaStream_t s,
+                       bool pdl) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(dim3(1), dim3(256), 0, s, pdl, attr);
+    check_launch(cudaLaunchKernelEx(&cfg, final_norm_kernel, h, g, eps, H, out, out2, ctl, which, bump,
+                                    skip_if_stopped));
+}
+
+}  // namespace vxc

@@ -1,0 +1,199 @@
+// Kernel launch interface of libvoxcpm2_cuda (host side, sm_100a).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace vxc {
+
+// ---------------------------------------------------------------- GEMV ---
+// Batch-1 matrix-vector products over fp16 weights [rows][K] with an fp32
+// input vector, fp32 accumulation. The input can be RMS-normalised on the fly
+// (gain g, eps), formed by concatenating two vectors, or read from a d-major
+// latent patch transposed to frame-major.
+enum GemvMode : int {
+    GEMV_PLAIN = 0,   // y[r] = act(dot + bias[r])
+    GEMV_RESID = 1,   // resid[r] += rscale * dot                    (o_proj, down_proj)
+    GEMV_GATEUP = 2,  // y[r] = silu(dot(gate r)) * dot(up r)        (rows r and r + pairs)
+    GEMV_QKV = 3,     // q/k/v rows in RoPE pairs; q -> y, k/v -> fp16 KV cache at ctl->kv_len
+};
+enum GemvAct : int { ACT_NONE = 0, ACT_SILU = 1, ACT_FSQ = 2 };
+enum GemvInput : int { IN_PLAIN = 0, IN_CONCAT = 1, IN_LATENT_T = 2 };
+
+struct GemvArgs {
+    int mode = GEMV_PLAIN;
+    const __half* w = nullptr;
+    const __half* bias = nullptr;
+    const float* x = nullptr;
+    const float* x2 = nullptr;      // IN_CONCAT: second part, starting at k1
+    int k1 = 0;
+    int in_mode = IN_PLAIN;
+    int lat_d = 0, lat_p = 0;       // IN_LATENT_T: latent [lat_d][lat_p]
+    const __half* norm_g = nullptr;  // RMSNorm gain of the input, or null
+    float eps = 1e-5f;
+    int K = 0;
+    int rows = 0;                   // output rows (row pairs for GATEUP / QKV)
+    int act = ACT_NONE;
+    float act_scale = 1.0f;         // ACT_FSQ quantisation scale
+    float rscale = 1.0f;            // GEMV_RESID residual scale
+    float* y = nullptr;
+    float* y2 = nullptr;            // optional second copy of y
+    float* resid = nullptr;
+    // GEMV_QKV
+    int q_heads = 0, kv_heads = 0, head_dim = 0;
+    const float* rope_cos = nullptr;  // [capacity][head_dim] or null (no RoPE)
+    const float* rope_sin = nullptr;
+    __half* k_cache = nullptr;      // this layer: [kv_heads][cap][head_dim]
+    __half* v_cache = nullptr;
+    int cap = 0;
+    int which = 0;                  // which decoder's kv_len indexes the cache
+    // control
+    StreamCtl* ctl = nullptr;
+    int skip_if_stopped = 0;
+};
+
+void launch_gemv(const GemvArgs& a, cudaStream_t s, bool pdl);
+
+// ------------------------------------------------------ flash decode -----
+// One query token of each of q_heads heads attends over keys [0, T) of a GQA
+// cache split into two segments (seg0 of len0 rows, then seg1), split-K over
+// 'splits' CTAs per KV head with a last-CTA combine. Either segment may hold
+// fp16 (cache) or fp32 (layer contract) rows; 'T' is read from ctl->kv_len[which] + 1
+// when ctl is non-null (then len0 must hold the cache capacity, which sizes the
+// shared-memory score buffer), else T = len0 + len1.
+struct AttnArgs {
+    const float* q = nullptr;          // [q_heads][d]
+    const void* k0 = nullptr; const void* v0 = nullptr;  // [kv_heads][stride0][d]
+    const void* k1 = nullptr; const void* v1 = nullptr;  // [kv_heads][stride1][d]
+    int len0 = 0, len1 = 0;
+    long stride0 = 0, stride1 = 0;     // rows per KV head plane
+    const float* mask = nullptr;       // additive [T] (one query row) or null
+    int q_heads = 0, kv_heads = 0, head_dim = 0;
+    float scale = 0.125f;
+    int splits = 16;
+    float* partial = nullptr;          // [kv_heads][splits][group][head_dim + 2]
+    int* counters = nullptr;           // [kv_heads], zero between launches
+    float* out = nullptr;              // [q_heads][head_dim]
+    StreamCtl* ctl = nullptr;
+    int which = 0;
+    int skip_if_stopped = 0;
+};
+void launch_attn_decode(const AttnArgs& a, bool fp16_kv, cudaStream_t s, bool pdl);
+
+// final RMSNorm of a decoder step: out = norm(h) * g; optionally bump kv_len.
+void launch_final_norm(const float* h, const __half* g, float eps, int H, float* out, float* out2,
+                       StreamCtl* ctl, int which, int bump, int skip_if_stopped, cudaStream_t s,
+                       bool pdl);
+
+// ----------------------------------------------------- token batches -----
+// Y[m][r] for M tokens (prefill rows, the DiT's 2 x 11 tokens).
+struct RowsArgs {
+    const __half* w = nullptr;
+    const __half* bias = nullptr;
+    const float* x = nullptr;  // [M][ldx]
+    int ldx = 0;
+    int K = 0;
+    int rows = 0;              // output rows (pairs for GATEUP)
+    int M = 0;
+    int mode = GEMV_PLAIN;     // PLAIN (act) / RESID / GATEUP
+    int act = ACT_NONE;
+    float rscale = 1.0f;
+    float* y = nullptr;        // [M][ldy] (RESID: accumulated in place)
+    int ldy = 0;
+    StreamCtl* ctl = nullptr;
+    int skip_if_stopped = 0;
+};
+void launch_rows_linear(const RowsArgs& a, cudaStream_t s, bool pdl);
+
+// out[m] = x[m] / rms(x[m]) * g for M rows of width K
+void launch_rmsnorm_rows(const float* x, int ldx, const __half* g, float eps, int K, int M,
+                         float* out, int ldo, StreamCtl* ctl, int skip_if_stopped,
+                         cudaStream_t s, bool pdl);
+
+// RoPE on the q and k parts of qkv rows [M][(hq+2hkv)d], in place, at position
+// past + (m % pos_mod) of row m (tables indexed by position). With a cache, k/v
+// of row m are also appended (fp16) at cache row past + m (prefill).
+void launch_qkv_rows_post(float* qkv, int M, int q_heads, int kv_heads, int d, int past,
+                          int pos_mod, const float* rope_cos, const float* rope_sin,
+                          __half* k_cache, __half* v_cache, int cap, StreamCtl* ctl,
+                          cudaStream_t s, bool pdl);
+
+// Causal attention of M prefill rows (positions past..past+M-1) over the fp16 cache.
+void launch_attn_rows_cache(const float* qkv, int M, int q_heads, int kv_heads, int d, int past,
+                            const __half* k_cache, const __half* v_cache, int cap, float scale,
+                            float* out, cudaStream_t s, bool pdl);
+
+// DiT: full (non-causal, unmasked) attention within each sequence of 'seq'
+// rows of an already-rotated qkv buffer [nseq*seq][(hq+2hkv)d].
+void launch_dit_attention(const float* qkv, int nseq, int seq, int q_heads, int kv_heads, int d,
+                          float scale, float* out, StreamCtl* ctl, cudaStream_t s, bool pdl);
+
+// h[m] = table[ids[m]] * scale
+void launch_embed_gather(const __half* table, const int32_t* ids, int M, int H, float scale,
+                         float* out, cudaStream_t s);
+
+// ------------------------------------------------------------- DiT ------
+struct DitEmbedArgs {
+    const __half* in_w; const __half* in_b; const __half* cond_w; const __half* cond_b;
+    const float* x;       // [D*P] d-major sample of CFG row 0
+    const float* cond;    // [D*P] d-major condition of CFG row 0
+    const float* mu;      // [2*Hd] mu tokens of CFG row 0
+    const float* t_tok0;  // [Hd] time_mlp(emb(t)) of CFG row 0
+    const float* t_tok1;  // ... of CFG row 1
+    const float* dt_tok0; // [Hd] delta_time_mlp(emb(dt)) of CFG row 0
+    const float* dt_tok1;
+    int Hd, D, P;
+    float* hidden;        // [2][3 + 2P][Hd]
+    StreamCtl* ctl;
+    const float* mu_uncond;  // [2*Hd] of CFG row 1, or null (zeros)
+    const float* x_uncond;   // [D*P] of CFG row 1, or null (same as x)
+    const float* cond_uncond;// [D*P] of CFG row 1, or null (same as cond)
+};
+void launch_dit_embed(const DitEmbedArgs& a, cudaStream_t s, bool pdl);
+
+// sinusoidal timestep embedding of one value (VoxCPM2TimestepEmbedding):
+// schedule != 0 derives t from (step_index, timesteps) like schedule mode 1.
+void launch_timestep_embedding(float t_or_step, float timesteps, int schedule, int half_dim,
+                               float* out, StreamCtl* ctl, cudaStream_t s, bool pdl);
+
+struct DitOutArgs {
+    const float* hidden;    // [2][seq][Hd] pre-final-norm residual stream
+    int seq, Hd, D, P;
+    const __half* norm_g; float eps;
+    const __half* out_w; const __half* out_b;
+    float* est_out;         // optional [2][D*P] raw estimator output
+    float* x;               // [D*P] sample updated in place (null: no update)
+    float dt, cfg;
+    StreamCtl* ctl;
+};
+void launch_dit_out(const DitOutArgs& a, cudaStream_t s, bool pdl);
+
+// stop decision: logits = head_w [2][H] . mid; ctl->stopped = step > min_patches && l1 > l0
+void launch_stop_decide(const __half* head_w, const float* mid, int H, StreamCtl* ctl,
+                        float* logits_out, cudaStream_t s, bool pdl);
+
+// per-patch prologue: x = noise[ctl->patch]; cond = latents[ctl->patch - 1], or
+// init_cond for the first patch (synthesizer.cpp:561-563, 445-447); clears the stop flag.
+void launch_patch_begin(const float* noise_table, const float* latents, const float* init_cond,
+                        int per_patch, float* x, float* cond, StreamCtl* ctl, cudaStream_t s,
+                        bool pdl);
+// per-patch epilogue: latents[ctl->patch] = x; patch and step counters advance.
+void launch_patch_end(const float* x, float* latents, int per_patch, StreamCtl* ctl,
+                      cudaStream_t s, bool pdl);
+
+// VoxCPM2SDPA layer contract (fp32, any src rows, optional mask and cache concat).
+void launch_sdpa_rows_f32(const float* q, int heads, int src, int d, const float* k,
+                          const float* v, int groups, int cur, int dv, const float* mask,
+                          int mask_c, const float* past_k, const float* past_v, int past,
+                          float scale, float* out, cudaStream_t s);
+void launch_concat_kv(const float* past, const float* cur, int groups, int past_len, int cur_len,
+                      int d, float* out, cudaStream_t s);
+
+// Raise the dynamic shared-memory limit of the kernels that need more than 48 KB
+// (call once per device, outside stream capture).
+void init_kernel_attributes();
+
+}  // namespace vxc

@@ -1,0 +1,1579 @@
+// Host runtime and C ABI of libvoxcpm2_cuda.
+//
+// Mirrors the reference's host side for the patch loop: Synthesizer::Impl's
+// generate_with_caches (src/synthesizer.cpp:353-659), cfm_sample (:86-170),
+// the RoPE tables (:928-974) and run_decoder_with_kv (src/kvcache.cpp:232-279),
+// with every ncnn graph replaced by sm_100a kernels and each patch iteration
+// captured once as a CUDA graph (positions come from a device control block,
+// so the same graph is replayed for every patch).
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstring>
+#include <initializer_list>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <new>
+#include <numbers>
+#include <random>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/voxcpm2_cuda.h"
+#include "kernels.cuh"
+
+using namespace vxc;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+struct InvalidState : std::runtime_error {
+    using std::runtime_error::runtime_error;
+};
+struct Cancelled : std::runtime_error {
+    Cancelled() : std::runtime_error("operation cancelled") {}
+};
+struct DeviceOom : std::runtime_error {
+    using std::runtime_error::runtime_error;
+};
+
+void ck(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return;
+    cudaGetLastError();
+    if (e == cudaErrorMemoryAllocation) throw DeviceOom(std::string(what) + ": " + cudaGetErrorString(e));
+    throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// Exceptions -> status codes, as guard() in src/c_api.cpp:168-193.
+template <typename F>
+int32_t guard(F&& f) noexcept {
+    try {
+        f();
+        return VXC_STATUS_OK;
+    } catch (const Cancelled& e) {
+        g_last_error = e.what();
+        return VXC_STATUS_CANCELLED;
+    } catch (const InvalidState& e) {
+        g_last_error = e.what();
+        return VXC_STATUS_INVALID_STATE;
+    } catch (const std::invalid_argument& e) {
+        g_last_error = e.what();
+        return VXC_STATUS_INVALID_ARGUMENT;
+    } catch (const DeviceOom& e) {
+        g_last_error = e.what();
+        return VXC_STATUS_OUT_OF_MEMORY;
+    } catch (const std::bad_alloc&) {
+        g_last_error = "native allocation failed";
+        return VXC_STATUS_OUT_OF_MEMORY;
+    } catch (const std::exception& e) {
+        g_last_error = e.what();
+        return VXC_STATUS_RUNTIME_ERROR;
+    } catch (...) {
+        g_last_error = "unknown native exception";
+        return VXC_STATUS_RUNTIME_ERROR;
+    }
+}
+
+void require(bool ok, const char* msg) {
+    if (!ok) throw std::invalid_argument(msg);
+}
+
+// ------------------------------------------------------------ weights ----
+struct LayerW {
+    const __half *in_norm, *wqkv, *wo, *post_norm, *wgateup, *wdown;
+};
+struct DecoderShape {
+    int h, f, hq, hkv, d, layers;
+};
+
+size_t decoder_count(const DecoderShape& s) {
+    const size_t H = s.h, F = s.f, Q = static_cast<size_t>(s.hq) * s.d, KV = static_cast<size_t>(s.hkv) * s.d;
+    return static_cast<size_t>(s.layers) * (H + Q * H + 2 * KV * H + H * Q + H + 2 * F * H + H * F) + H;
+}
+
+// The decoder blob stores per layer: input_norm, q, k, v, o, post_norm, gate,
+// up, down (voxcpm2_b200/config.py). q/k/v are consecutive row blocks, i.e. one
+// fused [(hq + 2 hkv) d][H] matrix; gate/up likewise form one [2F][H] matrix.
+std::vector<LayerW> carve_decoder(const __half* base, const DecoderShape& s, const __half** final_norm) {
+    const size_t H = s.h, F = s.f, Q = static_cast<size_t>(s.hq) * s.d, KV = static_cast<size_t>(s.hkv) * s.d;
+    std::vector<LayerW> out;
+    size_t off = 0;
+    for (int l = 0; l < s.layers; ++l) {
+        LayerW L{};
+        L.in_norm = base + off;
+        off += H;
+        L.wqkv = base + off;
+        off += (Q + 2 * KV) * H;
+        L.wo = base + off;
+        off += H * Q;
+        L.post_norm = base + off;
+        off += H;
+        L.wgateup = base + off;
+        off += 2 * F * H;
+        L.wdown = base + off;
+        off += H * F;
+        out.push_back(L);
+    }
+    *final_norm = base + off;
+    return out;
+}
+
+DecoderShape base_shape(const vxc_model_desc& d) {
+    return {d.hidden, d.ffn, d.q_heads, d.kv_heads, d.head_dim, d.base_layers};
+}
+DecoderShape res_shape(const vxc_model_desc& d) {
+    return {d.hidden, d.ffn, d.q_heads, d.kv_heads, d.head_dim, d.res_layers};
+}
+DecoderShape dit_shape(const vxc_model_desc& d) {
+    return {d.dit_hidden, d.dit_ffn, d.dit_q_heads, d.dit_kv_heads, d.dit_hidden / d.dit_q_heads, d.dit_layers};
+}
+
+size_t component_count(const vxc_model_desc& d, int c) {
+    const size_t H = d.hidden, Hd = d.dit_hidden, D = d.feat_dim, P = d.patch_size, Q = d.fsq_dim;
+    switch (c) {
+        case VXC_TEXT_EMBED: return static_cast<size_t>(d.vocab) * H;
+        case VXC_BASE_DECODER: return decoder_count(base_shape(d));
+        case VXC_RESIDUAL_DECODER: return decoder_count(res_shape(d));
+        case VXC_FSQ: return Q * H + Q + H * Q + H;
+        case VXC_FUSION_PROJ: return H * 2 * H + H;
+        case VXC_DIT_PROJ: return 2 * (Hd * H + Hd);
+        case VXC_STOP_HEAD: return H * H + H + 2 * H;
+        case VXC_FEAT_ENCODER: return H * (P * D) + H + H * H + H;
+        case VXC_DIT_ESTIMATOR:
+            return 2 * (Hd * D + Hd) + 4 * (Hd * Hd + Hd) + decoder_count(dit_shape(d)) + D * Hd + D;
+        default: return 0;
+    }
+}
+
+void validate_desc(const vxc_model_desc& d) {
+    require(d.hidden > 0 && d.hidden % 8 == 0, "hidden must be a positive multiple of 8");
+    require(d.ffn > 0 && d.ffn % 8 == 0, "ffn must be a positive multiple of 8");
+    require(d.head_dim == 64, "head_dim must be 64");
+    require(d.q_heads > 0 && d.kv_heads > 0 && d.q_heads % d.kv_heads == 0 && d.q_heads / d.kv_heads <= 16,
+            "q_heads must be a multiple of kv_heads (group <= 16)");
+    require(d.base_layers > 0 && d.res_layers > 0 && d.dit_layers > 0, "layer counts must be positive");
+    require(d.dit_hidden > 0 && d.dit_hidden % 8 == 0 && d.dit_q_heads > 0 &&
+                d.dit_hidden % d.dit_q_heads == 0 && d.dit_hidden / d.dit_q_heads == 64,
+            "dit head_dim must be 64");
+    require(d.dit_kv_heads > 0 && d.dit_q_heads % d.dit_kv_heads == 0, "dit heads must group");
+    require(d.dit_ffn > 0 && d.dit_ffn % 8 == 0, "dit_ffn must be a positive multiple of 8");
+    require(d.feat_dim > 0 && d.patch_size > 0 && 2 * d.patch_size <= 8 &&
+                (d.feat_dim * d.patch_size) % 8 == 0,
+            "unsupported patch shape");
+    require(d.fsq_dim > 0 && d.fsq_dim % 8 == 0 && d.fsq_scale > 0.f, "bad fsq shape");
+    require(d.vocab > 0, "vocab must be positive");
+    require(d.rms_eps > 0.f && d.rope_theta > 0.f && d.rope_original_max > 0, "bad norm/rope settings");
+    require(d.hidden <= 4096 && d.ffn <= 4096 && d.dit_hidden <= 4096 && d.dit_ffn <= 4096,
+            "dimensions above 4096 are not supported");
+    require(d.audio_start_token >= 0 && d.audio_start_token < d.vocab, "audio_start_token out of range");
+}
+
+// RoPE tables of Synthesizer::Impl::make_rope_cache (synthesizer.cpp:928-974)
+// with all LongRoPE factors 1: one row per position.
+void rope_table(int head_dim, float theta, int positions, std::vector<float>& cos_t, std::vector<float>& sin_t) {
+    const int half = head_dim / 2;
+    std::vector<float> inv(half);
+    for (int j = 0; j < half; ++j) {
+        const float exponent = (2.0f * static_cast<float>(j)) / static_cast<float>(head_dim);
+        inv[j] = 1.0f / std::pow(theta, exponent);
+    }
+    cos_t.assign(static_cast<size_t>(positions) * head_dim, 0.f);
+    sin_t.assign(cos_t.size(), 0.f);
+    for (int p = 0; p < positions; ++p) {
+        for (int j = 0; j < half; ++j) {
+            const float freq = (static_cast<float>(p) / 1.0f) * inv[j];
+            const float c = std::cos(freq), s = std::sin(freq);
+            cos_t[static_cast<size_t>(p) * head_dim + j] = c;
+            cos_t[static_cast<size_t>(p) * head_dim + j + half] = c;
+            sin_t[static_cast<size_t>(p) * head_dim + j] = s;
+            sin_t[static_cast<size_t>(p) * head_dim + j + half] = s;
+        }
+    }
+}
+
+// Euler dt of each estimator step in cfm_sample's float arithmetic
+// (synthesizer.cpp:49-60, 121-167): dts[step] for step = 1..T.
+std::vector<float> euler_dts(int T) {
+    std::vector<float> t_span(static_cast<size_t>(T) + 1);
+    for (int i = 0; i <= T; ++i) {
+        const float t = 1.0f - static_cast<float>(i) / static_cast<float>(T);
+        t_span[i] = t + (std::cos(std::numbers::pi_v<float> * 0.5f * t) - 1.0f + t);
+    }
+    std::vector<float> dts(static_cast<size_t>(T) + 1, 0.f);
+    float t = t_span[0];
+    float dt = t_span[0] - (T >= 1 ? t_span[1] : 0.f);
+    for (int step = 1; step <= T; ++step) {
+        dts[step] = dt;
+        t -= dt;
+        if (step < T) dt = t - t_span[static_cast<size_t>(step) + 1];
+    }
+    return dts;
+}
+
+int zero_init_steps(int T) { return std::max(1, static_cast<int>((T + 1) * 0.04f)); }
+
+int max_patches_for_target(int target_text_tokens, int hard_cap) {
+    const int text_tokens = std::max(1, target_text_tokens);
+    const int cap = static_cast<int>(static_cast<float>(text_tokens) * 6.0f + 10.0f);
+    return std::max(1, std::min(hard_cap, cap));
+}
+
+template <typename T>
+T* dev_alloc(size_t n) {
+    void* p = nullptr;
+    ck(cudaMalloc(&p, std::max<size_t>(n, 1) * sizeof(T)), "cudaMalloc");
+    return static_cast<T*>(p);
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        ck(cudaSetDevice(dev), "cudaSetDevice");
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+constexpr int dit_tokens_per_seq(int P) { return 3 + 2 * P; }
+
+}  // namespace
+
+// =================================================================== device ==
+struct vxc_device {
+    int device = 0;
+    vxc_model_desc desc{};
+    __half* blob[9] = {};
+    bool loaded[9] = {};
+    std::vector<LayerW> base, res, dit;
+    const __half *base_norm = nullptr, *res_norm = nullptr, *dit_norm = nullptr;
+    float *dit_rope_cos = nullptr, *dit_rope_sin = nullptr;  // positions 0..seq-1
+};
+
+namespace {
+
+struct DitPtrs {
+    const __half *in_w, *in_b, *cond_w, *cond_b, *t1_w, *t1_b, *t2_w, *t2_b, *dt1_w, *dt1_b, *dt2_w, *dt2_b;
+    const __half *out_w, *out_b;
+};
+
+DitPtrs dit_ptrs(const vxc_device* dev) {
+    const vxc_model_desc& d = dev->desc;
+    const size_t Hd = d.dit_hidden, D = d.feat_dim;
+    const __half* p = dev->blob[VXC_DIT_ESTIMATOR];
+    DitPtrs w{};
+    w.in_w = p; p += Hd * D;
+    w.in_b = p; p += Hd;
+    w.cond_w = p; p += Hd * D;
+    w.cond_b = p; p += Hd;
+    w.t1_w = p; p += Hd * Hd;
+    w.t1_b = p; p += Hd;
+    w.t2_w = p; p += Hd * Hd;
+    w.t2_b = p; p += Hd;
+    w.dt1_w = p; p += Hd * Hd;
+    w.dt1_b = p; p += Hd;
+    w.dt2_w = p; p += Hd * Hd;
+    w.dt2_b = p; p += Hd;
+    p += decoder_count(dit_shape(d));
+    w.out_w = p; p += D * Hd;
+    w.out_b = p;
+    return w;
+}
+
+}  // namespace
+
+// =================================================================== stream ==
+struct vxc_stream {
+    vxc_device* dev = nullptr;
+    cudaStream_t cs = nullptr;
+    int cap = 0;
+    int splits = 16;
+    std::mutex call_mutex;  // serialises calls on one stream (src/c_api.cpp:234-283)
+    std::atomic<bool> cancel{false};
+
+    StreamCtl* ctl = nullptr;       // device
+    StreamCtl* ctl_host = nullptr;  // pinned mirror
+    __half *kc[2] = {}, *vc[2] = {};
+    float *rope_cos = nullptr, *rope_sin = nullptr;
+    // batch-1 step buffers
+    float *h[2] = {}, *out[2] = {}, *q = nullptr, *attn = nullptr, *act = nullptr;
+    float *lm_h = nullptr, *res_h = nullptr, *feat = nullptr, *mid = nullptr, *mid2 = nullptr;
+    float* partial = nullptr;
+    int* counters = nullptr;
+    // CFM / DiT buffers
+    float *mu = nullptr, *x = nullptr, *cond = nullptr, *cond0 = nullptr, *noise = nullptr, *latents = nullptr;
+    float *temb = nullptr, *tmid = nullptr, *ttok = nullptr, *dtemb = nullptr, *dtmid = nullptr, *dttok = nullptr;
+    float *dtemb1 = nullptr, *dtmid1 = nullptr, *dttok1 = nullptr;
+    float *dh = nullptr, *dxn = nullptr, *dqkv = nullptr, *dattn = nullptr, *dact = nullptr, *est = nullptr;
+    float* gen_in = nullptr;  // staging for generic calls
+    float* pin = nullptr;     // pinned host staging
+    // prefill buffers (grown on demand)
+    int pre_rows = 0;
+    float *ph = nullptr, *pxn = nullptr, *pqkv = nullptr, *pattn = nullptr, *pact = nullptr, *pcat = nullptr;
+    int32_t* pids = nullptr;
+
+    // host mirror
+    int kv_len[2] = {0, 0};
+    int patches = 0;
+    int prefix_len = 0;
+    bool prefilled = false;
+    int graph_T = -1;
+    float graph_cfg = 0.f;
+    cudaGraphExec_t graph = nullptr;
+    int min_patches_dev = -1;
+
+    ~vxc_stream();
+};
+
+namespace {
+
+void free_all(vxc_stream* s) {
+    if (s->graph) cudaGraphExecDestroy(s->graph);
+    s->graph = nullptr;
+    void* ptrs[] = {s->ctl, s->kc[0], s->kc[1], s->vc[0], s->vc[1], s->rope_cos, s->rope_sin, s->h[0], s->h[1],
+                    s->out[0], s->out[1], s->q, s->attn, s->act, s->lm_h, s->res_h, s->feat, s->mid, s->mid2,
+                    s->partial, s->counters, s->mu, s->x, s->cond, s->cond0, s->noise, s->latents, s->temb,
+                    s->tmid, s->ttok, s->dtemb, s->dtmid, s->dttok, s->dtemb1, s->dtmid1, s->dttok1, s->dh,
+                    s->dxn, s->dqkv, s->dattn, s->dact, s->est, s->gen_in, s->ph, s->pxn, s->pqkv, s->pattn,
+                    s->pact, s->pcat, s->pids};
+    for (void* p : ptrs)
+        if (p) cudaFree(p);
+    if (s->ctl_host) cudaFreeHost(s->ctl_host);
+    if (s->pin) cudaFreeHost(s->pin);
+    if (s->cs) cudaStreamDestroy(s->cs);
+}
+
+void check_loaded(const vxc_device* dev, std::initializer_list<int> comps) {
+    for (int c : comps)
+        if (!dev->loaded[c]) throw InvalidState("weights of a required component are not loaded");
+}
+
+GemvArgs plain_gemv(const __half* w, const __half* b, const float* x, int K, int rows, float* y, int act,
+                    StreamCtl* ctl, int skip) {
+    GemvArgs a;
+    a.mode = GEMV_PLAIN;
+    a.w = w;
+    a.bias = b;
+    a.x = x;
+    a.K = K;
+    a.rows = rows;
+    a.y = y;
+    a.act = act;
+    a.ctl = ctl;
+    a.skip_if_stopped = skip;
+    return a;
+}
+
+// ----------------------------------------------------------- enqueue ------
+// Batch-1 decoder step over s->h[which] (the residual stream, already holding
+// the input embedding); writes the final-norm output to out (+ out2) and bumps
+// kv_len[which] on the device.
+void enqueue_decoder_step(vxc_stream* s, int which, float* out, float* out2, int skip) {
+    const vxc_device* dev = s->dev;
+    const vxc_model_desc& d = dev->desc;
+    const std::vector<LayerW>& layers = which == 0 ? dev->base : dev->res;
+    const __half* fnorm = which == 0 ? dev->base_norm : dev->res_norm;
+    const float rscale = which == 0 ? d.base_residual_scale : d.res_residual_scale;
+    const int H = d.hidden, F = d.ffn, hq = d.q_heads, hkv = d.kv_heads, hd = d.head_dim;
+    const size_t plane = static_cast<size_t>(hkv) * s->cap * hd;
+    for (size_t l = 0; l < layers.size(); ++l) {
+        const LayerW& L = layers[l];
+        GemvArgs qa;
+        qa.mode = GEMV_QKV;
+        qa.w = L.wqkv;
+        qa.x = s->h[which];
+        qa.norm_g = L.in_norm;
+        qa.eps = d.rms_eps;
+        qa.K = H;
+        qa.rows = (hq + 2 * hkv) * hd / 2;
+        qa.y = s->q;
+        qa.q_heads = hq;
+        qa.kv_heads = hkv;
+        qa.head_dim = hd;
+        qa.rope_cos = which == 0 ? s->rope_cos : nullptr;
+        qa.rope_sin = which == 0 ? s->rope_sin : nullptr;
+        qa.k_cache = s->kc[which] + l * plane;
+        qa.v_cache = s->vc[which] + l * plane;
+        qa.cap = s->cap;
+        qa.which = which;
+        qa.ctl = s->ctl;
+        qa.skip_if_stopped = skip;
+        launch_gemv(qa, s->cs, true);
+
+        AttnArgs aa;
+        aa.q = s->q;
+        aa.k0 = s->kc[which] + l * plane;
+        aa.v0 = s->vc[which] + l * plane;
+        aa.len0 = s->cap;
+        aa.stride0 = s->cap;
+        aa.q_heads = hq;
+        aa.kv_heads = hkv;
+        aa.head_dim = hd;
+        aa.scale = 1.0f / std::sqrt(static_cast<float>(hd));
+        aa.splits = s->splits;
+        aa.partial = s->partial;
+        aa.counters = s->counters;
+        aa.out = s->attn;
+        aa.ctl = s->ctl;
+        aa.which = which;
+        aa.skip_if_stopped = skip;
+        launch_attn_decode(aa, true, s->cs, true);
+
+        GemvArgs oa;
+        oa.mode = GEMV_RESID;
+        oa.w = L.wo;
+        oa.x = s->attn;
+        oa.K = hq * hd;
+        oa.rows = H;
+        oa.resid = s->h[which];
+        oa.rscale = rscale;
+        oa.ctl = s->ctl;
+        oa.skip_if_stopped = skip;
+        launch_gemv(oa, s->cs, true);
+
+        GemvArgs ga;
+        ga.mode = GEMV_GATEUP;
+        ga.w = L.wgateup;
+        ga.x = s->h[which];
+        ga.norm_g = L.post_norm;
+        ga.eps = d.rms_eps;
+        ga.K = H;
+        ga.rows = F;
+        ga.y = s->act;
+        ga.ctl = s->ctl;
+        ga.skip_if_stopped = skip;
+        launch_gemv(ga, s->cs, true);
+
+        GemvArgs da;
+        da.mode = GEMV_RESID;
+        da.w = L.wdown;
+        da.x = s->act;
+        da.K = F;
+        da.rows = H;
+        da.resid = s->h[which];
+        da.rscale = rscale;
+        da.ctl = s->ctl;
+        da.skip_if_stopped = skip;
+        launch_gemv(da, s->cs, true);
+    }
+    launch_final_norm(s->h[which], fnorm, d.rms_eps, H, out, out2, s->ctl, which, 1, skip, s->cs, true);
+}
+
+// DiT decoder over the 2 x seq rows in s->dh.
+void enqueue_dit_layers(vxc_stream* s, StreamCtl* ctl) {
+    const vxc_device* dev = s->dev;
+    const vxc_model_desc& d = dev->desc;
+    const int Hd = d.dit_hidden, F = d.dit_ffn, hq = d.dit_q_heads, hkv = d.dit_kv_heads, hd = Hd / hq;
+    const int seq = dit_tokens_per_seq(d.patch_size), M = 2 * seq;
+    const int wqkv = (hq + 2 * hkv) * hd;
+    const int sk = ctl ? 1 : 0;
+    for (const LayerW& L : dev->dit) {
+        launch_rmsnorm_rows(s->dh, Hd, L.in_norm, d.rms_eps, Hd, M, s->dxn, Hd, ctl, sk, s->cs, true);
+        RowsArgs qa;
+        qa.w = L.wqkv;
+        qa.x = s->dxn;
+        qa.ldx = Hd;
+        qa.K = Hd;
+        qa.rows = wqkv;
+        qa.M = M;
+        qa.y = s->dqkv;
+        qa.ldy = wqkv;
+        qa.ctl = ctl;
+        qa.skip_if_stopped = sk;
+        launch_rows_linear(qa, s->cs, true);
+        launch_qkv_rows_post(s->dqkv, M, hq, hkv, hd, 0, seq, dev->dit_rope_cos, dev->dit_rope_sin, nullptr,
+                             nullptr, 0, ctl, s->cs, true);
+        launch_dit_attention(s->dqkv, 2, seq, hq, hkv, hd, 1.0f / std::sqrt(static_cast<float>(hd)), s->dattn,
+                             ctl, s->cs, true);
+        RowsArgs oa;
+        oa.w = L.wo;
+        oa.x = s->dattn;
+        oa.ldx = hq * hd;
+        oa.K = hq * hd;
+        oa.rows = Hd;
+        oa.M = M;
+        oa.mode = GEMV_RESID;
+        oa.rscale = d.dit_residual_scale;
+        oa.y = s->dh;
+        oa.ldy = Hd;
+        oa.ctl = ctl;
+        oa.skip_if_stopped = sk;
+        launch_rows_linear(oa, s->cs, true);
+        launch_rmsnorm_rows(s->dh, Hd, L.post_norm, d.rms_eps, Hd, M, s->dxn, Hd, ctl, sk, s->cs, true);
+        RowsArgs ga;
+        ga.w = L.wgateup;
+        ga.x = s->dxn;
+        ga.ldx = Hd;
+        ga.K = Hd;
+        ga.rows = F;
+        ga.M = M;
+        ga.mode = GEMV_GATEUP;
+        ga.y = s->dact;
+        ga.ldy = F;
+        ga.ctl = ctl;
+        ga.skip_if_stopped = sk;
+        launch_rows_linear(ga, s->cs, true);
+        RowsArgs da;
+        da.w = L.wdown;
+        da.x = s->dact;
+        da.ldx = F;
+        da.K = F;
+        da.rows = Hd;
+        da.M = M;
+        da.mode = GEMV_RESID;
+        da.rscale = d.dit_residual_scale;
+        da.y = s->dh;
+        da.ldy = Hd;
+        da.ctl = ctl;
+        da.skip_if_stopped = sk;
+        launch_rows_linear(da, s->cs, true);
+    }
+}
+
+// time_mlp(emb(t)) for estimator step 'step_index' (schedule mode) into
+// s->ttok, and delta_time_mlp(emb(dt)) rows into s->dttok / s->dttok1.
+void enqueue_time_tokens(vxc_stream* s, float step_index, float T, const float* dt_raw, StreamCtl* ctl) {
+    const vxc_model_desc& d = s->dev->desc;
+    const DitPtrs w = dit_ptrs(s->dev);
+    const int Hd = d.dit_hidden;
+    const int sk = ctl ? 1 : 0;
+    launch_timestep_embedding(step_index, T, 1, Hd / 2, s->temb, ctl, s->cs, true);
+    launch_gemv(plain_gemv(w.t1_w, w.t1_b, s->temb, Hd, Hd, s->tmid, ACT_SILU, ctl, sk), s->cs, true);
+    launch_gemv(plain_gemv(w.t2_w, w.t2_b, s->tmid, Hd, Hd, s->ttok, ACT_NONE, ctl, sk), s->cs, true);
+    launch_timestep_embedding(dt_raw[0], 0.f, 0, Hd / 2, s->dtemb, ctl, s->cs, true);
+    launch_gemv(plain_gemv(w.dt1_w, w.dt1_b, s->dtemb, Hd, Hd, s->dtmid, ACT_SILU, ctl, sk), s->cs, true);
+    launch_gemv(plain_gemv(w.dt2_w, w.dt2_b, s->dtmid, Hd, Hd, s->dttok, ACT_NONE, ctl, sk), s->cs, true);
+    if (dt_raw[1] != dt_raw[0]) {
+        launch_timestep_embedding(dt_raw[1], 0.f, 0, Hd / 2, s->dtemb1, ctl, s->cs, true);
+        launch_gemv(plain_gemv(w.dt1_w, w.dt1_b, s->dtemb1, Hd, Hd, s->dtmid1, ACT_SILU, ctl, sk), s->cs, true);
+        launch_gemv(plain_gemv(w.dt2_w, w.dt2_b, s->dtmid1, Hd, Hd, s->dttok1, ACT_NONE, ctl, sk), s->cs, true);
+    }
+}
+
+// One estimator evaluation + (if x_update) the CFG-zero* Euler update.
+void enqueue_dit_eval(vxc_stream* s, const float* x, const float* x_unc, const float* mu, const float* mu_unc,
+                      const float* cond, const float* cond_unc, bool dt_rows_differ, float* est_out,
+                      float* x_update, float dt, float cfg, StreamCtl* ctl) {
+    const vxc_model_desc& d = s->dev->desc;
+    const DitPtrs w = dit_ptrs(s->dev);
+    DitEmbedArgs e{};
+    e.in_w = w.in_w;
+    e.in_b = w.in_b;
+    e.cond_w = w.cond_w;
+    e.cond_b = w.cond_b;
+    e.x = x;
+    e.cond = cond;
+    e.mu = mu;
+    e.t_tok0 = s->ttok;
+    e.t_tok1 = s->ttok;
+    e.dt_tok0 = s->dttok;
+    e.dt_tok1 = dt_rows_differ ? s->dttok1 : s->dttok;
+    e.Hd = d.dit_hidden;
+    e.D = d.feat_dim;
+    e.P = d.patch_size;
+    e.hidden = s->dh;
+    e.ctl = ctl;
+    e.mu_uncond = mu_unc;
+    e.x_uncond = x_unc;
+    e.cond_uncond = cond_unc;
+    launch_dit_embed(e, s->cs, true);
+    enqueue_dit_layers(s, ctl);
+    DitOutArgs o{};
+    o.hidden = s->dh;
+    o.seq = dit_tokens_per_seq(d.patch_size);
+    o.Hd = d.dit_hidden;
+    o.D = d.feat_dim;
+    o.P = d.patch_size;
+    o.norm_g = s->dev->dit_norm;
+    o.eps = d.rms_eps;
+    o.out_w = w.out_w;
+    o.out_b = w.out_b;
+    o.est_out = est_out;
+    o.x = x_update;
+    o.dt = dt;
+    o.cfg = cfg;
+    o.ctl = ctl;
+    launch_dit_out(o, s->cs, true);
+}
+
+// cfm_sample over s->x (holding the noise), mu = s->mu (row 1 of mu_in stays
+// zero: the unconditional CFG branch, synthesizer.cpp:52, 114).
+void enqueue_cfm(vxc_stream* s, const float* cond_dev, int T, float cfg) {
+    const std::vector<float> dts = euler_dts(T);
+    const int z = zero_init_steps(T);
+    const float dt0[2] = {0.f, 0.f};
+    for (int step = 1; step <= T; ++step) {
+        if (step <= z) continue;  // zero-init steps leave x untouched (synthesizer.cpp:123-126)
+        enqueue_time_tokens(s, static_cast<float>(step - 1), static_cast<float>(T), dt0, s->ctl);
+        enqueue_dit_eval(s, s->x, nullptr, s->mu, nullptr, cond_dev, nullptr, false, nullptr, s->x, dts[step], cfg,
+                         s->ctl);
+    }
+}
+
+// The whole patch iteration (synthesizer.cpp:546-658) on s->cs.
+void enqueue_patch(vxc_stream* s, int T, float cfg) {
+    const vxc_device* dev = s->dev;
+    const vxc_model_desc& d = dev->desc;
+    const int H = d.hidden, Hd = d.dit_hidden, L = d.feat_dim * d.patch_size;
+    launch_patch_begin(s->noise, s->latents, s->cond0, L, s->x, s->cond, s->ctl, s->cs, true);
+    // dit_proj: cat(lm_to_dit_proj(lm), res_to_dit_proj(res))
+    const __half* dp = dev->blob[VXC_DIT_PROJ];
+    const size_t dps = static_cast<size_t>(Hd) * H;
+    launch_gemv(plain_gemv(dp, dp + dps, s->lm_h, H, Hd, s->mu, ACT_NONE, s->ctl, 0), s->cs, true);
+    launch_gemv(plain_gemv(dp + dps + Hd, dp + 2 * dps + Hd, s->res_h, H, Hd, s->mu + Hd, ACT_NONE, s->ctl, 0),
+                s->cs, true);
+    enqueue_cfm(s, s->cond, T, cfg);
+    // stop head on the hidden state entering this patch
+    const __half* sh = dev->blob[VXC_STOP_HEAD];
+    launch_gemv(plain_gemv(sh, sh + static_cast<size_t>(H) * H, s->lm_h, H, H, s->mid, ACT_SILU, s->ctl, 0), s->cs,
+                true);
+    launch_stop_decide(sh + static_cast<size_t>(H) * H + H, s->mid, H, s->ctl, nullptr, s->cs, true);
+    // feat_encoder(latent) -> feat and the base decoder input
+    const __half* fe = dev->blob[VXC_FEAT_ENCODER];
+    const size_t fin = static_cast<size_t>(H) * L;
+    GemvArgs fa = plain_gemv(fe, fe + fin, s->x, L, H, s->mid2, ACT_SILU, s->ctl, 1);
+    fa.in_mode = IN_LATENT_T;
+    fa.lat_d = d.feat_dim;
+    fa.lat_p = d.patch_size;
+    launch_gemv(fa, s->cs, true);
+    GemvArgs fb = plain_gemv(fe + fin + H, fe + fin + H + static_cast<size_t>(H) * H, s->mid2, H, H, s->feat,
+                             ACT_NONE, s->ctl, 1);
+    fb.y2 = s->h[0];
+    launch_gemv(fb, s->cs, true);
+    enqueue_decoder_step(s, 0, s->out[0], nullptr, 1);
+    // fsq
+    const __half* fq = dev->blob[VXC_FSQ];
+    const size_t Q = d.fsq_dim;
+    GemvArgs qa = plain_gemv(fq, fq + Q * H, s->out[0], H, static_cast<int>(Q), s->mid, ACT_FSQ, s->ctl, 1);
+    qa.act_scale = d.fsq_scale;
+    launch_gemv(qa, s->cs, true);
+    launch_gemv(plain_gemv(fq + Q * H + Q, fq + Q * H + Q + H * Q, s->mid, static_cast<int>(Q), H, s->lm_h, ACT_NONE,
+                           s->ctl, 1),
+                s->cs, true);
+    // fusion_proj(cat(lm, feat)) -> residual decoder input
+    const __half* fu = dev->blob[VXC_FUSION_PROJ];
+    GemvArgs ua = plain_gemv(fu, fu + static_cast<size_t>(H) * 2 * H, s->lm_h, 2 * H, H, s->h[1], ACT_NONE, s->ctl, 1);
+    ua.in_mode = IN_CONCAT;
+    ua.x2 = s->feat;
+    ua.k1 = H;
+    launch_gemv(ua, s->cs, true);
+    enqueue_decoder_step(s, 1, s->res_h, nullptr, 1);
+    launch_patch_end(s->x, s->latents, L, s->ctl, s->cs, true);
+}
+
+void sync_ctl(vxc_stream* s) {
+    ck(cudaMemcpyAsync(s->ctl_host, s->ctl, sizeof(StreamCtl), cudaMemcpyDeviceToHost, s->cs), "ctl readback");
+    ck(cudaStreamSynchronize(s->cs), "cudaStreamSynchronize");
+    const int err = s->ctl_host->error;
+    if (err != 0) {
+        s->ctl_host->error = 0;
+        cudaMemcpyAsync(&s->ctl->error, &s->ctl_host->error, sizeof(int), cudaMemcpyHostToDevice, s->cs);
+        cudaStreamSynchronize(s->cs);
+        if (err == 1) throw std::runtime_error("KV cache capacity exceeded on the device");
+        if (err == 2) throw std::runtime_error("dit_estimator produced non-finite values");
+        throw std::runtime_error("device-side check failed");
+    }
+    s->kv_len[0] = s->ctl_host->kv_len[0];
+    s->kv_len[1] = s->ctl_host->kv_len[1];
+    s->patches = s->ctl_host->patch;
+}
+
+void write_ctl(vxc_stream* s) {
+    ck(cudaMemcpyAsync(s->ctl, s->ctl_host, sizeof(StreamCtl), cudaMemcpyHostToDevice, s->cs), "ctl upload");
+    ck(cudaStreamSynchronize(s->cs), "cudaStreamSynchronize");
+}
+
+void ensure_prefill_rows(vxc_stream* s, int n) {
+    if (n <= s->pre_rows) return;
+    const vxc_model_desc& d = s->dev->desc;
+    for (float* p : {s->ph, s->pxn, s->pqkv, s->pattn, s->pact, s->pcat})
+        if (p) cudaFree(p);
+    if (s->pids) cudaFree(s->pids);
+    s->ph = s->pxn = s->pqkv = s->pattn = s->pact = s->pcat = nullptr;
+    s->pids = nullptr;
+    s->pre_rows = 0;
+    const size_t H = d.hidden, F = d.ffn, W = static_cast<size_t>(d.q_heads + 2 * d.kv_heads) * d.head_dim;
+    s->ph = dev_alloc<float>(n * H);
+    s->pxn = dev_alloc<float>(n * H);
+    s->pqkv = dev_alloc<float>(n * W);
+    s->pattn = dev_alloc<float>(n * static_cast<size_t>(d.q_heads) * d.head_dim);
+    s->pact = dev_alloc<float>(n * F);
+    s->pcat = dev_alloc<float>(n * 2 * H);
+    s->pids = dev_alloc<int32_t>(n);
+    s->pre_rows = n;
+}
+
+// Multi-row decoder call (prefill): rows already in s->ph; out [n][H] device.
+void run_decoder_rows(vxc_stream* s, int which, int n, float* out_dev) {
+    const vxc_device* dev = s->dev;
+    const vxc_model_desc& d = dev->desc;
+    const std::vector<LayerW>& layers = which == 0 ? dev->base : dev->res;
+    const __half* fnorm = which == 0 ? dev->base_norm : dev->res_norm;
+    const float rscale = which == 0 ? d.base_residual_scale : d.res_residual_scale;
+    const int H = d.hidden, F = d.ffn, hq = d.q_heads, hkv = d.kv_heads, hd = d.head_dim;
+    const int W = (hq + 2 * hkv) * hd;
+    const int past = s->kv_len[which];
+    const size_t plane = static_cast<size_t>(hkv) * s->cap * hd;
+    for (size_t l = 0; l < layers.size(); ++l) {
+        const LayerW& L = layers[l];
+        launch_rmsnorm_rows(s->ph, H, L.in_norm, d.rms_eps, H, n, s->pxn, H, nullptr, 0, s->cs, false);
+        RowsArgs qa;
+        qa.w = L.wqkv;
+        qa.x = s->pxn;
+        qa.ldx = H;
+        qa.K = H;
+        qa.rows = W;
+        qa.M = n;
+        qa.y = s->pqkv;
+        qa.ldy = W;
+        launch_rows_linear(qa, s->cs, false);
+        launch_qkv_rows_post(s->pqkv, n, hq, hkv, hd, past, 1 << 30, which == 0 ? s->rope_cos : nullptr,
+                             which == 0 ? s->rope_sin : nullptr, s->kc[which] + l * plane, s->vc[which] + l * plane,
+                             s->cap, s->ctl, s->cs, false);
+        launch_attn_rows_cache(s->pqkv, n, hq, hkv, hd, past, s->kc[which] + l * plane, s->vc[which] + l * plane,
+                               s->cap, 1.0f / std::sqrt(static_cast<float>(hd)), s->pattn, s->cs, false);
+        RowsArgs oa;
+        oa.w = L.wo;
+        oa.x = s->pattn;
+        oa.ldx = hq * hd;
+        oa.K = hq * hd;
+        oa.rows = H;
+        oa.M = n;
+        oa.mode = GEMV_RESID;
+        oa.rscale = rscale;
+        oa.y = s->ph;
+        oa.ldy = H;
+        launch_rows_linear(oa, s->cs, false);
+        launch_rmsnorm_rows(s->ph, H, L.post_norm, d.rms_eps, H, n, s->pxn, H, nullptr, 0, s->cs, false);
+        RowsArgs ga;
+        ga.w = L.wgateup;
+        ga.x = s->pxn;
+        ga.ldx = H;
+        ga.K = H;
+        ga.rows = F;
+        ga.M = n;
+        ga.mode = GEMV_GATEUP;
+        ga.y = s->pact;
+        ga.ldy = F;
+        launch_rows_linear(ga, s->cs, false);
+        RowsArgs da;
+        da.w = L.wdown;
+        da.x = s->pact;
+        da.ldx = F;
+        da.K = F;
+        da.rows = H;
+        da.M = n;
+        da.mode = GEMV_RESID;
+        da.rscale = rscale;
+        da.y = s->ph;
+        da.ldy = H;
+        launch_rows_linear(da, s->cs, false);
+    }
+    launch_rmsnorm_rows(s->ph, H, fnorm, d.rms_eps, H, n, out_dev, H, nullptr, 0, s->cs, false);
+    s->ctl_host->kv_len[which] = past + n;
+    ck(cudaMemcpyAsync(&s->ctl->kv_len[which], &s->ctl_host->kv_len[which], sizeof(int), cudaMemcpyHostToDevice,
+                       s->cs),
+       "kv_len update");
+    ck(cudaStreamSynchronize(s->cs), "cudaStreamSynchronize");
+    s->kv_len[which] = past + n;
+}
+
+void decoder_call(vxc_stream* s, int which, const float* embed, int n, float* out) {
+    const vxc_model_desc& d = s->dev->desc;
+    const int H = d.hidden;
+    check_loaded(s->dev, {which == 0 ? VXC_BASE_DECODER : VXC_RESIDUAL_DECODER});
+    if (s->kv_len[which] + n > s->cap) throw std::invalid_argument("decoder KV cache capacity exceeded");
+    if (n == 1) {
+        ck(cudaMemcpyAsync(s->h[which], embed, sizeof(float) * H, cudaMemcpyHostToDevice, s->cs), "upload");
+        enqueue_decoder_step(s, which, s->out[which], nullptr, 0);
+        ck(cudaMemcpyAsync(out, s->out[which], sizeof(float) * H, cudaMemcpyDeviceToHost, s->cs), "download");
+        sync_ctl(s);
+    } else {
+        ensure_prefill_rows(s, n);
+        ck(cudaMemcpyAsync(s->ph, embed, sizeof(float) * H * n, cudaMemcpyHostToDevice, s->cs), "upload");
+        run_decoder_rows(s, which, n, s->pxn);
+        ck(cudaMemcpy(out, s->pxn, sizeof(float) * H * n, cudaMemcpyDeviceToHost), "download");
+    }
+}
+
+void capture_patch_graph(vxc_stream* s, int T, float cfg) {
+    if (s->graph && s->graph_T == T && s->graph_cfg == cfg) return;
+    if (s->graph) {
+        cudaGraphExecDestroy(s->graph);
+        s->graph = nullptr;
+    }
+    cudaGraph_t g = nullptr;
+    ck(cudaStreamBeginCapture(s->cs, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+    try {
+        enqueue_patch(s, T, cfg);
+    } catch (...) {
+        cudaStreamEndCapture(s->cs, &g);
+        if (g) cudaGraphDestroy(g);
+        throw;
+    }
+    ck(cudaStreamEndCapture(s->cs, &g), "cudaStreamEndCapture");
+    const cudaError_t e = cudaGraphInstantiate(&s->graph, g, 0);
+    cudaGraphDestroy(g);
+    ck(e, "cudaGraphInstantiate");
+    s->graph_T = T;
+    s->graph_cfg = cfg;
+}
+
+void set_min_patches(vxc_stream* s, int min_patches) {
+    if (s->min_patches_dev == min_patches) return;
+    s->ctl_host->min_patches = min_patches;
+    ck(cudaMemcpyAsync(&s->ctl->min_patches, &s->ctl_host->min_patches, sizeof(int), cudaMemcpyHostToDevice, s->cs),
+       "min_patches");
+    ck(cudaStreamSynchronize(s->cs), "sync");
+    s->min_patches_dev = min_patches;
+}
+
+void check_patch_preconditions(vxc_stream* s, int T) {
+    check_loaded(s->dev, {1, 2, 3, 4, 5, 6, 7, 8});
+    if (!s->prefilled) throw InvalidState("vxc_prefill must run before patch steps");
+    if (T <= 0) throw std::invalid_argument("inference timesteps must be positive");
+    const vxc_model_desc& d = s->dev->desc;
+    // synthesizer.cpp:542-544
+    if (s->prefix_len + s->patches >= d.rope_original_max)
+        throw std::runtime_error("VoxCPM2 KV cache reached the exported RoPE range");
+    if (s->kv_len[0] + 1 > s->cap || s->kv_len[1] + 1 > s->cap || s->patches >= s->cap)
+        throw std::invalid_argument("KV cache capacity exceeded: create the stream with a larger kv_capacity");
+}
+
+void patch_step(vxc_stream* s, const float* noise, int min_patches, float cfg, int T, float* out_latent,
+                int* out_stop) {
+    check_patch_preconditions(s, T);
+    const int L = s->dev->desc.feat_dim * s->dev->desc.patch_size;
+    if (noise) {
+        std::memcpy(s->pin, noise, sizeof(float) * L);
+        ck(cudaMemcpyAsync(s->noise + static_cast<size_t>(s->patches) * L, s->pin, sizeof(float) * L,
+                           cudaMemcpyHostToDevice, s->cs),
+           "noise upload");
+    }
+    set_min_patches(s, min_patches);
+    capture_patch_graph(s, T, cfg);
+    ck(cudaGraphLaunch(s->graph, s->cs), "cudaGraphLaunch");
+    const int idx = s->patches;
+    ck(cudaMemcpyAsync(s->pin + L, s->latents + static_cast<size_t>(idx) * L, sizeof(float) * L,
+                       cudaMemcpyDeviceToHost, s->cs),
+       "latent download");
+    sync_ctl(s);
+    if (out_latent) std::memcpy(out_latent, s->pin + L, sizeof(float) * L);
+    if (out_stop) *out_stop = s->ctl_host->stopped;
+}
+
+void prefill(vxc_stream* s, const int32_t* text_ids, int n_text) {
+    const vxc_device* dev = s->dev;
+    const vxc_model_desc& d = dev->desc;
+    check_loaded(dev, {0, 1, 2, 4});
+    require(text_ids != nullptr && n_text > 0, "text must not be empty");
+    const int L = n_text + 1;
+    require(L <= s->cap, "prompt longer than the KV capacity");
+    require(L <= d.rope_original_max, "prompt longer than the RoPE range");
+    for (int i = 0; i < n_text; ++i) require(text_ids[i] >= 0 && text_ids[i] < d.vocab, "token id out of range");
+    const int H = d.hidden;
+    ensure_prefill_rows(s, L);
+    std::vector<int32_t> ids(text_ids, text_ids + n_text);
+    ids.push_back(d.audio_start_token);
+    // new utterance: empty caches, zero counters (synthesizer.cpp:348-350)
+    std::memset(s->ctl_host, 0, sizeof(StreamCtl));
+    s->ctl_host->min_patches = s->min_patches_dev;
+    write_ctl(s);
+    s->kv_len[0] = s->kv_len[1] = 0;
+    s->patches = 0;
+    s->prefilled = false;
+    ck(cudaMemcpyAsync(s->pids, ids.data(), sizeof(int32_t) * L, cudaMemcpyHostToDevice, s->cs), "ids");
+    launch_embed_gather(dev->blob[VXC_TEXT_EMBED], s->pids, L, H, d.embed_scale, s->ph, s->cs);
+    run_decoder_rows(s, 0, L, s->pxn);  // base_hidden -> pxn
+    // text-only prefix: no audio rows, so lm_prefix_hidden == base_hidden and
+    // residual_feat_embed == 0 (synthesizer.cpp:476-495)
+    ck(cudaMemcpy2DAsync(s->pcat, sizeof(float) * 2 * H, s->pxn, sizeof(float) * H, sizeof(float) * H, L,
+                         cudaMemcpyDeviceToDevice, s->cs),
+       "concat");
+    ck(cudaMemset2DAsync(s->pcat + H, sizeof(float) * 2 * H, 0, sizeof(float) * H, L, s->cs), "concat zeros");
+    ck(cudaMemcpyAsync(s->lm_h, s->pxn + static_cast<size_t>(L - 1) * H, sizeof(float) * H,
+                       cudaMemcpyDeviceToDevice, s->cs),
+       "lm row");
+    const __half* fu = dev->blob[VXC_FUSION_PROJ];
+    RowsArgs fa;
+    fa.w = fu;
+    fa.bias = fu + static_cast<size_t>(H) * 2 * H;
+    fa.x = s->pcat;
+    fa.ldx = 2 * H;
+    fa.K = 2 * H;
+    fa.rows = H;
+    fa.M = L;
+    fa.y = s->ph;
+    fa.ldy = H;
+    launch_rows_linear(fa, s->cs, false);
+    run_decoder_rows(s, 1, L, s->pxn);
+    ck(cudaMemcpyAsync(s->res_h, s->pxn + static_cast<size_t>(L - 1) * H, sizeof(float) * H,
+                       cudaMemcpyDeviceToDevice, s->cs),
+       "res row");
+    // the first patch is conditioned on zeros (synthesizer.cpp:445-447)
+    ck(cudaMemsetAsync(s->cond0, 0, sizeof(float) * d.feat_dim * d.patch_size, s->cs), "cond");
+    sync_ctl(s);
+    s->prefix_len = L;
+    s->prefilled = true;
+}
+
+}  // namespace
+
+vxc_stream::~vxc_stream() { free_all(this); }
+
+// ==================================================================== C ABI ==
+extern "C" {
+
+VXC_API uint32_t vxc_abi_version(void) { return VXC_ABI_VERSION; }
+
+VXC_API const char* vxc_last_error(void) { return g_last_error.c_str(); }
+
+VXC_API size_t vxc_component_weight_count(const vxc_model_desc* desc, int32_t component) {
+    return desc ? component_count(*desc, component) : 0;
+}
+
+VXC_API int32_t vxc_device_create(int32_t device, const vxc_model_desc* desc, vxc_device** out) {
+    return guard([&] {
+        require(desc != nullptr && out != nullptr, "desc and out must not be null");
+        *out = nullptr;
+        validate_desc(*desc);
+        int n = 0;
+        ck(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
+        require(device >= 0 && device < n, "CUDA device index out of range");
+        cudaDeviceProp prop{};
+        ck(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+        if (prop.major != 10) throw std::runtime_error("libvoxcpm2_cuda is built for sm_100a (B200) devices only");
+        DeviceGuard g(device);
+        init_kernel_attributes();
+        auto dev = std::make_unique<vxc_device>();
+        dev->device = device;
+        dev->desc = *desc;
+        const int seq = dit_tokens_per_seq(desc->patch_size);
+        std::vector<float> c, s;
+        rope_table(64, desc->rope_theta, seq, c, s);
+        dev->dit_rope_cos = dev_alloc<float>(c.size());
+        dev->dit_rope_sin = dev_alloc<float>(s.size());
+        ck(cudaMemcpy(dev->dit_rope_cos, c.data(), sizeof(float) * c.size(), cudaMemcpyHostToDevice), "rope");
+        ck(cudaMemcpy(dev->dit_rope_sin, s.data(), sizeof(float) * s.size(), cudaMemcpyHostToDevice), "rope");
+        *out = dev.release();
+    });
+}
+
+VXC_API void vxc_device_destroy(vxc_device* dev) {
+    if (!dev) return;
+    {
+        DeviceGuard g(dev->device);
+        for (__half* p : dev->blob)
+            if (p) cudaFree(p);
+        if (dev->dit_rope_cos) cudaFree(dev->dit_rope_cos);
+        if (dev->dit_rope_sin) cudaFree(dev->dit_rope_sin);
+    }
+    delete dev;
+}
+
+VXC_API int32_t vxc_load_weights(vxc_device* dev, int32_t component, const void* fp16, size_t count) {
+    return guard([&] {
+        require(dev != nullptr && fp16 != nullptr, "device and weights must not be null");
+        require(component >= 0 && component <= 8, "unknown component id");
+        require(count == component_count(dev->desc, component), "weight count does not match the model description");
+        DeviceGuard g(dev->device);
+        if (!dev->blob[component]) dev->blob[component] = dev_alloc<__half>(count);
+        ck(cudaMemcpy(dev->blob[component], fp16, count * sizeof(__half), cudaMemcpyHostToDevice), "weights upload");
+        dev->loaded[component] = true;
+        const __half* fn = nullptr;
+        if (component == VXC_BASE_DECODER) {
+            dev->base = carve_decoder(dev->blob[component], base_shape(dev->desc), &fn);
+            dev->base_norm = fn;
+        } else if (component == VXC_RESIDUAL_DECODER) {
+            dev->res = carve_decoder(dev->blob[component], res_shape(dev->desc), &fn);
+            dev->res_norm = fn;
+        } else if (component == VXC_DIT_ESTIMATOR) {
+            const size_t Hd = dev->desc.dit_hidden, D = dev->desc.feat_dim;
+            const __half* base = dev->blob[component] + 2 * (Hd * D + Hd) + 4 * (Hd * Hd + Hd);
+            dev->dit = carve_decoder(base, dit_shape(dev->desc), &fn);
+            dev->dit_norm = fn;
+        }
+    });
+}
+
+VXC_API int32_t vxc_stream_create(vxc_device* dev, int32_t kv_capacity, vxc_stream** out) {
+    return guard([&] {
+        require(dev != nullptr && out != nullptr, "device and out must not be null");
+        *out = nullptr;
+        require(kv_capacity > 1 && kv_capacity <= 32768, "kv_capacity must be in [2, 32768]");
+        DeviceGuard g(dev->device);
+        const vxc_model_desc& d = dev->desc;
+        auto s = std::make_unique<vxc_stream>();
+        s->dev = dev;
+        s->cap = kv_capacity;
+        s->splits = std::min(32, std::max(4, (kv_capacity + 31) / 32));
+        ck(cudaStreamCreateWithFlags(&s->cs, cudaStreamNonBlocking), "cudaStreamCreate");
+        s->ctl = dev_alloc<StreamCtl>(1);
+        ck(cudaMallocHost(&s->ctl_host, sizeof(StreamCtl)), "cudaMallocHost");
+        std::memset(s->ctl_host, 0, sizeof(StreamCtl));
+        ck(cudaMemset(s->ctl, 0, sizeof(StreamCtl)), "ctl");
+        const size_t H = d.hidden, F = d.ffn, hd = d.head_dim, hq = d.q_heads, hkv = d.kv_heads;
+        const int layers[2] = {d.base_layers, d.res_layers};
+        for (int w = 0; w < 2; ++w) {
+            const size_t n = static_cast<size_t>(layers[w]) * hkv * kv_capacity * hd;
+            s->kc[w] = dev_alloc<__half>(n);
+            s->vc[w] = dev_alloc<__half>(n);
+            ck(cudaMemset(s->kc[w], 0, n * sizeof(__half)), "cache");
+            ck(cudaMemset(s->vc[w], 0, n * sizeof(__half)), "cache");
+            s->h[w] = dev_alloc<float>(H);
+            s->out[w] = dev_alloc<float>(H);
+        }
+        std::vector<float> c, sn;
+        rope_table(static_cast<int>(hd), d.rope_theta, kv_capacity, c, sn);
+        s->rope_cos = dev_alloc<float>(c.size());
+        s->rope_sin = dev_alloc<float>(sn.size());
+        ck(cudaMemcpy(s->rope_cos, c.data(), sizeof(float) * c.size(), cudaMemcpyHostToDevice), "rope");
+        ck(cudaMemcpy(s->rope_sin, sn.data(), sizeof(float) * sn.size(), cudaMemcpyHostToDevice), "rope");
+        s->q = dev_alloc<float>(hq * hd);
+        s->attn = dev_alloc<float>(hq * hd);
+        s->act = dev_alloc<float>(F);
+        s->lm_h = dev_alloc<float>(H);
+        s->res_h = dev_alloc<float>(H);
+        s->feat = dev_alloc<float>(H);
+        s->mid = dev_alloc<float>(std::max<size_t>(H, d.fsq_dim));
+        s->mid2 = dev_alloc<float>(H);
+        const size_t G = hq / hkv;
+        s->partial = dev_alloc<float>(hkv * s->splits * G * (hd + 2));
+        s->counters = dev_alloc<int>(hkv);
+        ck(cudaMemset(s->counters, 0, sizeof(int) * hkv), "counters");
+        const size_t Hd = d.dit_hidden, L = static_cast<size_t>(d.feat_dim) * d.patch_size;
+        const size_t M = 2 * static_cast<size_t>(dit_tokens_per_seq(d.patch_size));
+        const size_t Wd = static_cast<size_t>(d.dit_q_heads + 2 * d.dit_kv_heads) * (Hd / d.dit_q_heads);
+        s->mu = dev_alloc<float>(2 * Hd);
+        s->x = dev_alloc<float>(L);
+        s->cond = dev_alloc<float>(L);
+        s->cond0 = dev_alloc<float>(L);
+        ck(cudaMemset(s->cond0, 0, sizeof(float) * L), "cond");
+        s->noise = dev_alloc<float>(static_cast<size_t>(kv_capacity) * L);
+        ck(cudaMemset(s->noise, 0, sizeof(float) * kv_capacity * L), "noise");
+        s->latents = dev_alloc<float>(static_cast<size_t>(kv_capacity) * L);
+        for (float** p : {&s->temb, &s->tmid, &s->ttok, &s->dtemb, &s->dtmid, &s->dttok, &s->dtemb1, &s->dtmid1,
+                          &s->dttok1})
+            *p = dev_alloc<float>(Hd);
+        s->dh = dev_alloc<float>(M * Hd);
+        s->dxn = dev_alloc<float>(M * Hd);
+        s->dqkv = dev_alloc<float>(M * Wd);
+        s->dattn = dev_alloc<float>(M * Hd);
+        s->dact = dev_alloc<float>(M * d.dit_ffn);
+        s->est = dev_alloc<float>(2 * L);
+        s->gen_in = dev_alloc<float>(std::max(8 * Hd + 8 * L, 4 * H));
+        ck(cudaMallocHost(&s->pin, sizeof(float) * (4 * std::max<size_t>(L, 2 * Hd) + 4 * H)), "cudaMallocHost");
+        *out = s.release();
+    });
+}
+
+VXC_API void vxc_stream_destroy(vxc_stream* s) {
+    if (!s) return;
+    s->cancel.store(true);
+    {
+        std::lock_guard<std::mutex> lk(s->call_mutex);  // wait for an active call to leave
+        DeviceGuard g(s->dev->device);
+        cudaStreamSynchronize(s->cs);
+    }
+    DeviceGuard g(s->dev->device);
+    delete s;
+}
+
+VXC_API void vxc_stream_cancel(vxc_stream* s) {
+    if (s) s->cancel.store(true, std::memory_order_release);
+}
+
+VXC_API int32_t vxc_stream_reset(vxc_stream* s) {
+    return guard([&] {
+        require(s != nullptr, "stream must not be null");
+        std::lock_guard<std::mutex> lk(s->call_mutex);
+        DeviceGuard g(s->dev->device);
+        std::memset(s->ctl_host, 0, sizeof(StreamCtl));
+        s->ctl_host->min_patches = s->min_patches_dev;
+        write_ctl(s);
+        s->kv_len[0] = s->kv_len[1] = 0;
+        s->patches = 0;
+        s->prefilled = false;
+    });
+}
+
+VXC_API int32_t vxc_token_count(vxc_stream* s, int32_t which, int32_t* out) {
+    return guard([&] {
+        require(s != nullptr && out != nullptr && (which == 0 || which == 1), "bad arguments");
+        std::lock_guard<std::mutex> lk(s->call_mutex);
+        DeviceGuard g(s->dev->device);
+        sync_ctl(s);
+        *out = s->kv_len[which];
+    });
+}
+
+VXC_API int32_t vxc_read_cache(vxc_stream* s, int32_t which, int32_t layer, float* k, float* v) {
+    return guard([&] {
+        require(s != nullptr && k != nullptr && v != nullptr && (which == 0 || which == 1), "bad arguments");
+        std::lock_guard<std::mutex> lk(s->call_mutex);
+        const vxc_model_desc& d = s->dev->desc;
+        const int layers = which == 0 ? d.base_layers : d.res_layers;
+        require(layer >= 0 && layer < layers, "decoder kv layer index out of range");
+        DeviceGuard g(s->dev->device);
+        sync_ctl(s);
+        const int T = s->kv_len[which], hd = d.head_dim, hkv = d.kv_heads;
+        std::vector<__half> hk(static_cast<size_t>(hkv) * s->cap * hd), hv(hk.size());
+        const size_t plane = hk.size();
+        ck(cudaMemcpy(hk.data(), s->kc[which] + layer * plane, plane * sizeof(__half), cudaMemcpyDeviceToHost), "k");
+        ck(cudaMemcpy(hv.data(), s->vc[which] + layer * plane, plane * sizeof(__half), cudaMemcpyDeviceToHost), "v");
+        for (int h = 0; h < hkv; ++h)
+            for (int t = 0; t < T; ++t)
+                for (int e = 0; e < hd; ++e) {
+                    const size_t src = (static_cast<size_t>(h) * s->cap + t) * hd + e;
+                    const size_t dst = (static_cast<size_t>(h) * T + t) * hd + e;
+                    k[dst] = __half2float(hk[src]);
+                    v[dst] = __half2float(hv[src]);
+                }
+    });
+}
+
+VXC_API int32_t vxc_decoder_step(vxc_stream* s, int32_t which, const float* embed, int32_t n, float* out) {
+    return guard([&] {
+        require(s != nullptr && embed != nullptr && out != nullptr, "null argument");
+        require(which == 0 || which == 1, "which must be VXC_BASE or VXC_RESIDUAL");
+        require(n > 0, "invalid decoder attention mask shape");
+        std::lock_guard<std::mutex> lk(s->call_mutex);
+        DeviceGuard g(s->dev->device);
+        decoder_call(s, which, embed, n, out);
+    });
+}
+
+VXC_API int32_t vxc_text_embed(vxc_stream* s, const int32_t* ids, int32_t n, float* out) {
+    return guard([&] {
+        require(s != nullptr && ids != nullptr && out != nullptr && n > 0, "bad arguments");
+        std::lock_guard<std::mutex> lk(s->call_mutex);
+        const vxc_model_desc& d = s->dev->desc;
+        check_loaded(s->dev, {VXC_TEXT_EMBED});
+        for (int i = 0; i < n; ++i) require(ids[i] >= 0 && ids[i] < d.vocab, "token id out of range");
+        DeviceGuard g(s->dev->device);
+        ensure_prefill_rows(s, n);
+        ck(cudaMemcpyAsync(s->pids, ids, sizeof(int32_t) * n, cudaMemcpyHostToDevice, s->cs), "ids");
+        launch_embed_gather(s->dev->blob[VXC_TEXT_EMBED], s->pids, n, d.hidden, d.embed_scale, s->pxn, s->cs);
+        ck(cudaMemcpyAsync(out, s->pxn, sizeof(float) * n * d.hidden, cudaMemcpyDeviceToHost, s->cs), "download");
+        ck(cudaStreamSynchronize(s->cs), "sync");
+    });
+}
+
+VXC_API int32_t vxc_run_component(vxc_stream* s, int32_t component, const float* in0, const float* in1, float* out) {
+    return guard([&] {
+        require(s != nullptr && in0 != nullptr && out != nullptr, "null argument");
+        require(component >= VXC_FSQ && component <= VXC_FEAT_ENCODER,
+                "vxc_run_component serves fsq, fusion_proj, dit_proj, stop_head, feat_encoder");
+        std::lock_guard<std::mutex> lk(s->call_mutex);
+        vxc_device* dev = s->dev;
+        const vxc_model_desc& d = dev->desc;
+        const int H = d.hidden, Hd = d.dit_hidden, L = d.feat_dim * d.patch_size, Q = d.fsq_dim;
+        DeviceGuard g(dev->device);
+        check_loaded(dev, {component});
+        float* a = s->gen_in;      // [H]
+        float* b = s->gen_in + H;  // [H]
+        int out_n = H;
+        switch (component) {
+            case VXC_FSQ: {
+                ck(cudaMemcpyAsync(a, in0, sizeof(float) * H, cudaMemcpyHostToDevice, s->cs), "upload");
+                const __half* fq = dev->blob[VXC_FSQ];
+                const size_t qh = static_cast<size_t>(Q) * H;
+                GemvArgs qa = plain_gemv(fq, fq + qh, a, H, Q, s->mid, ACT_FSQ, nullptr, 0);
+                qa.act_scale = d.fsq_scale;
+                launch_gemv(qa, s->cs, false);
+                launch_gemv(plain_gemv(fq + qh + Q, fq + qh + Q + qh, s->mid, Q, H, s->feat, ACT_NONE, nullptr, 0),
+                            s->cs, false);
+                break;
+            }
+            case VXC_FUSION_PROJ: {
+                require(in1 != nullptr, "fusion_proj needs two inputs");
+                ck(cudaMemcpyAsync(a, in0, sizeof(float) * H, cudaMemcpyHostToDevice, s->cs), "upload");
+                ck(cudaMemcpyAsync(b, in1, sizeof(float) * H, cudaMemcpyHostToDevice, s->cs), "upload");
+                const __half* fu = dev->blob[VXC_FUSION_PROJ];
+                GemvArgs ua = plain_gemv(fu, fu + static_cast<size_t>(H) * 2 * H, a, 2 * H, H, s->feat, ACT_NONE,
+                                         nullptr, 0);
+                ua.in_mode = IN_CONCAT;
+                ua.x2 = b;
+                ua.k1 = H;
+                launch_gemv(ua, s->cs, false);
+                break;
+            }
+            case VXC_DIT_PROJ: {
+                require(in1 != nullptr, "dit_proj needs two inputs");
+                ck(cudaMemcpyAsync(a, in0, sizeof(float) * H, cudaMemcpyHostToDevice, s->cs), "upload");
+                ck(cudaMemcpyAsync(b, in1, sizeof(float) * H, cudaMemcpyHostToDevice, s->cs), "upload");
+                const __half* dp = dev->blob[VXC_DIT_PROJ];
+                const size_t dps = static_cast<size_t>(Hd) * H;
+                launch_gemv(plain_gemv(dp, dp + dps, a, H, Hd, s->mu, ACT_NONE, nullptr, 0), s->cs, false);
+                launch_gemv(plain_gemv(dp + dps + Hd, dp + 2 * dps + Hd, b, H, Hd, s->mu + Hd, ACT_NONE, nullptr, 0),
+                            s->cs, false);
+                ck(cudaMemcpyAsync(out, s->mu, sizeof(float) * 2 * Hd, cudaMemcpyDeviceToHost, s->cs), "download");
+                ck(cudaStreamSynchronize(s->cs), "sync");
+                return;
+            }
+            case VXC_STOP_HEAD: {
+                ck(cudaMemcpyAsync(a, in0, sizeof(float) * H, cudaMemcpyHostToDevice, s->cs), "upload");
+                const __half* sh = dev->blob[VXC_STOP_HEAD];
+                launch_gemv(plain_gemv(sh, sh + static_cast<size_t>(H) * H, a, H, H, s->mid, ACT_SILU, nullptr, 0),
+                            s->cs, false);
+                launch_stop_decide(sh + static_cast<size_t>(H) * H + H, s->mid, H, nullptr, s->feat, s->cs, false);
+                out_n = 2;
+                break;
+            }
+            default: {  // VXC_FEAT_ENCODER
+                ck(cudaMemcpyAsync(a, in0, sizeof(float) * L, cudaMemcpyHostToDevice, s->cs), "upload");
+                const __half* fe = dev->blob[VXC_FEAT_ENCODER];
+                const size_t fin = static_cast<size_t>(H) * L;
+                GemvArgs fa = plain_gemv(fe, fe + fin, a, L, H, s->mid, ACT_SILU, nullptr, 0);
+                fa.in_mode = IN_LATENT_T;
+                fa.lat_d = d.feat_dim;
+                fa.lat_p = d.patch_size;
+                launch_gemv(fa, s->cs, false);
+                launch_gemv(plain_gemv(fe + fin + H, fe + fin + H + static_cast<size_t>(H) * H, s->mid, H, H, s->feat,
+                                       ACT_NONE, nullptr, 0),
+                            s->cs, false);
+                break;
+            }
+        }
+        ck(cudaMemcpyAsync(out, s->feat, sizeof(float) * out_n, cudaMemcpyDeviceToHost, s->cs), "download");
+        ck(cudaStreamSynchronize(s->cs), "sync");
+    });
+}
+
+VXC_API int32_t vxc_dit_estimator(vxc_stream* s, const float* x_in, const float* mu_in, const float* t_in,
+                                  const float* cond_in, const float* dt_in, float* out) {
+    return guard([&] {
+        require(s && x_in && mu_in && t_in && cond_in && dt_in && out, "null argument");
+        std::lock_guard<std::mutex> lk(s->call_mutex);
+        check_loaded(s->dev, {VXC_DIT_ESTIMATOR});
+        const vxc_model_desc& d = s->dev->desc;
+        const int Hd = d.dit_hidden, L = d.feat_dim * d.patch_size;
+        DeviceGuard g(s->dev->device);
+        float* xin = s->gen_in;    // [2][L]
+        float* cin = xin + 2 * L;  // [2][L]
+        float* min_ = cin + 2 * L; // [2][2Hd]
+        ck(cudaMemcpyAsync(xin, x_in, sizeof(float) * 2 * L, cudaMemcpyHostToDevice, s->cs), "x");
+        ck(cudaMemcpyAsync(cin, cond_in, sizeof(float) * 2 * L, cudaMemcpyHostToDevice, s->cs), "cond");
+        ck(cudaMemcpyAsync(min_, mu_in, sizeof(float) * 4 * Hd, cudaMemcpyHostToDevice, s->cs), "mu");
+        enqueue_time_tokens(s, t_in[0], t_in[1], dt_in, nullptr);
+        enqueue_dit_eval(s, xin, xin + L, min_, min_ + 2 * Hd, cin, cin + L, dt_in[1] != dt_in[0], s->est, nullptr,
+                         0.f, 0.f, nullptr);
+        ck(cudaMemcpyAsync(out, s->est, sizeof(float) * 2 * L, cudaMemcpyDeviceToHost, s->cs), "download");
+        ck(cudaStreamSynchronize(s->cs), "sync");
+    });
+}
+
+VXC_API int32_t vxc_cfm_sample(vxc_stream* s, const float* mu, const float* cond, const float* noise,
+                               int32_t timesteps, float cfg_value, float* out_latent) {
+    return guard([&] {
+        require(s && mu && cond && noise && out_latent, "null argument");
+        require(timesteps > 0, "inference timesteps must be positive");
+        std::lock_guard<std::mutex> lk(s->call_mutex);
+        check_loaded(s->dev, {VXC_DIT_ESTIMATOR});
+        const vxc_model_desc& d = s->dev->desc;
+        const int Hd = d.dit_hidden, L = d.feat_dim * d.patch_size;
+        DeviceGuard g(s->dev->device);
+        float* c = s->gen_in;
+        ck(cudaMemcpyAsync(s->mu, mu, sizeof(float) * 2 * Hd, cudaMemcpyHostToDevice, s->cs), "mu");
+        ck(cudaMemcpyAsync(c, cond, sizeof(float) * L, cudaMemcpyHostToDevice, s->cs), "cond");
+        ck(cudaMemcpyAsync(s->x, noise, sizeof(float) * L, cudaMemcpyHostToDevice, s->cs), "noise");
+        // standalone call: a stale stop flag must not skip the kernels
+        s->ctl_host->stopped = 0;
+        ck(cudaMemcpyAsync(&s->ctl->stopped, &s->ctl_host->stopped, sizeof(int), cudaMemcpyHostToDevice, s->cs), "ctl");
+        enqueue_cfm(s, c, timesteps, cfg_value);
+        ck(cudaMemcpyAsync(out_latent, s->x, sizeof(float) * L, cudaMemcpyDeviceToHost, s->cs), "download");
+        sync_ctl(s);
+    });
+}
+
+VXC_API int32_t vxc_prefill(vxc_stream* s, const int32_t* text_ids, int32_t n_text) {
+    return guard([&] {
+        require(s != nullptr, "stream must not be null");
+        std::lock_guard<std::mutex> lk(s->call_mutex);
+        DeviceGuard g(s->dev->device);
+        prefill(s, text_ids, n_text);
+    });
+}
+
+VXC_API int32_t vxc_patch_step(vxc_stream* s, const float* noise, int32_t min_patches, int32_t step, float cfg_value,
+                               int32_t timesteps, float* out_latent, int32_t* out_stop) {
+    return guard([&] {
+        require(s != nullptr, "stream must not be null");
+        std::lock_guard<std::mutex> lk(s->call_mutex);
+        DeviceGuard g(s->dev->device);
+        if (step != s->patches) throw InvalidState("step must equal the number of patches generated so far");
+        int stop = 0;
+        patch_step(s, noise, min_patches, cfg_value, timesteps, out_latent, &stop);
+        if (out_stop) *out_stop = stop;
+    });
+}
+
+VXC_API int32_t vxc_generate(vxc_stream* s, const int32_t* text_ids, int32_t n_text, int32_t min_patches,
+                             int32_t timesteps, float cfg_value, int32_t max_patches_override, uint32_t seed,
+                             float* out_latents, int32_t* out_patches, float* lm_trace, float* res_trace,
+                             float* stop_trace, vxc_progress_fn progress, void* progress_user_data) {
+    return guard([&] {
+        require(s != nullptr && out_latents != nullptr && out_patches != nullptr, "null argument");
+        require(timesteps > 0, "inference timesteps must be positive");
+        std::lock_guard<std::mutex> lk(s->call_mutex);
+        DeviceGuard g(s->dev->device);
+        s->cancel.store(false);
+        *out_patches = 0;
+        const vxc_model_desc& d = s->dev->desc;
+        const int H = d.hidden, L = d.feat_dim * d.patch_size;
+        int max_patches = max_patches_for_target(n_text, d.max_generation_patches);
+        if (max_patches_override > 0) max_patches = std::min(max_patches, max_patches_override);
+        require(n_text + 1 + max_patches <= s->cap,
+                "KV cache capacity exceeded: prefix + max_patches exceeds the stream's kv_capacity");
+        prefill(s, text_ids, n_text);
+        std::mt19937 rng(seed);
+        std::vector<float> noise(static_cast<size_t>(L));
+        for (int step = 0; step < max_patches; ++step) {
+            if (s->cancel.load(std::memory_order_acquire)) throw Cancelled();
+            if (progress && progress(progress_user_data, step, max_patches) == 0) throw Cancelled();
+            if (lm_trace)
+                ck(cudaMemcpyAsync(lm_trace + static_cast<size_t>(step) * H, s->lm_h, sizeof(float) * H,
+                                   cudaMemcpyDeviceToHost, s->cs),
+                   "trace");
+            if (res_trace)
+                ck(cudaMemcpyAsync(res_trace + static_cast<size_t>(step) * H, s->res_h, sizeof(float) * H,
+                                   cudaMemcpyDeviceToHost, s->cs),
+                   "trace");
+            // cfm_sample draws the patch's values from a fresh normal_distribution (synthesizer.cpp:108-112)
+            std::normal_distribution<float> normal(0.0f, 1.0f);
+            for (float& v : noise) v = normal(rng);
+            int stop = 0;
+            patch_step(s, noise.data(), min_patches, cfg_value, timesteps, out_latents + static_cast<size_t>(step) * L,
+                       &stop);
+            if (stop_trace) {
+                stop_trace[2 * step] = s->ctl_host->stop_logits[0];
+                stop_trace[2 * step + 1] = s->ctl_host->stop_logits[1];
+            }
+            *out_patches = step + 1;
+            if (stop) break;
+        }
+        if (progress) progress(progress_user_data, *out_patches, max_patches);
+    });
+}
+
+VXC_API int32_t vxc_sdpa(const float* q, int32_t heads, int32_t src, int32_t d, const float* k, const float* v,
+                         int32_t groups, int32_t cur, int32_t dv, const float* mask, int32_t mask_c,
+                         const float* past_k, const float* past_v, int32_t past, float scale, float* out,
+                         float* out_k, float* out_v, void* cuda_stream) {
+    return guard([&] {
+        require(q && k && v && out, "null argument");
+        require(heads > 0 && groups > 0 && heads % groups == 0 && src > 0 && cur > 0 && d > 0 && dv > 0 && past >= 0,
+                "bad SDPA shape");
+        require(past == 0 || (past_k && past_v), "past cache pointers missing");
+        cudaStream_t cs = static_cast<cudaStream_t>(cuda_stream);
+        const float rs = scale == 0.f ? 1.f / std::sqrt(static_cast<float>(d)) : scale;
+        const int G = heads / groups;
+        if (src == 1 && d == 64 && dv == 64 && G <= 16 && mask_c <= 1 && groups <= 64) {
+            // split-K flash decode over [past | cur] (fp32 rows). Its split partials
+            // live in a scratch buffer kept per (device, CUDA stream): calls on one
+            // stream run in order, calls on different streams never share it.
+            int dev_id = 0;
+            ck(cudaGetDevice(&dev_id), "cudaGetDevice");
+            struct Scratch {
+                float* partial = nullptr;
+                int* counters = nullptr;
+                size_t cap = 0;
+            };
+            static std::mutex mu;
+            static std::map<std::pair<int, cudaStream_t>, Scratch> scratch;
+            const int T = past + cur;
+            const int splits = std::min(32, std::max(1, (T + 31) / 32));
+            const size_t need = static_cast<size_t>(groups) * splits * G * (d + 2);
+            std::lock_guard<std::mutex> lk(mu);
+            Scratch& sc = scratch[{dev_id, cs}];
+            if (sc.cap < need || sc.counters == nullptr) {
+                ck(cudaStreamSynchronize(cs), "sync");
+                if (sc.partial) cudaFree(sc.partial);
+                if (sc.counters) cudaFree(sc.counters);
+                sc = Scratch{};
+                sc.partial = dev_alloc<float>(need);
+                sc.counters = dev_alloc<int>(64);
+                ck(cudaMemset(sc.counters, 0, sizeof(int) * 64), "counters");
+                sc.cap = need;
+            }
+            AttnArgs aa;
+            aa.q = q;
+            aa.k0 = past > 0 ? past_k : k;
+            aa.v0 = past > 0 ? past_v : v;
+            aa.len0 = past > 0 ? past : cur;
+            aa.stride0 = past > 0 ? past : cur;
+            aa.k1 = past > 0 ? k : nullptr;
+            aa.v1 = past > 0 ? v : nullptr;
+            aa.len1 = past > 0 ? cur : 0;
+            aa.stride1 = cur;
+            aa.mask = mask;
+            aa.q_heads = heads;
+            aa.kv_heads = groups;
+            aa.head_dim = d;
+            aa.scale = rs;
+            aa.splits = splits;
+            aa.partial = sc.partial;
+            aa.counters = sc.counters;
+            aa.out = out;
+            launch_attn_decode(aa, false, cs, false);
+        } else {
+            launch_sdpa_rows_f32(q, heads, src, d, k, v, groups, cur, dv, mask, mask_c, past_k, past_v, past, rs, out, cs);
+        }
+        if (out_k) launch_concat_kv(past_k, k, groups, past, cur, d, out_k, cs);
+        if (out_v) launch_concat_kv(past_v, v, groups, past, cur, dv, out_v, cs);
+    });
+}
+
+VXC_API int32_t vxc_sdpa_host(const float* q, int32_t heads, int32_t src, int32_t d, const float* k, const float* v,
+                              int32_t groups, int32_t cur, int32_t dv, const float* mask, int32_t mask_c,
+                              const float* past_k, const float* past_v, int32_t past, float scale, float* out,
+                              float* out_k, float* out_v) {
+    return guard([&] {
+        require(q && k && v && out, "null argument");
+        require(heads > 0 && groups > 0 && src > 0 && cur > 0 && d > 0 && dv > 0 && past >= 0, "bad SDPA shape");
+        const int dst = past + cur;
+        const size_t nq = static_cast<size_t>(heads) * src * d, nk = static_cast<size_t>(groups) * cur * d,
+                     nv = static_cast<size_t>(groups) * cur * dv, npk = static_cast<size_t>(groups) * past * d,
+                     npv = static_cast<size_t>(groups) * past * dv,
+                     nm = mask ? static_cast<size_t>(std::max(1, mask_c)) * src * dst : 0,
+                     no = static_cast<size_t>(heads) * src * dv, nok = static_cast<size_t>(groups) * dst * d,
+                     nov = static_cast<size_t>(groups) * dst * dv;
+        std::vector<float*> bufs;
+        auto release = [&] {
+            for (float* p : bufs) cudaFree(p);
+            bufs.clear();
+        };
+        auto up = [&](const float* h, size_t n) -> float* {
+            if (!h || n == 0) return nullptr;
+            float* p = dev_alloc<float>(n);
+            bufs.push_back(p);
+            ck(cudaMemcpy(p, h, n * sizeof(float), cudaMemcpyHostToDevice), "upload");
+            return p;
+        };
+        auto alloc = [&](size_t n) -> float* {
+            float* p = dev_alloc<float>(n);
+            bufs.push_back(p);
+            return p;
+        };
+        try {
+            float* dq = up(q, nq);
+            float* dk = up(k, nk);
+            float* dvv = up(v, nv);
+            float* dpk = up(past_k, npk);
+            float* dpv = up(past_v, npv);
+            float* dm = up(mask, nm);
+            float* dout = alloc(no);
+            float* dok = out_k ? alloc(nok) : nullptr;
+            float* dov = out_v ? alloc(nov) : nullptr;
+            const int32_t rc = vxc_sdpa(dq, heads, src, d, dk, dvv, groups, cur, dv, dm, mask_c, dpk, dpv, past, scale,
+                                        dout, dok, dov, nullptr);
+            if (rc != VXC_STATUS_OK) {
+                const std::string msg = g_last_error;
+                release();
+                if (rc == VXC_STATUS_INVALID_ARGUMENT) throw std::invalid_argument(msg);
+                throw std::runtime_error(msg);
+            }
+            ck(cudaMemcpy(out, dout, no * sizeof(float), cudaMemcpyDeviceToHost), "download");
+            if (out_k) ck(cudaMemcpy(out_k, dok, nok * sizeof(float), cudaMemcpyDeviceToHost), "download");
+            if (out_v) ck(cudaMemcpy(out_v, dov, nov * sizeof(float), cudaMemcpyDeviceToHost), "download");
+        } catch (...) {
+            release();
+            throw;
+        }
+        release();
+    });
+}
+
+VXC_API int32_t vxc_upload_noise(vxc_stream* s, const float* noise, int32_t patches) {
+    return guard([&] {
+        require(s && noise && patches > 0, "bad arguments");
+        std::lock_guard<std::mutex> lk(s->call_mutex);
+        require(patches <= s->cap, "more noise rows than the stream holds (kv_capacity)");
+        const int L = s->dev->desc.feat_dim * s->dev->desc.patch_size;
+        DeviceGuard g(s->dev->device);
+        ck(cudaMemcpy(s->noise, noise, sizeof(float) * L * patches, cudaMemcpyHostToDevice), "noise");
+    });
+}
+
+VXC_API int32_t vxc_patch_step_async(vxc_stream* s, int32_t min_patches, float cfg_value, int32_t timesteps) {
+    return guard([&] {
+        require(s != nullptr, "stream must not be null");
+        std::lock_guard<std::mutex> lk(s->call_mutex);
+        DeviceGuard g(s->dev->device);
+        check_patch_preconditions(s, timesteps);
+        set_min_patches(s, min_patches);
+        capture_patch_graph(s, timesteps, cfg_value);
+        ck(cudaGraphLaunch(s->graph, s->cs), "cudaGraphLaunch");
+        // host mirror advances optimistically; vxc_read_state re-syncs it
+        s->patches += 1;
+        s->kv_len[0] += 1;
+        s->kv_len[1] += 1;
+    });
+}
+
+VXC_API int32_t vxc_stream_synchronize(vxc_stream* s) {
+    return guard([&] {
+        require(s != nullptr, "stream must not be null");
+        DeviceGuard g(s->dev->device);
+        ck(cudaStreamSynchronize(s->cs), "cudaStreamSynchronize");
+    });
+}
+
+VXC_API int32_t vxc_read_state(vxc_stream* s, vxc_stream_state* out) {
+    return guard([&] {
+        require(s != nullptr && out != nullptr, "null argument");
+        std::lock_guard<std::mutex> lk(s->call_mutex);
+        DeviceGuard g(s->dev->device);
+        ck(cudaMemcpyAsync(s->ctl_host, s->ctl, sizeof(StreamCtl), cudaMemcpyDeviceToHost, s->cs), "ctl");
+        ck(cudaStreamSynchronize(s->cs), "sync");
+        out->kv_len[0] = s->ctl_host->kv_len[0];
+        out->kv_len[1] = s->ctl_host->kv_len[1];
+        out->patches = s->ctl_host->patch;
+        out->stopped = s->ctl_host->stopped;
+        out->stop_logits[0] = s->ctl_host->stop_logits[0];
+        out->stop_logits[1] = s->ctl_host->stop_logits[1];
+        out->prefix_len = s->prefix_len;
+        out->error = s->ctl_host->error;
+        s->kv_len[0] = out->kv_len[0];
+        s->kv_len[1] = out->kv_len[1];
+        s->patches = out->patches;
+    });
+}
+
+VXC_API int32_t vxc_read_hidden(vxc_stream* s, float* lm, float* res) {
+    return guard([&] {
+        require(s != nullptr, "stream must not be null");
+        std::lock_guard<std::mutex> lk(s->call_mutex);
+        const int H = s->dev->desc.hidden;
+        DeviceGuard g(s->dev->device);
+        if (lm) ck(cudaMemcpyAsync(lm, s->lm_h, sizeof(float) * H, cudaMemcpyDeviceToHost, s->cs), "lm");
+        if (res) ck(cudaMemcpyAsync(res, s->res_h, sizeof(float) * H, cudaMemcpyDeviceToHost, s->cs), "res");
+        ck(cudaStreamSynchronize(s->cs), "sync");
+    });
+}
+
+VXC_API int32_t vxc_read_latents(vxc_stream* s, int32_t first, int32_t count, float* out) {
+    return guard([&] {
+        require(s != nullptr && out != nullptr && first >= 0 && count >= 0 && first + count <= s->cap, "bad range");
+        std::lock_guard<std::mutex> lk(s->call_mutex);
+        const int L = s->dev->desc.feat_dim * s->dev->desc.patch_size;
+        DeviceGuard g(s->dev->device);
+        ck(cudaMemcpyAsync(out, s->latents + static_cast<size_t>(first) * L, sizeof(float) * L * count,
+                           cudaMemcpyDeviceToHost, s->cs),
+           "latents");
+        ck(cudaStreamSynchronize(s->cs), "sync");
+    });
+}
+
+VXC_API int32_t vxc_stream_cuda_handle(vxc_stream* s, void** out) {
+    return guard([&] {
+        require(s != nullptr && out != nullptr, "null argument");
+        *out = static_cast<void*>(s->cs);
+    });
+}
+
+}  // extern "C"
