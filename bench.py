@@ -1,0 +1,343 @@
+#!/usr/bin/env python
+"""Benchmark of the VoxCPM2 patch loop on B200: latent patches/s at batch 1.
+
+Workload: the full synthesis loop at the benchmark shapes (24-layer base and
+8-layer residual decoders, 12-layer DiT, hidden 1024, 16/2 heads of 64, SwiGLU
+4096; 64 random text tokens, 10 timesteps, cfg 2.0, min_patches 100) with
+random fp16 weights. Each GPU runs S independent batch-1 synthesis streams
+(request parallel, no collective on the data path); a "step" is one patch of
+every stream on the GPU.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--streams S] [--impl ours|reference]
+
+Under torchrun (N > 1) every rank drives its own GPU; rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "latent patches/sec/GPU at batch 1; p50 per-patch latency; HBM roofline frac"
+TEXT_TOKENS = 64
+MIN_PATCHES = 100
+TIMESTEPS = 10
+CFG = 2.0
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--streams", type=int, default=16, help="independent batch-1 streams per GPU")
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--cpu-sample-patches", type=int, default=6)
+    return p.parse_args()
+
+
+def workload(streams_per_gpu: int, steps: int, warmup: int):
+    # min_patches stays at 100 unless a longer run needs it raised so the stop
+    # head cannot end a stream inside the measured steps
+    min_patches = max(MIN_PATCHES, steps + warmup + 1)
+    return {
+        "workload": "full patch loop: base decode (24 layers) + residual decode (8) + 9 DiT evals (12 layers, "
+                    "CFG 2x11 tokens) + dit_proj/stop/feat_encoder/fsq/fusion per patch; hidden 1024, 16/2 heads x 64, "
+                    f"SwiGLU 4096; {TEXT_TOKENS} text tokens, {TIMESTEPS} timesteps, cfg {CFG}",
+        "min_patches": min_patches,
+        "streams_per_gpu": streams_per_gpu,
+        "batch_per_stream": 1,
+        "l2": "no flush: each patch streams ~4.7 GB of weights, far above the 126 MB L2",
+    }, min_patches
+
+
+# --------------------------------------------------------------- clocks ---
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = Path(f"/tmp/vxc_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            self.proc.wait(timeout=10)
+
+    def summary(self):
+        if not self.path.exists():
+            return None
+        rows = [r.split(",") for r in self.path.read_text().strip().splitlines() if r.count(",") >= 6]
+        self.path.unlink(missing_ok=True)
+        if not rows:
+            return None
+        sm = [float(r[0]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[3 + i].strip().lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": float(rows[0][1]), "samples": len(rows),
+                "power_w_max": max(float(r[2]) for r in rows), "reasons": reasons}
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------ CPU loops ---
+def oracle_patch_rate(patches: int, warmup: int, threads: int):
+    """The reference's patch loop restated on the CPU (the oracle), one stream:
+    prefill untimed, 'warmup' patches untimed, then 'patches' timed patches."""
+    import oracle
+    from voxcpm2_b200 import synthetic
+    from voxcpm2_b200.config import BENCH
+    oracle.set_threads(threads)
+    cfg = BENCH
+    o = oracle.Oracle(cfg, synthetic.model_blobs(cfg, 0))
+    ids = np.append(synthetic.token_ids(cfg, TEXT_TOKENS, seed=1000), cfg.audio_start_token).astype(np.int32)
+    o.reset()
+    base = o.decoder_forward(0, o.text_embed(ids))
+    res = o.decoder_forward(1, o.fusion_proj(base, np.zeros_like(base)))
+    lm, rs = base[-1].copy(), res[-1].copy()
+    noise = oracle.noise_table(0, warmup + patches, cfg.latent)
+    cond = np.zeros(cfg.latent, np.float32)
+    times = []
+    for step in range(warmup + patches):
+        t0 = time.perf_counter()
+        mu = o.dit_proj(lm, rs)
+        lat = o.cfm_sample(mu, cond, noise[step], TIMESTEPS, CFG)
+        o.stop_head(lm)
+        feat = o.feat_encoder(lat)
+        lm = o.fsq(o.decoder_forward(0, feat[None]))[0]
+        rs = o.decoder_forward(1, o.fusion_proj(lm, feat))[0]
+        cond = lat
+        if step >= warmup:
+            times.append(time.perf_counter() - t0)
+    return len(times) / sum(times), times
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    cfg_info, _ = workload(1, args.steps, args.warmup)
+    threads = os.cpu_count() or 1
+    rate, times = oracle_patch_rate(args.steps, args.warmup, threads)
+    sample = (f"{args.steps} timed patches (after {args.warmup} untimed) of one stream of the benchmark loop, "
+              f"reference math restated in C++ (oracle), {threads} threads")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": rate, "unit": "patches/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * float(np.mean(times)),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (fp16 weights)",
+        "data": "synthetic", "config": cfg_info,
+        "p50_patch_ms": 1e3 * float(np.median(times)),
+        "cpu_baseline": {"value": rate, "unit": "patches/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": rate, "unit": "patches/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------- GPU arm ---
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from voxcpm2_b200 import runtime as rt
+    from voxcpm2_b200 import synthetic
+    from voxcpm2_b200.config import BENCH
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    S, K, W = args.streams, args.steps, args.warmup
+    cfg_info, min_patches = workload(S, K, W)
+    cfg = BENCH
+    L = cfg.latent
+    dev = rt.Device(cfg, local, synthetic.model_blobs(cfg, 0))
+    cap = TEXT_TOKENS + 1 + W + K + 8
+    streams = [rt.Stream(dev, kv_capacity=max(cap, 512)) for _ in range(S)]
+    ids = [synthetic.token_ids(cfg, TEXT_TOKENS, seed=1000 + rank * S + i) for i in range(S)]
+    noise = [synthetic.normal((W + K, L), seed=rank * S + i) for i in range(S)]
+
+    # ---- value: device-resident, graphs replayed from the uploaded noise tables
+    for s, i, n in zip(streams, ids, noise):
+        s.prefill(i)
+        s.upload_noise(n)
+    for _ in range(W):
+        for s in streams:
+            s.patch_step_async(min_patches, CFG, TIMESTEPS)
+    for s in streams:
+        s.synchronize()
+    ext = [torch.cuda.ExternalStream(s.cuda_stream()) for s in streams]
+    main = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        e0.record(main)
+        for st in ext:
+            st.wait_event(e0)
+        for _ in range(K):
+            for s in streams:
+                s.patch_step_async(min_patches, CFG, TIMESTEPS)
+        for st in ext:
+            ev = torch.cuda.Event()
+            ev.record(st)
+            main.wait_event(ev)
+        e1.record(main)
+        e1.synchronize()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    states = [s.state() for s in streams]
+    assert all(st.patches == W + K and st.error == 0 for st in states), "a stream did not complete its patches"
+    graph_kernels = states[0].graph_kernels
+    value = world * S * K / (ms / 1e3)
+
+    # ---- dominant kernel, timed alone with CUDA events on the stream
+    peak, peak_kind = measured_peaks()
+    prof_ms, prof_bytes = streams[0].profile_kernel("dit_gateup", 100)
+    achieved = prof_bytes / (prof_ms / 1e3) / 1e9
+    roofline = {"kernel": "rows_linear_kernel<GATEUP> (DiT gate/up, 2x11 tokens)", "bound": "hbm",
+                "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "peak_kind": f"{peak_kind} burst copy bandwidth", "bytes_per_launch": prof_bytes,
+                "us_per_launch": 1e3 * prof_ms, "traffic": None}
+    kernels = {}
+    for k in ("dit_down", "dit_qkv", "base_gateup", "base_down", "base_qkv", "base_attn"):
+        km, kb = streams[0].profile_kernel(k, 50)
+        kernels[k] = {"us": round(1e3 * km, 2), "GB/s": round(kb / (km / 1e3) / 1e9, 1)}
+
+    # ---- single-stream per-patch latency (device time per patch)
+    one = streams[0]
+    one.prefill(ids[0])
+    one.upload_noise(noise[0])
+    ext0 = ext[0]
+    lat_ms = []
+    for step in range(W + min(K, 12)):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(ext0)
+        one.patch_step_async(min_patches, CFG, TIMESTEPS)
+        b.record(ext0)
+        b.synchronize()
+        if step >= W:
+            lat_ms.append(a.elapsed_time(b))
+    p50_single = float(np.median(lat_ms))
+
+    # ---- e2e: the public C ABI with host buffers (noise in, latent + state out), one thread per stream
+    for s, i in zip(streams, ids):
+        s.prefill(i)
+    per_call = [[] for _ in range(S)]
+    # each thread runs its warm-up steps, then waits for the timed start
+    done_warm = [threading.Event() for _ in range(S)]
+    go = threading.Event()
+
+    def worker(j):
+        s = streams[j]
+        for step in range(W):
+            s.patch_step(noise[j][step], min_patches, step, CFG, TIMESTEPS)
+        done_warm[j].set()
+        go.wait()
+        for step in range(W, W + K):
+            t0 = time.perf_counter()
+            s.patch_step(noise[j][step], min_patches, step, CFG, TIMESTEPS)
+            per_call[j].append(time.perf_counter() - t0)
+
+    threads = [threading.Thread(target=worker, args=(j,)) for j in range(S)]
+    for t in threads:
+        t.start()
+    for ev in done_warm:
+        ev.wait()
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    go.set()
+    for t in threads:
+        t.join()
+    torch.cuda.synchronize()
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    barrier()
+    e2e_value = world * S * K / e2e_s
+    calls = np.concatenate([np.array(c) for c in per_call]) * 1e3
+    h2d = S * L * 4                   # each stream's noise patch
+    d2h = S * (L * 4 + 40)            # each stream's latent patch + its 40-byte control block
+
+    # ---- CPU baseline: the oracle port on this host, bounded sample (rank 0, N = 1)
+    cpu = None
+    if rank == 0 and world == 1:
+        threads_cpu = os.cpu_count() or 1
+        rate, _ = oracle_patch_rate(args.cpu_sample_patches, 1, threads_cpu)
+        cpu = {"value": rate, "unit": "patches/s", "cores": threads_cpu, "kind": "port",
+               "sample": f"{args.cpu_sample_patches} patches (after 1 untimed) of one stream, oracle (reference "
+                         f"CPU math restated in C++), {threads_cpu} threads"}
+
+    clk = clocks.summary()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "patches/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16 weights, f32 compute and KV", "data": "synthetic (random fp16 weights N(0,0.02), "
+            "uniform token ids, N(0,1) noise)", "config": cfg_info,
+            "p50_patch_ms": p50_single, "p50_patch_ms_under_load": float(np.median(calls)),
+            "per_gpu_patches_per_s": value / world,
+            "e2e": {"value": e2e_value, "unit": "patches/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": graph_kernels * S * K, "roofline": roofline, "kernels": kernels,
+            "cpu_baseline": cpu, "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    for s in streams:
+        s.close()
+    dev.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

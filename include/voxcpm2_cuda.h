@@ -98,7 +98,19 @@ typedef struct vxc_stream_state {
     float stop_logits[2];   /* the last stop_head logits */
     int32_t prefix_len;
     int32_t error;          /* last device-side check code (0 = none) */
+    int32_t graph_kernels;  /* kernel launches in one captured patch step (0 before the first) */
 } vxc_stream_state;
+
+/* Hot kernels vxc_profile_kernel can time in isolation. */
+enum {
+    VXC_PROF_DIT_GATEUP = 0,   /* DiT gate/up projection of layer 0 over the 2 x 11 tokens */
+    VXC_PROF_DIT_DOWN = 1,     /* DiT down projection of layer 0 */
+    VXC_PROF_DIT_QKV = 2,      /* DiT q/k/v projection of layer 0 */
+    VXC_PROF_BASE_GATEUP = 3,  /* base decoder gate/up GEMV of layer 0 (RMSNorm fused) */
+    VXC_PROF_BASE_DOWN = 4,    /* base decoder down GEMV of layer 0 */
+    VXC_PROF_BASE_QKV = 5,     /* base decoder q/k/v GEMV + RoPE + KV append of layer 0 */
+    VXC_PROF_BASE_ATTN = 6,    /* base decoder flash-decode attention of layer 0 */
+};
 
 /* Progress callback of vxc_generate: return non-zero to continue, zero to cancel
  * (the same contract as voxcpm2_progress_callback, include/voxcpm2/c_api.h:98-106). */
@@ -219,6 +231,14 @@ VXC_API int32_t vxc_read_state(vxc_stream* s, vxc_stream_state* out);
 VXC_API int32_t vxc_read_hidden(vxc_stream* s, float* lm, float* res);
 /* Latents of patches [first, first + count) generated since the last prefill. */
 VXC_API int32_t vxc_read_latents(vxc_stream* s, int32_t first, int32_t count, float* out);
+/* Times one hot kernel alone on the stream's own buffers: 'iters' back-to-back
+ * launches between CUDA events on the stream (after one warm-up launch).
+ * Writes the mean milliseconds per launch and the algorithmic bytes one launch
+ * must move (weights + activations in + out). Call it between patch steps: it
+ * leaves the stream's positions and valid KV rows as they were, but overwrites
+ * scratch activations and the next free KV row of base layer 0. */
+VXC_API int32_t vxc_profile_kernel(vxc_stream* s, int32_t kernel, int32_t iters, float* ms_per_launch,
+                                   double* bytes_per_launch);
 /* The stream's cudaStream_t, for callers timing it with CUDA events. */
 VXC_API int32_t vxc_stream_cuda_handle(vxc_stream* s, void** out);
 

@@ -1,0 +1,230 @@
+"""GPU parity of the whole patch loop against the CPU oracle, and its failure handling.
+
+The bar (from the task's parity contract): identical stop decisions and patch
+counts; per-patch latents and hidden states within max-abs 2e-2 and cosine >= 0.999.
+Failure handling is exercised from the host only: bad arguments, capacity,
+cancellation (callback and another thread), non-finite estimator output.
+"""
+from __future__ import annotations
+
+import threading
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import close_stats
+from voxcpm2_b200 import synthetic
+from voxcpm2_b200.config import BENCH, TINY
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def rt():
+    from voxcpm2_b200 import runtime
+    return runtime
+
+
+@pytest.fixture(scope="module")
+def tiny(rt):
+    blobs = synthetic.model_blobs(TINY, 0)
+    dev = rt.Device(TINY, 0, blobs)
+    yield TINY, blobs, dev, oracle.Oracle(TINY, blobs)
+    dev.close()
+
+
+@pytest.fixture(scope="module")
+def bench(rt):
+    blobs = synthetic.model_blobs(BENCH, 0)
+    dev = rt.Device(BENCH, 0, blobs)
+    yield BENCH, blobs, dev, oracle.Oracle(BENCH, blobs)
+    dev.close()
+
+
+def compare_runs(got, want, what, min_patches):
+    """Identical patch count and stop decisions; every per-patch latent and hidden
+    state within max-abs 2e-2 and cosine >= 0.999. Reports the worst patch."""
+    n = min(got["patches"], want["patches"])
+    worst = {}
+    for key in ("latents", "lm_hidden", "res_hidden"):
+        stats = [close_stats(got[key][i], want[key][i]) for i in range(n)]
+        worst[key] = (max(s[0] for s in stats), min(s[1] for s in stats))
+    decisions_g = [bool(l[1] > l[0]) for l in got["stop_logits"][:n]]
+    decisions_w = [bool(l[1] > l[0]) for l in want["stop_logits"][:n]]
+    margin = float(np.min(np.abs(want["stop_logits"][:n, 1] - want["stop_logits"][:n, 0])))
+    summary = f"{what}: patches {got['patches']}/{want['patches']}, worst {worst}, min stop margin {margin:.2e}"
+    print(summary)
+    assert got["patches"] == want["patches"], summary
+    assert decisions_g[min_patches + 1:] == decisions_w[min_patches + 1:], summary
+    for key, (err, cos) in worst.items():
+        assert err <= 2e-2 and cos >= 0.999, summary
+
+
+def test_generate_tiny_full_loop(rt, tiny):
+    cfg, blobs, dev, orc = tiny
+    s = rt.Stream(dev, kv_capacity=128)
+    ids = synthetic.token_ids(cfg, 12, seed=9)
+    want = orc.generate(ids, min_patches=6, timesteps=10, cfg_value=2.0, max_patches_override=60, seed=0)
+    got = s.generate(ids, min_patches=6, timesteps=10, cfg_value=2.0, max_patches_override=60, seed=0)
+    compare_runs(got, want, "tiny", 6)
+    assert got["patches"] >= 8
+    s.close()
+
+
+def test_generate_bench_first_patches(rt, bench):
+    """The benchmark model: 64 text tokens, the first 10 patches of the loop."""
+    cfg, blobs, dev, orc = bench
+    s = rt.Stream(dev, kv_capacity=512)
+    ids = synthetic.token_ids(cfg, 64, seed=1)
+    want = orc.generate(ids, min_patches=100, timesteps=10, cfg_value=2.0, max_patches_override=10, seed=0)
+    got = s.generate(ids, min_patches=100, timesteps=10, cfg_value=2.0, max_patches_override=10, seed=0)
+    compare_runs(got, want, "bench", 100)
+    st = s.state()
+    assert st.prefix_len == 65 and st.patches == 10
+    assert st.kv_len[0] == st.kv_len[1] == 65 + 10
+    s.close()
+
+
+def test_patch_step_matches_generate(rt, tiny):
+    cfg, blobs, dev, orc = tiny
+    ids = synthetic.token_ids(cfg, 8, seed=2)
+    a = rt.Stream(dev, kv_capacity=64)
+    ref = a.generate(ids, min_patches=3, timesteps=6, cfg_value=2.0, max_patches_override=20, seed=5)
+    b = rt.Stream(dev, kv_capacity=64)
+    b.prefill(ids)
+    noise = oracle.noise_table(5, 20, cfg.latent)
+    lat = []
+    for step in range(ref["patches"]):
+        x, stop = b.patch_step(noise[step], min_patches=3, step=step, cfg_value=2.0, timesteps=6)
+        lat.append(x)
+        if stop:
+            break
+    assert len(lat) == ref["patches"]
+    assert np.array_equal(np.stack(lat), ref["latents"])
+    # device-resident driving replays the same graph from an uploaded noise table
+    c = rt.Stream(dev, kv_capacity=64)
+    c.prefill(ids)
+    c.upload_noise(noise)
+    for _ in range(ref["patches"]):
+        c.patch_step_async(3, 2.0, 6)
+    c.synchronize()
+    st = c.state()
+    assert st.patches == ref["patches"]
+    assert np.array_equal(c.latents(0, ref["patches"]), ref["latents"])
+    for s in (a, b, c):
+        s.close()
+
+
+def test_streams_run_concurrently(rt, tiny):
+    cfg, blobs, dev, orc = tiny
+    ids = synthetic.token_ids(cfg, 8, seed=3)
+    ref = rt.Stream(dev, kv_capacity=64).generate(ids, min_patches=2, timesteps=5, max_patches_override=12, seed=1)
+    streams = [rt.Stream(dev, kv_capacity=64) for _ in range(4)]
+    results = [None] * 4
+
+    def run(i):
+        results[i] = streams[i].generate(ids, min_patches=2, timesteps=5, max_patches_override=12, seed=1)
+
+    threads = [threading.Thread(target=run, args=(i,)) for i in range(4)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    for r in results:
+        assert r["patches"] == ref["patches"]
+        assert np.array_equal(r["latents"], ref["latents"])
+    for s in streams:
+        s.close()
+
+
+# ------------------------------------------------------------- failures ---
+def test_step_must_follow_patch_count(rt, tiny):
+    cfg, blobs, dev, orc = tiny
+    s = rt.Stream(dev, kv_capacity=32)
+    with pytest.raises(rt.VxcError) as e:
+        s.patch_step(np.zeros(cfg.latent, np.float32), 2, 0)
+    assert e.value.status == 2  # INVALID_STATE: no prefill yet
+    s.prefill(synthetic.token_ids(cfg, 4, seed=0))
+    with pytest.raises(rt.VxcError) as e:
+        s.patch_step(np.zeros(cfg.latent, np.float32), 2, 3)
+    assert e.value.status == 2
+    s.patch_step(np.zeros(cfg.latent, np.float32), 2, 0)
+    s.close()
+
+
+def test_capacity_overflow_rejected_before_launch(rt, tiny):
+    cfg, blobs, dev, orc = tiny
+    s = rt.Stream(dev, kv_capacity=20)
+    ids = synthetic.token_ids(cfg, 8, seed=0)
+    with pytest.raises(rt.VxcError) as e:  # 9 prefix rows + 58 patches > 20
+        s.generate(ids, min_patches=2, timesteps=4)
+    assert e.value.status == 1
+    r = s.generate(ids, min_patches=2, timesteps=4, max_patches_override=10)  # the stream is still usable
+    assert 1 <= r["patches"] <= 10
+    s.close()
+
+
+def test_cancel_from_progress_callback(rt, tiny):
+    cfg, blobs, dev, orc = tiny
+    s = rt.Stream(dev, kv_capacity=128)
+    seen = []
+
+    def progress(done, total):
+        seen.append(done)
+        return done < 3
+
+    with pytest.raises(rt.VxcError) as e:
+        s.generate(synthetic.token_ids(cfg, 8, seed=0), min_patches=50, timesteps=4, progress=progress)
+    assert e.value.status == 3
+    assert seen[-1] == 3 and s.state().patches == 3
+    s.close()
+
+
+def test_cancel_from_another_thread(rt, tiny):
+    cfg, blobs, dev, orc = tiny
+    s = rt.Stream(dev, kv_capacity=128)
+    started = threading.Event()
+
+    def progress(done, total):
+        if done == 2:
+            started.set()
+            threading.Event().wait(0.05)
+        return True
+
+    err = []
+
+    def run():
+        try:
+            s.generate(synthetic.token_ids(cfg, 8, seed=0), min_patches=50, timesteps=4, progress=progress)
+        except rt.VxcError as e:
+            err.append(e.status)
+
+    t = threading.Thread(target=run)
+    t.start()
+    started.wait(30)
+    s.cancel()
+    t.join(60)
+    assert err == [3]
+    s.close()
+
+
+def test_non_finite_estimator_output_raises(rt):
+    """A NaN planted in the DiT out_proj bias (host-side input) must raise, as synthesizer.cpp:150 does."""
+    from voxcpm2_b200.config import DIT_ESTIMATOR, component_offsets
+    blobs = synthetic.model_blobs(TINY, 0)
+    off, _ = component_offsets(TINY, DIT_ESTIMATOR)["out_proj.bias"]
+    blobs[DIT_ESTIMATOR] = blobs[DIT_ESTIMATOR].copy()
+    blobs[DIT_ESTIMATOR][off] = np.float16(np.nan)
+    dev = rt.Device(TINY, 0, blobs)
+    s = rt.Stream(dev, kv_capacity=32)
+    rng = np.random.default_rng(0)
+    with pytest.raises(rt.VxcError) as e:
+        s.cfm_sample(rng.standard_normal(2 * TINY.dit_hidden), np.zeros(TINY.latent), rng.standard_normal(TINY.latent), 4)
+    assert e.value.status == 5 and "non-finite" in str(e.value)
+    s.prefill(synthetic.token_ids(TINY, 4, seed=0))
+    with pytest.raises(rt.VxcError) as e:
+        s.patch_step(np.zeros(TINY.latent, np.float32), 2, 0)
+    assert "non-finite" in str(e.value)
+    s.close()
+    dev.close()

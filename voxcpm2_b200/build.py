@@ -17,7 +17,10 @@ OBJ = PKG / "_build"
 LIB = PKG / "libvoxcpm2_cuda.so"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-FLAGS = ["-O3", "-lineinfo", "-std=c++20", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC,-fvisibility=hidden",
+# host code: no FMA contraction, so the noise draws (std::normal_distribution) and the
+# CFM schedule round exactly as the reference's C++ does.
+FLAGS = ["-O3", "-lineinfo", "-std=c++20", "--expt-relaxed-constexpr",
+         "-Xcompiler", "-fPIC,-fvisibility=hidden,-ffp-contract=off",
          "-ccbin", "/usr/bin/g++", f"-I{ROOT / 'include'}"]
 
 

@@ -139,7 +139,7 @@ __global__ void rmsnorm_rows_kernel(const float* x, int ldx, const __half* g, fl
 
 __global__ void qkv_rows_post_kernel(float* qkv, int q_heads, int kv_heads, int d, int past,
                                      int pos_mod, const float* rope_cos, const float* rope_sin,
-                                     __half* k_cache, __half* v_cache, int cap, StreamCtl* ctl) {
+                                     float* k_cache, float* v_cache, int cap, StreamCtl* ctl) {
     pdl_launch_dependents();
     pdl_wait();
     const int m = blockIdx.x;
@@ -170,20 +170,20 @@ __global__ void qkv_rows_post_kernel(float* qkv, int q_heads, int kv_heads, int 
                 continue;
             }
             const int kvh = is_v ? hh - q_heads - kv_heads : hh - q_heads;
-            __half* dst = (is_v ? v_cache : k_cache) + (static_cast<size_t>(kvh) * cap + crow) * d;
-            dst[j] = __float2half_rn(a0);
-            dst[j + half] = __float2half_rn(a1);
+            float* dst = (is_v ? v_cache : k_cache) + (static_cast<size_t>(kvh) * cap + crow) * d;
+            dst[j] = a0;
+            dst[j + half] = a1;
         }
     }
 }
 
 // One CTA per (head, query row): scores in shared memory, two-pass softmax, P.V.
-// SRC 0: prefill rows over the fp16 cache, keys [0, past + m] (the causal -1e4
+// SRC 0: prefill rows over the KV cache, keys [0, past + m] (the causal -1e4
 // mask of make_decoder_mask removes later keys exactly: exp underflows to 0).
 // SRC 1: DiT rows over the qkv rows of the same 'seq'-row sequence, no mask.
 template <int SRC>
 __global__ void attn_rows_kernel(const float* qkv, int q_heads, int kv_heads, int d, int past,
-                                 int seq, const __half* k_cache, const __half* v_cache, int cap,
+                                 int seq, const float* k_cache, const float* v_cache, int cap,
                                  float scale, float* out, StreamCtl* ctl) {
     extern __shared__ float sm[];
     __shared__ float red[32];
@@ -208,8 +208,8 @@ __global__ void attn_rows_kernel(const float* qkv, int q_heads, int kv_heads, in
     for (int t = threadIdx.x; t < T; t += blockDim.x) {
         float s = 0.f;
         if (SRC == 0) {
-            const __half* kp = k_cache + (static_cast<size_t>(kvh) * cap + t) * d;
-            for (int e = 0; e < d; ++e) s = fmaf(qs[e], __half2float(kp[e]), s);
+            const float* kp = k_cache + (static_cast<size_t>(kvh) * cap + t) * d;
+            for (int e = 0; e < d; ++e) s = fmaf(qs[e], kp[e], s);
         } else {
             const float* kp = qkv + static_cast<size_t>(key0 + t) * width + q_heads * d + kvh * d;
             for (int e = 0; e < d; ++e) s = fmaf(qs[e], kp[e], s);
@@ -240,8 +240,8 @@ __global__ void attn_rows_kernel(const float* qkv, int q_heads, int kv_heads, in
     for (int e = threadIdx.x; e < d; e += blockDim.x) {
         float acc = 0.f;
         if (SRC == 0) {
-            const __half* vp = v_cache + static_cast<size_t>(kvh) * cap * d + e;
-            for (int t = 0; t < T; ++t) acc = fmaf(sc[t], __half2float(vp[static_cast<size_t>(t) * d]), acc);
+            const float* vp = v_cache + static_cast<size_t>(kvh) * cap * d + e;
+            for (int t = 0; t < T; ++t) acc = fmaf(sc[t], vp[static_cast<size_t>(t) * d], acc);
         } else {
             const float* vp = qkv + static_cast<size_t>(key0) * width + (q_heads + kv_heads) * d + kvh * d + e;
             for (int t = 0; t < T; ++t) acc = fmaf(sc[t], vp[static_cast<size_t>(t) * width], acc);
@@ -576,7 +576,7 @@ void launch_rmsnorm_rows(const float* x, int ldx, const __half* g, float eps, in
 
 void launch_qkv_rows_post(float* qkv, int M, int q_heads, int kv_heads, int d, int past,
                           int pos_mod, const float* rope_cos, const float* rope_sin,
-                          __half* k_cache, __half* v_cache, int cap, StreamCtl* ctl,
+                          float* k_cache, float* v_cache, int cap, StreamCtl* ctl,
                           cudaStream_t s, bool pdl) {
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = make_cfg(dim3(M), dim3(256), 0, s, pdl, attr);
@@ -585,7 +585,7 @@ void launch_qkv_rows_post(float* qkv, int M, int q_heads, int kv_heads, int d, i
 }
 
 void launch_attn_rows_cache(const float* qkv, int M, int q_heads, int kv_heads, int d, int past,
-                            const __half* k_cache, const __half* v_cache, int cap, float scale,
+                            const float* k_cache, const float* v_cache, int cap, float scale,
                             float* out, cudaStream_t s, bool pdl) {
     if (past + M > cap) throw std::invalid_argument("prefill attention: rows beyond the cache capacity");
     const size_t smem = static_cast<size_t>(d + past + M) * sizeof(float);
@@ -602,7 +602,7 @@ void launch_dit_attention(const float* qkv, int nseq, int seq, int q_heads, int 
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = make_cfg(dim3(q_heads, nseq * seq), dim3(64), smem, s, pdl, attr);
     check_launch(cudaLaunchKernelEx(&cfg, attn_rows_kernel<1>, qkv, q_heads, kv_heads, d, 0, seq,
-                                    static_cast<const __half*>(nullptr), static_cast<const __half*>(nullptr), 0,
+                                    static_cast<const float*>(nullptr), static_cast<const float*>(nullptr), 0,
                                     scale, out, ctl));
 }
 

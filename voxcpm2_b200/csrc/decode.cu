@@ -7,7 +7,10 @@
 // the previous kernel (programmatic dependent launch), so weight streaming of
 // kernel i+1 overlaps kernel i; only the small fp32 input vector is read after
 // the dependency resolves. RMSNorm is folded into the GEMV prologue, RoPE and
-// the fp16 KV append into the q/k/v epilogue.
+// the KV append into the q/k/v epilogue. The KV cache is fp32, as the
+// reference's HostDecoderKvCache (src/kvcache.cpp:86-93): at the loop's
+// lengths it is under 2% of a decode step's bytes.
+#include <algorithm>
 #include <cfloat>
 #include <stdexcept>
 
@@ -148,9 +151,9 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
             a.ctl->error = 1;  // KV capacity exceeded: the host checks before launch
         } else {
             const int kvh = is_v ? hh - a.q_heads - a.kv_heads : hh - a.q_heads;
-            __half* dst = (is_v ? a.v_cache : a.k_cache) + (static_cast<size_t>(kvh) * a.cap + pos) * d;
-            dst[j] = __float2half_rn(o0);
-            dst[j + half] = __float2half_rn(o1);
+            float* dst = (is_v ? a.v_cache : a.k_cache) + (static_cast<size_t>(kvh) * a.cap + pos) * d;
+            dst[j] = o0;
+            dst[j + half] = o1;
         }
     }
 }
@@ -199,6 +202,41 @@ __device__ __forceinline__ float load_kv<float>(const float* p, int e) { return 
 constexpr int kAttnThreads = 128;
 constexpr int kMaxGroup = 16;
 
+constexpr int kMinKeysPerSplit = 16;
+
+template <typename KV>
+__device__ __forceinline__ void load_row64(const KV* p, float* r);
+template <>
+__device__ __forceinline__ void load_row64<float>(const float* p, float* r) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const float4 v = *reinterpret_cast<const float4*>(p + 4 * i);
+        r[4 * i] = v.x;
+        r[4 * i + 1] = v.y;
+        r[4 * i + 2] = v.z;
+        r[4 * i + 3] = v.w;
+    }
+}
+template <>
+__device__ __forceinline__ void load_row64<__half>(const __half* p, float* r) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint4 v = *reinterpret_cast<const uint4*>(p + 8 * i);
+        const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 f = __half22float2(h[j]);
+            r[8 * i + 2 * j] = f.x;
+            r[8 * i + 2 * j + 1] = f.y;
+        }
+    }
+}
+
+// Split-K flash decode. The number of active splits follows the current key
+// count T (at least kMinKeysPerSplit keys each, at most 'splits'), so short
+// caches do not pay for empty splits; inactive CTAs leave at once. The last
+// active CTA of a KV head combines the partial (max, sum, P.V) triples, staged in
+// shared memory with one parallel load so the combine costs one L2 round trip.
 template <typename KV, int D>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArgs a, int max_chunk) {
     extern __shared__ float sm[];
@@ -217,7 +255,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
         len1 = 0;
     }
     const int T = len0 + len1;
-    const int chunk = (T + a.splits - 1) / a.splits;
+    const int active = max(1, min(a.splits, (T + kMinKeysPerSplit - 1) / kMinKeysPerSplit));
+    if (split >= active) return;
+    const int chunk = (T + active - 1) / active;
     const int t0 = split * chunk;
     const int n = max(0, min(min(T, t0 + chunk) - t0, max_chunk));
 
@@ -236,8 +276,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
         const int row = t0 + t;
         const KV* kp = row < len0 ? k0 + static_cast<size_t>(row) * D : k1 + static_cast<size_t>(row - len0) * D;
         float kr[D];
-#pragma unroll
-        for (int e = 0; e < D; ++e) kr[e] = load_kv(kp, e);
+        load_row64(kp, kr);
         const float madd = a.mask ? a.mask[row] : 0.f;
         for (int g = 0; g < G; ++g) {
             float s = 0.f;
@@ -283,22 +322,26 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
     }
     __threadfence();
     __syncthreads();
-    if (tid == 0) s_last = atomicAdd(&a.counters[kvh], 1) == a.splits - 1;
+    if (tid == 0) s_last = atomicAdd(&a.counters[kvh], 1) == active - 1;
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    // combine the splits of this KV head
+    // combine the active splits of this KV head from shared memory
     const float* pk = a.partial + static_cast<size_t>(kvh) * a.splits * G * (D + 2);
+    float* ps = sm;  // [active][G][D + 2], reuses the score buffer
+    const int total = active * G * (D + 2);
+    for (int i = tid; i < total; i += kAttnThreads) ps[i] = __ldcg(pk + i);
+    __syncthreads();
     for (int it = tid; it < G * D; it += kAttnThreads) {
         const int g = it / D, e = it - g * D;
         float M = -1e30f;
-        for (int sp = 0; sp < a.splits; ++sp) M = fmaxf(M, __ldcg(pk + (sp * G + g) * (D + 2) + D));
+        for (int sp = 0; sp < active; ++sp) M = fmaxf(M, ps[(sp * G + g) * (D + 2) + D]);
         float num = 0.f, den = 0.f;
-        for (int sp = 0; sp < a.splits; ++sp) {
-            const float* pp = pk + (sp * G + g) * (D + 2);
-            const float w = __expf(__ldcg(pp + D) - M);
-            num = fmaf(w, __ldcg(pp + e), num);
-            den = fmaf(w, __ldcg(pp + D + 1), den);
+        for (int sp = 0; sp < active; ++sp) {
+            const float* pp = ps + (sp * G + g) * (D + 2);
+            const float w = __expf(pp[D] - M);
+            num = fmaf(w, pp[e], num);
+            den = fmaf(w, pp[D + 1], den);
         }
         a.out[(kvh * G + g) * D + e] = num / den;
     }
@@ -351,8 +394,10 @@ void launch_attn_decode(const AttnArgs& a, bool fp16_kv, cudaStream_t s, bool pd
     if (G < 1 || G > kMaxGroup) throw std::invalid_argument("attention: more than 16 query heads per KV head");
     // the longest split any launch of this configuration can see
     const int t_max = a.ctl ? a.len0 : a.len0 + a.len1;
-    const int max_chunk = (t_max + a.splits - 1) / a.splits;
-    const size_t smem = static_cast<size_t>(G) * (64 + max_chunk) * sizeof(float);
+    // the longest split: a short cache runs fewer splits of >= kMinKeysPerSplit keys
+    const int max_chunk = std::max((t_max + a.splits - 1) / a.splits, kMinKeysPerSplit);
+    const size_t smem = std::max(static_cast<size_t>(G) * (64 + max_chunk),
+                                 static_cast<size_t>(a.splits) * G * (64 + 2)) * sizeof(float);
     if (smem > 200 * 1024) throw std::invalid_argument("attention: sequence too long for one split");
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = make_cfg(dim3(a.splits, a.kv_heads), dim3(kAttnThreads), smem, s, pdl, attr);

@@ -18,7 +18,7 @@ enum GemvMode : int {
     GEMV_PLAIN = 0,   // y[r] = act(dot + bias[r])
     GEMV_RESID = 1,   // resid[r] += rscale * dot                    (o_proj, down_proj)
     GEMV_GATEUP = 2,  // y[r] = silu(dot(gate r)) * dot(up r)        (rows r and r + pairs)
-    GEMV_QKV = 3,     // q/k/v rows in RoPE pairs; q -> y, k/v -> fp16 KV cache at ctl->kv_len
+    GEMV_QKV = 3,     // q/k/v rows in RoPE pairs; q -> y, k/v -> fp32 KV cache at ctl->kv_len
 };
 enum GemvAct : int { ACT_NONE = 0, ACT_SILU = 1, ACT_FSQ = 2 };
 enum GemvInput : int { IN_PLAIN = 0, IN_CONCAT = 1, IN_LATENT_T = 2 };
@@ -46,8 +46,8 @@ struct GemvArgs {
     int q_heads = 0, kv_heads = 0, head_dim = 0;
     const float* rope_cos = nullptr;  // [capacity][head_dim] or null (no RoPE)
     const float* rope_sin = nullptr;
-    __half* k_cache = nullptr;      // this layer: [kv_heads][cap][head_dim]
-    __half* v_cache = nullptr;
+    float* k_cache = nullptr;       // this layer: [kv_heads][cap][head_dim]
+    float* v_cache = nullptr;
     int cap = 0;
     int which = 0;                  // which decoder's kv_len indexes the cache
     // control
@@ -60,8 +60,8 @@ void launch_gemv(const GemvArgs& a, cudaStream_t s, bool pdl);
 // ------------------------------------------------------ flash decode -----
 // One query token of each of q_heads heads attends over keys [0, T) of a GQA
 // cache split into two segments (seg0 of len0 rows, then seg1), split-K over
-// 'splits' CTAs per KV head with a last-CTA combine. Either segment may hold
-// fp16 (cache) or fp32 (layer contract) rows; 'T' is read from ctl->kv_len[which] + 1
+// 'splits' CTAs per KV head with a last-CTA combine. Rows are fp32 (the decoder
+// caches and the layer contract; an fp16 instantiation exists for fp16 callers); 'T' is read from ctl->kv_len[which] + 1
 // when ctl is non-null (then len0 must hold the cache capacity, which sizes the
 // shared-memory score buffer), else T = len0 + len1.
 struct AttnArgs {
@@ -115,15 +115,15 @@ void launch_rmsnorm_rows(const float* x, int ldx, const __half* g, float eps, in
 
 // RoPE on the q and k parts of qkv rows [M][(hq+2hkv)d], in place, at position
 // past + (m % pos_mod) of row m (tables indexed by position). With a cache, k/v
-// of row m are also appended (fp16) at cache row past + m (prefill).
+// of row m are also appended at cache row past + m (prefill).
 void launch_qkv_rows_post(float* qkv, int M, int q_heads, int kv_heads, int d, int past,
                           int pos_mod, const float* rope_cos, const float* rope_sin,
-                          __half* k_cache, __half* v_cache, int cap, StreamCtl* ctl,
+                          float* k_cache, float* v_cache, int cap, StreamCtl* ctl,
                           cudaStream_t s, bool pdl);
 
-// Causal attention of M prefill rows (positions past..past+M-1) over the fp16 cache.
+// Causal attention of M prefill rows (positions past..past+M-1) over the KV cache.
 void launch_attn_rows_cache(const float* qkv, int M, int q_heads, int kv_heads, int d, int past,
-                            const __half* k_cache, const __half* v_cache, int cap, float scale,
+                            const float* k_cache, const float* v_cache, int cap, float scale,
                             float* out, cudaStream_t s, bool pdl);
 
 // DiT: full (non-causal, unmasked) attention within each sequence of 'seq'

@@ -10,6 +10,7 @@
 #include <atomic>
 #include <cmath>
 #include <cstring>
+#include <functional>
 #include <initializer_list>
 #include <map>
 #include <memory>
@@ -230,9 +231,11 @@ T* dev_alloc(size_t n) {
 
 struct DeviceGuard {
     int prev = -1;
-    explicit DeviceGuard(int dev) {
-        cudaGetDevice(&prev);
-        ck(cudaSetDevice(dev), "cudaSetDevice");
+    explicit DeviceGuard(int dev, bool nothrow = false) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        const cudaError_t e = cudaSetDevice(dev);
+        if (!nothrow) ck(e, "cudaSetDevice");
+        else if (e != cudaSuccess) cudaGetLastError();
     }
     ~DeviceGuard() {
         if (prev >= 0) cudaSetDevice(prev);
@@ -297,7 +300,7 @@ struct vxc_stream {
 
     StreamCtl* ctl = nullptr;       // device
     StreamCtl* ctl_host = nullptr;  // pinned mirror
-    __half *kc[2] = {}, *vc[2] = {};
+    float *kc[2] = {}, *vc[2] = {};  // fp32 KV caches [layers][kv_heads][cap][head_dim]
     float *rope_cos = nullptr, *rope_sin = nullptr;
     // batch-1 step buffers
     float *h[2] = {}, *out[2] = {}, *q = nullptr, *attn = nullptr, *act = nullptr;
@@ -324,6 +327,7 @@ struct vxc_stream {
     int graph_T = -1;
     float graph_cfg = 0.f;
     cudaGraphExec_t graph = nullptr;
+    int graph_kernels = 0;
     int min_patches_dev = -1;
 
     ~vxc_stream();
@@ -421,7 +425,7 @@ void enqueue_decoder_step(vxc_stream* s, int which, float* out, float* out2, int
         aa.ctl = s->ctl;
         aa.which = which;
         aa.skip_if_stopped = skip;
-        launch_attn_decode(aa, true, s->cs, true);
+        launch_attn_decode(aa, false, s->cs, true);
 
         GemvArgs oa;
         oa.mode = GEMV_RESID;
@@ -816,6 +820,17 @@ void capture_patch_graph(vxc_stream* s, int T, float cfg) {
         throw;
     }
     ck(cudaStreamEndCapture(s->cs, &g), "cudaStreamEndCapture");
+    size_t n_nodes = 0;
+    ck(cudaGraphGetNodes(g, nullptr, &n_nodes), "cudaGraphGetNodes");
+    std::vector<cudaGraphNode_t> nodes(n_nodes);
+    if (n_nodes) ck(cudaGraphGetNodes(g, nodes.data(), &n_nodes), "cudaGraphGetNodes");
+    int kernels = 0;
+    for (cudaGraphNode_t nd : nodes) {
+        cudaGraphNodeType t;
+        ck(cudaGraphNodeGetType(nd, &t), "cudaGraphNodeGetType");
+        if (t == cudaGraphNodeTypeKernel) ++kernels;
+    }
+    s->graph_kernels = kernels;
     const cudaError_t e = cudaGraphInstantiate(&s->graph, g, 0);
     cudaGraphDestroy(g);
     ck(e, "cudaGraphInstantiate");
@@ -966,7 +981,7 @@ VXC_API int32_t vxc_device_create(int32_t device, const vxc_model_desc* desc, vx
 VXC_API void vxc_device_destroy(vxc_device* dev) {
     if (!dev) return;
     {
-        DeviceGuard g(dev->device);
+        DeviceGuard g(dev->device, true);  // teardown never throws (also at process exit)
         for (__half* p : dev->blob)
             if (p) cudaFree(p);
         if (dev->dit_rope_cos) cudaFree(dev->dit_rope_cos);
@@ -1020,10 +1035,10 @@ VXC_API int32_t vxc_stream_create(vxc_device* dev, int32_t kv_capacity, vxc_stre
         const int layers[2] = {d.base_layers, d.res_layers};
         for (int w = 0; w < 2; ++w) {
             const size_t n = static_cast<size_t>(layers[w]) * hkv * kv_capacity * hd;
-            s->kc[w] = dev_alloc<__half>(n);
-            s->vc[w] = dev_alloc<__half>(n);
-            ck(cudaMemset(s->kc[w], 0, n * sizeof(__half)), "cache");
-            ck(cudaMemset(s->vc[w], 0, n * sizeof(__half)), "cache");
+            s->kc[w] = dev_alloc<float>(n);
+            s->vc[w] = dev_alloc<float>(n);
+            ck(cudaMemset(s->kc[w], 0, n * sizeof(float)), "cache");
+            ck(cudaMemset(s->vc[w], 0, n * sizeof(float)), "cache");
             s->h[w] = dev_alloc<float>(H);
             s->out[w] = dev_alloc<float>(H);
         }
@@ -1076,10 +1091,10 @@ VXC_API void vxc_stream_destroy(vxc_stream* s) {
     s->cancel.store(true);
     {
         std::lock_guard<std::mutex> lk(s->call_mutex);  // wait for an active call to leave
-        DeviceGuard g(s->dev->device);
+        DeviceGuard g(s->dev->device, true);
         cudaStreamSynchronize(s->cs);
     }
-    DeviceGuard g(s->dev->device);
+    DeviceGuard g(s->dev->device, true);  // teardown never throws (also at process exit)
     delete s;
 }
 
@@ -1121,17 +1136,17 @@ VXC_API int32_t vxc_read_cache(vxc_stream* s, int32_t which, int32_t layer, floa
         DeviceGuard g(s->dev->device);
         sync_ctl(s);
         const int T = s->kv_len[which], hd = d.head_dim, hkv = d.kv_heads;
-        std::vector<__half> hk(static_cast<size_t>(hkv) * s->cap * hd), hv(hk.size());
+        std::vector<float> hk(static_cast<size_t>(hkv) * s->cap * hd), hv(hk.size());
         const size_t plane = hk.size();
-        ck(cudaMemcpy(hk.data(), s->kc[which] + layer * plane, plane * sizeof(__half), cudaMemcpyDeviceToHost), "k");
-        ck(cudaMemcpy(hv.data(), s->vc[which] + layer * plane, plane * sizeof(__half), cudaMemcpyDeviceToHost), "v");
+        ck(cudaMemcpy(hk.data(), s->kc[which] + layer * plane, plane * sizeof(float), cudaMemcpyDeviceToHost), "k");
+        ck(cudaMemcpy(hv.data(), s->vc[which] + layer * plane, plane * sizeof(float), cudaMemcpyDeviceToHost), "v");
         for (int h = 0; h < hkv; ++h)
             for (int t = 0; t < T; ++t)
                 for (int e = 0; e < hd; ++e) {
                     const size_t src = (static_cast<size_t>(h) * s->cap + t) * hd + e;
                     const size_t dst = (static_cast<size_t>(h) * T + t) * hd + e;
-                    k[dst] = __half2float(hk[src]);
-                    v[dst] = __half2float(hv[src]);
+                    k[dst] = hk[src];
+                    v[dst] = hv[src];
                 }
     });
 }
@@ -1538,6 +1553,7 @@ VXC_API int32_t vxc_read_state(vxc_stream* s, vxc_stream_state* out) {
         out->stop_logits[1] = s->ctl_host->stop_logits[1];
         out->prefix_len = s->prefix_len;
         out->error = s->ctl_host->error;
+        out->graph_kernels = s->graph_kernels;
         s->kv_len[0] = out->kv_len[0];
         s->kv_len[1] = out->kv_len[1];
         s->patches = out->patches;
@@ -1566,6 +1582,115 @@ VXC_API int32_t vxc_read_latents(vxc_stream* s, int32_t first, int32_t count, fl
                            cudaMemcpyDeviceToHost, s->cs),
            "latents");
         ck(cudaStreamSynchronize(s->cs), "sync");
+    });
+}
+
+VXC_API int32_t vxc_profile_kernel(vxc_stream* s, int32_t kernel, int32_t iters, float* ms_per_launch,
+                                   double* bytes_per_launch) {
+    return guard([&] {
+        require(s != nullptr && ms_per_launch != nullptr && bytes_per_launch != nullptr, "null argument");
+        require(iters > 0 && iters <= 100000, "iters must be in [1, 100000]");
+        require(kernel >= VXC_PROF_DIT_GATEUP && kernel <= VXC_PROF_BASE_ATTN, "unknown kernel id");
+        std::lock_guard<std::mutex> lk(s->call_mutex);
+        const vxc_device* dev = s->dev;
+        const vxc_model_desc& d = dev->desc;
+        check_loaded(dev, {VXC_BASE_DECODER, VXC_DIT_ESTIMATOR});
+        DeviceGuard g(dev->device);
+        const int Hd = d.dit_hidden, Fd = d.dit_ffn, H = d.hidden, F = d.ffn;
+        const int M = 2 * dit_tokens_per_seq(d.patch_size);
+        const int hq = d.q_heads, hkv = d.kv_heads, hd = d.head_dim;
+        const size_t plane = static_cast<size_t>(hkv) * s->cap * hd;
+        double bytes = 0.0;
+        std::function<void()> launch;
+        const LayerW& DL = dev->dit[0];
+        const LayerW& BL = dev->base[0];
+        // the profiled decode kernels read kv_len from a private control block set to
+        // the next free cache row (the q/k/v launch writes there), so valid rows stay intact
+        const int pos = std::min(s->kv_len[0], s->cap - 1);
+        const int T = pos + 1;
+        switch (kernel) {
+            case VXC_PROF_DIT_GATEUP: {
+                RowsArgs a;
+                a.w = DL.wgateup; a.x = s->dxn; a.ldx = Hd; a.K = Hd; a.rows = Fd; a.M = M;
+                a.mode = GEMV_GATEUP; a.y = s->dact; a.ldy = Fd;
+                bytes = 2.0 * Fd * Hd * 2 + 4.0 * M * Hd + 4.0 * M * Fd;
+                launch = [=] { launch_rows_linear(a, s->cs, false); };
+                break;
+            }
+            case VXC_PROF_DIT_DOWN: {
+                RowsArgs a;
+                a.w = DL.wdown; a.x = s->dact; a.ldx = Fd; a.K = Fd; a.rows = Hd; a.M = M;
+                a.mode = GEMV_RESID; a.y = s->dxn; a.ldy = Hd;
+                bytes = 2.0 * Hd * Fd + 4.0 * M * Fd + 8.0 * M * Hd;
+                launch = [=] { launch_rows_linear(a, s->cs, false); };
+                break;
+            }
+            case VXC_PROF_DIT_QKV: {
+                const int W = (d.dit_q_heads + 2 * d.dit_kv_heads) * (Hd / d.dit_q_heads);
+                RowsArgs a;
+                a.w = DL.wqkv; a.x = s->dxn; a.ldx = Hd; a.K = Hd; a.rows = W; a.M = M;
+                a.y = s->dqkv; a.ldy = W;
+                bytes = 2.0 * W * Hd + 4.0 * M * Hd + 4.0 * M * W;
+                launch = [=] { launch_rows_linear(a, s->cs, false); };
+                break;
+            }
+            case VXC_PROF_BASE_GATEUP: {
+                GemvArgs a;
+                a.mode = GEMV_GATEUP; a.w = BL.wgateup; a.x = s->out[0]; a.norm_g = BL.post_norm; a.eps = d.rms_eps;
+                a.K = H; a.rows = F; a.y = s->act;
+                bytes = 2.0 * 2 * F * H + 4.0 * H + 4.0 * F;
+                launch = [=] { launch_gemv(a, s->cs, false); };
+                break;
+            }
+            case VXC_PROF_BASE_DOWN: {
+                GemvArgs a;
+                a.mode = GEMV_RESID; a.w = BL.wdown; a.x = s->act; a.K = F; a.rows = H; a.resid = s->out[0];
+                bytes = 2.0 * H * F + 4.0 * F + 8.0 * H;
+                launch = [=] { launch_gemv(a, s->cs, false); };
+                break;
+            }
+            case VXC_PROF_BASE_QKV:
+            case VXC_PROF_BASE_ATTN: {
+                // run on a private control block so the stream's positions stay untouched
+                StreamCtl probe{};
+                probe.kv_len[0] = pos;
+                StreamCtl* pctl = reinterpret_cast<StreamCtl*>(s->est);  // >= sizeof(StreamCtl) floats
+                ck(cudaMemcpyAsync(pctl, &probe, sizeof(StreamCtl), cudaMemcpyHostToDevice, s->cs), "probe ctl");
+                ck(cudaStreamSynchronize(s->cs), "sync");
+                if (kernel == VXC_PROF_BASE_QKV) {
+                    GemvArgs a;
+                    a.mode = GEMV_QKV; a.w = BL.wqkv; a.x = s->out[0]; a.norm_g = BL.in_norm; a.eps = d.rms_eps;
+                    a.K = H; a.rows = (hq + 2 * hkv) * hd / 2; a.y = s->q; a.q_heads = hq; a.kv_heads = hkv;
+                    a.head_dim = hd; a.rope_cos = s->rope_cos; a.rope_sin = s->rope_sin;
+                    a.k_cache = s->kc[0]; a.v_cache = s->vc[0]; a.cap = s->cap; a.which = 0; a.ctl = pctl;
+                    bytes = 2.0 * (hq + 2 * hkv) * hd * H + 4.0 * H + 4.0 * hq * hd + 4.0 * 2 * hkv * hd;
+                    launch = [=] { launch_gemv(a, s->cs, false); };
+                } else {
+                    AttnArgs a;
+                    a.q = s->q; a.k0 = s->kc[0]; a.v0 = s->vc[0]; a.len0 = s->cap; a.stride0 = s->cap;
+                    a.q_heads = hq; a.kv_heads = hkv; a.head_dim = hd; a.scale = 0.125f; a.splits = s->splits;
+                    a.partial = s->partial; a.counters = s->counters; a.out = s->attn; a.ctl = pctl; a.which = 0;
+                    bytes = 4.0 * 2 * hkv * static_cast<double>(T) * hd + 8.0 * hq * hd;
+                    launch = [=] { launch_attn_decode(a, false, s->cs, false); };
+                }
+                break;
+            }
+        }
+        (void)plane;
+        launch();  // warm-up
+        cudaEvent_t e0, e1;
+        ck(cudaEventCreate(&e0), "event");
+        ck(cudaEventCreate(&e1), "event");
+        ck(cudaEventRecord(e0, s->cs), "event");
+        for (int i = 0; i < iters; ++i) launch();
+        ck(cudaEventRecord(e1, s->cs), "event");
+        ck(cudaEventSynchronize(e1), "event");
+        float ms = 0.f;
+        ck(cudaEventElapsedTime(&ms, e0, e1), "event");
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+        *ms_per_launch = ms / static_cast<float>(iters);
+        *bytes_per_launch = bytes;
     });
 }
 

@@ -50,7 +50,12 @@ class Desc(C.Structure):
 
 class StreamState(C.Structure):
     _fields_ = [("kv_len", C.c_int32 * 2), ("patches", C.c_int32), ("stopped", C.c_int32),
-                ("stop_logits", C.c_float * 2), ("prefix_len", C.c_int32), ("error", C.c_int32)]
+                ("stop_logits", C.c_float * 2), ("prefix_len", C.c_int32), ("error", C.c_int32),
+                ("graph_kernels", C.c_int32)]
+
+
+PROFILE_KERNELS = {"dit_gateup": 0, "dit_down": 1, "dit_qkv": 2, "base_gateup": 3, "base_down": 4,
+                   "base_qkv": 5, "base_attn": 6}
 
 
 PROGRESS_FN = C.CFUNCTYPE(C.c_int32, C.c_void_p, C.c_int32, C.c_int32)
@@ -91,6 +96,7 @@ def _signatures():
         "vxc_read_state": ([vp, C.POINTER(StreamState)], i),
         "vxc_read_hidden": ([vp, vp, vp], i),
         "vxc_read_latents": ([vp, i, i, vp], i),
+        "vxc_profile_kernel": ([vp, i, i, C.POINTER(f), C.POINTER(C.c_double)], i),
         "vxc_stream_cuda_handle": ([vp, C.POINTER(vp)], i),
     }
 
@@ -155,7 +161,10 @@ class Device:
             self._h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except Exception:  # interpreter shutdown: module globals may already be gone
+            pass
 
 
 class Stream:
@@ -175,7 +184,10 @@ class Stream:
             self._h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except Exception:  # interpreter shutdown: module globals may already be gone
+            pass
 
     # -- KV cache runner ---------------------------------------------------
     def reset(self) -> None:
@@ -291,6 +303,13 @@ class Stream:
         out = np.empty((count, self.cfg.latent), np.float32)
         _check(lib().vxc_read_latents(self._h, first, count, _p(out)))
         return out
+
+    def profile_kernel(self, kernel: str, iters: int = 50):
+        """(ms per launch, algorithmic bytes per launch) of one hot kernel timed alone."""
+        ms = C.c_float()
+        nb = C.c_double()
+        _check(lib().vxc_profile_kernel(self._h, PROFILE_KERNELS[kernel], iters, C.byref(ms), C.byref(nb)))
+        return float(ms.value), float(nb.value)
 
     def cuda_stream(self) -> int:
         h = C.c_void_p()
