@@ -1387,6 +1387,19 @@ VXC_API int32_t vxc_sdpa(const float* q, int32_t heads, int32_t src, int32_t d, 
         cudaStream_t cs = static_cast<cudaStream_t>(cuda_stream);
         const float rs = scale == 0.f ? 1.f / std::sqrt(static_cast<float>(d)) : scale;
         const int G = heads / groups;
+        {
+            // the op may be used without a vxc_device: raise the kernels' shared-memory
+            // limits once per device on first use
+            static std::mutex attr_mu;
+            static std::vector<int> ready;
+            int dev_id = 0;
+            ck(cudaGetDevice(&dev_id), "cudaGetDevice");
+            std::lock_guard<std::mutex> lk(attr_mu);
+            if (std::find(ready.begin(), ready.end(), dev_id) == ready.end()) {
+                init_kernel_attributes();
+                ready.push_back(dev_id);
+            }
+        }
         if (src == 1 && d == 64 && dv == 64 && G <= 16 && mask_c <= 1 && groups <= 64) {
             // split-K flash decode over [past | cur] (fp32 rows). Its split partials
             // live in a scratch buffer kept per (device, CUDA stream): calls on one
