@@ -213,6 +213,23 @@ VXC_API int32_t vxc_sdpa(const float* q, int32_t heads, int32_t src, int32_t d, 
                          int32_t groups, int32_t cur, int32_t dv, const float* mask, int32_t mask_c,
                          const float* past_k, const float* past_v, int32_t past, float scale, float* out,
                          float* out_k, float* out_v, void* cuda_stream);
+/* No counterpart in the reference. vxc_sdpa for one query row (src = 1,
+ * head dim 64, at most 64 query heads, <= 16 per KV group, mask [past+cur] or
+ * NULL), for callers that cannot let a library allocate device memory -- a
+ * plugin host that forbids allocation inside its enqueue call, or a real-time
+ * thread that cannot absorb cudaMalloc's device synchronisation. It allocates
+ * nothing: its split-K scratch is a fixed 528.3 KiB device array that every GPU
+ * loading the library keeps until exit. The first call on a device resolves
+ * that array's address (and raises kernel shared-memory limits), so make it
+ * before any stream capture. Larger shapes return VXC_STATUS_INVALID_ARGUMENT.
+ * All calls share the one array: calls that overlap on the GPU (different
+ * streams, or host threads racing on one device) corrupt each other's results;
+ * serialise them, e.g. on one stream. Device pointers, asynchronous on
+ * cuda_stream (a cudaStream_t; NULL = legacy default stream). */
+VXC_API int32_t vxc_sdpa_decode_noalloc(const float* q, int32_t heads, int32_t d, const float* k, const float* v,
+                                        int32_t groups, int32_t cur, const float* mask, const float* past_k,
+                                        const float* past_v, int32_t past, float scale, float* out, float* out_k,
+                                        float* out_v, void* cuda_stream);
 /* The same on HOST pointers (what the ncnn CPU layer receives); synchronous. */
 VXC_API int32_t vxc_sdpa_host(const float* q, int32_t heads, int32_t src, int32_t d, const float* k,
                               const float* v, int32_t groups, int32_t cur, int32_t dv, const float* mask,

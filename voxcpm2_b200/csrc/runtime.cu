@@ -940,6 +940,9 @@ void prefill(vxc_stream* s, const int32_t* text_ids, int n_text) {
 
 vxc_stream::~vxc_stream() { free_all(this); }
 
+// Error message slot shared with the other translation units of the library.
+void vxc_internal_set_error(const char* msg) { g_last_error = msg; }
+
 // ==================================================================== C ABI ==
 extern "C" {
 

@@ -90,6 +90,7 @@ def _signatures():
         "vxc_generate": ([vp, vp, i, i, i, f, i, u, vp, C.POINTER(i), vp, vp, vp, PROGRESS_FN, vp], i),
         "vxc_sdpa": ([vp, i, i, i, vp, vp, i, i, i, vp, i, vp, vp, i, f, vp, vp, vp, vp], i),
         "vxc_sdpa_host": ([vp, i, i, i, vp, vp, i, i, i, vp, i, vp, vp, i, f, vp, vp, vp], i),
+        "vxc_sdpa_decode_noalloc": ([vp, i, i, vp, vp, i, i, vp, vp, vp, i, f, vp, vp, vp, vp], i),
         "vxc_upload_noise": ([vp, vp, i], i),
         "vxc_patch_step_async": ([vp, i, f, i], i),
         "vxc_stream_synchronize": ([vp], i),
@@ -342,3 +343,13 @@ def sdpa_device(q_ptr: int, heads: int, src: int, d: int, k_ptr: int, v_ptr: int
     _check(lib().vxc_sdpa(q_ptr, heads, src, d, k_ptr, v_ptr, groups, cur, dv, mask_ptr or None, mask_c,
                           pk_ptr or None, pv_ptr or None, past, scale, out_ptr, ok_ptr or None, ov_ptr or None,
                           stream or None))
+
+
+def sdpa_decode_noalloc(q_ptr: int, heads: int, d: int, k_ptr: int, v_ptr: int, groups: int, cur: int,
+                        mask_ptr: int, pk_ptr: int, pv_ptr: int, past: int, scale: float, out_ptr: int,
+                        ok_ptr: int = 0, ov_ptr: int = 0, stream: int = 0) -> None:
+    """vxc_sdpa_decode_noalloc on device pointers: one query row, no device allocation
+    (its scratch is a fixed array inside the library); asynchronous on 'stream'."""
+    _check(lib().vxc_sdpa_decode_noalloc(q_ptr, heads, d, k_ptr, v_ptr, groups, cur, mask_ptr or None,
+                                         pk_ptr or None, pv_ptr or None, past, scale, out_ptr, ok_ptr or None,
+                                         ov_ptr or None, stream or None))
