@@ -238,7 +238,7 @@ def run_ours(args):
     peak, peak_kind = measured_peaks()
     prof_ms, prof_bytes = streams[0].profile_kernel("dit_gateup", 100)
     achieved = prof_bytes / (prof_ms / 1e3) / 1e9
-    roofline = {"kernel": "rows_linear_kernel<GATEUP> (DiT gate/up, 2x11 tokens)", "bound": "hbm",
+    roofline = {"kernel": "tc_linear_kernel gate/up (DiT, tcgen05, 2x11 tokens)", "bound": "hbm",
                 "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                 "peak_kind": f"{peak_kind} burst copy bandwidth", "bytes_per_launch": prof_bytes,
                 "us_per_launch": 1e3 * prof_ms, "traffic": None}

@@ -250,6 +250,85 @@ __global__ void attn_rows_kernel(const float* qkv, int q_heads, int kv_heads, in
     }
 }
 
+__device__ __forceinline__ void split_store(__half* xb, int ld, int m, int col, float v) {
+    const __half hi = __float2half_rn(v);
+    xb[static_cast<size_t>(m) * ld + col] = hi;
+    xb[static_cast<size_t>(24 + m) * ld + col] = __float2half_rn(v - __half2float(hi));
+}
+
+__global__ void rmsnorm_rows_split_kernel(const float* x, int ldx, const __half* g, float eps, int K,
+                                          __half* xb, StreamCtl* ctl) {
+    __shared__ float red[32];
+    pdl_launch_dependents();
+    pdl_wait();
+    if (ctl && ctl->stopped) return;
+    const int m = blockIdx.x;
+    const float* xr = x + static_cast<size_t>(m) * ldx;
+    float ss = 0.f;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) ss += xr[k] * xr[k];
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float t = 0.f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += red[w];
+    const float a = rsqrtf(t / static_cast<float>(K) + eps);
+    for (int k = threadIdx.x; k < K; k += blockDim.x) split_store(xb, K, m, k, xr[k] * a * __half2float(g[k]));
+}
+
+// One CTA per (head, sequence): RoPE on q/k (apply_rotary_pos_emb, rotate_half),
+// scores, softmax and P.V for the sequence's rows (VoxCPM2SDPA without mask or
+// cache, voxcpm2_sdpa.cpp:187-252), written as the o projection's split operand.
+constexpr int kDitMaxSeq = 16;
+__global__ void __launch_bounds__(128) dit_attention_split_kernel(const float* qkv, int seq, int q_heads,
+                                                                  int kv_heads, const float* rope_cos,
+                                                                  const float* rope_sin, float scale, __half* xb,
+                                                                  StreamCtl* ctl) {
+    constexpr int D = 64, H = 32;
+    __shared__ float qs[kDitMaxSeq][D], ks[kDitMaxSeq][D], vs[kDitMaxSeq][D], ps[kDitMaxSeq][kDitMaxSeq + 1];
+    pdl_launch_dependents();
+    pdl_wait();
+    if (ctl && ctl->stopped) return;
+    const int h = blockIdx.x, sq = blockIdx.y, kvh = h / (q_heads / kv_heads);
+    const int width = (q_heads + 2 * kv_heads) * D;
+    for (int idx = threadIdx.x; idx < seq * D; idx += blockDim.x) {
+        const int i = idx / D, e = idx - i * D;
+        const float* row = qkv + static_cast<size_t>(sq * seq + i) * width;
+        const float c = rope_cos[i * D + e], sn = rope_sin[i * D + e];
+        const float* qp = row + h * D;
+        const float* kp = row + (q_heads + kvh) * D;
+        qs[i][e] = e < H ? qp[e] * c + (-qp[e + H]) * sn : qp[e] * c + qp[e - H] * sn;
+        ks[i][e] = e < H ? kp[e] * c + (-kp[e + H]) * sn : kp[e] * c + kp[e - H] * sn;
+        vs[i][e] = row[(q_heads + kv_heads + kvh) * D + e];
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < seq * seq; idx += blockDim.x) {
+        const int i = idx / seq, j = idx - i * seq;
+        float sum = 0.f;
+        for (int e = 0; e < D; ++e) sum = fmaf(qs[i][e], ks[j][e], sum);
+        ps[i][j] = sum * scale;
+    }
+    __syncthreads();
+    if (threadIdx.x < seq) {
+        const int i = threadIdx.x;
+        float mx = -FLT_MAX;
+        for (int j = 0; j < seq; ++j) mx = fmaxf(mx, ps[i][j]);
+        float sum = 0.f;
+        for (int j = 0; j < seq; ++j) {
+            ps[i][j] = expf(ps[i][j] - mx);
+            sum += ps[i][j];
+        }
+        for (int j = 0; j < seq; ++j) ps[i][j] /= sum;
+    }
+    __syncthreads();
+    const int ld = q_heads * D;
+    for (int idx = threadIdx.x; idx < seq * D; idx += blockDim.x) {
+        const int i = idx / D, e = idx - i * D;
+        float acc = 0.f;
+        for (int j = 0; j < seq; ++j) acc = fmaf(ps[i][j], vs[j][e], acc);
+        split_store(xb, ld, sq * seq + i, h * D + e, acc);
+    }
+}
+
 __global__ void embed_gather_kernel(const __half* table, const int32_t* ids, int H, float scale,
                                     float* out) {
     const int m = blockIdx.x;
@@ -604,6 +683,24 @@ void launch_dit_attention(const float* qkv, int nseq, int seq, int q_heads, int 
     check_launch(cudaLaunchKernelEx(&cfg, attn_rows_kernel<1>, qkv, q_heads, kv_heads, d, 0, seq,
                                     static_cast<const float*>(nullptr), static_cast<const float*>(nullptr), 0,
                                     scale, out, ctl));
+}
+
+void launch_rmsnorm_rows_split(const float* x, int ldx, const __half* g, float eps, int K, int M, __half* xb,
+                               StreamCtl* ctl, cudaStream_t s, bool pdl) {
+    if (M > 24) throw std::invalid_argument("rmsnorm_split: at most 24 rows");
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(dim3(M), dim3(256), 0, s, pdl, attr);
+    check_launch(cudaLaunchKernelEx(&cfg, rmsnorm_rows_split_kernel, x, ldx, g, eps, K, xb, ctl));
+}
+
+void launch_dit_attention_split(const float* qkv, int nseq, int seq, int q_heads, int kv_heads, int d,
+                                const float* rope_cos, const float* rope_sin, float scale, __half* xb,
+                                StreamCtl* ctl, cudaStream_t s, bool pdl) {
+    if (d != 64 || seq > kDitMaxSeq || nseq * seq > 24) throw std::invalid_argument("dit attention: unsupported shape");
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(dim3(q_heads, nseq), dim3(128), 0, s, pdl, attr);
+    check_launch(cudaLaunchKernelEx(&cfg, dit_attention_split_kernel, qkv, seq, q_heads, kv_heads, rope_cos, rope_sin,
+                                    scale, xb, ctl));
 }
 
 void launch_embed_gather(const __half* table, const int32_t* ids, int M, int H, float scale,

@@ -412,6 +412,7 @@ void init_kernel_attributes() {
     check_launch(cudaFuncSetAttribute(attn_decode_kernel<__half, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax));
     check_launch(cudaFuncSetAttribute(attn_decode_kernel<float, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax));
     init_batched_attributes();
+    init_tc_attributes();
 }
 
 void launch_final_norm(const float* h, const __half* g, float eps, int H, float* out, float* out2,

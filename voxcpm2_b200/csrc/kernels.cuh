@@ -1,6 +1,7 @@
 // Kernel launch interface of libvoxcpm2_cuda (host side, sm_100a).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -131,6 +132,17 @@ void launch_attn_rows_cache(const float* qkv, int M, int q_heads, int kv_heads, 
 void launch_dit_attention(const float* qkv, int nseq, int seq, int q_heads, int kv_heads, int d,
                           float scale, float* out, StreamCtl* ctl, cudaStream_t s, bool pdl);
 
+// DiT, tensor-core operand producers. Both write the next tcgen05 linear's B
+// operand: split fp16 rows [48][ld] (row m = fp16(v), row 24 + m = fp16(v - fp16(v))).
+// RMSNorm of the M residual rows:
+void launch_rmsnorm_rows_split(const float* x, int ldx, const __half* g, float eps, int K, int M, __half* xb,
+                               StreamCtl* ctl, cudaStream_t s, bool pdl);
+// RoPE (positions 0..seq-1) + full attention within each sequence, one CTA per
+// (head, sequence), from the fp32 q/k/v rows [nseq*seq][(hq+2hkv)d]:
+void launch_dit_attention_split(const float* qkv, int nseq, int seq, int q_heads, int kv_heads, int d,
+                                const float* rope_cos, const float* rope_sin, float scale, __half* xb,
+                                StreamCtl* ctl, cudaStream_t s, bool pdl);
+
 // h[m] = table[ids[m]] * scale
 void launch_embed_gather(const __half* table, const int32_t* ids, int M, int H, float scale,
                          float* out, cudaStream_t s);
@@ -191,6 +203,30 @@ void launch_sdpa_rows_f32(const float* q, int heads, int src, int d, const float
                           float scale, float* out, cudaStream_t s);
 void launch_concat_kv(const float* past, const float* cur, int groups, int past_len, int cur_len,
                       int d, float* out, cudaStream_t s);
+
+// ------------------------------------------------------- tcgen05 linear ---
+// Y = X W^T for <= 24 token rows on the 5th-generation tensor cores. A = W (fp16
+// [rows][K], tensor map box 64 rows x 64 cols, 128B swizzle); B = the token rows as
+// split fp16 [48][K] (rows m: fp16(x), rows 24 + m: fp16(x - fp16(x)); pad rows 0).
+struct TcLinearArgs {
+    int K = 0;           // multiple of 64
+    int M = 0;           // token rows (<= 24)
+    int rows = 0;        // output features (GATEUP: gate/up pairs)
+    int splits = 1;      // K split = cluster size (<= 8)
+    int gateup = 0;      // tile = 64 gate rows + the matching 64 up rows; out = SiLU(g) * u
+    int resid = 0;       // y += rscale * out (else y = out)
+    float rscale = 1.0f;
+    float* y = nullptr;  // fp32 [M][ldy] (plain / residual)
+    int ldy = 0;
+    __half* yb = nullptr;  // GATEUP: split-fp16 [48][ldyb], the next linear's B operand
+    int ldyb = 0;
+    StreamCtl* ctl = nullptr;  // receives error 3 if a bounded wait gave up
+};
+CUtensorMap make_tensor_map_f16(const void* base, int rows, int cols, int box_rows);
+size_t tc_linear_smem_bytes(int K, int splits);
+void launch_tc_linear(const CUtensorMap& map_a, const CUtensorMap& map_b, const TcLinearArgs& a, cudaStream_t s,
+                      bool pdl);
+void init_tc_attributes();
 
 // Raise the dynamic shared-memory limit of the kernels that need more than 48 KB
 // (call once per device, outside stream capture).

@@ -7,6 +7,7 @@
 // captured once as a CUDA graph (positions come from a device control block,
 // so the same graph is replayed for every patch).
 #include <algorithm>
+#include <array>
 #include <atomic>
 #include <cmath>
 #include <cstring>
@@ -169,6 +170,10 @@ void validate_desc(const vxc_model_desc& d) {
     require(d.rms_eps > 0.f && d.rope_theta > 0.f && d.rope_original_max > 0, "bad norm/rope settings");
     require(d.hidden <= 4096 && d.ffn <= 4096 && d.dit_hidden <= 4096 && d.dit_ffn <= 4096,
             "dimensions above 4096 are not supported");
+    // tensor-core DiT linears: 128-feature tiles (64 gate/up pairs), 64-wide K chunks, <= 24 token rows
+    require(d.dit_hidden % 128 == 0 && d.dit_ffn % 64 == 0 &&
+                ((d.dit_q_heads + 2 * d.dit_kv_heads) * 64) % 128 == 0 && 2 * (3 + 2 * d.patch_size) <= 24,
+            "DiT shape must tile by 128 features and 64-element K chunks");
     require(d.audio_start_token >= 0 && d.audio_start_token < d.vocab, "audio_start_token out of range");
 }
 
@@ -255,6 +260,8 @@ struct vxc_device {
     std::vector<LayerW> base, res, dit;
     const __half *base_norm = nullptr, *res_norm = nullptr, *dit_norm = nullptr;
     float *dit_rope_cos = nullptr, *dit_rope_sin = nullptr;  // positions 0..seq-1
+    // per DiT layer: TMA maps of W_qkv, W_o, W_gate|up, W_down (A operands)
+    std::vector<std::array<CUtensorMap, 4>> dit_maps;
 };
 
 namespace {
@@ -312,6 +319,9 @@ struct vxc_stream {
     float *temb = nullptr, *tmid = nullptr, *ttok = nullptr, *dtemb = nullptr, *dtmid = nullptr, *dttok = nullptr;
     float *dtemb1 = nullptr, *dtmid1 = nullptr, *dttok1 = nullptr;
     float *dh = nullptr, *dxn = nullptr, *dqkv = nullptr, *dattn = nullptr, *dact = nullptr, *est = nullptr;
+    // split-fp16 B operands of the DiT's tensor-core linears ([48][K], rows 24+m = residuals)
+    __half *xb_n = nullptr, *xb_a = nullptr, *xb_act = nullptr;
+    CUtensorMap map_xb_n{}, map_xb_a{}, map_xb_act{};
     float* gen_in = nullptr;  // staging for generic calls
     float* pin = nullptr;     // pinned host staging
     // prefill buffers (grown on demand)
@@ -343,7 +353,7 @@ void free_all(vxc_stream* s) {
                     s->partial, s->counters, s->mu, s->x, s->cond, s->cond0, s->noise, s->latents, s->temb,
                     s->tmid, s->ttok, s->dtemb, s->dtmid, s->dttok, s->dtemb1, s->dtmid1, s->dttok1, s->dh,
                     s->dxn, s->dqkv, s->dattn, s->dact, s->est, s->gen_in, s->ph, s->pxn, s->pqkv, s->pattn,
-                    s->pact, s->pcat, s->pids};
+                    s->pact, s->pcat, s->pids, s->xb_n, s->xb_a, s->xb_act};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     if (s->ctl_host) cudaFreeHost(s->ctl_host);
@@ -467,74 +477,69 @@ void enqueue_decoder_step(vxc_stream* s, int which, float* out, float* out2, int
     launch_final_norm(s->h[which], fnorm, d.rms_eps, H, out, out2, s->ctl, which, 1, skip, s->cs, true);
 }
 
-// DiT decoder over the 2 x seq rows in s->dh.
+// K split (cluster size) of a tensor-core linear: about one CTA per SM overall.
+int choose_splits(int tiles, int k) {
+    const int chunks = k / 64;
+    const int want = std::max(1, (148 + tiles / 2) / tiles);
+    return std::max(1, std::min({8, chunks, want}));
+}
+
+// DiT decoder over the 2 x seq rows in s->dh (DitEstimator.decoder,
+// export_components.py:625-659), the four linears of each layer on tcgen05.
 void enqueue_dit_layers(vxc_stream* s, StreamCtl* ctl) {
     const vxc_device* dev = s->dev;
     const vxc_model_desc& d = dev->desc;
     const int Hd = d.dit_hidden, F = d.dit_ffn, hq = d.dit_q_heads, hkv = d.dit_kv_heads, hd = Hd / hq;
     const int seq = dit_tokens_per_seq(d.patch_size), M = 2 * seq;
-    const int wqkv = (hq + 2 * hkv) * hd;
-    const int sk = ctl ? 1 : 0;
-    for (const LayerW& L : dev->dit) {
-        launch_rmsnorm_rows(s->dh, Hd, L.in_norm, d.rms_eps, Hd, M, s->dxn, Hd, ctl, sk, s->cs, true);
-        RowsArgs qa;
-        qa.w = L.wqkv;
-        qa.x = s->dxn;
-        qa.ldx = Hd;
+    const int W = (hq + 2 * hkv) * hd;
+    for (size_t l = 0; l < dev->dit.size(); ++l) {
+        const LayerW& L = dev->dit[l];
+        const std::array<CUtensorMap, 4>& maps = dev->dit_maps[l];
+        launch_rmsnorm_rows_split(s->dh, Hd, L.in_norm, d.rms_eps, Hd, M, s->xb_n, ctl, s->cs, true);
+        TcLinearArgs qa;
         qa.K = Hd;
-        qa.rows = wqkv;
         qa.M = M;
+        qa.rows = W;
+        qa.splits = choose_splits(W / 128, Hd);
         qa.y = s->dqkv;
-        qa.ldy = wqkv;
+        qa.ldy = W;
         qa.ctl = ctl;
-        qa.skip_if_stopped = sk;
-        launch_rows_linear(qa, s->cs, true);
-        launch_qkv_rows_post(s->dqkv, M, hq, hkv, hd, 0, seq, dev->dit_rope_cos, dev->dit_rope_sin, nullptr,
-                             nullptr, 0, ctl, s->cs, true);
-        launch_dit_attention(s->dqkv, 2, seq, hq, hkv, hd, 1.0f / std::sqrt(static_cast<float>(hd)), s->dattn,
-                             ctl, s->cs, true);
-        RowsArgs oa;
-        oa.w = L.wo;
-        oa.x = s->dattn;
-        oa.ldx = hq * hd;
+        launch_tc_linear(maps[0], s->map_xb_n, qa, s->cs, true);
+        launch_dit_attention_split(s->dqkv, 2, seq, hq, hkv, hd, dev->dit_rope_cos, dev->dit_rope_sin,
+                                   1.0f / std::sqrt(static_cast<float>(hd)), s->xb_a, ctl, s->cs, true);
+        TcLinearArgs oa;
         oa.K = hq * hd;
-        oa.rows = Hd;
         oa.M = M;
-        oa.mode = GEMV_RESID;
+        oa.rows = Hd;
+        oa.splits = choose_splits(Hd / 128, hq * hd);
+        oa.resid = 1;
         oa.rscale = d.dit_residual_scale;
         oa.y = s->dh;
         oa.ldy = Hd;
         oa.ctl = ctl;
-        oa.skip_if_stopped = sk;
-        launch_rows_linear(oa, s->cs, true);
-        launch_rmsnorm_rows(s->dh, Hd, L.post_norm, d.rms_eps, Hd, M, s->dxn, Hd, ctl, sk, s->cs, true);
-        RowsArgs ga;
-        ga.w = L.wgateup;
-        ga.x = s->dxn;
-        ga.ldx = Hd;
+        launch_tc_linear(maps[1], s->map_xb_a, oa, s->cs, true);
+        launch_rmsnorm_rows_split(s->dh, Hd, L.post_norm, d.rms_eps, Hd, M, s->xb_n, ctl, s->cs, true);
+        TcLinearArgs ga;
         ga.K = Hd;
-        ga.rows = F;
         ga.M = M;
-        ga.mode = GEMV_GATEUP;
-        ga.y = s->dact;
-        ga.ldy = F;
+        ga.rows = F;
+        ga.splits = choose_splits(F / 64, Hd);
+        ga.gateup = 1;
+        ga.yb = s->xb_act;
+        ga.ldyb = F;
         ga.ctl = ctl;
-        ga.skip_if_stopped = sk;
-        launch_rows_linear(ga, s->cs, true);
-        RowsArgs da;
-        da.w = L.wdown;
-        da.x = s->dact;
-        da.ldx = F;
+        launch_tc_linear(maps[2], s->map_xb_n, ga, s->cs, true);
+        TcLinearArgs da;
         da.K = F;
-        da.rows = Hd;
         da.M = M;
-        da.mode = GEMV_RESID;
+        da.rows = Hd;
+        da.splits = choose_splits(Hd / 128, F);
+        da.resid = 1;
         da.rscale = d.dit_residual_scale;
         da.y = s->dh;
         da.ldy = Hd;
         da.ctl = ctl;
-        da.skip_if_stopped = sk;
-        launch_rows_linear(da, s->cs, true);
+        launch_tc_linear(maps[3], s->map_xb_act, da, s->cs, true);
     }
 }
 
@@ -679,6 +684,7 @@ void sync_ctl(vxc_stream* s) {
         cudaStreamSynchronize(s->cs);
         if (err == 1) throw std::runtime_error("KV cache capacity exceeded on the device");
         if (err == 2) throw std::runtime_error("dit_estimator produced non-finite values");
+        if (err == 3) throw std::runtime_error("a tensor-core pipeline wait timed out");
         throw std::runtime_error("device-side check failed");
     }
     s->kv_len[0] = s->ctl_host->kv_len[0];
@@ -1014,6 +1020,13 @@ VXC_API int32_t vxc_load_weights(vxc_device* dev, int32_t component, const void*
             const __half* base = dev->blob[component] + 2 * (Hd * D + Hd) + 4 * (Hd * Hd + Hd);
             dev->dit = carve_decoder(base, dit_shape(dev->desc), &fn);
             dev->dit_norm = fn;
+            const int dh = dev->desc.dit_hidden, df = dev->desc.dit_ffn;
+            const int W = (dev->desc.dit_q_heads + 2 * dev->desc.dit_kv_heads) * 64;
+            dev->dit_maps.clear();
+            for (const LayerW& L : dev->dit)
+                dev->dit_maps.push_back({make_tensor_map_f16(L.wqkv, W, dh, 64), make_tensor_map_f16(L.wo, dh, dh, 64),
+                                         make_tensor_map_f16(L.wgateup, 2 * df, dh, 64),
+                                         make_tensor_map_f16(L.wdown, dh, df, 64)});
         }
     });
 }
@@ -1083,6 +1096,14 @@ VXC_API int32_t vxc_stream_create(vxc_device* dev, int32_t kv_capacity, vxc_stre
         s->dattn = dev_alloc<float>(M * Hd);
         s->dact = dev_alloc<float>(M * d.dit_ffn);
         s->est = dev_alloc<float>(2 * L);
+        for (__half** xb : {&s->xb_n, &s->xb_a, &s->xb_act}) {
+            const size_t k = xb == &s->xb_act ? d.dit_ffn : Hd;
+            *xb = dev_alloc<__half>(48 * k);
+            ck(cudaMemset(*xb, 0, 48 * k * sizeof(__half)), "operand");  // pad rows stay zero
+        }
+        s->map_xb_n = make_tensor_map_f16(s->xb_n, 48, static_cast<int>(Hd), 48);
+        s->map_xb_a = make_tensor_map_f16(s->xb_a, 48, static_cast<int>(Hd), 48);
+        s->map_xb_act = make_tensor_map_f16(s->xb_act, 48, d.dit_ffn, 48);
         s->gen_in = dev_alloc<float>(std::max(8 * Hd + 8 * L, 4 * H));
         ck(cudaMallocHost(&s->pin, sizeof(float) * (4 * std::max<size_t>(L, 2 * Hd) + 4 * H)), "cudaMallocHost");
         *out = s.release();
@@ -1626,28 +1647,31 @@ VXC_API int32_t vxc_profile_kernel(vxc_stream* s, int32_t kernel, int32_t iters,
         const int T = pos + 1;
         switch (kernel) {
             case VXC_PROF_DIT_GATEUP: {
-                RowsArgs a;
-                a.w = DL.wgateup; a.x = s->dxn; a.ldx = Hd; a.K = Hd; a.rows = Fd; a.M = M;
-                a.mode = GEMV_GATEUP; a.y = s->dact; a.ldy = Fd;
-                bytes = 2.0 * Fd * Hd * 2 + 4.0 * M * Hd + 4.0 * M * Fd;
-                launch = [=] { launch_rows_linear(a, s->cs, false); };
+                TcLinearArgs a;
+                a.K = Hd; a.M = M; a.rows = Fd; a.splits = choose_splits(Fd / 64, Hd); a.gateup = 1;
+                a.yb = s->xb_act; a.ldyb = Fd;
+                bytes = 2.0 * 2 * Fd * Hd + 2.0 * 48 * Hd + 2.0 * 48 * Fd;
+                const CUtensorMap ma = dev->dit_maps[0][2], mb = s->map_xb_n;
+                launch = [=] { launch_tc_linear(ma, mb, a, s->cs, false); };
                 break;
             }
             case VXC_PROF_DIT_DOWN: {
-                RowsArgs a;
-                a.w = DL.wdown; a.x = s->dact; a.ldx = Fd; a.K = Fd; a.rows = Hd; a.M = M;
-                a.mode = GEMV_RESID; a.y = s->dxn; a.ldy = Hd;
-                bytes = 2.0 * Hd * Fd + 4.0 * M * Fd + 8.0 * M * Hd;
-                launch = [=] { launch_rows_linear(a, s->cs, false); };
+                TcLinearArgs a;
+                a.K = Fd; a.M = M; a.rows = Hd; a.splits = choose_splits(Hd / 128, Fd); a.resid = 1;
+                a.y = s->dxn; a.ldy = Hd;
+                bytes = 2.0 * Hd * Fd + 2.0 * 48 * Fd + 8.0 * M * Hd;
+                const CUtensorMap ma = dev->dit_maps[0][3], mb = s->map_xb_act;
+                launch = [=] { launch_tc_linear(ma, mb, a, s->cs, false); };
                 break;
             }
             case VXC_PROF_DIT_QKV: {
                 const int W = (d.dit_q_heads + 2 * d.dit_kv_heads) * (Hd / d.dit_q_heads);
-                RowsArgs a;
-                a.w = DL.wqkv; a.x = s->dxn; a.ldx = Hd; a.K = Hd; a.rows = W; a.M = M;
+                TcLinearArgs a;
+                a.K = Hd; a.M = M; a.rows = W; a.splits = choose_splits(W / 128, Hd);
                 a.y = s->dqkv; a.ldy = W;
-                bytes = 2.0 * W * Hd + 4.0 * M * Hd + 4.0 * M * W;
-                launch = [=] { launch_rows_linear(a, s->cs, false); };
+                bytes = 2.0 * W * Hd + 2.0 * 48 * Hd + 4.0 * M * W;
+                const CUtensorMap ma = dev->dit_maps[0][0], mb = s->map_xb_n;
+                launch = [=] { launch_tc_linear(ma, mb, a, s->cs, false); };
                 break;
             }
             case VXC_PROF_BASE_GATEUP: {
