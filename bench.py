@@ -163,32 +163,67 @@ def run_reference(args):
     return 0
 
 
+# ---------------------------------------------------------------- ranks ---
+class Ranks:
+    """One process per GPU, launched by torchrun (RANK / LOCAL_RANK / WORLD_SIZE /
+    MASTER_* in the environment). The streams are independent, so the data path
+    has no collective: the process group only brackets the timed region with
+    barriers and takes the slowest rank's time."""
+
+    def __init__(self, backend: str = "nccl", device=None, timeout_s: int = 600):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.device = device
+        if self.world > 1:
+            import torch.distributed as dist
+            from datetime import timedelta
+            kw = {"device_id": device} if backend == "nccl" else {}
+            dist.init_process_group(backend, timeout=timedelta(seconds=timeout_s), **kw)
+
+    def barrier(self):
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max(self, x: float) -> float:
+        if self.world == 1:
+            return x
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([x], dtype=torch.float64, device=self.device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+def stream_seeds(rank: int, streams_per_gpu: int):
+    """(token-id seed, noise seed) of each stream on this rank: disjoint across ranks."""
+    return [(1000 + rank * streams_per_gpu + i, rank * streams_per_gpu + i) for i in range(streams_per_gpu)]
+
+
+def job_rate(world: int, streams_per_gpu: int, steps: int, seconds: float) -> float:
+    """Whole-job patches/s: every rank ran `steps` patches on each of its streams
+    within `seconds` (the slowest rank's time)."""
+    return world * streams_per_gpu * steps / seconds
+
+
 # --------------------------------------------------------------- GPU arm ---
 def run_ours(args):
     import torch
-    import torch.distributed as dist
     from voxcpm2_b200 import runtime as rt
     from voxcpm2_b200 import synthetic
     from voxcpm2_b200.config import BENCH
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    ranks = Ranks("nccl", torch.device("cuda", local))
+    world, rank = ranks.world, ranks.rank
+    barrier, max_over_ranks = ranks.barrier, ranks.max
 
     S, K, W = args.streams, args.steps, args.warmup
     cfg_info, min_patches = workload(S, K, W)
@@ -197,8 +232,9 @@ def run_ours(args):
     dev = rt.Device(cfg, local, synthetic.model_blobs(cfg, 0))
     cap = TEXT_TOKENS + 1 + W + K + 8
     streams = [rt.Stream(dev, kv_capacity=max(cap, 512)) for _ in range(S)]
-    ids = [synthetic.token_ids(cfg, TEXT_TOKENS, seed=1000 + rank * S + i) for i in range(S)]
-    noise = [synthetic.normal((W + K, L), seed=rank * S + i) for i in range(S)]
+    seeds = stream_seeds(rank, S)
+    ids = [synthetic.token_ids(cfg, TEXT_TOKENS, seed=a) for a, _ in seeds]
+    noise = [synthetic.normal((W + K, L), seed=b) for _, b in seeds]
 
     # ---- value: device-resident, graphs replayed from the uploaded noise tables
     for s, i, n in zip(streams, ids, noise):
@@ -232,7 +268,7 @@ def run_ours(args):
     states = [s.state() for s in streams]
     assert all(st.patches == W + K and st.error == 0 for st in states), "a stream did not complete its patches"
     graph_kernels = states[0].graph_kernels
-    value = world * S * K / (ms / 1e3)
+    value = job_rate(world, S, K, ms / 1e3)
 
     # ---- dominant kernel, timed alone with CUDA events on the stream
     peak, peak_kind = measured_peaks()
@@ -296,7 +332,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     barrier()
-    e2e_value = world * S * K / e2e_s
+    e2e_value = job_rate(world, S, K, e2e_s)
     calls = np.concatenate([np.array(c) for c in per_call]) * 1e3
     h2d = S * L * 4                   # each stream's noise patch
     d2h = S * (L * 4 + 40)            # each stream's latent patch + its 40-byte control block
@@ -327,8 +363,7 @@ def run_ours(args):
     for s in streams:
         s.close()
     dev.close()
-    if world > 1:
-        dist.destroy_process_group()
+    ranks.close()
     return 0
 
 
