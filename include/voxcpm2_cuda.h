@@ -101,15 +101,17 @@ typedef struct vxc_stream_state {
     int32_t graph_kernels;  /* kernel launches in one captured patch step (0 before the first) */
 } vxc_stream_state;
 
-/* Hot kernels vxc_profile_kernel can time in isolation. */
+/* Hot kernels vxc_profile_kernel can time. */
 enum {
-    VXC_PROF_DIT_GATEUP = 0,   /* DiT gate/up projection of layer 0 over the 2 x 11 tokens */
-    VXC_PROF_DIT_DOWN = 1,     /* DiT down projection of layer 0 */
-    VXC_PROF_DIT_QKV = 2,      /* DiT q/k/v projection of layer 0 */
-    VXC_PROF_BASE_GATEUP = 3,  /* base decoder gate/up GEMV of layer 0 (RMSNorm fused) */
-    VXC_PROF_BASE_DOWN = 4,    /* base decoder down GEMV of layer 0 */
-    VXC_PROF_BASE_QKV = 5,     /* base decoder q/k/v GEMV + RoPE + KV append of layer 0 */
-    VXC_PROF_BASE_ATTN = 6,    /* base decoder flash-decode attention of layer 0 */
+    VXC_PROF_DIT_GATEUP = 0,   /* DiT gate/up projection over the 2 x 11 tokens (post-attention RMSNorm fused) */
+    VXC_PROF_DIT_DOWN = 1,     /* DiT down projection + residual */
+    VXC_PROF_DIT_QKV = 2,      /* DiT q/k/v projection (input RMSNorm fused) */
+    VXC_PROF_BASE_GATEUP = 3,  /* base decoder gate/up GEMV (RMSNorm fused) */
+    VXC_PROF_BASE_DOWN = 4,    /* base decoder down GEMV */
+    VXC_PROF_BASE_QKV = 5,     /* base decoder q/k/v GEMV + RoPE + KV append */
+    VXC_PROF_BASE_ATTN = 6,    /* base decoder flash-decode attention */
+    VXC_PROF_DIT_O = 7,        /* DiT attention + o projection + residual */
+    VXC_PROF_DIT_LAYERS = 8,   /* persistent DiT decoder: all layers of one evaluation (one launch) */
 };
 
 /* Progress callback of vxc_generate: return non-zero to continue, zero to cancel
@@ -248,12 +250,16 @@ VXC_API int32_t vxc_read_state(vxc_stream* s, vxc_stream_state* out);
 VXC_API int32_t vxc_read_hidden(vxc_stream* s, float* lm, float* res);
 /* Latents of patches [first, first + count) generated since the last prefill. */
 VXC_API int32_t vxc_read_latents(vxc_stream* s, int32_t first, int32_t count, float* out);
-/* Times one hot kernel alone on the stream's own buffers: 'iters' back-to-back
- * launches between CUDA events on the stream (after one warm-up launch).
- * Writes the mean milliseconds per launch and the algorithmic bytes one launch
- * must move (weights + activations in + out). Call it between patch steps: it
- * leaves the stream's positions and valid KV rows as they were, but overwrites
- * scratch activations and the next free KV row of base layer 0. */
+/* Times one hot kernel on the stream's own buffers in the form the patch graph
+ * runs it: 'iters' launches cycling through the layers' weights (for the
+ * benchmark model more than the L2 holds), captured in one CUDA graph with
+ * programmatic dependent launch between them, timed with CUDA events on the
+ * stream after one warm-up replay. VXC_PROF_DIT_LAYERS times each persistent
+ * launch alone between two events. Writes the mean milliseconds per launch and
+ * the algorithmic bytes one launch must move (weights + activations in + out).
+ * Call it between patch steps: it leaves the stream's positions and valid KV
+ * rows as they were, but overwrites scratch activations and the next free KV
+ * row of every base layer. */
 VXC_API int32_t vxc_profile_kernel(vxc_stream* s, int32_t kernel, int32_t iters, float* ms_per_launch,
                                    double* bytes_per_launch);
 /* The stream's cudaStream_t, for callers timing it with CUDA events. */

@@ -15,7 +15,7 @@ import pytest
 import oracle
 from conftest import close_stats
 from voxcpm2_b200 import synthetic
-from voxcpm2_b200.config import BENCH, TINY
+from voxcpm2_b200.config import BENCH, DIT_ESTIMATOR, TINY
 
 pytestmark = pytest.mark.gpu
 
@@ -226,5 +226,50 @@ def test_non_finite_estimator_output_raises(rt):
     with pytest.raises(rt.VxcError) as e:
         s.patch_step(np.zeros(TINY.latent, np.float32), 2, 0)
     assert "non-finite" in str(e.value)
+    s.close()
+    dev.close()
+
+
+def test_dit_layer_forms_agree(rt, bench, monkeypatch):
+    """The three forms of the DiT decoder match the oracle: the persistent
+    launch (one cooperative kernel per estimator evaluation, the default), the
+    fused 4-launch layers (RMSNorm and attention built inside the tensor-core
+    linears) and the 7-launch layers."""
+    cfg, blobs, dev, orc = bench
+    ids = synthetic.token_ids(cfg, 16, seed=4)
+    want = orc.generate(ids, min_patches=100, timesteps=10, cfg_value=2.0, max_patches_override=3, seed=2)
+    streams = {}
+    for form in ("persistent", "fused", "split"):
+        monkeypatch.setenv("VXC_DIT_FORM", form)
+        streams[form] = rt.Stream(dev, kv_capacity=64)
+    monkeypatch.delenv("VXC_DIT_FORM")
+    for form, s in streams.items():
+        got = s.generate(ids, min_patches=100, timesteps=10, cfg_value=2.0, max_patches_override=3, seed=2)
+        compare_runs(got, want, f"{form} DiT layers", 100)
+    n_layers, evals = cfg.dit_layers, 9
+    k = {form: s.state().graph_kernels for form, s in streams.items()}
+    assert k["split"] - k["fused"] == 3 * n_layers * evals
+    assert k["fused"] - k["persistent"] == (4 * n_layers - 1) * evals
+    for s in streams.values():
+        s.close()
+
+
+def test_time_tables_follow_weight_reload(rt, tiny):
+    """The per-T time-token tables are derived from the DiT weights: a reload of
+    those weights must show up in the next patch."""
+    cfg, blobs, _, _ = tiny
+    dev = rt.Device(cfg, 0, blobs)
+    s = rt.Stream(dev, kv_capacity=64)
+    ids = synthetic.token_ids(cfg, 8, seed=6)
+    s.generate(ids, min_patches=2, timesteps=6, cfg_value=2.0, max_patches_override=3, seed=3)
+    other = synthetic.model_blobs(cfg, 1)
+    dit = DIT_ESTIMATOR
+    dev.load(dit, other[dit])
+    mixed = dict(blobs)
+    mixed[dit] = other[dit]
+    want = oracle.Oracle(cfg, mixed).generate(ids, min_patches=2, timesteps=6, cfg_value=2.0,
+                                              max_patches_override=3, seed=3)
+    got = s.generate(ids, min_patches=2, timesteps=6, cfg_value=2.0, max_patches_override=3, seed=3)
+    compare_runs(got, want, "after DiT weight reload", 2)
     s.close()
     dev.close()

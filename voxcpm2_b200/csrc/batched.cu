@@ -338,45 +338,90 @@ __global__ void embed_gather_kernel(const __half* table, const int32_t* ids, int
 }
 
 // ------------------------------------------------------------------ DiT ---
-// hidden[b] = [mu_b0, mu_b1, t_b + dt_b, cond_proj(cond_b frames), in_proj(x_b frames)]
-__global__ void dit_embed_kernel(const DitEmbedArgs a) {
+// DiT input rows of both CFG sequences: [mu0, mu1, t + dt, cond_proj(cond) x P,
+// in_proj(x) x P]. One CTA per 32 hidden features: the features' in/cond weight
+// rows are staged in shared memory (row stride 2D + 1 floats: conflict-free
+// column reads), then each thread computes 4P / 8 of the feature's 4P dot
+// products (2 sequences x P frames x {in, cond}).
+constexpr int kEmbedFeatures = 32;
+constexpr int kEmbedThreads = 256;
+
+__global__ void __launch_bounds__(kEmbedThreads) dit_embed_kernel(const DitEmbedArgs a) {
     extern __shared__ float sm[];
     pdl_launch_dependents();
+    const int D = a.D, P = a.P, DP = D * P, ws = 2 * D + 1;
+    const int f0 = blockIdx.x * kEmbedFeatures;
+    float* w_s = sm;                              // [32][2D + 1]: in row, cond row
+    float* xs = sm + kEmbedFeatures * ws;         // [2][D*P]
+    float* cs = xs + 2 * DP;                      // [2][D*P]
+    // weights first: they do not depend on the previous kernel
+    for (int i = threadIdx.x; i < kEmbedFeatures * 2 * D; i += kEmbedThreads) {
+        const int fl = i / (2 * D), r = i - fl * 2 * D, kind = r / D, e = r - kind * D;
+        const int f = f0 + fl;
+        float w = 0.f;
+        if (f < a.Hd) w = __half2float((kind == 0 ? a.in_w : a.cond_w)[static_cast<size_t>(f) * D + e]);
+        w_s[fl * ws + kind * D + e] = w;
+    }
     pdl_wait();
+    if (a.sync_reset && blockIdx.x == 0)
+        for (int i = threadIdx.x; i < a.sync_words; i += kEmbedThreads) a.sync_reset[i] = 0u;
     if (a.ctl && a.ctl->stopped) return;
-    const int DP = a.D * a.P;
-    float* xs = sm;           // [2][D*P]
-    float* cs = sm + 2 * DP;  // [2][D*P]
-    for (int i = threadIdx.x; i < DP; i += blockDim.x) {
+    for (int i = threadIdx.x; i < DP; i += kEmbedThreads) {
         xs[i] = a.x[i];
         xs[DP + i] = a.x_uncond ? a.x_uncond[i] : a.x[i];
         cs[i] = a.cond[i];
         cs[DP + i] = a.cond_uncond ? a.cond_uncond[i] : a.cond[i];
     }
     __syncthreads();
-    const int f = blockIdx.x * blockDim.x + threadIdx.x;
-    if (f >= a.Hd) return;
-    const int seq = 3 + 2 * a.P;
-    const __half* wi = a.in_w + static_cast<size_t>(f) * a.D;
-    const __half* wc = a.cond_w + static_cast<size_t>(f) * a.D;
-    const float bi = __half2float(a.in_b[f]), bc = __half2float(a.cond_b[f]);
-    for (int b = 0; b < 2; ++b) {
-        float* h = a.hidden + static_cast<size_t>(b) * seq * a.Hd;
+    const int fl = threadIdx.x & (kEmbedFeatures - 1), j = threadIdx.x / kEmbedFeatures;
+    const int f = f0 + fl;
+    const bool live = f < a.Hd;
+    const int seq = 3 + 2 * P;
+    __shared__ float vals[24][kEmbedFeatures + 1];  // this block's outputs, for the sums of squares
+    if (j < 2) {  // mu tokens and the time token of sequence j
+        const int b = j;
         const float* mu = b == 0 ? a.mu : a.mu_uncond;
-        h[f] = mu ? mu[f] : 0.f;
-        h[a.Hd + f] = mu ? mu[a.Hd + f] : 0.f;
-        h[2 * a.Hd + f] = (b == 0 ? a.t_tok0 : a.t_tok1)[f] + (b == 0 ? a.dt_tok0 : a.dt_tok1)[f];
-        for (int p = 0; p < a.P; ++p) {
-            float sx = 0.f, scd = 0.f;
-            for (int e = 0; e < a.D; ++e) {
-                // frame p of a d-major [D][P] patch
-                sx = fmaf(__half2float(wi[e]), xs[b * DP + e * a.P + p], sx);
-                scd = fmaf(__half2float(wc[e]), cs[b * DP + e * a.P + p], scd);
-            }
-            h[static_cast<size_t>(3 + p) * a.Hd + f] = scd + bc;
-            h[static_cast<size_t>(3 + a.P + p) * a.Hd + f] = sx + bi;
+        float v0 = 0.f, v1 = 0.f, v2 = 0.f;
+        if (live) {
+            v0 = mu ? mu[f] : 0.f;
+            v1 = mu ? mu[a.Hd + f] : 0.f;
+            v2 = a.tsum ? a.tsum[f] : (b == 0 ? a.t_tok0 : a.t_tok1)[f] + (b == 0 ? a.dt_tok0 : a.dt_tok1)[f];
+            float* h = a.hidden + static_cast<size_t>(b) * seq * a.Hd;
+            h[f] = v0;
+            h[a.Hd + f] = v1;
+            h[2 * a.Hd + f] = v2;
+        }
+        if (b * seq + 2 < 24) {
+            vals[b * seq][fl] = v0;
+            vals[b * seq + 1][fl] = v1;
+            vals[b * seq + 2][fl] = v2;
         }
     }
+    const float* wr = w_s + fl * ws;
+    for (int o = j; o < 4 * P; o += kEmbedThreads / kEmbedFeatures) {
+        const int kind = o & 1, b = (o >> 1) & 1, p = o >> 2;
+        const float* src = (kind == 0 ? xs : cs) + b * DP + p;
+        const float* w = wr + kind * D;
+        float acc = 0.f;
+        for (int e = 0; e < D; ++e) acc = fmaf(w[e], src[e * P], acc);  // frame p of a d-major [D][P] patch
+        const int tok = kind == 0 ? 3 + P + p : 3 + p;
+        const float v = live ? acc + __half2float(kind == 0 ? a.in_b[f] : a.cond_b[f]) : 0.f;
+        if (live) a.hidden[static_cast<size_t>(b * seq + tok) * a.Hd + f] = v;
+        if (b * seq + tok < 24) vals[b * seq + tok][fl] = v;
+    }
+    if (a.ssq_out) {
+        __syncthreads();
+        if (threadIdx.x < 2 * seq && threadIdx.x < 24) {
+            float t = 0.f;
+            for (int i = 0; i < kEmbedFeatures; ++i) t += vals[threadIdx.x][i] * vals[threadIdx.x][i];
+            a.ssq_out[blockIdx.x * 24 + threadIdx.x] = t;
+        }
+    }
+}
+
+__global__ void vec_add_kernel(const float* a, const float* b, float* out, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = a[i] + b[i];
 }
 
 __global__ void timestep_embedding_kernel(float t_or_step, float timesteps, int schedule,
@@ -402,70 +447,66 @@ __global__ void timestep_embedding_kernel(float t_or_step, float timesteps, int 
 }
 
 // final norm of the x rows, out_proj, then CFG-zero* and the Euler step
-// (synthesizer.cpp:147-161). One CTA.
-__global__ void __launch_bounds__(256) dit_out_kernel(const DitOutArgs a) {
+// (synthesizer.cpp:147-161). Each CTA normalises the 2P x rows into shared
+// memory and computes kOutFeatures output features of both CFG rows; the last
+// CTA to arrive reads the whole [2][D*P] estimate back and runs the CFG-zero*
+// scale (double, fixed summation order) and the Euler update.
+constexpr int kOutFeatures = 4;
+constexpr int kOutThreads = 256;
+
+__global__ void __launch_bounds__(kOutThreads) dit_out_kernel(const DitOutArgs a) {
     extern __shared__ float sm[];
-    __shared__ float red[32];
-    __shared__ double dred[2][8];
+    __shared__ double dred[2][kOutThreads / 32];
+    __shared__ int s_last;
     pdl_launch_dependents();
+    const int R = 2 * a.P;        // rows (b, p), at most 8
+    const int L = a.D * a.P;      // latent size
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = kOutThreads / 32;
+    float* xn = sm;               // [R][Hd]
+    float* wsm = sm + R * a.Hd;   // [kOutFeatures][Hd] out_proj rows of this CTA
+    const int e0 = blockIdx.x * kOutFeatures;
+    for (int i = threadIdx.x; i < kOutFeatures * a.Hd; i += kOutThreads) {
+        const int el = i / a.Hd, k = i - el * a.Hd;
+        wsm[i] = e0 + el < a.D ? __half2float(a.out_w[static_cast<size_t>(e0 + el) * a.Hd + k]) : 0.f;
+    }
     pdl_wait();
     if (a.ctl && a.ctl->stopped) return;
-    const int R = 2 * a.P;        // rows (b, p)
-    const int L = a.D * a.P;      // latent size
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    float* xn = sm;               // [R][Hd]
-    float* est = sm + R * a.Hd;   // [2][L]
-    for (int r = 0; r < R; ++r) {
+    // warp r normalises row r
+    for (int r = warp; r < R; r += nw) {
         const int b = r / a.P, p = r - b * a.P;
         const float* h = a.hidden + (static_cast<size_t>(b) * a.seq + 3 + a.P + p) * a.Hd;
         float ss = 0.f;
-        for (int k = threadIdx.x; k < a.Hd; k += blockDim.x) ss += h[k] * h[k];
+        for (int k = lane; k < a.Hd; k += 32) ss = fmaf(h[k], h[k], ss);
         ss = warp_sum(ss);
-        if (lane == 0) red[warp] = ss;
-        __syncthreads();
-        float t = 0.f;
-        for (int w = 0; w < nw; ++w) t += red[w];
-        const float inv = rsqrtf(t / static_cast<float>(a.Hd) + a.eps);
-        for (int k = threadIdx.x; k < a.Hd; k += blockDim.x)
-            xn[r * a.Hd + k] = h[k] * inv * __half2float(a.norm_g[k]);
-        __syncthreads();
-    }
-    // out_proj: warp per output feature e, all R rows
-    for (int e = warp; e < a.D; e += nw) {
-        float acc[8];
-#pragma unroll
-        for (int r = 0; r < 8; ++r) acc[r] = 0.f;
-        const __half* wr = a.out_w + static_cast<size_t>(e) * a.Hd;
-        for (int k = lane * 8; k < a.Hd; k += kWarp * 8) {
-            const uint4 w = __ldg(reinterpret_cast<const uint4*>(wr + k));
-#pragma unroll
-            for (int r = 0; r < 8; ++r) {
-                if (r < R) {
-                    const float4 x0 = *reinterpret_cast<const float4*>(&xn[r * a.Hd + k]);
-                    const float4 x1 = *reinterpret_cast<const float4*>(&xn[r * a.Hd + k + 4]);
-                    acc[r] = dot8(w, x0, x1, acc[r]);
-                }
-            }
-        }
-        const float bias = __half2float(a.out_b[e]);
-#pragma unroll
-        for (int r = 0; r < 8; ++r) {
-            const float v = warp_sum(acc[r]);
-            if (lane == 0 && r < R) {
-                const int b = r / a.P, p = r - b * a.P;
-                est[b * L + e * a.P + p] = v + bias;  // [2][D][P]
-            }
-        }
+        const float inv = rsqrtf(ss / static_cast<float>(a.Hd) + a.eps);
+        for (int k = lane; k < a.Hd; k += 32) xn[r * a.Hd + k] = h[k] * inv * __half2float(a.norm_g[k]);
     }
     __syncthreads();
-    if (a.est_out)
-        for (int i = threadIdx.x; i < 2 * L; i += blockDim.x) a.est_out[i] = est[i];
+    // (feature, row) pairs: warp w takes pairs w, w + 8, ...
+    for (int q = warp; q < kOutFeatures * R; q += nw) {
+        const int el = q / R, r = q - el * R, e = e0 + el;
+        if (e >= a.D) continue;
+        float acc = 0.f;
+        for (int k = lane; k < a.Hd; k += 32) acc = fmaf(wsm[el * a.Hd + k], xn[r * a.Hd + k], acc);
+        acc = warp_sum(acc);
+        if (lane == 0) {
+            const int b = r / a.P, p = r - b * a.P;
+            a.est_buf[b * L + e * a.P + p] = acc + __half2float(a.out_b[e]);  // [2][D][P]
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(a.counter, 1) == static_cast<int>(gridDim.x) - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (threadIdx.x == 0) *a.counter = 0;
     if (!a.x) return;
     // optimized_scale in double (synthesizer.cpp:76-84) + finiteness check (:150)
     double dot = 0.0, nrm = 0.0;
     int bad = 0;
-    for (int i = threadIdx.x; i < L; i += blockDim.x) {
-        const float p = est[i], n = est[L + i];
+    for (int i = threadIdx.x; i < L; i += kOutThreads) {
+        const float p = __ldcg(a.est_buf + i), n = __ldcg(a.est_buf + L + i);
         if (!isfinite(p) || !isfinite(n)) bad = 1;
         dot += static_cast<double>(p) * n;
         nrm += static_cast<double>(n) * n;
@@ -491,8 +532,8 @@ __global__ void __launch_bounds__(256) dit_out_kernel(const DitOutArgs a) {
         nm += dred[1][w];
     }
     const float sc = static_cast<float>(dt_ / nm);
-    for (int i = threadIdx.x; i < L; i += blockDim.x) {
-        const float pos = est[i], neg = est[L + i];
+    for (int i = threadIdx.x; i < L; i += kOutThreads) {
+        const float pos = __ldcg(a.est_buf + i), neg = __ldcg(a.est_buf + L + i);
         const float dphi = neg * sc + a.cfg * (pos - neg * sc);
         a.x[i] -= a.dt * dphi;
     }
@@ -626,6 +667,7 @@ void init_batched_attributes() {
     constexpr int kMax = 200 * 1024;
     check_launch(cudaFuncSetAttribute(attn_rows_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax));
     check_launch(cudaFuncSetAttribute(dit_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax));
+    check_launch(cudaFuncSetAttribute(dit_embed_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax));
     check_launch(cudaFuncSetAttribute(sdpa_rows_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax));
 }
 
@@ -711,9 +753,16 @@ void launch_embed_gather(const __half* table, const int32_t* ids, int M, int H, 
 
 void launch_dit_embed(const DitEmbedArgs& a, cudaStream_t s, bool pdl) {
     cudaLaunchAttribute attr[1];
-    const size_t smem = static_cast<size_t>(4 * a.D * a.P) * sizeof(float);
-    cudaLaunchConfig_t cfg = make_cfg(dim3((a.Hd + 127) / 128), dim3(128), smem, s, pdl, attr);
+    const size_t smem = static_cast<size_t>(kEmbedFeatures * (2 * a.D + 1) + 4 * a.D * a.P) * sizeof(float);
+    if (smem > 200 * 1024) throw std::invalid_argument("dit_embed: patch too large");
+    cudaLaunchConfig_t cfg = make_cfg(dim3((a.Hd + kEmbedFeatures - 1) / kEmbedFeatures), dim3(kEmbedThreads), smem,
+                                      s, pdl, attr);
     check_launch(cudaLaunchKernelEx(&cfg, dit_embed_kernel, a));
+}
+
+void launch_vec_add(const float* a, const float* b, float* out, int n, cudaStream_t s) {
+    vec_add_kernel<<<(n + 255) / 256, 256, 0, s>>>(a, b, out, n);
+    check_launch(cudaGetLastError());
 }
 
 void launch_timestep_embedding(float t_or_step, float timesteps, int schedule, int half_dim,
@@ -725,11 +774,12 @@ void launch_timestep_embedding(float t_or_step, float timesteps, int schedule, i
 }
 
 void launch_dit_out(const DitOutArgs& a, cudaStream_t s, bool pdl) {
-    if (2 * a.P > 8 || a.Hd % 8 != 0) throw std::invalid_argument("dit_out: unsupported patch shape");
-    const size_t smem = static_cast<size_t>(2 * a.P * a.Hd + 2 * a.D * a.P) * sizeof(float);
+    if (!a.est_buf || !a.counter) throw std::invalid_argument("dit_out: scratch buffers missing");
+    const size_t smem = static_cast<size_t>(2 * a.P + kOutFeatures) * a.Hd * sizeof(float);
     if (smem > 200 * 1024) throw std::invalid_argument("dit_out: hidden too large");
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = make_cfg(dim3(1), dim3(256), smem, s, pdl, attr);
+    cudaLaunchConfig_t cfg = make_cfg(dim3((a.D + kOutFeatures - 1) / kOutFeatures), dim3(kOutThreads), smem, s, pdl,
+                                      attr);
     check_launch(cudaLaunchKernelEx(&cfg, dit_out_kernel, a));
 }
 

@@ -192,56 +192,55 @@ void dispatch_gemv(const GemvArgs& a, cudaStream_t s, bool pdl) {
 }
 
 // ------------------------------------------------------------ attention ---
-template <typename KV>
-__device__ __forceinline__ float load_kv(const KV* p, int e);
-template <>
-__device__ __forceinline__ float load_kv<__half>(const __half* p, int e) { return __half2float(p[e]); }
-template <>
-__device__ __forceinline__ float load_kv<float>(const float* p, int e) { return p[e]; }
-
 constexpr int kAttnThreads = 128;
 constexpr int kMaxGroup = 16;
 
 constexpr int kMinKeysPerSplit = 16;
 
+// four consecutive elements of a K/V row starting at element c (c % 4 == 0;
+// rows start on 16-byte boundaries, which the launcher checks)
 template <typename KV>
-__device__ __forceinline__ void load_row64(const KV* p, float* r);
+__device__ __forceinline__ void load4(const KV* p, int c, float* r);
 template <>
-__device__ __forceinline__ void load_row64<float>(const float* p, float* r) {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        const float4 v = *reinterpret_cast<const float4*>(p + 4 * i);
-        r[4 * i] = v.x;
-        r[4 * i + 1] = v.y;
-        r[4 * i + 2] = v.z;
-        r[4 * i + 3] = v.w;
-    }
+__device__ __forceinline__ void load4<float>(const float* p, int c, float* r) {
+    const float4 v = *reinterpret_cast<const float4*>(p + c);
+    r[0] = v.x;
+    r[1] = v.y;
+    r[2] = v.z;
+    r[3] = v.w;
 }
 template <>
-__device__ __forceinline__ void load_row64<__half>(const __half* p, float* r) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const uint4 v = *reinterpret_cast<const uint4*>(p + 8 * i);
-        const __half2* h = reinterpret_cast<const __half2*>(&v);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float2 f = __half22float2(h[j]);
-            r[8 * i + 2 * j] = f.x;
-            r[8 * i + 2 * j + 1] = f.y;
-        }
-    }
+__device__ __forceinline__ void load4<__half>(const __half* p, int c, float* r) {
+    const uint2 v = *reinterpret_cast<const uint2*>(p + c);
+    const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+    const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+    r[0] = lo.x;
+    r[1] = lo.y;
+    r[2] = hi.x;
+    r[3] = hi.y;
 }
 
 // Split-K flash decode. The number of active splits follows the current key
 // count T (at least kMinKeysPerSplit keys each, at most 'splits'), so short
-// caches do not pay for empty splits; inactive CTAs leave at once. The last
-// active CTA of a KV head combines the partial (max, sum, P.V) triples, staged in
-// shared memory with one parallel load so the combine costs one L2 round trip.
+// caches do not pay for empty splits; inactive CTAs leave at once. Each split
+// walks its keys in tiles of kKeyTile rows: the tile's K and V rows are staged
+// in shared memory by one batch of parallel loads, scores for all G query heads
+// of the KV group come from shared memory, and an online softmax (running max
+// and sum per head) rescales the P.V accumulators. The last active CTA of a KV
+// head combines the partial (max, sum, P.V) triples.
+constexpr int kKeyTile = 32;
+constexpr int kRowPad = 65;  // padded shared-memory row: conflict-free column reads
+
 template <typename KV, int D>
-__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArgs a, int max_chunk) {
-    extern __shared__ float sm[];
-    __shared__ float s_m[kMaxGroup], s_l[kMaxGroup];
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArgs a) {
+    static_assert(D == 64, "head_dim 64");
+    __shared__ float qs[kMaxGroup][kRowPad];
+    __shared__ float ks[kKeyTile][kRowPad];
+    __shared__ float vs[kKeyTile][D];
+    __shared__ float sc[kMaxGroup][kKeyTile];
+    __shared__ float m_s[kMaxGroup], l_s[kMaxGroup], alpha_s[kMaxGroup];
     __shared__ int s_last;
+    extern __shared__ float ps[];  // combine staging: [splits][G][D + 2]
     pdl_launch_dependents();
     pdl_wait();
     if (a.skip_if_stopped && a.ctl && a.ctl->stopped) return;
@@ -259,66 +258,88 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
     if (split >= active) return;
     const int chunk = (T + active - 1) / active;
     const int t0 = split * chunk;
-    const int n = max(0, min(min(T, t0 + chunk) - t0, max_chunk));
+    const int n = max(0, min(T, t0 + chunk) - t0);
 
-    float* qs = sm;                 // [G][D]
-    float* sc = sm + G * D;         // [G][max_chunk]
-    for (int i = tid; i < G * D; i += kAttnThreads) qs[i] = a.q[kvh * G * D + i] * a.scale;
-    __syncthreads();
-
+    for (int i = tid; i < G * D; i += kAttnThreads) qs[i / D][i % D] = a.q[kvh * G * D + i] * a.scale;
+    if (tid < G) {
+        m_s[tid] = -1e30f;
+        l_s[tid] = 0.f;
+    }
     const KV* k0 = static_cast<const KV*>(a.k0) + static_cast<size_t>(kvh) * a.stride0 * D;
     const KV* v0 = static_cast<const KV*>(a.v0) + static_cast<size_t>(kvh) * a.stride0 * D;
     const KV* k1 = a.k1 ? static_cast<const KV*>(a.k1) + static_cast<size_t>(kvh) * a.stride1 * D : nullptr;
     const KV* v1 = a.v1 ? static_cast<const KV*>(a.v1) + static_cast<size_t>(kvh) * a.stride1 * D : nullptr;
 
-    // scores: one key row per thread, all G heads of the group
-    for (int t = tid; t < n; t += kAttnThreads) {
-        const int row = t0 + t;
-        const KV* kp = row < len0 ? k0 + static_cast<size_t>(row) * D : k1 + static_cast<size_t>(row - len0) * D;
-        float kr[D];
-        load_row64(kp, kr);
-        const float madd = a.mask ? a.mask[row] : 0.f;
-        for (int g = 0; g < G; ++g) {
-            float s = 0.f;
+    // P.V ownership: column e, and half of the group's heads
+    const int e = tid & (D - 1), gh = tid / D;
+    const int hg = (G + 1) / 2, g_lo = gh * hg, g_hi = min(G, g_lo + hg);
+    float acc[8];
 #pragma unroll
-            for (int e = 0; e < D; ++e) s = fmaf(qs[g * D + e], kr[e], s);
-            sc[g * max_chunk + t] = s + madd;
-        }
-    }
-    __syncthreads();
-    // softmax statistics per head (one warp per head)
-    for (int g = warp; g < G; g += kAttnThreads / kWarp) {
-        float m = -1e30f;
-        for (int t = lane; t < n; t += kWarp) m = fmaxf(m, sc[g * max_chunk + t]);
-        m = warp_max(m);
-        float l = 0.f;
-        for (int t = lane; t < n; t += kWarp) {
-            const float p = __expf(sc[g * max_chunk + t] - m);
-            sc[g * max_chunk + t] = p;
-            l += p;
-        }
-        l = warp_sum(l);
-        if (lane == 0) {
-            s_m[g] = n > 0 ? m : -1e30f;
-            s_l[g] = l;
-        }
-    }
-    __syncthreads();
-    // P.V partials
-    float* part = a.partial + (static_cast<size_t>(kvh) * a.splits + split) * G * (D + 2);
-    for (int it = tid; it < G * D; it += kAttnThreads) {
-        const int g = it / D, e = it - g * D;
-        float acc = 0.f;
-        for (int t = 0; t < n; ++t) {
-            const int row = t0 + t;
+    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+
+    for (int tb = 0; tb < n; tb += kKeyTile) {
+        const int nt = min(kKeyTile, n - tb);
+        __syncthreads();  // previous tile fully consumed (and q / stats initialised)
+#pragma unroll 4
+        for (int i = tid; i < nt * (D / 4); i += kAttnThreads) {
+            const int r = i / (D / 4), c = (i % (D / 4)) * 4;
+            const int row = t0 + tb + r;
+            const KV* kp = row < len0 ? k0 + static_cast<size_t>(row) * D : k1 + static_cast<size_t>(row - len0) * D;
             const KV* vp = row < len0 ? v0 + static_cast<size_t>(row) * D : v1 + static_cast<size_t>(row - len0) * D;
-            acc = fmaf(sc[g * max_chunk + t], load_kv(vp, e), acc);
+            float kr[4], vr[4];
+            load4(kp, c, kr);
+            load4(vp, c, vr);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                ks[r][c + j] = kr[j];
+                vs[r][c + j] = vr[j];
+            }
         }
-        part[g * (D + 2) + e] = acc;
-        if (e == 0) {
-            part[g * (D + 2) + D] = s_m[g];
-            part[g * (D + 2) + D + 1] = s_l[g];
+        __syncthreads();
+        for (int i = tid; i < G * nt; i += kAttnThreads) {
+            const int g = i / nt, t = i - g * nt;
+            float s = 0.f;
+#pragma unroll 16
+            for (int c = 0; c < D; ++c) s = fmaf(qs[g][c], ks[t][c], s);
+            sc[g][t] = s + (a.mask ? a.mask[t0 + tb + t] : 0.f);
         }
+        __syncthreads();
+        for (int g = warp; g < G; g += kAttnThreads / kWarp) {
+            const float x = lane < nt ? sc[g][lane] : -1e30f;
+            const float m_old = m_s[g];
+            const float m_new = fmaxf(m_old, warp_max(x));
+            const float p = lane < nt ? __expf(x - m_new) : 0.f;
+            if (lane < nt) sc[g][lane] = p;
+            const float psum = warp_sum(p);
+            if (lane == 0) {
+                const float alpha = __expf(m_old - m_new);
+                alpha_s[g] = alpha;
+                l_s[g] = l_s[g] * alpha + psum;
+                m_s[g] = m_new;
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (g_lo + j < g_hi) acc[j] *= alpha_s[g_lo + j];
+        for (int t = 0; t < nt; ++t) {
+            const float v = vs[t][e];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (g_lo + j < g_hi) acc[j] = fmaf(sc[g_lo + j][t], v, acc[j]);
+        }
+    }
+    __syncthreads();
+    // this split's partial (m, l, P.V) per head
+    float* part = a.partial + (static_cast<size_t>(kvh) * a.splits + split) * G * (D + 2);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int g = g_lo + j;
+        if (g < g_hi) part[g * (D + 2) + e] = acc[j];
+    }
+    if (tid < G) {
+        part[tid * (D + 2) + D] = n > 0 ? m_s[tid] : -1e30f;
+        part[tid * (D + 2) + D + 1] = l_s[tid];
     }
     __threadfence();
     __syncthreads();
@@ -326,24 +347,35 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    // combine the active splits of this KV head from shared memory
+    // combine the active splits of this KV head, staged with 8 loads in flight per thread
     const float* pk = a.partial + static_cast<size_t>(kvh) * a.splits * G * (D + 2);
-    float* ps = sm;  // [active][G][D + 2], reuses the score buffer
     const int total = active * G * (D + 2);
-    for (int i = tid; i < total; i += kAttnThreads) ps[i] = __ldcg(pk + i);
+    for (int base = tid; base < total; base += kAttnThreads * 8) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int i = base + j * kAttnThreads;
+            v[j] = i < total ? __ldcg(pk + i) : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int i = base + j * kAttnThreads;
+            if (i < total) ps[i] = v[j];
+        }
+    }
     __syncthreads();
     for (int it = tid; it < G * D; it += kAttnThreads) {
-        const int g = it / D, e = it - g * D;
+        const int g = it / D, c = it - g * D;
         float M = -1e30f;
         for (int sp = 0; sp < active; ++sp) M = fmaxf(M, ps[(sp * G + g) * (D + 2) + D]);
         float num = 0.f, den = 0.f;
         for (int sp = 0; sp < active; ++sp) {
             const float* pp = ps + (sp * G + g) * (D + 2);
             const float w = __expf(pp[D] - M);
-            num = fmaf(w, pp[e], num);
+            num = fmaf(w, pp[c], num);
             den = fmaf(w, pp[D + 1], den);
         }
-        a.out[(kvh * G + g) * D + e] = num / den;
+        a.out[(kvh * G + g) * D + c] = num / den;
     }
     if (tid == 0) a.counters[kvh] = 0;
 }
@@ -392,17 +424,16 @@ void launch_attn_decode(const AttnArgs& a, bool fp16_kv, cudaStream_t s, bool pd
         throw std::invalid_argument("attention: bad head grouping");
     const int G = a.q_heads / a.kv_heads;
     if (G < 1 || G > kMaxGroup) throw std::invalid_argument("attention: more than 16 query heads per KV head");
-    // the longest split any launch of this configuration can see
-    const int t_max = a.ctl ? a.len0 : a.len0 + a.len1;
-    // the longest split: a short cache runs fewer splits of >= kMinKeysPerSplit keys
-    const int max_chunk = std::max((t_max + a.splits - 1) / a.splits, kMinKeysPerSplit);
-    const size_t smem = std::max(static_cast<size_t>(G) * (64 + max_chunk),
-                                 static_cast<size_t>(a.splits) * G * (64 + 2)) * sizeof(float);
+    for (const void* p : {a.k0, a.v0, a.k1, a.v1})
+        if (reinterpret_cast<uintptr_t>(p) % 16 != 0)
+            throw std::invalid_argument("attention: key/value rows must start on 16-byte boundaries");
+    // dynamic shared memory holds only the combine's staged partials
+    const size_t smem = static_cast<size_t>(a.splits) * G * (64 + 2) * sizeof(float);
     if (smem > 200 * 1024) throw std::invalid_argument("attention: sequence too long for one split");
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = make_cfg(dim3(a.splits, a.kv_heads), dim3(kAttnThreads), smem, s, pdl, attr);
-    if (fp16_kv) check_launch(cudaLaunchKernelEx(&cfg, attn_decode_kernel<__half, 64>, a, max_chunk));
-    else check_launch(cudaLaunchKernelEx(&cfg, attn_decode_kernel<float, 64>, a, max_chunk));
+    if (fp16_kv) check_launch(cudaLaunchKernelEx(&cfg, attn_decode_kernel<__half, 64>, a));
+    else check_launch(cudaLaunchKernelEx(&cfg, attn_decode_kernel<float, 64>, a));
 }
 
 void init_batched_attributes();
@@ -413,6 +444,7 @@ void init_kernel_attributes() {
     check_launch(cudaFuncSetAttribute(attn_decode_kernel<float, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax));
     init_batched_attributes();
     init_tc_attributes();
+    init_dit_layers_attributes();
 }
 
 void launch_final_norm(const float* h, const __half* g, float eps, int H, float* out, float* out2,

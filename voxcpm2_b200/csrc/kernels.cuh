@@ -163,6 +163,10 @@ struct DitEmbedArgs {
     const float* mu_uncond;  // [2*Hd] of CFG row 1, or null (zeros)
     const float* x_uncond;   // [D*P] of CFG row 1, or null (same as x)
     const float* cond_uncond;// [D*P] of CFG row 1, or null (same as cond)
+    const float* tsum;       // [Hd] precomputed t_tok + dt_tok of both CFG rows, or null
+    float* ssq_out;          // or null: per 32-feature block, row sums of squares [block][24]
+    unsigned* sync_reset;    // or null: words zeroed by block 0 (the next persistent launch's sync block)
+    int sync_words;
 };
 void launch_dit_embed(const DitEmbedArgs& a, cudaStream_t s, bool pdl);
 
@@ -180,10 +184,15 @@ struct DitOutArgs {
     float* x;               // [D*P] sample updated in place (null: no update)
     float dt, cfg;
     StreamCtl* ctl;
+    float* est_buf;         // [2][D*P] estimator output (est_out or a scratch buffer)
+    int* counter;           // arrival counter, zero between launches
 };
 void launch_dit_out(const DitOutArgs& a, cudaStream_t s, bool pdl);
 
 // stop decision: logits = head_w [2][H] . mid; ctl->stopped = step > min_patches && l1 > l0
+// out[i] = a[i] + b[i]
+void launch_vec_add(const float* a, const float* b, float* out, int n, cudaStream_t s);
+
 void launch_stop_decide(const __half* head_w, const float* mid, int H, StreamCtl* ctl,
                         float* logits_out, cudaStream_t s, bool pdl);
 
@@ -221,12 +230,66 @@ struct TcLinearArgs {
     __half* yb = nullptr;  // GATEUP: split-fp16 [48][ldyb], the next linear's B operand
     int ldyb = 0;
     StreamCtl* ctl = nullptr;  // receives error 3 if a bounded wait gave up
+    // Where the B operand (the token rows) comes from:
+    //   TC_B_TMA:  TMA loads of a split-fp16 [48][K] buffer (map_b);
+    //   TC_B_NORM: RMSNorm of fp32 rows x [M][ldx] with weight g, built in shared
+    //              memory; the rows' sums of squares come as ssq_parts partial sums
+    //              ssq_in [part][24] written by the kernel that produced x;
+    //   TC_B_ATTN: per-head attention (RoPE, softmax, P.V) over the fp32 q/k/v
+    //              rows qkv [M][(q_heads + 2 kv_heads) * 64] of 2 sequences of
+    //              'seq' tokens, built in shared memory (K = q_heads * 64).
+    int bmode = 0;
+    const float* x = nullptr;
+    int ldx = 0;
+    const __half* g = nullptr;
+    float eps = 0.f;
+    const float* ssq_in = nullptr;
+    int ssq_parts = 0;
+    const float* qkv = nullptr;
+    int q_heads = 0, kv_heads = 0, seq = 0;
+    const float* rope_cos = nullptr;  // [seq][64]
+    const float* rope_sin = nullptr;
+    float scale = 1.f;
+    int attn_round = 2;  // heads computed together (scratch: ~20 KB each); see tc_attn_round
+    int max_stages = 8;  // shared-memory ring depth (1..8); fused token tiles need one stage per K chunk
+    // residual epilogue: partial sums of squares of the updated rows, one part per
+    // (tile, owner CTA) = tile * splits + rank, written to ssq_out [part][24]
+    float* ssq_out = nullptr;
 };
+enum { TC_B_TMA = 0, TC_B_NORM = 1, TC_B_ATTN = 2 };
+constexpr int kSsqStride = 24;  // floats per part in a sums-of-squares buffer
 CUtensorMap make_tensor_map_f16(const void* base, int rows, int cols, int box_rows);
-size_t tc_linear_smem_bytes(int K, int splits);
+size_t tc_linear_smem_bytes(int K, int splits, int bmode, int attn_round = 1, int max_stages = 8);
+// heads per attention round that fit beside the stages of a TC_B_ATTN launch (2, else 1)
+int tc_attn_round(int K, int splits, int max_stages = 8);
 void launch_tc_linear(const CUtensorMap& map_a, const CUtensorMap& map_b, const TcLinearArgs& a, cudaStream_t s,
                       bool pdl);
 void init_tc_attributes();
+
+// Persistent DiT decoder (all layers of one estimator evaluation, one
+// cooperative launch, one CTA per SM; dit_persist.cu).
+struct DitLayersArgs {
+    const CUtensorMap* maps;     // [layers][4] weight maps in device memory: q/k/v, o, gate|up, down
+    const __half* const* norms;  // [layers][2] device array: input and post-attention RMSNorm weights
+    int layers = 0, Hd = 0, F = 0, hq = 0, hkv = 0, seq = 0, M = 0;
+    float eps = 0.f, rscale = 1.f, scale = 1.f;
+    const float* rope_cos = nullptr;  // [seq][64]
+    const float* rope_sin = nullptr;
+    float* dh = nullptr;         // [M][Hd] residual stream, in and out
+    float* ssq = nullptr;        // [>= grid][24] per-slice row sums of squares of dh
+    int embed_parts = 0;         // slices dit_embed left in ssq for layer 0's input RMSNorm
+    float* qkv = nullptr;        // [M][(hq + 2 hkv) * 64]
+    __half* act = nullptr;       // [48][F] split-fp16 SiLU(gate) * up (pad rows zero)
+    float* part = nullptr;       // dit_layers_part_floats(grid)
+    unsigned* sync = nullptr;    // dit_layers_sync_words() words, zero at launch
+    StreamCtl* ctl = nullptr;    // receives error 3 if a bounded wait gave up
+};
+int dit_layers_grid();                       // CTAs of one launch (one per SM)
+size_t dit_layers_part_floats(int grid);
+int dit_layers_sync_words();
+void check_dit_layers(const DitLayersArgs& a, int grid);  // throws std::invalid_argument if unsupported
+void launch_dit_layers(const DitLayersArgs& a, int grid, cudaStream_t s);
+void init_dit_layers_attributes();
 
 // Raise the dynamic shared-memory limit of the kernels that need more than 48 KB
 // (call once per device, outside stream capture).

@@ -10,6 +10,7 @@
 #include <array>
 #include <atomic>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <functional>
 #include <initializer_list>
@@ -262,6 +263,9 @@ struct vxc_device {
     float *dit_rope_cos = nullptr, *dit_rope_sin = nullptr;  // positions 0..seq-1
     // per DiT layer: TMA maps of W_qkv, W_o, W_gate|up, W_down (A operands)
     std::vector<std::array<CUtensorMap, 4>> dit_maps;
+    CUtensorMap* dit_maps_dev = nullptr;       // the same maps in device memory (persistent DiT kernel)
+    const __half** dit_norms_dev = nullptr;    // [layers][2] input / post-attention RMSNorm weights
+    uint64_t epoch = 0;  // bumped by every weight upload (invalidates derived tables)
 };
 
 namespace {
@@ -336,6 +340,27 @@ struct vxc_stream {
     bool prefilled = false;
     int graph_T = -1;
     float graph_cfg = 0.f;
+    // per timestep count T: rows t_tok(step) + dt_tok(0) of the sampler's
+    // estimator steps, [T + 1][Hd]; contents follow the device's weight epoch
+    struct TimeTable {
+        float* dev = nullptr;
+        uint64_t epoch = ~0ull;
+    };
+    std::map<int, TimeTable> ttab;
+    float* dest = nullptr;  // [2][D*P] estimator output scratch of dit_out
+    float* dssq = nullptr;  // [parts][24] row sums of squares of s->dh, by slice
+    // DiT decoder form: 0 persistent (one cooperative launch per evaluation), 1 fused (4 tcgen05
+    // launches per layer), 2 split (7 launches per layer: RMSNorm and attention as their own kernels)
+    int dit_form = 0;
+    int dit_grid = 0;           // CTAs of the persistent launch
+    // ring depth of the per-layer tensor-core launches (VXC_TC_STAGES): a shallow ring keeps a
+    // CTA's shared memory small, so linears of several concurrent streams share an SM
+    int tc_stages = 2;
+    // programmatic dependent launch between the patch graph's kernels (VXC_NO_PDL=1 turns it off)
+    bool pdl = true;
+    float* dpart = nullptr;     // persistent launch: partial tiles
+    unsigned* dsync = nullptr;  // persistent launch: grid barrier and tile counters
+    int* dcount = nullptr;  // dit_out arrival counter
     cudaGraphExec_t graph = nullptr;
     int graph_kernels = 0;
     int min_patches_dev = -1;
@@ -356,6 +381,13 @@ void free_all(vxc_stream* s) {
                     s->pact, s->pcat, s->pids, s->xb_n, s->xb_a, s->xb_act};
     for (void* p : ptrs)
         if (p) cudaFree(p);
+    for (auto& kv : s->ttab)
+        if (kv.second.dev) cudaFree(kv.second.dev);
+    if (s->dest) cudaFree(s->dest);
+    if (s->dssq) cudaFree(s->dssq);
+    if (s->dpart) cudaFree(s->dpart);
+    if (s->dsync) cudaFree(s->dsync);
+    if (s->dcount) cudaFree(s->dcount);
     if (s->ctl_host) cudaFreeHost(s->ctl_host);
     if (s->pin) cudaFreeHost(s->pin);
     if (s->cs) cudaStreamDestroy(s->cs);
@@ -416,7 +448,7 @@ void enqueue_decoder_step(vxc_stream* s, int which, float* out, float* out2, int
         qa.which = which;
         qa.ctl = s->ctl;
         qa.skip_if_stopped = skip;
-        launch_gemv(qa, s->cs, true);
+        launch_gemv(qa, s->cs, s->pdl);
 
         AttnArgs aa;
         aa.q = s->q;
@@ -435,7 +467,7 @@ void enqueue_decoder_step(vxc_stream* s, int which, float* out, float* out2, int
         aa.ctl = s->ctl;
         aa.which = which;
         aa.skip_if_stopped = skip;
-        launch_attn_decode(aa, false, s->cs, true);
+        launch_attn_decode(aa, false, s->cs, s->pdl);
 
         GemvArgs oa;
         oa.mode = GEMV_RESID;
@@ -447,7 +479,7 @@ void enqueue_decoder_step(vxc_stream* s, int which, float* out, float* out2, int
         oa.rscale = rscale;
         oa.ctl = s->ctl;
         oa.skip_if_stopped = skip;
-        launch_gemv(oa, s->cs, true);
+        launch_gemv(oa, s->cs, s->pdl);
 
         GemvArgs ga;
         ga.mode = GEMV_GATEUP;
@@ -460,7 +492,7 @@ void enqueue_decoder_step(vxc_stream* s, int which, float* out, float* out2, int
         ga.y = s->act;
         ga.ctl = s->ctl;
         ga.skip_if_stopped = skip;
-        launch_gemv(ga, s->cs, true);
+        launch_gemv(ga, s->cs, s->pdl);
 
         GemvArgs da;
         da.mode = GEMV_RESID;
@@ -472,9 +504,9 @@ void enqueue_decoder_step(vxc_stream* s, int which, float* out, float* out2, int
         da.rscale = rscale;
         da.ctl = s->ctl;
         da.skip_if_stopped = skip;
-        launch_gemv(da, s->cs, true);
+        launch_gemv(da, s->cs, s->pdl);
     }
-    launch_final_norm(s->h[which], fnorm, d.rms_eps, H, out, out2, s->ctl, which, 1, skip, s->cs, true);
+    launch_final_norm(s->h[which], fnorm, d.rms_eps, H, out, out2, s->ctl, which, 1, skip, s->cs, s->pdl);
 }
 
 // K split (cluster size) of a tensor-core linear: about one CTA per SM overall.
@@ -484,62 +516,174 @@ int choose_splits(int tiles, int k) {
     return std::max(1, std::min({8, chunks, want}));
 }
 
+// K split and ring depth of one tensor-core launch: about one CTA per SM, and
+// with an operand built in shared memory (fused) one stage per K chunk.
+TcLinearArgs tc_plan(const vxc_stream* s, int tiles, int K, bool fused_b) {
+    TcLinearArgs a;
+    const int nch = K / 64;
+    a.splits = choose_splits(tiles, K);
+    a.max_stages = s->tc_stages;
+    if (fused_b) a.splits = std::min(std::min(8, nch), std::max(a.splits, (nch + a.max_stages - 1) / a.max_stages));
+    return a;
+}
+
 // DiT decoder over the 2 x seq rows in s->dh (DitEstimator.decoder,
 // export_components.py:625-659), the four linears of each layer on tcgen05.
+// Fused form (4 launches per layer): each linear builds its token operand in
+// shared memory: q/k/v and gate/up from RMSNorm(dh) (row sums of squares left
+// by the kernel that last wrote dh), o from the attention over the q/k/v rows.
+// Shapes whose per-CTA K range exceeds 8 chunks take the 7-launch form with
+// separate RMSNorm and attention kernels.
+bool dit_fused_ok(const vxc_model_desc& d) {
+    const int Hd = d.dit_hidden, hq = d.dit_q_heads, hkv = d.dit_kv_heads;
+    const int seq = dit_tokens_per_seq(d.patch_size);
+    const int W = (hq + 2 * hkv) * (Hd / hq);
+    auto fits = [](int k, int splits) { return (k / 64 + splits - 1) / splits <= 8; };
+    return Hd / hq == 64 && seq <= 12 && hkv > 0 && hq % hkv == 0 &&
+           fits(Hd, choose_splits(W / 128, Hd)) && fits(Hd, choose_splits(d.dit_ffn / 64, Hd)) &&
+           fits(hq * 64, choose_splits(Hd / 128, hq * 64));
+}
+
+DitLayersArgs dit_layers_shape(const vxc_model_desc& d) {
+    DitLayersArgs a;
+    a.layers = d.dit_layers;
+    a.Hd = d.dit_hidden;
+    a.F = d.dit_ffn;
+    a.hq = d.dit_q_heads;
+    a.hkv = d.dit_kv_heads;
+    a.seq = dit_tokens_per_seq(d.patch_size);
+    a.M = 2 * a.seq;
+    a.eps = d.rms_eps;
+    a.rscale = d.dit_residual_scale;
+    a.scale = 1.0f / std::sqrt(static_cast<float>(d.dit_hidden / d.dit_q_heads));
+    return a;
+}
+
+bool dit_persistent_ok(const vxc_model_desc& d, int grid) {
+    try {
+        check_dit_layers(dit_layers_shape(d), grid);
+        return d.dit_hidden / d.dit_q_heads == 64;
+    } catch (const std::invalid_argument&) {
+        return false;
+    }
+}
+
+DitLayersArgs dit_layers_args(vxc_stream* s, StreamCtl* ctl) {
+    const vxc_device* dev = s->dev;
+    DitLayersArgs a = dit_layers_shape(dev->desc);
+    a.maps = dev->dit_maps_dev;
+    a.norms = dev->dit_norms_dev;
+    a.rope_cos = dev->dit_rope_cos;
+    a.rope_sin = dev->dit_rope_sin;
+    a.dh = s->dh;
+    a.ssq = s->dssq;
+    a.embed_parts = (a.Hd + 31) / 32;
+    a.qkv = s->dqkv;
+    a.act = s->xb_act;
+    a.part = s->dpart;
+    a.sync = s->dsync;
+    a.ctl = ctl;
+    for (const LayerW& L : dev->dit)  // the operand builders read the norm weights 4 at a time
+        if ((reinterpret_cast<uintptr_t>(L.in_norm) | reinterpret_cast<uintptr_t>(L.post_norm)) & 7)
+            throw std::invalid_argument("dit_layers: RMSNorm weights must be 8-byte aligned");
+    return a;
+}
+
 void enqueue_dit_layers(vxc_stream* s, StreamCtl* ctl) {
     const vxc_device* dev = s->dev;
     const vxc_model_desc& d = dev->desc;
     const int Hd = d.dit_hidden, F = d.dit_ffn, hq = d.dit_q_heads, hkv = d.dit_kv_heads, hd = Hd / hq;
     const int seq = dit_tokens_per_seq(d.patch_size), M = 2 * seq;
     const int W = (hq + 2 * hkv) * hd;
+    if (s->dit_form == 0) {
+        DitLayersArgs a = dit_layers_args(s, ctl);
+        launch_dit_layers(a, s->dit_grid, s->cs);
+        return;
+    }
+    const bool fused = s->dit_form == 1;
+    const float scale = 1.0f / std::sqrt(static_cast<float>(hd));
+    // sums-of-squares parts of s->dh: dit_embed leaves one per 32 features
+    int parts = (Hd + 31) / 32;
     for (size_t l = 0; l < dev->dit.size(); ++l) {
         const LayerW& L = dev->dit[l];
         const std::array<CUtensorMap, 4>& maps = dev->dit_maps[l];
-        launch_rmsnorm_rows_split(s->dh, Hd, L.in_norm, d.rms_eps, Hd, M, s->xb_n, ctl, s->cs, true);
-        TcLinearArgs qa;
+        TcLinearArgs qa = tc_plan(s, W / 128, Hd, fused);
         qa.K = Hd;
         qa.M = M;
         qa.rows = W;
-        qa.splits = choose_splits(W / 128, Hd);
         qa.y = s->dqkv;
         qa.ldy = W;
         qa.ctl = ctl;
-        launch_tc_linear(maps[0], s->map_xb_n, qa, s->cs, true);
-        launch_dit_attention_split(s->dqkv, 2, seq, hq, hkv, hd, dev->dit_rope_cos, dev->dit_rope_sin,
-                                   1.0f / std::sqrt(static_cast<float>(hd)), s->xb_a, ctl, s->cs, true);
-        TcLinearArgs oa;
+        if (fused) {
+            qa.bmode = TC_B_NORM;
+            qa.x = s->dh;
+            qa.ldx = Hd;
+            qa.g = L.in_norm;
+            qa.eps = d.rms_eps;
+            qa.ssq_in = s->dssq;
+            qa.ssq_parts = parts;
+        } else {
+            launch_rmsnorm_rows_split(s->dh, Hd, L.in_norm, d.rms_eps, Hd, M, s->xb_n, ctl, s->cs, s->pdl);
+        }
+        launch_tc_linear(maps[0], s->map_xb_n, qa, s->cs, s->pdl);
+        TcLinearArgs oa = tc_plan(s, Hd / 128, hq * hd, fused);
         oa.K = hq * hd;
         oa.M = M;
         oa.rows = Hd;
-        oa.splits = choose_splits(Hd / 128, hq * hd);
         oa.resid = 1;
         oa.rscale = d.dit_residual_scale;
         oa.y = s->dh;
         oa.ldy = Hd;
         oa.ctl = ctl;
-        launch_tc_linear(maps[1], s->map_xb_a, oa, s->cs, true);
-        launch_rmsnorm_rows_split(s->dh, Hd, L.post_norm, d.rms_eps, Hd, M, s->xb_n, ctl, s->cs, true);
-        TcLinearArgs ga;
+        if (fused) {
+            oa.bmode = TC_B_ATTN;
+            oa.qkv = s->dqkv;
+            oa.q_heads = hq;
+            oa.kv_heads = hkv;
+            oa.seq = seq;
+            oa.rope_cos = dev->dit_rope_cos;
+            oa.rope_sin = dev->dit_rope_sin;
+            oa.scale = scale;
+            oa.attn_round = tc_attn_round(oa.K, oa.splits, oa.max_stages);
+            oa.ssq_out = s->dssq;
+        } else {
+            launch_dit_attention_split(s->dqkv, 2, seq, hq, hkv, hd, dev->dit_rope_cos, dev->dit_rope_sin, scale,
+                                       s->xb_a, ctl, s->cs, s->pdl);
+        }
+        launch_tc_linear(maps[1], s->map_xb_a, oa, s->cs, s->pdl);
+        const int o_parts = (Hd / 128) * oa.splits;
+        TcLinearArgs ga = tc_plan(s, F / 64, Hd, fused);
         ga.K = Hd;
         ga.M = M;
         ga.rows = F;
-        ga.splits = choose_splits(F / 64, Hd);
         ga.gateup = 1;
         ga.yb = s->xb_act;
         ga.ldyb = F;
         ga.ctl = ctl;
-        launch_tc_linear(maps[2], s->map_xb_n, ga, s->cs, true);
-        TcLinearArgs da;
+        if (fused) {
+            ga.bmode = TC_B_NORM;
+            ga.x = s->dh;
+            ga.ldx = Hd;
+            ga.g = L.post_norm;
+            ga.eps = d.rms_eps;
+            ga.ssq_in = s->dssq;
+            ga.ssq_parts = o_parts;
+        } else {
+            launch_rmsnorm_rows_split(s->dh, Hd, L.post_norm, d.rms_eps, Hd, M, s->xb_n, ctl, s->cs, s->pdl);
+        }
+        launch_tc_linear(maps[2], s->map_xb_n, ga, s->cs, s->pdl);
+        TcLinearArgs da = tc_plan(s, Hd / 128, F, false);
         da.K = F;
         da.M = M;
         da.rows = Hd;
-        da.splits = choose_splits(Hd / 128, F);
         da.resid = 1;
         da.rscale = d.dit_residual_scale;
         da.y = s->dh;
         da.ldy = Hd;
         da.ctl = ctl;
-        launch_tc_linear(maps[3], s->map_xb_act, da, s->cs, true);
+        if (fused) da.ssq_out = s->dssq;
+        launch_tc_linear(maps[3], s->map_xb_act, da, s->cs, s->pdl);
+        parts = (Hd / 128) * da.splits;
     }
 }
 
@@ -550,23 +694,23 @@ void enqueue_time_tokens(vxc_stream* s, float step_index, float T, const float* 
     const DitPtrs w = dit_ptrs(s->dev);
     const int Hd = d.dit_hidden;
     const int sk = ctl ? 1 : 0;
-    launch_timestep_embedding(step_index, T, 1, Hd / 2, s->temb, ctl, s->cs, true);
-    launch_gemv(plain_gemv(w.t1_w, w.t1_b, s->temb, Hd, Hd, s->tmid, ACT_SILU, ctl, sk), s->cs, true);
-    launch_gemv(plain_gemv(w.t2_w, w.t2_b, s->tmid, Hd, Hd, s->ttok, ACT_NONE, ctl, sk), s->cs, true);
-    launch_timestep_embedding(dt_raw[0], 0.f, 0, Hd / 2, s->dtemb, ctl, s->cs, true);
-    launch_gemv(plain_gemv(w.dt1_w, w.dt1_b, s->dtemb, Hd, Hd, s->dtmid, ACT_SILU, ctl, sk), s->cs, true);
-    launch_gemv(plain_gemv(w.dt2_w, w.dt2_b, s->dtmid, Hd, Hd, s->dttok, ACT_NONE, ctl, sk), s->cs, true);
+    launch_timestep_embedding(step_index, T, 1, Hd / 2, s->temb, ctl, s->cs, s->pdl);
+    launch_gemv(plain_gemv(w.t1_w, w.t1_b, s->temb, Hd, Hd, s->tmid, ACT_SILU, ctl, sk), s->cs, s->pdl);
+    launch_gemv(plain_gemv(w.t2_w, w.t2_b, s->tmid, Hd, Hd, s->ttok, ACT_NONE, ctl, sk), s->cs, s->pdl);
+    launch_timestep_embedding(dt_raw[0], 0.f, 0, Hd / 2, s->dtemb, ctl, s->cs, s->pdl);
+    launch_gemv(plain_gemv(w.dt1_w, w.dt1_b, s->dtemb, Hd, Hd, s->dtmid, ACT_SILU, ctl, sk), s->cs, s->pdl);
+    launch_gemv(plain_gemv(w.dt2_w, w.dt2_b, s->dtmid, Hd, Hd, s->dttok, ACT_NONE, ctl, sk), s->cs, s->pdl);
     if (dt_raw[1] != dt_raw[0]) {
-        launch_timestep_embedding(dt_raw[1], 0.f, 0, Hd / 2, s->dtemb1, ctl, s->cs, true);
-        launch_gemv(plain_gemv(w.dt1_w, w.dt1_b, s->dtemb1, Hd, Hd, s->dtmid1, ACT_SILU, ctl, sk), s->cs, true);
-        launch_gemv(plain_gemv(w.dt2_w, w.dt2_b, s->dtmid1, Hd, Hd, s->dttok1, ACT_NONE, ctl, sk), s->cs, true);
+        launch_timestep_embedding(dt_raw[1], 0.f, 0, Hd / 2, s->dtemb1, ctl, s->cs, s->pdl);
+        launch_gemv(plain_gemv(w.dt1_w, w.dt1_b, s->dtemb1, Hd, Hd, s->dtmid1, ACT_SILU, ctl, sk), s->cs, s->pdl);
+        launch_gemv(plain_gemv(w.dt2_w, w.dt2_b, s->dtmid1, Hd, Hd, s->dttok1, ACT_NONE, ctl, sk), s->cs, s->pdl);
     }
 }
 
 // One estimator evaluation + (if x_update) the CFG-zero* Euler update.
 void enqueue_dit_eval(vxc_stream* s, const float* x, const float* x_unc, const float* mu, const float* mu_unc,
                       const float* cond, const float* cond_unc, bool dt_rows_differ, float* est_out,
-                      float* x_update, float dt, float cfg, StreamCtl* ctl) {
+                      float* x_update, float dt, float cfg, StreamCtl* ctl, const float* tsum) {
     const vxc_model_desc& d = s->dev->desc;
     const DitPtrs w = dit_ptrs(s->dev);
     DitEmbedArgs e{};
@@ -589,7 +733,13 @@ void enqueue_dit_eval(vxc_stream* s, const float* x, const float* x_unc, const f
     e.mu_uncond = mu_unc;
     e.x_uncond = x_unc;
     e.cond_uncond = cond_unc;
-    launch_dit_embed(e, s->cs, true);
+    e.tsum = tsum;
+    e.ssq_out = s->dssq;
+    if (s->dit_form == 0) {  // the persistent launch that follows expects a zeroed sync block
+        e.sync_reset = s->dsync;
+        e.sync_words = dit_layers_sync_words();
+    }
+    launch_dit_embed(e, s->cs, s->pdl);
     enqueue_dit_layers(s, ctl);
     DitOutArgs o{};
     o.hidden = s->dh;
@@ -606,20 +756,43 @@ void enqueue_dit_eval(vxc_stream* s, const float* x, const float* x_unc, const f
     o.dt = dt;
     o.cfg = cfg;
     o.ctl = ctl;
-    launch_dit_out(o, s->cs, true);
+    o.est_buf = est_out ? est_out : s->dest;
+    o.counter = s->dcount;
+    launch_dit_out(o, s->cs, s->pdl);
 }
 
 // cfm_sample over s->x (holding the noise), mu = s->mu (row 1 of mu_in stays
 // zero: the unconditional CFG branch, synthesizer.cpp:52, 114).
+// The sampler's time tokens depend only on the weights and (step, T): the
+// time_mlp(emb(t_step)) + delta_time_mlp(emb(0)) rows are computed once per T
+// (by the same kernels, eagerly, outside any capture) and re-used by every
+// patch. Refreshed when the weights change.
+const float* time_table(vxc_stream* s, int T) {
+    vxc_stream::TimeTable& t = s->ttab[T];
+    const int Hd = s->dev->desc.dit_hidden;
+    if (!t.dev) t.dev = dev_alloc<float>(static_cast<size_t>(T + 1) * Hd);
+    if (t.epoch != s->dev->epoch) {
+        const float dt0[2] = {0.f, 0.f};
+        for (int step = 1; step <= T; ++step) {
+            enqueue_time_tokens(s, static_cast<float>(step - 1), static_cast<float>(T), dt0, nullptr);
+            launch_vec_add(s->ttok, s->dttok, t.dev + static_cast<size_t>(step) * Hd, Hd, s->cs);
+        }
+        ck(cudaStreamSynchronize(s->cs), "time table");
+        t.epoch = s->dev->epoch;
+    }
+    return t.dev;
+}
+
+// cfm_sample's Euler loop; time_table(s, T) must be current.
 void enqueue_cfm(vxc_stream* s, const float* cond_dev, int T, float cfg) {
     const std::vector<float> dts = euler_dts(T);
     const int z = zero_init_steps(T);
-    const float dt0[2] = {0.f, 0.f};
+    const int Hd = s->dev->desc.dit_hidden;
+    const float* tab = s->ttab.at(T).dev;
     for (int step = 1; step <= T; ++step) {
         if (step <= z) continue;  // zero-init steps leave x untouched (synthesizer.cpp:123-126)
-        enqueue_time_tokens(s, static_cast<float>(step - 1), static_cast<float>(T), dt0, s->ctl);
         enqueue_dit_eval(s, s->x, nullptr, s->mu, nullptr, cond_dev, nullptr, false, nullptr, s->x, dts[step], cfg,
-                         s->ctl);
+                         s->ctl, tab + static_cast<size_t>(step) * Hd);
     }
 }
 
@@ -628,19 +801,19 @@ void enqueue_patch(vxc_stream* s, int T, float cfg) {
     const vxc_device* dev = s->dev;
     const vxc_model_desc& d = dev->desc;
     const int H = d.hidden, Hd = d.dit_hidden, L = d.feat_dim * d.patch_size;
-    launch_patch_begin(s->noise, s->latents, s->cond0, L, s->x, s->cond, s->ctl, s->cs, true);
+    launch_patch_begin(s->noise, s->latents, s->cond0, L, s->x, s->cond, s->ctl, s->cs, s->pdl);
     // dit_proj: cat(lm_to_dit_proj(lm), res_to_dit_proj(res))
     const __half* dp = dev->blob[VXC_DIT_PROJ];
     const size_t dps = static_cast<size_t>(Hd) * H;
-    launch_gemv(plain_gemv(dp, dp + dps, s->lm_h, H, Hd, s->mu, ACT_NONE, s->ctl, 0), s->cs, true);
+    launch_gemv(plain_gemv(dp, dp + dps, s->lm_h, H, Hd, s->mu, ACT_NONE, s->ctl, 0), s->cs, s->pdl);
     launch_gemv(plain_gemv(dp + dps + Hd, dp + 2 * dps + Hd, s->res_h, H, Hd, s->mu + Hd, ACT_NONE, s->ctl, 0),
-                s->cs, true);
+                s->cs, s->pdl);
     enqueue_cfm(s, s->cond, T, cfg);
     // stop head on the hidden state entering this patch
     const __half* sh = dev->blob[VXC_STOP_HEAD];
     launch_gemv(plain_gemv(sh, sh + static_cast<size_t>(H) * H, s->lm_h, H, H, s->mid, ACT_SILU, s->ctl, 0), s->cs,
                 true);
-    launch_stop_decide(sh + static_cast<size_t>(H) * H + H, s->mid, H, s->ctl, nullptr, s->cs, true);
+    launch_stop_decide(sh + static_cast<size_t>(H) * H + H, s->mid, H, s->ctl, nullptr, s->cs, s->pdl);
     // feat_encoder(latent) -> feat and the base decoder input
     const __half* fe = dev->blob[VXC_FEAT_ENCODER];
     const size_t fin = static_cast<size_t>(H) * L;
@@ -648,30 +821,30 @@ void enqueue_patch(vxc_stream* s, int T, float cfg) {
     fa.in_mode = IN_LATENT_T;
     fa.lat_d = d.feat_dim;
     fa.lat_p = d.patch_size;
-    launch_gemv(fa, s->cs, true);
+    launch_gemv(fa, s->cs, s->pdl);
     GemvArgs fb = plain_gemv(fe + fin + H, fe + fin + H + static_cast<size_t>(H) * H, s->mid2, H, H, s->feat,
                              ACT_NONE, s->ctl, 1);
     fb.y2 = s->h[0];
-    launch_gemv(fb, s->cs, true);
+    launch_gemv(fb, s->cs, s->pdl);
     enqueue_decoder_step(s, 0, s->out[0], nullptr, 1);
     // fsq
     const __half* fq = dev->blob[VXC_FSQ];
     const size_t Q = d.fsq_dim;
     GemvArgs qa = plain_gemv(fq, fq + Q * H, s->out[0], H, static_cast<int>(Q), s->mid, ACT_FSQ, s->ctl, 1);
     qa.act_scale = d.fsq_scale;
-    launch_gemv(qa, s->cs, true);
+    launch_gemv(qa, s->cs, s->pdl);
     launch_gemv(plain_gemv(fq + Q * H + Q, fq + Q * H + Q + H * Q, s->mid, static_cast<int>(Q), H, s->lm_h, ACT_NONE,
                            s->ctl, 1),
-                s->cs, true);
+                s->cs, s->pdl);
     // fusion_proj(cat(lm, feat)) -> residual decoder input
     const __half* fu = dev->blob[VXC_FUSION_PROJ];
     GemvArgs ua = plain_gemv(fu, fu + static_cast<size_t>(H) * 2 * H, s->lm_h, 2 * H, H, s->h[1], ACT_NONE, s->ctl, 1);
     ua.in_mode = IN_CONCAT;
     ua.x2 = s->feat;
     ua.k1 = H;
-    launch_gemv(ua, s->cs, true);
+    launch_gemv(ua, s->cs, s->pdl);
     enqueue_decoder_step(s, 1, s->res_h, nullptr, 1);
-    launch_patch_end(s->x, s->latents, L, s->ctl, s->cs, true);
+    launch_patch_end(s->x, s->latents, L, s->ctl, s->cs, s->pdl);
 }
 
 void sync_ctl(vxc_stream* s) {
@@ -811,6 +984,7 @@ void decoder_call(vxc_stream* s, int which, const float* embed, int n, float* ou
 }
 
 void capture_patch_graph(vxc_stream* s, int T, float cfg) {
+    time_table(s, T);  // the graph reads the table; keep it current before every replay
     if (s->graph && s->graph_T == T && s->graph_cfg == cfg) return;
     if (s->graph) {
         cudaGraphExecDestroy(s->graph);
@@ -995,6 +1169,8 @@ VXC_API void vxc_device_destroy(vxc_device* dev) {
             if (p) cudaFree(p);
         if (dev->dit_rope_cos) cudaFree(dev->dit_rope_cos);
         if (dev->dit_rope_sin) cudaFree(dev->dit_rope_sin);
+        if (dev->dit_maps_dev) cudaFree(dev->dit_maps_dev);
+        if (dev->dit_norms_dev) cudaFree(dev->dit_norms_dev);
     }
     delete dev;
 }
@@ -1008,6 +1184,7 @@ VXC_API int32_t vxc_load_weights(vxc_device* dev, int32_t component, const void*
         if (!dev->blob[component]) dev->blob[component] = dev_alloc<__half>(count);
         ck(cudaMemcpy(dev->blob[component], fp16, count * sizeof(__half), cudaMemcpyHostToDevice), "weights upload");
         dev->loaded[component] = true;
+        ++dev->epoch;
         const __half* fn = nullptr;
         if (component == VXC_BASE_DECODER) {
             dev->base = carve_decoder(dev->blob[component], base_shape(dev->desc), &fn);
@@ -1023,10 +1200,21 @@ VXC_API int32_t vxc_load_weights(vxc_device* dev, int32_t component, const void*
             const int dh = dev->desc.dit_hidden, df = dev->desc.dit_ffn;
             const int W = (dev->desc.dit_q_heads + 2 * dev->desc.dit_kv_heads) * 64;
             dev->dit_maps.clear();
-            for (const LayerW& L : dev->dit)
+            std::vector<const __half*> norms;
+            for (const LayerW& L : dev->dit) {
                 dev->dit_maps.push_back({make_tensor_map_f16(L.wqkv, W, dh, 64), make_tensor_map_f16(L.wo, dh, dh, 64),
                                          make_tensor_map_f16(L.wgateup, 2 * df, dh, 64),
                                          make_tensor_map_f16(L.wdown, dh, df, 64)});
+                norms.push_back(L.in_norm);
+                norms.push_back(L.post_norm);
+            }
+            const size_t nl = dev->dit.size();
+            if (!dev->dit_maps_dev) dev->dit_maps_dev = dev_alloc<CUtensorMap>(4 * nl);
+            if (!dev->dit_norms_dev) dev->dit_norms_dev = dev_alloc<const __half*>(2 * nl);
+            ck(cudaMemcpy(dev->dit_maps_dev, dev->dit_maps.data(), sizeof(CUtensorMap) * 4 * nl,
+                          cudaMemcpyHostToDevice), "tensor maps");
+            ck(cudaMemcpy(dev->dit_norms_dev, norms.data(), sizeof(const __half*) * 2 * nl, cudaMemcpyHostToDevice),
+               "norm pointers");
         }
     });
 }
@@ -1096,6 +1284,39 @@ VXC_API int32_t vxc_stream_create(vxc_device* dev, int32_t kv_capacity, vxc_stre
         s->dattn = dev_alloc<float>(M * Hd);
         s->dact = dev_alloc<float>(M * d.dit_ffn);
         s->est = dev_alloc<float>(2 * L);
+        s->dest = dev_alloc<float>(2 * L);
+        s->dcount = dev_alloc<int>(1);
+        ck(cudaMemset(s->dcount, 0, sizeof(int)), "cudaMemset");
+        // DiT decoder form: the 7-launch layers by default (separate RMSNorm and attention
+        // kernels around four tcgen05 linears; the fastest with several concurrent streams);
+        // VXC_DIT_FORM=persistent|fused|split picks one explicitly (an unsupported choice is an error)
+        s->dit_grid = dit_layers_grid();
+        if (const char* np = std::getenv("VXC_NO_PDL")) s->pdl = std::string(np) != "1";
+        if (const char* st = std::getenv("VXC_TC_STAGES")) {
+            s->tc_stages = std::atoi(st);
+            if (s->tc_stages < 1 || s->tc_stages > 8) throw std::invalid_argument("VXC_TC_STAGES must be in [1, 8]");
+        }
+        const bool persist_ok = dit_persistent_ok(d, s->dit_grid), fused_ok = dit_fused_ok(d);
+        s->dit_form = 2;
+        if (const char* f = std::getenv("VXC_DIT_FORM")) {
+            const std::string form(f);
+            if (form == "persistent") s->dit_form = 0;
+            else if (form == "fused") s->dit_form = 1;
+            else if (form == "split") s->dit_form = 2;
+            else throw std::invalid_argument("VXC_DIT_FORM must be persistent, fused or split");
+            if ((s->dit_form == 0 && !persist_ok) || (s->dit_form == 1 && !fused_ok))
+                throw std::invalid_argument("VXC_DIT_FORM: that form does not support this model's shapes");
+        }
+        if (s->dit_form == 0) {
+            const size_t pf = dit_layers_part_floats(s->dit_grid);
+            s->dpart = dev_alloc<float>(pf);
+            const int sw = dit_layers_sync_words();
+            s->dsync = dev_alloc<unsigned>(sw);
+            ck(cudaMemset(s->dsync, 0, sizeof(unsigned) * sw), "cudaMemset");
+        }
+        const size_t ssq_n = static_cast<size_t>(std::max<int>(static_cast<int>(Hd / 16 + Hd / 32 + 1), s->dit_grid)) * kSsqStride;
+        s->dssq = dev_alloc<float>(ssq_n);
+        ck(cudaMemset(s->dssq, 0, ssq_n * sizeof(float)), "cudaMemset");
         for (__half** xb : {&s->xb_n, &s->xb_a, &s->xb_act}) {
             const size_t k = xb == &s->xb_act ? d.dit_ffn : Hd;
             *xb = dev_alloc<__half>(48 * k);
@@ -1300,7 +1521,7 @@ VXC_API int32_t vxc_dit_estimator(vxc_stream* s, const float* x_in, const float*
         ck(cudaMemcpyAsync(min_, mu_in, sizeof(float) * 4 * Hd, cudaMemcpyHostToDevice, s->cs), "mu");
         enqueue_time_tokens(s, t_in[0], t_in[1], dt_in, nullptr);
         enqueue_dit_eval(s, xin, xin + L, min_, min_ + 2 * Hd, cin, cin + L, dt_in[1] != dt_in[0], s->est, nullptr,
-                         0.f, 0.f, nullptr);
+                         0.f, 0.f, nullptr, nullptr);
         ck(cudaMemcpyAsync(out, s->est, sizeof(float) * 2 * L, cudaMemcpyDeviceToHost, s->cs), "download");
         ck(cudaStreamSynchronize(s->cs), "sync");
     });
@@ -1323,6 +1544,7 @@ VXC_API int32_t vxc_cfm_sample(vxc_stream* s, const float* mu, const float* cond
         // standalone call: a stale stop flag must not skip the kernels
         s->ctl_host->stopped = 0;
         ck(cudaMemcpyAsync(&s->ctl->stopped, &s->ctl_host->stopped, sizeof(int), cudaMemcpyHostToDevice, s->cs), "ctl");
+        time_table(s, timesteps);
         enqueue_cfm(s, c, timesteps, cfg_value);
         ck(cudaMemcpyAsync(out_latent, s->x, sizeof(float) * L, cudaMemcpyDeviceToHost, s->cs), "download");
         sync_ctl(s);
@@ -1627,108 +1849,203 @@ VXC_API int32_t vxc_profile_kernel(vxc_stream* s, int32_t kernel, int32_t iters,
     return guard([&] {
         require(s != nullptr && ms_per_launch != nullptr && bytes_per_launch != nullptr, "null argument");
         require(iters > 0 && iters <= 100000, "iters must be in [1, 100000]");
-        require(kernel >= VXC_PROF_DIT_GATEUP && kernel <= VXC_PROF_BASE_ATTN, "unknown kernel id");
+        require(kernel >= VXC_PROF_DIT_GATEUP && kernel <= VXC_PROF_DIT_LAYERS, "unknown kernel id");
         std::lock_guard<std::mutex> lk(s->call_mutex);
         const vxc_device* dev = s->dev;
         const vxc_model_desc& d = dev->desc;
         check_loaded(dev, {VXC_BASE_DECODER, VXC_DIT_ESTIMATOR});
         DeviceGuard g(dev->device);
+        if (kernel == VXC_PROF_DIT_LAYERS) {
+            // one persistent launch = every DiT layer of one evaluation; each launch timed
+            // alone between CUDA events (its sync block zeroed before it, outside the events)
+            require(s->dit_form == 0, "the stream does not use the persistent DiT form");
+            const DitLayersArgs a = dit_layers_args(s, s->ctl);
+            const size_t Hd = d.dit_hidden, F = d.dit_ffn;
+            const size_t W = static_cast<size_t>(d.dit_q_heads + 2 * d.dit_kv_heads) * (Hd / d.dit_q_heads);
+            const size_t M = 2 * static_cast<size_t>(dit_tokens_per_seq(d.patch_size));
+            const double per_layer = 2.0 * (W * Hd + Hd * Hd + 2 * F * Hd + Hd * F) + 4.0 * M * (2 * Hd + W);
+            const int sw = dit_layers_sync_words();
+            std::vector<cudaEvent_t> ev(2 * static_cast<size_t>(iters) + 2, nullptr);
+            cudaError_t err = cudaSuccess;
+            for (auto& e : ev)
+                if (err == cudaSuccess) err = cudaEventCreate(&e);
+            for (int i = -1; i < iters && err == cudaSuccess; ++i) {  // i = -1: warm-up
+                err = cudaMemsetAsync(s->dsync, 0, sizeof(unsigned) * sw, s->cs);
+                const size_t k = static_cast<size_t>(i + 1);
+                if (err == cudaSuccess) err = cudaEventRecord(ev[2 * k], s->cs);
+                if (err == cudaSuccess) {
+                    try {
+                        launch_dit_layers(a, s->dit_grid, s->cs);
+                    } catch (const std::exception&) {
+                        err = cudaErrorLaunchFailure;
+                    }
+                }
+                if (err == cudaSuccess) err = cudaEventRecord(ev[2 * k + 1], s->cs);
+            }
+            if (err == cudaSuccess) err = cudaStreamSynchronize(s->cs);
+            float total = 0.f;
+            for (int i = 0; i < iters && err == cudaSuccess; ++i) {
+                float ms = 0.f;
+                const size_t k = static_cast<size_t>(i + 1);
+                err = cudaEventElapsedTime(&ms, ev[2 * k], ev[2 * k + 1]);
+                total += ms;
+            }
+            for (auto& e : ev)
+                if (e) cudaEventDestroy(e);
+            ck(err, "persistent DiT profile");
+            sync_ctl(s);
+            *ms_per_launch = total / static_cast<float>(iters);
+            *bytes_per_launch = per_layer * d.dit_layers;
+            return;
+        }
         const int Hd = d.dit_hidden, Fd = d.dit_ffn, H = d.hidden, F = d.ffn;
-        const int M = 2 * dit_tokens_per_seq(d.patch_size);
+        const int seq = dit_tokens_per_seq(d.patch_size), M = 2 * seq;
         const int hq = d.q_heads, hkv = d.kv_heads, hd = d.head_dim;
+        const int dq = d.dit_q_heads, dkv = d.dit_kv_heads;
         const size_t plane = static_cast<size_t>(hkv) * s->cap * hd;
+        const bool fused = s->dit_form != 2;
+        const int Wd = (dq + 2 * dkv) * (Hd / dq);
         double bytes = 0.0;
-        std::function<void()> launch;
-        const LayerW& DL = dev->dit[0];
-        const LayerW& BL = dev->base[0];
+        // one launch per layer, in the form the patch graph runs it
+        std::vector<std::function<void(bool)>> launch;
         // the profiled decode kernels read kv_len from a private control block set to
         // the next free cache row (the q/k/v launch writes there), so valid rows stay intact
         const int pos = std::min(s->kv_len[0], s->cap - 1);
         const int T = pos + 1;
-        switch (kernel) {
-            case VXC_PROF_DIT_GATEUP: {
-                TcLinearArgs a;
-                a.K = Hd; a.M = M; a.rows = Fd; a.splits = choose_splits(Fd / 64, Hd); a.gateup = 1;
-                a.yb = s->xb_act; a.ldyb = Fd;
-                bytes = 2.0 * 2 * Fd * Hd + 2.0 * 48 * Hd + 2.0 * 48 * Fd;
-                const CUtensorMap ma = dev->dit_maps[0][2], mb = s->map_xb_n;
-                launch = [=] { launch_tc_linear(ma, mb, a, s->cs, false); };
-                break;
-            }
-            case VXC_PROF_DIT_DOWN: {
-                TcLinearArgs a;
-                a.K = Fd; a.M = M; a.rows = Hd; a.splits = choose_splits(Hd / 128, Fd); a.resid = 1;
-                a.y = s->dxn; a.ldy = Hd;
-                bytes = 2.0 * Hd * Fd + 2.0 * 48 * Fd + 8.0 * M * Hd;
-                const CUtensorMap ma = dev->dit_maps[0][3], mb = s->map_xb_act;
-                launch = [=] { launch_tc_linear(ma, mb, a, s->cs, false); };
-                break;
-            }
-            case VXC_PROF_DIT_QKV: {
-                const int W = (d.dit_q_heads + 2 * d.dit_kv_heads) * (Hd / d.dit_q_heads);
-                TcLinearArgs a;
-                a.K = Hd; a.M = M; a.rows = W; a.splits = choose_splits(W / 128, Hd);
-                a.y = s->dqkv; a.ldy = W;
-                bytes = 2.0 * W * Hd + 2.0 * 48 * Hd + 4.0 * M * W;
-                const CUtensorMap ma = dev->dit_maps[0][0], mb = s->map_xb_n;
-                launch = [=] { launch_tc_linear(ma, mb, a, s->cs, false); };
-                break;
-            }
-            case VXC_PROF_BASE_GATEUP: {
-                GemvArgs a;
-                a.mode = GEMV_GATEUP; a.w = BL.wgateup; a.x = s->out[0]; a.norm_g = BL.post_norm; a.eps = d.rms_eps;
-                a.K = H; a.rows = F; a.y = s->act;
-                bytes = 2.0 * 2 * F * H + 4.0 * H + 4.0 * F;
-                launch = [=] { launch_gemv(a, s->cs, false); };
-                break;
-            }
-            case VXC_PROF_BASE_DOWN: {
-                GemvArgs a;
-                a.mode = GEMV_RESID; a.w = BL.wdown; a.x = s->act; a.K = F; a.rows = H; a.resid = s->out[0];
-                bytes = 2.0 * H * F + 4.0 * F + 8.0 * H;
-                launch = [=] { launch_gemv(a, s->cs, false); };
-                break;
-            }
-            case VXC_PROF_BASE_QKV:
-            case VXC_PROF_BASE_ATTN: {
-                // run on a private control block so the stream's positions stay untouched
-                StreamCtl probe{};
-                probe.kv_len[0] = pos;
-                StreamCtl* pctl = reinterpret_cast<StreamCtl*>(s->est);  // >= sizeof(StreamCtl) floats
-                ck(cudaMemcpyAsync(pctl, &probe, sizeof(StreamCtl), cudaMemcpyHostToDevice, s->cs), "probe ctl");
-                ck(cudaStreamSynchronize(s->cs), "sync");
-                if (kernel == VXC_PROF_BASE_QKV) {
+        StreamCtl* pctl = reinterpret_cast<StreamCtl*>(s->est);  // >= sizeof(StreamCtl) floats
+        if (kernel == VXC_PROF_BASE_QKV || kernel == VXC_PROF_BASE_ATTN) {
+            StreamCtl probe{};
+            probe.kv_len[0] = pos;
+            ck(cudaMemcpyAsync(pctl, &probe, sizeof(StreamCtl), cudaMemcpyHostToDevice, s->cs), "probe ctl");
+            ck(cudaStreamSynchronize(s->cs), "sync");
+        }
+        const bool dit = kernel <= VXC_PROF_DIT_QKV || kernel == VXC_PROF_DIT_O;
+        const size_t nl = dit ? dev->dit.size() : dev->base.size();
+        for (size_t l = 0; l < nl; ++l) {
+            switch (kernel) {
+                case VXC_PROF_DIT_GATEUP: {
+                    TcLinearArgs a = tc_plan(s, Fd / 64, Hd, fused);
+                    a.K = Hd; a.M = M; a.rows = Fd; a.gateup = 1;
+                    a.yb = s->xb_act; a.ldyb = Fd; a.ctl = s->ctl;
+                    if (fused) {
+                        a.bmode = TC_B_NORM; a.x = s->dh; a.ldx = Hd; a.g = dev->dit[l].post_norm; a.eps = d.rms_eps;
+                        a.ssq_in = s->dssq; a.ssq_parts = (Hd / 128) * tc_plan(s, Hd / 128, dq * 64, true).splits;
+                    }
+                    bytes = 2.0 * 2 * Fd * Hd + (fused ? 4.0 * M * Hd : 2.0 * 48 * Hd) + 2.0 * 48 * Fd;
+                    const CUtensorMap ma = dev->dit_maps[l][2], mb = s->map_xb_n;
+                    launch.push_back([=](bool pdl) { launch_tc_linear(ma, mb, a, s->cs, pdl); });
+                    break;
+                }
+                case VXC_PROF_DIT_DOWN: {
+                    TcLinearArgs a = tc_plan(s, Hd / 128, Fd, false);
+                    a.K = Fd; a.M = M; a.rows = Hd; a.resid = 1;
+                    a.y = s->dxn; a.ldy = Hd; a.ctl = s->ctl;
+                    if (fused) a.ssq_out = s->dssq + static_cast<size_t>(Hd / 16) * kSsqStride;  // spare parts
+                    bytes = 2.0 * Hd * Fd + 2.0 * 48 * Fd + 8.0 * M * Hd;
+                    const CUtensorMap ma = dev->dit_maps[l][3], mb = s->map_xb_act;
+                    launch.push_back([=](bool pdl) { launch_tc_linear(ma, mb, a, s->cs, pdl); });
+                    break;
+                }
+                case VXC_PROF_DIT_QKV: {
+                    TcLinearArgs a = tc_plan(s, Wd / 128, Hd, fused);
+                    a.K = Hd; a.M = M; a.rows = Wd;
+                    a.y = s->dqkv; a.ldy = Wd; a.ctl = s->ctl;
+                    if (fused) {
+                        a.bmode = TC_B_NORM; a.x = s->dh; a.ldx = Hd; a.g = dev->dit[l].in_norm; a.eps = d.rms_eps;
+                        a.ssq_in = s->dssq; a.ssq_parts = (Hd + 31) / 32;
+                    }
+                    bytes = 2.0 * Wd * Hd + (fused ? 4.0 * M * Hd : 2.0 * 48 * Hd) + 4.0 * M * Wd;
+                    const CUtensorMap ma = dev->dit_maps[l][0], mb = s->map_xb_n;
+                    launch.push_back([=](bool pdl) { launch_tc_linear(ma, mb, a, s->cs, pdl); });
+                    break;
+                }
+                case VXC_PROF_DIT_O: {
+                    TcLinearArgs a = tc_plan(s, Hd / 128, dq * 64, fused);
+                    a.K = dq * 64; a.M = M; a.rows = Hd; a.resid = 1;
+                    a.y = s->dxn; a.ldy = Hd; a.ctl = s->ctl;
+                    if (fused) {
+                        a.bmode = TC_B_ATTN; a.qkv = s->dqkv; a.q_heads = dq; a.kv_heads = dkv; a.seq = seq;
+                        a.rope_cos = dev->dit_rope_cos; a.rope_sin = dev->dit_rope_sin; a.scale = 0.125f;
+                        a.attn_round = tc_attn_round(a.K, a.splits, a.max_stages);
+                        a.ssq_out = s->dssq + static_cast<size_t>(Hd / 16) * kSsqStride;
+                    }
+                    bytes = 2.0 * Hd * dq * 64 + (fused ? 4.0 * M * Wd : 2.0 * 48 * dq * 64) + 8.0 * M * Hd;
+                    const CUtensorMap ma = dev->dit_maps[l][1], mb = s->map_xb_a;
+                    launch.push_back([=](bool pdl) { launch_tc_linear(ma, mb, a, s->cs, pdl); });
+                    break;
+                }
+                case VXC_PROF_BASE_GATEUP: {
+                    const LayerW& BL = dev->base[l];
+                    GemvArgs a;
+                    a.mode = GEMV_GATEUP; a.w = BL.wgateup; a.x = s->out[0]; a.norm_g = BL.post_norm; a.eps = d.rms_eps;
+                    a.K = H; a.rows = F; a.y = s->act;
+                    bytes = 2.0 * 2 * F * H + 4.0 * H + 4.0 * F;
+                    launch.push_back([=](bool pdl) { launch_gemv(a, s->cs, pdl); });
+                    break;
+                }
+                case VXC_PROF_BASE_DOWN: {
+                    GemvArgs a;
+                    a.mode = GEMV_RESID; a.w = dev->base[l].wdown; a.x = s->act; a.K = F; a.rows = H; a.resid = s->out[0];
+                    bytes = 2.0 * H * F + 4.0 * F + 8.0 * H;
+                    launch.push_back([=](bool pdl) { launch_gemv(a, s->cs, pdl); });
+                    break;
+                }
+                case VXC_PROF_BASE_QKV: {
+                    const LayerW& BL = dev->base[l];
                     GemvArgs a;
                     a.mode = GEMV_QKV; a.w = BL.wqkv; a.x = s->out[0]; a.norm_g = BL.in_norm; a.eps = d.rms_eps;
                     a.K = H; a.rows = (hq + 2 * hkv) * hd / 2; a.y = s->q; a.q_heads = hq; a.kv_heads = hkv;
                     a.head_dim = hd; a.rope_cos = s->rope_cos; a.rope_sin = s->rope_sin;
-                    a.k_cache = s->kc[0]; a.v_cache = s->vc[0]; a.cap = s->cap; a.which = 0; a.ctl = pctl;
+                    a.k_cache = s->kc[0] + l * plane; a.v_cache = s->vc[0] + l * plane; a.cap = s->cap; a.which = 0;
+                    a.ctl = pctl;
                     bytes = 2.0 * (hq + 2 * hkv) * hd * H + 4.0 * H + 4.0 * hq * hd + 4.0 * 2 * hkv * hd;
-                    launch = [=] { launch_gemv(a, s->cs, false); };
-                } else {
-                    AttnArgs a;
-                    a.q = s->q; a.k0 = s->kc[0]; a.v0 = s->vc[0]; a.len0 = s->cap; a.stride0 = s->cap;
-                    a.q_heads = hq; a.kv_heads = hkv; a.head_dim = hd; a.scale = 0.125f; a.splits = s->splits;
-                    a.partial = s->partial; a.counters = s->counters; a.out = s->attn; a.ctl = pctl; a.which = 0;
-                    bytes = 4.0 * 2 * hkv * static_cast<double>(T) * hd + 8.0 * hq * hd;
-                    launch = [=] { launch_attn_decode(a, false, s->cs, false); };
+                    launch.push_back([=](bool pdl) { launch_gemv(a, s->cs, pdl); });
+                    break;
                 }
-                break;
+                case VXC_PROF_BASE_ATTN: {
+                    AttnArgs a;
+                    a.q = s->q; a.k0 = s->kc[0] + l * plane; a.v0 = s->vc[0] + l * plane; a.len0 = s->cap;
+                    a.stride0 = s->cap; a.q_heads = hq; a.kv_heads = hkv; a.head_dim = hd; a.scale = 0.125f;
+                    a.splits = s->splits; a.partial = s->partial; a.counters = s->counters; a.out = s->attn;
+                    a.ctl = pctl; a.which = 0;
+                    bytes = 4.0 * 2 * hkv * static_cast<double>(T) * hd + 8.0 * hq * hd;
+                    launch.push_back([=](bool pdl) { launch_attn_decode(a, false, s->cs, pdl); });
+                    break;
+                }
             }
         }
-        (void)plane;
-        launch();  // warm-up
-        cudaEvent_t e0, e1;
-        ck(cudaEventCreate(&e0), "event");
-        ck(cudaEventCreate(&e1), "event");
-        ck(cudaEventRecord(e0, s->cs), "event");
-        for (int i = 0; i < iters; ++i) launch();
-        ck(cudaEventRecord(e1, s->cs), "event");
-        ck(cudaEventSynchronize(e1), "event");
+        // iters launches cycling through the layers, captured in one graph with
+        // programmatic dependent launch between them like the patch graph
+        for (auto& f : launch) f(false);  // warm-up, eager
+        cudaGraph_t gr = nullptr;
+        ck(cudaStreamBeginCapture(s->cs, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+        try {
+            for (int i = 0; i < iters; ++i) launch[static_cast<size_t>(i) % launch.size()](i > 0);
+        } catch (...) {
+            cudaStreamEndCapture(s->cs, &gr);
+            if (gr) cudaGraphDestroy(gr);
+            throw;
+        }
+        ck(cudaStreamEndCapture(s->cs, &gr), "cudaStreamEndCapture");
+        cudaGraphExec_t ge = nullptr;
+        const cudaError_t ie = cudaGraphInstantiate(&ge, gr, 0);
+        cudaGraphDestroy(gr);
+        ck(ie, "cudaGraphInstantiate");
+        cudaEvent_t e0 = nullptr, e1 = nullptr;
         float ms = 0.f;
-        ck(cudaEventElapsedTime(&ms, e0, e1), "event");
-        cudaEventDestroy(e0);
-        cudaEventDestroy(e1);
+        cudaError_t err = cudaGraphLaunch(ge, s->cs);  // warm-up replay
+        if (err == cudaSuccess) err = cudaEventCreate(&e0);
+        if (err == cudaSuccess) err = cudaEventCreate(&e1);
+        if (err == cudaSuccess) err = cudaEventRecord(e0, s->cs);
+        if (err == cudaSuccess) err = cudaGraphLaunch(ge, s->cs);
+        if (err == cudaSuccess) err = cudaEventRecord(e1, s->cs);
+        if (err == cudaSuccess) err = cudaEventSynchronize(e1);
+        if (err == cudaSuccess) err = cudaEventElapsedTime(&ms, e0, e1);
+        if (e0) cudaEventDestroy(e0);
+        if (e1) cudaEventDestroy(e1);
+        cudaGraphExecDestroy(ge);
+        ck(err, "profile replay");
+        sync_ctl(s);  // a bounded wait that gave up inside the profiled kernels surfaces here
         *ms_per_launch = ms / static_cast<float>(iters);
         *bytes_per_launch = bytes;
     });

@@ -27,123 +27,210 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cfloat>
 #include <stdexcept>
 
 #include "kernels.cuh"
+#include "tc_common.cuh"
 
 namespace vxc {
 namespace {
 
+using namespace tc;
+
 constexpr int kTcThreads = 128;
-constexpr int kTileRows = 128;      // MMA M (output features per tile)
-constexpr int kKChunk = 64;         // fp16 elements per 128-byte swizzle row
-constexpr int kBRows = 48;          // MMA N (hi tokens 0..23, lo tokens 24..47)
-constexpr int kLoOffset = 24;
-constexpr int kABytes = kTileRows * kKChunk * 2;  // 16 KiB
-constexpr int kBBytes = kBRows * kKChunk * 2;     // 6 KiB
 constexpr int kStageBytes = kABytes + kBBytes;    // 22 KiB, keeps 1 KiB alignment
 constexpr int kMaxStages = 8;
 constexpr int kRowFloats = 25;      // exchange-buffer row stride: 24 tokens + 1 (odd: conflict-free reads)
 constexpr int kTmemCols = 64;
-constexpr uint32_t kWaitLimit = 1u << 22;
 
-__device__ __forceinline__ uint32_t smem_addr(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
-                 : "memory");
-}
-
-// Bounded wait for phase 'parity' of an mbarrier; false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    const uint32_t addr = smem_addr(bar);
-    for (uint32_t i = 0; i < kWaitLimit; ++i) {
-        uint32_t done;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(done)
-            : "r"(addr), "r"(parity)
-            : "memory");
-        if (done) return true;
+// Zero token rows M..23 (and their residual rows) of 'cs' B tiles.
+__device__ __forceinline__ void zero_pad_rows(uint8_t* smem, int cs, int M) {
+    const int pad = kLoOffset - M;
+    for (int u = threadIdx.x; u < cs * pad * 16; u += kTcThreads) {
+        const int ch = u / (pad * 16), r = u - ch * pad * 16, m = M + r / 16, col = (r & 15) * 4;
+        put_split4(smem + ch * kStageBytes + kABytes, m, col, make_float4(0.f, 0.f, 0.f, 0.f));
     }
-    return false;
 }
 
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-        ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
-        : "memory");
-}
-
-// K-major, 128-byte-swizzle UMMA shared-memory descriptor: start address >> 4,
-// leading offset 1 (unused for swizzled K-major), stride offset 1024 B between
-// 8-row groups, descriptor version 1, layout type 2 (SWIZZLE_128B).
-__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
-    return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) |
-           (2ull << 61);
-}
-
-// kind::f16 instruction descriptor: fp32 accumulate, fp16 A and B, both K-major.
-__host__ __device__ constexpr uint32_t umma_idesc(int m, int n) {
-    return (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
-}
-
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                     smem_addr(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-    uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
+// B = split-fp16 RMSNorm(x) for chunks c0 .. c0 + cs - 1 (RMSNorm as in
+// rmsnorm_rows_split_kernel: x * rsqrt(mean(x^2) + eps) * g). The row sums of
+// squares are the fixed-order sum of the producer's partials. Every thread
+// issues its loads in batches before it uses any (each global round trip costs
+// about a microsecond here).
+__device__ void build_b_norm(uint8_t* smem, const TcLinearArgs& a, int c0, int cs, float* inv_s, float4* red) {
+    const int tid = threadIdx.x;
+    // 120 threads = 20 part groups x 6 token quads, then a fixed-order sum over the groups
+    if (tid < 120) {
+        const int r = tid / 6, q = tid - r * 6;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int p0 = 0; p0 < a.ssq_parts; p0 += 160) {
+            float4 v[8];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+            for (int i = 0; i < 8; ++i) {
+                const int p = p0 + r + 20 * i;
+                v[i] = p < a.ssq_parts ? __ldcg(reinterpret_cast<const float4*>(a.ssq_in + p * kSsqStride) + q)
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                acc.x += v[i].x;
+                acc.y += v[i].y;
+                acc.z += v[i].z;
+                acc.w += v[i].w;
+            }
+        }
+        red[r * 6 + q] = acc;
+    }
+    __syncthreads();
+    if (tid < kLoOffset) {
+        const float* rf = reinterpret_cast<const float*>(red);
+        float t = 0.f;
+        for (int r = 0; r < 20; ++r) t += rf[r * 24 + tid];
+        inv_s[tid] = rsqrtf(t / static_cast<float>(a.K) + a.eps);
+    }
+    __syncthreads();
+    const int per = cs * 16, total = a.M * per;  // float4 units per token row, in all
+    constexpr int kB = 8;
+    for (int base = 0; base < total; base += kTcThreads * kB) {
+        float4 xv[kB];
+        uint2 gw[kB];
+#pragma unroll
+        for (int i = 0; i < kB; ++i) {
+            const int u = base + tid + kTcThreads * i;
+            if (u < total) {
+                const int m = u / per, q = u - m * per, k = (c0 + (q >> 4)) * kKChunk + (q & 15) * 4;
+                xv[i] = __ldcg(reinterpret_cast<const float4*>(a.x + static_cast<size_t>(m) * a.ldx + k));
+                gw[i] = __ldg(reinterpret_cast<const uint2*>(a.g + k));
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < kB; ++i) {
+            const int u = base + tid + kTcThreads * i;
+            if (u < total) {
+                const int m = u / per, q = u - m * per, ch = q >> 4, col = (q & 15) * 4;
+                const float2 g01 = __half22float2(*reinterpret_cast<const __half2*>(&gw[i].x));
+                const float2 g23 = __half22float2(*reinterpret_cast<const __half2*>(&gw[i].y));
+                const float iv = inv_s[m];
+                put_split4(smem + ch * kStageBytes + kABytes, m, col,
+                           make_float4(xv[i].x * iv * g01.x, xv[i].y * iv * g01.y, xv[i].z * iv * g23.x,
+                                       xv[i].w * iv * g23.y));
+            }
+        }
+    }
+    zero_pad_rows(smem, cs, a.M);
 }
 
-__device__ __forceinline__ void cluster_sync() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+// Attention scratch per head of a round (floats): q and k [24][65], v [24][64],
+// probabilities [2 sequences][12][13].
+constexpr int kAttnRow = 65;
+constexpr int kAttnHeadFloats = 2 * 24 * kAttnRow + 24 * 64 + 2 * 12 * 13;
+constexpr size_t kSmemOptin = 232448;  // B200: opt-in shared memory per CTA (227 KB)
+size_t g_dyn_limit = 0;                // kSmemOptin less the kernel's static shared memory (set once)
+
+// B = split-fp16 attention output of heads c0 .. c0 + cs - 1 (one 64-wide head
+// per K chunk), the math of dit_attention_split_kernel: RoPE (rotate_half) on q
+// and k, scores * scale, softmax, P.V, both sequences, 'round' heads at a time.
+__device__ void build_b_attn(uint8_t* smem, const TcLinearArgs& a, int c0, int cs, int round, float* scratch) {
+    constexpr int D = 64, HALF = 32;
+    const int tid = threadIdx.x, M = a.M, seq = a.seq;
+    const int W = (a.q_heads + 2 * a.kv_heads) * D, grp = a.q_heads / a.kv_heads;
+    float* qs = scratch;
+    float* ks = qs + round * 24 * kAttnRow;
+    float* vs = ks + round * 24 * kAttnRow;
+    float* ps = vs + round * 24 * D;
+    for (int h0 = 0; h0 < cs; h0 += round) {
+        const int nh = min(round, cs - h0);
+        // raw q / k / v rows of the round's heads (nh x M x 3 x 16 float4), loads in batches
+        constexpr int kB = 9;
+        const int total = nh * M * 48;
+        for (int base = 0; base < total; base += kTcThreads * kB) {
+            float4 v[kB];
+#pragma unroll
+            for (int i = 0; i < kB; ++i) {
+                const int u = base + tid + kTcThreads * i;
+                if (u < total) {
+                    const int hl = u / (M * 48), r2 = u - hl * M * 48, i2 = r2 / 48, w = r2 - i2 * 48;
+                    const int kind = w >> 4, e4 = (w & 15) * 4, h = c0 + h0 + hl, kvh = h / grp;
+                    const int col = kind == 0 ? h * D : kind == 1 ? (a.q_heads + kvh) * D
+                                                                  : (a.q_heads + a.kv_heads + kvh) * D;
+                    v[i] = __ldcg(reinterpret_cast<const float4*>(a.qkv + static_cast<size_t>(i2) * W + col + e4));
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < kB; ++i) {
+                const int u = base + tid + kTcThreads * i;
+                if (u < total) {
+                    const int hl = u / (M * 48), r2 = u - hl * M * 48, i2 = r2 / 48, w = r2 - i2 * 48;
+                    const int kind = w >> 4, e4 = (w & 15) * 4;
+                    float* dst = kind == 0 ? qs + (hl * 24 + i2) * kAttnRow
+                                           : kind == 1 ? ks + (hl * 24 + i2) * kAttnRow : vs + (hl * 24 + i2) * D;
+                    dst[e4] = v[i].x;
+                    dst[e4 + 1] = v[i].y;
+                    dst[e4 + 2] = v[i].z;
+                    dst[e4 + 3] = v[i].w;
+                }
+            }
+        }
+        __syncthreads();
+        // RoPE (rotate_half) on q and k in place: each unit owns the pair (e, e + 32)
+        for (int u = tid; u < nh * 2 * M * HALF; u += kTcThreads) {
+            const int hl = u / (2 * M * HALF), r2 = u - hl * 2 * M * HALF, which = r2 / (M * HALF);
+            const int r3 = r2 - which * M * HALF, i = r3 / HALF, e = r3 - i * HALF, pos = i % seq;
+            float* row = (which == 0 ? qs : ks) + (hl * 24 + i) * kAttnRow;
+            const float c1 = __ldg(a.rope_cos + pos * D + e), c2 = __ldg(a.rope_cos + pos * D + e + HALF);
+            const float s1 = __ldg(a.rope_sin + pos * D + e), s2 = __ldg(a.rope_sin + pos * D + e + HALF);
+            const float v1 = row[e], v2 = row[e + HALF];
+            row[e] = v1 * c1 + (-v2) * s1;
+            row[e + HALF] = v2 * c2 + v1 * s2;
+        }
+        __syncthreads();
+        for (int u = tid; u < nh * 2 * seq * seq; u += kTcThreads) {
+            const int hl = u / (2 * seq * seq), r = u - hl * 2 * seq * seq, b = r / (seq * seq);
+            const int r2 = r - b * seq * seq, i = r2 / seq, j = r2 - i * seq;
+            const float* q = qs + (hl * 24 + b * seq + i) * kAttnRow;
+            const float* k = ks + (hl * 24 + b * seq + j) * kAttnRow;
+            float sum = 0.f;
+#pragma unroll 16
+            for (int e = 0; e < D; ++e) sum = fmaf(q[e], k[e], sum);
+            ps[((hl * 2 + b) * 12 + i) * 13 + j] = sum * a.scale;
+        }
+        __syncthreads();
+        for (int u = tid; u < nh * 2 * seq; u += kTcThreads) {
+            float* pr = ps + ((u / seq) * 12 + (u % seq)) * 13;  // u = (head * 2 + b) * seq + i
+            float mx = -FLT_MAX;
+            for (int j = 0; j < seq; ++j) mx = fmaxf(mx, pr[j]);
+            float sum = 0.f;
+            for (int j = 0; j < seq; ++j) {
+                pr[j] = expf(pr[j] - mx);
+                sum += pr[j];
+            }
+            for (int j = 0; j < seq; ++j) pr[j] /= sum;
+        }
+        __syncthreads();
+        for (int u = tid; u < nh * M * 16; u += kTcThreads) {
+            const int hl = u / (M * 16), r = u - hl * M * 16, m = r >> 4, col = (r & 15) * 4;
+            const int b = m / seq, i = m - b * seq;
+            const float* pr = ps + ((hl * 2 + b) * 12 + i) * 13;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int j = 0; j < seq; ++j) {
+                const float p = pr[j];
+                const float* vr = vs + (hl * 24 + b * seq + j) * D + col;
+                acc.x = fmaf(p, vr[0], acc.x);
+                acc.y = fmaf(p, vr[1], acc.y);
+                acc.z = fmaf(p, vr[2], acc.z);
+                acc.w = fmaf(p, vr[3], acc.w);
+            }
+            put_split4(smem + (h0 + hl) * kStageBytes + kABytes, m, col, acc);
+        }
+        __syncthreads();  // the next head pair reuses the scratch
+    }
+    zero_pad_rows(smem, cs, M);
 }
 
-// Address of 'local' in the shared memory of cluster CTA 'rank'.
-__device__ __forceinline__ uint32_t peer_addr(const void* local, uint32_t rank) {
-    uint32_t remote;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_addr(local)), "r"(rank));
-    return remote;
-}
-__device__ __forceinline__ void st_peer(uint32_t remote, float v) {  // fire and forget
-    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
-}
-
-__device__ __forceinline__ void store_split(__half* yb, int ld, int m, int col, float v) {
-    const __half hi = __float2half_rn(v);
-    yb[static_cast<size_t>(m) * ld + col] = hi;
-    yb[static_cast<size_t>(kLoOffset + m) * ld + col] = __float2half_rn(v - __half2float(hi));
-}
-
+// BM: where the token operand comes from (TC_B_TMA / TC_B_NORM / TC_B_ATTN); one
+// instantiation each, so the TMA form does not carry the builders' registers.
+template <int BM>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_linear_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                      const TcLinearArgs a) {
@@ -151,24 +238,29 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __shared__ uint64_t full_bar[kMaxStages], empty_bar[kMaxStages], done_bar;
     __shared__ uint32_t tmem_base_s;
     __shared__ int failed_s;
+    __shared__ float inv_s[kLoOffset];
+    __shared__ float4 red_s[120];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int split = blockIdx.x, tile = blockIdx.y;
     const int S = a.splits;
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    constexpr bool b_tma = BM == TC_B_TMA;
 
     const int nch = a.K / kKChunk;
     const int c0 = split * nch / S, c1 = (split + 1) * nch / S, cs = c1 - c0;
-    const int stages = min(kMaxStages, max(cs, 1));
+    const int stages = min(a.max_stages, max(cs, 1));
     // the receive buffer sits after the stage area of the largest split: the same
     // offset in every CTA of the cluster, whatever its own chunk count
-    const int stage_area = min(kMaxStages, max((nch + S - 1) / S, 1));
+    const int stage_area = min(a.max_stages, max((nch + S - 1) / S, 1));
 
     // thread 0: barriers, then the weight loads at once (they depend on no earlier
     // kernel); warp 1 meanwhile allocates the TMEM accumulator
     const int r0 = a.gateup ? tile * 64 : tile * kTileRows;   // rows of W in this tile: two
     const int r1 = a.gateup ? a.rows + tile * 64 : tile * kTileRows + 64;  // 64-row boxes
     const int pre = min(stages, cs);
+    // bytes landing on a stage's barrier: the weight tile, plus the token tile when TMA brings it
+    const uint32_t stage_tx = b_tma ? kStageBytes : kABytes;
     int issued[kMaxStages];  // producer: loads issued per stage (for the drain below)
     if (tid == 0) {
         for (int i = 0; i < stages; ++i) {
@@ -179,12 +271,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         failed_s = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b)) : "memory");
+        if (b_tma) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b)) : "memory");
 #pragma unroll
         for (int i = 0; i < kMaxStages; ++i) issued[i] = 0;
         for (int i = 0; i < pre; ++i) {
             uint8_t* st = smem + i * kStageBytes;
-            mbar_expect_tx(&full_bar[i], kStageBytes);
+            mbar_expect_tx(&full_bar[i], stage_tx);
             tma_load_2d(st, &map_a, (c0 + i) * kKChunk, r0, &full_bar[i]);
             tma_load_2d(st + kABytes / 2, &map_a, (c0 + i) * kKChunk, r1, &full_bar[i]);
             issued[i] = 1;
@@ -202,25 +294,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const uint32_t tmem_d = tmem_base_s;
     pdl_launch_dependents();
 
-    if (tid == 0) {
-        pdl_wait();
-        for (int i = 0; i < pre; ++i)
-            tma_load_2d(smem + i * kStageBytes + kABytes, &map_b, (c0 + i) * kKChunk, 0, &full_bar[i]);
-        for (int i = pre; i < cs; ++i) {
-            const int s = i % stages;
-            if (!mbar_wait(&empty_bar[s], ((i / stages) - 1) & 1)) {
-                failed_s = 1;
-                break;
-            }
-            uint8_t* st = smem + s * kStageBytes;
-            mbar_expect_tx(&full_bar[s], kStageBytes);
-            tma_load_2d(st, &map_a, (c0 + i) * kKChunk, r0, &full_bar[s]);
-            tma_load_2d(st + kABytes / 2, &map_a, (c0 + i) * kKChunk, r1, &full_bar[s]);
-            tma_load_2d(st + kABytes, &map_b, (c0 + i) * kKChunk, 0, &full_bar[s]);
-            issued[s] += 1;
-        }
-    } else if (tid == 32) {
-        pdl_wait();
+    // tensor-core issue: thread 32, one 128 x 48 x 16 MMA per 16 fp16 of K
+    auto mma_loop = [&] {
         const uint32_t idesc = umma_idesc(kTileRows, kBRows);
         for (int i = 0; i < cs; ++i) {
             const int s = i % stages;
@@ -236,8 +311,47 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             umma_commit(&empty_bar[s]);  // frees the stage once these MMAs have read it
         }
         umma_commit(&done_bar);  // arrives when every MMA issued above has completed
+    };
+
+    if constexpr (b_tma) {
+        if (tid == 0) {
+            pdl_wait();
+            for (int i = 0; i < pre; ++i)
+                tma_load_2d(smem + i * kStageBytes + kABytes, &map_b, (c0 + i) * kKChunk, 0, &full_bar[i]);
+            for (int i = pre; i < cs; ++i) {
+                const int s = i % stages;
+                if (!mbar_wait(&empty_bar[s], ((i / stages) - 1) & 1)) {
+                    failed_s = 1;
+                    break;
+                }
+                uint8_t* st = smem + s * kStageBytes;
+                mbar_expect_tx(&full_bar[s], kStageBytes);
+                tma_load_2d(st, &map_a, (c0 + i) * kKChunk, r0, &full_bar[s]);
+                tma_load_2d(st + kABytes / 2, &map_a, (c0 + i) * kKChunk, r1, &full_bar[s]);
+                tma_load_2d(st + kABytes, &map_b, (c0 + i) * kKChunk, 0, &full_bar[s]);
+                issued[s] += 1;
+            }
+        } else if (tid == 32) {
+            pdl_wait();
+            mma_loop();
+        } else {
+            pdl_wait();
+        }
     } else {
+        // all chunks have their own stage (cs <= stages, checked by the launcher):
+        // every thread builds the token tiles next to the weight tiles in flight
         pdl_wait();
+        if constexpr (BM == TC_B_NORM) {
+            build_b_norm(smem, a, c0, cs, inv_s, red_s);
+        } else {
+            const int slice_rows = max((kTileRows + S - 1) / S, 2 * ((64 + S - 1) / S));
+            float* scratch = reinterpret_cast<float*>(smem + static_cast<size_t>(stage_area) * kStageBytes) +
+                             S * slice_rows * kRowFloats;
+            build_b_attn(smem, a, c0, cs, a.attn_round, scratch);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic-proxy writes -> tensor core
+        __syncthreads();
+        if (tid == 32) mma_loop();
     }
 
     // drain the accumulator: warp w owns TMEM lanes (tile rows) 32w .. 32w + 31
@@ -291,6 +405,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (S > 1) cluster_sync();  // every partial has landed in its owner's buffer
     else __syncthreads();
     const int u0 = split * units / S, nu = (split + 1) * units / S - u0;
+    float* sq = reinterpret_cast<float*>(smem);  // the stage area is idle now: squares of updated rows
     for (int it = tid; it < nu * a.M; it += kTcThreads) {
         const int m = it / nu, lu = it - m * nu;
         if (a.gateup) {
@@ -304,11 +419,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             float v = 0.f;
             for (int p = 0; p < S; ++p) v += recv[(p * slice + lu) * kRowFloats + m];
             float* y = a.y + static_cast<size_t>(m) * a.ldy + tile * kTileRows + u0 + lu;
-            if (a.resid) *y = *y + (a.rscale == 1.f ? v : v * a.rscale);
-            else *y = v;
+            const float nv = a.resid ? *y + (a.rscale == 1.f ? v : v * a.rscale) : v;
+            *y = nv;
+            if (a.ssq_out) sq[m * nu + lu] = nv * nv;
         }
     }
     __syncthreads();
+    if (a.ssq_out && tid < a.M) {  // this owner's part of each row's sum of squares, fixed order
+        float t = 0.f;
+        for (int lu = 0; lu < nu; ++lu) t += sq[tid * nu + lu];
+        a.ssq_out[(tile * S + split) * kSsqStride + tid] = t;
+    }
     if (tid == 0 && failed_s && a.ctl) a.ctl->error = 3;
     if (warp == 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(kTmemCols)
@@ -317,15 +438,36 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
 }  // namespace
 
-size_t tc_linear_smem_bytes(int K, int splits) {
+size_t tc_linear_smem_bytes(int K, int splits, int bmode, int attn_round, int max_stages) {
     const int nch = K / kKChunk;
     const int cs = (nch + splits - 1) / splits;
-    const int stages = std::min(kMaxStages, std::max(cs, 1));
+    const int stages = std::min(std::min(max_stages, kMaxStages), std::max(cs, 1));
     const size_t stage_bytes = static_cast<size_t>(stages) * kStageBytes;
     // receive buffer: per source split, an owner slice of rows (or of gate/up pairs, 2 rows each)
     const size_t slice_rows = std::max((128 + splits - 1) / splits, 2 * ((64 + splits - 1) / splits));
     const size_t recv_bytes = static_cast<size_t>(splits) * slice_rows * kRowFloats * sizeof(float);
-    return stage_bytes + recv_bytes + 1024;  // + alignment slack
+    const size_t scratch = bmode == TC_B_ATTN ? static_cast<size_t>(attn_round) * kAttnHeadFloats * sizeof(float) : 0;
+    return stage_bytes + recv_bytes + scratch + 1024;  // + alignment slack
+}
+
+size_t dyn_limit() {
+    if (!g_dyn_limit) {
+        size_t most = 0;
+        for (const void* f : {reinterpret_cast<const void*>(tc_linear_kernel<TC_B_TMA>),
+                              reinterpret_cast<const void*>(tc_linear_kernel<TC_B_NORM>),
+                              reinterpret_cast<const void*>(tc_linear_kernel<TC_B_ATTN>)}) {
+            cudaFuncAttributes fa{};
+            const cudaError_t e = cudaFuncGetAttributes(&fa, f);
+            if (e != cudaSuccess) throw std::runtime_error(std::string("tc_linear attributes: ") + cudaGetErrorString(e));
+            most = std::max(most, fa.sharedSizeBytes);
+        }
+        g_dyn_limit = kSmemOptin - most;
+    }
+    return g_dyn_limit;
+}
+
+int tc_attn_round(int K, int splits, int max_stages) {
+    return tc_linear_smem_bytes(K, splits, TC_B_ATTN, 2, max_stages) <= dyn_limit() ? 2 : 1;
 }
 
 void launch_tc_linear(const CUtensorMap& map_a, const CUtensorMap& map_b, const TcLinearArgs& a, cudaStream_t s,
@@ -336,10 +478,26 @@ void launch_tc_linear(const CUtensorMap& map_a, const CUtensorMap& map_b, const 
         throw std::invalid_argument("tc_linear: splits must be in [1, 8] and at most K / 64");
     const int n_tiles = a.gateup ? a.rows / 64 : a.rows / kTileRows;
     if ((a.gateup ? a.rows % 64 : a.rows % kTileRows) != 0) throw std::invalid_argument("tc_linear: rows");
+    if (a.bmode != TC_B_TMA) {
+        const int nch = a.K / kKChunk;
+        if ((nch + a.splits - 1) / a.splits > a.max_stages)
+            throw std::invalid_argument("tc_linear: a fused token tile needs a stage per K chunk of the CTA");
+    }
+    if (a.bmode == TC_B_NORM && (!a.x || !a.g || !a.ssq_in || a.ssq_parts <= 0 || a.ldx % 4 != 0 ||
+                                 (reinterpret_cast<uintptr_t>(a.x) & 15) != 0 ||
+                                 (reinterpret_cast<uintptr_t>(a.g) & 7) != 0))
+        throw std::invalid_argument("tc_linear: bad RMSNorm operand");
+    if (a.bmode == TC_B_ATTN &&
+        (!a.qkv || !a.rope_cos || !a.rope_sin || a.kv_heads <= 0 || a.q_heads % a.kv_heads != 0 ||
+         a.K != a.q_heads * 64 || a.seq <= 0 || a.seq > 12 || a.M != 2 * a.seq || a.attn_round < 1))
+        throw std::invalid_argument("tc_linear: bad attention operand");
+    if (a.ssq_out && (a.gateup || a.M > kSsqStride)) throw std::invalid_argument("tc_linear: bad ssq_out");
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.splits, n_tiles);
     cfg.blockDim = dim3(kTcThreads);
-    cfg.dynamicSmemBytes = tc_linear_smem_bytes(a.K, a.splits);
+    if (a.max_stages < 1 || a.max_stages > kMaxStages) throw std::invalid_argument("tc_linear: max_stages in [1, 8]");
+    cfg.dynamicSmemBytes = tc_linear_smem_bytes(a.K, a.splits, a.bmode, a.attn_round, a.max_stages);
+    if (cfg.dynamicSmemBytes > dyn_limit()) throw std::invalid_argument("tc_linear: shared memory over 227 KB");
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -350,16 +508,22 @@ void launch_tc_linear(const CUtensorMap& map_a, const CUtensorMap& map_b, const 
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, tc_linear_kernel, map_a, map_b, a);
+    const cudaError_t e =
+        a.bmode == TC_B_TMA ? cudaLaunchKernelEx(&cfg, tc_linear_kernel<TC_B_TMA>, map_a, map_b, a)
+        : a.bmode == TC_B_NORM ? cudaLaunchKernelEx(&cfg, tc_linear_kernel<TC_B_NORM>, map_a, map_b, a)
+                               : cudaLaunchKernelEx(&cfg, tc_linear_kernel<TC_B_ATTN>, map_a, map_b, a);
     if (e != cudaSuccess) throw std::runtime_error(std::string("tc_linear launch: ") + cudaGetErrorString(e));
 }
 
 void init_tc_attributes() {
-    size_t most = 0;  // the largest launch: 8 stages plus the largest receive buffer over split counts
-    for (int sp = 1; sp <= 8; ++sp) most = std::max(most, tc_linear_smem_bytes(64 * 8 * sp, sp));
-    const cudaError_t e = cudaFuncSetAttribute(tc_linear_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(most));
-    if (e != cudaSuccess) throw std::runtime_error(std::string("tc_linear attribute: ") + cudaGetErrorString(e));
+    // every launch checks its own need against this limit
+    for (const void* f : {reinterpret_cast<const void*>(tc_linear_kernel<TC_B_TMA>),
+                          reinterpret_cast<const void*>(tc_linear_kernel<TC_B_NORM>),
+                          reinterpret_cast<const void*>(tc_linear_kernel<TC_B_ATTN>)}) {
+        const cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   static_cast<int>(dyn_limit()));
+        if (e != cudaSuccess) throw std::runtime_error(std::string("tc_linear attribute: ") + cudaGetErrorString(e));
+    }
 }
 
 // ------------------------------------------------------------ tensor maps ---

@@ -55,7 +55,7 @@ class StreamState(C.Structure):
 
 
 PROFILE_KERNELS = {"dit_gateup": 0, "dit_down": 1, "dit_qkv": 2, "base_gateup": 3, "base_down": 4,
-                   "base_qkv": 5, "base_attn": 6}
+                   "base_qkv": 5, "base_attn": 6, "dit_o": 7, "dit_layers": 8}
 
 
 PROGRESS_FN = C.CFUNCTYPE(C.c_int32, C.c_void_p, C.c_int32, C.c_int32)
@@ -306,7 +306,8 @@ class Stream:
         return out
 
     def profile_kernel(self, kernel: str, iters: int = 50):
-        """(ms per launch, algorithmic bytes per launch) of one hot kernel timed alone."""
+        """(ms per launch, algorithmic bytes per launch) of one hot kernel, timed as
+        'iters' graph-captured launches cycling through the layers."""
         ms = C.c_float()
         nb = C.c_double()
         _check(lib().vxc_profile_kernel(self._h, PROFILE_KERNELS[kernel], iters, C.byref(ms), C.byref(nb)))
