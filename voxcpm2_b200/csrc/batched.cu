@@ -256,28 +256,63 @@ __device__ __forceinline__ void split_store(__half* xb, int ld, int m, int col, 
     xb[static_cast<size_t>(24 + m) * ld + col] = __float2half_rn(v - __half2float(hi));
 }
 
-__global__ void rmsnorm_rows_split_kernel(const float* x, int ldx, const __half* g, float eps, int K,
-                                          __half* xb, StreamCtl* ctl) {
-    __shared__ float red[32];
+// One CTA per token row: RMSNorm (x * rsqrt(mean(x^2) + eps) * g) written as the
+// tensor-core linears' split-fp16 operand. Every thread issues its loads of the
+// row and of g in one batch before any arithmetic (each global round trip costs
+// about a microsecond), then one block reduction.
+constexpr int kNormThreads = 256;
+constexpr int kNormBatch = 4;  // float4 per thread in flight: rows up to 4096 in one batch
+
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_rows_split_kernel(const float* x, int ldx, const __half* g,
+                                                                         float eps, int K, __half* xb,
+                                                                         StreamCtl* ctl) {
+    __shared__ float red[kNormThreads / 32];
     pdl_launch_dependents();
+    const int m = blockIdx.x, tid = threadIdx.x, n4 = K / 4;
+    // g does not depend on the previous kernel
+    uint2 gw[kNormBatch];
+#pragma unroll
+    for (int i = 0; i < kNormBatch; ++i) {
+        const int u = tid + kNormThreads * i;
+        gw[i] = u < n4 ? __ldg(reinterpret_cast<const uint2*>(g) + u) : make_uint2(0u, 0u);
+    }
     pdl_wait();
     if (ctl && ctl->stopped) return;
-    const int m = blockIdx.x;
-    const float* xr = x + static_cast<size_t>(m) * ldx;
+    const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(m) * ldx);
+    float4 v[kNormBatch];
+#pragma unroll
+    for (int i = 0; i < kNormBatch; ++i) {
+        const int u = tid + kNormThreads * i;
+        v[i] = u < n4 ? xr[u] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     float ss = 0.f;
-    for (int k = threadIdx.x; k < K; k += blockDim.x) ss += xr[k] * xr[k];
+#pragma unroll
+    for (int i = 0; i < kNormBatch; ++i) ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
     ss = warp_sum(ss);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
     __syncthreads();
     float t = 0.f;
-    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += red[w];
+#pragma unroll
+    for (int w = 0; w < kNormThreads / 32; ++w) t += red[w];
     const float a = rsqrtf(t / static_cast<float>(K) + eps);
-    for (int k = threadIdx.x; k < K; k += blockDim.x) split_store(xb, K, m, k, xr[k] * a * __half2float(g[k]));
+#pragma unroll
+    for (int i = 0; i < kNormBatch; ++i) {
+        const int u = tid + kNormThreads * i;
+        if (u < n4) {
+            const float2 g01 = __half22float2(*reinterpret_cast<const __half2*>(&gw[i].x));
+            const float2 g23 = __half22float2(*reinterpret_cast<const __half2*>(&gw[i].y));
+            split_store(xb, K, m, 4 * u, v[i].x * a * g01.x);
+            split_store(xb, K, m, 4 * u + 1, v[i].y * a * g01.y);
+            split_store(xb, K, m, 4 * u + 2, v[i].z * a * g23.x);
+            split_store(xb, K, m, 4 * u + 3, v[i].w * a * g23.y);
+        }
+    }
 }
 
 // One CTA per (head, sequence): RoPE on q/k (apply_rotary_pos_emb, rotate_half),
 // scores, softmax and P.V for the sequence's rows (VoxCPM2SDPA without mask or
 // cache, voxcpm2_sdpa.cpp:187-252), written as the o projection's split operand.
+// The q/k/v rows and the RoPE tables arrive in one batch of loads.
 constexpr int kDitMaxSeq = 16;
 __global__ void __launch_bounds__(128) dit_attention_split_kernel(const float* qkv, int seq, int q_heads,
                                                                   int kv_heads, const float* rope_cos,
@@ -285,31 +320,60 @@ __global__ void __launch_bounds__(128) dit_attention_split_kernel(const float* q
                                                                   StreamCtl* ctl) {
     constexpr int D = 64, H = 32;
     __shared__ float qs[kDitMaxSeq][D], ks[kDitMaxSeq][D], vs[kDitMaxSeq][D], ps[kDitMaxSeq][kDitMaxSeq + 1];
+    __shared__ float cs_[kDitMaxSeq][D], sn_[kDitMaxSeq][D];
     pdl_launch_dependents();
+    const int h = blockIdx.x, sq = blockIdx.y, kvh = h / (q_heads / kv_heads), tid = threadIdx.x;
+    const int width = (q_heads + 2 * kv_heads) * D;
+    // RoPE tables first: they do not depend on the previous kernel
+    for (int u = tid; u < seq * 16; u += 128) {
+        const int i = u >> 4, e4 = (u & 15) * 4;
+        *reinterpret_cast<float4*>(&cs_[i][e4]) = __ldg(reinterpret_cast<const float4*>(rope_cos + i * D + e4));
+        *reinterpret_cast<float4*>(&sn_[i][e4]) = __ldg(reinterpret_cast<const float4*>(rope_sin + i * D + e4));
+    }
     pdl_wait();
     if (ctl && ctl->stopped) return;
-    const int h = blockIdx.x, sq = blockIdx.y, kvh = h / (q_heads / kv_heads);
-    const int width = (q_heads + 2 * kv_heads) * D;
-    for (int idx = threadIdx.x; idx < seq * D; idx += blockDim.x) {
-        const int i = idx / D, e = idx - i * D;
-        const float* row = qkv + static_cast<size_t>(sq * seq + i) * width;
-        const float c = rope_cos[i * D + e], sn = rope_sin[i * D + e];
-        const float* qp = row + h * D;
-        const float* kp = row + (q_heads + kvh) * D;
-        qs[i][e] = e < H ? qp[e] * c + (-qp[e + H]) * sn : qp[e] * c + qp[e - H] * sn;
-        ks[i][e] = e < H ? kp[e] * c + (-kp[e + H]) * sn : kp[e] * c + kp[e - H] * sn;
-        vs[i][e] = row[(q_heads + kv_heads + kvh) * D + e];
+    {
+        constexpr int kB = 7;  // seq * 48 float4 (<= 768) over 128 threads
+        const int total = seq * 48;
+        float4 v[kB];
+#pragma unroll
+        for (int i = 0; i < kB; ++i) {
+            const int u = tid + 128 * i;
+            if (u < total) {
+                const int r = u / 48, w = u - r * 48, kind = w >> 4, e4 = (w & 15) * 4;
+                const int col = kind == 0 ? h * D : kind == 1 ? (q_heads + kvh) * D : (q_heads + kv_heads + kvh) * D;
+                v[i] = *reinterpret_cast<const float4*>(qkv + static_cast<size_t>(sq * seq + r) * width + col + e4);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < kB; ++i) {
+            const int u = tid + 128 * i;
+            if (u < total) {
+                const int r = u / 48, w = u - r * 48, kind = w >> 4, e4 = (w & 15) * 4;
+                float* dst = kind == 0 ? &qs[r][e4] : kind == 1 ? &ks[r][e4] : &vs[r][e4];
+                *reinterpret_cast<float4*>(dst) = v[i];
+            }
+        }
     }
     __syncthreads();
-    for (int idx = threadIdx.x; idx < seq * seq; idx += blockDim.x) {
+    // rotate_half RoPE in place: each unit owns the pair (e, e + 32) of a q or k row
+    for (int u = tid; u < 2 * seq * H; u += 128) {
+        const int which = u / (seq * H), r = u - which * seq * H, i = r / H, e = r - i * H;
+        float* row = which == 0 ? qs[i] : ks[i];
+        const float v1 = row[e], v2 = row[e + H];
+        row[e] = v1 * cs_[i][e] + (-v2) * sn_[i][e];
+        row[e + H] = v2 * cs_[i][e + H] + v1 * sn_[i][e + H];
+    }
+    __syncthreads();
+    for (int idx = tid; idx < seq * seq; idx += 128) {
         const int i = idx / seq, j = idx - i * seq;
         float sum = 0.f;
         for (int e = 0; e < D; ++e) sum = fmaf(qs[i][e], ks[j][e], sum);
         ps[i][j] = sum * scale;
     }
     __syncthreads();
-    if (threadIdx.x < seq) {
-        const int i = threadIdx.x;
+    if (tid < seq) {
+        const int i = tid;
         float mx = -FLT_MAX;
         for (int j = 0; j < seq; ++j) mx = fmaxf(mx, ps[i][j]);
         float sum = 0.f;
@@ -321,7 +385,7 @@ __global__ void __launch_bounds__(128) dit_attention_split_kernel(const float* q
     }
     __syncthreads();
     const int ld = q_heads * D;
-    for (int idx = threadIdx.x; idx < seq * D; idx += blockDim.x) {
+    for (int idx = tid; idx < seq * D; idx += 128) {
         const int i = idx / D, e = idx - i * D;
         float acc = 0.f;
         for (int j = 0; j < seq; ++j) acc = fmaf(ps[i][j], vs[j][e], acc);
@@ -730,15 +794,21 @@ void launch_dit_attention(const float* qkv, int nseq, int seq, int q_heads, int 
 void launch_rmsnorm_rows_split(const float* x, int ldx, const __half* g, float eps, int K, int M, __half* xb,
                                StreamCtl* ctl, cudaStream_t s, bool pdl) {
     if (M > 24) throw std::invalid_argument("rmsnorm_split: at most 24 rows");
+    if (K % 4 != 0 || K > 4 * kNormThreads * kNormBatch || ldx % 4 != 0 || (reinterpret_cast<uintptr_t>(x) & 15) ||
+        (reinterpret_cast<uintptr_t>(g) & 7))
+        throw std::invalid_argument("rmsnorm_split: row length or alignment unsupported");
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = make_cfg(dim3(M), dim3(256), 0, s, pdl, attr);
+    cudaLaunchConfig_t cfg = make_cfg(dim3(M), dim3(kNormThreads), 0, s, pdl, attr);
     check_launch(cudaLaunchKernelEx(&cfg, rmsnorm_rows_split_kernel, x, ldx, g, eps, K, xb, ctl));
 }
 
 void launch_dit_attention_split(const float* qkv, int nseq, int seq, int q_heads, int kv_heads, int d,
                                 const float* rope_cos, const float* rope_sin, float scale, __half* xb,
                                 StreamCtl* ctl, cudaStream_t s, bool pdl) {
-    if (d != 64 || seq > kDitMaxSeq || nseq * seq > 24) throw std::invalid_argument("dit attention: unsupported shape");
+    if (d != 64 || seq > kDitMaxSeq || seq * 48 > 128 * 7 || nseq * seq > 24 ||
+        (reinterpret_cast<uintptr_t>(qkv) & 15) || (reinterpret_cast<uintptr_t>(rope_cos) & 15) ||
+        (reinterpret_cast<uintptr_t>(rope_sin) & 15))
+        throw std::invalid_argument("dit attention: unsupported shape");
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = make_cfg(dim3(q_heads, nseq), dim3(128), 0, s, pdl, attr);
     check_launch(cudaLaunchKernelEx(&cfg, dit_attention_split_kernel, qkv, seq, q_heads, kv_heads, rope_cos, rope_sin,

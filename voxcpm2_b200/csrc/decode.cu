@@ -231,52 +231,37 @@ __device__ __forceinline__ void load4<__half>(const __half* p, int c, float* r) 
 constexpr int kKeyTile = 32;
 constexpr int kRowPad = 65;  // padded shared-memory row: conflict-free column reads
 
+// Shared memory of one split's pass over its keys.
+struct AttnSmem {
+    float qs[kMaxGroup][kRowPad];
+    float ks[kKeyTile][kRowPad];
+    float vs[kKeyTile][64];
+    float sc[kMaxGroup][kKeyTile];
+    float m_s[kMaxGroup], l_s[kMaxGroup], alpha_s[kMaxGroup];
+};
+
+// Keys [t0, t0 + n) of KV head kvh against the group's G query heads: tiles of
+// kKeyTile rows staged by one batch of loads, online softmax per head. On
+// return S.m_s / S.l_s hold the running max and sum, acc[j] the P.V partial of
+// head g_lo + j at column e = tid % 64 (heads split between the two halves of
+// the block).
 template <typename KV, int D>
-__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArgs a) {
-    static_assert(D == 64, "head_dim 64");
-    __shared__ float qs[kMaxGroup][kRowPad];
-    __shared__ float ks[kKeyTile][kRowPad];
-    __shared__ float vs[kKeyTile][D];
-    __shared__ float sc[kMaxGroup][kKeyTile];
-    __shared__ float m_s[kMaxGroup], l_s[kMaxGroup], alpha_s[kMaxGroup];
-    __shared__ int s_last;
-    extern __shared__ float ps[];  // combine staging: [splits][G][D + 2]
-    pdl_launch_dependents();
-    pdl_wait();
-    if (a.skip_if_stopped && a.ctl && a.ctl->stopped) return;
-
-    const int G = a.q_heads / a.kv_heads;
-    const int split = blockIdx.x, kvh = blockIdx.y;
+__device__ __forceinline__ void attend_keys(const AttnArgs& a, AttnSmem& S, int kvh, int G, int t0, int n, int len0,
+                                            float* acc) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    int len0 = a.len0, len1 = a.len1;
-    if (a.ctl) {
-        len0 = min(a.ctl->kv_len[a.which] + 1, a.len0);  // len0 holds the capacity here
-        len1 = 0;
-    }
-    const int T = len0 + len1;
-    const int active = max(1, min(a.splits, (T + kMinKeysPerSplit - 1) / kMinKeysPerSplit));
-    if (split >= active) return;
-    const int chunk = (T + active - 1) / active;
-    const int t0 = split * chunk;
-    const int n = max(0, min(T, t0 + chunk) - t0);
-
-    for (int i = tid; i < G * D; i += kAttnThreads) qs[i / D][i % D] = a.q[kvh * G * D + i] * a.scale;
+    for (int i = tid; i < G * D; i += kAttnThreads) S.qs[i / D][i % D] = a.q[kvh * G * D + i] * a.scale;
     if (tid < G) {
-        m_s[tid] = -1e30f;
-        l_s[tid] = 0.f;
+        S.m_s[tid] = -1e30f;
+        S.l_s[tid] = 0.f;
     }
     const KV* k0 = static_cast<const KV*>(a.k0) + static_cast<size_t>(kvh) * a.stride0 * D;
     const KV* v0 = static_cast<const KV*>(a.v0) + static_cast<size_t>(kvh) * a.stride0 * D;
     const KV* k1 = a.k1 ? static_cast<const KV*>(a.k1) + static_cast<size_t>(kvh) * a.stride1 * D : nullptr;
     const KV* v1 = a.v1 ? static_cast<const KV*>(a.v1) + static_cast<size_t>(kvh) * a.stride1 * D : nullptr;
-
-    // P.V ownership: column e, and half of the group's heads
     const int e = tid & (D - 1), gh = tid / D;
     const int hg = (G + 1) / 2, g_lo = gh * hg, g_hi = min(G, g_lo + hg);
-    float acc[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-
     for (int tb = 0; tb < n; tb += kKeyTile) {
         const int nt = min(kKeyTile, n - tb);
         __syncthreads();  // previous tile fully consumed (and q / stats initialised)
@@ -291,8 +276,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
             load4(vp, c, vr);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                ks[r][c + j] = kr[j];
-                vs[r][c + j] = vr[j];
+                S.ks[r][c + j] = kr[j];
+                S.vs[r][c + j] = vr[j];
             }
         }
         __syncthreads();
@@ -300,35 +285,67 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
             const int g = i / nt, t = i - g * nt;
             float s = 0.f;
 #pragma unroll 16
-            for (int c = 0; c < D; ++c) s = fmaf(qs[g][c], ks[t][c], s);
-            sc[g][t] = s + (a.mask ? a.mask[t0 + tb + t] : 0.f);
+            for (int c = 0; c < D; ++c) s = fmaf(S.qs[g][c], S.ks[t][c], s);
+            S.sc[g][t] = s + (a.mask ? a.mask[t0 + tb + t] : 0.f);
         }
         __syncthreads();
         for (int g = warp; g < G; g += kAttnThreads / kWarp) {
-            const float x = lane < nt ? sc[g][lane] : -1e30f;
-            const float m_old = m_s[g];
+            const float x = lane < nt ? S.sc[g][lane] : -1e30f;
+            const float m_old = S.m_s[g];
             const float m_new = fmaxf(m_old, warp_max(x));
             const float p = lane < nt ? __expf(x - m_new) : 0.f;
-            if (lane < nt) sc[g][lane] = p;
+            if (lane < nt) S.sc[g][lane] = p;
             const float psum = warp_sum(p);
             if (lane == 0) {
                 const float alpha = __expf(m_old - m_new);
-                alpha_s[g] = alpha;
-                l_s[g] = l_s[g] * alpha + psum;
-                m_s[g] = m_new;
+                S.alpha_s[g] = alpha;
+                S.l_s[g] = S.l_s[g] * alpha + psum;
+                S.m_s[g] = m_new;
             }
         }
         __syncthreads();
 #pragma unroll
         for (int j = 0; j < 8; ++j)
-            if (g_lo + j < g_hi) acc[j] *= alpha_s[g_lo + j];
+            if (g_lo + j < g_hi) acc[j] *= S.alpha_s[g_lo + j];
         for (int t = 0; t < nt; ++t) {
-            const float v = vs[t][e];
+            const float v = S.vs[t][e];
 #pragma unroll
             for (int j = 0; j < 8; ++j)
-                if (g_lo + j < g_hi) acc[j] = fmaf(sc[g_lo + j][t], v, acc[j]);
+                if (g_lo + j < g_hi) acc[j] = fmaf(S.sc[g_lo + j][t], v, acc[j]);
         }
     }
+}
+
+template <typename KV, int D>
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArgs a) {
+    static_assert(D == 64, "head_dim 64");
+    __shared__ AttnSmem S;
+    __shared__ int s_last;
+    extern __shared__ float ps[];  // combine staging: [splits][G][D + 2]
+    pdl_launch_dependents();
+    pdl_wait();
+    if (a.skip_if_stopped && a.ctl && a.ctl->stopped) return;
+
+    const int G = a.q_heads / a.kv_heads;
+    const int split = blockIdx.x, kvh = blockIdx.y;
+    const int tid = threadIdx.x;
+    int len0 = a.len0, len1 = a.len1;
+    if (a.ctl) {
+        len0 = min(a.ctl->kv_len[a.which] + 1, a.len0);  // len0 holds the capacity here
+        len1 = 0;
+    }
+    const int T = len0 + len1;
+    const int active = max(1, min(a.splits, (T + kMinKeysPerSplit - 1) / kMinKeysPerSplit));
+    if (split >= active) return;
+    const int chunk = (T + active - 1) / active;
+    const int t0 = split * chunk;
+    const int n = max(0, min(T, t0 + chunk) - t0);
+    const int e = tid & (D - 1), gh = tid / D;
+    const int hg = (G + 1) / 2, g_lo = gh * hg, g_hi = min(G, g_lo + hg);
+    float acc[8];
+    attend_keys<KV, D>(a, S, kvh, G, t0, n, len0, acc);
+    float* m_s = S.m_s;
+    float* l_s = S.l_s;
     __syncthreads();
     // this split's partial (m, l, P.V) per head
     float* part = a.partial + (static_cast<size_t>(kvh) * a.splits + split) * G * (D + 2);
@@ -416,6 +433,107 @@ void launch_gemv(const GemvArgs& a, cudaStream_t s, bool pdl) {
             break;
         default: throw std::invalid_argument("gemv: unknown mode");
     }
+}
+
+// The same decode with the split-K combine inside a thread-block cluster: the
+// cluster's CTAs take one contiguous key range each, publish (max, sum, P.V) in
+// their own shared memory, and after one cluster barrier CTA r combines heads
+// g = r, r + C, ... reading the others' partials through distributed shared
+// memory. A second barrier keeps every CTA's shared memory alive until the
+// readers are done. No global scratch, no atomics.
+constexpr int kAttnCluster = 8;
+
+__device__ __forceinline__ float ld_peer(const float* local, uint32_t rank) {
+    uint32_t addr;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+                 : "=r"(addr)
+                 : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(local))), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ void cluster_barrier() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+template <typename KV, int D>
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_cluster_kernel(const AttnArgs a) {
+    static_assert(D == 64, "head_dim 64");
+    __shared__ AttnSmem S;
+    __shared__ float pacc[kMaxGroup][D], pm[kMaxGroup], pl[kMaxGroup];
+    pdl_launch_dependents();
+    pdl_wait();
+    // uniform over the grid: the flag cannot change while the kernel runs
+    if (a.skip_if_stopped && a.ctl && a.ctl->stopped) return;
+    const int G = a.q_heads / a.kv_heads, C = kAttnCluster;
+    const int rank = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x;
+    int len0 = a.len0, len1 = a.len1;
+    if (a.ctl) {
+        len0 = min(a.ctl->kv_len[a.which] + 1, a.len0);  // len0 holds the capacity here
+        len1 = 0;
+    }
+    const int T = len0 + len1;
+    const int chunk = (T + C - 1) / C, t0 = rank * chunk, n = max(0, min(T, t0 + chunk) - t0);
+    const int e = tid & (D - 1), gh = tid / D;
+    const int hg = (G + 1) / 2, g_lo = gh * hg, g_hi = min(G, g_lo + hg);
+    float acc[8];
+    attend_keys<KV, D>(a, S, kvh, G, t0, n, len0, acc);
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        if (g_lo + j < g_hi) pacc[g_lo + j][e] = acc[j];
+    if (tid < G) {
+        pm[tid] = n > 0 ? S.m_s[tid] : -1e30f;
+        pl[tid] = S.l_s[tid];
+    }
+    cluster_barrier();  // every CTA's partial is visible cluster-wide
+    for (int g = rank; g < G; g += C) {
+        if (tid < D) {
+            float mr[kAttnCluster], lr[kAttnCluster], ar[kAttnCluster];
+#pragma unroll
+            for (int r = 0; r < kAttnCluster; ++r) {
+                mr[r] = ld_peer(&pm[g], r);
+                lr[r] = ld_peer(&pl[g], r);
+                ar[r] = ld_peer(&pacc[g][tid], r);
+            }
+            float M = -1e30f;
+#pragma unroll
+            for (int r = 0; r < kAttnCluster; ++r) M = fmaxf(M, mr[r]);
+            float num = 0.f, den = 0.f;
+#pragma unroll
+            for (int r = 0; r < kAttnCluster; ++r) {
+                const float w = __expf(mr[r] - M);
+                num = fmaf(w, ar[r], num);
+                den = fmaf(w, lr[r], den);
+            }
+            a.out[(kvh * G + g) * D + tid] = num / den;
+        }
+    }
+    cluster_barrier();  // no CTA leaves while another still reads its shared memory
+}
+
+void launch_attn_decode_cluster(const AttnArgs& a, cudaStream_t s, bool pdl) {
+    if (a.head_dim != 64) throw std::invalid_argument("attention: head_dim must be 64");
+    if (a.kv_heads <= 0 || a.q_heads % a.kv_heads != 0) throw std::invalid_argument("attention: bad head grouping");
+    const int G = a.q_heads / a.kv_heads;
+    if (G < 1 || G > kMaxGroup) throw std::invalid_argument("attention: more than 16 query heads per KV head");
+    for (const void* p : {a.k0, a.v0, a.k1, a.v1})
+        if (reinterpret_cast<uintptr_t>(p) % 16 != 0)
+            throw std::invalid_argument("attention: key/value rows must start on 16-byte boundaries");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kAttnCluster, a.kv_heads);
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kAttnCluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
+    check_launch(cudaLaunchKernelEx(&cfg, attn_decode_cluster_kernel<float, 64>, a));
 }
 
 void launch_attn_decode(const AttnArgs& a, bool fp16_kv, cudaStream_t s, bool pdl) {

@@ -83,6 +83,9 @@ struct AttnArgs {
     int skip_if_stopped = 0;
 };
 void launch_attn_decode(const AttnArgs& a, bool fp16_kv, cudaStream_t s, bool pdl);
+// The same (fp32 KV) with the split-K combine inside one 8-CTA cluster per KV head
+// (distributed shared memory; no scratch, no atomics). Ignores splits/partial/counters.
+void launch_attn_decode_cluster(const AttnArgs& a, cudaStream_t s, bool pdl);
 
 // final RMSNorm of a decoder step: out = norm(h) * g; optionally bump kv_len.
 void launch_final_norm(const float* h, const __half* g, float eps, int H, float* out, float* out2,

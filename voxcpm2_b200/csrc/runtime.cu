@@ -356,6 +356,10 @@ struct vxc_stream {
     // ring depth of the per-layer tensor-core launches (VXC_TC_STAGES): a shallow ring keeps a
     // CTA's shared memory small, so linears of several concurrent streams share an SM
     int tc_stages = 2;
+    // CTAs a per-layer tensor-core launch aims at (VXC_TC_TARGET): 32 by default, so most
+    // linears run without a K split (no cluster exchange) and concurrent streams share the SMs;
+    // 148 (one per SM) trades ~45% of the multi-stream throughput for ~8% lower single-stream latency
+    int tc_target = 32;
     // programmatic dependent launch between the patch graph's kernels (VXC_NO_PDL=1 turns it off)
     bool pdl = true;
     float* dpart = nullptr;     // persistent launch: partial tiles
@@ -467,7 +471,7 @@ void enqueue_decoder_step(vxc_stream* s, int which, float* out, float* out2, int
         aa.ctl = s->ctl;
         aa.which = which;
         aa.skip_if_stopped = skip;
-        launch_attn_decode(aa, false, s->cs, s->pdl);
+        launch_attn_decode_cluster(aa, s->cs, s->pdl);
 
         GemvArgs oa;
         oa.mode = GEMV_RESID;
@@ -509,10 +513,12 @@ void enqueue_decoder_step(vxc_stream* s, int which, float* out, float* out2, int
     launch_final_norm(s->h[which], fnorm, d.rms_eps, H, out, out2, s->ctl, which, 1, skip, s->cs, s->pdl);
 }
 
-// K split (cluster size) of a tensor-core linear: about one CTA per SM overall.
-int choose_splits(int tiles, int k) {
+// K split (cluster size) of a tensor-core linear: about 'target' CTAs per launch
+// (one per SM for a single stream; fewer when many streams share the GPU, which
+// saves each CTA's fixed setup and split-K exchange).
+int choose_splits(int tiles, int k, int target = 148) {
     const int chunks = k / 64;
-    const int want = std::max(1, (148 + tiles / 2) / tiles);
+    const int want = std::max(1, (target + tiles / 2) / tiles);
     return std::max(1, std::min({8, chunks, want}));
 }
 
@@ -521,7 +527,7 @@ int choose_splits(int tiles, int k) {
 TcLinearArgs tc_plan(const vxc_stream* s, int tiles, int K, bool fused_b) {
     TcLinearArgs a;
     const int nch = K / 64;
-    a.splits = choose_splits(tiles, K);
+    a.splits = choose_splits(tiles, K, s->tc_target);
     a.max_stages = s->tc_stages;
     if (fused_b) a.splits = std::min(std::min(8, nch), std::max(a.splits, (nch + a.max_stages - 1) / a.max_stages));
     return a;
@@ -1292,6 +1298,10 @@ VXC_API int32_t vxc_stream_create(vxc_device* dev, int32_t kv_capacity, vxc_stre
         // VXC_DIT_FORM=persistent|fused|split picks one explicitly (an unsupported choice is an error)
         s->dit_grid = dit_layers_grid();
         if (const char* np = std::getenv("VXC_NO_PDL")) s->pdl = std::string(np) != "1";
+        if (const char* tt = std::getenv("VXC_TC_TARGET")) {
+            s->tc_target = std::atoi(tt);
+            if (s->tc_target < 1 || s->tc_target > 4096) throw std::invalid_argument("VXC_TC_TARGET must be in [1, 4096]");
+        }
         if (const char* st = std::getenv("VXC_TC_STAGES")) {
             s->tc_stages = std::atoi(st);
             if (s->tc_stages < 1 || s->tc_stages > 8) throw std::invalid_argument("VXC_TC_STAGES must be in [1, 8]");
@@ -2009,7 +2019,7 @@ VXC_API int32_t vxc_profile_kernel(vxc_stream* s, int32_t kernel, int32_t iters,
                     a.splits = s->splits; a.partial = s->partial; a.counters = s->counters; a.out = s->attn;
                     a.ctl = pctl; a.which = 0;
                     bytes = 4.0 * 2 * hkv * static_cast<double>(T) * hd + 8.0 * hq * hd;
-                    launch.push_back([=](bool pdl) { launch_attn_decode(a, false, s->cs, pdl); });
+                    launch.push_back([=](bool pdl) { launch_attn_decode_cluster(a, s->cs, pdl); });
                     break;
                 }
             }
