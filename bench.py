@@ -61,6 +61,18 @@ def workload(streams_per_gpu: int, steps: int, warmup: int):
     }, min_patches
 
 
+def profiled_traffic(name: str):
+    """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from the
+    committed ncu summary profiles/<name>.md, or None."""
+    f = ROOT / "profiles" / f"{name}.md"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.startswith("dram_bytes_per_launch:"):
+            return float(line.split(":", 1)[1])
+    return None
+
+
 def patch_bytes(cfg, kv_tokens: float) -> float:
     """Algorithmic HBM bytes of one patch: every weight the patch reads once (fp16:
     one base and one residual decoder step, 9 DiT estimator evaluations without the
@@ -292,9 +304,11 @@ def run_ours(args):
     try:  # the persistent DiT decoder when the stream runs that form (all 12 layers per launch)
         prof_ms, prof_bytes = streams[0].profile_kernel("dit_layers", 20)
         kname = "dit_layers_kernel (persistent DiT decoder, 12 layers, tcgen05 + TMA, one launch per evaluation)"
+        traffic = None
     except rt.VxcError:  # the default form: per-layer tcgen05 linears
         prof_ms, prof_bytes = streams[0].profile_kernel("dit_gateup", 100)
         kname = "tc_linear_kernel gate/up (DiT, tcgen05 + TMA, 2x11 tokens, SiLU*up epilogue)"
+        traffic = profiled_traffic("tc_linear_gateup_dit")
     achieved = prof_bytes / (prof_ms / 1e3) / 1e9
     # whole job: algorithmic bytes of all patches / the timed region (all streams together)
     bpp = patch_bytes(cfg, TEXT_TOKENS + 1 + W + K / 2)
@@ -303,7 +317,9 @@ def run_ours(args):
     roofline = {"kernel": kname, "bound": "hbm",
                 "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                 "peak_kind": f"{peak_kind} burst copy bandwidth", "bytes_per_launch": prof_bytes,
-                "us_per_launch": 1e3 * prof_ms, "traffic": None}
+                "us_per_launch": 1e3 * prof_ms, "traffic": traffic,
+                "traffic_source": "profiles/tc_linear_gateup_dit.md (ncu dram__bytes_read.sum + write, one launch)"
+                if traffic else None}
     kernels = {}
     for k in ("dit_qkv", "dit_o", "dit_down", "base_qkv", "base_attn", "base_gateup", "base_down"):
         km, kb = streams[0].profile_kernel(k, 50)

@@ -319,7 +319,8 @@ __global__ void __launch_bounds__(128) dit_attention_split_kernel(const float* q
                                                                   const float* rope_sin, float scale, __half* xb,
                                                                   StreamCtl* ctl) {
     constexpr int D = 64, H = 32;
-    __shared__ float qs[kDitMaxSeq][D], ks[kDitMaxSeq][D], vs[kDitMaxSeq][D], ps[kDitMaxSeq][kDitMaxSeq + 1];
+    // q and k rows padded to 65 floats: the score loop reads 11 different rows per warp
+    __shared__ float qs[kDitMaxSeq][D + 1], ks[kDitMaxSeq][D + 1], vs[kDitMaxSeq][D], ps[kDitMaxSeq][kDitMaxSeq + 1];
     __shared__ float cs_[kDitMaxSeq][D], sn_[kDitMaxSeq][D];
     pdl_launch_dependents();
     const int h = blockIdx.x, sq = blockIdx.y, kvh = h / (q_heads / kv_heads), tid = threadIdx.x;
@@ -351,7 +352,10 @@ __global__ void __launch_bounds__(128) dit_attention_split_kernel(const float* q
             if (u < total) {
                 const int r = u / 48, w = u - r * 48, kind = w >> 4, e4 = (w & 15) * 4;
                 float* dst = kind == 0 ? &qs[r][e4] : kind == 1 ? &ks[r][e4] : &vs[r][e4];
-                *reinterpret_cast<float4*>(dst) = v[i];
+                dst[0] = v[i].x;
+                dst[1] = v[i].y;
+                dst[2] = v[i].z;
+                dst[3] = v[i].w;
             }
         }
     }
