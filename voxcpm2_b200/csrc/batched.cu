@@ -132,7 +132,7 @@ __global__ void rmsnorm_rows_kernel(const float* x, int ldx, const __half* g, fl
     __syncthreads();
     float t = 0.f;
     for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += red[w];
-    const float a = rsqrtf(t / static_cast<float>(K) + eps);
+    const float a = g ? rsqrtf(t / static_cast<float>(K) + eps) : 1.f;
     float* orow = out + static_cast<size_t>(blockIdx.x) * ldo;
     for (int k = threadIdx.x; k < K; k += blockDim.x) orow[k] = xr[k] * a * __half2float(g[k]);
 }
@@ -250,10 +250,11 @@ __global__ void attn_rows_kernel(const float* qkv, int q_heads, int kv_heads, in
     }
 }
 
-__device__ __forceinline__ void split_store(__half* xb, int ld, int m, int col, float v) {
+// split-fp16 operand row m: fp16(v) in row m, fp16(v - fp16(v)) in row lo + m
+__device__ __forceinline__ void split_store(__half* xb, int ld, int m, int col, float v, int lo = 24) {
     const __half hi = __float2half_rn(v);
     xb[static_cast<size_t>(m) * ld + col] = hi;
-    xb[static_cast<size_t>(24 + m) * ld + col] = __float2half_rn(v - __half2float(hi));
+    xb[static_cast<size_t>(lo + m) * ld + col] = __float2half_rn(v - __half2float(hi));
 }
 
 // One CTA per token row: RMSNorm (x * rsqrt(mean(x^2) + eps) * g) written as the
@@ -263,9 +264,10 @@ __device__ __forceinline__ void split_store(__half* xb, int ld, int m, int col, 
 constexpr int kNormThreads = 256;
 constexpr int kNormBatch = 4;  // float4 per thread in flight: rows up to 4096 in one batch
 
+// g == nullptr: no normalisation (a plain split of the rows); lo: row offset of the residual half
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_rows_split_kernel(const float* x, int ldx, const __half* g,
                                                                          float eps, int K, __half* xb,
-                                                                         StreamCtl* ctl) {
+                                                                         StreamCtl* ctl, int lo) {
     __shared__ float red[kNormThreads / 32];
     pdl_launch_dependents();
     const int m = blockIdx.x, tid = threadIdx.x, n4 = K / 4;
@@ -274,7 +276,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_rows_split_kernel(const 
 #pragma unroll
     for (int i = 0; i < kNormBatch; ++i) {
         const int u = tid + kNormThreads * i;
-        gw[i] = u < n4 ? __ldg(reinterpret_cast<const uint2*>(g) + u) : make_uint2(0u, 0u);
+        gw[i] = u < n4 && g ? __ldg(reinterpret_cast<const uint2*>(g) + u) : make_uint2(0x3c003c00u, 0x3c003c00u);
     }
     pdl_wait();
     if (ctl && ctl->stopped) return;
@@ -294,17 +296,17 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_rows_split_kernel(const 
     float t = 0.f;
 #pragma unroll
     for (int w = 0; w < kNormThreads / 32; ++w) t += red[w];
-    const float a = rsqrtf(t / static_cast<float>(K) + eps);
+    const float a = g ? rsqrtf(t / static_cast<float>(K) + eps) : 1.f;
 #pragma unroll
     for (int i = 0; i < kNormBatch; ++i) {
         const int u = tid + kNormThreads * i;
         if (u < n4) {
             const float2 g01 = __half22float2(*reinterpret_cast<const __half2*>(&gw[i].x));
             const float2 g23 = __half22float2(*reinterpret_cast<const __half2*>(&gw[i].y));
-            split_store(xb, K, m, 4 * u, v[i].x * a * g01.x);
-            split_store(xb, K, m, 4 * u + 1, v[i].y * a * g01.y);
-            split_store(xb, K, m, 4 * u + 2, v[i].z * a * g23.x);
-            split_store(xb, K, m, 4 * u + 3, v[i].w * a * g23.y);
+            split_store(xb, K, m, 4 * u, v[i].x * a * g01.x, lo);
+            split_store(xb, K, m, 4 * u + 1, v[i].y * a * g01.y, lo);
+            split_store(xb, K, m, 4 * u + 2, v[i].z * a * g23.x, lo);
+            split_store(xb, K, m, 4 * u + 3, v[i].w * a * g23.y, lo);
         }
     }
 }
@@ -796,14 +798,14 @@ void launch_dit_attention(const float* qkv, int nseq, int seq, int q_heads, int 
 }
 
 void launch_rmsnorm_rows_split(const float* x, int ldx, const __half* g, float eps, int K, int M, __half* xb,
-                               StreamCtl* ctl, cudaStream_t s, bool pdl) {
-    if (M > 24) throw std::invalid_argument("rmsnorm_split: at most 24 rows");
+                               StreamCtl* ctl, cudaStream_t s, bool pdl, int lo) {
+    if (M > lo) throw std::invalid_argument("rmsnorm_split: more rows than the operand's row block");
     if (K % 4 != 0 || K > 4 * kNormThreads * kNormBatch || ldx % 4 != 0 || (reinterpret_cast<uintptr_t>(x) & 15) ||
         (reinterpret_cast<uintptr_t>(g) & 7))
         throw std::invalid_argument("rmsnorm_split: row length or alignment unsupported");
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = make_cfg(dim3(M), dim3(kNormThreads), 0, s, pdl, attr);
-    check_launch(cudaLaunchKernelEx(&cfg, rmsnorm_rows_split_kernel, x, ldx, g, eps, K, xb, ctl));
+    check_launch(cudaLaunchKernelEx(&cfg, rmsnorm_rows_split_kernel, x, ldx, g, eps, K, xb, ctl, lo));
 }
 
 void launch_dit_attention_split(const float* qkv, int nseq, int seq, int q_heads, int kv_heads, int d,

@@ -138,8 +138,11 @@ void launch_dit_attention(const float* qkv, int nseq, int seq, int q_heads, int 
 // DiT, tensor-core operand producers. Both write the next tcgen05 linear's B
 // operand: split fp16 rows [48][ld] (row m = fp16(v), row 24 + m = fp16(v - fp16(v))).
 // RMSNorm of the M residual rows:
+// RMSNorm of M rows (g == nullptr: no normalisation) into a split-fp16 operand:
+// fp16(v) in row m, fp16(v - fp16(v)) in row lo + m (lo = 24 for the DiT linears,
+// kRowBlock for the prefill's row-block linears)
 void launch_rmsnorm_rows_split(const float* x, int ldx, const __half* g, float eps, int K, int M, __half* xb,
-                               StreamCtl* ctl, cudaStream_t s, bool pdl);
+                               StreamCtl* ctl, cudaStream_t s, bool pdl, int lo = 24);
 // RoPE (positions 0..seq-1) + full attention within each sequence, one CTA per
 // (head, sequence), from the fp32 q/k/v rows [nseq*seq][(hq+2hkv)d]:
 void launch_dit_attention_split(const float* qkv, int nseq, int seq, int q_heads, int kv_heads, int d,
@@ -268,6 +271,26 @@ int tc_attn_round(int K, int splits, int max_stages = 8);
 void launch_tc_linear(const CUtensorMap& map_a, const CUtensorMap& map_b, const TcLinearArgs& a, cudaStream_t s,
                       bool pdl);
 void init_tc_attributes();
+
+// Row-block tcgen05 linear (prefill): Y[m][r] for m < M <= kRowBlock rows, one
+// CTA per 128-feature tile (gate/up: 64 gate + 64 up rows), no K split
+// (tc_rows.cu). The token operand is split fp16 [2 * kRowBlock][K] (map_b, box
+// rows 2 * kRowBlock): fp16(x) in rows 0.., the residuals in rows kRowBlock...
+constexpr int kRowBlock = 128;
+struct TcRowsArgs {
+    int K = 0, M = 0, rows = 0;
+    int gateup = 0;            // out = SiLU(gate) * up, as split fp16 into yb [2 * kRowBlock][ldyb]
+    int resid = 0;             // y += rscale * out (else y = out)
+    float rscale = 1.f;
+    float* y = nullptr;        // fp32 [M][ldy]
+    int ldy = 0;
+    __half* yb = nullptr;
+    int ldyb = 0;
+    int stages = 4;            // shared-memory ring depth (1..4)
+    StreamCtl* ctl = nullptr;  // receives error 3 if a bounded wait gave up
+};
+void launch_tc_rows(const CUtensorMap& map_a, const CUtensorMap& map_b, const TcRowsArgs& a, cudaStream_t s);
+void init_tc_rows_attributes();
 
 // Persistent DiT decoder (all layers of one estimator evaluation, one
 // cooperative launch, one CTA per SM; dit_persist.cu).

@@ -124,6 +124,17 @@ std::vector<LayerW> carve_decoder(const __half* base, const DecoderShape& s, con
     return out;
 }
 
+// TMA maps (64 x 64 boxes, 128-byte swizzle) of one decoder's per-layer matrices
+std::vector<std::array<CUtensorMap, 4>> decoder_maps(const vxc_model_desc& d, const std::vector<LayerW>& layers) {
+    const int H = d.hidden, F = d.ffn, Q = d.q_heads * d.head_dim;
+    const int W = (d.q_heads + 2 * d.kv_heads) * d.head_dim;
+    std::vector<std::array<CUtensorMap, 4>> maps;
+    for (const LayerW& L : layers)
+        maps.push_back({make_tensor_map_f16(L.wqkv, W, H, 64), make_tensor_map_f16(L.wo, H, Q, 64),
+                        make_tensor_map_f16(L.wgateup, 2 * F, H, 64), make_tensor_map_f16(L.wdown, H, F, 64)});
+    return maps;
+}
+
 DecoderShape base_shape(const vxc_model_desc& d) {
     return {d.hidden, d.ffn, d.q_heads, d.kv_heads, d.head_dim, d.base_layers};
 }
@@ -263,6 +274,8 @@ struct vxc_device {
     float *dit_rope_cos = nullptr, *dit_rope_sin = nullptr;  // positions 0..seq-1
     // per DiT layer: TMA maps of W_qkv, W_o, W_gate|up, W_down (A operands)
     std::vector<std::array<CUtensorMap, 4>> dit_maps;
+    // per decoder layer: TMA maps of W_qkv, W_o, W_gate|up, W_down for the prefill's row-block linears
+    std::vector<std::array<CUtensorMap, 4>> base_maps, res_maps;
     CUtensorMap* dit_maps_dev = nullptr;       // the same maps in device memory (persistent DiT kernel)
     const __half** dit_norms_dev = nullptr;    // [layers][2] input / post-attention RMSNorm weights
     uint64_t epoch = 0;  // bumped by every weight upload (invalidates derived tables)
@@ -331,6 +344,9 @@ struct vxc_stream {
     // prefill buffers (grown on demand)
     int pre_rows = 0;
     float *ph = nullptr, *pxn = nullptr, *pqkv = nullptr, *pattn = nullptr, *pact = nullptr, *pcat = nullptr;
+    // row-block split-fp16 operands of the prefill's tcgen05 linears ([2 * kRowBlock][K]) and their maps
+    __half *xr_n = nullptr, *xr_a = nullptr, *xr_act = nullptr;
+    CUtensorMap map_xr_n{}, map_xr_a{}, map_xr_act{};
     int32_t* pids = nullptr;
 
     // host mirror
@@ -390,6 +406,8 @@ void free_all(vxc_stream* s) {
     if (s->dest) cudaFree(s->dest);
     if (s->dssq) cudaFree(s->dssq);
     if (s->dpart) cudaFree(s->dpart);
+    for (__half* p : {s->xr_n, s->xr_a, s->xr_act})
+        if (p) cudaFree(p);
     if (s->dsync) cudaFree(s->dsync);
     if (s->dcount) cudaFree(s->dcount);
     if (s->ctl_host) cudaFreeHost(s->ctl_host);
@@ -894,73 +912,91 @@ void ensure_prefill_rows(vxc_stream* s, int n) {
     s->pcat = dev_alloc<float>(n * 2 * H);
     s->pids = dev_alloc<int32_t>(n);
     s->pre_rows = n;
+    if (!s->xr_n) {  // row-block operands: one block of kRowBlock rows, reused block after block
+        const size_t Q = static_cast<size_t>(d.q_heads) * d.head_dim;
+        s->xr_n = dev_alloc<__half>(2 * kRowBlock * H);
+        s->xr_a = dev_alloc<__half>(2 * kRowBlock * Q);
+        s->xr_act = dev_alloc<__half>(2 * kRowBlock * F);
+        ck(cudaMemset(s->xr_n, 0, 2 * kRowBlock * H * sizeof(__half)), "cudaMemset");
+        ck(cudaMemset(s->xr_a, 0, 2 * kRowBlock * Q * sizeof(__half)), "cudaMemset");
+        ck(cudaMemset(s->xr_act, 0, 2 * kRowBlock * F * sizeof(__half)), "cudaMemset");
+        s->map_xr_n = make_tensor_map_f16(s->xr_n, 2 * kRowBlock, static_cast<int>(H), 2 * kRowBlock);
+        s->map_xr_a = make_tensor_map_f16(s->xr_a, 2 * kRowBlock, static_cast<int>(Q), 2 * kRowBlock);
+        s->map_xr_act = make_tensor_map_f16(s->xr_act, 2 * kRowBlock, static_cast<int>(F), 2 * kRowBlock);
+    }
 }
 
 // Multi-row decoder call (prefill): rows already in s->ph; out [n][H] device.
+// The four linears of each layer run on tcgen05 over blocks of up to kRowBlock
+// rows (tc_rows_kernel, weights read once per block); RMSNorm, RoPE + cache
+// append and the causal attention run over all rows.
 void run_decoder_rows(vxc_stream* s, int which, int n, float* out_dev) {
     const vxc_device* dev = s->dev;
     const vxc_model_desc& d = dev->desc;
     const std::vector<LayerW>& layers = which == 0 ? dev->base : dev->res;
+    const std::vector<std::array<CUtensorMap, 4>>& maps = which == 0 ? dev->base_maps : dev->res_maps;
     const __half* fnorm = which == 0 ? dev->base_norm : dev->res_norm;
     const float rscale = which == 0 ? d.base_residual_scale : d.res_residual_scale;
-    const int H = d.hidden, F = d.ffn, hq = d.q_heads, hkv = d.kv_heads, hd = d.head_dim;
+    const int H = d.hidden, F = d.ffn, hq = d.q_heads, hkv = d.kv_heads, hd = d.head_dim, Q = hq * hd;
     const int W = (hq + 2 * hkv) * hd;
     const int past = s->kv_len[which];
     const size_t plane = static_cast<size_t>(hkv) * s->cap * hd;
     for (size_t l = 0; l < layers.size(); ++l) {
         const LayerW& L = layers[l];
-        launch_rmsnorm_rows(s->ph, H, L.in_norm, d.rms_eps, H, n, s->pxn, H, nullptr, 0, s->cs, false);
-        RowsArgs qa;
-        qa.w = L.wqkv;
-        qa.x = s->pxn;
-        qa.ldx = H;
-        qa.K = H;
-        qa.rows = W;
-        qa.M = n;
-        qa.y = s->pqkv;
-        qa.ldy = W;
-        launch_rows_linear(qa, s->cs, false);
+        for (int r0 = 0; r0 < n; r0 += kRowBlock) {
+            const int mb = std::min(kRowBlock, n - r0);
+            launch_rmsnorm_rows_split(s->ph + static_cast<size_t>(r0) * H, H, L.in_norm, d.rms_eps, H, mb, s->xr_n,
+                                      nullptr, s->cs, false, kRowBlock);
+            TcRowsArgs qa;
+            qa.K = H;
+            qa.M = mb;
+            qa.rows = W;
+            qa.y = s->pqkv + static_cast<size_t>(r0) * W;
+            qa.ldy = W;
+            qa.ctl = s->ctl;
+            launch_tc_rows(maps[l][0], s->map_xr_n, qa, s->cs);
+        }
         launch_qkv_rows_post(s->pqkv, n, hq, hkv, hd, past, 1 << 30, which == 0 ? s->rope_cos : nullptr,
                              which == 0 ? s->rope_sin : nullptr, s->kc[which] + l * plane, s->vc[which] + l * plane,
                              s->cap, s->ctl, s->cs, false);
         launch_attn_rows_cache(s->pqkv, n, hq, hkv, hd, past, s->kc[which] + l * plane, s->vc[which] + l * plane,
                                s->cap, 1.0f / std::sqrt(static_cast<float>(hd)), s->pattn, s->cs, false);
-        RowsArgs oa;
-        oa.w = L.wo;
-        oa.x = s->pattn;
-        oa.ldx = hq * hd;
-        oa.K = hq * hd;
-        oa.rows = H;
-        oa.M = n;
-        oa.mode = GEMV_RESID;
-        oa.rscale = rscale;
-        oa.y = s->ph;
-        oa.ldy = H;
-        launch_rows_linear(oa, s->cs, false);
-        launch_rmsnorm_rows(s->ph, H, L.post_norm, d.rms_eps, H, n, s->pxn, H, nullptr, 0, s->cs, false);
-        RowsArgs ga;
-        ga.w = L.wgateup;
-        ga.x = s->pxn;
-        ga.ldx = H;
-        ga.K = H;
-        ga.rows = F;
-        ga.M = n;
-        ga.mode = GEMV_GATEUP;
-        ga.y = s->pact;
-        ga.ldy = F;
-        launch_rows_linear(ga, s->cs, false);
-        RowsArgs da;
-        da.w = L.wdown;
-        da.x = s->pact;
-        da.ldx = F;
-        da.K = F;
-        da.rows = H;
-        da.M = n;
-        da.mode = GEMV_RESID;
-        da.rscale = rscale;
-        da.y = s->ph;
-        da.ldy = H;
-        launch_rows_linear(da, s->cs, false);
+        for (int r0 = 0; r0 < n; r0 += kRowBlock) {
+            const int mb = std::min(kRowBlock, n - r0);
+            float* hb = s->ph + static_cast<size_t>(r0) * H;
+            launch_rmsnorm_rows_split(s->pattn + static_cast<size_t>(r0) * Q, Q, nullptr, 0.f, Q, mb, s->xr_a, nullptr,
+                                      s->cs, false, kRowBlock);
+            TcRowsArgs oa;
+            oa.K = Q;
+            oa.M = mb;
+            oa.rows = H;
+            oa.resid = 1;
+            oa.rscale = rscale;
+            oa.y = hb;
+            oa.ldy = H;
+            oa.ctl = s->ctl;
+            launch_tc_rows(maps[l][1], s->map_xr_a, oa, s->cs);
+            launch_rmsnorm_rows_split(hb, H, L.post_norm, d.rms_eps, H, mb, s->xr_n, nullptr, s->cs, false, kRowBlock);
+            TcRowsArgs ga;
+            ga.K = H;
+            ga.M = mb;
+            ga.rows = F;
+            ga.gateup = 1;
+            ga.yb = s->xr_act;
+            ga.ldyb = F;
+            ga.ctl = s->ctl;
+            launch_tc_rows(maps[l][2], s->map_xr_n, ga, s->cs);
+            TcRowsArgs da;
+            da.K = F;
+            da.M = mb;
+            da.rows = H;
+            da.resid = 1;
+            da.rscale = rscale;
+            da.y = hb;
+            da.ldy = H;
+            da.ctl = s->ctl;
+            launch_tc_rows(maps[l][3], s->map_xr_act, da, s->cs);
+        }
     }
     launch_rmsnorm_rows(s->ph, H, fnorm, d.rms_eps, H, n, out_dev, H, nullptr, 0, s->cs, false);
     s->ctl_host->kv_len[which] = past + n;
@@ -1195,9 +1231,11 @@ VXC_API int32_t vxc_load_weights(vxc_device* dev, int32_t component, const void*
         if (component == VXC_BASE_DECODER) {
             dev->base = carve_decoder(dev->blob[component], base_shape(dev->desc), &fn);
             dev->base_norm = fn;
+            dev->base_maps = decoder_maps(dev->desc, dev->base);
         } else if (component == VXC_RESIDUAL_DECODER) {
             dev->res = carve_decoder(dev->blob[component], res_shape(dev->desc), &fn);
             dev->res_norm = fn;
+            dev->res_maps = decoder_maps(dev->desc, dev->res);
         } else if (component == VXC_DIT_ESTIMATOR) {
             const size_t Hd = dev->desc.dit_hidden, D = dev->desc.feat_dim;
             const __half* base = dev->blob[component] + 2 * (Hd * D + Hd) + 4 * (Hd * Hd + Hd);
