@@ -265,7 +265,8 @@ struct TcLinearArgs {
 enum { TC_B_TMA = 0, TC_B_NORM = 1, TC_B_ATTN = 2 };
 constexpr int kSsqStride = 24;  // floats per part in a sums-of-squares buffer
 CUtensorMap make_tensor_map_f16(const void* base, int rows, int cols, int box_rows);
-size_t tc_linear_smem_bytes(int K, int splits, int bmode, int attn_round = 1, int max_stages = 8);
+size_t tc_linear_smem_bytes(int K, int splits, int bmode, int attn_round = 1, int max_stages = 8,
+                            bool ssq_out = false);
 // heads per attention round that fit beside the stages of a TC_B_ATTN launch (2, else 1)
 int tc_attn_round(int K, int splits, int max_stages = 8);
 void launch_tc_linear(const CUtensorMap& map_a, const CUtensorMap& map_b, const TcLinearArgs& a, cudaStream_t s,

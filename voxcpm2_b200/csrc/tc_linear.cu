@@ -228,6 +228,12 @@ __device__ void build_b_attn(uint8_t* smem, const TcLinearArgs& a, int c0, int c
     zero_pad_rows(smem, cs, M);
 }
 
+// The receive buffer can share the stage area when nothing else needs it there:
+// TMA-fed token tiles, no K split (no remote pushes), no squares scratch.
+__host__ __device__ constexpr bool recv_in_stage_area(bool b_tma, int splits, bool ssq_out) {
+    return b_tma && splits == 1 && !ssq_out;
+}
+
 // BM: where the token operand comes from (TC_B_TMA / TC_B_NORM / TC_B_ATTN); one
 // instantiation each, so the TMA form does not carry the builders' registers.
 template <int BM>
@@ -365,7 +371,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int units = a.gateup ? 64 : kTileRows;
     const int slice = (units + S - 1) / S;
     const int halves = a.gateup ? 2 : 1;
-    float* recv = reinterpret_cast<float*>(smem + static_cast<size_t>(stage_area) * kStageBytes);
+    // Without a K split the receive buffer lives in the (then idle) stage area: the
+    // CTA needs no extra shared memory, so more CTAs of concurrent streams fit on an SM.
+    const bool recv_in_stages = recv_in_stage_area(b_tma, S, a.ssq_out != nullptr);
+    float* recv = reinterpret_cast<float*>(recv_in_stages ? smem : smem + static_cast<size_t>(stage_area) * kStageBytes);
+    if (recv_in_stages) {
+        if (tid == 0) {
+            // every load has landed before the stage area is reused (bounded when something failed)
+            for (int i = 0; i < stages; ++i)
+                if (issued[i] > 0 && !mbar_wait(&full_bar[i], (issued[i] - 1) & 1)) failed_s = 1;
+        }
+        __syncthreads();
+    }
     {
         float d[kBRows];
         if (ok) {
@@ -395,7 +412,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (m < a.M) st_peer(remote + 4 * m, d[m] + d[kLoOffset + m]);
         }
     }
-    if (tid == 0) {
+    if (tid == 0 && !recv_in_stages) {
         // no copy may still be landing in this CTA's shared memory when it moves on
         // (a no-op when every stage was consumed; bounded when something failed)
         for (int i = 0; i < stages; ++i)
@@ -438,11 +455,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
 }  // namespace
 
-size_t tc_linear_smem_bytes(int K, int splits, int bmode, int attn_round, int max_stages) {
+size_t tc_linear_smem_bytes(int K, int splits, int bmode, int attn_round, int max_stages, bool ssq_out) {
     const int nch = K / kKChunk;
     const int cs = (nch + splits - 1) / splits;
     const int stages = std::min(std::min(max_stages, kMaxStages), std::max(cs, 1));
     const size_t stage_bytes = static_cast<size_t>(stages) * kStageBytes;
+    if (recv_in_stage_area(bmode == TC_B_TMA, splits, ssq_out)) return stage_bytes + 1024;  // + alignment slack
     // receive buffer: per source split, an owner slice of rows (or of gate/up pairs, 2 rows each)
     const size_t slice_rows = std::max((128 + splits - 1) / splits, 2 * ((64 + splits - 1) / splits));
     const size_t recv_bytes = static_cast<size_t>(splits) * slice_rows * kRowFloats * sizeof(float);
@@ -496,7 +514,7 @@ void launch_tc_linear(const CUtensorMap& map_a, const CUtensorMap& map_b, const 
     cfg.gridDim = dim3(a.splits, n_tiles);
     cfg.blockDim = dim3(kTcThreads);
     if (a.max_stages < 1 || a.max_stages > kMaxStages) throw std::invalid_argument("tc_linear: max_stages in [1, 8]");
-    cfg.dynamicSmemBytes = tc_linear_smem_bytes(a.K, a.splits, a.bmode, a.attn_round, a.max_stages);
+    cfg.dynamicSmemBytes = tc_linear_smem_bytes(a.K, a.splits, a.bmode, a.attn_round, a.max_stages, a.ssq_out != nullptr);
     if (cfg.dynamicSmemBytes > dyn_limit()) throw std::invalid_argument("tc_linear: shared memory over 227 KB");
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
