@@ -132,6 +132,27 @@ def test_decoder_prefill_then_decode(rt, models, name, which):
     s.close()
 
 
+@pytest.mark.parametrize("name,which,n", [("tiny", 0, 128), ("tiny", 1, 129), ("small", 0, 200), ("bench", 0, 200)])
+def test_decoder_prefill_row_blocks(rt, models, name, which, n):
+    """Prefill longer than one 128-row block of the tensor-core linears (full block,
+    one row over, and a ragged second block), then one decode step."""
+    cfg, blobs, dev, orc = models(name)
+    s = rt.Stream(dev, kv_capacity=256)
+    rng = np.random.default_rng(11 + n)
+    pre = rng.standard_normal((n, cfg.hidden), dtype=np.float32)
+    orc.reset()
+    want = orc.decoder_forward(which, pre)
+    got = s.decoder_step(which, pre)
+    assert_parity(got, want, 2e-2, 0.999, f"{name} prefill of {n} rows")
+    x = rng.standard_normal((1, cfg.hidden), dtype=np.float32)
+    assert_parity(s.decoder_step(which, x), orc.decoder_forward(which, x), 2e-2, 0.999, f"{name} decode after {n}")
+    gk, _ = s.read_cache(which, 0)
+    wk, _ = orc.read_cache(which, 0)
+    assert gk.shape == wk.shape == (cfg.kv_heads, n + 1, cfg.head_dim)
+    assert np.abs(gk - wk).max() <= 1e-4 * max(1.0, np.abs(wk).max())
+    s.close()
+
+
 def test_decoder_capacity_checked_before_launch(rt, models):
     cfg, blobs, dev, orc = models("tiny")
     s = rt.Stream(dev, kv_capacity=4)
