@@ -43,6 +43,10 @@ def parse():
     p.add_argument("--streams", type=int, default=16, help="independent batch-1 streams per GPU")
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--cpu-sample-patches", type=int, default=6)
+    p.add_argument("--range", choices=["patches", "profile"], default=None,
+                   help="run one cudaProfilerStart/Stop range for an ncu app-range capture and exit: 'patches' = "
+                        "6 patches of every stream, 'profile' = the concurrent gate/up linear profile call "
+                        "(graph builds and warm-up replays included)")
     return p.parse_args()
 
 
@@ -61,14 +65,13 @@ def workload(streams_per_gpu: int, steps: int, warmup: int):
     }, min_patches
 
 
-def profiled_traffic(name: str):
-    """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from the
-    committed ncu summary profiles/<name>.md, or None."""
+def profiled_value(name: str, key: str):
+    """A figure ('key: value' line) from the committed ncu summary profiles/<name>.md, or None."""
     f = ROOT / "profiles" / f"{name}.md"
     if not f.exists():
         return None
     for line in f.read_text().splitlines():
-        if line.startswith("dram_bytes_per_launch:"):
+        if line.startswith(key + ":"):
             return float(line.split(":", 1)[1])
     return None
 
@@ -308,18 +311,34 @@ def run_ours(args):
     except rt.VxcError:  # the default form: per-layer tcgen05 linears
         prof_ms, prof_bytes = streams[0].profile_kernel("dit_gateup", 100)
         kname = "tc_linear_kernel gate/up (DiT, tcgen05 + TMA, 2x11 tokens, SiLU*up epilogue)"
-        traffic = profiled_traffic("tc_linear_gateup_dit")
+        traffic = profiled_value("tc_linear_gateup_dit", "dram_bytes_per_launch")
     achieved = prof_bytes / (prof_ms / 1e3) / 1e9
     # whole job: algorithmic bytes of all patches / the timed region (all streams together)
     bpp = patch_bytes(cfg, TEXT_TOKENS + 1 + W + K / 2)
     hbm_job = {"bytes_per_patch": bpp, "achieved": value * bpp / 1e9, "peak": peak, "unit": "GB/s",
                "frac": value * bpp / 1e9 / peak, "note": "patches/s x algorithmic bytes per patch, all streams"}
+    dram_pp = profiled_value("patch_loop_16streams_dram_range", "dram_bytes_per_patch")
+    if dram_pp:  # measured DRAM bytes: concurrent streams share weights through the L2
+        hbm_job.update({"dram_bytes_per_patch": dram_pp, "achieved_dram": value * dram_pp / 1e9,
+                        "frac_dram": value * dram_pp / 1e9 / peak,
+                        "dram_source": "profiles/patch_loop_16streams_dram_range.md (ncu app-range capture of "
+                                       "16 streams; the L2-shared fraction varies with the streams' timing)"})
     roofline = {"kernel": kname, "bound": "hbm",
                 "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                 "peak_kind": f"{peak_kind} burst copy bandwidth", "bytes_per_launch": prof_bytes,
                 "us_per_launch": 1e3 * prof_ms, "traffic": traffic,
                 "traffic_source": "profiles/tc_linear_gateup_dit.md (ncu dram__bytes_read.sum + write, one launch)"
                 if traffic else None}
+    # the same kernel in the regime the bench runs it: every stream replays its own
+    # graph of launches at once (aggregate algorithmic bytes / elapsed)
+    if not kname.startswith("dit_layers"):
+        iters_c = 100
+        cms, cbytes = rt.Stream.profile_kernel_concurrent(streams, "dit_gateup", iters_c)
+        agg = S * iters_c * cbytes / (cms / 1e3) / 1e9
+        roofline["concurrent"] = {"streams": S, "launches": S * iters_c, "achieved": agg, "frac": agg / peak,
+                                  "us_per_launch_avg": 1e3 * cms / (S * iters_c)}
+        roofline["concurrent"]["note"] = ("algorithmic bytes; the streams cycle through the same 12 layers' "
+                                          "weights and share part of them through the L2")
     kernels = {}
     for k in ("dit_qkv", "dit_o", "dit_down", "base_qkv", "base_attn", "base_gateup", "base_down"):
         km, kb = streams[0].profile_kernel(k, 50)
@@ -417,8 +436,53 @@ def run_ours(args):
     return 0
 
 
+def run_range(args):
+    """The workload of an ncu app-range capture (DRAM bytes of concurrent streams)."""
+    import torch
+    from voxcpm2_b200 import runtime as rt
+    from voxcpm2_b200 import synthetic
+    from voxcpm2_b200.config import BENCH
+    S, K, W = args.streams, 6, 3
+    dev = rt.Device(BENCH, 0, synthetic.model_blobs(BENCH, 0))
+    streams = [rt.Stream(dev, kv_capacity=512) for _ in range(S)]
+    if args.range == "profile":
+        rt.Stream.profile_kernel_concurrent(streams, "dit_gateup", 100)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        ms, nb = rt.Stream.profile_kernel_concurrent(streams, "dit_gateup", 100)
+        torch.cuda.profiler.stop()
+        print(json.dumps({"range": "profile", "ms": ms, "algorithmic_bytes": S * 100 * nb}))
+    else:
+        for i, (a, b) in enumerate(stream_seeds(0, S)):
+            streams[i].prefill(synthetic.token_ids(BENCH, TEXT_TOKENS, seed=a))
+            streams[i].upload_noise(synthetic.normal((W + K, BENCH.latent), seed=b))
+        for _ in range(W):
+            for s in streams:
+                s.patch_step_async(MIN_PATCHES, CFG, TIMESTEPS)
+        for s in streams:
+            s.synchronize()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        torch.cuda.profiler.start()
+        for _ in range(K):
+            for s in streams:
+                s.patch_step_async(MIN_PATCHES, CFG, TIMESTEPS)
+        for s in streams:
+            s.synchronize()
+        torch.cuda.profiler.stop()
+        dt = time.perf_counter() - t0
+        print(json.dumps({"range": "patches", "patches": S * K, "wall_ms": 1e3 * dt,
+                          "algorithmic_bytes": S * K * patch_bytes(BENCH, TEXT_TOKENS + 1 + W + K / 2)}))
+    for s in streams:
+        s.close()
+    dev.close()
+    return 0
+
+
 def main():
     args = parse()
+    if args.range:
+        return run_range(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

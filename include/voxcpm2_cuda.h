@@ -262,6 +262,12 @@ VXC_API int32_t vxc_read_latents(vxc_stream* s, int32_t first, int32_t count, fl
  * row of every base layer. */
 VXC_API int32_t vxc_profile_kernel(vxc_stream* s, int32_t kernel, int32_t iters, float* ms_per_launch,
                                    double* bytes_per_launch);
+/* The same kernel on n streams of one device at once: each stream replays its own
+ * graph of 'iters' launches, all started after one event on streams[0] and joined
+ * before a second; writes the elapsed milliseconds of the whole set (n * iters
+ * launches) and the algorithmic bytes of one launch. Not for VXC_PROF_DIT_LAYERS. */
+VXC_API int32_t vxc_profile_kernel_concurrent(vxc_stream** streams, int32_t n, int32_t kernel, int32_t iters,
+                                              float* ms_total, double* bytes_per_launch);
 /* The stream's cudaStream_t, for callers timing it with CUDA events. */
 VXC_API int32_t vxc_stream_cuda_handle(vxc_stream* s, void** out);
 

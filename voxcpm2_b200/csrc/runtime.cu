@@ -1892,6 +1892,158 @@ VXC_API int32_t vxc_read_latents(vxc_stream* s, int32_t first, int32_t count, fl
     });
 }
 
+namespace {
+
+// One launch function per layer of 'kernel', in the form the patch graph runs it
+// (the argument turns programmatic dependent launch on); 'bytes' receives the
+// algorithmic bytes of one launch. Called with the stream's mutex held.
+std::vector<std::function<void(bool)>> profile_launches(vxc_stream* s, int kernel, double& bytes) {
+    const vxc_device* dev = s->dev;
+    const vxc_model_desc& d = dev->desc;
+    const int Hd = d.dit_hidden, Fd = d.dit_ffn, H = d.hidden, F = d.ffn;
+    const int seq = dit_tokens_per_seq(d.patch_size), M = 2 * seq;
+    const int hq = d.q_heads, hkv = d.kv_heads, hd = d.head_dim;
+    const int dq = d.dit_q_heads, dkv = d.dit_kv_heads;
+    const size_t plane = static_cast<size_t>(hkv) * s->cap * hd;
+    const bool fused = s->dit_form != 2;
+    const int Wd = (dq + 2 * dkv) * (Hd / dq);
+    bytes = 0.0;
+    // one launch per layer, in the form the patch graph runs it
+    std::vector<std::function<void(bool)>> launch;
+    // the profiled decode kernels read kv_len from a private control block set to
+    // the next free cache row (the q/k/v launch writes there), so valid rows stay intact
+    const int pos = std::min(s->kv_len[0], s->cap - 1);
+    const int T = pos + 1;
+    StreamCtl* pctl = reinterpret_cast<StreamCtl*>(s->est);  // >= sizeof(StreamCtl) floats
+    if (kernel == VXC_PROF_BASE_QKV || kernel == VXC_PROF_BASE_ATTN) {
+        StreamCtl probe{};
+        probe.kv_len[0] = pos;
+        ck(cudaMemcpyAsync(pctl, &probe, sizeof(StreamCtl), cudaMemcpyHostToDevice, s->cs), "probe ctl");
+        ck(cudaStreamSynchronize(s->cs), "sync");
+    }
+    const bool dit = kernel <= VXC_PROF_DIT_QKV || kernel == VXC_PROF_DIT_O;
+    const size_t nl = dit ? dev->dit.size() : dev->base.size();
+    for (size_t l = 0; l < nl; ++l) {
+        switch (kernel) {
+            case VXC_PROF_DIT_GATEUP: {
+                TcLinearArgs a = tc_plan(s, Fd / 64, Hd, fused);
+                a.K = Hd; a.M = M; a.rows = Fd; a.gateup = 1;
+                a.yb = s->xb_act; a.ldyb = Fd; a.ctl = s->ctl;
+                if (fused) {
+                    a.bmode = TC_B_NORM; a.x = s->dh; a.ldx = Hd; a.g = dev->dit[l].post_norm; a.eps = d.rms_eps;
+                    a.ssq_in = s->dssq; a.ssq_parts = (Hd / 128) * tc_plan(s, Hd / 128, dq * 64, true).splits;
+                }
+                bytes = 2.0 * 2 * Fd * Hd + (fused ? 4.0 * M * Hd : 2.0 * 48 * Hd) + 2.0 * 48 * Fd;
+                const CUtensorMap ma = dev->dit_maps[l][2], mb = s->map_xb_n;
+                launch.push_back([=](bool pdl) { launch_tc_linear(ma, mb, a, s->cs, pdl); });
+                break;
+            }
+            case VXC_PROF_DIT_DOWN: {
+                TcLinearArgs a = tc_plan(s, Hd / 128, Fd, false);
+                a.K = Fd; a.M = M; a.rows = Hd; a.resid = 1;
+                a.y = s->dxn; a.ldy = Hd; a.ctl = s->ctl;
+                if (fused) a.ssq_out = s->dssq + static_cast<size_t>(Hd / 16) * kSsqStride;  // spare parts
+                bytes = 2.0 * Hd * Fd + 2.0 * 48 * Fd + 8.0 * M * Hd;
+                const CUtensorMap ma = dev->dit_maps[l][3], mb = s->map_xb_act;
+                launch.push_back([=](bool pdl) { launch_tc_linear(ma, mb, a, s->cs, pdl); });
+                break;
+            }
+            case VXC_PROF_DIT_QKV: {
+                TcLinearArgs a = tc_plan(s, Wd / 128, Hd, fused);
+                a.K = Hd; a.M = M; a.rows = Wd;
+                a.y = s->dqkv; a.ldy = Wd; a.ctl = s->ctl;
+                if (fused) {
+                    a.bmode = TC_B_NORM; a.x = s->dh; a.ldx = Hd; a.g = dev->dit[l].in_norm; a.eps = d.rms_eps;
+                    a.ssq_in = s->dssq; a.ssq_parts = (Hd + 31) / 32;
+                }
+                bytes = 2.0 * Wd * Hd + (fused ? 4.0 * M * Hd : 2.0 * 48 * Hd) + 4.0 * M * Wd;
+                const CUtensorMap ma = dev->dit_maps[l][0], mb = s->map_xb_n;
+                launch.push_back([=](bool pdl) { launch_tc_linear(ma, mb, a, s->cs, pdl); });
+                break;
+            }
+            case VXC_PROF_DIT_O: {
+                TcLinearArgs a = tc_plan(s, Hd / 128, dq * 64, fused);
+                a.K = dq * 64; a.M = M; a.rows = Hd; a.resid = 1;
+                a.y = s->dxn; a.ldy = Hd; a.ctl = s->ctl;
+                if (fused) {
+                    a.bmode = TC_B_ATTN; a.qkv = s->dqkv; a.q_heads = dq; a.kv_heads = dkv; a.seq = seq;
+                    a.rope_cos = dev->dit_rope_cos; a.rope_sin = dev->dit_rope_sin; a.scale = 0.125f;
+                    a.attn_round = tc_attn_round(a.K, a.splits, a.max_stages);
+                    a.ssq_out = s->dssq + static_cast<size_t>(Hd / 16) * kSsqStride;
+                }
+                bytes = 2.0 * Hd * dq * 64 + (fused ? 4.0 * M * Wd : 2.0 * 48 * dq * 64) + 8.0 * M * Hd;
+                const CUtensorMap ma = dev->dit_maps[l][1], mb = s->map_xb_a;
+                launch.push_back([=](bool pdl) { launch_tc_linear(ma, mb, a, s->cs, pdl); });
+                break;
+            }
+            case VXC_PROF_BASE_GATEUP: {
+                const LayerW& BL = dev->base[l];
+                GemvArgs a;
+                a.mode = GEMV_GATEUP; a.w = BL.wgateup; a.x = s->out[0]; a.norm_g = BL.post_norm; a.eps = d.rms_eps;
+                a.K = H; a.rows = F; a.y = s->act;
+                bytes = 2.0 * 2 * F * H + 4.0 * H + 4.0 * F;
+                launch.push_back([=](bool pdl) { launch_gemv(a, s->cs, pdl); });
+                break;
+            }
+            case VXC_PROF_BASE_DOWN: {
+                GemvArgs a;
+                a.mode = GEMV_RESID; a.w = dev->base[l].wdown; a.x = s->act; a.K = F; a.rows = H; a.resid = s->out[0];
+                bytes = 2.0 * H * F + 4.0 * F + 8.0 * H;
+                launch.push_back([=](bool pdl) { launch_gemv(a, s->cs, pdl); });
+                break;
+            }
+            case VXC_PROF_BASE_QKV: {
+                const LayerW& BL = dev->base[l];
+                GemvArgs a;
+                a.mode = GEMV_QKV; a.w = BL.wqkv; a.x = s->out[0]; a.norm_g = BL.in_norm; a.eps = d.rms_eps;
+                a.K = H; a.rows = (hq + 2 * hkv) * hd / 2; a.y = s->q; a.q_heads = hq; a.kv_heads = hkv;
+                a.head_dim = hd; a.rope_cos = s->rope_cos; a.rope_sin = s->rope_sin;
+                a.k_cache = s->kc[0] + l * plane; a.v_cache = s->vc[0] + l * plane; a.cap = s->cap; a.which = 0;
+                a.ctl = pctl;
+                bytes = 2.0 * (hq + 2 * hkv) * hd * H + 4.0 * H + 4.0 * hq * hd + 4.0 * 2 * hkv * hd;
+                launch.push_back([=](bool pdl) { launch_gemv(a, s->cs, pdl); });
+                break;
+            }
+            case VXC_PROF_BASE_ATTN: {
+                AttnArgs a;
+                a.q = s->q; a.k0 = s->kc[0] + l * plane; a.v0 = s->vc[0] + l * plane; a.len0 = s->cap;
+                a.stride0 = s->cap; a.q_heads = hq; a.kv_heads = hkv; a.head_dim = hd; a.scale = 0.125f;
+                a.splits = s->splits; a.partial = s->partial; a.counters = s->counters; a.out = s->attn;
+                a.ctl = pctl; a.which = 0;
+                bytes = 4.0 * 2 * hkv * static_cast<double>(T) * hd + 8.0 * hq * hd;
+                launch.push_back([=](bool pdl) { launch_attn_decode_cluster(a, s->cs, pdl); });
+                break;
+            }
+        }
+    }
+    return launch;
+}
+
+// Captures 'iters' launches of 'kernel' cycling through the layers in one graph,
+// starting at layer 'first' (after one eager warm-up launch per layer), and
+// instantiates it.
+cudaGraphExec_t profile_graph(vxc_stream* s, int kernel, int iters, double& bytes, int first = 0) {
+    std::vector<std::function<void(bool)>> launch = profile_launches(s, kernel, bytes);
+    for (auto& f : launch) f(false);  // warm-up, eager
+    cudaGraph_t gr = nullptr;
+    ck(cudaStreamBeginCapture(s->cs, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+    try {
+        for (int i = 0; i < iters; ++i) launch[static_cast<size_t>(i + first) % launch.size()](i > 0);
+    } catch (...) {
+        cudaStreamEndCapture(s->cs, &gr);
+        if (gr) cudaGraphDestroy(gr);
+        throw;
+    }
+    ck(cudaStreamEndCapture(s->cs, &gr), "cudaStreamEndCapture");
+    cudaGraphExec_t ge = nullptr;
+    const cudaError_t ie = cudaGraphInstantiate(&ge, gr, 0);
+    cudaGraphDestroy(gr);
+    ck(ie, "cudaGraphInstantiate");
+    return ge;
+}
+
+}  // namespace
+
 VXC_API int32_t vxc_profile_kernel(vxc_stream* s, int32_t kernel, int32_t iters, float* ms_per_launch,
                                    double* bytes_per_launch) {
     return guard([&] {
@@ -1946,139 +2098,10 @@ VXC_API int32_t vxc_profile_kernel(vxc_stream* s, int32_t kernel, int32_t iters,
             *bytes_per_launch = per_layer * d.dit_layers;
             return;
         }
-        const int Hd = d.dit_hidden, Fd = d.dit_ffn, H = d.hidden, F = d.ffn;
-        const int seq = dit_tokens_per_seq(d.patch_size), M = 2 * seq;
-        const int hq = d.q_heads, hkv = d.kv_heads, hd = d.head_dim;
-        const int dq = d.dit_q_heads, dkv = d.dit_kv_heads;
-        const size_t plane = static_cast<size_t>(hkv) * s->cap * hd;
-        const bool fused = s->dit_form != 2;
-        const int Wd = (dq + 2 * dkv) * (Hd / dq);
-        double bytes = 0.0;
-        // one launch per layer, in the form the patch graph runs it
-        std::vector<std::function<void(bool)>> launch;
-        // the profiled decode kernels read kv_len from a private control block set to
-        // the next free cache row (the q/k/v launch writes there), so valid rows stay intact
-        const int pos = std::min(s->kv_len[0], s->cap - 1);
-        const int T = pos + 1;
-        StreamCtl* pctl = reinterpret_cast<StreamCtl*>(s->est);  // >= sizeof(StreamCtl) floats
-        if (kernel == VXC_PROF_BASE_QKV || kernel == VXC_PROF_BASE_ATTN) {
-            StreamCtl probe{};
-            probe.kv_len[0] = pos;
-            ck(cudaMemcpyAsync(pctl, &probe, sizeof(StreamCtl), cudaMemcpyHostToDevice, s->cs), "probe ctl");
-            ck(cudaStreamSynchronize(s->cs), "sync");
-        }
-        const bool dit = kernel <= VXC_PROF_DIT_QKV || kernel == VXC_PROF_DIT_O;
-        const size_t nl = dit ? dev->dit.size() : dev->base.size();
-        for (size_t l = 0; l < nl; ++l) {
-            switch (kernel) {
-                case VXC_PROF_DIT_GATEUP: {
-                    TcLinearArgs a = tc_plan(s, Fd / 64, Hd, fused);
-                    a.K = Hd; a.M = M; a.rows = Fd; a.gateup = 1;
-                    a.yb = s->xb_act; a.ldyb = Fd; a.ctl = s->ctl;
-                    if (fused) {
-                        a.bmode = TC_B_NORM; a.x = s->dh; a.ldx = Hd; a.g = dev->dit[l].post_norm; a.eps = d.rms_eps;
-                        a.ssq_in = s->dssq; a.ssq_parts = (Hd / 128) * tc_plan(s, Hd / 128, dq * 64, true).splits;
-                    }
-                    bytes = 2.0 * 2 * Fd * Hd + (fused ? 4.0 * M * Hd : 2.0 * 48 * Hd) + 2.0 * 48 * Fd;
-                    const CUtensorMap ma = dev->dit_maps[l][2], mb = s->map_xb_n;
-                    launch.push_back([=](bool pdl) { launch_tc_linear(ma, mb, a, s->cs, pdl); });
-                    break;
-                }
-                case VXC_PROF_DIT_DOWN: {
-                    TcLinearArgs a = tc_plan(s, Hd / 128, Fd, false);
-                    a.K = Fd; a.M = M; a.rows = Hd; a.resid = 1;
-                    a.y = s->dxn; a.ldy = Hd; a.ctl = s->ctl;
-                    if (fused) a.ssq_out = s->dssq + static_cast<size_t>(Hd / 16) * kSsqStride;  // spare parts
-                    bytes = 2.0 * Hd * Fd + 2.0 * 48 * Fd + 8.0 * M * Hd;
-                    const CUtensorMap ma = dev->dit_maps[l][3], mb = s->map_xb_act;
-                    launch.push_back([=](bool pdl) { launch_tc_linear(ma, mb, a, s->cs, pdl); });
-                    break;
-                }
-                case VXC_PROF_DIT_QKV: {
-                    TcLinearArgs a = tc_plan(s, Wd / 128, Hd, fused);
-                    a.K = Hd; a.M = M; a.rows = Wd;
-                    a.y = s->dqkv; a.ldy = Wd; a.ctl = s->ctl;
-                    if (fused) {
-                        a.bmode = TC_B_NORM; a.x = s->dh; a.ldx = Hd; a.g = dev->dit[l].in_norm; a.eps = d.rms_eps;
-                        a.ssq_in = s->dssq; a.ssq_parts = (Hd + 31) / 32;
-                    }
-                    bytes = 2.0 * Wd * Hd + (fused ? 4.0 * M * Hd : 2.0 * 48 * Hd) + 4.0 * M * Wd;
-                    const CUtensorMap ma = dev->dit_maps[l][0], mb = s->map_xb_n;
-                    launch.push_back([=](bool pdl) { launch_tc_linear(ma, mb, a, s->cs, pdl); });
-                    break;
-                }
-                case VXC_PROF_DIT_O: {
-                    TcLinearArgs a = tc_plan(s, Hd / 128, dq * 64, fused);
-                    a.K = dq * 64; a.M = M; a.rows = Hd; a.resid = 1;
-                    a.y = s->dxn; a.ldy = Hd; a.ctl = s->ctl;
-                    if (fused) {
-                        a.bmode = TC_B_ATTN; a.qkv = s->dqkv; a.q_heads = dq; a.kv_heads = dkv; a.seq = seq;
-                        a.rope_cos = dev->dit_rope_cos; a.rope_sin = dev->dit_rope_sin; a.scale = 0.125f;
-                        a.attn_round = tc_attn_round(a.K, a.splits, a.max_stages);
-                        a.ssq_out = s->dssq + static_cast<size_t>(Hd / 16) * kSsqStride;
-                    }
-                    bytes = 2.0 * Hd * dq * 64 + (fused ? 4.0 * M * Wd : 2.0 * 48 * dq * 64) + 8.0 * M * Hd;
-                    const CUtensorMap ma = dev->dit_maps[l][1], mb = s->map_xb_a;
-                    launch.push_back([=](bool pdl) { launch_tc_linear(ma, mb, a, s->cs, pdl); });
-                    break;
-                }
-                case VXC_PROF_BASE_GATEUP: {
-                    const LayerW& BL = dev->base[l];
-                    GemvArgs a;
-                    a.mode = GEMV_GATEUP; a.w = BL.wgateup; a.x = s->out[0]; a.norm_g = BL.post_norm; a.eps = d.rms_eps;
-                    a.K = H; a.rows = F; a.y = s->act;
-                    bytes = 2.0 * 2 * F * H + 4.0 * H + 4.0 * F;
-                    launch.push_back([=](bool pdl) { launch_gemv(a, s->cs, pdl); });
-                    break;
-                }
-                case VXC_PROF_BASE_DOWN: {
-                    GemvArgs a;
-                    a.mode = GEMV_RESID; a.w = dev->base[l].wdown; a.x = s->act; a.K = F; a.rows = H; a.resid = s->out[0];
-                    bytes = 2.0 * H * F + 4.0 * F + 8.0 * H;
-                    launch.push_back([=](bool pdl) { launch_gemv(a, s->cs, pdl); });
-                    break;
-                }
-                case VXC_PROF_BASE_QKV: {
-                    const LayerW& BL = dev->base[l];
-                    GemvArgs a;
-                    a.mode = GEMV_QKV; a.w = BL.wqkv; a.x = s->out[0]; a.norm_g = BL.in_norm; a.eps = d.rms_eps;
-                    a.K = H; a.rows = (hq + 2 * hkv) * hd / 2; a.y = s->q; a.q_heads = hq; a.kv_heads = hkv;
-                    a.head_dim = hd; a.rope_cos = s->rope_cos; a.rope_sin = s->rope_sin;
-                    a.k_cache = s->kc[0] + l * plane; a.v_cache = s->vc[0] + l * plane; a.cap = s->cap; a.which = 0;
-                    a.ctl = pctl;
-                    bytes = 2.0 * (hq + 2 * hkv) * hd * H + 4.0 * H + 4.0 * hq * hd + 4.0 * 2 * hkv * hd;
-                    launch.push_back([=](bool pdl) { launch_gemv(a, s->cs, pdl); });
-                    break;
-                }
-                case VXC_PROF_BASE_ATTN: {
-                    AttnArgs a;
-                    a.q = s->q; a.k0 = s->kc[0] + l * plane; a.v0 = s->vc[0] + l * plane; a.len0 = s->cap;
-                    a.stride0 = s->cap; a.q_heads = hq; a.kv_heads = hkv; a.head_dim = hd; a.scale = 0.125f;
-                    a.splits = s->splits; a.partial = s->partial; a.counters = s->counters; a.out = s->attn;
-                    a.ctl = pctl; a.which = 0;
-                    bytes = 4.0 * 2 * hkv * static_cast<double>(T) * hd + 8.0 * hq * hd;
-                    launch.push_back([=](bool pdl) { launch_attn_decode_cluster(a, s->cs, pdl); });
-                    break;
-                }
-            }
-        }
         // iters launches cycling through the layers, captured in one graph with
         // programmatic dependent launch between them like the patch graph
-        for (auto& f : launch) f(false);  // warm-up, eager
-        cudaGraph_t gr = nullptr;
-        ck(cudaStreamBeginCapture(s->cs, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
-        try {
-            for (int i = 0; i < iters; ++i) launch[static_cast<size_t>(i) % launch.size()](i > 0);
-        } catch (...) {
-            cudaStreamEndCapture(s->cs, &gr);
-            if (gr) cudaGraphDestroy(gr);
-            throw;
-        }
-        ck(cudaStreamEndCapture(s->cs, &gr), "cudaStreamEndCapture");
-        cudaGraphExec_t ge = nullptr;
-        const cudaError_t ie = cudaGraphInstantiate(&ge, gr, 0);
-        cudaGraphDestroy(gr);
-        ck(ie, "cudaGraphInstantiate");
+        double bytes = 0.0;
+        cudaGraphExec_t ge = profile_graph(s, kernel, iters, bytes);
         cudaEvent_t e0 = nullptr, e1 = nullptr;
         float ms = 0.f;
         cudaError_t err = cudaGraphLaunch(ge, s->cs);  // warm-up replay
@@ -2095,6 +2118,71 @@ VXC_API int32_t vxc_profile_kernel(vxc_stream* s, int32_t kernel, int32_t iters,
         ck(err, "profile replay");
         sync_ctl(s);  // a bounded wait that gave up inside the profiled kernels surfaces here
         *ms_per_launch = ms / static_cast<float>(iters);
+        *bytes_per_launch = bytes;
+    });
+}
+
+VXC_API int32_t vxc_profile_kernel_concurrent(vxc_stream** streams, int32_t n, int32_t kernel, int32_t iters,
+                                              float* ms_total, double* bytes_per_launch) {
+    return guard([&] {
+        require(streams != nullptr && ms_total != nullptr && bytes_per_launch != nullptr, "null argument");
+        require(n >= 1 && n <= 256, "stream count must be in [1, 256]");
+        require(iters > 0 && iters <= 100000, "iters must be in [1, 100000]");
+        require(kernel >= VXC_PROF_DIT_GATEUP && kernel <= VXC_PROF_DIT_O, "unknown kernel id");
+        std::vector<vxc_stream*> ss(streams, streams + n);
+        for (vxc_stream* x : ss) require(x != nullptr && x->dev == ss[0]->dev, "streams must share one device");
+        std::vector<vxc_stream*> order(ss);
+        std::sort(order.begin(), order.end());
+        require(std::adjacent_find(order.begin(), order.end()) == order.end(), "streams must be distinct");
+        std::vector<std::unique_lock<std::mutex>> locks;
+        for (vxc_stream* x : order) locks.emplace_back(x->call_mutex);  // address order: no lock cycles
+        check_loaded(ss[0]->dev, {VXC_BASE_DECODER, VXC_DIT_ESTIMATOR});
+        DeviceGuard g(ss[0]->dev->device);
+        double bytes = 0.0;
+        std::vector<cudaGraphExec_t> graphs;
+        std::vector<cudaEvent_t> done(ss.size(), nullptr);
+        cudaEvent_t e0 = nullptr, e1 = nullptr;
+        cudaError_t err = cudaSuccess;
+        float ms = 0.f;
+        try {
+            // stream i starts at layer i * layers / n, so the streams do not read the same
+            // layer's weights in lockstep (which would let them share them through the L2)
+            const int layers = kernel <= VXC_PROF_DIT_QKV || kernel == VXC_PROF_DIT_O
+                                   ? static_cast<int>(ss[0]->dev->dit.size())
+                                   : static_cast<int>(ss[0]->dev->base.size());
+            for (size_t i = 0; i < ss.size(); ++i)
+                graphs.push_back(profile_graph(ss[i], kernel, iters, bytes,
+                                               static_cast<int>(i * layers / ss.size())));
+            for (size_t i = 0; i < ss.size() && err == cudaSuccess; ++i) err = cudaGraphLaunch(graphs[i], ss[i]->cs);
+            for (vxc_stream* x : ss)
+                if (err == cudaSuccess) err = cudaStreamSynchronize(x->cs);  // warm-up replays done
+            for (auto& e : done)
+                if (err == cudaSuccess) err = cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
+            if (err == cudaSuccess) err = cudaEventCreate(&e0);
+            if (err == cudaSuccess) err = cudaEventCreate(&e1);
+            // all graphs start after e0 on the first stream and end before e1 on it
+            if (err == cudaSuccess) err = cudaEventRecord(e0, ss[0]->cs);
+            for (size_t i = 1; i < ss.size() && err == cudaSuccess; ++i) err = cudaStreamWaitEvent(ss[i]->cs, e0, 0);
+            for (size_t i = 0; i < ss.size() && err == cudaSuccess; ++i) err = cudaGraphLaunch(graphs[i], ss[i]->cs);
+            for (size_t i = 1; i < ss.size() && err == cudaSuccess; ++i) {
+                err = cudaEventRecord(done[i], ss[i]->cs);
+                if (err == cudaSuccess) err = cudaStreamWaitEvent(ss[0]->cs, done[i], 0);
+            }
+            if (err == cudaSuccess) err = cudaEventRecord(e1, ss[0]->cs);
+            if (err == cudaSuccess) err = cudaEventSynchronize(e1);
+            if (err == cudaSuccess) err = cudaEventElapsedTime(&ms, e0, e1);
+        } catch (...) {
+            for (cudaGraphExec_t ge : graphs) cudaGraphExecDestroy(ge);
+            throw;
+        }
+        for (auto e : done)
+            if (e) cudaEventDestroy(e);
+        if (e0) cudaEventDestroy(e0);
+        if (e1) cudaEventDestroy(e1);
+        for (cudaGraphExec_t ge : graphs) cudaGraphExecDestroy(ge);
+        ck(err, "concurrent profile");
+        for (vxc_stream* x : ss) sync_ctl(x);
+        *ms_total = ms;
         *bytes_per_launch = bytes;
     });
 }

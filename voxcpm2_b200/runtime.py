@@ -98,6 +98,7 @@ def _signatures():
         "vxc_read_hidden": ([vp, vp, vp], i),
         "vxc_read_latents": ([vp, i, i, vp], i),
         "vxc_profile_kernel": ([vp, i, i, C.POINTER(f), C.POINTER(C.c_double)], i),
+        "vxc_profile_kernel_concurrent": ([C.POINTER(vp), i, i, i, C.POINTER(f), C.POINTER(C.c_double)], i),
         "vxc_stream_cuda_handle": ([vp, C.POINTER(vp)], i),
     }
 
@@ -311,6 +312,17 @@ class Stream:
         ms = C.c_float()
         nb = C.c_double()
         _check(lib().vxc_profile_kernel(self._h, PROFILE_KERNELS[kernel], iters, C.byref(ms), C.byref(nb)))
+        return float(ms.value), float(nb.value)
+
+    @staticmethod
+    def profile_kernel_concurrent(streams, kernel: str, iters: int = 100):
+        """(ms for the whole set, algorithmic bytes per launch): the kernel's graph of
+        'iters' launches replayed on every stream at once."""
+        arr = (C.c_void_p * len(streams))(*[st._h for st in streams])
+        ms = C.c_float()
+        nb = C.c_double()
+        _check(lib().vxc_profile_kernel_concurrent(arr, len(streams), PROFILE_KERNELS[kernel], iters, C.byref(ms),
+                                                   C.byref(nb)))
         return float(ms.value), float(nb.value)
 
     def cuda_stream(self) -> int:
