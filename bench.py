@@ -41,6 +41,9 @@ def parse():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--streams", type=int, default=16, help="independent batch-1 streams per GPU")
+    p.add_argument("--groups", type=int, default=8,
+                   help="stream groups per GPU for the group measurement (0 skips it)")
+    p.add_argument("--group-members", type=int, default=4, help="streams per group (1..4)")
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--cpu-sample-patches", type=int, default=6)
     p.add_argument("--range", choices=["patches", "profile"], default=None,
@@ -245,6 +248,65 @@ def job_rate(world: int, streams_per_gpu: int, steps: int, seconds: float) -> fl
 
 
 # --------------------------------------------------------------- GPU arm ---
+def group_rate(rt, synthetic, dev, cfg, groups, members, K, W, min_patches, rank, barrier, max_over_ranks, world):
+    """Device-resident patches/s of `groups` stream groups of `members` streams each
+    (every member its own prompt and noise), timed like the headline; plus the
+    device time of one group patch with the other groups idle."""
+    import torch
+    gs = [rt.Group(dev, members, kv_capacity=TEXT_TOKENS + 1 + W + K + 8 + 512) for _ in range(groups)]
+    for gi, g in enumerate(gs):
+        for m, st in enumerate(g.streams):
+            a = 7919 * (rank * 1000 + gi * members + m) + 13
+            st.prefill(synthetic.token_ids(cfg, TEXT_TOKENS, seed=a))
+            st.upload_noise(synthetic.normal((W + K + 4, cfg.latent), seed=a + 1))
+    for _ in range(W):
+        for g in gs:
+            g.patch_step_async(min_patches, CFG, TIMESTEPS)
+    for g in gs:
+        g.synchronize()
+    ext = [torch.cuda.ExternalStream(g.streams[0].cuda_stream()) for g in gs]
+    main = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(main)
+    for st in ext:
+        st.wait_event(e0)
+    for _ in range(K):
+        for g in gs:
+            g.patch_step_async(min_patches, CFG, TIMESTEPS)
+    for st in ext:
+        ev = torch.cuda.Event()
+        ev.record(st)
+        main.wait_event(ev)
+    e1.record(main)
+    e1.synchronize()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    for g in gs:
+        g.synchronize()
+        for st in g.streams:
+            s = st.state()
+            assert s.patches == W + K and s.error == 0, "a group member did not complete its patches"
+    lat = []
+    for _ in range(3):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(ext[0])
+        gs[0].patch_step_async(min_patches, CFG, TIMESTEPS)
+        b.record(ext[0])
+        b.synchronize()
+        lat.append(a.elapsed_time(b))
+    kernels = gs[0].graph_kernels()
+    for g in gs:
+        g.close()
+    return {"groups_per_gpu": groups, "members": members, "streams_per_gpu": groups * members,
+            "value": world * groups * members * K / (ms / 1e3), "unit": "patches/s", "ms_per_step": ms / K,
+            "group_patch_ms": float(np.median(lat)), "kernels_per_group_patch": kernels,
+            "gpu_launches": groups * K * kernels,
+            "note": "each group steps its members as one CUDA graph; the 9 estimator evaluations of all "
+                    "members run as one tcgen05 pass over the DiT weights (22 rows per member)"}
+
+
 def run_ours(args):
     import torch
     from voxcpm2_b200 import runtime as rt
@@ -405,6 +467,12 @@ def run_ours(args):
     h2d = S * L * 4                   # each stream's noise patch
     d2h = S * (L * 4 + 40)            # each stream's latent patch + its 40-byte control block
 
+    # ---- stream groups: the same workload with each group's estimator passes batched
+    group = None
+    if args.groups > 0:
+        group = group_rate(rt, synthetic, dev, cfg, args.groups, args.group_members, K, W, min_patches, rank,
+                           barrier, max_over_ranks, world)
+
     # ---- CPU baseline: the oracle port on this host, bounded sample (rank 0, N = 1)
     cpu = None
     if rank == 0 and world == 1:
@@ -426,7 +494,7 @@ def run_ours(args):
             "per_gpu_patches_per_s": value / world,
             "e2e": {"value": e2e_value, "unit": "patches/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": graph_kernels * S * K, "roofline": roofline, "hbm_job": hbm_job, "kernels": kernels,
-            "cpu_baseline": cpu, "clocks": clk,
+            "cpu_baseline": cpu, "clocks": clk, "group": group,
         }
         print(json.dumps(line), flush=True)
     for s in streams:

@@ -31,6 +31,7 @@ extern "C" {
 
 typedef struct vxc_device vxc_device;
 typedef struct vxc_stream vxc_stream;
+typedef struct vxc_group vxc_group;
 
 /* Same values and meaning as voxcpm2_status (include/voxcpm2/c_api.h:37-44). */
 typedef enum vxc_status {
@@ -269,6 +270,25 @@ VXC_API int32_t vxc_profile_kernel(vxc_stream* s, int32_t kernel, int32_t iters,
 VXC_API int32_t vxc_profile_kernel_concurrent(vxc_stream** streams, int32_t n, int32_t kernel, int32_t iters,
                                               float* ms_total, double* bytes_per_launch);
 /* The stream's cudaStream_t, for callers timing it with CUDA events. */
+/* Groups: up to 4 streams whose patch steps run together as one CUDA graph. Each
+ * member keeps its own prompt, KV caches, noise, stop state and latents (use the
+ * stream calls above on vxc_group_stream's handle: vxc_prefill, vxc_upload_noise,
+ * vxc_read_state, vxc_read_latents ...); the 9 estimator evaluations of all
+ * members run as one batched pass over 22 rows per member, so the DiT weights are
+ * read once per group patch. No reference counterpart: the reference synthesises
+ * one utterance at a time. Group steps are stream-ordered with the members' own
+ * calls: a step waits for work queued on every member stream, and later calls on a
+ * member stream wait for the step. */
+VXC_API int32_t vxc_group_create(vxc_device* dev, int32_t n_streams, int32_t kv_capacity, vxc_group** out);
+VXC_API void vxc_group_destroy(vxc_group* g);
+VXC_API int32_t vxc_group_stream(vxc_group* g, int32_t member, vxc_stream** out);
+/* One patch of every member (as vxc_patch_step_async), noise from each member's uploaded table. */
+VXC_API int32_t vxc_group_patch_step_async(vxc_group* g, int32_t min_patches, float cfg_value, int32_t timesteps);
+/* Waits for the group's work; reports a device-side failure of any member. */
+VXC_API int32_t vxc_group_synchronize(vxc_group* g);
+/* Kernel launches in one captured group patch step (0 before the first). */
+VXC_API int32_t vxc_group_graph_kernels(vxc_group* g, int32_t* out);
+
 VXC_API int32_t vxc_stream_cuda_handle(vxc_stream* s, void** out);
 
 #ifdef __cplusplus

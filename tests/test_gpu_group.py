@@ -1,0 +1,105 @@
+"""GPU parity of stream groups: several streams stepped as one CUDA graph with
+their estimator evaluations batched into one pass over the DiT weights.
+
+Each member has its own prompt and noise table; its latents must match the
+oracle's generate() for that prompt and seed at the patch-loop bar (per patch
+max-abs 2e-2, cosine >= 0.999), and its KV lengths and patch count must advance
+as a lone stream's do. Stop decisions are kept out of play (min_patches above
+the patches run) so every member runs every patch.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import close_stats
+from voxcpm2_b200 import synthetic
+from voxcpm2_b200.config import BENCH, TINY
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def rt():
+    from voxcpm2_b200 import runtime
+    return runtime
+
+
+def run_group(rt, cfg, dev, prompts, seeds, patches, timesteps=10, cfg_value=2.0):
+    g = rt.Group(dev, len(prompts), kv_capacity=256)
+    for st, ids, seed in zip(g.streams, prompts, seeds):
+        st.prefill(ids)
+        st.upload_noise(oracle.noise_table(seed, patches, cfg.latent))
+    for _ in range(patches):
+        g.patch_step_async(10 * patches, cfg_value, timesteps)
+    g.synchronize()
+    out = []
+    for st, ids in zip(g.streams, prompts):
+        s = st.state()
+        assert s.patches == patches
+        assert s.kv_len[0] == s.kv_len[1] == len(ids) + 1 + patches
+        out.append(st.latents(0, patches))
+    kernels = g.graph_kernels()
+    g.close()
+    return out, kernels
+
+
+def check_members(orc, prompts, seeds, got, patches, timesteps=10, cfg_value=2.0):
+    for m, (ids, seed) in enumerate(zip(prompts, seeds)):
+        want = orc.generate(ids, min_patches=10 * patches, timesteps=timesteps, cfg_value=cfg_value,
+                            max_patches_override=patches, seed=seed)
+        assert want["patches"] == patches
+        stats = [close_stats(got[m][i], want["latents"][i]) for i in range(patches)]
+        err, cos = max(s[0] for s in stats), min(s[1] for s in stats)
+        print(f"member {m}: worst max-abs {err:.3e}, cosine {cos:.6f}")
+        assert err <= 2e-2 and cos >= 0.999, (m, err, cos)
+
+
+@pytest.mark.parametrize("members", [1, 4])
+def test_group_tiny_matches_oracle(rt, members):
+    blobs = synthetic.model_blobs(TINY, 0)
+    dev = rt.Device(TINY, 0, blobs)
+    orc = oracle.Oracle(TINY, blobs)
+    prompts = [synthetic.token_ids(TINY, 6 + 3 * m, seed=20 + m) for m in range(members)]
+    seeds = [100 + m for m in range(members)]
+    got, kernels = run_group(rt, TINY, dev, prompts, seeds, patches=8, timesteps=6)
+    check_members(orc, prompts, seeds, got, 8, timesteps=6)
+    assert kernels > 0
+    dev.close()
+
+
+def test_group_bench_matches_oracle(rt):
+    """The benchmark model, 3 members with different prompts, 4 patches."""
+    blobs = synthetic.model_blobs(BENCH, 0)
+    dev = rt.Device(BENCH, 0, blobs)
+    orc = oracle.Oracle(BENCH, blobs)
+    prompts = [synthetic.token_ids(BENCH, n, seed=30 + n) for n in (64, 40, 17)]
+    seeds = [7, 8, 9]
+    got, kernels = run_group(rt, BENCH, dev, prompts, seeds, patches=4)
+    check_members(orc, prompts, seeds, got, 4)
+    # the estimator layers run once per Euler step for all members: a lone
+    # stream's patch is 947 kernels, 3 separate members would be 3 x 947
+    assert kernels < 2 * 947, kernels
+    dev.close()
+
+
+def test_group_orders_with_member_calls(rt):
+    """Member-stream calls queued around a group step see its results without a
+    group synchronize: the step waits for them and they wait for the step."""
+    blobs = synthetic.model_blobs(TINY, 0)
+    dev = rt.Device(TINY, 0, blobs)
+    prompts = [synthetic.token_ids(TINY, 7, seed=41), synthetic.token_ids(TINY, 9, seed=42)]
+    g = rt.Group(dev, 2, kv_capacity=64)
+    ref, _ = run_group(rt, TINY, dev, prompts, [3, 4], patches=3, timesteps=5)
+    for st, ids, seed in zip(g.streams, prompts, [3, 4]):
+        st.prefill(ids)
+        st.upload_noise(oracle.noise_table(seed, 3, TINY.latent))
+    for _ in range(3):
+        g.patch_step_async(30, 2.0, 5)
+    for m, st in enumerate(g.streams):  # no g.synchronize(): read_latents is ordered on the member stream
+        assert np.array_equal(st.latents(0, 3), ref[m])
+    g.close()
+    with pytest.raises(rt.VxcError):
+        rt.Group(dev, 5, kv_capacity=64)
+    dev.close()

@@ -319,7 +319,7 @@ constexpr int kDitMaxSeq = 16;
 __global__ void __launch_bounds__(128) dit_attention_split_kernel(const float* qkv, int seq, int q_heads,
                                                                   int kv_heads, const float* rope_cos,
                                                                   const float* rope_sin, float scale, __half* xb,
-                                                                  StreamCtl* ctl) {
+                                                                  StreamCtl* ctl, int lo) {
     constexpr int D = 64, H = 32;
     // q and k rows padded to 65 floats: the score loop reads 11 different rows per warp
     __shared__ float qs[kDitMaxSeq][D + 1], ks[kDitMaxSeq][D + 1], vs[kDitMaxSeq][D], ps[kDitMaxSeq][kDitMaxSeq + 1];
@@ -395,7 +395,7 @@ __global__ void __launch_bounds__(128) dit_attention_split_kernel(const float* q
         const int i = idx / D, e = idx - i * D;
         float acc = 0.f;
         for (int j = 0; j < seq; ++j) acc = fmaf(ps[i][j], vs[j][e], acc);
-        split_store(xb, ld, sq * seq + i, h * D + e, acc);
+        split_store(xb, ld, sq * seq + i, h * D + e, acc, lo);
     }
 }
 
@@ -810,15 +810,15 @@ void launch_rmsnorm_rows_split(const float* x, int ldx, const __half* g, float e
 
 void launch_dit_attention_split(const float* qkv, int nseq, int seq, int q_heads, int kv_heads, int d,
                                 const float* rope_cos, const float* rope_sin, float scale, __half* xb,
-                                StreamCtl* ctl, cudaStream_t s, bool pdl) {
-    if (d != 64 || seq > kDitMaxSeq || seq * 48 > 128 * 7 || nseq * seq > 24 ||
+                                StreamCtl* ctl, cudaStream_t s, bool pdl, int lo) {
+    if (d != 64 || seq > kDitMaxSeq || seq * 48 > 128 * 7 || nseq * seq > lo ||
         (reinterpret_cast<uintptr_t>(qkv) & 15) || (reinterpret_cast<uintptr_t>(rope_cos) & 15) ||
         (reinterpret_cast<uintptr_t>(rope_sin) & 15))
         throw std::invalid_argument("dit attention: unsupported shape");
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = make_cfg(dim3(q_heads, nseq), dim3(128), 0, s, pdl, attr);
     check_launch(cudaLaunchKernelEx(&cfg, dit_attention_split_kernel, qkv, seq, q_heads, kv_heads, rope_cos, rope_sin,
-                                    scale, xb, ctl));
+                                    scale, xb, ctl, lo));
 }
 
 void launch_embed_gather(const __half* table, const int32_t* ids, int M, int H, float scale,

@@ -564,6 +564,7 @@ void init_kernel_attributes() {
     init_tc_attributes();
     init_dit_layers_attributes();
     init_tc_rows_attributes();
+    init_tc_wide_attributes();
 }
 
 void launch_final_norm(const float* h, const __half* g, float eps, int H, float* out, float* out2,

@@ -147,7 +147,7 @@ void launch_rmsnorm_rows_split(const float* x, int ldx, const __half* g, float e
 // (head, sequence), from the fp32 q/k/v rows [nseq*seq][(hq+2hkv)d]:
 void launch_dit_attention_split(const float* qkv, int nseq, int seq, int q_heads, int kv_heads, int d,
                                 const float* rope_cos, const float* rope_sin, float scale, __half* xb,
-                                StreamCtl* ctl, cudaStream_t s, bool pdl);
+                                StreamCtl* ctl, cudaStream_t s, bool pdl, int lo = 24);
 
 // h[m] = table[ids[m]] * scale
 void launch_embed_gather(const __half* table, const int32_t* ids, int M, int H, float scale,
@@ -292,6 +292,28 @@ struct TcRowsArgs {
 };
 void launch_tc_rows(const CUtensorMap& map_a, const CUtensorMap& map_b, const TcRowsArgs& a, cudaStream_t s);
 void init_tc_rows_attributes();
+
+// Wide-token tcgen05 linear (the DiT of a group of streams): Y[m][r] for
+// m < M <= kWideTokens rows, K split across a cluster of 'splits' CTAs
+// (tc_wide.cu). The token operand is split fp16 [2 * kWideTokens][K] (map_b, box
+// rows 2 * kWideTokens): fp16(x) in rows 0.., the residuals in rows kWideTokens...
+constexpr int kWideTokens = 96;
+struct TcWideArgs {
+    int K = 0, M = 0, rows = 0;
+    int splits = 1;
+    int gateup = 0;            // out = SiLU(gate) * up, as split fp16 into yb [2 * kWideTokens][ldyb]
+    int resid = 0;             // y += rscale * out (else y = out)
+    float rscale = 1.f;
+    float* y = nullptr;        // fp32 [M][ldy]
+    int ldy = 0;
+    __half* yb = nullptr;
+    int ldyb = 0;
+    int stages = 2;            // shared-memory ring depth (1..4)
+    StreamCtl* ctl = nullptr;  // receives error 3 if a bounded wait gave up
+};
+void launch_tc_wide(const CUtensorMap& map_a, const CUtensorMap& map_b, const TcWideArgs& a, cudaStream_t s,
+                    bool pdl);
+void init_tc_wide_attributes();
 
 // Persistent DiT decoder (all layers of one estimator evaluation, one
 // cooperative launch, one CTA per SM; dit_persist.cu).

@@ -820,19 +820,34 @@ void enqueue_cfm(vxc_stream* s, const float* cond_dev, int T, float cfg) {
     }
 }
 
-// The whole patch iteration (synthesizer.cpp:546-658) on s->cs.
-void enqueue_patch(vxc_stream* s, int T, float cfg) {
+// The patch iteration before the sampler: noise and condition of this patch,
+// then dit_proj: mu = cat(lm_to_dit_proj(lm), res_to_dit_proj(res)).
+void enqueue_patch_pre(vxc_stream* s) {
     const vxc_device* dev = s->dev;
     const vxc_model_desc& d = dev->desc;
     const int H = d.hidden, Hd = d.dit_hidden, L = d.feat_dim * d.patch_size;
     launch_patch_begin(s->noise, s->latents, s->cond0, L, s->x, s->cond, s->ctl, s->cs, s->pdl);
-    // dit_proj: cat(lm_to_dit_proj(lm), res_to_dit_proj(res))
     const __half* dp = dev->blob[VXC_DIT_PROJ];
     const size_t dps = static_cast<size_t>(Hd) * H;
     launch_gemv(plain_gemv(dp, dp + dps, s->lm_h, H, Hd, s->mu, ACT_NONE, s->ctl, 0), s->cs, s->pdl);
     launch_gemv(plain_gemv(dp + dps + Hd, dp + 2 * dps + Hd, s->res_h, H, Hd, s->mu + Hd, ACT_NONE, s->ctl, 0),
                 s->cs, s->pdl);
+}
+
+// The whole patch iteration (synthesizer.cpp:546-658) on s->cs.
+void enqueue_patch_post(vxc_stream* s);
+void enqueue_patch(vxc_stream* s, int T, float cfg) {
+    enqueue_patch_pre(s);
     enqueue_cfm(s, s->cond, T, cfg);
+    enqueue_patch_post(s);
+}
+
+// The patch iteration after the sampler: the stop decision, feat_encoder, both
+// decoder steps, FSQ and fusion, and the latent's store.
+void enqueue_patch_post(vxc_stream* s) {
+    const vxc_device* dev = s->dev;
+    const vxc_model_desc& d = dev->desc;
+    const int H = d.hidden, L = d.feat_dim * d.patch_size;
     // stop head on the hidden state entering this patch
     const __half* sh = dev->blob[VXC_STOP_HEAD];
     launch_gemv(plain_gemv(sh, sh + static_cast<size_t>(H) * H, s->lm_h, H, H, s->mid, ACT_SILU, s->ctl, 0), s->cs,
@@ -1166,6 +1181,231 @@ vxc_stream::~vxc_stream() { free_all(this); }
 void vxc_internal_set_error(const char* msg) { g_last_error = msg; }
 
 // ==================================================================== C ABI ==
+// ------------------------------------------------------------- groups ----
+// A group of up to 4 streams whose patch steps run as one CUDA graph: each
+// member's decoder steps and small graphs on its own stream (forked branches),
+// and the 9 estimator evaluations of all members batched into one pass over
+// 22 rows per member, so every DiT weight byte is read once per group patch.
+constexpr int kGroupMax = kWideTokens / 22;
+
+struct vxc_group {
+    vxc_device* dev = nullptr;
+    std::vector<vxc_stream*> members;
+    std::mutex call_mutex;
+    float* gdh = nullptr;   // [22 n][Hd] residual stream of all members' DiT rows
+    float* gqkv = nullptr;  // [22 n][(Hq + 2 Hkv) d]
+    __half *xw_n = nullptr, *xw_a = nullptr, *xw_act = nullptr;  // [2 kWideTokens][K] split operands
+    CUtensorMap map_xw_n{}, map_xw_a{}, map_xw_act{};
+    int tc_target = 32;              // CTAs aimed at per wide linear (VXC_GROUP_TC_TARGET; 32 suits
+                                     // several groups at once, 148 a lone group's latency)
+    int tc_stages = 2;               // TMA ring depth of the wide linears (VXC_GROUP_TC_STAGES)
+    StreamCtl* gctl = nullptr;       // error reports of the batched linears
+    StreamCtl* gctl_host = nullptr;
+    std::vector<cudaEvent_t> events;  // fork / join points of the group graph
+    cudaGraphExec_t graph = nullptr;
+    int graph_T = -1;
+    float graph_cfg = 0.f;
+    int graph_kernels = 0;
+    ~vxc_group();
+};
+
+namespace {
+
+// The estimator layers over all members' rows (the split form: RMSNorm and
+// attention kernels around four wide tensor-core linears).
+void enqueue_group_layers(vxc_group* g) {
+    vxc_stream* s0 = g->members[0];
+    const vxc_device* dev = g->dev;
+    const vxc_model_desc& d = dev->desc;
+    const int n = static_cast<int>(g->members.size());
+    const int Hd = d.dit_hidden, F = d.dit_ffn, hq = d.dit_q_heads, hkv = d.dit_kv_heads, hd = Hd / hq;
+    const int seq = dit_tokens_per_seq(d.patch_size), M = 2 * seq * n;
+    const int W = (hq + 2 * hkv) * hd;
+    const float scale = 1.0f / std::sqrt(static_cast<float>(hd));
+    cudaStream_t cs = s0->cs;
+    const bool pdl = s0->pdl;
+    auto plan = [&](int tiles, int K) {
+        TcWideArgs a;
+        const int want = choose_splits(tiles, K, g->tc_target);
+        a.splits = want >= 8 ? 8 : want >= 4 ? 4 : want >= 2 ? 2 : 1;  // the wide kernel splits by powers of 2
+        a.stages = g->tc_stages;
+        a.M = M;
+        a.K = K;
+        a.ctl = g->gctl;
+        return a;
+    };
+    for (size_t l = 0; l < dev->dit.size(); ++l) {
+        const LayerW& L = dev->dit[l];
+        const std::array<CUtensorMap, 4>& maps = dev->dit_maps[l];
+        launch_rmsnorm_rows_split(g->gdh, Hd, L.in_norm, d.rms_eps, Hd, M, g->xw_n, nullptr, cs, pdl, kWideTokens);
+        TcWideArgs qa = plan(W / 128, Hd);
+        qa.rows = W;
+        qa.y = g->gqkv;
+        qa.ldy = W;
+        launch_tc_wide(maps[0], g->map_xw_n, qa, cs, pdl);
+        launch_dit_attention_split(g->gqkv, 2 * n, seq, hq, hkv, hd, dev->dit_rope_cos, dev->dit_rope_sin, scale,
+                                   g->xw_a, nullptr, cs, pdl, kWideTokens);
+        TcWideArgs oa = plan(Hd / 128, hq * hd);
+        oa.rows = Hd;
+        oa.resid = 1;
+        oa.rscale = d.dit_residual_scale;
+        oa.y = g->gdh;
+        oa.ldy = Hd;
+        launch_tc_wide(maps[1], g->map_xw_a, oa, cs, pdl);
+        launch_rmsnorm_rows_split(g->gdh, Hd, L.post_norm, d.rms_eps, Hd, M, g->xw_n, nullptr, cs, pdl,
+                                  kWideTokens);
+        TcWideArgs ga = plan(F / 64, Hd);
+        ga.rows = F;
+        ga.gateup = 1;
+        ga.yb = g->xw_act;
+        ga.ldyb = F;
+        launch_tc_wide(maps[2], g->map_xw_n, ga, cs, pdl);
+        TcWideArgs da = plan(Hd / 128, F);
+        da.rows = Hd;
+        da.resid = 1;
+        da.rscale = d.dit_residual_scale;
+        da.y = g->gdh;
+        da.ldy = Hd;
+        launch_tc_wide(maps[3], g->map_xw_act, da, cs, pdl);
+    }
+}
+
+// cfm_sample of every member at once (synthesizer.cpp:86-170): per step, each
+// member's input rows, the batched layers, then each member's output projection
+// with its own CFG-zero* scale and Euler update. Members whose stop flag is set
+// skip their embed and update.
+void enqueue_group_cfm(vxc_group* g, int T, float cfg) {
+    vxc_stream* s0 = g->members[0];
+    const vxc_device* dev = g->dev;
+    const vxc_model_desc& d = dev->desc;
+    const int Hd = d.dit_hidden, seq = dit_tokens_per_seq(d.patch_size);
+    const std::vector<float> dts = euler_dts(T);
+    const int z = zero_init_steps(T);
+    const float* tab = s0->ttab.at(T).dev;
+    const DitPtrs w = dit_ptrs(dev);
+    for (int step = 1; step <= T; ++step) {
+        if (step <= z) continue;  // zero-init steps leave x untouched (synthesizer.cpp:123-126)
+        for (size_t m = 0; m < g->members.size(); ++m) {
+            vxc_stream* s = g->members[m];
+            DitEmbedArgs e{};
+            e.in_w = w.in_w;
+            e.in_b = w.in_b;
+            e.cond_w = w.cond_w;
+            e.cond_b = w.cond_b;
+            e.x = s->x;
+            e.cond = s->cond;
+            e.mu = s->mu;
+            e.Hd = Hd;
+            e.D = d.feat_dim;
+            e.P = d.patch_size;
+            e.hidden = g->gdh + m * 2 * seq * static_cast<size_t>(Hd);
+            e.ctl = s->ctl;
+            e.tsum = tab + static_cast<size_t>(step) * Hd;
+            launch_dit_embed(e, s0->cs, s0->pdl);
+        }
+        enqueue_group_layers(g);
+        for (size_t m = 0; m < g->members.size(); ++m) {
+            vxc_stream* s = g->members[m];
+            DitOutArgs o{};
+            o.hidden = g->gdh + m * 2 * seq * static_cast<size_t>(Hd);
+            o.seq = seq;
+            o.Hd = Hd;
+            o.D = d.feat_dim;
+            o.P = d.patch_size;
+            o.norm_g = dev->dit_norm;
+            o.eps = d.rms_eps;
+            o.out_w = w.out_w;
+            o.out_b = w.out_b;
+            o.x = s->x;
+            o.dt = dts[step];
+            o.cfg = cfg;
+            o.ctl = s->ctl;
+            o.est_buf = s->dest;
+            o.counter = s->dcount;
+            launch_dit_out(o, s0->cs, s0->pdl);
+        }
+    }
+}
+
+// The members' streams join the capture on members[0]'s stream (fork) and it
+// waits for all of them (join); 'k' indexes the event pair used.
+void group_fork(vxc_group* g, int k) {
+    const int n = static_cast<int>(g->members.size());
+    cudaEvent_t ev = g->events[static_cast<size_t>(k) * (n + 1)];
+    ck(cudaEventRecord(ev, g->members[0]->cs), "fork");
+    for (int m = 1; m < n; ++m) ck(cudaStreamWaitEvent(g->members[m]->cs, ev, 0), "fork");
+}
+void group_join(vxc_group* g, int k) {
+    const int n = static_cast<int>(g->members.size());
+    for (int m = 1; m < n; ++m) {
+        cudaEvent_t ev = g->events[static_cast<size_t>(k) * (n + 1) + m];
+        ck(cudaEventRecord(ev, g->members[m]->cs), "join");
+        ck(cudaStreamWaitEvent(g->members[0]->cs, ev, 0), "join");
+    }
+}
+
+void capture_group_graph(vxc_group* g, int T, float cfg) {
+    time_table(g->members[0], T);  // the graph reads it; keep it current before every replay
+    if (g->graph && g->graph_T == T && g->graph_cfg == cfg) return;
+    if (g->graph) {
+        cudaGraphExecDestroy(g->graph);
+        g->graph = nullptr;
+    }
+    cudaStream_t c0 = g->members[0]->cs;
+    cudaGraph_t gr = nullptr;
+    ck(cudaStreamBeginCapture(c0, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+    try {
+        group_fork(g, 0);
+        for (vxc_stream* s : g->members) enqueue_patch_pre(s);
+        group_join(g, 0);
+        enqueue_group_cfm(g, T, cfg);
+        group_fork(g, 1);
+        for (vxc_stream* s : g->members) enqueue_patch_post(s);
+        group_join(g, 1);
+    } catch (...) {
+        cudaStreamEndCapture(c0, &gr);
+        if (gr) cudaGraphDestroy(gr);
+        throw;
+    }
+    ck(cudaStreamEndCapture(c0, &gr), "cudaStreamEndCapture");
+    size_t n_nodes = 0;
+    ck(cudaGraphGetNodes(gr, nullptr, &n_nodes), "cudaGraphGetNodes");
+    std::vector<cudaGraphNode_t> nodes(n_nodes);
+    if (n_nodes) ck(cudaGraphGetNodes(gr, nodes.data(), &n_nodes), "cudaGraphGetNodes");
+    int kernels = 0;
+    for (cudaGraphNode_t nd : nodes) {
+        cudaGraphNodeType t;
+        ck(cudaGraphNodeGetType(nd, &t), "cudaGraphNodeGetType");
+        if (t == cudaGraphNodeTypeKernel) ++kernels;
+    }
+    g->graph_kernels = kernels;
+    const cudaError_t e = cudaGraphInstantiate(&g->graph, gr, 0);
+    cudaGraphDestroy(gr);
+    ck(e, "cudaGraphInstantiate");
+    g->graph_T = T;
+    g->graph_cfg = cfg;
+}
+
+void free_group(vxc_group* g) {
+    if (g->graph) cudaGraphExecDestroy(g->graph);
+    g->graph = nullptr;
+    for (cudaEvent_t e : g->events)
+        if (e) cudaEventDestroy(e);
+    g->events.clear();
+    for (void* p : {static_cast<void*>(g->gdh), static_cast<void*>(g->gqkv), static_cast<void*>(g->xw_n),
+                    static_cast<void*>(g->xw_a), static_cast<void*>(g->xw_act), static_cast<void*>(g->gctl)})
+        if (p) cudaFree(p);
+    if (g->gctl_host) cudaFreeHost(g->gctl_host);
+    g->gdh = g->gqkv = nullptr;
+    g->xw_n = g->xw_a = g->xw_act = nullptr;
+    g->gctl = nullptr;
+    g->gctl_host = nullptr;
+}
+
+}  // namespace
+
+vxc_group::~vxc_group() = default;
+
 extern "C" {
 
 VXC_API uint32_t vxc_abi_version(void) { return VXC_ABI_VERSION; }
@@ -2191,6 +2431,137 @@ VXC_API int32_t vxc_stream_cuda_handle(vxc_stream* s, void** out) {
     return guard([&] {
         require(s != nullptr && out != nullptr, "null argument");
         *out = static_cast<void*>(s->cs);
+    });
+}
+
+VXC_API int32_t vxc_group_create(vxc_device* dev, int32_t n_streams, int32_t kv_capacity, vxc_group** out) {
+    return guard([&] {
+        require(dev != nullptr && out != nullptr, "device and out must not be null");
+        *out = nullptr;
+        require(n_streams >= 1 && n_streams <= kGroupMax, "a group holds 1 to 4 streams");
+        const vxc_model_desc& d = dev->desc;
+        require(dit_tokens_per_seq(d.patch_size) == 11 && d.dit_hidden / d.dit_q_heads == 64,
+                "groups need the 2 x 11-token DiT with 64-wide heads");
+        DeviceGuard g(dev->device);
+        auto grp = std::make_unique<vxc_group>();
+        grp->dev = dev;
+        if (const char* tt = std::getenv("VXC_GROUP_TC_TARGET")) {
+            grp->tc_target = std::atoi(tt);
+            require(grp->tc_target >= 1 && grp->tc_target <= 4096, "VXC_GROUP_TC_TARGET must be in [1, 4096]");
+        }
+        if (const char* st = std::getenv("VXC_GROUP_TC_STAGES")) {
+            grp->tc_stages = std::atoi(st);
+            require(grp->tc_stages >= 1 && grp->tc_stages <= 4, "VXC_GROUP_TC_STAGES must be in [1, 4]");
+        }
+        try {
+            for (int m = 0; m < n_streams; ++m) {
+                vxc_stream* s = nullptr;
+                if (vxc_stream_create(dev, kv_capacity, &s) != VXC_STATUS_OK)
+                    throw std::runtime_error(std::string("group member: ") + g_last_error);
+                grp->members.push_back(s);
+            }
+            const size_t Hd = d.dit_hidden, F = d.dit_ffn, Q = static_cast<size_t>(d.dit_q_heads) * 64;
+            const size_t W = static_cast<size_t>(d.dit_q_heads + 2 * d.dit_kv_heads) * 64;
+            const size_t M = 22 * static_cast<size_t>(n_streams);
+            grp->gdh = dev_alloc<float>(M * Hd);
+            grp->gqkv = dev_alloc<float>(M * W);
+            grp->xw_n = dev_alloc<__half>(2 * kWideTokens * Hd);
+            grp->xw_a = dev_alloc<__half>(2 * kWideTokens * Q);
+            grp->xw_act = dev_alloc<__half>(2 * kWideTokens * F);
+            ck(cudaMemset(grp->xw_n, 0, 2 * kWideTokens * Hd * sizeof(__half)), "cudaMemset");
+            ck(cudaMemset(grp->xw_a, 0, 2 * kWideTokens * Q * sizeof(__half)), "cudaMemset");
+            ck(cudaMemset(grp->xw_act, 0, 2 * kWideTokens * F * sizeof(__half)), "cudaMemset");
+            grp->map_xw_n = make_tensor_map_f16(grp->xw_n, 2 * kWideTokens, static_cast<int>(Hd), 2 * kWideTokens);
+            grp->map_xw_a = make_tensor_map_f16(grp->xw_a, 2 * kWideTokens, static_cast<int>(Q), 2 * kWideTokens);
+            grp->map_xw_act = make_tensor_map_f16(grp->xw_act, 2 * kWideTokens, static_cast<int>(F), 2 * kWideTokens);
+            grp->gctl = dev_alloc<StreamCtl>(1);
+            ck(cudaMemset(grp->gctl, 0, sizeof(StreamCtl)), "cudaMemset");
+            ck(cudaMallocHost(&grp->gctl_host, sizeof(StreamCtl)), "cudaMallocHost");
+            grp->events.assign(3 * static_cast<size_t>(n_streams + 1), nullptr);
+            for (auto& e : grp->events) ck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+        } catch (...) {
+            free_group(grp.get());
+            for (vxc_stream* s : grp->members) vxc_stream_destroy(s);
+            throw;
+        }
+        *out = grp.release();
+    });
+}
+
+VXC_API void vxc_group_destroy(vxc_group* g) {
+    if (!g) return;
+    {
+        std::lock_guard<std::mutex> lk(g->call_mutex);
+        DeviceGuard dg(g->dev->device, true);
+        if (!g->members.empty()) cudaStreamSynchronize(g->members[0]->cs);
+        free_group(g);
+    }
+    for (vxc_stream* s : g->members) vxc_stream_destroy(s);
+    delete g;
+}
+
+VXC_API int32_t vxc_group_stream(vxc_group* g, int32_t member, vxc_stream** out) {
+    return guard([&] {
+        require(g != nullptr && out != nullptr, "null argument");
+        require(member >= 0 && member < static_cast<int>(g->members.size()), "member index out of range");
+        *out = g->members[static_cast<size_t>(member)];
+    });
+}
+
+VXC_API int32_t vxc_group_patch_step_async(vxc_group* g, int32_t min_patches, float cfg_value, int32_t timesteps) {
+    return guard([&] {
+        require(g != nullptr, "group must not be null");
+        std::lock_guard<std::mutex> lk(g->call_mutex);
+        std::vector<std::unique_lock<std::mutex>> locks;
+        for (vxc_stream* s : g->members) locks.emplace_back(s->call_mutex);
+        DeviceGuard dg(g->dev->device);
+        for (vxc_stream* s : g->members) {
+            check_patch_preconditions(s, timesteps);
+            set_min_patches(s, min_patches);
+        }
+        capture_group_graph(g, timesteps, cfg_value);
+        // The graph runs on members[0]'s stream: it waits for work queued on the
+        // other members' streams (noise uploads ...), and their later calls wait for it.
+        const size_t n = g->members.size(), base = 2 * (n + 1);
+        cudaStream_t c0 = g->members[0]->cs;
+        for (size_t m = 1; m < n; ++m) {
+            ck(cudaEventRecord(g->events[base + m], g->members[m]->cs), "group order");
+            ck(cudaStreamWaitEvent(c0, g->events[base + m], 0), "group order");
+        }
+        ck(cudaGraphLaunch(g->graph, c0), "cudaGraphLaunch");
+        ck(cudaEventRecord(g->events[base], c0), "group order");
+        for (size_t m = 1; m < n; ++m) ck(cudaStreamWaitEvent(g->members[m]->cs, g->events[base], 0), "group order");
+        for (vxc_stream* s : g->members) {  // host mirrors advance optimistically; read_state re-syncs them
+            s->patches += 1;
+            s->kv_len[0] += 1;
+            s->kv_len[1] += 1;
+        }
+    });
+}
+
+VXC_API int32_t vxc_group_synchronize(vxc_group* g) {
+    return guard([&] {
+        require(g != nullptr, "group must not be null");
+        std::lock_guard<std::mutex> lk(g->call_mutex);
+        DeviceGuard dg(g->dev->device);
+        ck(cudaStreamSynchronize(g->members[0]->cs), "cudaStreamSynchronize");
+        ck(cudaMemcpy(g->gctl_host, g->gctl, sizeof(StreamCtl), cudaMemcpyDeviceToHost), "group ctl");
+        if (g->gctl_host->error != 0) {
+            g->gctl_host->error = 0;
+            cudaMemcpy(&g->gctl->error, &g->gctl_host->error, sizeof(int), cudaMemcpyHostToDevice);
+            throw std::runtime_error("a tensor-core pipeline wait timed out in the group's estimator");
+        }
+        for (vxc_stream* s : g->members) {
+            std::lock_guard<std::mutex> sl(s->call_mutex);
+            sync_ctl(s);
+        }
+    });
+}
+
+VXC_API int32_t vxc_group_graph_kernels(vxc_group* g, int32_t* out) {
+    return guard([&] {
+        require(g != nullptr && out != nullptr, "null argument");
+        *out = g->graph_kernels;
     });
 }
 

@@ -1,0 +1,347 @@
+// tcgen05 linear over a wide token block: up to kWideTokens = 96 rows, for the
+// DiT estimator of a group of streams evaluated together (DitEstimator.decoder,
+// tools/export_components.py:625-659, over 22 rows per stream).
+//
+// The weight tile is the MMA A operand (128 output features, K-major, 128-byte
+// swizzle, TMA); the token rows are the B operand, fp16(x) in rows 0..95 and
+// fp16(x - fp16(x)) in rows 96..191 of each K chunk. Both halves accumulate into
+// the same 96 fp32 TMEM columns (two N = 96 MMAs per K step), so the
+// accumulator already holds W (x_hi + x_lo). K is split across a thread-block
+// cluster of 1, 2, 4 or 8 CTAs: after the MMAs each CTA pushes its partials,
+// token-major, to the CTA that owns those output features (a warp's store is
+// one contiguous run in the owner's shared memory), one cluster barrier, then
+// the owner sums the partials in rank order and writes the epilogue: plain,
+// residual (y += rscale * v), or SiLU(gate) * up into the next linear's split
+// operand (residual half at row offset 96).
+//
+// Shared memory never drops below kFloor, so an SM holds at most two of these
+// CTAs (2 x 128 TMEM columns) and no 24-token linear beside them: the SM's 512
+// TMEM columns are never oversubscribed, and a cluster CTA never waits for TMEM.
+// Every wait is bounded; on timeout the kernel records error 3, still passes the
+// cluster barrier, drains its loads and frees its TMEM.
+#include <cuda.h>
+
+#include <algorithm>
+#include <stdexcept>
+#include <string>
+
+#include "kernels.cuh"
+#include "tc_common.cuh"
+
+namespace vxc {
+namespace {
+
+using namespace tc;
+
+constexpr int kThreads = 128;
+constexpr int kN = kWideTokens;                       // MMA N: hi and lo rows share the columns
+constexpr int kLoBytes = kWideTokens * kKChunk * 2;   // offset of the lo rows in a B tile (12 KiB)
+constexpr int kBTile = 2 * kLoBytes;                  // 24 KiB
+constexpr int kStage = kABytes + kBTile;              // 40 KiB (1 KiB aligned)
+constexpr int kMaxRing = 4;
+constexpr int kTmem = 128;
+constexpr size_t kRecvBytes = static_cast<size_t>(kTileRows) * kWideTokens * 4;  // 48 KiB
+constexpr size_t kFloor = 92 * 1024;
+
+void check_launch(cudaError_t e) {
+    if (e != cudaSuccess) throw std::runtime_error(std::string("tc_wide: ") + cudaGetErrorString(e));
+}
+
+__device__ __forceinline__ void cluster_barrier() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// The receive buffer lives in the (then idle) stage area when the CTA has no
+// K split and the stage area is large enough for it.
+__host__ __device__ constexpr bool recv_in_stages(int splits, int stages) {
+    return splits == 1 && static_cast<size_t>(stages) * kStage >= kRecvBytes;
+}
+
+// S = K split (cluster size): a template parameter so the partial sums unroll.
+template <int S>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_wide_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                   const TcWideArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    __shared__ uint64_t full_bar[kMaxRing], empty_bar[kMaxRing], done_bar;
+    __shared__ uint32_t tmem_base_s;
+    __shared__ int failed_s;
+
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int split = blockIdx.x, tile = blockIdx.y, M = a.M;
+    // 1 KiB aligned, derived from smem_raw by pointer arithmetic so that the
+    // compiler keeps shared-memory addressing for everything carved from it
+    uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    const int nch = a.K / kKChunk;
+    const int c0 = split * nch / S, c1 = (split + 1) * nch / S, cs = c1 - c0;
+    const int stages = min(a.stages, max(cs, 1));
+    // the receive buffer offset is the same in every CTA of the cluster
+    const int stage_area = min(a.stages, max((nch + S - 1) / S, 1));
+    const int r0 = a.gateup ? tile * 64 : tile * kTileRows;
+    const int r1 = a.gateup ? a.rows + tile * 64 : tile * kTileRows + 64;
+    const int pre = min(stages, cs);
+    int issued[kMaxRing];
+
+    if (tid == 0) {
+        for (int i = 0; i < stages; ++i) {
+            mbar_init(&full_bar[i], 1);
+            mbar_init(&empty_bar[i], 1);
+        }
+        mbar_init(&done_bar, 1);
+        failed_s = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b)) : "memory");
+#pragma unroll
+        for (int i = 0; i < kMaxRing; ++i) issued[i] = 0;
+        // weights first: they depend on no earlier kernel
+        for (int i = 0; i < pre; ++i) {
+            uint8_t* st = smem + i * kStage;
+            mbar_expect_tx(&full_bar[i], kStage);
+            tma_load_2d(st, &map_a, (c0 + i) * kKChunk, r0, &full_bar[i]);
+            tma_load_2d(st + kABytes / 2, &map_a, (c0 + i) * kKChunk, r1, &full_bar[i]);
+            issued[i] = 1;
+        }
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_addr(&tmem_base_s)), "r"(kTmem)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = tmem_base_s;
+    pdl_launch_dependents();
+
+    if (tid == 0) {
+        pdl_wait();
+        for (int i = 0; i < pre; ++i)
+            tma_load_2d(smem + i * kStage + kABytes, &map_b, (c0 + i) * kKChunk, 0, &full_bar[i]);
+        for (int i = pre; i < cs; ++i) {
+            const int s = i % stages;
+            if (!mbar_wait(&empty_bar[s], ((i / stages) - 1) & 1)) {
+                failed_s = 1;
+                break;
+            }
+            uint8_t* st = smem + s * kStage;
+            mbar_expect_tx(&full_bar[s], kStage);
+            tma_load_2d(st, &map_a, (c0 + i) * kKChunk, r0, &full_bar[s]);
+            tma_load_2d(st + kABytes / 2, &map_a, (c0 + i) * kKChunk, r1, &full_bar[s]);
+            tma_load_2d(st + kABytes, &map_b, (c0 + i) * kKChunk, 0, &full_bar[s]);
+            issued[s] += 1;
+        }
+    } else if (tid == 32) {
+        pdl_wait();
+        const uint32_t idesc = umma_idesc(kTileRows, kN);
+        for (int i = 0; i < cs; ++i) {
+            const int s = i % stages;
+            if (!mbar_wait(&full_bar[s], (i / stages) & 1)) {
+                failed_s = 1;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t sa = smem_addr(smem + s * kStage), sb = sa + kABytes;
+#pragma unroll
+            for (int kk = 0; kk < kKChunk / 16; ++kk) {
+                umma_f16(tmem, umma_desc(sa + kk * 32), umma_desc(sb + kk * 32), idesc, (i | kk) != 0);
+                umma_f16(tmem, umma_desc(sa + kk * 32), umma_desc(sb + kLoBytes + kk * 32), idesc, 1);
+            }
+            umma_commit(&empty_bar[s]);
+        }
+        umma_commit(&done_bar);
+    } else {
+        pdl_wait();
+    }
+
+    const bool ok = mbar_wait(&done_bar, 0);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (!ok) failed_s = 1;
+    // output features of the tile: 128 (or 64 gate + 64 up); CTA p of the
+    // cluster owns features [p nu, (p + 1) nu) of each half
+    const int units = a.gateup ? 64 : kTileRows, halves = a.gateup ? 2 : 1;
+    const int nu = units / S;
+    const bool local_recv = recv_in_stages(S, stages);
+    if (tid == 0) {
+        // no copy may still be landing in this CTA's shared memory (bounded when something failed)
+        for (int i = 0; i < stages; ++i)
+            if (issued[i] > 0 && !mbar_wait(&full_bar[i], (issued[i] - 1) & 1)) failed_s = 1;
+    }
+    __syncthreads();
+    float v[kWideTokens];  // this thread's accumulator row: output feature tid, token rows 0..M-1
+    {
+        const uint32_t lanes = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+        if (ok) {
+#pragma unroll
+            for (int c = 0; c < kWideTokens; c += 16)
+                if (c < M) tmem_ld16(lanes + c, v + c);
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        } else {
+#pragma unroll
+            for (int m = 0; m < kWideTokens; ++m) v[m] = 0.f;
+        }
+    }
+    if (S == 1 && !a.gateup) {
+        // no split, one feature per thread: straight from registers, coalesced
+        // across the warp (consecutive features of one token row)
+        float* yc = a.y + tile * kTileRows + tid;
+#pragma unroll
+        for (int mb = 0; mb < kWideTokens; mb += 16) {
+            if (mb < M) {
+                float r[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    r[j] = (a.resid && mb + j < M) ? yc[static_cast<size_t>(mb + j) * a.ldy] : 0.f;
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (mb + j < M)
+                        yc[static_cast<size_t>(mb + j) * a.ldy] =
+                            a.resid ? r[j] + (a.rscale == 1.f ? v[mb + j] : v[mb + j] * a.rscale) : v[mb + j];
+            }
+        }
+    } else {
+        // partials, token-major per owner: recv[((p * halves + half) * M + m) * nu + lu]
+        float* recv = reinterpret_cast<float*>(local_recv ? smem : smem + static_cast<size_t>(stage_area) * kStage);
+        {
+            const int u = a.gateup ? (tid & 63) : tid, half = a.gateup ? (tid >> 6) : 0;
+            const int owner = u / nu, lu = u - owner * nu;
+            float* dst = recv + static_cast<size_t>((split * halves + half) * M) * nu + lu;
+            if (owner == split) {
+#pragma unroll
+                for (int m = 0; m < kWideTokens; ++m)
+                    if (m < M) dst[m * nu] = v[m];
+            } else {
+                uint32_t remote;
+                asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+                             : "=r"(remote)
+                             : "r"(smem_addr(dst)), "r"(static_cast<uint32_t>(owner)));
+#pragma unroll
+                for (int m = 0; m < kWideTokens; ++m)
+                    if (m < M)
+                        asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote + 4u * m * nu), "f"(v[m])
+                                     : "memory");
+            }
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        if (S > 1) cluster_barrier();  // every partial has landed in its owner's buffer
+        else __syncthreads();
+        // this CTA's features: thread -> (feature lu, token rows m0, m0 + per, ...);
+        // each batch issues all its loads before any of its stores
+        const int per = kThreads / nu, lu = tid % nu, m0 = tid / nu;
+        const int col = split * nu + lu;
+        if (a.gateup) {
+            constexpr int kBatch = 4;
+            const size_t ocol = static_cast<size_t>(tile) * 64 + col;
+            for (int mb = m0; mb < M; mb += per * kBatch) {
+                float g[kBatch][S], up[kBatch][S];
+#pragma unroll
+                for (int j = 0; j < kBatch; ++j) {
+                    const int m = min(mb + j * per, M - 1);
+#pragma unroll
+                    for (int p = 0; p < S; ++p) {
+                        g[j][p] = recv[static_cast<size_t>((p * 2 + 0) * M + m) * nu + lu];
+                        up[j][p] = recv[static_cast<size_t>((p * 2 + 1) * M + m) * nu + lu];
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < kBatch; ++j) {
+                    const int m = mb + j * per;
+                    if (m < M) {
+                        float gs = 0.f, us = 0.f;
+#pragma unroll
+                        for (int p = 0; p < S; ++p) {
+                            gs += g[j][p];
+                            us += up[j][p];
+                        }
+                        const float o = silu(gs) * us;
+                        const __half h = __float2half_rn(o);
+                        a.yb[static_cast<size_t>(m) * a.ldyb + ocol] = h;
+                        a.yb[static_cast<size_t>(kWideTokens + m) * a.ldyb + ocol] =
+                            __float2half_rn(o - __half2float(h));
+                    }
+                }
+            }
+        } else {
+            constexpr int kBatch = 8;
+            float* yc = a.y + tile * kTileRows + col;
+            for (int mb = m0; mb < M; mb += per * kBatch) {
+                float part[kBatch][S], r[kBatch];
+#pragma unroll
+                for (int j = 0; j < kBatch; ++j) {
+                    const int m = mb + j * per;
+                    const int mc = min(m, M - 1);
+#pragma unroll
+                    for (int p = 0; p < S; ++p) part[j][p] = recv[static_cast<size_t>(p * M + mc) * nu + lu];
+                    r[j] = (a.resid && m < M) ? yc[static_cast<size_t>(m) * a.ldy] : 0.f;
+                }
+#pragma unroll
+                for (int j = 0; j < kBatch; ++j) {
+                    const int m = mb + j * per;
+                    if (m < M) {
+                        float s = 0.f;
+#pragma unroll
+                        for (int p = 0; p < S; ++p) s += part[j][p];
+                        yc[static_cast<size_t>(m) * a.ldy] = a.resid ? r[j] + (a.rscale == 1.f ? s : s * a.rscale) : s;
+                    }
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (tid == 0 && failed_s && a.ctl) a.ctl->error = 3;
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmem) : "memory");
+}
+
+size_t smem_bytes(int K, int splits, int stages_cap) {
+    const int nch = K / kKChunk;
+    const int cs = (nch + splits - 1) / splits;
+    const int stages = std::min(stages_cap, std::max(cs, 1));
+    size_t bytes = static_cast<size_t>(stages) * kStage + 1024;
+    if (!recv_in_stages(splits, stages)) bytes += kRecvBytes;  // (unused by an unsplit plain/residual launch)
+    return std::max(bytes, kFloor);
+}
+
+}  // namespace
+
+void launch_tc_wide(const CUtensorMap& map_a, const CUtensorMap& map_b, const TcWideArgs& a, cudaStream_t s,
+                    bool pdl) {
+    if (a.K % kKChunk != 0 || a.K <= 0) throw std::invalid_argument("tc_wide: K must be a multiple of 64");
+    if (a.M <= 0 || a.M > kWideTokens) throw std::invalid_argument("tc_wide: 1..96 token rows");
+    if ((a.splits != 1 && a.splits != 2 && a.splits != 4 && a.splits != 8) || a.splits > a.K / kKChunk)
+        throw std::invalid_argument("tc_wide: splits must be 1, 2, 4 or 8 and at most K / 64");
+    if (a.stages < 1 || a.stages > kMaxRing) throw std::invalid_argument("tc_wide: stages in [1, 4]");
+    if ((a.gateup ? a.rows % 64 : a.rows % kTileRows) != 0) throw std::invalid_argument("tc_wide: rows");
+    const int n_tiles = a.gateup ? a.rows / 64 : a.rows / kTileRows;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.splits, n_tiles);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem_bytes(a.K, a.splits, a.stages);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = a.splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
+    switch (a.splits) {
+        case 1: check_launch(cudaLaunchKernelEx(&cfg, tc_wide_kernel<1>, map_a, map_b, a)); break;
+        case 2: check_launch(cudaLaunchKernelEx(&cfg, tc_wide_kernel<2>, map_a, map_b, a)); break;
+        case 4: check_launch(cudaLaunchKernelEx(&cfg, tc_wide_kernel<4>, map_a, map_b, a)); break;
+        default: check_launch(cudaLaunchKernelEx(&cfg, tc_wide_kernel<8>, map_a, map_b, a)); break;
+    }
+}
+
+void init_tc_wide_attributes() {
+    size_t most = kFloor;
+    for (int sp = 1; sp <= 8; ++sp) most = std::max(most, smem_bytes(64 * kMaxRing * sp, sp, kMaxRing));
+    for (const void* f : {reinterpret_cast<const void*>(tc_wide_kernel<1>), reinterpret_cast<const void*>(tc_wide_kernel<2>),
+                          reinterpret_cast<const void*>(tc_wide_kernel<4>), reinterpret_cast<const void*>(tc_wide_kernel<8>)})
+        check_launch(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(most)));
+}
+
+}  // namespace vxc

@@ -100,6 +100,12 @@ def _signatures():
         "vxc_profile_kernel": ([vp, i, i, C.POINTER(f), C.POINTER(C.c_double)], i),
         "vxc_profile_kernel_concurrent": ([C.POINTER(vp), i, i, i, C.POINTER(f), C.POINTER(C.c_double)], i),
         "vxc_stream_cuda_handle": ([vp, C.POINTER(vp)], i),
+        "vxc_group_create": ([vp, i, i, C.POINTER(vp)], i),
+        "vxc_group_destroy": ([vp], None),
+        "vxc_group_stream": ([vp, i, C.POINTER(vp)], i),
+        "vxc_group_patch_step_async": ([vp, i, f, i], i),
+        "vxc_group_synchronize": ([vp], i),
+        "vxc_group_graph_kernels": ([vp, C.POINTER(i)], i),
     }
 
 
@@ -179,10 +185,23 @@ class Stream:
         h = C.c_void_p()
         _check(lib().vxc_stream_create(device._h, kv_capacity, C.byref(h)))
         self._h = h
+        self._owned = True
+
+    @classmethod
+    def _member(cls, device: Device, handle: C.c_void_p, kv_capacity: int) -> "Stream":
+        """A view of a stream owned by a Group (closing it does not free it)."""
+        st = cls.__new__(cls)
+        st.dev = device
+        st.cfg = device.cfg
+        st.cap = kv_capacity
+        st._h = handle
+        st._owned = False
+        return st
 
     def close(self) -> None:
         if getattr(self, "_h", None):
-            lib().vxc_stream_destroy(self._h)
+            if self._owned:
+                lib().vxc_stream_destroy(self._h)
             self._h = None
 
     def __del__(self):
@@ -329,6 +348,47 @@ class Stream:
         h = C.c_void_p()
         _check(lib().vxc_stream_cuda_handle(self._h, C.byref(h)))
         return h.value or 0
+
+
+class Group:
+    """Up to 4 streams stepped together: one CUDA graph per group patch, with the
+    estimator evaluations of all members batched into one pass over the DiT
+    weights. Members are ordinary streams (prefill, noise, state, latents)."""
+
+    def __init__(self, device: Device, n_streams: int, kv_capacity: int = 1024):
+        self.dev = device
+        h = C.c_void_p()
+        _check(lib().vxc_group_create(device._h, n_streams, kv_capacity, C.byref(h)))
+        self._h = h
+        self.streams = []
+        for m in range(n_streams):
+            sh = C.c_void_p()
+            _check(lib().vxc_group_stream(self._h, m, C.byref(sh)))
+            self.streams.append(Stream._member(device, sh, kv_capacity))
+
+    def patch_step_async(self, min_patches: int, cfg_value: float = 2.0, timesteps: int = 10) -> None:
+        _check(lib().vxc_group_patch_step_async(self._h, min_patches, cfg_value, timesteps))
+
+    def synchronize(self) -> None:
+        _check(lib().vxc_group_synchronize(self._h))
+
+    def graph_kernels(self) -> int:
+        n = C.c_int32()
+        _check(lib().vxc_group_graph_kernels(self._h, C.byref(n)))
+        return int(n.value)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            for st in self.streams:
+                st._h = None
+            lib().vxc_group_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # interpreter shutdown: module globals may already be gone
+            pass
 
 
 def sdpa(q, k, v, mask=None, past_k=None, past_v=None, scale: float = 0.0, want_cache: bool = False):
