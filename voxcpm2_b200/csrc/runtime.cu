@@ -540,14 +540,20 @@ int choose_splits(int tiles, int k, int target = 148) {
     return std::max(1, std::min({8, chunks, want}));
 }
 
+// The tensor-core kernels split K over 1, 2, 4 or 8 CTAs.
+int pow2_floor(int v) { return v >= 8 ? 8 : v >= 4 ? 4 : v >= 2 ? 2 : 1; }
+int pow2_ceil(int v) { return v <= 1 ? 1 : v <= 2 ? 2 : v <= 4 ? 4 : 8; }
+
 // K split and ring depth of one tensor-core launch: about one CTA per SM, and
 // with an operand built in shared memory (fused) one stage per K chunk.
 TcLinearArgs tc_plan(const vxc_stream* s, int tiles, int K, bool fused_b) {
     TcLinearArgs a;
     const int nch = K / 64;
-    a.splits = choose_splits(tiles, K, s->tc_target);
+    a.splits = pow2_floor(choose_splits(tiles, K, s->tc_target));
     a.max_stages = s->tc_stages;
-    if (fused_b) a.splits = std::min(std::min(8, nch), std::max(a.splits, (nch + a.max_stages - 1) / a.max_stages));
+    if (fused_b)
+        a.splits = std::min(pow2_floor(std::min(8, nch)),
+                            pow2_ceil(std::max(a.splits, (nch + a.max_stages - 1) / a.max_stages)));
     return a;
 }
 
@@ -1226,8 +1232,7 @@ void enqueue_group_layers(vxc_group* g) {
     const bool pdl = s0->pdl;
     auto plan = [&](int tiles, int K) {
         TcWideArgs a;
-        const int want = choose_splits(tiles, K, g->tc_target);
-        a.splits = want >= 8 ? 8 : want >= 4 ? 4 : want >= 2 ? 2 : 1;  // the wide kernel splits by powers of 2
+        a.splits = pow2_floor(choose_splits(tiles, K, g->tc_target));
         a.stages = g->tc_stages;
         a.M = M;
         a.K = K;

@@ -29,6 +29,8 @@
 #include <algorithm>
 #include <cfloat>
 #include <stdexcept>
+#include <type_traits>
+#include <vector>
 
 #include "kernels.cuh"
 #include "tc_common.cuh"
@@ -41,7 +43,7 @@ using namespace tc;
 constexpr int kTcThreads = 128;
 constexpr int kStageBytes = kABytes + kBBytes;    // 22 KiB, keeps 1 KiB alignment
 constexpr int kMaxStages = 8;
-constexpr int kRowFloats = 25;      // exchange-buffer row stride: 24 tokens + 1 (odd: conflict-free reads)
+constexpr int kRecvFloats = kTileRows * kLoOffset;  // split-K receive buffer: every partial of one tile
 constexpr int kTmemCols = 64;
 
 // Zero token rows M..23 (and their residual rows) of 'cs' B tiles.
@@ -236,7 +238,9 @@ __host__ __device__ constexpr bool recv_in_stage_area(bool b_tma, int splits, bo
 
 // BM: where the token operand comes from (TC_B_TMA / TC_B_NORM / TC_B_ATTN); one
 // instantiation each, so the TMA form does not carry the builders' registers.
-template <int BM>
+// S: the K split (cluster size, 1, 2, 4 or 8), a template parameter so that the
+// rank-order sums of the partials unroll and their loads issue together.
+template <int BM, int S>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_linear_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                      const TcLinearArgs a) {
@@ -249,8 +253,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int split = blockIdx.x, tile = blockIdx.y;
-    const int S = a.splits;
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // 1 KiB aligned, derived from smem_raw by pointer arithmetic so that the
+    // compiler keeps shared-memory addressing for everything carved from it
+    uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     constexpr bool b_tma = BM == TC_B_TMA;
 
     const int nch = a.K / kKChunk;
@@ -350,9 +355,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if constexpr (BM == TC_B_NORM) {
             build_b_norm(smem, a, c0, cs, inv_s, red_s);
         } else {
-            const int slice_rows = max((kTileRows + S - 1) / S, 2 * ((64 + S - 1) / S));
             float* scratch = reinterpret_cast<float*>(smem + static_cast<size_t>(stage_area) * kStageBytes) +
-                             S * slice_rows * kRowFloats;
+                             kRecvFloats;
             build_b_attn(smem, a, c0, cs, a.attn_round, scratch);
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic-proxy writes -> tensor core
@@ -364,25 +368,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const bool ok = mbar_wait(&done_bar, 0);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (!ok) failed_s = 1;
-    // Split-K exchange by push: each CTA stores its partial rows straight into the
-    // receive buffer of the CTA that owns them (non-blocking remote stores), one
-    // cluster barrier, then owners sum the splits in rank order (deterministic).
-    // Owner slices: tile units (rows, or gate/up pairs) [o * units / S, (o+1) * units / S).
-    const int units = a.gateup ? 64 : kTileRows;
-    const int slice = (units + S - 1) / S;
-    const int halves = a.gateup ? 2 : 1;
-    // Without a K split the receive buffer lives in the (then idle) stage area: the
-    // CTA needs no extra shared memory, so more CTAs of concurrent streams fit on an SM.
-    const bool recv_in_stages = recv_in_stage_area(b_tma, S, a.ssq_out != nullptr);
-    float* recv = reinterpret_cast<float*>(recv_in_stages ? smem : smem + static_cast<size_t>(stage_area) * kStageBytes);
-    if (recv_in_stages) {
-        if (tid == 0) {
-            // every load has landed before the stage area is reused (bounded when something failed)
-            for (int i = 0; i < stages; ++i)
-                if (issued[i] > 0 && !mbar_wait(&full_bar[i], (issued[i] - 1) & 1)) failed_s = 1;
-        }
-        __syncthreads();
-    }
+    // Output units of the tile: 128 rows, or 64 gate/up pairs; CTA p of the cluster
+    // owns units [p nu, (p + 1) nu). Each thread holds one accumulator row
+    // (tile row tid): v[m] = hi + lo columns of token m.
+    const int units = a.gateup ? 64 : kTileRows, halves = a.gateup ? 2 : 1;
+    const int nu = units / S;
+    float v[kLoOffset];
     {
         float d[kBRows];
         if (ok) {
@@ -395,57 +386,120 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
             for (int i = 0; i < kBRows; ++i) d[i] = 0.f;
         }
-        const int row = warp * 32 + lane;
-        const int u = a.gateup ? (row & 63) : row, half = a.gateup ? (row >> 6) : 0;
-        int owner = 0;
-        while (owner + 1 < S && u >= (owner + 1) * units / S) ++owner;
-        const int lu = u - owner * units / S;
-        float* dst = recv + ((split * slice + lu) * halves + half) * kRowFloats;
-        if (S == 1) {
 #pragma unroll
-            for (int m = 0; m < kLoOffset; ++m)
-                if (m < a.M) dst[m] = d[m] + d[kLoOffset + m];
-        } else {
-            const uint32_t remote = peer_addr(dst, owner);
-#pragma unroll
-            for (int m = 0; m < kLoOffset; ++m)
-                if (m < a.M) st_peer(remote + 4 * m, d[m] + d[kLoOffset + m]);
-        }
+        for (int m = 0; m < kLoOffset; ++m) v[m] = d[m] + d[kLoOffset + m];
     }
-    if (tid == 0 && !recv_in_stages) {
-        // no copy may still be landing in this CTA's shared memory when it moves on
-        // (a no-op when every stage was consumed; bounded when something failed)
+    if (tid == 0) {
+        // no copy may still be landing in this CTA's shared memory when it is reused
+        // or the CTA exits (a no-op when every stage was consumed; bounded when something failed)
         for (int i = 0; i < stages; ++i)
             if (issued[i] > 0 && !mbar_wait(&full_bar[i], (issued[i] - 1) & 1)) failed_s = 1;
     }
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-    if (S > 1) cluster_sync();  // every partial has landed in its owner's buffer
-    else __syncthreads();
-    const int u0 = split * units / S, nu = (split + 1) * units / S - u0;
-    float* sq = reinterpret_cast<float*>(smem);  // the stage area is idle now: squares of updated rows
-    for (int it = tid; it < nu * a.M; it += kTcThreads) {
-        const int m = it / nu, lu = it - m * nu;
-        if (a.gateup) {
-            float g = 0.f, up = 0.f;
-            for (int p = 0; p < S; ++p) {
-                g += recv[((p * slice + lu) * 2 + 0) * kRowFloats + m];
-                up += recv[((p * slice + lu) * 2 + 1) * kRowFloats + m];
+    if (S == 1 && !a.gateup && !a.ssq_out) {
+        // no split: straight from registers, coalesced across the warp
+        float* yc = a.y + tile * kTileRows + tid;
+        float r[kLoOffset];
+#pragma unroll
+        for (int m = 0; m < kLoOffset; ++m) r[m] = (a.resid && m < a.M) ? yc[static_cast<size_t>(m) * a.ldy] : 0.f;
+#pragma unroll
+        for (int m = 0; m < kLoOffset; ++m)
+            if (m < a.M)
+                yc[static_cast<size_t>(m) * a.ldy] = a.resid ? r[m] + (a.rscale == 1.f ? v[m] : v[m] * a.rscale) : v[m];
+        __syncthreads();
+    } else {
+        // Split-K exchange by push: each CTA stores its partials straight into the
+        // receive buffer of the CTA that owns them (non-blocking remote stores),
+        // token-major so that a warp's store is one contiguous run; one cluster
+        // barrier; then owners sum the splits in rank order (deterministic).
+        // recv[((p * halves + half) * M + m) * nu + lu]. Without a K split it lives in
+        // the (then idle) stage area, so more CTAs of concurrent streams fit on an SM.
+        const bool recv_in_stages = recv_in_stage_area(b_tma, S, a.ssq_out != nullptr);
+        float* recv =
+            reinterpret_cast<float*>(recv_in_stages ? smem : smem + static_cast<size_t>(stage_area) * kStageBytes);
+        __syncthreads();  // the stage area is idle
+        {
+            const int u = a.gateup ? (tid & 63) : tid, half = a.gateup ? (tid >> 6) : 0;
+            const int owner = u / nu, lu = u - owner * nu;
+            float* dst = recv + static_cast<size_t>((split * halves + half) * a.M) * nu + lu;
+            if (owner == split) {
+#pragma unroll
+                for (int m = 0; m < kLoOffset; ++m)
+                    if (m < a.M) dst[m * nu] = v[m];
+            } else {
+                const uint32_t remote = peer_addr(dst, owner);
+#pragma unroll
+                for (int m = 0; m < kLoOffset; ++m)
+                    if (m < a.M) st_peer(remote + 4u * m * nu, v[m]);
             }
-            store_split(a.yb, a.ldyb, m, tile * 64 + u0 + lu, silu(g) * up);
-        } else {
-            float v = 0.f;
-            for (int p = 0; p < S; ++p) v += recv[(p * slice + lu) * kRowFloats + m];
-            float* y = a.y + static_cast<size_t>(m) * a.ldy + tile * kTileRows + u0 + lu;
-            const float nv = a.resid ? *y + (a.rscale == 1.f ? v : v * a.rscale) : v;
-            *y = nv;
-            if (a.ssq_out) sq[m * nu + lu] = nv * nv;
         }
-    }
-    __syncthreads();
-    if (a.ssq_out && tid < a.M) {  // this owner's part of each row's sum of squares, fixed order
-        float t = 0.f;
-        for (int lu = 0; lu < nu; ++lu) t += sq[tid * nu + lu];
-        a.ssq_out[(tile * S + split) * kSsqStride + tid] = t;
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        if (S > 1) cluster_sync();  // every partial has landed in its owner's buffer
+        else __syncthreads();
+        // this CTA's units: thread -> (unit lu, token rows m0, m0 + per, ...);
+        // each batch issues all its loads before any of its stores
+        const int per = kTcThreads / nu, lu = tid % nu, m0 = tid / nu;
+        const int col = split * nu + lu;
+        float* sq = reinterpret_cast<float*>(smem);  // the stage area is idle now: squares of updated rows
+        if (a.gateup) {
+            constexpr int kBatch = 4;
+            for (int mb = m0; mb < a.M; mb += per * kBatch) {
+                float g[kBatch][S], up[kBatch][S];
+#pragma unroll
+                for (int j = 0; j < kBatch; ++j) {
+                    const int mc = min(mb + j * per, a.M - 1);
+#pragma unroll
+                    for (int p = 0; p < S; ++p) {
+                        g[j][p] = recv[static_cast<size_t>((p * 2 + 0) * a.M + mc) * nu + lu];
+                        up[j][p] = recv[static_cast<size_t>((p * 2 + 1) * a.M + mc) * nu + lu];
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < kBatch; ++j) {
+                    const int m = mb + j * per;
+                    if (m < a.M) {
+                        float gs = 0.f, us = 0.f;
+#pragma unroll
+                        for (int p = 0; p < S; ++p) {
+                            gs += g[j][p];
+                            us += up[j][p];
+                        }
+                        store_split(a.yb, a.ldyb, m, tile * 64 + col, silu(gs) * us);
+                    }
+                }
+            }
+        } else {
+            constexpr int kBatch = 8;
+            float* yc = a.y + tile * kTileRows + col;
+            for (int mb = m0; mb < a.M; mb += per * kBatch) {
+                float part[kBatch][S], r[kBatch];
+#pragma unroll
+                for (int j = 0; j < kBatch; ++j) {
+                    const int m = mb + j * per;
+                    const int mc = min(m, a.M - 1);
+#pragma unroll
+                    for (int p = 0; p < S; ++p) part[j][p] = recv[static_cast<size_t>(p * a.M + mc) * nu + lu];
+                    r[j] = (a.resid && m < a.M) ? yc[static_cast<size_t>(m) * a.ldy] : 0.f;
+                }
+#pragma unroll
+                for (int j = 0; j < kBatch; ++j) {
+                    const int m = mb + j * per;
+                    if (m < a.M) {
+                        float sum = 0.f;
+#pragma unroll
+                        for (int p = 0; p < S; ++p) sum += part[j][p];
+                        const float nv = a.resid ? r[j] + (a.rscale == 1.f ? sum : sum * a.rscale) : sum;
+                        yc[static_cast<size_t>(m) * a.ldy] = nv;
+                        if (a.ssq_out) sq[m * nu + lu] = nv * nv;
+                    }
+                }
+            }
+        }
+        __syncthreads();
+        if (a.ssq_out && tid < a.M) {  // this owner's part of each row's sum of squares, fixed order
+            float t = 0.f;
+            for (int l = 0; l < nu; ++l) t += sq[tid * nu + l];
+            a.ssq_out[(tile * S + split) * kSsqStride + tid] = t;
+        }
     }
     if (tid == 0 && failed_s && a.ctl) a.ctl->error = 3;
     if (warp == 1)
@@ -461,19 +515,42 @@ size_t tc_linear_smem_bytes(int K, int splits, int bmode, int attn_round, int ma
     const int stages = std::min(std::min(max_stages, kMaxStages), std::max(cs, 1));
     const size_t stage_bytes = static_cast<size_t>(stages) * kStageBytes;
     if (recv_in_stage_area(bmode == TC_B_TMA, splits, ssq_out)) return stage_bytes + 1024;  // + alignment slack
-    // receive buffer: per source split, an owner slice of rows (or of gate/up pairs, 2 rows each)
-    const size_t slice_rows = std::max((128 + splits - 1) / splits, 2 * ((64 + splits - 1) / splits));
-    const size_t recv_bytes = static_cast<size_t>(splits) * slice_rows * kRowFloats * sizeof(float);
+    const size_t recv_bytes = static_cast<size_t>(kRecvFloats) * sizeof(float);
     const size_t scratch = bmode == TC_B_ATTN ? static_cast<size_t>(attn_round) * kAttnHeadFloats * sizeof(float) : 0;
     return stage_bytes + recv_bytes + scratch + 1024;  // + alignment slack
+}
+
+template <int BM>
+cudaError_t launch_split(cudaLaunchConfig_t& cfg, const CUtensorMap& map_a, const CUtensorMap& map_b,
+                         const TcLinearArgs& a) {
+    switch (a.splits) {
+        case 1: return cudaLaunchKernelEx(&cfg, tc_linear_kernel<BM, 1>, map_a, map_b, a);
+        case 2: return cudaLaunchKernelEx(&cfg, tc_linear_kernel<BM, 2>, map_a, map_b, a);
+        case 4: return cudaLaunchKernelEx(&cfg, tc_linear_kernel<BM, 4>, map_a, map_b, a);
+        default: return cudaLaunchKernelEx(&cfg, tc_linear_kernel<BM, 8>, map_a, map_b, a);
+    }
+}
+
+// every instantiation (token-operand mode x split)
+std::vector<const void*> tc_linear_kernels() {
+    std::vector<const void*> k;
+    auto add = [&k](auto bm) {
+        constexpr int B = decltype(bm)::value;
+        k.push_back(reinterpret_cast<const void*>(tc_linear_kernel<B, 1>));
+        k.push_back(reinterpret_cast<const void*>(tc_linear_kernel<B, 2>));
+        k.push_back(reinterpret_cast<const void*>(tc_linear_kernel<B, 4>));
+        k.push_back(reinterpret_cast<const void*>(tc_linear_kernel<B, 8>));
+    };
+    add(std::integral_constant<int, TC_B_TMA>{});
+    add(std::integral_constant<int, TC_B_NORM>{});
+    add(std::integral_constant<int, TC_B_ATTN>{});
+    return k;
 }
 
 size_t dyn_limit() {
     if (!g_dyn_limit) {
         size_t most = 0;
-        for (const void* f : {reinterpret_cast<const void*>(tc_linear_kernel<TC_B_TMA>),
-                              reinterpret_cast<const void*>(tc_linear_kernel<TC_B_NORM>),
-                              reinterpret_cast<const void*>(tc_linear_kernel<TC_B_ATTN>)}) {
+        for (const void* f : tc_linear_kernels()) {
             cudaFuncAttributes fa{};
             const cudaError_t e = cudaFuncGetAttributes(&fa, f);
             if (e != cudaSuccess) throw std::runtime_error(std::string("tc_linear attributes: ") + cudaGetErrorString(e));
@@ -492,8 +569,8 @@ void launch_tc_linear(const CUtensorMap& map_a, const CUtensorMap& map_b, const 
                       bool pdl) {
     if (a.K % kKChunk != 0 || a.K <= 0) throw std::invalid_argument("tc_linear: K must be a multiple of 64");
     if (a.M <= 0 || a.M > kLoOffset) throw std::invalid_argument("tc_linear: at most 24 token rows");
-    if (a.splits < 1 || a.splits > 8 || a.splits > a.K / kKChunk || a.M > kRowFloats)
-        throw std::invalid_argument("tc_linear: splits must be in [1, 8] and at most K / 64");
+    if ((a.splits != 1 && a.splits != 2 && a.splits != 4 && a.splits != 8) || a.splits > a.K / kKChunk)
+        throw std::invalid_argument("tc_linear: splits must be 1, 2, 4 or 8 and at most K / 64");
     const int n_tiles = a.gateup ? a.rows / 64 : a.rows / kTileRows;
     if ((a.gateup ? a.rows % 64 : a.rows % kTileRows) != 0) throw std::invalid_argument("tc_linear: rows");
     if (a.bmode != TC_B_TMA) {
@@ -526,18 +603,15 @@ void launch_tc_linear(const CUtensorMap& map_a, const CUtensorMap& map_b, const 
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
-    const cudaError_t e =
-        a.bmode == TC_B_TMA ? cudaLaunchKernelEx(&cfg, tc_linear_kernel<TC_B_TMA>, map_a, map_b, a)
-        : a.bmode == TC_B_NORM ? cudaLaunchKernelEx(&cfg, tc_linear_kernel<TC_B_NORM>, map_a, map_b, a)
-                               : cudaLaunchKernelEx(&cfg, tc_linear_kernel<TC_B_ATTN>, map_a, map_b, a);
+    const cudaError_t e = a.bmode == TC_B_TMA    ? launch_split<TC_B_TMA>(cfg, map_a, map_b, a)
+                          : a.bmode == TC_B_NORM ? launch_split<TC_B_NORM>(cfg, map_a, map_b, a)
+                                                 : launch_split<TC_B_ATTN>(cfg, map_a, map_b, a);
     if (e != cudaSuccess) throw std::runtime_error(std::string("tc_linear launch: ") + cudaGetErrorString(e));
 }
 
 void init_tc_attributes() {
     // every launch checks its own need against this limit
-    for (const void* f : {reinterpret_cast<const void*>(tc_linear_kernel<TC_B_TMA>),
-                          reinterpret_cast<const void*>(tc_linear_kernel<TC_B_NORM>),
-                          reinterpret_cast<const void*>(tc_linear_kernel<TC_B_ATTN>)}) {
+    for (const void* f : tc_linear_kernels()) {
         const cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                    static_cast<int>(dyn_limit()));
         if (e != cudaSuccess) throw std::runtime_error(std::string("tc_linear attribute: ") + cudaGetErrorString(e));
