@@ -79,6 +79,15 @@ def profiled_value(name: str, key: str):
     return None
 
 
+def dit_patch_bytes(cfg) -> float:
+    """Algorithmic HBM bytes of the estimator weights one patch reads (9 evaluations,
+    fp16, without the cached time MLPs)."""
+    from voxcpm2_b200.config import DIT_ESTIMATOR, component_count
+    hd = cfg.dit_hidden
+    evals = TIMESTEPS - max(1, int((TIMESTEPS + 1) * 0.04))
+    return 2.0 * evals * (component_count(cfg, DIT_ESTIMATOR) - 4 * (hd * hd + hd))
+
+
 def patch_bytes(cfg, kv_tokens: float) -> float:
     """Algorithmic HBM bytes of one patch: every weight the patch reads once (fp16:
     one base and one residual decoder step, 9 DiT estimator evaluations without the
@@ -248,7 +257,8 @@ def job_rate(world: int, streams_per_gpu: int, steps: int, seconds: float) -> fl
 
 
 # --------------------------------------------------------------- GPU arm ---
-def group_rate(rt, synthetic, dev, cfg, groups, members, K, W, min_patches, rank, barrier, max_over_ranks, world):
+def group_rate(rt, synthetic, dev, cfg, groups, members, K, W, min_patches, rank, barrier, max_over_ranks, world,
+               peak):
     """Device-resident patches/s of `groups` stream groups of `members` streams each
     (every member its own prompt and noise), timed like the headline; plus the
     device time of one group patch with the other groups idle."""
@@ -299,8 +309,14 @@ def group_rate(rt, synthetic, dev, cfg, groups, members, K, W, min_patches, rank
     kernels = gs[0].graph_kernels()
     for g in gs:
         g.close()
+    value = world * groups * members * K / (ms / 1e3)
+    # a group patch reads the estimator weights once for all its members
+    bpp = patch_bytes(cfg, TEXT_TOKENS + 1 + W + K / 2) - dit_patch_bytes(cfg) * (members - 1) / members
     return {"groups_per_gpu": groups, "members": members, "streams_per_gpu": groups * members,
-            "value": world * groups * members * K / (ms / 1e3), "unit": "patches/s", "ms_per_step": ms / K,
+            "value": value, "unit": "patches/s", "ms_per_step": ms / K,
+            "hbm_job": {"bytes_per_patch": bpp, "achieved": value * bpp / 1e9, "peak": peak, "unit": "GB/s",
+                        "frac": value * bpp / 1e9 / peak,
+                        "note": "algorithmic bytes per member patch (estimator weights shared by the group)"},
             "group_patch_ms": float(np.median(lat)), "kernels_per_group_patch": kernels,
             "gpu_launches": groups * K * kernels,
             "note": "each group steps its members as one CUDA graph; the 9 estimator evaluations of all "
@@ -405,6 +421,14 @@ def run_ours(args):
     for k in ("dit_qkv", "dit_o", "dit_down", "base_qkv", "base_attn", "base_gateup", "base_down"):
         km, kb = streams[0].profile_kernel(k, 50)
         kernels[k] = {"us": round(1e3 * km, 2), "GB/s": round(kb / (km / 1e3) / 1e9, 1)}
+    # one whole KV-cache decode step at batch 1 (configs 2 and 3: every weight of the
+    # decoder once + the K/V rows), replayed as a graph at the stream's KV length
+    decode_step = {}
+    for k, name in (("base_step", "base_decoder"), ("res_step", "residual_decoder")):
+        km, kb = streams[0].profile_kernel(k, 50)
+        gbs = kb / (km / 1e3) / 1e9
+        decode_step[name] = {"us": round(1e3 * km, 2), "bytes": kb, "GB/s": round(gbs, 1), "frac": gbs / peak,
+                             "kv_rows": TEXT_TOKENS + 1 + W + K}
 
     # ---- prefill of the 64-token prompt (65 rows through both decoders; synchronous call)
     one = streams[0]
@@ -471,7 +495,7 @@ def run_ours(args):
     group = None
     if args.groups > 0:
         group = group_rate(rt, synthetic, dev, cfg, args.groups, args.group_members, K, W, min_patches, rank,
-                           barrier, max_over_ranks, world)
+                           barrier, max_over_ranks, world, peak)
 
     # ---- CPU baseline: the oracle port on this host, bounded sample (rank 0, N = 1)
     cpu = None
@@ -494,6 +518,7 @@ def run_ours(args):
             "per_gpu_patches_per_s": value / world,
             "e2e": {"value": e2e_value, "unit": "patches/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": graph_kernels * S * K, "roofline": roofline, "hbm_job": hbm_job, "kernels": kernels,
+            "decode_step": decode_step,
             "cpu_baseline": cpu, "clocks": clk, "group": group,
         }
         print(json.dumps(line), flush=True)

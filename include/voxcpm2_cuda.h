@@ -113,6 +113,8 @@ enum {
     VXC_PROF_BASE_ATTN = 6,    /* base decoder flash-decode attention */
     VXC_PROF_DIT_O = 7,        /* DiT attention + o projection + residual */
     VXC_PROF_DIT_LAYERS = 8,   /* persistent DiT decoder: all layers of one evaluation (one launch) */
+    VXC_PROF_BASE_STEP = 9,    /* one whole base decoder KV-cache step (24 layers + final norm) */
+    VXC_PROF_RES_STEP = 10,    /* one whole residual decoder KV-cache step */
 };
 
 /* Progress callback of vxc_generate: return non-zero to continue, zero to cancel

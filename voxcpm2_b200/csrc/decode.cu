@@ -32,88 +32,10 @@ __device__ __forceinline__ float gemv_input(const GemvArgs& a, int k) {
     return a.x[k];
 }
 
-template <int MODE, int MAXCH, int RPW>
-__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
-    extern __shared__ float xs[];
-    __shared__ float red[kGemvWarps];
-    pdl_launch_dependents();
-
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int item = blockIdx.x * kGemvWarps + warp;
-    const bool active = item < a.rows;
-    const int K = a.K;
-
-    // rows owned by this warp
-    int row[RPW];
-    if constexpr (MODE == GEMV_GATEUP) {
-        row[0] = item;
-        row[1] = item + a.rows;
-    } else if constexpr (MODE == GEMV_QKV) {
-        const int half = a.head_dim >> 1;
-        const int hh = item / half, j = item - hh * half;
-        row[0] = hh * a.head_dim + j;
-        row[1] = row[0] + half;
-    } else {
-#pragma unroll
-        for (int r = 0; r < RPW; ++r) row[r] = item * RPW + r;
-    }
-
-    // 1) stream this warp's weight rows into registers (independent of inputs)
-    uint4 wr[RPW][MAXCH];
-#pragma unroll
-    for (int r = 0; r < RPW; ++r) {
-        const __half* wrow = a.w + static_cast<size_t>(row[r]) * K;
-#pragma unroll
-        for (int c = 0; c < MAXCH; ++c) {
-            const int e = (c * kWarp + lane) * 8;
-            wr[r][c] = (active && e < K) ? ld_stream(wrow + e) : make_uint4(0, 0, 0, 0);
-        }
-    }
-
-    // 2) wait for the producer of the input vector
-    pdl_wait();
-    if (a.skip_if_stopped && a.ctl && a.ctl->stopped) return;
-
-    // 3) stage the (optionally RMS-normalised) input in shared memory
-    float ss = 0.f;
-    for (int k = threadIdx.x; k < K; k += kGemvThreads) {
-        const float v = gemv_input(a, k);
-        ss += v * v;
-        xs[k] = a.norm_g ? v * __half2float(a.norm_g[k]) : v;
-    }
-    float inv_rms = 1.f;
-    if (a.norm_g) {
-        ss = warp_sum(ss);
-        if (lane == 0) red[warp] = ss;
-        __syncthreads();
-        float t = 0.f;
-#pragma unroll
-        for (int w = 0; w < kGemvWarps; ++w) t += red[w];
-        inv_rms = rsqrtf(t / static_cast<float>(K) + a.eps);
-    } else {
-        __syncthreads();
-    }
-    if (!active) return;
-
-    // 4) dot products
-    float acc[RPW];
-#pragma unroll
-    for (int r = 0; r < RPW; ++r) acc[r] = 0.f;
-#pragma unroll
-    for (int c = 0; c < MAXCH; ++c) {
-        const int e = (c * kWarp + lane) * 8;
-        if (e < K) {
-            const float4 x0 = *reinterpret_cast<const float4*>(&xs[e]);
-            const float4 x1 = *reinterpret_cast<const float4*>(&xs[e + 4]);
-#pragma unroll
-            for (int r = 0; r < RPW; ++r) acc[r] = dot8(wr[r][c], x0, x1, acc[r]);
-        }
-    }
-#pragma unroll
-    for (int r = 0; r < RPW; ++r) acc[r] = warp_sum(acc[r]) * inv_rms;
-    if (lane != 0) return;
-
-    // 5) epilogue
+// Epilogue of one GEMV output unit (lane 0 of its warp): bias / activation,
+// residual update, SiLU(gate) * up, or RoPE + KV append for q/k/v.
+template <int MODE, int RPW>
+__device__ __forceinline__ void gemv_store(const GemvArgs& a, int item, const int* row, const float* acc) {
     if constexpr (MODE == GEMV_PLAIN) {
 #pragma unroll
         for (int r = 0; r < RPW; ++r) {
@@ -158,6 +80,122 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
     }
 }
 
+template <int MODE, int MAXCH, int RPW>
+__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
+    extern __shared__ float xs[];
+    __shared__ float red[kGemvWarps];
+    pdl_launch_dependents();
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int item = blockIdx.x * kGemvWarps + warp;
+    const bool active = item < a.rows;
+    const int K = a.K;
+
+    // rows owned by this warp
+    int row[RPW];
+    if constexpr (MODE == GEMV_GATEUP) {
+        row[0] = item;
+        row[1] = item + a.rows;
+    } else if constexpr (MODE == GEMV_QKV) {
+        const int half = a.head_dim >> 1;
+        const int hh = item / half, j = item - hh * half;
+        row[0] = hh * a.head_dim + j;
+        row[1] = row[0] + half;
+    } else {
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) row[r] = item * RPW + r;
+    }
+
+    // 1) stream this warp's weight rows into registers (independent of inputs)
+    uint4 wr[RPW][MAXCH];
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+        const __half* wrow = a.w + static_cast<size_t>(row[r]) * K;
+#pragma unroll
+        for (int c = 0; c < MAXCH; ++c) {
+            const int e = (c * kWarp + lane) * 8;
+            wr[r][c] = (active && e < K) ? ld_stream(wrow + e) : make_uint4(0, 0, 0, 0);
+        }
+    }
+
+    // 2) wait for the producer of the input vector
+    pdl_wait();
+    if (a.skip_if_stopped && a.ctl && a.ctl->stopped) return;
+
+    // 3) stage the (optionally RMS-normalised) input in shared memory. A plain
+    // input is read as float4 (and its gain as 4 x fp16), every load of the thread
+    // issued before any is used: one L2 round trip instead of a chain of them.
+    float ss = 0.f;
+    const bool vec = a.in_mode == IN_PLAIN && (K & 3) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(a.norm_g) & 7) == 0;
+    if (vec) {
+        constexpr int kV = MAXCH >= 2 ? MAXCH / 2 : 1;  // float4 per thread: K <= 256 MAXCH
+        const int n4 = K >> 2;
+        float4 xv[kV];
+        uint2 gv[kV];
+#pragma unroll
+        for (int j = 0; j < kV; ++j) {
+            const int i = threadIdx.x + j * kGemvThreads;
+            xv[j] = i < n4 ? reinterpret_cast<const float4*>(a.x)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+            gv[j] = (a.norm_g && i < n4) ? reinterpret_cast<const uint2*>(a.norm_g)[i] : make_uint2(0u, 0u);
+        }
+#pragma unroll
+        for (int j = 0; j < kV; ++j) {
+            const int i = threadIdx.x + j * kGemvThreads;
+            if (i < n4) {
+                float4 v = xv[j];
+                ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                if (a.norm_g) {
+                    const float2 g01 = __half22float2(*reinterpret_cast<const __half2*>(&gv[j].x));
+                    const float2 g23 = __half22float2(*reinterpret_cast<const __half2*>(&gv[j].y));
+                    v = make_float4(v.x * g01.x, v.y * g01.y, v.z * g23.x, v.w * g23.y);
+                }
+                reinterpret_cast<float4*>(xs)[i] = v;
+            }
+        }
+    } else {
+        for (int k = threadIdx.x; k < K; k += kGemvThreads) {
+            const float v = gemv_input(a, k);
+            ss += v * v;
+            xs[k] = a.norm_g ? v * __half2float(a.norm_g[k]) : v;
+        }
+    }
+    float inv_rms = 1.f;
+    if (a.norm_g) {
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        float t = 0.f;
+#pragma unroll
+        for (int w = 0; w < kGemvWarps; ++w) t += red[w];
+        inv_rms = rsqrtf(t / static_cast<float>(K) + a.eps);
+    } else {
+        __syncthreads();
+    }
+    if (!active) return;
+
+    // 4) dot products
+    float acc[RPW];
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) acc[r] = 0.f;
+#pragma unroll
+    for (int c = 0; c < MAXCH; ++c) {
+        const int e = (c * kWarp + lane) * 8;
+        if (e < K) {
+            const float4 x0 = *reinterpret_cast<const float4*>(&xs[e]);
+            const float4 x1 = *reinterpret_cast<const float4*>(&xs[e + 4]);
+#pragma unroll
+            for (int r = 0; r < RPW; ++r) acc[r] = dot8(wr[r][c], x0, x1, acc[r]);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) acc[r] = warp_sum(acc[r]) * inv_rms;
+    if (lane != 0) return;
+
+    // 5) epilogue
+    gemv_store<MODE, RPW>(a, item, row, acc);
+}
+
 cudaLaunchConfig_t make_cfg(dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
                             cudaLaunchAttribute* attr) {
     cudaLaunchConfig_t cfg = {};
@@ -189,6 +227,192 @@ void dispatch_gemv(const GemvArgs& a, cudaStream_t s, bool pdl) {
     else if (nch <= 8) check_launch(cudaLaunchKernelEx(&cfg, gemv_kernel<MODE, 8, RPW>, a));
     else if (RPW == 1 && nch <= 16) check_launch(cudaLaunchKernelEx(&cfg, gemv_kernel<MODE, 16, 1>, a));
     else throw std::invalid_argument("gemv: input dimension too large");
+}
+
+// ------------------------------------------------------------ bulk GEMV ---
+// The decoder-step form of the GEMV: at most one block per SM, each block's
+// weight rows copied into shared memory by the bulk-copy engine
+// (cp.async.bulk, completing on an mbarrier) BEFORE the dependency wait. A block
+// holds no weights in registers, so the next kernel of the chain fits on the
+// SM beside it and its copies stream while this one computes: HBM reads run
+// ahead of the dependent chain instead of starting when a kernel starts.
+constexpr int kBulkThreads = 256;
+constexpr int kBulkWarps = kBulkThreads / kWarp;
+constexpr int kBulkBlocks = 148;
+constexpr size_t kBulkSmemMax = 180 * 1024;
+
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+        "l"(src), "r"(bytes), "r"(static_cast<uint32_t>(__cvta_generic_to_shared(bar)))
+        : "memory");
+}
+
+// Bounded wait for phase 0 of a one-shot mbarrier; false on timeout.
+__device__ __forceinline__ bool bulk_wait(uint64_t* bar) {
+    const uint32_t addr = static_cast<uint32_t>(__cvta_generic_to_shared(bar));
+    for (uint32_t i = 0; i < (1u << 22); ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(addr)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+// Weight rows per output unit: gate + up, or the two rows of a RoPE pair.
+template <int MODE>
+constexpr int bulk_rows() {
+    return (MODE == GEMV_GATEUP || MODE == GEMV_QKV) ? 2 : 1;
+}
+
+// Output units [blockIdx.x * upb, + upb) of a.rows; IN_PLAIN input only.
+template <int MODE>
+__global__ void __launch_bounds__(kBulkThreads) gemv_bulk_kernel(const GemvArgs a, int upb) {
+    constexpr int R = bulk_rows<MODE>();
+    extern __shared__ __align__(16) uint8_t bulk_sm[];
+    __shared__ uint64_t bar;
+    __shared__ float red[kBulkWarps];
+    pdl_launch_dependents();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int K = a.K;
+    const int u0 = blockIdx.x * upb, nu = max(min(upb, a.rows - u0), 0);
+    const size_t rowb = static_cast<size_t>(K) * 2;
+    __half* ws = reinterpret_cast<__half*>(bulk_sm);  // [R * upb][K]
+    float* xs = reinterpret_cast<float*>(bulk_sm + static_cast<size_t>(R) * upb * rowb);
+
+    // 1) this block's weight rows into shared memory (independent of earlier kernels)
+    if (tid == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(&bar)))
+                     : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        if (nu > 0) {
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
+                             static_cast<uint32_t>(__cvta_generic_to_shared(&bar))),
+                         "r"(static_cast<uint32_t>(R * nu * rowb))
+                         : "memory");
+            if constexpr (MODE == GEMV_GATEUP) {
+                bulk_g2s(ws, a.w + static_cast<size_t>(u0) * K, static_cast<uint32_t>(nu * rowb), &bar);
+                bulk_g2s(ws + static_cast<size_t>(upb) * K, a.w + static_cast<size_t>(a.rows + u0) * K,
+                         static_cast<uint32_t>(nu * rowb), &bar);
+            } else if constexpr (MODE == GEMV_QKV) {
+                const int half = a.head_dim >> 1;
+                for (int i = 0; i < nu; ++i) {
+                    const int p = u0 + i, hh = p / half, j = p - hh * half;
+                    const size_t r0 = static_cast<size_t>(hh) * a.head_dim + j;
+                    bulk_g2s(ws + static_cast<size_t>(2 * i) * K, a.w + r0 * K, static_cast<uint32_t>(rowb), &bar);
+                    bulk_g2s(ws + static_cast<size_t>(2 * i + 1) * K, a.w + (r0 + half) * K,
+                             static_cast<uint32_t>(rowb), &bar);
+                }
+            } else {
+                bulk_g2s(ws, a.w + static_cast<size_t>(u0) * K, static_cast<uint32_t>(nu * rowb), &bar);
+            }
+        }
+    }
+    __syncthreads();  // the barrier is initialised before anyone waits on it
+
+    // 2) wait for the producer of the input vector
+    pdl_wait();
+    const bool stopped = a.skip_if_stopped && a.ctl && a.ctl->stopped;
+
+    // 3) the (optionally RMS-normalised) input: float4 loads, all issued at once
+    float inv_rms = 1.f;
+    if (!stopped) {
+        float ss = 0.f;
+        const int n4 = K >> 2;
+        constexpr int kV = 4;  // K <= 4096
+        float4 xv[kV];
+        uint2 gv[kV];
+#pragma unroll
+        for (int j = 0; j < kV; ++j) {
+            const int i = tid + j * kBulkThreads;
+            xv[j] = i < n4 ? reinterpret_cast<const float4*>(a.x)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+            gv[j] = (a.norm_g && i < n4) ? reinterpret_cast<const uint2*>(a.norm_g)[i] : make_uint2(0u, 0u);
+        }
+#pragma unroll
+        for (int j = 0; j < kV; ++j) {
+            const int i = tid + j * kBulkThreads;
+            if (i < n4) {
+                float4 v = xv[j];
+                ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                if (a.norm_g) {
+                    const float2 g01 = __half22float2(*reinterpret_cast<const __half2*>(&gv[j].x));
+                    const float2 g23 = __half22float2(*reinterpret_cast<const __half2*>(&gv[j].y));
+                    v = make_float4(v.x * g01.x, v.y * g01.y, v.z * g23.x, v.w * g23.y);
+                }
+                reinterpret_cast<float4*>(xs)[i] = v;
+            }
+        }
+        if (a.norm_g) {
+            ss = warp_sum(ss);
+            if (lane == 0) red[warp] = ss;
+        }
+        __syncthreads();
+        if (a.norm_g) {
+            float t = 0.f;
+#pragma unroll
+            for (int w = 0; w < kBulkWarps; ++w) t += red[w];
+            inv_rms = rsqrtf(t / static_cast<float>(K) + a.eps);
+        }
+    }
+
+    // 4) the weights have landed (every thread waits: none may read early, and the
+    // block may not exit with a copy in flight; bounded)
+    const bool ok = nu == 0 || bulk_wait(&bar);
+    if (!ok && tid == 0 && a.ctl) a.ctl->error = 3;
+    if (stopped || !ok) return;
+
+    // 5) dot products: warp w takes units w, w + 8, ...
+    for (int i = warp; i < nu; i += kBulkWarps) {
+        const __half* w0 = ws + static_cast<size_t>(MODE == GEMV_QKV ? 2 * i : i) * K;
+        const __half* w1 = MODE == GEMV_GATEUP ? ws + static_cast<size_t>(upb + i) * K : w0 + K;
+        float acc[2] = {0.f, 0.f};
+        for (int e = lane * 8; e < K; e += kWarp * 8) {
+            const float4 x0 = *reinterpret_cast<const float4*>(&xs[e]);
+            const float4 x1 = *reinterpret_cast<const float4*>(&xs[e + 4]);
+            acc[0] = dot8(*reinterpret_cast<const uint4*>(w0 + e), x0, x1, acc[0]);
+            if (R == 2) acc[1] = dot8(*reinterpret_cast<const uint4*>(w1 + e), x0, x1, acc[1]);
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) acc[r] = warp_sum(acc[r]) * inv_rms;
+        if (lane == 0) {
+            const int item = u0 + i;
+            int row[2];
+            if constexpr (MODE == GEMV_GATEUP) {
+                row[0] = item;
+                row[1] = item + a.rows;
+            } else if constexpr (MODE == GEMV_QKV) {
+                const int half = a.head_dim >> 1;
+                const int hh = item / half, j = item - hh * half;
+                row[0] = hh * a.head_dim + j;
+                row[1] = row[0] + half;
+            } else {
+                row[0] = item;
+                row[1] = item;
+            }
+            gemv_store<MODE, R>(a, item, row, acc);
+        }
+    }
+}
+
+template <int MODE>
+void dispatch_gemv_bulk(const GemvArgs& a, cudaStream_t s, bool pdl) {
+    constexpr int R = bulk_rows<MODE>();
+    const size_t rowb = static_cast<size_t>(a.K) * 2;
+    int upb = (a.rows + kBulkBlocks - 1) / kBulkBlocks;
+    while (upb > 1 && R * upb * rowb + static_cast<size_t>(a.K) * 4 > kBulkSmemMax) upb = (upb + 1) / 2;
+    const size_t smem = R * upb * rowb + static_cast<size_t>(a.K) * 4;
+    if (smem > kBulkSmemMax) throw std::invalid_argument("gemv_bulk: rows too long for shared memory");
+    const int blocks = (a.rows + upb - 1) / upb;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(dim3(blocks), dim3(kBulkThreads), smem, s, pdl, attr);
+    check_launch(cudaLaunchKernelEx(&cfg, gemv_bulk_kernel<MODE>, a, upb));
 }
 
 // ------------------------------------------------------------ attention ---
@@ -421,6 +645,23 @@ __global__ void final_norm_kernel(const float* h, const __half* g, float eps, in
 
 }  // namespace
 
+void launch_gemv_bulk(const GemvArgs& a, cudaStream_t s, bool pdl) {
+    if (a.K <= 0 || a.K % 8 != 0 || a.K > 4096 || a.rows <= 0 || a.in_mode != IN_PLAIN ||
+        (reinterpret_cast<uintptr_t>(a.w) & 15) != 0 || (reinterpret_cast<uintptr_t>(a.x) & 15) != 0 ||
+        (reinterpret_cast<uintptr_t>(a.norm_g) & 7) != 0)
+        throw std::invalid_argument("gemv_bulk: bad shape or alignment");
+    switch (a.mode) {
+        case GEMV_PLAIN: dispatch_gemv_bulk<GEMV_PLAIN>(a, s, pdl); break;
+        case GEMV_RESID: dispatch_gemv_bulk<GEMV_RESID>(a, s, pdl); break;
+        case GEMV_GATEUP: dispatch_gemv_bulk<GEMV_GATEUP>(a, s, pdl); break;
+        case GEMV_QKV:
+            if (a.head_dim % 2 != 0 || a.ctl == nullptr) throw std::invalid_argument("gemv_bulk: bad q/k/v setup");
+            dispatch_gemv_bulk<GEMV_QKV>(a, s, pdl);
+            break;
+        default: throw std::invalid_argument("gemv_bulk: unknown mode");
+    }
+}
+
 void launch_gemv(const GemvArgs& a, cudaStream_t s, bool pdl) {
     if (a.K <= 0 || a.K % 8 != 0 || a.rows <= 0) throw std::invalid_argument("gemv: bad shape");
     switch (a.mode) {
@@ -560,6 +801,11 @@ void init_kernel_attributes() {
     constexpr int kMax = 200 * 1024;
     check_launch(cudaFuncSetAttribute(attn_decode_kernel<__half, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax));
     check_launch(cudaFuncSetAttribute(attn_decode_kernel<float, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax));
+    for (const void* f : {reinterpret_cast<const void*>(gemv_bulk_kernel<GEMV_PLAIN>),
+                          reinterpret_cast<const void*>(gemv_bulk_kernel<GEMV_RESID>),
+                          reinterpret_cast<const void*>(gemv_bulk_kernel<GEMV_GATEUP>),
+                          reinterpret_cast<const void*>(gemv_bulk_kernel<GEMV_QKV>)})
+        check_launch(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kBulkSmemMax)));
     init_batched_attributes();
     init_tc_attributes();
     init_dit_layers_attributes();

@@ -57,6 +57,10 @@ struct GemvArgs {
 };
 
 void launch_gemv(const GemvArgs& a, cudaStream_t s, bool pdl);
+// The same product with at most one block per SM whose weight rows are copied
+// into shared memory by the bulk-copy engine before the dependency wait (the
+// decoder-step form); IN_PLAIN input, K <= 4096.
+void launch_gemv_bulk(const GemvArgs& a, cudaStream_t s, bool pdl);
 
 // ------------------------------------------------------ flash decode -----
 // One query token of each of q_heads heads attends over keys [0, T) of a GQA

@@ -378,6 +378,9 @@ struct vxc_stream {
     int tc_target = 32;
     // programmatic dependent launch between the patch graph's kernels (VXC_NO_PDL=1 turns it off)
     bool pdl = true;
+    // decoder-step GEMVs copy their weight rows into shared memory with the bulk-copy
+    // engine before the dependency wait (VXC_BULK_GEMV=0 selects the register-streaming form)
+    bool bulk_gemv = true;
     float* dpart = nullptr;     // persistent launch: partial tiles
     unsigned* dsync = nullptr;  // persistent launch: grid barrier and tile counters
     int* dcount = nullptr;  // dit_out arrival counter
@@ -439,8 +442,12 @@ GemvArgs plain_gemv(const __half* w, const __half* b, const float* x, int K, int
 // ----------------------------------------------------------- enqueue ------
 // Batch-1 decoder step over s->h[which] (the residual stream, already holding
 // the input embedding); writes the final-norm output to out (+ out2) and bumps
-// kv_len[which] on the device.
-void enqueue_decoder_step(vxc_stream* s, int which, float* out, float* out2, int skip) {
+// kv_len[which] on the device (unless advance is 0). ctl_override replaces the
+// stream's control block (the step profile runs on a private one).
+void enqueue_decoder_step(vxc_stream* s, int which, float* out, float* out2, int skip,
+                          StreamCtl* ctl_override = nullptr, int advance = 1) {
+    StreamCtl* ctl = ctl_override ? ctl_override : s->ctl;
+    auto gemv = s->bulk_gemv ? launch_gemv_bulk : launch_gemv;
     const vxc_device* dev = s->dev;
     const vxc_model_desc& d = dev->desc;
     const std::vector<LayerW>& layers = which == 0 ? dev->base : dev->res;
@@ -468,9 +475,9 @@ void enqueue_decoder_step(vxc_stream* s, int which, float* out, float* out2, int
         qa.v_cache = s->vc[which] + l * plane;
         qa.cap = s->cap;
         qa.which = which;
-        qa.ctl = s->ctl;
+        qa.ctl = ctl;
         qa.skip_if_stopped = skip;
-        launch_gemv(qa, s->cs, s->pdl);
+        gemv(qa, s->cs, s->pdl);
 
         AttnArgs aa;
         aa.q = s->q;
@@ -486,7 +493,7 @@ void enqueue_decoder_step(vxc_stream* s, int which, float* out, float* out2, int
         aa.partial = s->partial;
         aa.counters = s->counters;
         aa.out = s->attn;
-        aa.ctl = s->ctl;
+        aa.ctl = ctl;
         aa.which = which;
         aa.skip_if_stopped = skip;
         launch_attn_decode_cluster(aa, s->cs, s->pdl);
@@ -499,9 +506,9 @@ void enqueue_decoder_step(vxc_stream* s, int which, float* out, float* out2, int
         oa.rows = H;
         oa.resid = s->h[which];
         oa.rscale = rscale;
-        oa.ctl = s->ctl;
+        oa.ctl = ctl;
         oa.skip_if_stopped = skip;
-        launch_gemv(oa, s->cs, s->pdl);
+        gemv(oa, s->cs, s->pdl);
 
         GemvArgs ga;
         ga.mode = GEMV_GATEUP;
@@ -512,9 +519,9 @@ void enqueue_decoder_step(vxc_stream* s, int which, float* out, float* out2, int
         ga.K = H;
         ga.rows = F;
         ga.y = s->act;
-        ga.ctl = s->ctl;
+        ga.ctl = ctl;
         ga.skip_if_stopped = skip;
-        launch_gemv(ga, s->cs, s->pdl);
+        gemv(ga, s->cs, s->pdl);
 
         GemvArgs da;
         da.mode = GEMV_RESID;
@@ -524,11 +531,11 @@ void enqueue_decoder_step(vxc_stream* s, int which, float* out, float* out2, int
         da.rows = H;
         da.resid = s->h[which];
         da.rscale = rscale;
-        da.ctl = s->ctl;
+        da.ctl = ctl;
         da.skip_if_stopped = skip;
-        launch_gemv(da, s->cs, s->pdl);
+        gemv(da, s->cs, s->pdl);
     }
-    launch_final_norm(s->h[which], fnorm, d.rms_eps, H, out, out2, s->ctl, which, 1, skip, s->cs, s->pdl);
+    launch_final_norm(s->h[which], fnorm, d.rms_eps, H, out, out2, ctl, which, advance, skip, s->cs, s->pdl);
 }
 
 // K split (cluster size) of a tensor-core linear: about 'target' CTAs per launch
@@ -1581,6 +1588,7 @@ VXC_API int32_t vxc_stream_create(vxc_device* dev, int32_t kv_capacity, vxc_stre
         // VXC_DIT_FORM=persistent|fused|split picks one explicitly (an unsupported choice is an error)
         s->dit_grid = dit_layers_grid();
         if (const char* np = std::getenv("VXC_NO_PDL")) s->pdl = std::string(np) != "1";
+        if (const char* bg = std::getenv("VXC_BULK_GEMV")) s->bulk_gemv = std::string(bg) != "0";
         if (const char* tt = std::getenv("VXC_TC_TARGET")) {
             s->tc_target = std::atoi(tt);
             if (s->tc_target < 1 || s->tc_target > 4096) throw std::invalid_argument("VXC_TC_TARGET must be in [1, 4096]");
@@ -2160,6 +2168,25 @@ std::vector<std::function<void(bool)>> profile_launches(vxc_stream* s, int kerne
     const int pos = std::min(s->kv_len[0], s->cap - 1);
     const int T = pos + 1;
     StreamCtl* pctl = reinterpret_cast<StreamCtl*>(s->est);  // >= sizeof(StreamCtl) floats
+    if (kernel == VXC_PROF_BASE_STEP || kernel == VXC_PROF_RES_STEP) {
+        // a whole decoder step over the stream's current KV length, on a private
+        // control block that it does not advance (each replay re-appends the same row)
+        const int which = kernel == VXC_PROF_BASE_STEP ? 0 : 1;
+        const std::vector<LayerW>& layers = which == 0 ? dev->base : dev->res;
+        StreamCtl probe{};
+        probe.kv_len[0] = std::min(s->kv_len[0], s->cap - 1);
+        probe.kv_len[1] = std::min(s->kv_len[1], s->cap - 1);
+        ck(cudaMemcpyAsync(pctl, &probe, sizeof(StreamCtl), cudaMemcpyHostToDevice, s->cs), "probe ctl");
+        ck(cudaStreamSynchronize(s->cs), "sync");
+        const double per_layer = static_cast<double>(hq + 2 * hkv) * hd * H + static_cast<double>(H) * hq * hd +
+                                 3.0 * F * H + 2.0 * H;  // q/k/v, o, gate/up + down, two norms
+        const double kv_rows = probe.kv_len[which] + 1.0;
+        bytes = 2.0 * per_layer * layers.size() + 2.0 * H                        // fp16 weights + final norm
+                + 4.0 * 2 * hkv * hd * kv_rows * layers.size();                    // fp32 K and V rows read
+        // output into scratch: the residual step's real output feeds the next patch
+        launch.push_back([=](bool) { enqueue_decoder_step(s, which, s->mid2, nullptr, 0, pctl, 0); });
+        return launch;
+    }
     if (kernel == VXC_PROF_BASE_QKV || kernel == VXC_PROF_BASE_ATTN) {
         StreamCtl probe{};
         probe.kv_len[0] = pos;
@@ -2294,7 +2321,7 @@ VXC_API int32_t vxc_profile_kernel(vxc_stream* s, int32_t kernel, int32_t iters,
     return guard([&] {
         require(s != nullptr && ms_per_launch != nullptr && bytes_per_launch != nullptr, "null argument");
         require(iters > 0 && iters <= 100000, "iters must be in [1, 100000]");
-        require(kernel >= VXC_PROF_DIT_GATEUP && kernel <= VXC_PROF_DIT_LAYERS, "unknown kernel id");
+        require(kernel >= VXC_PROF_DIT_GATEUP && kernel <= VXC_PROF_RES_STEP, "unknown kernel id");
         std::lock_guard<std::mutex> lk(s->call_mutex);
         const vxc_device* dev = s->dev;
         const vxc_model_desc& d = dev->desc;
