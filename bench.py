@@ -46,10 +46,11 @@ def parse():
     p.add_argument("--group-members", type=int, default=4, help="streams per group (1..4)")
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--cpu-sample-patches", type=int, default=6)
-    p.add_argument("--range", choices=["patches", "profile"], default=None,
+    p.add_argument("--range", choices=["patches", "profile", "group"], default=None,
                    help="run one cudaProfilerStart/Stop range for an ncu app-range capture and exit: 'patches' = "
                         "6 patches of every stream, 'profile' = the concurrent gate/up linear profile call "
-                        "(graph builds and warm-up replays included)")
+                        "(graph builds and warm-up replays included); 'group' = 3 patches of one stream group "
+                        "(--group-members streams), no profiler range")
     return p.parse_args()
 
 
@@ -537,6 +538,22 @@ def run_range(args):
     from voxcpm2_b200.config import BENCH
     S, K, W = args.streams, 6, 3
     dev = rt.Device(BENCH, 0, synthetic.model_blobs(BENCH, 0))
+    if args.range == "group":
+        # one group of --group-members streams: 2 warm-up group patches, then 1
+        # (launch list: the last kernels_per_group_patch launches are that patch)
+        g = rt.Group(dev, args.group_members, kv_capacity=512)
+        for m, st in enumerate(g.streams):
+            a = 7919 * m + 13
+            st.prefill(synthetic.token_ids(BENCH, TEXT_TOKENS, seed=a))
+            st.upload_noise(synthetic.normal((4, BENCH.latent), seed=a + 1))
+        for _ in range(3):
+            g.patch_step_async(MIN_PATCHES, CFG, TIMESTEPS)
+        g.synchronize()
+        print(json.dumps({"range": "group", "members": args.group_members,
+                          "kernels_per_group_patch": g.graph_kernels()}))
+        g.close()
+        dev.close()
+        return 0
     streams = [rt.Stream(dev, kv_capacity=512) for _ in range(S)]
     if args.range == "profile":
         rt.Stream.profile_kernel_concurrent(streams, "dit_gateup", 100)
