@@ -89,6 +89,12 @@ def dit_patch_bytes(cfg) -> float:
     return 2.0 * evals * (component_count(cfg, DIT_ESTIMATOR) - 4 * (hd * hd + hd))
 
 
+def decoder_weight_bytes(cfg) -> float:
+    """fp16 weight bytes of one base + one residual decoder step."""
+    from voxcpm2_b200.config import BASE_DECODER, RESIDUAL_DECODER, component_count
+    return 2.0 * (component_count(cfg, BASE_DECODER) + component_count(cfg, RESIDUAL_DECODER))
+
+
 def patch_bytes(cfg, kv_tokens: float) -> float:
     """Algorithmic HBM bytes of one patch: every weight the patch reads once (fp16:
     one base and one residual decoder step, 9 DiT estimator evaluations without the
@@ -311,17 +317,21 @@ def group_rate(rt, synthetic, dev, cfg, groups, members, K, W, min_patches, rank
     for g in gs:
         g.close()
     value = world * groups * members * K / (ms / 1e3)
-    # a group patch reads the estimator weights once for all its members
-    bpp = patch_bytes(cfg, TEXT_TOKENS + 1 + W + K / 2) - dit_patch_bytes(cfg) * (members - 1) / members
+    # a group patch reads the estimator and decoder weights once for all its members
+    # (the small graphs and each member's KV rows stay per member)
+    shared = dit_patch_bytes(cfg) + decoder_weight_bytes(cfg)
+    bpp = patch_bytes(cfg, TEXT_TOKENS + 1 + W + K / 2) - shared * (members - 1) / members
     return {"groups_per_gpu": groups, "members": members, "streams_per_gpu": groups * members,
             "value": value, "unit": "patches/s", "ms_per_step": ms / K,
             "hbm_job": {"bytes_per_patch": bpp, "achieved": value * bpp / 1e9, "peak": peak, "unit": "GB/s",
                         "frac": value * bpp / 1e9 / peak,
-                        "note": "algorithmic bytes per member patch (estimator weights shared by the group)"},
+                        "note": "algorithmic bytes per member patch (estimator and decoder weights shared by "
+                                "the group)"},
             "group_patch_ms": float(np.median(lat)), "kernels_per_group_patch": kernels,
             "gpu_launches": groups * K * kernels,
-            "note": "each group steps its members as one CUDA graph; the 9 estimator evaluations of all "
-                    "members run as one tcgen05 pass over the DiT weights (22 rows per member)"}
+            "note": "each group steps its members as one CUDA graph: the 9 estimator evaluations of all "
+                    "members run as one tcgen05 pass over the DiT weights (22 rows per member), and both "
+                    "decoder steps as batched GEMVs (one weight read, one dot product per member)"}
 
 
 def run_ours(args):

@@ -103,3 +103,58 @@ def test_group_orders_with_member_calls(rt):
     with pytest.raises(rt.VxcError):
         rt.Group(dev, 5, kv_capacity=64)
     dev.close()
+
+
+def stop_prone_blobs():
+    """TINY weights whose stop head's 'stop' row is the 'continue' row plus a
+    random N(0, 0.5) vector (seed 1): the stop logit gap then has a spread of ~1,
+    so decisions flip early and with clear margins (the random-init head's gap is
+    ~1e-3 and never favours stopping within 24 patches)."""
+    from voxcpm2_b200.config import STOP_HEAD
+    blobs = dict(synthetic.model_blobs(TINY, 0))
+    H = TINY.hidden
+    sh = np.array(blobs[STOP_HEAD], dtype=np.float16).copy()
+    off = H * H + H
+    v = np.random.default_rng(1).normal(0, 0.5, H).astype(np.float32)
+    sh[off + H: off + 2 * H] = (sh[off: off + H].astype(np.float32) + v).astype(np.float16)
+    blobs[STOP_HEAD] = sh
+    return blobs
+
+
+def test_group_members_stop_independently(rt):
+    """Small min_patches: members reach the stop rule at their own patches (their
+    decoder steps inside the batched kernels skip once their own flag is set).
+    Each member's stop patch and latents up to it match the oracle's generate()
+    (with these weights the oracle stops the members after 5, never, 6 and 8 patches)."""
+    blobs = stop_prone_blobs()
+    dev = rt.Device(TINY, 0, blobs)
+    orc = oracle.Oracle(TINY, blobs)
+    cap_patches = 24
+    prompts = [synthetic.token_ids(TINY, 5 + 2 * m, seed=60 + m) for m in range(4)]
+    seeds = [300 + m for m in range(4)]
+    g = rt.Group(dev, 4, kv_capacity=128)
+    for st, ids, seed in zip(g.streams, prompts, seeds):
+        st.prefill(ids)
+        st.upload_noise(oracle.noise_table(seed, cap_patches, TINY.latent))
+    first_stop = [None] * 4
+    for step in range(cap_patches):
+        g.patch_step_async(2, 2.0, 6)
+        g.synchronize()
+        for m, st in enumerate(g.streams):
+            if first_stop[m] is None and st.state().stopped:
+                first_stop[m] = step
+        if all(f is not None for f in first_stop):
+            break
+    for m, (st, ids, seed) in enumerate(zip(g.streams, prompts, seeds)):
+        want = orc.generate(ids, min_patches=2, timesteps=6, cfg_value=2.0, max_patches_override=cap_patches,
+                            seed=seed)
+        got_n = cap_patches if first_stop[m] is None else first_stop[m] + 1
+        assert got_n == want["patches"], (m, got_n, want["patches"])
+        got = st.latents(0, got_n)
+        stats = [close_stats(got[i], want["latents"][i]) for i in range(got_n)]
+        err, cos = max(s[0] for s in stats), min(s[1] for s in stats)
+        print(f"member {m}: stop after {got_n} patches, worst max-abs {err:.3e}, cosine {cos:.6f}")
+        assert err <= 2e-2 and cos >= 0.999, (m, err, cos)
+    assert sum(f is not None for f in first_stop) >= 2
+    g.close()
+    dev.close()

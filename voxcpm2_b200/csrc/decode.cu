@@ -272,20 +272,21 @@ constexpr int bulk_rows() {
     return (MODE == GEMV_GATEUP || MODE == GEMV_QKV) ? 2 : 1;
 }
 
-// Output units [blockIdx.x * upb, + upb) of a.rows; IN_PLAIN input only.
+// Output units [blockIdx.x * upb, + upb) of a.rows for the b.n members; IN_PLAIN input only.
 template <int MODE>
-__global__ void __launch_bounds__(kBulkThreads) gemv_bulk_kernel(const GemvArgs a, int upb) {
+__global__ void __launch_bounds__(kBulkThreads) gemv_bulk_kernel(const GemvArgs a, const GemvBatch b, int upb) {
     constexpr int R = bulk_rows<MODE>();
+    constexpr int NB = kGemvBatch;
     extern __shared__ __align__(16) uint8_t bulk_sm[];
     __shared__ uint64_t bar;
-    __shared__ float red[kBulkWarps];
+    __shared__ float red[NB][kBulkWarps];
     pdl_launch_dependents();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int K = a.K;
+    const int K = a.K, nb = b.n;
     const int u0 = blockIdx.x * upb, nu = max(min(upb, a.rows - u0), 0);
     const size_t rowb = static_cast<size_t>(K) * 2;
     __half* ws = reinterpret_cast<__half*>(bulk_sm);  // [R * upb][K]
-    float* xs = reinterpret_cast<float*>(bulk_sm + static_cast<size_t>(R) * upb * rowb);
+    float* xs = reinterpret_cast<float*>(bulk_sm + static_cast<size_t>(R) * upb * rowb);  // [nb][K]
 
     // 1) this block's weight rows into shared memory (independent of earlier kernels)
     if (tid == 0) {
@@ -317,71 +318,111 @@ __global__ void __launch_bounds__(kBulkThreads) gemv_bulk_kernel(const GemvArgs 
     }
     __syncthreads();  // the barrier is initialised before anyone waits on it
 
-    // 2) wait for the producer of the input vector
+    // 2) wait for the producers of the input vectors
     pdl_wait();
-    const bool stopped = a.skip_if_stopped && a.ctl && a.ctl->stopped;
+    bool live[NB];
+    bool any = false;
+#pragma unroll
+    for (int m = 0; m < NB; ++m) {
+        live[m] = m < nb && !(a.skip_if_stopped && b.ctl[m] && b.ctl[m]->stopped);
+        any = any || live[m];
+    }
 
-    // 3) the (optionally RMS-normalised) input: float4 loads, all issued at once
-    float inv_rms = 1.f;
-    if (!stopped) {
-        float ss = 0.f;
+    // 3) each member's (optionally RMS-normalised) input: float4 loads, all issued at once
+    float inv_rms[NB];
+#pragma unroll
+    for (int m = 0; m < NB; ++m) inv_rms[m] = 1.f;
+    if (any) {
         const int n4 = K >> 2;
         constexpr int kV = 4;  // K <= 4096
-        float4 xv[kV];
         uint2 gv[kV];
 #pragma unroll
         for (int j = 0; j < kV; ++j) {
             const int i = tid + j * kBulkThreads;
-            xv[j] = i < n4 ? reinterpret_cast<const float4*>(a.x)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
             gv[j] = (a.norm_g && i < n4) ? reinterpret_cast<const uint2*>(a.norm_g)[i] : make_uint2(0u, 0u);
         }
 #pragma unroll
-        for (int j = 0; j < kV; ++j) {
-            const int i = tid + j * kBulkThreads;
-            if (i < n4) {
-                float4 v = xv[j];
-                ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-                if (a.norm_g) {
-                    const float2 g01 = __half22float2(*reinterpret_cast<const __half2*>(&gv[j].x));
-                    const float2 g23 = __half22float2(*reinterpret_cast<const __half2*>(&gv[j].y));
-                    v = make_float4(v.x * g01.x, v.y * g01.y, v.z * g23.x, v.w * g23.y);
-                }
-                reinterpret_cast<float4*>(xs)[i] = v;
+        for (int m = 0; m < NB; ++m) {
+            if (!live[m]) continue;
+            float4 xv[kV];
+#pragma unroll
+            for (int j = 0; j < kV; ++j) {
+                const int i = tid + j * kBulkThreads;
+                xv[j] = i < n4 ? reinterpret_cast<const float4*>(b.x[m])[i] : make_float4(0.f, 0.f, 0.f, 0.f);
             }
-        }
-        if (a.norm_g) {
-            ss = warp_sum(ss);
-            if (lane == 0) red[warp] = ss;
+            float ss = 0.f;
+#pragma unroll
+            for (int j = 0; j < kV; ++j) {
+                const int i = tid + j * kBulkThreads;
+                if (i < n4) {
+                    float4 v = xv[j];
+                    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                    if (a.norm_g) {
+                        const float2 g01 = __half22float2(*reinterpret_cast<const __half2*>(&gv[j].x));
+                        const float2 g23 = __half22float2(*reinterpret_cast<const __half2*>(&gv[j].y));
+                        v = make_float4(v.x * g01.x, v.y * g01.y, v.z * g23.x, v.w * g23.y);
+                    }
+                    reinterpret_cast<float4*>(xs + static_cast<size_t>(m) * K)[i] = v;
+                }
+            }
+            if (a.norm_g) {
+                ss = warp_sum(ss);
+                if (lane == 0) red[m][warp] = ss;
+            }
         }
         __syncthreads();
         if (a.norm_g) {
-            float t = 0.f;
 #pragma unroll
-            for (int w = 0; w < kBulkWarps; ++w) t += red[w];
-            inv_rms = rsqrtf(t / static_cast<float>(K) + a.eps);
+            for (int m = 0; m < NB; ++m) {
+                if (!live[m]) continue;
+                float t = 0.f;
+#pragma unroll
+                for (int w = 0; w < kBulkWarps; ++w) t += red[m][w];
+                inv_rms[m] = rsqrtf(t / static_cast<float>(K) + a.eps);
+            }
         }
     }
 
     // 4) the weights have landed (every thread waits: none may read early, and the
     // block may not exit with a copy in flight; bounded)
     const bool ok = nu == 0 || bulk_wait(&bar);
-    if (!ok && tid == 0 && a.ctl) a.ctl->error = 3;
-    if (stopped || !ok) return;
+    if (!ok && tid == 0)
+        for (int m = 0; m < nb; ++m)
+            if (b.ctl[m]) b.ctl[m]->error = 3;
+    if (!any || !ok) return;
 
-    // 5) dot products: warp w takes units w, w + 8, ...
+    // 5) dot products: warp w takes units w, w + 8, ...; each weight row is read
+    // once from shared memory for every member
     for (int i = warp; i < nu; i += kBulkWarps) {
         const __half* w0 = ws + static_cast<size_t>(MODE == GEMV_QKV ? 2 * i : i) * K;
         const __half* w1 = MODE == GEMV_GATEUP ? ws + static_cast<size_t>(upb + i) * K : w0 + K;
-        float acc[2] = {0.f, 0.f};
+        float acc[NB][2];
+#pragma unroll
+        for (int m = 0; m < NB; ++m) acc[m][0] = acc[m][1] = 0.f;
         for (int e = lane * 8; e < K; e += kWarp * 8) {
-            const float4 x0 = *reinterpret_cast<const float4*>(&xs[e]);
-            const float4 x1 = *reinterpret_cast<const float4*>(&xs[e + 4]);
-            acc[0] = dot8(*reinterpret_cast<const uint4*>(w0 + e), x0, x1, acc[0]);
-            if (R == 2) acc[1] = dot8(*reinterpret_cast<const uint4*>(w1 + e), x0, x1, acc[1]);
+            const uint4 wa = *reinterpret_cast<const uint4*>(w0 + e);
+            uint4 wb = wa;
+            if (R == 2) wb = *reinterpret_cast<const uint4*>(w1 + e);
+#pragma unroll
+            for (int m = 0; m < NB; ++m) {
+                if (!live[m]) continue;
+                const float* xm = xs + static_cast<size_t>(m) * K;
+                const float4 x0 = *reinterpret_cast<const float4*>(&xm[e]);
+                const float4 x1 = *reinterpret_cast<const float4*>(&xm[e + 4]);
+                acc[m][0] = dot8(wa, x0, x1, acc[m][0]);
+                if (R == 2) acc[m][1] = dot8(wb, x0, x1, acc[m][1]);
+            }
         }
 #pragma unroll
-        for (int r = 0; r < R; ++r) acc[r] = warp_sum(acc[r]) * inv_rms;
-        if (lane == 0) {
+        for (int m = 0; m < NB; ++m) {
+            if (!live[m]) continue;
+#pragma unroll
+            for (int r = 0; r < R; ++r) acc[m][r] = warp_sum(acc[m][r]) * inv_rms[m];
+        }
+        // lane m stores member m
+#pragma unroll
+        for (int m = 0; m < NB; ++m) {
+            if (lane != m || !live[m]) continue;
             const int item = u0 + i;
             int row[2];
             if constexpr (MODE == GEMV_GATEUP) {
@@ -396,23 +437,30 @@ __global__ void __launch_bounds__(kBulkThreads) gemv_bulk_kernel(const GemvArgs 
                 row[0] = item;
                 row[1] = item;
             }
-            gemv_store<MODE, R>(a, item, row, acc);
+            GemvArgs am = a;
+            am.x = b.x[m];
+            am.y = b.y[m];
+            am.resid = b.resid[m];
+            am.k_cache = b.k_cache[m];
+            am.v_cache = b.v_cache[m];
+            am.ctl = b.ctl[m];
+            gemv_store<MODE, R>(am, item, row, acc[m]);
         }
     }
 }
 
 template <int MODE>
-void dispatch_gemv_bulk(const GemvArgs& a, cudaStream_t s, bool pdl) {
+void dispatch_gemv_bulk(const GemvArgs& a, const GemvBatch& b, cudaStream_t s, bool pdl) {
     constexpr int R = bulk_rows<MODE>();
-    const size_t rowb = static_cast<size_t>(a.K) * 2;
+    const size_t rowb = static_cast<size_t>(a.K) * 2, xb = static_cast<size_t>(b.n) * a.K * 4;
     int upb = (a.rows + kBulkBlocks - 1) / kBulkBlocks;
-    while (upb > 1 && R * upb * rowb + static_cast<size_t>(a.K) * 4 > kBulkSmemMax) upb = (upb + 1) / 2;
-    const size_t smem = R * upb * rowb + static_cast<size_t>(a.K) * 4;
+    while (upb > 1 && R * upb * rowb + xb > kBulkSmemMax) upb = (upb + 1) / 2;
+    const size_t smem = R * upb * rowb + xb;
     if (smem > kBulkSmemMax) throw std::invalid_argument("gemv_bulk: rows too long for shared memory");
     const int blocks = (a.rows + upb - 1) / upb;
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = make_cfg(dim3(blocks), dim3(kBulkThreads), smem, s, pdl, attr);
-    check_launch(cudaLaunchKernelEx(&cfg, gemv_bulk_kernel<MODE>, a, upb));
+    check_launch(cudaLaunchKernelEx(&cfg, gemv_bulk_kernel<MODE>, a, b, upb));
 }
 
 // ------------------------------------------------------------ attention ---
@@ -645,21 +693,37 @@ __global__ void final_norm_kernel(const float* h, const __half* g, float eps, in
 
 }  // namespace
 
-void launch_gemv_bulk(const GemvArgs& a, cudaStream_t s, bool pdl) {
-    if (a.K <= 0 || a.K % 8 != 0 || a.K > 4096 || a.rows <= 0 || a.in_mode != IN_PLAIN ||
-        (reinterpret_cast<uintptr_t>(a.w) & 15) != 0 || (reinterpret_cast<uintptr_t>(a.x) & 15) != 0 ||
+void launch_gemv_bulk_batch(const GemvArgs& a, const GemvBatch& b, cudaStream_t s, bool pdl) {
+    bool aligned = true;
+    for (int m = 0; m < b.n; ++m) aligned = aligned && (reinterpret_cast<uintptr_t>(b.x[m]) & 15) == 0;
+    if (a.K <= 0 || a.K % 8 != 0 || a.K > 4096 || a.rows <= 0 || a.in_mode != IN_PLAIN || b.n < 1 ||
+        b.n > kGemvBatch || !aligned || (reinterpret_cast<uintptr_t>(a.w) & 15) != 0 ||
         (reinterpret_cast<uintptr_t>(a.norm_g) & 7) != 0)
-        throw std::invalid_argument("gemv_bulk: bad shape or alignment");
+        throw std::invalid_argument("gemv_bulk: bad shape, batch or alignment");
     switch (a.mode) {
-        case GEMV_PLAIN: dispatch_gemv_bulk<GEMV_PLAIN>(a, s, pdl); break;
-        case GEMV_RESID: dispatch_gemv_bulk<GEMV_RESID>(a, s, pdl); break;
-        case GEMV_GATEUP: dispatch_gemv_bulk<GEMV_GATEUP>(a, s, pdl); break;
+        case GEMV_PLAIN: dispatch_gemv_bulk<GEMV_PLAIN>(a, b, s, pdl); break;
+        case GEMV_RESID: dispatch_gemv_bulk<GEMV_RESID>(a, b, s, pdl); break;
+        case GEMV_GATEUP: dispatch_gemv_bulk<GEMV_GATEUP>(a, b, s, pdl); break;
         case GEMV_QKV:
-            if (a.head_dim % 2 != 0 || a.ctl == nullptr) throw std::invalid_argument("gemv_bulk: bad q/k/v setup");
-            dispatch_gemv_bulk<GEMV_QKV>(a, s, pdl);
+            for (int m = 0; m < b.n; ++m)
+                if (b.ctl[m] == nullptr) throw std::invalid_argument("gemv_bulk: q/k/v needs a control block");
+            if (a.head_dim % 2 != 0) throw std::invalid_argument("gemv_bulk: bad q/k/v setup");
+            dispatch_gemv_bulk<GEMV_QKV>(a, b, s, pdl);
             break;
         default: throw std::invalid_argument("gemv_bulk: unknown mode");
     }
+}
+
+void launch_gemv_bulk(const GemvArgs& a, cudaStream_t s, bool pdl) {
+    GemvBatch b;
+    b.n = 1;
+    b.x[0] = a.x;
+    b.y[0] = a.y;
+    b.resid[0] = a.resid;
+    b.k_cache[0] = a.k_cache;
+    b.v_cache[0] = a.v_cache;
+    b.ctl[0] = a.ctl;
+    launch_gemv_bulk_batch(a, b, s, pdl);
 }
 
 void launch_gemv(const GemvArgs& a, cudaStream_t s, bool pdl) {
@@ -698,11 +762,20 @@ __device__ __forceinline__ void cluster_barrier() {
 }
 
 template <typename KV, int D>
-__global__ void __launch_bounds__(kAttnThreads) attn_decode_cluster_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_cluster_kernel(const AttnArgs a0, const AttnBatch b) {
     static_assert(D == 64, "head_dim 64");
     __shared__ AttnSmem S;
     __shared__ float pacc[kMaxGroup][D], pm[kMaxGroup], pl[kMaxGroup];
     pdl_launch_dependents();
+    AttnArgs a = a0;
+    if (b.n > 0) {  // member blockIdx.z of a group (a cluster spans x only: one member per cluster)
+        const int m = blockIdx.z;
+        a.q = b.q[m];
+        a.k0 = b.k0[m];
+        a.v0 = b.v0[m];
+        a.out = b.out[m];
+        a.ctl = b.ctl[m];
+    }
     pdl_wait();
     // uniform over the grid: the flag cannot change while the kernel runs
     if (a.skip_if_stopped && a.ctl && a.ctl->stopped) return;
@@ -753,16 +826,20 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_cluster_kernel(const
     cluster_barrier();  // no CTA leaves while another still reads its shared memory
 }
 
-void launch_attn_decode_cluster(const AttnArgs& a, cudaStream_t s, bool pdl) {
+void launch_attn_decode_cluster_batch(const AttnArgs& a, const AttnBatch& b, cudaStream_t s, bool pdl) {
     if (a.head_dim != 64) throw std::invalid_argument("attention: head_dim must be 64");
     if (a.kv_heads <= 0 || a.q_heads % a.kv_heads != 0) throw std::invalid_argument("attention: bad head grouping");
     const int G = a.q_heads / a.kv_heads;
     if (G < 1 || G > kMaxGroup) throw std::invalid_argument("attention: more than 16 query heads per KV head");
+    if (b.n < 0 || b.n > 4) throw std::invalid_argument("attention: 1 to 4 members");
     for (const void* p : {a.k0, a.v0, a.k1, a.v1})
         if (reinterpret_cast<uintptr_t>(p) % 16 != 0)
             throw std::invalid_argument("attention: key/value rows must start on 16-byte boundaries");
+    for (int m = 0; m < b.n; ++m)
+        if ((reinterpret_cast<uintptr_t>(b.k0[m]) | reinterpret_cast<uintptr_t>(b.v0[m])) % 16 != 0)
+            throw std::invalid_argument("attention: key/value rows must start on 16-byte boundaries");
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(kAttnCluster, a.kv_heads);
+    cfg.gridDim = dim3(kAttnCluster, a.kv_heads, b.n > 0 ? b.n : 1);
     cfg.blockDim = dim3(kAttnThreads);
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
@@ -774,7 +851,11 @@ void launch_attn_decode_cluster(const AttnArgs& a, cudaStream_t s, bool pdl) {
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
-    check_launch(cudaLaunchKernelEx(&cfg, attn_decode_cluster_kernel<float, 64>, a));
+    check_launch(cudaLaunchKernelEx(&cfg, attn_decode_cluster_kernel<float, 64>, a, b));
+}
+
+void launch_attn_decode_cluster(const AttnArgs& a, cudaStream_t s, bool pdl) {
+    launch_attn_decode_cluster_batch(a, AttnBatch{}, s, pdl);
 }
 
 void launch_attn_decode(const AttnArgs& a, bool fp16_kv, cudaStream_t s, bool pdl) {

@@ -61,6 +61,21 @@ void launch_gemv(const GemvArgs& a, cudaStream_t s, bool pdl);
 // into shared memory by the bulk-copy engine before the dependency wait (the
 // decoder-step form); IN_PLAIN input, K <= 4096.
 void launch_gemv_bulk(const GemvArgs& a, cudaStream_t s, bool pdl);
+// Up to kGemvBatch members (streams of a group) through the same weights: one read
+// of each weight row, one dot product per member. Member m replaces a's x, y,
+// resid, k_cache, v_cache and ctl; each member skips (and appends no KV row) when
+// a.skip_if_stopped and its own ctl->stopped are set.
+constexpr int kGemvBatch = 4;
+struct GemvBatch {
+    int n = 0;
+    const float* x[kGemvBatch] = {};
+    float* y[kGemvBatch] = {};
+    float* resid[kGemvBatch] = {};
+    float* k_cache[kGemvBatch] = {};
+    float* v_cache[kGemvBatch] = {};
+    StreamCtl* ctl[kGemvBatch] = {};
+};
+void launch_gemv_bulk_batch(const GemvArgs& a, const GemvBatch& b, cudaStream_t s, bool pdl);
 
 // ------------------------------------------------------ flash decode -----
 // One query token of each of q_heads heads attends over keys [0, T) of a GQA
@@ -90,6 +105,17 @@ void launch_attn_decode(const AttnArgs& a, bool fp16_kv, cudaStream_t s, bool pd
 // The same (fp32 KV) with the split-K combine inside one 8-CTA cluster per KV head
 // (distributed shared memory; no scratch, no atomics). Ignores splits/partial/counters.
 void launch_attn_decode_cluster(const AttnArgs& a, cudaStream_t s, bool pdl);
+// The same for up to 4 members (grid z = member): member m replaces a's q, k0, v0,
+// out and ctl (its own KV length and stop flag).
+struct AttnBatch {
+    int n = 0;
+    const float* q[4] = {};
+    const void* k0[4] = {};
+    const void* v0[4] = {};
+    float* out[4] = {};
+    StreamCtl* ctl[4] = {};
+};
+void launch_attn_decode_cluster_batch(const AttnArgs& a, const AttnBatch& b, cudaStream_t s, bool pdl);
 
 // final RMSNorm of a decoder step: out = norm(h) * g; optionally bump kv_len.
 void launch_final_norm(const float* h, const __half* g, float eps, int H, float* out, float* out2,

@@ -855,9 +855,8 @@ void enqueue_patch(vxc_stream* s, int T, float cfg) {
     enqueue_patch_post(s);
 }
 
-// The patch iteration after the sampler: the stop decision, feat_encoder, both
-// decoder steps, FSQ and fusion, and the latent's store.
-void enqueue_patch_post(vxc_stream* s) {
+// Post-sampler part A: stop decision, feat_encoder (-> the base decoder input).
+void enqueue_post_stop_feat(vxc_stream* s) {
     const vxc_device* dev = s->dev;
     const vxc_model_desc& d = dev->desc;
     const int H = d.hidden, L = d.feat_dim * d.patch_size;
@@ -878,7 +877,13 @@ void enqueue_patch_post(vxc_stream* s) {
                              ACT_NONE, s->ctl, 1);
     fb.y2 = s->h[0];
     launch_gemv(fb, s->cs, s->pdl);
-    enqueue_decoder_step(s, 0, s->out[0], nullptr, 1);
+}
+
+// Part B, after the base decoder step: FSQ and fusion (-> the residual decoder input).
+void enqueue_post_fsq_fusion(vxc_stream* s) {
+    const vxc_device* dev = s->dev;
+    const vxc_model_desc& d = dev->desc;
+    const int H = d.hidden, L = d.feat_dim * d.patch_size;
     // fsq
     const __half* fq = dev->blob[VXC_FSQ];
     const size_t Q = d.fsq_dim;
@@ -895,8 +900,23 @@ void enqueue_patch_post(vxc_stream* s) {
     ua.x2 = s->feat;
     ua.k1 = H;
     launch_gemv(ua, s->cs, s->pdl);
+}
+
+// Part C, after the residual decoder step: the latent's store (on stream cs, or
+// the member's own stream).
+void enqueue_post_end(vxc_stream* s, cudaStream_t cs = nullptr) {
+    const int L = s->dev->desc.feat_dim * s->dev->desc.patch_size;
+    launch_patch_end(s->x, s->latents, L, s->ctl, cs ? cs : s->cs, s->pdl);
+}
+
+// The patch iteration after the sampler: the stop decision, feat_encoder, both
+// decoder steps, FSQ and fusion, and the latent's store.
+void enqueue_patch_post(vxc_stream* s) {
+    enqueue_post_stop_feat(s);
+    enqueue_decoder_step(s, 0, s->out[0], nullptr, 1);
+    enqueue_post_fsq_fusion(s);
     enqueue_decoder_step(s, 1, s->res_h, nullptr, 1);
-    launch_patch_end(s->x, s->latents, L, s->ctl, s->cs, s->pdl);
+    enqueue_post_end(s);
 }
 
 void sync_ctl(vxc_stream* s) {
@@ -1224,6 +1244,114 @@ struct vxc_group {
 
 namespace {
 
+// One decoder step (base: which 0, residual: 1) of every member at once
+// (base_decoder_kv / residual_decoder_kv, tools/export_components.py:496-550):
+// each linear reads its weights once for all members (gemv_bulk_batch), the
+// attention runs one cluster per (member, KV head) over the member's own cache,
+// and every member keeps its own KV length and stop flag.
+void enqueue_group_decoder_step(vxc_group* g, int which) {
+    vxc_stream* s0 = g->members[0];
+    const vxc_device* dev = g->dev;
+    const vxc_model_desc& d = dev->desc;
+    const std::vector<LayerW>& layers = which == 0 ? dev->base : dev->res;
+    const __half* fnorm = which == 0 ? dev->base_norm : dev->res_norm;
+    const float rscale = which == 0 ? d.base_residual_scale : d.res_residual_scale;
+    const int H = d.hidden, F = d.ffn, hq = d.q_heads, hkv = d.kv_heads, hd = d.head_dim;
+    const int n = static_cast<int>(g->members.size());
+    cudaStream_t cs = s0->cs;
+    const bool pdl = s0->pdl;
+    for (size_t l = 0; l < layers.size(); ++l) {
+        const LayerW& L = layers[l];
+        GemvBatch qb, ob, gb, db;
+        AttnBatch ab;
+        qb.n = ob.n = gb.n = db.n = ab.n = n;
+        for (int m = 0; m < n; ++m) {
+            vxc_stream* s = g->members[static_cast<size_t>(m)];
+            const size_t plane = static_cast<size_t>(hkv) * s->cap * hd;
+            qb.x[m] = s->h[which];
+            qb.y[m] = s->q;
+            qb.k_cache[m] = s->kc[which] + l * plane;
+            qb.v_cache[m] = s->vc[which] + l * plane;
+            qb.ctl[m] = s->ctl;
+            ab.q[m] = s->q;
+            ab.k0[m] = s->kc[which] + l * plane;
+            ab.v0[m] = s->vc[which] + l * plane;
+            ab.out[m] = s->attn;
+            ab.ctl[m] = s->ctl;
+            ob.x[m] = s->attn;
+            ob.resid[m] = s->h[which];
+            ob.ctl[m] = s->ctl;
+            gb.x[m] = s->h[which];
+            gb.y[m] = s->act;
+            gb.ctl[m] = s->ctl;
+            db.x[m] = s->act;
+            db.resid[m] = s->h[which];
+            db.ctl[m] = s->ctl;
+        }
+        GemvArgs qa;
+        qa.mode = GEMV_QKV;
+        qa.w = L.wqkv;
+        qa.norm_g = L.in_norm;
+        qa.eps = d.rms_eps;
+        qa.K = H;
+        qa.rows = (hq + 2 * hkv) * hd / 2;
+        qa.q_heads = hq;
+        qa.kv_heads = hkv;
+        qa.head_dim = hd;
+        qa.rope_cos = which == 0 ? s0->rope_cos : nullptr;  // the members share a capacity, so the same table
+        qa.rope_sin = which == 0 ? s0->rope_sin : nullptr;
+        qa.cap = s0->cap;
+        qa.which = which;
+        qa.skip_if_stopped = 1;
+        launch_gemv_bulk_batch(qa, qb, cs, pdl);
+
+        AttnArgs aa;
+        aa.k0 = ab.k0[0];
+        aa.v0 = ab.v0[0];
+        aa.len0 = s0->cap;
+        aa.stride0 = s0->cap;
+        aa.q_heads = hq;
+        aa.kv_heads = hkv;
+        aa.head_dim = hd;
+        aa.scale = 1.0f / std::sqrt(static_cast<float>(hd));
+        aa.ctl = s0->ctl;
+        aa.which = which;
+        aa.skip_if_stopped = 1;
+        launch_attn_decode_cluster_batch(aa, ab, cs, pdl);
+
+        GemvArgs oa;
+        oa.mode = GEMV_RESID;
+        oa.w = L.wo;
+        oa.K = hq * hd;
+        oa.rows = H;
+        oa.rscale = rscale;
+        oa.skip_if_stopped = 1;
+        launch_gemv_bulk_batch(oa, ob, cs, pdl);
+
+        GemvArgs ga;
+        ga.mode = GEMV_GATEUP;
+        ga.w = L.wgateup;
+        ga.norm_g = L.post_norm;
+        ga.eps = d.rms_eps;
+        ga.K = H;
+        ga.rows = F;
+        ga.skip_if_stopped = 1;
+        launch_gemv_bulk_batch(ga, gb, cs, pdl);
+
+        GemvArgs da;
+        da.mode = GEMV_RESID;
+        da.w = L.wdown;
+        da.K = F;
+        da.rows = H;
+        da.rscale = rscale;
+        da.skip_if_stopped = 1;
+        launch_gemv_bulk_batch(da, db, cs, pdl);
+    }
+    for (vxc_stream* s : g->members)
+        launch_final_norm(s->h[which], fnorm, d.rms_eps, H, which == 0 ? s->out[0] : s->res_h, nullptr, s->ctl, which,
+                          1, 1, cs, pdl);
+}
+
 // The estimator layers over all members' rows (the split form: RMSNorm and
 // attention kernels around four wide tensor-core linears).
 void enqueue_group_layers(vxc_group* g) {
@@ -1367,13 +1495,20 @@ void capture_group_graph(vxc_group* g, int T, float cfg) {
     cudaGraph_t gr = nullptr;
     ck(cudaStreamBeginCapture(c0, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
     try {
+        // per-member small graphs on forked branches, the heavy passes batched on members[0]'s stream
         group_fork(g, 0);
         for (vxc_stream* s : g->members) enqueue_patch_pre(s);
         group_join(g, 0);
         enqueue_group_cfm(g, T, cfg);
         group_fork(g, 1);
-        for (vxc_stream* s : g->members) enqueue_patch_post(s);
+        for (vxc_stream* s : g->members) enqueue_post_stop_feat(s);
         group_join(g, 1);
+        enqueue_group_decoder_step(g, 0);
+        group_fork(g, 2);
+        for (vxc_stream* s : g->members) enqueue_post_fsq_fusion(s);
+        group_join(g, 2);
+        enqueue_group_decoder_step(g, 1);
+        for (vxc_stream* s : g->members) enqueue_post_end(s, g->members[0]->cs);
     } catch (...) {
         cudaStreamEndCapture(c0, &gr);
         if (gr) cudaGraphDestroy(gr);
@@ -2509,7 +2644,7 @@ VXC_API int32_t vxc_group_create(vxc_device* dev, int32_t n_streams, int32_t kv_
             grp->gctl = dev_alloc<StreamCtl>(1);
             ck(cudaMemset(grp->gctl, 0, sizeof(StreamCtl)), "cudaMemset");
             ck(cudaMallocHost(&grp->gctl_host, sizeof(StreamCtl)), "cudaMallocHost");
-            grp->events.assign(3 * static_cast<size_t>(n_streams + 1), nullptr);
+            grp->events.assign(4 * static_cast<size_t>(n_streams + 1), nullptr);
             for (auto& e : grp->events) ck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
         } catch (...) {
             free_group(grp.get());
@@ -2554,7 +2689,7 @@ VXC_API int32_t vxc_group_patch_step_async(vxc_group* g, int32_t min_patches, fl
         capture_group_graph(g, timesteps, cfg_value);
         // The graph runs on members[0]'s stream: it waits for work queued on the
         // other members' streams (noise uploads ...), and their later calls wait for it.
-        const size_t n = g->members.size(), base = 2 * (n + 1);
+        const size_t n = g->members.size(), base = 3 * (n + 1);
         cudaStream_t c0 = g->members[0]->cs;
         for (size_t m = 1; m < n; ++m) {
             ck(cudaEventRecord(g->events[base + m], g->members[m]->cs), "group order");
