@@ -416,21 +416,64 @@ __global__ void embed_gather_kernel(const __half* table, const int32_t* ids, int
 constexpr int kEmbedFeatures = 32;
 constexpr int kEmbedThreads = 256;
 
-__global__ void __launch_bounds__(kEmbedThreads) dit_embed_kernel(const DitEmbedArgs a) {
+__global__ void __launch_bounds__(kEmbedThreads) dit_embed_kernel(const DitEmbedArgs a0) {
     extern __shared__ float sm[];
     pdl_launch_dependents();
+    DitEmbedArgs a = a0;
+    if (a0.members > 0) {  // member blockIdx.y of a group
+        const int m = blockIdx.y;
+        a.x = a0.mx[m];
+        a.cond = a0.mcond[m];
+        a.mu = a0.mmu[m];
+        a.ctl = a0.mctl[m];
+        a.hidden = a0.hidden + m * a0.member_stride;
+        a.ssq_out = nullptr;
+    }
     const int D = a.D, P = a.P, DP = D * P, ws = 2 * D + 1;
     const int f0 = blockIdx.x * kEmbedFeatures;
     float* w_s = sm;                              // [32][2D + 1]: in row, cond row
     float* xs = sm + kEmbedFeatures * ws;         // [2][D*P]
     float* cs = xs + 2 * DP;                      // [2][D*P]
-    // weights first: they do not depend on the previous kernel
-    for (int i = threadIdx.x; i < kEmbedFeatures * 2 * D; i += kEmbedThreads) {
-        const int fl = i / (2 * D), r = i - fl * 2 * D, kind = r / D, e = r - kind * D;
-        const int f = f0 + fl;
-        float w = 0.f;
-        if (f < a.Hd) w = __half2float((kind == 0 ? a.in_w : a.cond_w)[static_cast<size_t>(f) * D + e]);
-        w_s[fl * ws + kind * D + e] = w;
+    // weights first: they do not depend on the previous kernel. This block's rows of
+    // in_w and cond_w are contiguous: 16-byte loads, all issued before any is used.
+    const bool vec = (D & 7) == 0 && D <= 128 &&
+                     ((reinterpret_cast<uintptr_t>(a.in_w) | reinterpret_cast<uintptr_t>(a.cond_w)) & 15) == 0;
+    if (vec) {
+        constexpr int kV = 2;  // 16-byte loads per thread per matrix: 32 rows x D <= 2 * 256 * 8 halves (D <= 128)
+        const int n8 = kEmbedFeatures * D / 8;
+        uint4 wv[2][kV];
+#pragma unroll
+        for (int kind = 0; kind < 2; ++kind)
+#pragma unroll
+            for (int j = 0; j < kV; ++j) {
+                const int i = threadIdx.x + j * kEmbedThreads, fl = (i * 8) / D;
+                const __half* src = (kind == 0 ? a.in_w : a.cond_w) + static_cast<size_t>(f0) * D + i * 8;
+                wv[kind][j] = (i < n8 && f0 + fl < a.Hd) ? *reinterpret_cast<const uint4*>(src) : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+        for (int kind = 0; kind < 2; ++kind)
+#pragma unroll
+            for (int j = 0; j < kV; ++j) {
+                const int i = threadIdx.x + j * kEmbedThreads;
+                if (i >= n8) continue;
+                const int fl = (i * 8) / D, e = i * 8 - fl * D;
+                const __half2* h2 = reinterpret_cast<const __half2*>(&wv[kind][j]);
+                float* dst = w_s + fl * ws + kind * D + e;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float2 f2 = __half22float2(h2[q]);
+                    dst[2 * q] = f2.x;
+                    dst[2 * q + 1] = f2.y;
+                }
+            }
+    } else {
+        for (int i = threadIdx.x; i < kEmbedFeatures * 2 * D; i += kEmbedThreads) {
+            const int fl = i / (2 * D), r = i - fl * 2 * D, kind = r / D, e = r - kind * D;
+            const int f = f0 + fl;
+            float w = 0.f;
+            if (f < a.Hd) w = __half2float((kind == 0 ? a.in_w : a.cond_w)[static_cast<size_t>(f) * D + e]);
+            w_s[fl * ws + kind * D + e] = w;
+        }
     }
     pdl_wait();
     if (a.sync_reset && blockIdx.x == 0)
@@ -524,32 +567,97 @@ __global__ void timestep_embedding_kernel(float t_or_step, float timesteps, int 
 constexpr int kOutFeatures = 4;
 constexpr int kOutThreads = 256;
 
-__global__ void __launch_bounds__(kOutThreads) dit_out_kernel(const DitOutArgs a) {
+__global__ void __launch_bounds__(kOutThreads) dit_out_kernel(const DitOutArgs a0) {
     extern __shared__ float sm[];
     __shared__ double dred[2][kOutThreads / 32];
     __shared__ int s_last;
     pdl_launch_dependents();
+    DitOutArgs a = a0;
+    if (a0.members > 0) {  // member blockIdx.y of a group
+        const int m = blockIdx.y;
+        a.hidden = a0.hidden + m * a0.member_stride;
+        a.x = a0.mx[m];
+        a.ctl = a0.mctl[m];
+        a.est_buf = a0.mest[m];
+        a.counter = a0.mcounter[m];
+        a.est_out = nullptr;
+    }
     const int R = 2 * a.P;        // rows (b, p), at most 8
     const int L = a.D * a.P;      // latent size
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = kOutThreads / 32;
     float* xn = sm;               // [R][Hd]
     float* wsm = sm + R * a.Hd;   // [kOutFeatures][Hd] out_proj rows of this CTA
     const int e0 = blockIdx.x * kOutFeatures;
-    for (int i = threadIdx.x; i < kOutFeatures * a.Hd; i += kOutThreads) {
-        const int el = i / a.Hd, k = i - el * a.Hd;
-        wsm[i] = e0 + el < a.D ? __half2float(a.out_w[static_cast<size_t>(e0 + el) * a.Hd + k]) : 0.f;
+    // this CTA's out_proj rows are contiguous: 16-byte loads, all issued at once
+    const bool vec = (a.Hd & 7) == 0 && a.Hd <= 1024 && (reinterpret_cast<uintptr_t>(a.out_w) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(a.norm_g) & 7) == 0;
+    if (vec) {
+        constexpr int kV = kOutFeatures * 1024 / 8 / kOutThreads;  // Hd <= 1024
+        const int n8 = kOutFeatures * a.Hd / 8;
+        uint4 wv[kV];
+#pragma unroll
+        for (int j = 0; j < kV; ++j) {
+            const int i = threadIdx.x + j * kOutThreads, el = (i * 8) / a.Hd;
+            wv[j] = (i < n8 && e0 + el < a.D)
+                        ? *reinterpret_cast<const uint4*>(a.out_w + static_cast<size_t>(e0) * a.Hd + i * 8)
+                        : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int j = 0; j < kV; ++j) {
+            const int i = threadIdx.x + j * kOutThreads;
+            if (i >= n8) continue;
+            const __half2* h2 = reinterpret_cast<const __half2*>(&wv[j]);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float2 f2 = __half22float2(h2[q]);
+                wsm[i * 8 + 2 * q] = f2.x;
+                wsm[i * 8 + 2 * q + 1] = f2.y;
+            }
+        }
+    } else {
+        for (int i = threadIdx.x; i < kOutFeatures * a.Hd; i += kOutThreads) {
+            const int el = i / a.Hd, k = i - el * a.Hd;
+            wsm[i] = e0 + el < a.D ? __half2float(a.out_w[static_cast<size_t>(e0 + el) * a.Hd + k]) : 0.f;
+        }
     }
     pdl_wait();
     if (a.ctl && a.ctl->stopped) return;
-    // warp r normalises row r
+    // warp r normalises row r (the row read once, as float4, into registers)
     for (int r = warp; r < R; r += nw) {
         const int b = r / a.P, p = r - b * a.P;
         const float* h = a.hidden + (static_cast<size_t>(b) * a.seq + 3 + a.P + p) * a.Hd;
-        float ss = 0.f;
-        for (int k = lane; k < a.Hd; k += 32) ss = fmaf(h[k], h[k], ss);
-        ss = warp_sum(ss);
-        const float inv = rsqrtf(ss / static_cast<float>(a.Hd) + a.eps);
-        for (int k = lane; k < a.Hd; k += 32) xn[r * a.Hd + k] = h[k] * inv * __half2float(a.norm_g[k]);
+        if (vec) {
+            constexpr int kR = 1024 / 4 / 32;  // float4 per lane, Hd <= 1024
+            const int n4 = a.Hd / 4;
+            float4 hv[kR];
+            uint2 gv[kR];
+#pragma unroll
+            for (int j = 0; j < kR; ++j) {
+                const int i = lane + j * 32;
+                hv[j] = i < n4 ? reinterpret_cast<const float4*>(h)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+                gv[j] = i < n4 ? reinterpret_cast<const uint2*>(a.norm_g)[i] : make_uint2(0u, 0u);
+            }
+            float ss = 0.f;
+#pragma unroll
+            for (int j = 0; j < kR; ++j) ss += hv[j].x * hv[j].x + hv[j].y * hv[j].y + hv[j].z * hv[j].z + hv[j].w * hv[j].w;
+            ss = warp_sum(ss);
+            const float inv = rsqrtf(ss / static_cast<float>(a.Hd) + a.eps);
+#pragma unroll
+            for (int j = 0; j < kR; ++j) {
+                const int i = lane + j * 32;
+                if (i >= n4) continue;
+                const float2 g01 = __half22float2(*reinterpret_cast<const __half2*>(&gv[j].x));
+                const float2 g23 = __half22float2(*reinterpret_cast<const __half2*>(&gv[j].y));
+                reinterpret_cast<float4*>(xn + r * a.Hd)[i] =
+                    make_float4(hv[j].x * inv * g01.x, hv[j].y * inv * g01.y, hv[j].z * inv * g23.x, hv[j].w * inv * g23.y);
+            }
+        } else {
+            float ss = 0.f;
+            for (int k = lane; k < a.Hd; k += 32) ss = fmaf(h[k], h[k], ss);
+            ss = warp_sum(ss);
+            const float inv = rsqrtf(ss / static_cast<float>(a.Hd) + a.eps);
+            for (int k = lane; k < a.Hd; k += 32) xn[r * a.Hd + k] = h[k] * inv * __half2float(a.norm_g[k]);
+        }
     }
     __syncthreads();
     // (feature, row) pairs: warp w takes pairs w, w + 8, ...
@@ -831,7 +939,9 @@ void launch_dit_embed(const DitEmbedArgs& a, cudaStream_t s, bool pdl) {
     cudaLaunchAttribute attr[1];
     const size_t smem = static_cast<size_t>(kEmbedFeatures * (2 * a.D + 1) + 4 * a.D * a.P) * sizeof(float);
     if (smem > 200 * 1024) throw std::invalid_argument("dit_embed: patch too large");
-    cudaLaunchConfig_t cfg = make_cfg(dim3((a.Hd + kEmbedFeatures - 1) / kEmbedFeatures), dim3(kEmbedThreads), smem,
+    if (a.members < 0 || a.members > 4) throw std::invalid_argument("dit_embed: 0 to 4 members");
+    cudaLaunchConfig_t cfg = make_cfg(dim3((a.Hd + kEmbedFeatures - 1) / kEmbedFeatures, a.members > 0 ? a.members : 1),
+                                      dim3(kEmbedThreads), smem,
                                       s, pdl, attr);
     check_launch(cudaLaunchKernelEx(&cfg, dit_embed_kernel, a));
 }
@@ -854,7 +964,9 @@ void launch_dit_out(const DitOutArgs& a, cudaStream_t s, bool pdl) {
     const size_t smem = static_cast<size_t>(2 * a.P + kOutFeatures) * a.Hd * sizeof(float);
     if (smem > 200 * 1024) throw std::invalid_argument("dit_out: hidden too large");
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = make_cfg(dim3((a.D + kOutFeatures - 1) / kOutFeatures), dim3(kOutThreads), smem, s, pdl,
+    if (a.members < 0 || a.members > 4) throw std::invalid_argument("dit_out: 0 to 4 members");
+    cudaLaunchConfig_t cfg = make_cfg(dim3((a.D + kOutFeatures - 1) / kOutFeatures, a.members > 0 ? a.members : 1),
+                                      dim3(kOutThreads), smem, s, pdl,
                                       attr);
     check_launch(cudaLaunchKernelEx(&cfg, dit_out_kernel, a));
 }

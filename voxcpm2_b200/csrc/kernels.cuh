@@ -203,6 +203,14 @@ struct DitEmbedArgs {
     float* ssq_out;          // or null: per 32-feature block, row sums of squares [block][24]
     unsigned* sync_reset;    // or null: words zeroed by block 0 (the next persistent launch's sync block)
     int sync_words;
+    // group members (grid y = member, 0 = none): member m replaces x, cond, mu and ctl,
+    // and writes hidden + m * member_stride
+    int members;
+    const float* mx[4];
+    const float* mcond[4];
+    const float* mmu[4];
+    StreamCtl* mctl[4];
+    size_t member_stride;
 };
 void launch_dit_embed(const DitEmbedArgs& a, cudaStream_t s, bool pdl);
 
@@ -222,6 +230,14 @@ struct DitOutArgs {
     StreamCtl* ctl;
     float* est_buf;         // [2][D*P] estimator output (est_out or a scratch buffer)
     int* counter;           // arrival counter, zero between launches
+    // group members (grid y = member, 0 = none): member m reads hidden + m * member_stride
+    // and replaces x, ctl, est_buf and counter
+    int members = 0;
+    float* mx[4] = {};
+    StreamCtl* mctl[4] = {};
+    float* mest[4] = {};
+    int* mcounter[4] = {};
+    size_t member_stride = 0;
 };
 void launch_dit_out(const DitOutArgs& a, cudaStream_t s, bool pdl);
 

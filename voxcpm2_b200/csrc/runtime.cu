@@ -1425,45 +1425,57 @@ void enqueue_group_cfm(vxc_group* g, int T, float cfg) {
     const DitPtrs w = dit_ptrs(dev);
     for (int step = 1; step <= T; ++step) {
         if (step <= z) continue;  // zero-init steps leave x untouched (synthesizer.cpp:123-126)
-        for (size_t m = 0; m < g->members.size(); ++m) {
-            vxc_stream* s = g->members[m];
-            DitEmbedArgs e{};
-            e.in_w = w.in_w;
-            e.in_b = w.in_b;
-            e.cond_w = w.cond_w;
-            e.cond_b = w.cond_b;
-            e.x = s->x;
-            e.cond = s->cond;
-            e.mu = s->mu;
-            e.Hd = Hd;
-            e.D = d.feat_dim;
-            e.P = d.patch_size;
-            e.hidden = g->gdh + m * 2 * seq * static_cast<size_t>(Hd);
-            e.ctl = s->ctl;
-            e.tsum = tab + static_cast<size_t>(step) * Hd;
-            launch_dit_embed(e, s0->cs, s0->pdl);
+        const int n = static_cast<int>(g->members.size());
+        const size_t stride = 2 * seq * static_cast<size_t>(Hd);
+        DitEmbedArgs e{};
+        e.in_w = w.in_w;
+        e.in_b = w.in_b;
+        e.cond_w = w.cond_w;
+        e.cond_b = w.cond_b;
+        e.Hd = Hd;
+        e.D = d.feat_dim;
+        e.P = d.patch_size;
+        e.hidden = g->gdh;
+        e.tsum = tab + static_cast<size_t>(step) * Hd;
+        e.members = n;
+        e.member_stride = stride;
+        for (int m = 0; m < n; ++m) {
+            vxc_stream* s = g->members[static_cast<size_t>(m)];
+            e.mx[m] = s->x;
+            e.mcond[m] = s->cond;
+            e.mmu[m] = s->mu;
+            e.mctl[m] = s->ctl;
         }
+        e.x = e.mx[0];
+        e.cond = e.mcond[0];
+        e.mu = e.mmu[0];
+        launch_dit_embed(e, s0->cs, s0->pdl);
         enqueue_group_layers(g);
-        for (size_t m = 0; m < g->members.size(); ++m) {
-            vxc_stream* s = g->members[m];
-            DitOutArgs o{};
-            o.hidden = g->gdh + m * 2 * seq * static_cast<size_t>(Hd);
-            o.seq = seq;
-            o.Hd = Hd;
-            o.D = d.feat_dim;
-            o.P = d.patch_size;
-            o.norm_g = dev->dit_norm;
-            o.eps = d.rms_eps;
-            o.out_w = w.out_w;
-            o.out_b = w.out_b;
-            o.x = s->x;
-            o.dt = dts[step];
-            o.cfg = cfg;
-            o.ctl = s->ctl;
-            o.est_buf = s->dest;
-            o.counter = s->dcount;
-            launch_dit_out(o, s0->cs, s0->pdl);
+        DitOutArgs o{};
+        o.hidden = g->gdh;
+        o.seq = seq;
+        o.Hd = Hd;
+        o.D = d.feat_dim;
+        o.P = d.patch_size;
+        o.norm_g = dev->dit_norm;
+        o.eps = d.rms_eps;
+        o.out_w = w.out_w;
+        o.out_b = w.out_b;
+        o.dt = dts[step];
+        o.cfg = cfg;
+        o.members = n;
+        o.member_stride = stride;
+        for (int m = 0; m < n; ++m) {
+            vxc_stream* s = g->members[static_cast<size_t>(m)];
+            o.mx[m] = s->x;
+            o.mctl[m] = s->ctl;
+            o.mest[m] = s->dest;
+            o.mcounter[m] = s->dcount;
         }
+        o.x = o.mx[0];
+        o.est_buf = o.mest[0];
+        o.counter = o.mcounter[0];
+        launch_dit_out(o, s0->cs, s0->pdl);
     }
 }
 
