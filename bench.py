@@ -464,6 +464,31 @@ def run_ours(args):
             lat_ms.append(a.elapsed_time(b))
     p50_single = float(np.median(lat_ms))
 
+    # ---- the same for a stream tuned for one utterance at a time: ~296 CTAs per tensor-core
+    # launch and a 4-stage ring (the knobs are read when a stream is created)
+    LATENCY_TUNING = {"VXC_TC_TARGET": "296", "VXC_TC_STAGES": "4"}
+    os.environ.update(LATENCY_TUNING)
+    try:
+        solo = rt.Stream(dev, kv_capacity=max(cap, 512))
+    finally:
+        for k in LATENCY_TUNING:
+            os.environ.pop(k, None)
+    solo.prefill(ids[0])
+    solo.upload_noise(noise[0])
+    ext_solo = torch.cuda.ExternalStream(solo.cuda_stream())
+    lat_solo = []
+    for step in range(W + min(K, 12)):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(ext_solo)
+        solo.patch_step_async(min_patches, CFG, TIMESTEPS)
+        b.record(ext_solo)
+        b.synchronize()
+        if step >= W:
+            lat_solo.append(a.elapsed_time(b))
+    solo_ms, solo_bytes = solo.profile_kernel("dit_gateup", 100)  # the dominant kernel at this tuning
+    solo.close()
+    p50_solo = float(np.median(lat_solo))
+
     # ---- e2e: the public C ABI with host buffers (noise in, latent + state out), one thread per stream
     for s, i in zip(streams, ids):
         s.prefill(i)
@@ -517,6 +542,11 @@ def run_ours(args):
                "sample": f"{args.cpu_sample_patches} patches (after 1 untimed) of one stream, oracle (reference "
                          f"CPU math restated in C++), {threads_cpu} threads"}
 
+    if not kname.startswith("dit_layers"):
+        ach = solo_bytes / (solo_ms / 1e3) / 1e9
+        roofline["latency_tuned"] = {"tuning": LATENCY_TUNING, "us_per_launch": 1e3 * solo_ms, "achieved": ach,
+                                     "frac": ach / peak, "note": "the same kernel in a stream tuned for one "
+                                     "utterance at a time (graph-cycled over the 12 layers, CUDA events)"}
     clk = clocks.summary()
     if rank == 0:
         line = {
@@ -525,6 +555,7 @@ def run_ours(args):
             "dtype": "f16 weights, f32 compute and KV", "data": "synthetic (random fp16 weights N(0,0.02), "
             "uniform token ids, N(0,1) noise)", "config": cfg_info,
             "p50_patch_ms": p50_single, "p50_patch_ms_under_load": float(np.median(calls)),
+            "p50_patch_ms_latency_tuned": p50_solo, "latency_tuning": LATENCY_TUNING,
             "prefill_ms": float(np.median(pre_ms)),
             "per_gpu_patches_per_s": value / world,
             "e2e": {"value": e2e_value, "unit": "patches/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
