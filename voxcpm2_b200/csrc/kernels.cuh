@@ -307,6 +307,16 @@ struct TcLinearArgs {
     // residual epilogue: partial sums of squares of the updated rows, one part per
     // (tile, owner CTA) = tile * splits + rank, written to ssq_out [part][24]
     float* ssq_out = nullptr;
+    // residual epilogue with ssq_out: also write the next linear's TMA-fed B operand,
+    // split fp16 of (updated row * next_g) into next_b [48][ldnb]: its RMSNorm with
+    // the gain applied and the 1 / rms left to the consumer (row_scale)
+    const __half* next_g = nullptr;
+    __half* next_b = nullptr;
+    int ldnb = 0;
+    // consumer of such an operand: token row m of the result is multiplied by
+    // rsqrt(sum of the ssq_parts parts of ssq_in / K + eps), the RMSNorm's 1 / rms
+    // (W (x g) / rms = W (x g / rms))
+    int row_scale = 0;
 };
 enum { TC_B_TMA = 0, TC_B_NORM = 1, TC_B_ATTN = 2 };
 constexpr int kSsqStride = 24;  // floats per part in a sums-of-squares buffer

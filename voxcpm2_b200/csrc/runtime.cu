@@ -378,6 +378,9 @@ struct vxc_stream {
     int tc_target = 32;
     // programmatic dependent launch between the patch graph's kernels (VXC_NO_PDL=1 turns it off)
     bool pdl = true;
+    // split DiT form: RMSNorm folded into the neighbouring linears (the residual epilogue writes the
+    // next operand, the consumer scales rows by 1/rms); VXC_NORM_KERNELS=1 launches separate RMSNorm kernels
+    bool norm_kernels = false;
     // decoder-step GEMVs copy their weight rows into shared memory with the bulk-copy
     // engine before the dependency wait (VXC_BULK_GEMV=0 selects the register-streaming form)
     bool bulk_gemv = true;
@@ -659,8 +662,13 @@ void enqueue_dit_layers(vxc_stream* s, StreamCtl* ctl) {
             qa.eps = d.rms_eps;
             qa.ssq_in = s->dssq;
             qa.ssq_parts = parts;
-        } else {
+        } else if (l == 0 || s->norm_kernels) {
             launch_rmsnorm_rows_split(s->dh, Hd, L.in_norm, d.rms_eps, Hd, M, s->xb_n, ctl, s->cs, s->pdl);
+        } else {  // the previous down projection left split(dh * in_norm) and its sums of squares
+            qa.row_scale = 1;
+            qa.ssq_in = s->dssq;
+            qa.ssq_parts = parts;
+            qa.eps = d.rms_eps;
         }
         launch_tc_linear(maps[0], s->map_xb_n, qa, s->cs, s->pdl);
         TcLinearArgs oa = tc_plan(s, Hd / 128, hq * hd, fused);
@@ -686,6 +694,13 @@ void enqueue_dit_layers(vxc_stream* s, StreamCtl* ctl) {
         } else {
             launch_dit_attention_split(s->dqkv, 2, seq, hq, hkv, hd, dev->dit_rope_cos, dev->dit_rope_sin, scale,
                                        s->xb_a, ctl, s->cs, s->pdl);
+            if (!s->norm_kernels) {
+                // the residual epilogue also writes split(dh * post_norm) for gate/up, and the sums of squares
+                oa.ssq_out = s->dssq;
+                oa.next_g = L.post_norm;
+                oa.next_b = s->xb_n;
+                oa.ldnb = Hd;
+            }
         }
         launch_tc_linear(maps[1], s->map_xb_a, oa, s->cs, s->pdl);
         const int o_parts = (Hd / 128) * oa.splits;
@@ -705,8 +720,13 @@ void enqueue_dit_layers(vxc_stream* s, StreamCtl* ctl) {
             ga.eps = d.rms_eps;
             ga.ssq_in = s->dssq;
             ga.ssq_parts = o_parts;
-        } else {
+        } else if (s->norm_kernels) {
             launch_rmsnorm_rows_split(s->dh, Hd, L.post_norm, d.rms_eps, Hd, M, s->xb_n, ctl, s->cs, s->pdl);
+        } else {
+            ga.row_scale = 1;
+            ga.ssq_in = s->dssq;
+            ga.ssq_parts = o_parts;
+            ga.eps = d.rms_eps;
         }
         launch_tc_linear(maps[2], s->map_xb_n, ga, s->cs, s->pdl);
         TcLinearArgs da = tc_plan(s, Hd / 128, F, false);
@@ -719,6 +739,12 @@ void enqueue_dit_layers(vxc_stream* s, StreamCtl* ctl) {
         da.ldy = Hd;
         da.ctl = ctl;
         if (fused) da.ssq_out = s->dssq;
+        if (!fused && !s->norm_kernels && l + 1 < dev->dit.size()) {  // the next q/k/v operand, split(dh * in_norm)
+            da.ssq_out = s->dssq;
+            da.next_g = dev->dit[l + 1].in_norm;
+            da.next_b = s->xb_n;
+            da.ldnb = Hd;
+        }
         launch_tc_linear(maps[3], s->map_xb_act, da, s->cs, s->pdl);
         parts = (Hd / 128) * da.splits;
     }
@@ -1735,6 +1761,7 @@ VXC_API int32_t vxc_stream_create(vxc_device* dev, int32_t kv_capacity, vxc_stre
         // VXC_DIT_FORM=persistent|fused|split picks one explicitly (an unsupported choice is an error)
         s->dit_grid = dit_layers_grid();
         if (const char* np = std::getenv("VXC_NO_PDL")) s->pdl = std::string(np) != "1";
+        if (const char* nk = std::getenv("VXC_NORM_KERNELS")) s->norm_kernels = std::string(nk) == "1";
         if (const char* bg = std::getenv("VXC_BULK_GEMV")) s->bulk_gemv = std::string(bg) != "0";
         if (const char* tt = std::getenv("VXC_TC_TARGET")) {
             s->tc_target = std::atoi(tt);

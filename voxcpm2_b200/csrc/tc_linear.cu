@@ -364,6 +364,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (tid == 32) mma_loop();
     }
 
+    // row_scale: each token row's 1 / rms from the producer's sums of squares (warp 2,
+    // idle until the epilogue; parts summed in order)
+    if (a.row_scale && warp == 2) {
+        if (lane < a.M) {
+            float t = 0.f;
+#pragma unroll 8
+            for (int p = 0; p < a.ssq_parts; ++p) t += __ldcg(a.ssq_in + p * kSsqStride + lane);
+            inv_s[lane] = rsqrtf(t / static_cast<float>(a.K) + a.eps);
+        }
+    }
+
     // drain the accumulator: warp w owns TMEM lanes (tile rows) 32w .. 32w + 31
     const bool ok = mbar_wait(&done_bar, 0);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -395,8 +406,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int i = 0; i < stages; ++i)
             if (issued[i] > 0 && !mbar_wait(&full_bar[i], (issued[i] - 1) & 1)) failed_s = 1;
     }
+    if (a.row_scale) __syncthreads();  // inv_s is complete
     if (S == 1 && !a.gateup && !a.ssq_out) {
         // no split: straight from registers, coalesced across the warp
+        if (a.row_scale) {
+#pragma unroll
+            for (int m = 0; m < kLoOffset; ++m) v[m] *= inv_s[m];
+        }
         float* yc = a.y + tile * kTileRows + tid;
         float r[kLoOffset];
 #pragma unroll
@@ -463,6 +479,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                             gs += g[j][p];
                             us += up[j][p];
                         }
+                        if (a.row_scale) {
+                            gs *= inv_s[m];
+                            us *= inv_s[m];
+                        }
                         store_split(a.yb, a.ldyb, m, tile * 64 + col, silu(gs) * us);
                     }
                 }
@@ -470,6 +490,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         } else {
             constexpr int kBatch = 8;
             float* yc = a.y + tile * kTileRows + col;
+            const float gn = a.next_b ? __half2float(a.next_g[tile * kTileRows + col]) : 0.f;
             for (int mb = m0; mb < a.M; mb += per * kBatch) {
                 float part[kBatch][S], r[kBatch];
 #pragma unroll
@@ -487,9 +508,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         float sum = 0.f;
 #pragma unroll
                         for (int p = 0; p < S; ++p) sum += part[j][p];
+                        if (a.row_scale) sum *= inv_s[m];
                         const float nv = a.resid ? r[j] + (a.rscale == 1.f ? sum : sum * a.rscale) : sum;
                         yc[static_cast<size_t>(m) * a.ldy] = nv;
                         if (a.ssq_out) sq[m * nu + lu] = nv * nv;
+                        if (a.next_b) store_split(a.next_b, a.ldnb, m, tile * kTileRows + col, nv * gn);
                     }
                 }
             }
@@ -587,6 +610,10 @@ void launch_tc_linear(const CUtensorMap& map_a, const CUtensorMap& map_b, const 
          a.K != a.q_heads * 64 || a.seq <= 0 || a.seq > 12 || a.M != 2 * a.seq || a.attn_round < 1))
         throw std::invalid_argument("tc_linear: bad attention operand");
     if (a.ssq_out && (a.gateup || a.M > kSsqStride)) throw std::invalid_argument("tc_linear: bad ssq_out");
+    if (a.next_b && (!a.ssq_out || !a.next_g || !a.resid || a.ldnb < a.rows))
+        throw std::invalid_argument("tc_linear: next_b needs a residual launch with ssq_out and next_g");
+    if (a.row_scale && (!a.ssq_in || a.ssq_parts <= 0 || a.bmode != TC_B_TMA))
+        throw std::invalid_argument("tc_linear: row_scale needs ssq_in parts and a TMA-fed operand");
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.splits, n_tiles);
     cfg.blockDim = dim3(kTcThreads);
