@@ -55,6 +55,14 @@ def test_null_arguments_are_invalid_argument(rt):
     assert rt.lib().vxc_device_create(0, None, C.byref(h)) == 1
     assert b"null" in rt.lib().vxc_last_error()
     assert rt.lib().vxc_stream_create(None, 16, C.byref(h)) == 1
+    # stream groups
+    assert rt.lib().vxc_group_create(None, 2, 16, C.byref(h)) == 1
+    assert rt.lib().vxc_group_stream(None, 0, C.byref(h)) == 1
+    assert rt.lib().vxc_group_patch_step_async(None, 1, 2.0, 10) == 1
+    assert rt.lib().vxc_group_synchronize(None) == 1
+    n = C.c_int32()
+    assert rt.lib().vxc_group_graph_kernels(None, C.byref(n)) == 1
+    rt.lib().vxc_group_destroy(None)  # a no-op
 
 
 def test_bad_model_description_rejected(rt):

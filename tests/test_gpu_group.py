@@ -158,3 +158,28 @@ def test_group_members_stop_independently(rt):
     assert sum(f is not None for f in first_stop) >= 2
     g.close()
     dev.close()
+
+
+def test_group_rejects_bad_use(rt):
+    """Errors come back as statuses before anything is launched: an empty group, a
+    step before every member is prefilled, non-positive timesteps."""
+    blobs = synthetic.model_blobs(TINY, 0)
+    dev = rt.Device(TINY, 0, blobs)
+    with pytest.raises(rt.VxcError):
+        rt.Group(dev, 0, kv_capacity=64)
+    g = rt.Group(dev, 2, kv_capacity=64)
+    with pytest.raises(rt.VxcError):
+        g.patch_step_async(2, 2.0, 6)  # no member prefilled
+    g.streams[0].prefill(synthetic.token_ids(TINY, 6, seed=1))
+    with pytest.raises(rt.VxcError):
+        g.patch_step_async(2, 2.0, 6)  # member 1 not prefilled
+    g.streams[1].prefill(synthetic.token_ids(TINY, 7, seed=2))
+    with pytest.raises(rt.VxcError):
+        g.patch_step_async(2, 2.0, 0)
+    for st, seed in zip(g.streams, (5, 6)):
+        st.upload_noise(oracle.noise_table(seed, 2, TINY.latent))
+    g.patch_step_async(10, 2.0, 6)  # the group still works after the rejected calls
+    g.synchronize()
+    assert [st.state().patches for st in g.streams] == [1, 1]
+    g.close()
+    dev.close()
