@@ -381,9 +381,10 @@ struct vxc_stream {
     // split DiT form: RMSNorm folded into the neighbouring linears (the residual epilogue writes the
     // next operand, the consumer scales rows by 1/rms); VXC_NORM_KERNELS=1 launches separate RMSNorm kernels
     bool norm_kernels = false;
-    // decoder-step GEMVs copy their weight rows into shared memory with the bulk-copy
-    // engine before the dependency wait (VXC_BULK_GEMV=0 selects the register-streaming form)
-    bool bulk_gemv = true;
+    // decoder-step GEMVs: register-streaming (the default: the highest 16-stream throughput), or
+    // VXC_BULK_GEMV=1 for the bulk-copy form (weight rows into shared memory before the
+    // dependency wait; stream groups always use it, batched over their members)
+    bool bulk_gemv = false;
     float* dpart = nullptr;     // persistent launch: partial tiles
     unsigned* dsync = nullptr;  // persistent launch: grid barrier and tile counters
     int* dcount = nullptr;  // dit_out arrival counter
@@ -1762,7 +1763,7 @@ VXC_API int32_t vxc_stream_create(vxc_device* dev, int32_t kv_capacity, vxc_stre
         s->dit_grid = dit_layers_grid();
         if (const char* np = std::getenv("VXC_NO_PDL")) s->pdl = std::string(np) != "1";
         if (const char* nk = std::getenv("VXC_NORM_KERNELS")) s->norm_kernels = std::string(nk) == "1";
-        if (const char* bg = std::getenv("VXC_BULK_GEMV")) s->bulk_gemv = std::string(bg) != "0";
+        if (const char* bg = std::getenv("VXC_BULK_GEMV")) s->bulk_gemv = std::string(bg) == "1";
         if (const char* tt = std::getenv("VXC_TC_TARGET")) {
             s->tc_target = std::atoi(tt);
             if (s->tc_target < 1 || s->tc_target > 4096) throw std::invalid_argument("VXC_TC_TARGET must be in [1, 4096]");
