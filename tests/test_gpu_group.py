@@ -56,8 +56,11 @@ def check_members(orc, prompts, seeds, got, patches, timesteps=10, cfg_value=2.0
         assert err <= 2e-2 and cos >= 0.999, (m, err, cos)
 
 
-@pytest.mark.parametrize("members", [1, 4])
-def test_group_tiny_matches_oracle(rt, members):
+@pytest.mark.parametrize("members,bulk", [(1, "0"), (4, "0"), (4, "1")])
+def test_group_tiny_matches_oracle(rt, members, bulk, monkeypatch):
+    """TINY groups of 1 and 4 members; the decoder GEMVs in the register-streaming
+    batch form (the default) and in the bulk-copy form (VXC_GROUP_BULK_GEMV=1)."""
+    monkeypatch.setenv("VXC_GROUP_BULK_GEMV", bulk)
     blobs = synthetic.model_blobs(TINY, 0)
     dev = rt.Device(TINY, 0, blobs)
     orc = oracle.Oracle(TINY, blobs)

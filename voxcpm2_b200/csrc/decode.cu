@@ -196,6 +196,142 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
     gemv_store<MODE, RPW>(a, item, row, acc);
 }
 
+// The register-streaming GEMV for up to kGemvBatch members (streams of a group):
+// each warp's weight rows are loaded once into registers, every member's input is
+// staged (and RMS-normalised) in shared memory, and the warp forms one dot product
+// per member; lane m stores member m. IN_PLAIN inputs only.
+template <int MODE, int MAXCH, int RPW>
+__global__ void __launch_bounds__(kGemvThreads) gemv_batch_kernel(const GemvArgs a, const GemvBatch b) {
+    constexpr int NB = kGemvBatch;
+    extern __shared__ float xs[];  // [nb][K]
+    __shared__ float red[NB][kGemvWarps];
+    pdl_launch_dependents();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int item = blockIdx.x * kGemvWarps + warp;
+    const bool active = item < a.rows;
+    const int K = a.K;
+    int row[RPW];
+    if constexpr (MODE == GEMV_GATEUP) {
+        row[0] = item;
+        row[1] = item + a.rows;
+    } else if constexpr (MODE == GEMV_QKV) {
+        const int half = a.head_dim >> 1;
+        const int hh = item / half, j = item - hh * half;
+        row[0] = hh * a.head_dim + j;
+        row[1] = row[0] + half;
+    } else {
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) row[r] = item * RPW + r;
+    }
+    uint4 wr[RPW][MAXCH];
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+        const __half* wrow = a.w + static_cast<size_t>(row[r]) * K;
+#pragma unroll
+        for (int c = 0; c < MAXCH; ++c) {
+            const int e = (c * kWarp + lane) * 8;
+            wr[r][c] = (active && e < K) ? ld_stream(wrow + e) : make_uint4(0, 0, 0, 0);
+        }
+    }
+    pdl_wait();
+    bool live[NB];
+    bool any = false;
+#pragma unroll
+    for (int m = 0; m < NB; ++m) {
+        live[m] = m < b.n && !(a.skip_if_stopped && b.ctl[m] && b.ctl[m]->stopped);
+        any = any || live[m];
+    }
+    if (!any) return;
+    constexpr int kV = MAXCH >= 2 ? MAXCH / 2 : 1;
+    const int n4 = K >> 2;
+    uint2 gv[kV];
+#pragma unroll
+    for (int j = 0; j < kV; ++j) {
+        const int i = threadIdx.x + j * kGemvThreads;
+        gv[j] = (a.norm_g && i < n4) ? reinterpret_cast<const uint2*>(a.norm_g)[i] : make_uint2(0u, 0u);
+    }
+#pragma unroll
+    for (int m = 0; m < NB; ++m) {
+        if (!live[m]) continue;
+        float4 xv[kV];
+#pragma unroll
+        for (int j = 0; j < kV; ++j) {
+            const int i = threadIdx.x + j * kGemvThreads;
+            xv[j] = i < n4 ? reinterpret_cast<const float4*>(b.x[m])[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < kV; ++j) {
+            const int i = threadIdx.x + j * kGemvThreads;
+            if (i < n4) {
+                float4 v = xv[j];
+                ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                if (a.norm_g) {
+                    const float2 g01 = __half22float2(*reinterpret_cast<const __half2*>(&gv[j].x));
+                    const float2 g23 = __half22float2(*reinterpret_cast<const __half2*>(&gv[j].y));
+                    v = make_float4(v.x * g01.x, v.y * g01.y, v.z * g23.x, v.w * g23.y);
+                }
+                reinterpret_cast<float4*>(xs + static_cast<size_t>(m) * K)[i] = v;
+            }
+        }
+        if (a.norm_g) {
+            ss = warp_sum(ss);
+            if (lane == 0) red[m][warp] = ss;
+        }
+    }
+    __syncthreads();
+    float inv_rms[NB];
+#pragma unroll
+    for (int m = 0; m < NB; ++m) {
+        inv_rms[m] = 1.f;
+        if (a.norm_g && live[m]) {
+            float t = 0.f;
+#pragma unroll
+            for (int w = 0; w < kGemvWarps; ++w) t += red[m][w];
+            inv_rms[m] = rsqrtf(t / static_cast<float>(K) + a.eps);
+        }
+    }
+    if (!active) return;
+    float acc[NB][RPW];
+#pragma unroll
+    for (int m = 0; m < NB; ++m)
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) acc[m][r] = 0.f;
+#pragma unroll
+    for (int c = 0; c < MAXCH; ++c) {
+        const int e = (c * kWarp + lane) * 8;
+        if (e < K) {
+#pragma unroll
+            for (int m = 0; m < NB; ++m) {
+                if (!live[m]) continue;
+                const float* xm = xs + static_cast<size_t>(m) * K;
+                const float4 x0 = *reinterpret_cast<const float4*>(&xm[e]);
+                const float4 x1 = *reinterpret_cast<const float4*>(&xm[e + 4]);
+#pragma unroll
+                for (int r = 0; r < RPW; ++r) acc[m][r] = dot8(wr[r][c], x0, x1, acc[m][r]);
+            }
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < NB; ++m) {
+        if (!live[m]) continue;
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) acc[m][r] = warp_sum(acc[m][r]) * inv_rms[m];
+    }
+#pragma unroll
+    for (int m = 0; m < NB; ++m) {
+        if (lane != m || !live[m]) continue;
+        GemvArgs am = a;
+        am.x = b.x[m];
+        am.y = b.y[m];
+        am.resid = b.resid[m];
+        am.k_cache = b.k_cache[m];
+        am.v_cache = b.v_cache[m];
+        am.ctl = b.ctl[m];
+        gemv_store<MODE, RPW>(am, item, row, acc[m]);
+    }
+}
+
 cudaLaunchConfig_t make_cfg(dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
                             cudaLaunchAttribute* attr) {
     cudaLaunchConfig_t cfg = {};
@@ -463,6 +599,21 @@ void dispatch_gemv_bulk(const GemvArgs& a, const GemvBatch& b, cudaStream_t s, b
     check_launch(cudaLaunchKernelEx(&cfg, gemv_bulk_kernel<MODE>, a, b, upb));
 }
 
+template <int MODE, int RPW>
+void dispatch_gemv_batch(const GemvArgs& a, const GemvBatch& b, cudaStream_t s, bool pdl) {
+    const int nch = (a.K + 255) / 256;
+    const int blocks = (a.rows + kGemvWarps - 1) / kGemvWarps;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(dim3(blocks), dim3(kGemvThreads),
+                                      static_cast<size_t>(b.n) * ((a.K + 7) / 8) * 8 * sizeof(float), s, pdl, attr);
+    if (nch <= 1) check_launch(cudaLaunchKernelEx(&cfg, gemv_batch_kernel<MODE, 1, RPW>, a, b));
+    else if (nch <= 2) check_launch(cudaLaunchKernelEx(&cfg, gemv_batch_kernel<MODE, 2, RPW>, a, b));
+    else if (nch <= 4) check_launch(cudaLaunchKernelEx(&cfg, gemv_batch_kernel<MODE, 4, RPW>, a, b));
+    else if (nch <= 8) check_launch(cudaLaunchKernelEx(&cfg, gemv_batch_kernel<MODE, 8, RPW>, a, b));
+    else if (RPW == 1 && nch <= 16) check_launch(cudaLaunchKernelEx(&cfg, gemv_batch_kernel<MODE, 16, 1>, a, b));
+    else throw std::invalid_argument("gemv_batch: input dimension too large");
+}
+
 // ------------------------------------------------------------ attention ---
 constexpr int kAttnThreads = 128;
 constexpr int kMaxGroup = 16;
@@ -726,6 +877,27 @@ void launch_gemv_bulk(const GemvArgs& a, cudaStream_t s, bool pdl) {
     launch_gemv_bulk_batch(a, b, s, pdl);
 }
 
+void launch_gemv_batch(const GemvArgs& a, const GemvBatch& b, cudaStream_t s, bool pdl) {
+    bool aligned = true;
+    for (int m = 0; m < b.n; ++m) aligned = aligned && (reinterpret_cast<uintptr_t>(b.x[m]) & 15) == 0;
+    if (a.K <= 0 || a.K % 8 != 0 || a.rows <= 0 || a.in_mode != IN_PLAIN || b.n < 1 || b.n > kGemvBatch ||
+        !aligned || (reinterpret_cast<uintptr_t>(a.norm_g) & 7) != 0 ||
+        static_cast<size_t>(b.n) * a.K * 4 > 160 * 1024)
+        throw std::invalid_argument("gemv_batch: bad shape, batch or alignment");
+    switch (a.mode) {
+        case GEMV_PLAIN: dispatch_gemv_batch<GEMV_PLAIN, 1>(a, b, s, pdl); break;
+        case GEMV_RESID: dispatch_gemv_batch<GEMV_RESID, 1>(a, b, s, pdl); break;
+        case GEMV_GATEUP: dispatch_gemv_batch<GEMV_GATEUP, 2>(a, b, s, pdl); break;
+        case GEMV_QKV:
+            for (int m = 0; m < b.n; ++m)
+                if (b.ctl[m] == nullptr) throw std::invalid_argument("gemv_batch: q/k/v needs a control block");
+            if (a.head_dim % 2 != 0) throw std::invalid_argument("gemv_batch: bad q/k/v setup");
+            dispatch_gemv_batch<GEMV_QKV, 2>(a, b, s, pdl);
+            break;
+        default: throw std::invalid_argument("gemv_batch: unknown mode");
+    }
+}
+
 void launch_gemv(const GemvArgs& a, cudaStream_t s, bool pdl) {
     if (a.K <= 0 || a.K % 8 != 0 || a.rows <= 0) throw std::invalid_argument("gemv: bad shape");
     switch (a.mode) {
@@ -878,8 +1050,25 @@ void launch_attn_decode(const AttnArgs& a, bool fp16_kv, cudaStream_t s, bool pd
 
 void init_batched_attributes();
 
+template <int MODE, int RPW>
+void set_gemv_batch_attributes() {
+    constexpr int kSmem = 160 * 1024;  // up to kGemvBatch inputs of K <= 4096 (+ slack)
+    for (const void* f : {reinterpret_cast<const void*>(gemv_batch_kernel<MODE, 1, RPW>),
+                          reinterpret_cast<const void*>(gemv_batch_kernel<MODE, 2, RPW>),
+                          reinterpret_cast<const void*>(gemv_batch_kernel<MODE, 4, RPW>),
+                          reinterpret_cast<const void*>(gemv_batch_kernel<MODE, 8, RPW>)})
+        check_launch(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
+    if constexpr (RPW == 1)
+        check_launch(cudaFuncSetAttribute(gemv_batch_kernel<MODE, 16, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          kSmem));
+}
+
 void init_kernel_attributes() {
     constexpr int kMax = 200 * 1024;
+    set_gemv_batch_attributes<GEMV_PLAIN, 1>();
+    set_gemv_batch_attributes<GEMV_RESID, 1>();
+    set_gemv_batch_attributes<GEMV_GATEUP, 2>();
+    set_gemv_batch_attributes<GEMV_QKV, 2>();
     check_launch(cudaFuncSetAttribute(attn_decode_kernel<__half, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax));
     check_launch(cudaFuncSetAttribute(attn_decode_kernel<float, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax));
     for (const void* f : {reinterpret_cast<const void*>(gemv_bulk_kernel<GEMV_PLAIN>),

@@ -76,6 +76,8 @@ struct GemvBatch {
     StreamCtl* ctl[kGemvBatch] = {};
 };
 void launch_gemv_bulk_batch(const GemvArgs& a, const GemvBatch& b, cudaStream_t s, bool pdl);
+// The register-streaming form of the same member batch (weights loaded once per warp).
+void launch_gemv_batch(const GemvArgs& a, const GemvBatch& b, cudaStream_t s, bool pdl);
 
 // ------------------------------------------------------ flash decode -----
 // One query token of each of q_heads heads attends over keys [0, T) of a GQA

@@ -1259,6 +1259,8 @@ struct vxc_group {
     int tc_target = 32;              // CTAs aimed at per wide linear (VXC_GROUP_TC_TARGET; 32 suits
                                      // several groups at once, 148 a lone group's latency)
     int tc_stages = 2;               // TMA ring depth of the wide linears (VXC_GROUP_TC_STAGES)
+    bool bulk_gemv = false;          // decoder GEMVs: register-streaming batch form (0, the faster), or
+                                     // bulk-copy (VXC_GROUP_BULK_GEMV=1)
     StreamCtl* gctl = nullptr;       // error reports of the batched linears
     StreamCtl* gctl_host = nullptr;
     std::vector<cudaEvent_t> events;  // fork / join points of the group graph
@@ -1273,7 +1275,7 @@ namespace {
 
 // One decoder step (base: which 0, residual: 1) of every member at once
 // (base_decoder_kv / residual_decoder_kv, tools/export_components.py:496-550):
-// each linear reads its weights once for all members (gemv_bulk_batch), the
+// each linear reads its weights once for all members (member-batched GEMV), the
 // attention runs one cluster per (member, KV head) over the member's own cache,
 // and every member keeps its own KV length and stop flag.
 void enqueue_group_decoder_step(vxc_group* g, int which) {
@@ -1287,6 +1289,7 @@ void enqueue_group_decoder_step(vxc_group* g, int which) {
     const int n = static_cast<int>(g->members.size());
     cudaStream_t cs = s0->cs;
     const bool pdl = s0->pdl;
+    auto gemv = g->bulk_gemv ? launch_gemv_bulk_batch : launch_gemv_batch;
     for (size_t l = 0; l < layers.size(); ++l) {
         const LayerW& L = layers[l];
         GemvBatch qb, ob, gb, db;
@@ -1330,7 +1333,7 @@ void enqueue_group_decoder_step(vxc_group* g, int which) {
         qa.cap = s0->cap;
         qa.which = which;
         qa.skip_if_stopped = 1;
-        launch_gemv_bulk_batch(qa, qb, cs, pdl);
+        gemv(qa, qb, cs, pdl);
 
         AttnArgs aa;
         aa.k0 = ab.k0[0];
@@ -1353,7 +1356,7 @@ void enqueue_group_decoder_step(vxc_group* g, int which) {
         oa.rows = H;
         oa.rscale = rscale;
         oa.skip_if_stopped = 1;
-        launch_gemv_bulk_batch(oa, ob, cs, pdl);
+        gemv(oa, ob, cs, pdl);
 
         GemvArgs ga;
         ga.mode = GEMV_GATEUP;
@@ -1363,7 +1366,7 @@ void enqueue_group_decoder_step(vxc_group* g, int which) {
         ga.K = H;
         ga.rows = F;
         ga.skip_if_stopped = 1;
-        launch_gemv_bulk_batch(ga, gb, cs, pdl);
+        gemv(ga, gb, cs, pdl);
 
         GemvArgs da;
         da.mode = GEMV_RESID;
@@ -1372,7 +1375,7 @@ void enqueue_group_decoder_step(vxc_group* g, int which) {
         da.rows = H;
         da.rscale = rscale;
         da.skip_if_stopped = 1;
-        launch_gemv_bulk_batch(da, db, cs, pdl);
+        gemv(da, db, cs, pdl);
     }
     for (vxc_stream* s : g->members)
         launch_final_norm(s->h[which], fnorm, d.rms_eps, H, which == 0 ? s->out[0] : s->res_h, nullptr, s->ctl, which,
@@ -2656,6 +2659,7 @@ VXC_API int32_t vxc_group_create(vxc_device* dev, int32_t n_streams, int32_t kv_
             grp->tc_target = std::atoi(tt);
             require(grp->tc_target >= 1 && grp->tc_target <= 4096, "VXC_GROUP_TC_TARGET must be in [1, 4096]");
         }
+        if (const char* bg = std::getenv("VXC_GROUP_BULK_GEMV")) grp->bulk_gemv = std::string(bg) == "1";
         if (const char* st = std::getenv("VXC_GROUP_TC_STAGES")) {
             grp->tc_stages = std::atoi(st);
             require(grp->tc_stages >= 1 && grp->tc_stages <= 4, "VXC_GROUP_TC_STAGES must be in [1, 4]");
