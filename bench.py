@@ -435,7 +435,7 @@ def run_ours(args):
     # one whole KV-cache decode step at batch 1 (configs 2 and 3: every weight of the
     # decoder once + the K/V rows), replayed as a graph at the stream's KV length
     decode_step = {}
-    for k, name in (("base_step", "base_decoder"), ("res_step", "residual_decoder")):
+    for k, name in (("base_step", "base_decoder"), ("res_step", "residual_decoder"), ("dit_eval", "dit_estimator_eval")):
         km, kb = streams[0].profile_kernel(k, 50)
         gbs = kb / (km / 1e3) / 1e9
         decode_step[name] = {"us": round(1e3 * km, 2), "bytes": kb, "GB/s": round(gbs, 1), "frac": gbs / peak,
@@ -486,6 +486,11 @@ def run_ours(args):
         if step >= W:
             lat_solo.append(a.elapsed_time(b))
     solo_ms, solo_bytes = solo.profile_kernel("dit_gateup", 100)  # the dominant kernel at this tuning
+    ev_ms, ev_bytes = solo.profile_kernel("dit_eval", 20)
+    decode_step["dit_estimator_eval_latency_tuned"] = {"us": round(1e3 * ev_ms, 2), "bytes": ev_bytes,
+                                                        "GB/s": round(ev_bytes / (ev_ms / 1e3) / 1e9, 1),
+                                                        "frac": ev_bytes / (ev_ms / 1e3) / 1e9 / peak,
+                                                        "tuning": LATENCY_TUNING}
     solo.close()
     p50_solo = float(np.median(lat_solo))
 

@@ -115,6 +115,7 @@ enum {
     VXC_PROF_DIT_LAYERS = 8,   /* persistent DiT decoder: all layers of one evaluation (one launch) */
     VXC_PROF_BASE_STEP = 9,    /* one whole base decoder KV-cache step (24 layers + final norm) */
     VXC_PROF_RES_STEP = 10,    /* one whole residual decoder KV-cache step */
+    VXC_PROF_DIT_EVAL = 11,    /* one whole DiT estimator evaluation (embed, 12 layers, out projection) */
 };
 
 /* Progress callback of vxc_generate: return non-zero to continue, zero to cancel

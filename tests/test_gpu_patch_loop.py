@@ -282,8 +282,9 @@ def test_time_tables_follow_weight_reload(rt, tiny):
 
 
 def test_decode_step_profile_keeps_stream_state(rt, tiny):
-    """The whole-step profiles run on a private control block and write their
-    output to scratch: the stream's KV lengths and its next patch are unaffected."""
+    """The whole-step and whole-evaluation profiles run on a private control block
+    and write their output to scratch: the stream's KV lengths and its next patch
+    are unaffected."""
     cfg, blobs, dev, orc = tiny
     ids = synthetic.token_ids(cfg, 8, seed=4)
     noise = oracle.noise_table(6, 4, cfg.latent)
@@ -291,11 +292,14 @@ def test_decode_step_profile_keeps_stream_state(rt, tiny):
     a.prefill(ids)
     a.patch_step(noise[0], min_patches=10, step=0, cfg_value=2.0, timesteps=5)
     before = a.state()
-    for k in ("base_step", "res_step"):
+    for k in ("base_step", "res_step", "dit_eval"):
         ms, nb = a.profile_kernel(k, 5)
         assert ms > 0
-        layers = cfg.base_layers if k == "base_step" else cfg.res_layers
-        assert nb > 2 * layers * 3 * cfg.ffn * cfg.hidden  # at least the MLP weights
+        if k == "dit_eval":
+            assert nb > 2 * cfg.dit_layers * 3 * cfg.dit_ffn * cfg.dit_hidden  # at least the MLP weights
+        else:
+            layers = cfg.base_layers if k == "base_step" else cfg.res_layers
+            assert nb > 2 * layers * 3 * cfg.ffn * cfg.hidden
     after = a.state()
     assert (after.kv_len[0], after.kv_len[1], after.patches) == (before.kv_len[0], before.kv_len[1], before.patches)
     x1, _ = a.patch_step(noise[1], min_patches=10, step=1, cfg_value=2.0, timesteps=5)

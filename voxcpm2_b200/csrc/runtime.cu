@@ -2346,6 +2346,23 @@ std::vector<std::function<void(bool)>> profile_launches(vxc_stream* s, int kerne
     const int pos = std::min(s->kv_len[0], s->cap - 1);
     const int T = pos + 1;
     StreamCtl* pctl = reinterpret_cast<StreamCtl*>(s->est);  // >= sizeof(StreamCtl) floats
+    if (kernel == VXC_PROF_DIT_EVAL) {
+        // one whole estimator evaluation (embed, the 12 layers in the stream's DiT form, out
+        // projection), on the stream's current x / cond / mu and the cached time row of step 1
+        // of 10; no Euler update (the estimate goes to scratch), a private control block
+        const float* tab = time_table(s, 10);
+        StreamCtl probe{};
+        ck(cudaMemcpyAsync(pctl, &probe, sizeof(StreamCtl), cudaMemcpyHostToDevice, s->cs), "probe ctl");
+        ck(cudaStreamSynchronize(s->cs), "sync");
+        const double D = d.feat_dim;
+        const double per_layer = static_cast<double>(Wd) * Hd + static_cast<double>(Hd) * dq * 64 + 3.0 * Fd * Hd + 2.0 * Hd;
+        bytes = 2.0 * (per_layer * dev->dit.size() + 2.0 * (Hd * D + Hd) + D * Hd + D + Hd);
+        launch.push_back([=](bool) {
+            enqueue_dit_eval(s, s->x, nullptr, s->mu, nullptr, s->cond, nullptr, false, s->dest, nullptr, 0.f, 2.f, pctl,
+                             tab + Hd);
+        });
+        return launch;
+    }
     if (kernel == VXC_PROF_BASE_STEP || kernel == VXC_PROF_RES_STEP) {
         // a whole decoder step over the stream's current KV length, on a private
         // control block that it does not advance (each replay re-appends the same row)
@@ -2499,7 +2516,7 @@ VXC_API int32_t vxc_profile_kernel(vxc_stream* s, int32_t kernel, int32_t iters,
     return guard([&] {
         require(s != nullptr && ms_per_launch != nullptr && bytes_per_launch != nullptr, "null argument");
         require(iters > 0 && iters <= 100000, "iters must be in [1, 100000]");
-        require(kernel >= VXC_PROF_DIT_GATEUP && kernel <= VXC_PROF_RES_STEP, "unknown kernel id");
+        require(kernel >= VXC_PROF_DIT_GATEUP && kernel <= VXC_PROF_DIT_EVAL, "unknown kernel id");
         std::lock_guard<std::mutex> lk(s->call_mutex);
         const vxc_device* dev = s->dev;
         const vxc_model_desc& d = dev->desc;

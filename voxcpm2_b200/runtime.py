@@ -55,7 +55,8 @@ class StreamState(C.Structure):
 
 
 PROFILE_KERNELS = {"dit_gateup": 0, "dit_down": 1, "dit_qkv": 2, "base_gateup": 3, "base_down": 4,
-                   "base_qkv": 5, "base_attn": 6, "dit_o": 7, "dit_layers": 8, "base_step": 9, "res_step": 10}
+                   "base_qkv": 5, "base_attn": 6, "dit_o": 7, "dit_layers": 8, "base_step": 9, "res_step": 10,
+                   "dit_eval": 11}
 
 
 PROGRESS_FN = C.CFUNCTYPE(C.c_int32, C.c_void_p, C.c_int32, C.c_int32)
