@@ -89,3 +89,13 @@ def test_product_never_imports_the_oracle():
     for path in list(pkg.glob("*.py")) + list((pkg / "csrc").glob("*")):
         text = path.read_text(errors="ignore")
         assert "import oracle" not in text and "from oracle" not in text and "liborc" not in text, path
+
+
+def test_profile_kernel_ids_match_header():
+    """runtime.PROFILE_KERNELS mirrors the header's VXC_PROF_* enum."""
+    import re
+    from voxcpm2_b200 import runtime
+    text = (ROOT / "include" / "voxcpm2_cuda.h").read_text()
+    ids = {m.group(1).lower(): int(m.group(2)) for m in re.finditer(r"VXC_PROF_([A-Z_]+)\s*=\s*(\d+)", text)}
+    assert ids, "no VXC_PROF_* enumerators found"
+    assert runtime.PROFILE_KERNELS == ids
