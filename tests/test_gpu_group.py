@@ -186,3 +186,19 @@ def test_group_rejects_bad_use(rt):
     assert [st.state().patches for st in g.streams] == [1, 1]
     g.close()
     dev.close()
+
+
+def test_group_receive_buffer_forms_bit_identical(rt, monkeypatch):
+    """The wide linears' split-K partials in the stage area (the default) or in a
+    dedicated buffer (VXC_GROUP_RECV_SHARED=0): same sums, identical latents."""
+    blobs = synthetic.model_blobs(TINY, 0)
+    dev = rt.Device(TINY, 0, blobs)
+    prompts = [synthetic.token_ids(TINY, 6 + m, seed=80 + m) for m in range(4)]
+    got = []
+    for env in ("1", "0"):
+        monkeypatch.setenv("VXC_GROUP_RECV_SHARED", env)
+        lat, _ = run_group(rt, TINY, dev, prompts, [90, 91, 92, 93], patches=4, timesteps=6)
+        got.append(lat)
+    for a, b in zip(*got):
+        assert np.array_equal(a, b)
+    dev.close()

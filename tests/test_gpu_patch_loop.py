@@ -310,3 +310,19 @@ def test_decode_step_profile_keeps_stream_state(rt, tiny):
     assert np.array_equal(x1, y1)
     a.close()
     b.close()
+
+
+def test_shared_receive_buffer_is_bit_identical(rt, bench, monkeypatch):
+    """VXC_RECV_SHARED=1 only moves the split-K receive buffer into the stage area
+    (same rank-order sums): the latents are bit-identical to the default's."""
+    cfg, blobs, dev, orc = bench
+    ids = synthetic.token_ids(cfg, 16, seed=8)
+    a = rt.Stream(dev, kv_capacity=64)
+    monkeypatch.setenv("VXC_RECV_SHARED", "1")
+    b = rt.Stream(dev, kv_capacity=64)
+    monkeypatch.delenv("VXC_RECV_SHARED")
+    ra = a.generate(ids, min_patches=100, timesteps=10, cfg_value=2.0, max_patches_override=3, seed=4, trace=False)
+    rb = b.generate(ids, min_patches=100, timesteps=10, cfg_value=2.0, max_patches_override=3, seed=4, trace=False)
+    assert np.array_equal(ra["latents"], rb["latents"])
+    a.close()
+    b.close()

@@ -319,12 +319,16 @@ struct TcLinearArgs {
     // rsqrt(sum of the ssq_parts parts of ssq_in / K + eps), the RMSNorm's 1 / rms
     // (W (x g) / rms = W (x g / rms))
     int row_scale = 0;
+    // K split with a TMA-fed operand: receive the cluster's partials (and keep the
+    // squares) in the idle stage area after one more cluster barrier, instead of a
+    // dedicated buffer behind it (smaller CTAs, more of them per SM)
+    int recv_shared = 0;
 };
 enum { TC_B_TMA = 0, TC_B_NORM = 1, TC_B_ATTN = 2 };
 constexpr int kSsqStride = 24;  // floats per part in a sums-of-squares buffer
 CUtensorMap make_tensor_map_f16(const void* base, int rows, int cols, int box_rows);
 size_t tc_linear_smem_bytes(int K, int splits, int bmode, int attn_round = 1, int max_stages = 8,
-                            bool ssq_out = false);
+                            bool ssq_out = false, bool recv_shared = false);
 // heads per attention round that fit beside the stages of a TC_B_ATTN launch (2, else 1)
 int tc_attn_round(int K, int splits, int max_stages = 8);
 void launch_tc_linear(const CUtensorMap& map_a, const CUtensorMap& map_b, const TcLinearArgs& a, cudaStream_t s,
@@ -368,6 +372,9 @@ struct TcWideArgs {
     int ldyb = 0;
     int stages = 2;            // shared-memory ring depth (1..4)
     StreamCtl* ctl = nullptr;  // receives error 3 if a bounded wait gave up
+    // K split: receive the cluster's partials in the (by then idle) stage area after one
+    // more cluster barrier, instead of a dedicated 48 KB buffer (more CTAs per SM)
+    int recv_shared = 0;
 };
 void launch_tc_wide(const CUtensorMap& map_a, const CUtensorMap& map_b, const TcWideArgs& a, cudaStream_t s,
                     bool pdl);

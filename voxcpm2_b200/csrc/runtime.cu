@@ -378,6 +378,8 @@ struct vxc_stream {
     int tc_target = 32;
     // programmatic dependent launch between the patch graph's kernels (VXC_NO_PDL=1 turns it off)
     bool pdl = true;
+    // split tcgen05 linears receive their partials in the idle stage area (VXC_RECV_SHARED=1)
+    bool recv_shared = false;
     // split DiT form: RMSNorm folded into the neighbouring linears (the residual epilogue writes the
     // next operand, the consumer scales rows by 1/rms); VXC_NORM_KERNELS=1 launches separate RMSNorm kernels
     bool norm_kernels = false;
@@ -562,6 +564,7 @@ TcLinearArgs tc_plan(const vxc_stream* s, int tiles, int K, bool fused_b) {
     const int nch = K / 64;
     a.splits = pow2_floor(choose_splits(tiles, K, s->tc_target));
     a.max_stages = s->tc_stages;
+    a.recv_shared = s->recv_shared ? 1 : 0;
     if (fused_b)
         a.splits = std::min(pow2_floor(std::min(8, nch)),
                             pow2_ceil(std::max(a.splits, (nch + a.max_stages - 1) / a.max_stages)));
@@ -1259,6 +1262,7 @@ struct vxc_group {
     int tc_target = 32;              // CTAs aimed at per wide linear (VXC_GROUP_TC_TARGET; 32 suits
                                      // several groups at once, 148 a lone group's latency)
     int tc_stages = 2;               // TMA ring depth of the wide linears (VXC_GROUP_TC_STAGES)
+    bool recv_shared = true;         // split wide linears receive in their stage area (VXC_GROUP_RECV_SHARED=0: not)
     bool bulk_gemv = false;          // decoder GEMVs: register-streaming batch form (0, the faster), or
                                      // bulk-copy (VXC_GROUP_BULK_GEMV=1)
     StreamCtl* gctl = nullptr;       // error reports of the batched linears
@@ -1402,6 +1406,7 @@ void enqueue_group_layers(vxc_group* g) {
         a.M = M;
         a.K = K;
         a.ctl = g->gctl;
+        a.recv_shared = g->recv_shared ? 1 : 0;
         return a;
     };
     for (size_t l = 0; l < dev->dit.size(); ++l) {
@@ -1766,6 +1771,7 @@ VXC_API int32_t vxc_stream_create(vxc_device* dev, int32_t kv_capacity, vxc_stre
         s->dit_grid = dit_layers_grid();
         if (const char* np = std::getenv("VXC_NO_PDL")) s->pdl = std::string(np) != "1";
         if (const char* nk = std::getenv("VXC_NORM_KERNELS")) s->norm_kernels = std::string(nk) == "1";
+        if (const char* rs = std::getenv("VXC_RECV_SHARED")) s->recv_shared = std::string(rs) == "1";
         if (const char* bg = std::getenv("VXC_BULK_GEMV")) s->bulk_gemv = std::string(bg) == "1";
         if (const char* tt = std::getenv("VXC_TC_TARGET")) {
             s->tc_target = std::atoi(tt);
@@ -2677,6 +2683,7 @@ VXC_API int32_t vxc_group_create(vxc_device* dev, int32_t n_streams, int32_t kv_
             require(grp->tc_target >= 1 && grp->tc_target <= 4096, "VXC_GROUP_TC_TARGET must be in [1, 4096]");
         }
         if (const char* bg = std::getenv("VXC_GROUP_BULK_GEMV")) grp->bulk_gemv = std::string(bg) == "1";
+        if (const char* rs = std::getenv("VXC_GROUP_RECV_SHARED")) grp->recv_shared = std::string(rs) != "0";
         if (const char* st = std::getenv("VXC_GROUP_TC_STAGES")) {
             grp->tc_stages = std::atoi(st);
             require(grp->tc_stages >= 1 && grp->tc_stages <= 4, "VXC_GROUP_TC_STAGES must be in [1, 4]");

@@ -44,6 +44,13 @@ constexpr int kTcThreads = 128;
 constexpr int kStageBytes = kABytes + kBBytes;    // 22 KiB, keeps 1 KiB alignment
 constexpr int kMaxStages = 8;
 constexpr int kRecvFloats = kTileRows * kLoOffset;  // split-K receive buffer: every partial of one tile
+constexpr int kSqFloats = kTileRows * kLoOffset;    // squares of the updated rows (at most 128 x 24)
+
+// A split launch can receive in its stage area when the area holds the partials and,
+// behind them, the squares.
+__host__ __device__ constexpr bool shared_recv_fits(bool b_tma, int splits, int recv_shared, size_t area_bytes) {
+    return b_tma && splits > 1 && recv_shared && area_bytes >= static_cast<size_t>(kRecvFloats + kSqFloats) * 4;
+}
 constexpr int kTmemCols = 64;
 
 // Zero token rows M..23 (and their residual rows) of 'cs' B tiles.
@@ -429,10 +436,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // barrier; then owners sum the splits in rank order (deterministic).
         // recv[((p * halves + half) * M + m) * nu + lu]. Without a K split it lives in
         // the (then idle) stage area, so more CTAs of concurrent streams fit on an SM.
-        const bool recv_in_stages = recv_in_stage_area(b_tma, S, a.ssq_out != nullptr);
+        const bool shared = shared_recv_fits(b_tma, S, a.recv_shared, static_cast<size_t>(stage_area) * kStageBytes);
+        const bool recv_in_stages = recv_in_stage_area(b_tma, S, a.ssq_out != nullptr) || shared;
         float* recv =
             reinterpret_cast<float*>(recv_in_stages ? smem : smem + static_cast<size_t>(stage_area) * kStageBytes);
         __syncthreads();  // the stage area is idle
+        if (shared) cluster_sync();  // ... in every CTA of the cluster: partials may land in it
         {
             const int u = a.gateup ? (tid & 63) : tid, half = a.gateup ? (tid >> 6) : 0;
             const int owner = u / nu, lu = u - owner * nu;
@@ -455,7 +464,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // each batch issues all its loads before any of its stores
         const int per = kTcThreads / nu, lu = tid % nu, m0 = tid / nu;
         const int col = split * nu + lu;
-        float* sq = reinterpret_cast<float*>(smem);  // the stage area is idle now: squares of updated rows
+        // the stage area is idle now: squares of updated rows (behind the partials when those share it)
+        float* sq = reinterpret_cast<float*>(smem) + (shared ? kRecvFloats : 0);
         if (a.gateup) {
             constexpr int kBatch = 4;
             for (int mb = m0; mb < a.M; mb += per * kBatch) {
@@ -532,12 +542,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
 }  // namespace
 
-size_t tc_linear_smem_bytes(int K, int splits, int bmode, int attn_round, int max_stages, bool ssq_out) {
+size_t tc_linear_smem_bytes(int K, int splits, int bmode, int attn_round, int max_stages, bool ssq_out,
+                            bool recv_shared) {
     const int nch = K / kKChunk;
     const int cs = (nch + splits - 1) / splits;
     const int stages = std::min(std::min(max_stages, kMaxStages), std::max(cs, 1));
     const size_t stage_bytes = static_cast<size_t>(stages) * kStageBytes;
-    if (recv_in_stage_area(bmode == TC_B_TMA, splits, ssq_out)) return stage_bytes + 1024;  // + alignment slack
+    if (recv_in_stage_area(bmode == TC_B_TMA, splits, ssq_out) ||
+        shared_recv_fits(bmode == TC_B_TMA, splits, recv_shared, stage_bytes))
+        return stage_bytes + 1024;  // + alignment slack
     const size_t recv_bytes = static_cast<size_t>(kRecvFloats) * sizeof(float);
     const size_t scratch = bmode == TC_B_ATTN ? static_cast<size_t>(attn_round) * kAttnHeadFloats * sizeof(float) : 0;
     return stage_bytes + recv_bytes + scratch + 1024;  // + alignment slack
@@ -618,7 +631,8 @@ void launch_tc_linear(const CUtensorMap& map_a, const CUtensorMap& map_b, const 
     cfg.gridDim = dim3(a.splits, n_tiles);
     cfg.blockDim = dim3(kTcThreads);
     if (a.max_stages < 1 || a.max_stages > kMaxStages) throw std::invalid_argument("tc_linear: max_stages in [1, 8]");
-    cfg.dynamicSmemBytes = tc_linear_smem_bytes(a.K, a.splits, a.bmode, a.attn_round, a.max_stages, a.ssq_out != nullptr);
+    cfg.dynamicSmemBytes = tc_linear_smem_bytes(a.K, a.splits, a.bmode, a.attn_round, a.max_stages, a.ssq_out != nullptr,
+                                                a.recv_shared != 0);
     if (cfg.dynamicSmemBytes > dyn_limit()) throw std::invalid_argument("tc_linear: shared memory over 227 KB");
     cfg.stream = s;
     cudaLaunchAttribute attr[2];

@@ -162,7 +162,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // cluster owns features [p nu, (p + 1) nu) of each half
     const int units = a.gateup ? 64 : kTileRows, halves = a.gateup ? 2 : 1;
     const int nu = units / S;
-    const bool local_recv = recv_in_stages(S, stages);
+    // split launches may receive in the stage area too, once every CTA of the cluster is done with its own
+    const bool shared_recv = S > 1 && a.recv_shared && static_cast<size_t>(stage_area) * kStage >= kRecvBytes;
+    const bool local_recv = recv_in_stages(S, stages) || shared_recv;
     if (tid == 0) {
         // no copy may still be landing in this CTA's shared memory (bounded when something failed)
         for (int i = 0; i < stages; ++i)
@@ -203,6 +205,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         // partials, token-major per owner: recv[((p * halves + half) * M + m) * nu + lu]
         float* recv = reinterpret_cast<float*>(local_recv ? smem : smem + static_cast<size_t>(stage_area) * kStage);
+        if (shared_recv) cluster_barrier();  // every CTA's loads have landed: the stage areas are free
         {
             const int u = a.gateup ? (tid & 63) : tid, half = a.gateup ? (tid >> 6) : 0;
             const int owner = u / nu, lu = u - owner * nu;
@@ -294,12 +297,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmem) : "memory");
 }
 
-size_t smem_bytes(int K, int splits, int stages_cap) {
+size_t smem_bytes(int K, int splits, int stages_cap, bool recv_shared = false) {
     const int nch = K / kKChunk;
     const int cs = (nch + splits - 1) / splits;
     const int stages = std::min(stages_cap, std::max(cs, 1));
     size_t bytes = static_cast<size_t>(stages) * kStage + 1024;
-    if (!recv_in_stages(splits, stages)) bytes += kRecvBytes;  // (unused by an unsplit plain/residual launch)
+    const bool shared = splits > 1 && recv_shared && static_cast<size_t>(stages) * kStage >= kRecvBytes;
+    if (!recv_in_stages(splits, stages) && !shared) bytes += kRecvBytes;  // (unused by an unsplit plain/residual launch)
     return std::max(bytes, kFloor);
 }
 
@@ -317,7 +321,7 @@ void launch_tc_wide(const CUtensorMap& map_a, const CUtensorMap& map_b, const Tc
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.splits, n_tiles);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = smem_bytes(a.K, a.splits, a.stages);
+    cfg.dynamicSmemBytes = smem_bytes(a.K, a.splits, a.stages, a.recv_shared != 0);
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
