@@ -366,12 +366,12 @@ void dispatch_gemv(const GemvArgs& a, cudaStream_t s, bool pdl) {
 }
 
 // ------------------------------------------------------------ bulk GEMV ---
-// The decoder-step form of the GEMV: at most one block per SM, each block's
-// weight rows copied into shared memory by the bulk-copy engine
-// (cp.async.bulk, completing on an mbarrier) BEFORE the dependency wait. A block
-// holds no weights in registers, so the next kernel of the chain fits on the
-// SM beside it and its copies stream while this one computes: HBM reads run
-// ahead of the dependent chain instead of starting when a kernel starts.
+// A decoder-step form of the GEMV (an option; the register-streaming form is the
+// default): at most one block per SM, each block's weight rows copied into shared
+// memory by the bulk-copy engine (cp.async.bulk, completing on an mbarrier) BEFORE
+// the dependency wait. A block holds no weights in registers, so the next kernel
+// of the chain fits on the SM beside it and its copies stream while this one
+// computes.
 constexpr int kBulkThreads = 256;
 constexpr int kBulkWarps = kBulkThreads / kWarp;
 constexpr int kBulkBlocks = 148;
