@@ -189,6 +189,18 @@ VXC_API int32_t vxc_cfm_sample(vxc_stream* s, const float* mu, const float* cond
  * prefill, fusion_proj, residual prefill; resets the caches and the patch count. */
 VXC_API int32_t vxc_prefill(vxc_stream* s, const int32_t* text_ids, int32_t n_text);
 
+/* The prefix phase for a prefix given row by row, as the reference's PrefixRow
+ * list (synthesizer.cpp:43-47, 359-535), so prompt and reference audio can lead
+ * the utterance: token_ids of every row (audio rows' ids are embedded and then
+ * replaced; the reference uses 0), is_audio flags (NULL: all text), and the audio
+ * rows' latent patches in row order, [n_audio][D*P] d-major (as encoded by the
+ * audio VAE). An audio row is embedded by feat_encoder, its LM hidden after the base
+ * prefill is its FSQ output, and its feat_encoder embedding is its residual
+ * feature input; when the last row is audio, the first patch is conditioned on its
+ * latent. Resets the caches and the patch count. */
+VXC_API int32_t vxc_prefill_rows(vxc_stream* s, const int32_t* token_ids, const int32_t* is_audio,
+                                 const float* audio_latents, int32_t n_rows);
+
 /* One iteration of the patch loop (synthesizer.cpp:537-659), replayed as one
  * CUDA graph: dit_proj, cfm_sample (timesteps-1 estimator calls after the
  * zero-init skip), stop_head, and -- unless the stop rule fires --

@@ -844,43 +844,59 @@ int orc_cfm_sample(const orc_model* m, const float* mu, const float* cond, const
     return cfm_sample(m, mu, cond, noise, timesteps, cfg, out_latent);
 }
 
-int orc_generate(orc_model* m, const int32_t* text_ids, int n_text, int min_patches,
-                 int timesteps, float cfg, int max_patches_override, uint32_t seed,
-                 float* latents, float* lm_trace, float* res_trace, float* stop_trace,
-                 int* out_patches) {
+}  // extern "C"
+
+namespace {
+
+// generate_with_caches after the prefix is built (synthesizer.cpp:403-659): rows are
+// token rows (embedded by text_embed) or audio rows (latent patch, d-major; embedded
+// by feat_encoder, :415-443); the base decoder runs over all rows, audio rows of the
+// LM hidden take the FSQ output (:476-495), the residual decoder reads
+// fusion_proj(lm, feat) (:497-509), and the first patch is conditioned on the last
+// row's latent when that row is audio (:444-447). n_target_text sizes max_patches.
+int generate_prefix(orc_model* m, const std::vector<int32_t>& ids, const std::vector<int>& is_audio,
+                    const std::vector<const float*>& audio, int n_target_text, int min_patches, int timesteps,
+                    float cfg, int max_patches_override, uint32_t seed, float* latents, float* lm_trace,
+                    float* res_trace, float* stop_trace, int* out_patches) {
     const orc_desc& d = m->desc;
-    for (int c = 0; c <= 8; ++c)
-        if (!m->blob[c]) return -1;
-    if (n_text <= 0 || timesteps <= 0) return -1;
     const int H = d.hidden, latent = d.feat_dim * d.patch_size;
-    // prefix = target ids + audio_start (synthesizer.cpp:387-390)
-    std::vector<int32_t> ids(text_ids, text_ids + n_text);
-    ids.push_back(d.audio_start_token);
     const int L = static_cast<int>(ids.size());
-    std::vector<float> embed(static_cast<std::size_t>(L) * H);
+    std::vector<float> embed(static_cast<std::size_t>(L) * H), resfeat(static_cast<std::size_t>(L) * H, 0.0f);
     if (orc_text_embed(m, ids.data(), L, embed.data()) != 0) return -1;
+    for (int i = 0; i < L; ++i)
+        if (is_audio[static_cast<std::size_t>(i)]) {
+            float* row = embed.data() + static_cast<std::size_t>(i) * H;
+            orc_feat_encoder(m, audio[static_cast<std::size_t>(i)], row);
+            std::memcpy(resfeat.data() + static_cast<std::size_t>(i) * H, row, sizeof(float) * H);
+        }
     orc_reset_caches(m);
-    std::vector<float> base_hidden(embed.size()), res_in(embed.size()), res_hidden(embed.size()),
-        zeros(embed.size(), 0.0f);
-    decoder_forward(m, 0, embed.data(), L, nullptr, nullptr, nullptr, base_hidden.data());
-    // No audio rows in a text-only prefix: the fsq result of :478-483 replaces
-    // no row, so lm_prefix_hidden == base_hidden (:484-495).
-    orc_fusion_proj(m, base_hidden.data(), zeros.data(), L, res_in.data());
+    std::vector<float> lm_prefix(embed.size()), res_in(embed.size()), res_hidden(embed.size()), fsq_row(H);
+    decoder_forward(m, 0, embed.data(), L, nullptr, nullptr, nullptr, lm_prefix.data());
+    for (int i = 0; i < L; ++i)
+        if (is_audio[static_cast<std::size_t>(i)]) {
+            float* row = lm_prefix.data() + static_cast<std::size_t>(i) * H;
+            orc_fsq(m, row, 1, fsq_row.data());
+            std::memcpy(row, fsq_row.data(), sizeof(float) * H);
+        }
+    orc_fusion_proj(m, lm_prefix.data(), resfeat.data(), L, res_in.data());
     decoder_forward(m, 1, res_in.data(), L, nullptr, nullptr, nullptr, res_hidden.data());
-    std::vector<float> cur_lm(base_hidden.end() - H, base_hidden.end());
+    std::vector<float> cur_lm(lm_prefix.end() - H, lm_prefix.end());
     std::vector<float> cur_res(res_hidden.end() - H, res_hidden.end());
 
-    int max_patches = orc_max_patches(n_text, d.max_generation_patches);
+    int max_patches = orc_max_patches(n_target_text, d.max_generation_patches);
     if (max_patches_override > 0) max_patches = std::min(max_patches, max_patches_override);
     std::mt19937 rng(seed);
     std::vector<std::vector<float>> patches;
-    std::vector<float> zero_cond(static_cast<std::size_t>(latent), 0.0f), dit_hidden(2 * static_cast<std::size_t>(d.dit_hidden)),
-        noise(static_cast<std::size_t>(latent)), lat(static_cast<std::size_t>(latent)), feat(static_cast<std::size_t>(H)), base_out(static_cast<std::size_t>(H)), fus(static_cast<std::size_t>(H));
+    std::vector<float> init_cond(static_cast<std::size_t>(latent), 0.0f);
+    if (is_audio.back()) std::memcpy(init_cond.data(), audio.back(), sizeof(float) * latent);
+    std::vector<float> dit_hidden(2 * static_cast<std::size_t>(d.dit_hidden)), noise(static_cast<std::size_t>(latent)),
+        lat(static_cast<std::size_t>(latent)), feat(static_cast<std::size_t>(H)), base_out(static_cast<std::size_t>(H)),
+        fus(static_cast<std::size_t>(H));
     float logits[2];
     for (int step = 0; step < max_patches; ++step) {
         if (L + static_cast<int>(patches.size()) >= d.rope_original_max) return -3;
         orc_dit_proj(m, cur_lm.data(), cur_res.data(), dit_hidden.data());
-        const std::vector<float>& cond = patches.empty() ? zero_cond : patches.back();
+        const std::vector<float>& cond = patches.empty() ? init_cond : patches.back();
         std::normal_distribution<float> normal(0.0f, 1.0f);
         for (float& v : noise) v = normal(rng);
         const int rc = cfm_sample(m, dit_hidden.data(), cond.data(), noise.data(), timesteps, cfg, lat.data());
@@ -903,6 +919,54 @@ int orc_generate(orc_model* m, const int32_t* text_ids, int n_text, int min_patc
     }
     *out_patches = static_cast<int>(patches.size());
     return 0;
+}
+
+bool all_loaded(const orc_model* m) {
+    for (int c = 0; c <= 8; ++c)
+        if (!m->blob[c]) return false;
+    return true;
+}
+
+}  // namespace
+
+extern "C" {
+
+int orc_generate(orc_model* m, const int32_t* text_ids, int n_text, int min_patches,
+                 int timesteps, float cfg, int max_patches_override, uint32_t seed,
+                 float* latents, float* lm_trace, float* res_trace, float* stop_trace,
+                 int* out_patches) {
+    if (!all_loaded(m) || n_text <= 0 || timesteps <= 0) return -1;
+    // text-only prefix = target ids + audio_start (synthesizer.cpp:387-390)
+    std::vector<int32_t> ids(text_ids, text_ids + n_text);
+    ids.push_back(m->desc.audio_start_token);
+    const std::vector<int> is_audio(ids.size(), 0);
+    const std::vector<const float*> audio(ids.size(), nullptr);
+    return generate_prefix(m, ids, is_audio, audio, n_text, min_patches, timesteps, cfg, max_patches_override, seed,
+                           latents, lm_trace, res_trace, stop_trace, out_patches);
+}
+
+// A prefix given row by row (the reference's PrefixRow list, synthesizer.cpp:43-47,
+// 359-400): token ids of every row (audio rows' ids are embedded and then replaced),
+// is_audio flags, and the audio rows' latent patches in row order ([n_audio][D*P], d-major).
+int orc_generate_rows(orc_model* m, const int32_t* token_ids, const int32_t* is_audio, const float* audio_latents,
+                      int n_rows, int n_target_text, int min_patches, int timesteps, float cfg,
+                      int max_patches_override, uint32_t seed, float* latents, float* lm_trace, float* res_trace,
+                      float* stop_trace, int* out_patches) {
+    if (!all_loaded(m) || n_rows <= 0 || n_target_text <= 0 || timesteps <= 0 || !token_ids || !is_audio) return -1;
+    const int latent = m->desc.feat_dim * m->desc.patch_size;
+    std::vector<int32_t> ids(token_ids, token_ids + n_rows);
+    std::vector<int> flags(static_cast<std::size_t>(n_rows));
+    std::vector<const float*> audio(static_cast<std::size_t>(n_rows), nullptr);
+    int a = 0;
+    for (int i = 0; i < n_rows; ++i) {
+        flags[static_cast<std::size_t>(i)] = is_audio[i] != 0;
+        if (is_audio[i]) {
+            if (!audio_latents) return -1;
+            audio[static_cast<std::size_t>(i)] = audio_latents + static_cast<std::size_t>(a++) * latent;
+        }
+    }
+    return generate_prefix(m, ids, flags, audio, n_target_text, min_patches, timesteps, cfg, max_patches_override,
+                           seed, latents, lm_trace, res_trace, stop_trace, out_patches);
 }
 
 }  // extern "C"

@@ -144,6 +144,16 @@ int orc_generate(orc_model* model, const int32_t* text_ids, int n_text, int min_
                  float* latents, float* lm_hidden, float* res_hidden, float* stop_logits,
                  int* out_patches);
 
+/* The same from a prefix given row by row (synthesizer.cpp:43-47, 359-535): token
+ * ids of every row, is_audio flags, the audio rows' latent patches in row order
+ * ([n_audio][D*P], d-major); n_target_text sizes max_patches (the target text's
+ * token count). A prefix of text ids + audio_start with no audio rows gives
+ * orc_generate's result. */
+int orc_generate_rows(orc_model* model, const int32_t* token_ids, const int32_t* is_audio,
+                      const float* audio_latents, int n_rows, int n_target_text, int min_patches, int timesteps,
+                      float cfg, int max_patches_override, uint32_t seed, float* latents, float* lm_hidden,
+                      float* res_hidden, float* stop_logits, int* out_patches);
+
 #ifdef __cplusplus
 }
 #endif

@@ -105,6 +105,8 @@ def _setup(L) -> None:
     L.orc_cfm_sample.restype = i
     L.orc_generate.argtypes = [vp, vp, i, i, i, f, i, C.c_uint32, vp, vp, vp, vp, C.POINTER(C.c_int)]
     L.orc_generate.restype = i
+    L.orc_generate_rows.argtypes = [vp, vp, vp, vp, i, i, i, i, f, i, C.c_uint32, vp, vp, vp, vp, C.POINTER(C.c_int)]
+    L.orc_generate_rows.restype = i
 
 
 def _p(a: Optional[np.ndarray]):
@@ -323,6 +325,37 @@ class Oracle:
             raise RuntimeError("VoxCPM2 KV cache reached the exported RoPE range")
         if rc != 0:
             raise ValueError("orc_generate failed")
+        k = n.value
+        return {"patches": k, "latents": lat[:k], "lm_hidden": lm[:k], "res_hidden": res[:k],
+                "stop_logits": stop[:k]}
+
+    def generate_rows(self, token_ids, is_audio, audio_latents, n_target_text: int, min_patches: int = 2,
+                      timesteps: int = 10, cfg_value: float = 2.0, max_patches_override: int = 0,
+                      seed: int = 0) -> dict:
+        """generate() from a prefix given row by row: token ids, is_audio flags and
+        the audio rows' latent patches ([n_audio][D*P], d-major, row order)."""
+        ids = np.ascontiguousarray(token_ids, dtype=np.int32)
+        flags = np.ascontiguousarray(is_audio, dtype=np.int32)
+        if flags.shape != ids.shape:
+            raise ValueError("one is_audio flag per row")
+        lat_in = None if audio_latents is None else _f32(audio_latents).reshape(-1, self.cfg.latent)
+        cap = max_patches(n_target_text, self.cfg.max_generation_patches)
+        if max_patches_override > 0:
+            cap = min(cap, max_patches_override)
+        lat = np.zeros((cap, self.cfg.latent), np.float32)
+        lm = np.zeros((cap, self.cfg.hidden), np.float32)
+        res = np.zeros((cap, self.cfg.hidden), np.float32)
+        stop = np.zeros((cap, 2), np.float32)
+        n = C.c_int(0)
+        rc = lib().orc_generate_rows(self._m, _p(ids), _p(flags), _p(lat_in), ids.size, n_target_text, min_patches,
+                                     timesteps, cfg_value, max_patches_override, seed, _p(lat), _p(lm), _p(res),
+                                     _p(stop), C.byref(n))
+        if rc == -2:
+            raise RuntimeError("dit_estimator produced non-finite values")
+        if rc == -3:
+            raise RuntimeError("VoxCPM2 KV cache reached the exported RoPE range")
+        if rc != 0:
+            raise ValueError("orc_generate_rows failed")
         k = n.value
         return {"patches": k, "latents": lat[:k], "lm_hidden": lm[:k], "res_hidden": res[:k],
                 "stop_logits": stop[:k]}

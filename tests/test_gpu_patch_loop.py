@@ -326,3 +326,74 @@ def test_shared_receive_buffer_is_bit_identical(rt, bench, monkeypatch):
     assert np.array_equal(ra["latents"], rb["latents"])
     a.close()
     b.close()
+
+
+def _run_prefix(rt, dev, cfg, rows, flags, audio, seed, patches, timesteps):
+    s = rt.Stream(dev, kv_capacity=128)
+    s.prefill_rows(rows, flags, audio)
+    s.upload_noise(oracle.noise_table(seed, patches, cfg.latent))
+    for _ in range(patches):
+        s.patch_step_async(1000, 2.0, timesteps)
+    s.synchronize()
+    st = s.state()
+    assert st.prefix_len == len(rows) and st.patches == patches
+    lat = s.latents(0, patches)
+    s.close()
+    return lat
+
+
+@pytest.mark.parametrize("layout", ["prompt_audio_last", "reference_audio_inside"])
+def test_prefill_rows_with_audio_matches_oracle(rt, tiny, layout):
+    """Prefixes with audio rows (synthesizer.cpp:359-535): feat_encoder embeddings,
+    FSQ'd LM rows, the residual feature input, and the first patch's condition
+    (the last prompt patch, or zeros when the prefix ends in a token)."""
+    cfg, blobs, dev, orc = tiny
+    text = synthetic.token_ids(cfg, 7, seed=31)
+    audio = np.random.default_rng(3).standard_normal((3, cfg.latent)).astype(np.float32)
+    if layout == "prompt_audio_last":
+        rows = np.concatenate([text, [cfg.audio_start_token, 0, 0, 0]]).astype(np.int32)
+        flags = np.array([0] * (text.size + 1) + [1, 1, 1], np.int32)
+        aud = audio
+    else:  # reference audio between two marker tokens, then the target text
+        rows = np.concatenate([[102, 0, 0, 103], text, [cfg.audio_start_token]]).astype(np.int32)
+        flags = np.array([0, 1, 1, 0] + [0] * (text.size + 1), np.int32)
+        aud = audio[:2]
+    got = _run_prefix(rt, dev, cfg, rows, flags, aud, seed=12, patches=6, timesteps=6)
+    want = orc.generate_rows(rows, flags, aud, text.size, min_patches=1000, timesteps=6, max_patches_override=6,
+                             seed=12)
+    assert want["patches"] == 6
+    for i in range(6):
+        err, cos = close_stats(got[i], want["latents"][i])
+        assert err <= 2e-2 and cos >= 0.999, (layout, i, err, cos)
+
+
+def test_prefill_rows_text_only_is_prefill(rt, tiny):
+    """A row prefix of the text ids + audio_start and no audio rows is vxc_prefill's."""
+    cfg, blobs, dev, orc = tiny
+    text = synthetic.token_ids(cfg, 9, seed=32)
+    rows = np.append(text, cfg.audio_start_token).astype(np.int32)
+    a = _run_prefix(rt, dev, cfg, rows, None, None, seed=3, patches=3, timesteps=5)
+    s = rt.Stream(dev, kv_capacity=128)
+    s.prefill(text)
+    s.upload_noise(oracle.noise_table(3, 3, cfg.latent))
+    for _ in range(3):
+        s.patch_step_async(1000, 2.0, 5)
+    s.synchronize()
+    assert np.array_equal(a, s.latents(0, 3))
+    with pytest.raises(rt.VxcError):
+        s.prefill_rows(rows, np.ones(rows.size, np.int32), None)  # audio rows without latents
+    s.close()
+
+
+def test_prefill_rows_bench_model(rt, bench):
+    cfg, blobs, dev, orc = bench
+    text = synthetic.token_ids(cfg, 24, seed=33)
+    audio = np.random.default_rng(4).standard_normal((4, cfg.latent)).astype(np.float32)
+    rows = np.concatenate([text, [cfg.audio_start_token, 0, 0, 0, 0]]).astype(np.int32)
+    flags = np.array([0] * (text.size + 1) + [1] * 4, np.int32)
+    got = _run_prefix(rt, dev, cfg, rows, flags, audio, seed=21, patches=3, timesteps=10)
+    want = orc.generate_rows(rows, flags, audio, text.size, min_patches=1000, timesteps=10, max_patches_override=3,
+                             seed=21)
+    for i in range(3):
+        err, cos = close_stats(got[i], want["latents"][i])
+        assert err <= 2e-2 and cos >= 0.999, (i, err, cos)

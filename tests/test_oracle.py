@@ -149,3 +149,37 @@ def test_generate_stop_rule_and_cap(tiny_blobs):
         assert all(not (logits[k, 1] > logits[k, 0]) for k in range(4, s))
     else:
         assert not later
+
+
+def test_generate_rows_text_prefix_matches_generate(tiny_blobs):
+    """A row-by-row prefix of the target ids + audio_start, with no audio rows, is
+    generate()'s prefix (synthesizer.cpp:387-390): identical results."""
+    o = oracle.Oracle(TINY, tiny_blobs)
+    ids = np.arange(3, 11, dtype=np.int32)
+    want = o.generate(ids, min_patches=100, timesteps=4, max_patches_override=5, seed=3)
+    rows = np.append(ids, TINY.audio_start_token).astype(np.int32)
+    got = o.generate_rows(rows, np.zeros(rows.size, np.int32), None, ids.size, min_patches=100, timesteps=4,
+                          max_patches_override=5, seed=3)
+    assert got["patches"] == want["patches"]
+    for k in ("latents", "lm_hidden", "res_hidden", "stop_logits"):
+        assert np.array_equal(got[k], want[k]), k
+
+
+def test_generate_rows_audio_prefix(tiny_blobs):
+    """Audio rows change the prefix (feat_encoder embeddings, FSQ'd LM rows, the
+    residual decoder's feature input) and, when last, condition the first patch."""
+    o = oracle.Oracle(TINY, tiny_blobs)
+    ids = np.arange(3, 9, dtype=np.int32)
+    rng = np.random.default_rng(5)
+    audio = rng.standard_normal((3, TINY.latent)).astype(np.float32)
+    rows = np.concatenate([ids, [TINY.audio_start_token, 0, 0, 0]]).astype(np.int32)
+    flags = np.array([0] * (ids.size + 1) + [1, 1, 1], np.int32)
+    a = o.generate_rows(rows, flags, audio, ids.size, min_patches=100, timesteps=4, max_patches_override=4, seed=1)
+    text = o.generate_rows(rows[:ids.size + 1], flags[:ids.size + 1], None, ids.size, min_patches=100, timesteps=4,
+                           max_patches_override=4, seed=1)
+    assert a["patches"] == text["patches"] == 4
+    assert np.all(np.isfinite(a["latents"]))
+    assert not np.allclose(a["latents"], text["latents"])
+    assert not np.allclose(a["lm_hidden"][0], text["lm_hidden"][0])
+    with pytest.raises(ValueError):
+        o.generate_rows(rows, flags, None, ids.size, max_patches_override=2)  # audio rows without latents

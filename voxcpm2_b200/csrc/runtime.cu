@@ -1181,19 +1181,30 @@ void patch_step(vxc_stream* s, const float* noise, int min_patches, float cfg, i
     if (out_stop) *out_stop = s->ctl_host->stopped;
 }
 
-void prefill(vxc_stream* s, const int32_t* text_ids, int n_text) {
+// The prefix phase of generate_with_caches (synthesizer.cpp:403-535) for a prefix
+// given row by row (PrefixRow, :43-47, built at :359-400): every row's token id is
+// embedded by text_embed; an audio row's embedding is feat_encoder(its latent patch)
+// instead, which is also the row's residual feature input (:415-443); the base
+// decoder runs over all rows, and the LM hidden of audio rows is their FSQ output
+// (:476-495); the residual decoder reads fusion_proj(lm, feat) (:497-522). The first
+// patch is conditioned on the last row's latent when that row is audio, else on
+// zeros (:444-447). audio_latents: the audio rows' patches in row order, d-major.
+void prefill_rows(vxc_stream* s, const int32_t* ids_in, const int32_t* is_audio, const float* audio_latents, int L) {
     const vxc_device* dev = s->dev;
     const vxc_model_desc& d = dev->desc;
-    check_loaded(dev, {0, 1, 2, 4});
-    require(text_ids != nullptr && n_text > 0, "text must not be empty");
-    const int L = n_text + 1;
+    require(ids_in != nullptr && L > 0, "the prefix must not be empty");
+    std::vector<int> audio_rows;
+    for (int i = 0; i < L; ++i)
+        if (is_audio && is_audio[i]) audio_rows.push_back(i);
+    check_loaded(dev, audio_rows.empty() ? std::initializer_list<int>{0, 1, 2, 4}
+                                         : std::initializer_list<int>{0, 1, 2, 3, 4, 7});
+    require(audio_rows.empty() || audio_latents != nullptr, "audio rows need their latent patches");
     require(L <= s->cap, "prompt longer than the KV capacity");
     require(L <= d.rope_original_max, "prompt longer than the RoPE range");
-    for (int i = 0; i < n_text; ++i) require(text_ids[i] >= 0 && text_ids[i] < d.vocab, "token id out of range");
-    const int H = d.hidden;
+    for (int i = 0; i < L; ++i) require(ids_in[i] >= 0 && ids_in[i] < d.vocab, "token id out of range");
+    const int H = d.hidden, latent = d.feat_dim * d.patch_size;
+    const size_t A = audio_rows.size();
     ensure_prefill_rows(s, L);
-    std::vector<int32_t> ids(text_ids, text_ids + n_text);
-    ids.push_back(d.audio_start_token);
     // new utterance: empty caches, zero counters (synthesizer.cpp:348-350)
     std::memset(s->ctl_host, 0, sizeof(StreamCtl));
     s->ctl_host->min_patches = s->min_patches_dev;
@@ -1201,39 +1212,87 @@ void prefill(vxc_stream* s, const int32_t* text_ids, int n_text) {
     s->kv_len[0] = s->kv_len[1] = 0;
     s->patches = 0;
     s->prefilled = false;
-    ck(cudaMemcpyAsync(s->pids, ids.data(), sizeof(int32_t) * L, cudaMemcpyHostToDevice, s->cs), "ids");
-    launch_embed_gather(dev->blob[VXC_TEXT_EMBED], s->pids, L, H, d.embed_scale, s->ph, s->cs);
-    run_decoder_rows(s, 0, L, s->pxn);  // base_hidden -> pxn
-    // text-only prefix: no audio rows, so lm_prefix_hidden == base_hidden and
-    // residual_feat_embed == 0 (synthesizer.cpp:476-495)
-    ck(cudaMemcpy2DAsync(s->pcat, sizeof(float) * 2 * H, s->pxn, sizeof(float) * H, sizeof(float) * H, L,
-                         cudaMemcpyDeviceToDevice, s->cs),
-       "concat");
-    ck(cudaMemset2DAsync(s->pcat + H, sizeof(float) * 2 * H, 0, sizeof(float) * H, L, s->cs), "concat zeros");
-    ck(cudaMemcpyAsync(s->lm_h, s->pxn + static_cast<size_t>(L - 1) * H, sizeof(float) * H,
-                       cudaMemcpyDeviceToDevice, s->cs),
-       "lm row");
-    const __half* fu = dev->blob[VXC_FUSION_PROJ];
-    RowsArgs fa;
-    fa.w = fu;
-    fa.bias = fu + static_cast<size_t>(H) * 2 * H;
-    fa.x = s->pcat;
-    fa.ldx = 2 * H;
-    fa.K = 2 * H;
-    fa.rows = H;
-    fa.M = L;
-    fa.y = s->ph;
-    fa.ldy = H;
-    launch_rows_linear(fa, s->cs, false);
-    run_decoder_rows(s, 1, L, s->pxn);
-    ck(cudaMemcpyAsync(s->res_h, s->pxn + static_cast<size_t>(L - 1) * H, sizeof(float) * H,
-                       cudaMemcpyDeviceToDevice, s->cs),
-       "res row");
-    // the first patch is conditioned on zeros (synthesizer.cpp:445-447)
-    ck(cudaMemsetAsync(s->cond0, 0, sizeof(float) * d.feat_dim * d.patch_size, s->cs), "cond");
+    float* lat = nullptr;  // the audio rows' latents on the device (stream-ordered allocation)
+    if (A) {
+        ck(cudaMallocAsync(reinterpret_cast<void**>(&lat), sizeof(float) * latent * A, s->cs), "audio latents");
+        ck(cudaMemcpyAsync(lat, audio_latents, sizeof(float) * latent * A, cudaMemcpyHostToDevice, s->cs), "latents");
+    }
+    try {
+        ck(cudaMemcpyAsync(s->pids, ids_in, sizeof(int32_t) * L, cudaMemcpyHostToDevice, s->cs), "ids");
+        launch_embed_gather(dev->blob[VXC_TEXT_EMBED], s->pids, L, H, d.embed_scale, s->ph, s->cs);
+        // residual feature input: zeros, and feat_encoder(latent) on audio rows
+        ck(cudaMemset2DAsync(s->pcat + H, sizeof(float) * 2 * H, 0, sizeof(float) * H, L, s->cs), "feat zeros");
+        const __half* fe = dev->blob[VXC_FEAT_ENCODER];
+        const size_t fin = static_cast<size_t>(H) * latent;
+        for (size_t a = 0; a < A; ++a) {
+            const size_t r = static_cast<size_t>(audio_rows[a]);
+            GemvArgs fa = plain_gemv(fe, fe + fin, lat + a * latent, latent, H, s->mid2, ACT_SILU, nullptr, 0);
+            fa.in_mode = IN_LATENT_T;
+            fa.lat_d = d.feat_dim;
+            fa.lat_p = d.patch_size;
+            launch_gemv(fa, s->cs, false);
+            GemvArgs fb = plain_gemv(fe + fin + H, fe + fin + H + static_cast<size_t>(H) * H, s->mid2, H, H,
+                                     s->ph + r * H, ACT_NONE, nullptr, 0);
+            fb.y2 = s->pcat + r * 2 * H + H;
+            launch_gemv(fb, s->cs, false);
+        }
+        run_decoder_rows(s, 0, L, s->pxn);  // base_hidden -> pxn
+        // the LM hidden of audio rows is their FSQ output
+        const __half* fq = dev->blob[VXC_FSQ];
+        const size_t Q = d.fsq_dim;
+        for (size_t a = 0; a < A; ++a) {
+            float* row = s->pxn + static_cast<size_t>(audio_rows[a]) * H;
+            GemvArgs qa = plain_gemv(fq, fq + Q * H, row, H, static_cast<int>(Q), s->mid, ACT_FSQ, nullptr, 0);
+            qa.act_scale = d.fsq_scale;
+            launch_gemv(qa, s->cs, false);
+            launch_gemv(plain_gemv(fq + Q * H + Q, fq + Q * H + Q + H * Q, s->mid, static_cast<int>(Q), H, row,
+                                   ACT_NONE, nullptr, 0),
+                        s->cs, false);
+        }
+        ck(cudaMemcpy2DAsync(s->pcat, sizeof(float) * 2 * H, s->pxn, sizeof(float) * H, sizeof(float) * H, L,
+                             cudaMemcpyDeviceToDevice, s->cs),
+           "concat");
+        ck(cudaMemcpyAsync(s->lm_h, s->pxn + static_cast<size_t>(L - 1) * H, sizeof(float) * H,
+                           cudaMemcpyDeviceToDevice, s->cs),
+           "lm row");
+        const __half* fu = dev->blob[VXC_FUSION_PROJ];
+        RowsArgs fa;
+        fa.w = fu;
+        fa.bias = fu + static_cast<size_t>(H) * 2 * H;
+        fa.x = s->pcat;
+        fa.ldx = 2 * H;
+        fa.K = 2 * H;
+        fa.rows = H;
+        fa.M = L;
+        fa.y = s->ph;
+        fa.ldy = H;
+        launch_rows_linear(fa, s->cs, false);
+        run_decoder_rows(s, 1, L, s->pxn);
+        ck(cudaMemcpyAsync(s->res_h, s->pxn + static_cast<size_t>(L - 1) * H, sizeof(float) * H,
+                           cudaMemcpyDeviceToDevice, s->cs),
+           "res row");
+        if (A && audio_rows.back() == L - 1)  // conditioned on the prompt's last patch
+            ck(cudaMemcpyAsync(s->cond0, lat + (A - 1) * latent, sizeof(float) * latent, cudaMemcpyDeviceToDevice,
+                               s->cs),
+               "cond");
+        else
+            ck(cudaMemsetAsync(s->cond0, 0, sizeof(float) * latent, s->cs), "cond");
+    } catch (...) {
+        if (lat) cudaFreeAsync(lat, s->cs);
+        throw;
+    }
+    if (lat) ck(cudaFreeAsync(lat, s->cs), "audio latents");
     sync_ctl(s);
     s->prefix_len = L;
     s->prefilled = true;
+}
+
+// A text-only prompt: prefix = text ids + audio_start (synthesizer.cpp:387-390).
+void prefill(vxc_stream* s, const int32_t* text_ids, int n_text) {
+    require(text_ids != nullptr && n_text > 0, "text must not be empty");
+    std::vector<int32_t> ids(text_ids, text_ids + n_text);
+    ids.push_back(s->dev->desc.audio_start_token);
+    prefill_rows(s, ids.data(), nullptr, nullptr, static_cast<int>(ids.size()));
 }
 
 }  // namespace
@@ -2042,6 +2101,16 @@ VXC_API int32_t vxc_prefill(vxc_stream* s, const int32_t* text_ids, int32_t n_te
         std::lock_guard<std::mutex> lk(s->call_mutex);
         DeviceGuard g(s->dev->device);
         prefill(s, text_ids, n_text);
+    });
+}
+
+VXC_API int32_t vxc_prefill_rows(vxc_stream* s, const int32_t* token_ids, const int32_t* is_audio,
+                                 const float* audio_latents, int32_t n_rows) {
+    return guard([&] {
+        require(s != nullptr, "stream must not be null");
+        std::lock_guard<std::mutex> lk(s->call_mutex);
+        DeviceGuard g(s->dev->device);
+        prefill_rows(s, token_ids, is_audio, audio_latents, n_rows);
     });
 }
 

@@ -87,6 +87,7 @@ def _signatures():
         "vxc_dit_estimator": ([vp, vp, vp, vp, vp, vp, vp], i),
         "vxc_cfm_sample": ([vp, vp, vp, vp, i, f, vp], i),
         "vxc_prefill": ([vp, vp, i], i),
+        "vxc_prefill_rows": ([vp, vp, vp, vp, i], i),
         "vxc_patch_step": ([vp, vp, i, i, f, i, vp, C.POINTER(i)], i),
         "vxc_generate": ([vp, vp, i, i, i, f, i, u, vp, C.POINTER(i), vp, vp, vp, PROGRESS_FN, vp], i),
         "vxc_sdpa": ([vp, i, i, i, vp, vp, i, i, i, vp, i, vp, vp, i, f, vp, vp, vp, vp], i),
@@ -268,6 +269,16 @@ class Stream:
     def prefill(self, text_ids) -> None:
         ids = np.ascontiguousarray(text_ids, dtype=np.int32)
         _check(lib().vxc_prefill(self._h, _p(ids), ids.size))
+
+    def prefill_rows(self, token_ids, is_audio=None, audio_latents=None) -> None:
+        """Prefix given row by row: token ids, is_audio flags (None: all text) and the
+        audio rows' latent patches in row order ([n_audio][D*P], d-major)."""
+        ids = np.ascontiguousarray(token_ids, dtype=np.int32)
+        flags = None if is_audio is None else np.ascontiguousarray(is_audio, dtype=np.int32)
+        if flags is not None and flags.shape != ids.shape:
+            raise ValueError("one is_audio flag per row")
+        lat = None if audio_latents is None else _f32(audio_latents).reshape(-1, self.cfg.latent)
+        _check(lib().vxc_prefill_rows(self._h, _p(ids), _p(flags), _p(lat), ids.size))
 
     def patch_step(self, noise, min_patches: int, step: int, cfg_value: float = 2.0, timesteps: int = 10):
         lat = np.empty(self.cfg.latent, np.float32)
