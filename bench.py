@@ -494,40 +494,61 @@ def run_ours(args):
     solo.close()
     p50_solo = float(np.median(lat_solo))
 
-    # ---- e2e: the public C ABI with host buffers (noise in, latent + state out), one thread per stream
-    for s, i in zip(streams, ids):
-        s.prefill(i)
-    per_call = [[] for _ in range(S)]
-    # each thread runs its warm-up steps, then waits for the timed start
-    done_warm = [threading.Event() for _ in range(S)]
-    go = threading.Event()
+    # ---- e2e: the public C ABI with host buffers (noise in, latent + stop flag out, every
+    # step), one thread per stream. Two driving patterns: the synchronous vxc_patch_step, and
+    # the pipelined vxc_patch_submit / vxc_patch_collect with one patch queued ahead (the
+    # headline e2e: the stream's GPU queue does not drain while the host handles a patch).
+    def e2e_run(pipelined: bool):
+        for s, i in zip(streams, ids):
+            s.prefill(i)
+        per_call = [[] for _ in range(S)]
+        done_warm = [threading.Event() for _ in range(S)]  # warm-up steps done; wait for the timed start
+        go = threading.Event()
 
-    def worker(j):
-        s = streams[j]
-        for step in range(W):
-            s.patch_step(noise[j][step], min_patches, step, CFG, TIMESTEPS)
-        done_warm[j].set()
-        go.wait()
-        for step in range(W, W + K):
-            t0 = time.perf_counter()
-            s.patch_step(noise[j][step], min_patches, step, CFG, TIMESTEPS)
-            per_call[j].append(time.perf_counter() - t0)
+        def worker(j):
+            s = streams[j]
+            out = np.empty(L, np.float32)  # the collected latent (a host buffer the caller owns)
+            if pipelined:
+                s.patch_submit(noise[j][0], min_patches, CFG, TIMESTEPS)
+                for step in range(1, W):
+                    s.patch_submit(noise[j][step], min_patches, CFG, TIMESTEPS)
+                    s.patch_collect(out)
+                s.patch_collect(out)
+            else:
+                for step in range(W):
+                    s.patch_step(noise[j][step], min_patches, step, CFG, TIMESTEPS)
+            done_warm[j].set()
+            go.wait()
+            if pipelined:
+                s.patch_submit(noise[j][W], min_patches, CFG, TIMESTEPS)
+                for step in range(W + 1, W + K):
+                    s.patch_submit(noise[j][step], min_patches, CFG, TIMESTEPS)
+                    _, stop = s.patch_collect(out)
+                s.patch_collect(out)
+            else:
+                for step in range(W, W + K):
+                    t0 = time.perf_counter()
+                    s.patch_step(noise[j][step], min_patches, step, CFG, TIMESTEPS)
+                    per_call[j].append(time.perf_counter() - t0)
 
-    threads = [threading.Thread(target=worker, args=(j,)) for j in range(S)]
-    for t in threads:
-        t.start()
-    for ev in done_warm:
-        ev.wait()
-    barrier()
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    go.set()
-    for t in threads:
-        t.join()
-    torch.cuda.synchronize()
-    e2e_s = max_over_ranks(time.perf_counter() - t0)
-    barrier()
-    e2e_value = job_rate(world, S, K, e2e_s)
+        threads = [threading.Thread(target=worker, args=(j,)) for j in range(S)]
+        for t in threads:
+            t.start()
+        for ev in done_warm:
+            ev.wait()
+        barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        go.set()
+        for t in threads:
+            t.join()
+        torch.cuda.synchronize()
+        secs = max_over_ranks(time.perf_counter() - t0)
+        barrier()
+        return job_rate(world, S, K, secs), per_call
+
+    e2e_sync_value, per_call = e2e_run(False)
+    e2e_value, _ = e2e_run(True)
     calls = np.concatenate([np.array(c) for c in per_call]) * 1e3
     h2d = S * L * 4                   # each stream's noise patch
     d2h = S * (L * 4 + 40)            # each stream's latent patch + its 40-byte control block
@@ -563,7 +584,10 @@ def run_ours(args):
             "p50_patch_ms_latency_tuned": p50_solo, "latency_tuning": LATENCY_TUNING,
             "prefill_ms": float(np.median(pre_ms)),
             "per_gpu_patches_per_s": value / world,
-            "e2e": {"value": e2e_value, "unit": "patches/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "e2e": {"value": e2e_value, "unit": "patches/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "api": "vxc_patch_submit / vxc_patch_collect, one patch queued ahead per stream"},
+            "e2e_sync": {"value": e2e_sync_value, "unit": "patches/s", "h2d_bytes_per_step": h2d,
+                         "d2h_bytes_per_step": d2h, "api": "vxc_patch_step (synchronous)"},
             "gpu_launches": graph_kernels * S * K, "roofline": roofline, "hbm_job": hbm_job, "kernels": kernels,
             "decode_step": decode_step,
             "cpu_baseline": cpu, "clocks": clk, "group": group,

@@ -260,6 +260,18 @@ VXC_API int32_t vxc_upload_noise(vxc_stream* s, const float* noise, int32_t patc
 /* Enqueues one patch-step graph reading the device noise table; no host sync,
  * no host copies. The caller checks the stop flag later with vxc_read_state. */
 VXC_API int32_t vxc_patch_step_async(vxc_stream* s, int32_t min_patches, float cfg_value, int32_t timesteps);
+/* Pipelined patch loop: vxc_patch_submit queues one patch step (as vxc_patch_step:
+ * host noise [D*P] through a pinned slot, the patch graph, and copies of its latent
+ * and control block back to pinned slots) and returns without waiting; at most 4
+ * patches may be in flight. vxc_patch_collect waits for the oldest queued patch
+ * only and returns its latent and stop flag. A host keeps the next patch queued
+ * while it handles the previous one; when a collected patch has stop set, it
+ * discards the patch it queued after it (vxc_prefill or vxc_stream_reset drops
+ * queued patches). Collecting with nothing queued is VXC_STATUS_INVALID_STATE. */
+VXC_API int32_t vxc_patch_submit(vxc_stream* s, const float* noise, int32_t min_patches, float cfg_value,
+                                 int32_t timesteps);
+VXC_API int32_t vxc_patch_collect(vxc_stream* s, float* out_latent, int32_t* out_stop);
+
 VXC_API int32_t vxc_stream_synchronize(vxc_stream* s);
 VXC_API int32_t vxc_read_state(vxc_stream* s, vxc_stream_state* out);
 /* Current hidden states entering the next patch: lm [H], res [H] (either may be NULL). */

@@ -397,3 +397,38 @@ def test_prefill_rows_bench_model(rt, bench):
     for i in range(3):
         err, cos = close_stats(got[i], want["latents"][i])
         assert err <= 2e-2 and cos >= 0.999, (i, err, cos)
+
+
+def test_pipelined_submit_collect_matches_patch_step(rt, tiny):
+    """vxc_patch_submit / vxc_patch_collect with one patch queued ahead give the
+    synchronous vxc_patch_step's latents and stop flags, bit for bit."""
+    cfg, blobs, dev, orc = tiny
+    ids = synthetic.token_ids(cfg, 8, seed=14)
+    noise = oracle.noise_table(17, 10, cfg.latent)
+    a = rt.Stream(dev, kv_capacity=64)
+    a.prefill(ids)
+    want = [a.patch_step(noise[i], min_patches=2, step=i, cfg_value=2.0, timesteps=5) for i in range(10)]
+    b = rt.Stream(dev, kv_capacity=64)
+    b.prefill(ids)
+    with pytest.raises(rt.VxcError) as e:
+        b.patch_collect()  # nothing queued
+    assert e.value.status == 2
+    got = []
+    b.patch_submit(noise[0], 2, 2.0, 5)
+    for i in range(1, 10):
+        b.patch_submit(noise[i], 2, 2.0, 5)
+        got.append(b.patch_collect())
+    got.append(b.patch_collect())
+    for (gl, gs), (wl, ws) in zip(got, want):
+        assert np.array_equal(gl, wl) and gs == ws
+    st = b.state()
+    assert st.patches == 10 and st.kv_len[0] == a.state().kv_len[0]
+    for i in range(4):
+        b.patch_submit(noise[i], 2, 2.0, 5)
+    with pytest.raises(rt.VxcError):
+        b.patch_submit(noise[4], 2, 2.0, 5)  # four already in flight
+    b.prefill(ids)  # drops the queued patches
+    with pytest.raises(rt.VxcError):
+        b.patch_collect()
+    a.close()
+    b.close()

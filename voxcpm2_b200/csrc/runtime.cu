@@ -341,6 +341,14 @@ struct vxc_stream {
     CUtensorMap map_xb_n{}, map_xb_a{}, map_xb_act{};
     float* gen_in = nullptr;  // staging for generic calls
     float* pin = nullptr;     // pinned host staging
+    // pipelined driving (vxc_patch_submit / vxc_patch_collect): per in-flight patch a
+    // pinned noise slot, latent slot and control-block snapshot, and its completion event
+    static constexpr int kInflight = 4;
+    float* pin_noise = nullptr;      // [kInflight][D*P]
+    float* pin_lat = nullptr;        // [kInflight][D*P]
+    StreamCtl* pin_ctl = nullptr;    // [kInflight]
+    cudaEvent_t patch_ev[kInflight] = {};
+    int64_t submitted = 0, collected = 0;
     // prefill buffers (grown on demand)
     int pre_rows = 0;
     float *ph = nullptr, *pxn = nullptr, *pqkv = nullptr, *pattn = nullptr, *pact = nullptr, *pcat = nullptr;
@@ -421,6 +429,10 @@ void free_all(vxc_stream* s) {
     if (s->dcount) cudaFree(s->dcount);
     if (s->ctl_host) cudaFreeHost(s->ctl_host);
     if (s->pin) cudaFreeHost(s->pin);
+    for (void* p : {static_cast<void*>(s->pin_noise), static_cast<void*>(s->pin_lat), static_cast<void*>(s->pin_ctl)})
+        if (p) cudaFreeHost(p);
+    for (cudaEvent_t& e : s->patch_ev)
+        if (e) cudaEventDestroy(e);
     if (s->cs) cudaStreamDestroy(s->cs);
 }
 
@@ -1181,6 +1193,59 @@ void patch_step(vxc_stream* s, const float* noise, int min_patches, float cfg, i
     if (out_stop) *out_stop = s->ctl_host->stopped;
 }
 
+// Pipelined driving: one patch step is queued (noise through a pinned slot, the patch
+// graph, and copies of its latent and control block into pinned slots, then an event)
+// without waiting; patch_collect waits for the oldest queued patch only. A host can
+// keep the next patch queued while it handles the previous one, so the stream's GPU
+// work never drains between patches; after a stop it discards the patch it queued
+// speculatively.
+void patch_submit(vxc_stream* s, const float* noise, int min_patches, float cfg, int T) {
+    if (s->submitted - s->collected >= vxc_stream::kInflight)
+        throw InvalidState("four patches are in flight: collect one before submitting another");
+    check_patch_preconditions(s, T);
+    require(noise != nullptr, "noise must not be null");
+    const int L = s->dev->desc.feat_dim * s->dev->desc.patch_size;
+    const int slot = static_cast<int>(s->submitted % vxc_stream::kInflight);
+    float* pn = s->pin_noise + static_cast<size_t>(slot) * L;
+    // the slot's previous copies finished before its patch was collected
+    std::memcpy(pn, noise, sizeof(float) * L);
+    ck(cudaMemcpyAsync(s->noise + static_cast<size_t>(s->patches) * L, pn, sizeof(float) * L, cudaMemcpyHostToDevice,
+                       s->cs),
+       "noise upload");
+    set_min_patches(s, min_patches);
+    capture_patch_graph(s, T, cfg);
+    ck(cudaGraphLaunch(s->graph, s->cs), "cudaGraphLaunch");
+    ck(cudaMemcpyAsync(s->pin_lat + static_cast<size_t>(slot) * L, s->latents + static_cast<size_t>(s->patches) * L,
+                       sizeof(float) * L, cudaMemcpyDeviceToHost, s->cs),
+       "latent download");
+    ck(cudaMemcpyAsync(s->pin_ctl + slot, s->ctl, sizeof(StreamCtl), cudaMemcpyDeviceToHost, s->cs), "ctl download");
+    ck(cudaEventRecord(s->patch_ev[slot], s->cs), "cudaEventRecord");
+    s->submitted += 1;
+    s->patches += 1;  // host mirrors advance optimistically; collect re-syncs them
+    s->kv_len[0] += 1;
+    s->kv_len[1] += 1;
+}
+
+void patch_collect(vxc_stream* s, float* out_latent, int* out_stop) {
+    if (s->collected >= s->submitted) throw InvalidState("no patch in flight");
+    const int L = s->dev->desc.feat_dim * s->dev->desc.patch_size;
+    const int slot = static_cast<int>(s->collected % vxc_stream::kInflight);
+    ck(cudaEventSynchronize(s->patch_ev[slot]), "cudaEventSynchronize");
+    s->collected += 1;
+    const StreamCtl& c = s->pin_ctl[slot];
+    if (c.error != 0) {  // reports the device-side failure and clears it, like sync_ctl
+        sync_ctl(s);
+        throw std::runtime_error("device-side check failed");
+    }
+    if (out_latent) std::memcpy(out_latent, s->pin_lat + static_cast<size_t>(slot) * L, sizeof(float) * L);
+    if (out_stop) *out_stop = c.stopped;
+    if (s->collected == s->submitted) {  // nothing queued behind it: the snapshot is the stream's state
+        s->kv_len[0] = c.kv_len[0];
+        s->kv_len[1] = c.kv_len[1];
+        s->patches = c.patch;
+    }
+}
+
 // The prefix phase of generate_with_caches (synthesizer.cpp:403-535) for a prefix
 // given row by row (PrefixRow, :43-47, built at :359-400): every row's token id is
 // embedded by text_embed; an audio row's embedding is feat_encoder(its latent patch)
@@ -1212,6 +1277,7 @@ void prefill_rows(vxc_stream* s, const int32_t* ids_in, const int32_t* is_audio,
     s->kv_len[0] = s->kv_len[1] = 0;
     s->patches = 0;
     s->prefilled = false;
+    s->submitted = s->collected = 0;  // write_ctl synchronised the stream: queued patches are dropped
     float* lat = nullptr;  // the audio rows' latents on the device (stream-ordered allocation)
     if (A) {
         ck(cudaMallocAsync(reinterpret_cast<void**>(&lat), sizeof(float) * latent * A, s->cs), "audio latents");
@@ -1871,6 +1937,10 @@ VXC_API int32_t vxc_stream_create(vxc_device* dev, int32_t kv_capacity, vxc_stre
         s->map_xb_act = make_tensor_map_f16(s->xb_act, 48, d.dit_ffn, 48);
         s->gen_in = dev_alloc<float>(std::max(8 * Hd + 8 * L, 4 * H));
         ck(cudaMallocHost(&s->pin, sizeof(float) * (4 * std::max<size_t>(L, 2 * Hd) + 4 * H)), "cudaMallocHost");
+        ck(cudaMallocHost(&s->pin_noise, sizeof(float) * L * vxc_stream::kInflight), "cudaMallocHost");
+        ck(cudaMallocHost(&s->pin_lat, sizeof(float) * L * vxc_stream::kInflight), "cudaMallocHost");
+        ck(cudaMallocHost(&s->pin_ctl, sizeof(StreamCtl) * vxc_stream::kInflight), "cudaMallocHost");
+        for (cudaEvent_t& e : s->patch_ev) ck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
         *out = s.release();
     });
 }
@@ -1902,6 +1972,7 @@ VXC_API int32_t vxc_stream_reset(vxc_stream* s) {
         s->kv_len[0] = s->kv_len[1] = 0;
         s->patches = 0;
         s->prefilled = false;
+        s->submitted = s->collected = 0;
     });
 }
 
@@ -2340,6 +2411,27 @@ VXC_API int32_t vxc_patch_step_async(vxc_stream* s, int32_t min_patches, float c
         s->patches += 1;
         s->kv_len[0] += 1;
         s->kv_len[1] += 1;
+    });
+}
+
+VXC_API int32_t vxc_patch_submit(vxc_stream* s, const float* noise, int32_t min_patches, float cfg_value,
+                                 int32_t timesteps) {
+    return guard([&] {
+        require(s != nullptr, "stream must not be null");
+        std::lock_guard<std::mutex> lk(s->call_mutex);
+        DeviceGuard g(s->dev->device);
+        patch_submit(s, noise, min_patches, cfg_value, timesteps);
+    });
+}
+
+VXC_API int32_t vxc_patch_collect(vxc_stream* s, float* out_latent, int32_t* out_stop) {
+    return guard([&] {
+        require(s != nullptr, "stream must not be null");
+        std::lock_guard<std::mutex> lk(s->call_mutex);
+        DeviceGuard g(s->dev->device);
+        int stop = 0;
+        patch_collect(s, out_latent, &stop);
+        if (out_stop) *out_stop = stop;
     });
 }
 

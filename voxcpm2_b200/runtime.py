@@ -96,6 +96,8 @@ def _signatures():
         "vxc_upload_noise": ([vp, vp, i], i),
         "vxc_patch_step_async": ([vp, i, f, i], i),
         "vxc_stream_synchronize": ([vp], i),
+        "vxc_patch_submit": ([vp, vp, i, f, i], i),
+        "vxc_patch_collect": ([vp, vp, C.POINTER(i)], i),
         "vxc_read_state": ([vp, C.POINTER(StreamState)], i),
         "vxc_read_hidden": ([vp, vp, vp], i),
         "vxc_read_latents": ([vp, i, i, vp], i),
@@ -320,6 +322,27 @@ class Stream:
 
     def synchronize(self) -> None:
         _check(lib().vxc_stream_synchronize(self._h))
+
+    def patch_submit(self, noise, min_patches: int, cfg_value: float = 2.0, timesteps: int = 10) -> None:
+        """Queue one patch step (host noise) without waiting; see patch_collect. A
+        C-contiguous float32 noise array is passed without a copy."""
+        if not (isinstance(noise, np.ndarray) and noise.dtype == np.float32 and noise.flags.c_contiguous):
+            noise = _f32(noise)
+        rc = _lib.vxc_patch_submit(self._h, noise.ctypes.data, min_patches, cfg_value, timesteps)
+        if rc:
+            _check(rc)
+
+    def patch_collect(self, out=None):
+        """(latent, stop) of the oldest queued patch, waiting for that patch only.
+        out: an optional float32 [D*P] array that receives the latent."""
+        lat = np.empty(self.cfg.latent, np.float32) if out is None else out
+        if not (lat.dtype == np.float32 and lat.flags.c_contiguous and lat.size == self.cfg.latent):
+            raise ValueError("out must be a contiguous float32 array of one latent patch")
+        stop = self._stop_out = getattr(self, "_stop_out", None) or C.c_int32(0)
+        rc = _lib.vxc_patch_collect(self._h, lat.ctypes.data, C.byref(stop))
+        if rc:
+            _check(rc)
+        return lat, bool(stop.value)
 
     def state(self) -> StreamState:
         st = StreamState()
