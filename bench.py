@@ -528,7 +528,7 @@ def run_ours(args):
             else:
                 for step in range(W, W + K):
                     t0 = time.perf_counter()
-                    s.patch_step(noise[j][step], min_patches, step, CFG, TIMESTEPS)
+                    s.patch_step(noise[j][step], min_patches, step, CFG, TIMESTEPS, out=out)
                     per_call[j].append(time.perf_counter() - t0)
 
         threads = [threading.Thread(target=worker, args=(j,)) for j in range(S)]

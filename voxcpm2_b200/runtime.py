@@ -282,12 +282,22 @@ class Stream:
         lat = None if audio_latents is None else _f32(audio_latents).reshape(-1, self.cfg.latent)
         _check(lib().vxc_prefill_rows(self._h, _p(ids), _p(flags), _p(lat), ids.size))
 
-    def patch_step(self, noise, min_patches: int, step: int, cfg_value: float = 2.0, timesteps: int = 10):
-        lat = np.empty(self.cfg.latent, np.float32)
-        stop = C.c_int32(0)
-        nz = None if noise is None else _f32(noise)
-        _check(lib().vxc_patch_step(self._h, _p(nz), min_patches, step, cfg_value, timesteps, _p(lat),
-                                    C.byref(stop)))
+    def patch_step(self, noise, min_patches: int, step: int, cfg_value: float = 2.0, timesteps: int = 10,
+                   out=None):
+        """One synchronous patch step: (latent, stop). out: an optional float32 [D*P]
+        array that receives the latent; a C-contiguous float32 noise array is passed
+        without a copy."""
+        lat = np.empty(self.cfg.latent, np.float32) if out is None else out
+        if not (lat.dtype == np.float32 and lat.flags.c_contiguous and lat.size == self.cfg.latent):
+            raise ValueError("out must be a contiguous float32 array of one latent patch")
+        if noise is not None and not (isinstance(noise, np.ndarray) and noise.dtype == np.float32
+                                      and noise.flags.c_contiguous):
+            noise = _f32(noise)
+        stop = self._stop_out = getattr(self, "_stop_out", None) or C.c_int32(0)
+        rc = lib().vxc_patch_step(self._h, None if noise is None else noise.ctypes.data, min_patches, step,
+                                  cfg_value, timesteps, lat.ctypes.data, C.byref(stop))
+        if rc:
+            _check(rc)
         return lat, bool(stop.value)
 
     def generate(self, text_ids, min_patches: int = 2, timesteps: int = 10, cfg_value: float = 2.0,
