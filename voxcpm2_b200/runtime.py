@@ -293,7 +293,7 @@ class Stream:
         if noise is not None and not (isinstance(noise, np.ndarray) and noise.dtype == np.float32
                                       and noise.flags.c_contiguous):
             noise = _f32(noise)
-        stop = self._stop_out = getattr(self, "_stop_out", None) or C.c_int32(0)
+        stop = C.c_int32(0)
         rc = lib().vxc_patch_step(self._h, None if noise is None else noise.ctypes.data, min_patches, step,
                                   cfg_value, timesteps, lat.ctypes.data, C.byref(stop))
         if rc:
@@ -348,7 +348,7 @@ class Stream:
         lat = np.empty(self.cfg.latent, np.float32) if out is None else out
         if not (lat.dtype == np.float32 and lat.flags.c_contiguous and lat.size == self.cfg.latent):
             raise ValueError("out must be a contiguous float32 array of one latent patch")
-        stop = self._stop_out = getattr(self, "_stop_out", None) or C.c_int32(0)
+        stop = C.c_int32(0)
         rc = _lib.vxc_patch_collect(self._h, lat.ctypes.data, C.byref(stop))
         if rc:
             _check(rc)
