@@ -925,7 +925,7 @@ void enqueue_post_stop_feat(vxc_stream* s) {
 void enqueue_post_fsq_fusion(vxc_stream* s) {
     const vxc_device* dev = s->dev;
     const vxc_model_desc& d = dev->desc;
-    const int H = d.hidden, L = d.feat_dim * d.patch_size;
+    const int H = d.hidden;
     // fsq
     const __half* fq = dev->blob[VXC_FSQ];
     const size_t Q = d.fsq_dim;
