@@ -32,23 +32,6 @@ __device__ __forceinline__ float gemv_input(const GemvArgs& a, int k) {
     return a.x[k];
 }
 
-// Fixed-point residual updates (units of kFixedUnit) of the fused decoder layer.
-__device__ __forceinline__ long long to_fixed(float v) { return __float2ll_rn(v * (1.0f / kFixedUnit)); }
-__device__ __forceinline__ float4 add_fixed4(float4 v, const long long* d, int i) {
-    const longlong2 a = reinterpret_cast<const longlong2*>(d)[2 * i];
-    const longlong2 b = reinterpret_cast<const longlong2*>(d)[2 * i + 1];
-    return make_float4(v.x + __ll2float_rn(a.x) * kFixedUnit, v.y + __ll2float_rn(a.y) * kFixedUnit,
-                       v.z + __ll2float_rn(b.x) * kFixedUnit, v.w + __ll2float_rn(b.y) * kFixedUnit);
-}
-__device__ __forceinline__ void zero_fixed4(long long* d, int i) {
-    reinterpret_cast<longlong2*>(d)[2 * i] = make_longlong2(0, 0);
-    reinterpret_cast<longlong2*>(d)[2 * i + 1] = make_longlong2(0, 0);
-}
-// Integer addition is associative: the sum is the same in any order of arrival.
-__device__ __forceinline__ void add_fixed(long long* d, float v) {
-    atomicAdd(reinterpret_cast<unsigned long long*>(d), static_cast<unsigned long long>(to_fixed(v)));
-}
-
 // Epilogue of one GEMV output unit (lane 0 of its warp): bias / activation,
 // residual update, SiLU(gate) * up, or RoPE + KV append for q/k/v.
 template <int MODE, int RPW>
@@ -144,9 +127,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
     // issued before any is used: one L2 round trip instead of a chain of them.
     float ss = 0.f;
     const bool vec = a.in_mode == IN_PLAIN && (K & 3) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 &&
-                     (reinterpret_cast<uintptr_t>(a.norm_g) & 7) == 0 &&
-                     ((reinterpret_cast<uintptr_t>(a.delta) | reinterpret_cast<uintptr_t>(a.x_out) |
-                       reinterpret_cast<uintptr_t>(a.zero)) & 15) == 0;
+                     (reinterpret_cast<uintptr_t>(a.norm_g) & 7) == 0;
     if (vec) {
         constexpr int kV = MAXCH >= 2 ? MAXCH / 2 : 1;  // float4 per thread: K <= 256 MAXCH
         const int n4 = K >> 2;
@@ -157,23 +138,6 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
             const int i = threadIdx.x + j * kGemvThreads;
             xv[j] = i < n4 ? reinterpret_cast<const float4*>(a.x)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
             gv[j] = (a.norm_g && i < n4) ? reinterpret_cast<const uint2*>(a.norm_g)[i] : make_uint2(0u, 0u);
-        }
-        if (a.delta) {
-#pragma unroll
-            for (int j = 0; j < kV; ++j) {
-                const int i = threadIdx.x + j * kGemvThreads;
-                if (i < n4) xv[j] = add_fixed4(xv[j], a.delta, i);
-            }
-        }
-        if (blockIdx.x == 0) {
-#pragma unroll
-            for (int j = 0; j < kV; ++j) {
-                const int i = threadIdx.x + j * kGemvThreads;
-                if (i < n4) {
-                    if (a.x_out) reinterpret_cast<float4*>(a.x_out)[i] = xv[j];
-                    if (a.zero) zero_fixed4(a.zero, i);
-                }
-            }
         }
 #pragma unroll
         for (int j = 0; j < kV; ++j) {
@@ -191,12 +155,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
         }
     } else {
         for (int k = threadIdx.x; k < K; k += kGemvThreads) {
-            float v = gemv_input(a, k);
-            if (a.delta) v += __ll2float_rn(a.delta[k]) * kFixedUnit;
-            if (blockIdx.x == 0) {
-                if (a.x_out) a.x_out[k] = v;
-                if (a.zero) a.zero[k] = 0;
-            }
+            const float v = gemv_input(a, k);
             ss += v * v;
             xs[k] = a.norm_g ? v * __half2float(a.norm_g[k]) : v;
         }
@@ -862,18 +821,13 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
 }
 
 __global__ void final_norm_kernel(const float* h, const __half* g, float eps, int H, float* out,
-                                  float* out2, StreamCtl* ctl, int which, int bump, int skip,
-                                  const long long* delta) {
+                                  float* out2, StreamCtl* ctl, int which, int bump, int skip) {
     __shared__ float red[32];
     pdl_launch_dependents();
     pdl_wait();
     if (skip && ctl && ctl->stopped) return;
-    auto hv = [&](int k) { return delta ? h[k] + __ll2float_rn(delta[k]) * kFixedUnit : h[k]; };
     float ss = 0.f;
-    for (int k = threadIdx.x; k < H; k += blockDim.x) {
-        const float v = hv(k);
-        ss += v * v;
-    }
+    for (int k = threadIdx.x; k < H; k += blockDim.x) ss += h[k] * h[k];
     ss = warp_sum(ss);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
     __syncthreads();
@@ -881,7 +835,7 @@ __global__ void final_norm_kernel(const float* h, const __half* g, float eps, in
     for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += red[w];
     const float a = rsqrtf(t / static_cast<float>(H) + eps);
     for (int k = threadIdx.x; k < H; k += blockDim.x) {
-        const float v = hv(k) * a * __half2float(g[k]);
+        const float v = h[k] * a * __half2float(g[k]);
         out[k] = v;
         if (out2) out2[k] = v;
     }
@@ -1076,365 +1030,6 @@ void launch_attn_decode_cluster(const AttnArgs& a, cudaStream_t s, bool pdl) {
     launch_attn_decode_cluster_batch(a, AttnBatch{}, s, pdl);
 }
 
-// ------------------------------------------------ fused decoder layer -----
-namespace {
-
-constexpr int kMaxOwnHeads = 2;   // W_o head slices per cluster CTA (query heads per KV head <= 16)
-constexpr size_t kAttnOSmemMax = 200 * 1024;
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-
-__device__ __forceinline__ void bulk_bar_init(uint64_t* bar) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(bar)))
-                 : "memory");
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-__device__ __forceinline__ void bulk_expect(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
-                     static_cast<uint32_t>(__cvta_generic_to_shared(bar))),
-                 "r"(bytes)
-                 : "memory");
-}
-
-// Dynamic shared memory of attn_o_cluster_kernel: the W_o slices of up to 'own'
-// heads, then the cluster's partial-sum row [H].
-__host__ __device__ constexpr size_t attn_o_part_offset(int own, int H, int D) {
-    return static_cast<size_t>(own) * H * D * 2;
-}
-
-// Attention (the cluster kernel above) + delta += rscale * W_o attn.
-template <int D>
-__global__ void __launch_bounds__(kAttnThreads) attn_o_cluster_kernel(const AttnArgs a, const AttnOArgs o, int own_max) {
-    static_assert(D == 64, "head_dim 64");
-    extern __shared__ __align__(128) uint8_t dyn_sm[];
-    __shared__ AttnSmem S;
-    __shared__ float pacc[kMaxGroup][D], pm[kMaxGroup], pl[kMaxGroup];
-    __shared__ __align__(16) float att[kMaxOwnHeads][D];
-    __shared__ uint64_t bar;
-    const int G = a.q_heads / a.kv_heads, C = kAttnCluster, H = o.hidden;
-    const int rank = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x;
-    const int own = rank < G ? (G - rank + C - 1) / C : 0;  // heads rank, rank + C, ...
-    __half* wsm = reinterpret_cast<__half*>(dyn_sm);
-    float* part = reinterpret_cast<float*>(dyn_sm + attn_o_part_offset(own_max, H, D));
-
-    // 1) this CTA's W_o columns (independent of earlier kernels)
-    if (tid == 0) {
-        bulk_bar_init(&bar);
-        if (own > 0) {
-            bulk_expect(&bar, static_cast<uint32_t>(own * H * D * 2));
-            for (int i = 0; i < own; ++i)
-                bulk_g2s(wsm + static_cast<size_t>(i) * H * D,
-                         o.wo_heads + static_cast<size_t>(kvh * G + rank + i * C) * H * D,
-                         static_cast<uint32_t>(H * D * 2), &bar);
-        }
-    }
-    __syncthreads();
-    pdl_launch_dependents();
-    pdl_wait();
-    // uniform over the grid: the flag cannot change while the kernel runs
-    if (a.skip_if_stopped && a.ctl && a.ctl->stopped) {
-        if (own > 0) bulk_wait(&bar);  // no exit with a copy in flight
-        return;
-    }
-    if (rank == 0 && kvh == 0 && o.zero)
-        for (int k = tid; k < H; k += kAttnThreads) o.zero[k] = 0;
-
-    // 2) attention over this CTA's key range, combined across the cluster
-    const int len0 = min(a.ctl->kv_len[a.which] + 1, a.len0);  // len0 holds the capacity
-    const int T = len0;
-    const int chunk = (T + C - 1) / C, t0 = rank * chunk, n = max(0, min(T, t0 + chunk) - t0);
-    const int e = tid & (D - 1), gh = tid / D;
-    const int hg = (G + 1) / 2, g_lo = gh * hg, g_hi = min(G, g_lo + hg);
-    float acc[8];
-    attend_keys<float, D>(a, S, kvh, G, t0, n, len0, acc);
-    __syncthreads();
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-        if (g_lo + j < g_hi) pacc[g_lo + j][e] = acc[j];
-    if (tid < G) {
-        pm[tid] = n > 0 ? S.m_s[tid] : -1e30f;
-        pl[tid] = S.l_s[tid];
-    }
-    cluster_barrier();  // every CTA's partial is visible cluster-wide
-    for (int i = 0; i < own; ++i) {
-        const int g = rank + i * C;
-        if (tid < D) {
-            float mr[kAttnCluster], lr[kAttnCluster], ar[kAttnCluster];
-#pragma unroll
-            for (int r = 0; r < kAttnCluster; ++r) {
-                mr[r] = ld_peer(&pm[g], r);
-                lr[r] = ld_peer(&pl[g], r);
-                ar[r] = ld_peer(&pacc[g][tid], r);
-            }
-            float M = -1e30f;
-#pragma unroll
-            for (int r = 0; r < kAttnCluster; ++r) M = fmaxf(M, mr[r]);
-            float num = 0.f, den = 0.f;
-#pragma unroll
-            for (int r = 0; r < kAttnCluster; ++r) {
-                const float w = __expf(mr[r] - M);
-                num = fmaf(w, ar[r], num);
-                den = fmaf(w, lr[r], den);
-            }
-            att[i][tid] = num / den;
-        }
-    }
-    const bool ok = own == 0 || bulk_wait(&bar);
-    if (!ok && tid == 0) a.ctl->error = 3;
-    __syncthreads();
-
-    // 3) part[j] = sum over this CTA's heads of W_o[j][head cols] . att: 8 lanes per
-    // row (16 B each), 4 rows per warp instruction
-    const int lane = tid & 31, warp = tid >> 5, sub = lane & 7;
-    float4 a0[kMaxOwnHeads], a1[kMaxOwnHeads];
-#pragma unroll
-    for (int i = 0; i < kMaxOwnHeads; ++i) {
-        a0[i] = i < own ? *reinterpret_cast<const float4*>(&att[i][sub * 8]) : make_float4(0.f, 0.f, 0.f, 0.f);
-        a1[i] = i < own ? *reinterpret_cast<const float4*>(&att[i][sub * 8 + 4]) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    for (int j0 = warp * 4; j0 < H; j0 += (kAttnThreads / kWarp) * 4) {
-        const int j = j0 + (lane >> 3);
-        float sacc = 0.f;
-        if (ok) {
-#pragma unroll
-            for (int i = 0; i < kMaxOwnHeads; ++i)
-                if (i < own)
-                    sacc = dot8(*reinterpret_cast<const uint4*>(wsm + (static_cast<size_t>(i) * H + j) * D + sub * 8),
-                                a0[i], a1[i], sacc);
-        }
-        sacc += __shfl_xor_sync(0xffffffffu, sacc, 1);
-        sacc += __shfl_xor_sync(0xffffffffu, sacc, 2);
-        sacc += __shfl_xor_sync(0xffffffffu, sacc, 4);
-        if (sub == 0) part[j] = sacc;
-    }
-    cluster_barrier();
-    // 4) CTA r adds outputs [r H / C, (r + 1) H / C), summed over the cluster in rank order
-    const int per = H / C;
-    for (int j = rank * per + tid; j < (rank + 1) * per; j += kAttnThreads) {
-        float v = 0.f;
-#pragma unroll
-        for (int r = 0; r < kAttnCluster; ++r) v += ld_peer(&part[j], r);
-        add_fixed(o.delta + j, v * o.rscale);
-    }
-    cluster_barrier();  // no CTA leaves while another still reads its shared memory
-}
-
-constexpr int kFfnUnits = 16;
-constexpr int kFfnThreads = 256;
-constexpr int kFfnCluster = 8;
-
-__host__ __device__ constexpr size_t ffn_smem_bytes(int H) {
-    return 3 * static_cast<size_t>(kFfnUnits) * H * 2 + 2 * static_cast<size_t>(H) * 4;
-}
-
-__global__ void __launch_bounds__(kFfnThreads) ffn_fused_kernel(const FfnArgs f) {
-    constexpr int U = kFfnUnits;
-    extern __shared__ __align__(128) uint8_t dyn_sm[];
-    __shared__ uint64_t bar;
-    __shared__ float red[kFfnThreads / kWarp];
-    __shared__ float act[U];
-    const int H = f.hidden, F = f.ffn, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int u0 = blockIdx.x * U;
-    const size_t rows_bytes = static_cast<size_t>(U) * H * 2;
-    __half* wg = reinterpret_cast<__half*>(dyn_sm);
-    __half* wu = wg + static_cast<size_t>(U) * H;
-    __half* wd = wu + static_cast<size_t>(U) * H;
-    float* xs = reinterpret_cast<float*>(dyn_sm + 3 * rows_bytes);
-    float* part = xs + H;
-
-    // 1) gate, up and transposed down rows of this block's units
-    if (tid == 0) {
-        bulk_bar_init(&bar);
-        bulk_expect(&bar, static_cast<uint32_t>(3 * rows_bytes));
-        bulk_g2s(wg, f.wgateup + static_cast<size_t>(u0) * H, static_cast<uint32_t>(rows_bytes), &bar);
-        bulk_g2s(wu, f.wgateup + static_cast<size_t>(F + u0) * H, static_cast<uint32_t>(rows_bytes), &bar);
-        bulk_g2s(wd, f.wdown_t + static_cast<size_t>(u0) * H, static_cast<uint32_t>(rows_bytes), &bar);
-    }
-    __syncthreads();
-    pdl_launch_dependents();
-    pdl_wait();
-    if (f.skip_if_stopped && f.ctl && f.ctl->stopped) {
-        bulk_wait(&bar);
-        return;
-    }
-
-    // 2) x = h_in + delta_in (block 0 keeps it for the next layer), RMSNorm
-    float ss = 0.f;
-    for (int i = tid; i < H / 4; i += kFfnThreads) {
-        float4 v = reinterpret_cast<const float4*>(f.h_in)[i];
-        if (f.delta_in) v = add_fixed4(v, f.delta_in, i);
-        if (blockIdx.x == 0) reinterpret_cast<float4*>(f.h_out)[i] = v;
-        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-        const uint2 gv = reinterpret_cast<const uint2*>(f.norm_g)[i];
-        const float2 g01 = __half22float2(*reinterpret_cast<const __half2*>(&gv.x));
-        const float2 g23 = __half22float2(*reinterpret_cast<const __half2*>(&gv.y));
-        reinterpret_cast<float4*>(xs)[i] = make_float4(v.x * g01.x, v.y * g01.y, v.z * g23.x, v.w * g23.y);
-    }
-    ss = warp_sum(ss);
-    if (lane == 0) red[warp] = ss;
-    const bool ok = bulk_wait(&bar);
-    if (!ok && tid == 0 && f.ctl) f.ctl->error = 3;
-    __syncthreads();
-    float tot = 0.f;
-#pragma unroll
-    for (int w = 0; w < kFfnThreads / kWarp; ++w) tot += red[w];
-    const float inv_rms = rsqrtf(tot / static_cast<float>(H) + f.eps);
-
-    // 3) act[u] = silu(gate_u . n) * (up_u . n)
-    for (int u = warp; u < U; u += kFfnThreads / kWarp) {
-        float g = 0.f, up = 0.f;
-        if (ok) {
-            for (int k = lane * 8; k < H; k += kWarp * 8) {
-                const float4 x0 = *reinterpret_cast<const float4*>(&xs[k]);
-                const float4 x1 = *reinterpret_cast<const float4*>(&xs[k + 4]);
-                g = dot8(*reinterpret_cast<const uint4*>(wg + static_cast<size_t>(u) * H + k), x0, x1, g);
-                up = dot8(*reinterpret_cast<const uint4*>(wu + static_cast<size_t>(u) * H + k), x0, x1, up);
-            }
-        }
-        g = warp_sum(g) * inv_rms;
-        up = warp_sum(up) * inv_rms;
-        if (lane == 0) act[u] = silu(g) * up;
-    }
-    __syncthreads();
-
-    // 4) this block's share of W_down act: part[j] = sum_u W_down^T[u][j] act[u]
-    for (int j2 = tid; j2 < H / 2; j2 += kFfnThreads) {
-        float p0 = 0.f, p1 = 0.f;
-        if (ok) {
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const float2 w = __half22float2(reinterpret_cast<const __half2*>(wd + static_cast<size_t>(u) * H)[j2]);
-                p0 = fmaf(w.x, act[u], p0);
-                p1 = fmaf(w.y, act[u], p1);
-            }
-        }
-        reinterpret_cast<float2*>(part)[j2] = make_float2(p0, p1);
-    }
-    cluster_barrier();
-    // 5) CTA r adds outputs [r H / 8, (r + 1) H / 8), summed over the cluster in rank order
-    const int rank = static_cast<int>(cluster_rank()), per = H / kFfnCluster;
-    for (int j = rank * per + tid; j < (rank + 1) * per; j += kFfnThreads) {
-        float v = 0.f;
-#pragma unroll
-        for (int r = 0; r < kFfnCluster; ++r) v += ld_peer(&part[j], r);
-        add_fixed(f.delta_out + j, v * f.rscale);
-    }
-    cluster_barrier();
-}
-
-// out[h][j][e] = w[j][h d + e]
-__global__ void split_heads_kernel(const __half* w, __half* out, int H, int heads, int d) {
-    const size_t total = static_cast<size_t>(heads) * H * d;
-    for (size_t o = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; o < total;
-         o += static_cast<size_t>(gridDim.x) * blockDim.x) {
-        const int e = static_cast<int>(o % d);
-        const size_t r = o / d;
-        const int j = static_cast<int>(r % H), h = static_cast<int>(r / H);
-        out[o] = w[static_cast<size_t>(j) * heads * d + static_cast<size_t>(h) * d + e];
-    }
-}
-
-// out[c][r] = w[r][c] through 32 x 32 shared-memory tiles
-__global__ void transpose_f16_kernel(const __half* w, __half* out, int rows, int cols) {
-    __shared__ __half tile[32][33];
-    const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
-    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-        const int r = r0 + i, c = c0 + threadIdx.x;
-        if (r < rows && c < cols) tile[i][threadIdx.x] = w[static_cast<size_t>(r) * cols + c];
-    }
-    __syncthreads();
-    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-        const int c = c0 + i, r = r0 + threadIdx.x;
-        if (r < rows && c < cols) out[static_cast<size_t>(c) * rows + r] = tile[threadIdx.x][i];
-    }
-}
-
-}  // namespace
-
-bool attn_o_supported(int hidden, int q_heads, int kv_heads, int head_dim) {
-    if (head_dim != 64 || kv_heads <= 0 || q_heads % kv_heads != 0 || hidden % 64 != 0) return false;
-    const int G = q_heads / kv_heads;
-    const int own_max = (G + kAttnCluster - 1) / kAttnCluster;
-    return G <= kMaxGroup && own_max <= kMaxOwnHeads &&
-           attn_o_part_offset(own_max, hidden, head_dim) + static_cast<size_t>(hidden) * 4 <= kAttnOSmemMax;
-}
-
-void launch_attn_o(const AttnArgs& a, const AttnOArgs& o, cudaStream_t s, bool pdl) {
-    if (!attn_o_supported(o.hidden, a.q_heads, a.kv_heads, a.head_dim))
-        throw std::invalid_argument("attention + o: unsupported shape");
-    if (a.ctl == nullptr || o.delta == nullptr || o.wo_heads == nullptr)
-        throw std::invalid_argument("attention + o: needs the control block, W_o slices and an accumulator");
-    for (const void* p : {static_cast<const void*>(a.k0), static_cast<const void*>(a.v0),
-                          static_cast<const void*>(o.wo_heads), static_cast<const void*>(o.delta),
-                          static_cast<const void*>(o.zero)})
-        if (reinterpret_cast<uintptr_t>(p) % 16 != 0)
-            throw std::invalid_argument("attention + o: pointers must be 16-byte aligned");
-    const int G = a.q_heads / a.kv_heads;
-    const int own_max = (G + kAttnCluster - 1) / kAttnCluster;
-    const size_t smem = attn_o_part_offset(own_max, o.hidden, a.head_dim) + static_cast<size_t>(o.hidden) * 4;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(kAttnCluster, a.kv_heads, 1);
-    cfg.blockDim = dim3(kAttnThreads);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = kAttnCluster;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 2 : 1;
-    check_launch(cudaLaunchKernelEx(&cfg, attn_o_cluster_kernel<64>, a, o, own_max));
-}
-
-bool ffn_fused_supported(int hidden, int ffn) {
-    return hidden > 0 && hidden % 64 == 0 && ffn > 0 && ffn % (kFfnUnits * kFfnCluster) == 0 &&
-           ffn_smem_bytes(hidden) <= kAttnOSmemMax;
-}
-
-void launch_ffn_fused(const FfnArgs& f, cudaStream_t s, bool pdl) {
-    if (!ffn_fused_supported(f.hidden, f.ffn)) throw std::invalid_argument("fused MLP: unsupported shape");
-    if (f.h_in == nullptr || f.h_out == nullptr || f.delta_out == nullptr || f.norm_g == nullptr)
-        throw std::invalid_argument("fused MLP: missing buffer");
-    for (const void* p : {static_cast<const void*>(f.wgateup), static_cast<const void*>(f.wdown_t),
-                          static_cast<const void*>(f.h_in), static_cast<const void*>(f.delta_in),
-                          static_cast<const void*>(f.h_out), static_cast<const void*>(f.delta_out)})
-        if (reinterpret_cast<uintptr_t>(p) % 16 != 0)
-            throw std::invalid_argument("fused MLP: pointers must be 16-byte aligned");
-    if (reinterpret_cast<uintptr_t>(f.norm_g) % 8 != 0) throw std::invalid_argument("fused MLP: gain alignment");
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(f.ffn / kFfnUnits);
-    cfg.blockDim = dim3(kFfnThreads);
-    cfg.dynamicSmemBytes = ffn_smem_bytes(f.hidden);
-    cfg.stream = s;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = kFfnCluster;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 2 : 1;
-    check_launch(cudaLaunchKernelEx(&cfg, ffn_fused_kernel, f));
-}
-
-void launch_split_heads(const __half* w, __half* out, int H, int heads, int d, cudaStream_t s) {
-    split_heads_kernel<<<592, 256, 0, s>>>(w, out, H, heads, d);
-    check_launch(cudaGetLastError());
-}
-
-void launch_transpose_f16(const __half* w, __half* out, int rows, int cols, cudaStream_t s) {
-    transpose_f16_kernel<<<dim3((cols + 31) / 32, (rows + 31) / 32), dim3(32, 8), 0, s>>>(w, out, rows, cols);
-    check_launch(cudaGetLastError());
-}
-
 void launch_attn_decode(const AttnArgs& a, bool fp16_kv, cudaStream_t s, bool pdl) {
     if (a.head_dim != 64) throw std::invalid_argument("attention: head_dim must be 64");
     if (a.kv_heads <= 0 || a.q_heads % a.kv_heads != 0 || a.splits < 1)
@@ -1481,10 +1076,6 @@ void init_kernel_attributes() {
                           reinterpret_cast<const void*>(gemv_bulk_kernel<GEMV_GATEUP>),
                           reinterpret_cast<const void*>(gemv_bulk_kernel<GEMV_QKV>)})
         check_launch(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kBulkSmemMax)));
-    check_launch(cudaFuncSetAttribute(attn_o_cluster_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(kAttnOSmemMax)));
-    check_launch(cudaFuncSetAttribute(ffn_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(kAttnOSmemMax)));
     init_batched_attributes();
     init_tc_attributes();
     init_dit_layers_attributes();
@@ -1494,11 +1085,11 @@ void init_kernel_attributes() {
 
 void launch_final_norm(const float* h, const __half* g, float eps, int H, float* out, float* out2,
                        StreamCtl* ctl, int which, int bump, int skip_if_stopped, cudaStream_t s,
-                       bool pdl, const long long* delta) {
+                       bool pdl) {
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = make_cfg(dim3(1), dim3(256), 0, s, pdl, attr);
     check_launch(cudaLaunchKernelEx(&cfg, final_norm_kernel, h, g, eps, H, out, out2, ctl, which, bump,
-                                    skip_if_stopped, delta));
+                                    skip_if_stopped));
 }
 
 }  // namespace vxc

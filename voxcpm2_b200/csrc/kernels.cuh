@@ -51,11 +51,6 @@ struct GemvArgs {
     float* v_cache = nullptr;
     int cap = 0;
     int which = 0;                  // which decoder's kv_len indexes the cache
-    // fused decoder layers (IN_PLAIN): the input is x + delta (a fixed-point residual
-    // update, kFixedUnit units); block 0 writes that sum to x_out and clears 'zero'
-    const long long* delta = nullptr;  // [K] or null
-    float* x_out = nullptr;            // [K] or null
-    long long* zero = nullptr;         // [K] or null
     // control
     StreamCtl* ctl = nullptr;
     int skip_if_stopped = 0;
@@ -124,61 +119,10 @@ struct AttnBatch {
 };
 void launch_attn_decode_cluster_batch(const AttnArgs& a, const AttnBatch& b, cudaStream_t s, bool pdl);
 
-// final RMSNorm of a decoder step: out = norm(h + delta) * g (delta: a fixed-point
-// residual update, or null); optionally bump kv_len.
+// final RMSNorm of a decoder step: out = norm(h) * g; optionally bump kv_len.
 void launch_final_norm(const float* h, const __half* g, float eps, int H, float* out, float* out2,
                        StreamCtl* ctl, int which, int bump, int skip_if_stopped, cudaStream_t s,
-                       bool pdl, const long long* delta = nullptr);
-
-// ------------------------------------------------ fused decoder layer -----
-// A decoder layer in three launches: the q/k/v GEMV (launch_gemv with delta /
-// x_out / zero), attention with the o projection, and the whole MLP. The two
-// residual updates of a layer (o and down) are summed across CTAs as 64-bit
-// fixed-point integers (units of kFixedUnit) by atomic adds, so the result does
-// not depend on the order in which CTAs finish.
-constexpr float kFixedUnit = 1.0f / 68719476736.0f;  // 2^-36: +-1.3e8 range, 1.5e-11 resolution
-
-// Attention of one query token (as launch_attn_decode_cluster) followed by
-// delta += rscale * W_o attn: cluster CTA r holds the W_o columns of heads r,
-// r + 8, ... of its KV group (copied to shared memory before the dependency
-// wait), the cluster sums its heads' contributions in rank order and adds them
-// to delta. CTA (0, 0) clears 'zero' (the MLP's accumulator).
-struct AttnOArgs {
-    const __half* wo_heads = nullptr;  // [q_heads][H][head_dim]: W_o's columns per head
-    int hidden = 0;
-    float rscale = 1.0f;
-    long long* delta = nullptr;        // [H], accumulated
-    long long* zero = nullptr;         // [H] or null
-};
-void launch_attn_o(const AttnArgs& a, const AttnOArgs& o, cudaStream_t s, bool pdl);
-bool attn_o_supported(int hidden, int q_heads, int kv_heads, int head_dim);
-
-// The MLP of a decoder layer: x = h_in + delta_in (block 0 writes x to h_out),
-// delta_out += rscale * W_down (silu(W_gate n) * (W_up n)), n = RMSNorm(x) * g.
-// Block b owns intermediate units [16 b, 16 b + 16): their gate, up and
-// transposed down rows are copied to shared memory before the dependency wait;
-// an 8-CTA cluster sums its down contributions in rank order.
-struct FfnArgs {
-    const __half* wgateup = nullptr;   // [2F][H]: gate rows, then up rows
-    const __half* wdown_t = nullptr;   // [F][H]: W_down transposed
-    const __half* norm_g = nullptr;    // post-attention RMSNorm gain
-    float eps = 1e-5f;
-    int hidden = 0, ffn = 0;
-    float rscale = 1.0f;
-    const float* h_in = nullptr;
-    const long long* delta_in = nullptr;
-    float* h_out = nullptr;
-    long long* delta_out = nullptr;
-    StreamCtl* ctl = nullptr;
-    int skip_if_stopped = 0;
-};
-void launch_ffn_fused(const FfnArgs& f, cudaStream_t s, bool pdl);
-bool ffn_fused_supported(int hidden, int ffn);
-
-// Layout copies for the fused layer (one-time, at weight load):
-// out[h][j][e] = w[j][h * d + e] for w [H][heads * d]; and out = w^T for w [rows][cols].
-void launch_split_heads(const __half* w, __half* out, int H, int heads, int d, cudaStream_t s);
-void launch_transpose_f16(const __half* w, __half* out, int rows, int cols, cudaStream_t s);
+                       bool pdl);
 
 // ----------------------------------------------------- token batches -----
 // Y[m][r] for M tokens (prefill rows, the DiT's 2 x 11 tokens).

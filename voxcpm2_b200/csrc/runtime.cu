@@ -87,9 +87,6 @@ void require(bool ok, const char* msg) {
 // ------------------------------------------------------------ weights ----
 struct LayerW {
     const __half *in_norm, *wqkv, *wo, *post_norm, *wgateup, *wdown;
-    // layout copies for the fused decoder layer (decoders only; null elsewhere):
-    // W_o's columns per query head [hq][H][d], and W_down transposed [F][H]
-    const __half *wo_heads = nullptr, *wdown_t = nullptr;
 };
 struct DecoderShape {
     int h, f, hq, hkv, d, layers;
@@ -282,7 +279,6 @@ struct vxc_device {
     CUtensorMap* dit_maps_dev = nullptr;       // the same maps in device memory (persistent DiT kernel)
     const __half** dit_norms_dev = nullptr;    // [layers][2] input / post-attention RMSNorm weights
     uint64_t epoch = 0;  // bumped by every weight upload (invalidates derived tables)
-    __half* fused_copies[2] = {};  // base / residual decoder: the LayerW layout copies
 };
 
 namespace {
@@ -395,15 +391,10 @@ struct vxc_stream {
     // split DiT form: RMSNorm folded into the neighbouring linears (the residual epilogue writes the
     // next operand, the consumer scales rows by 1/rms); VXC_NORM_KERNELS=1 launches separate RMSNorm kernels
     bool norm_kernels = false;
-    // decoder-step GEMVs of the five-launch layer: register-streaming (the default), or
+    // decoder-step GEMVs: register-streaming (the default: the highest 16-stream throughput), or
     // VXC_BULK_GEMV=1 for the bulk-copy form (weight rows into shared memory before the
-    // dependency wait)
+    // dependency wait; stream groups always use it, batched over their members)
     bool bulk_gemv = false;
-    // decoder layers in three launches (q/k/v GEMV, attention + o, the whole MLP) with
-    // fixed-point residual updates; VXC_FUSED_LAYERS=1 selects them over the five-launch layer
-    bool fused_layers = false;
-    float* h2[2] = {};         // the residual stream's second buffer (fused layers)
-    long long* dacc[2] = {};   // per decoder [2][H]: the o and MLP updates, fixed point
     float* dpart = nullptr;     // persistent launch: partial tiles
     unsigned* dsync = nullptr;  // persistent launch: grid barrier and tile counters
     int* dcount = nullptr;  // dit_out arrival counter
@@ -424,8 +415,7 @@ void free_all(vxc_stream* s) {
                     s->partial, s->counters, s->mu, s->x, s->cond, s->cond0, s->noise, s->latents, s->temb,
                     s->tmid, s->ttok, s->dtemb, s->dtmid, s->dttok, s->dtemb1, s->dtmid1, s->dttok1, s->dh,
                     s->dxn, s->dqkv, s->dattn, s->dact, s->est, s->gen_in, s->ph, s->pxn, s->pqkv, s->pattn,
-                    s->pact, s->pcat, s->pids, s->xb_n, s->xb_a, s->xb_act, s->h2[0], s->h2[1], s->dacc[0],
-                    s->dacc[1]};
+                    s->pact, s->pcat, s->pids, s->xb_n, s->xb_a, s->xb_act};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     for (auto& kv : s->ttab)
@@ -472,102 +462,9 @@ GemvArgs plain_gemv(const __half* w, const __half* b, const float* x, int K, int
 // the input embedding); writes the final-norm output to out (+ out2) and bumps
 // kv_len[which] on the device (unless advance is 0). ctl_override replaces the
 // stream's control block (the step profile runs on a private one).
-// The same step in three launches per layer. The residual stream alternates
-// between s->h (input, and the MLP's input of each layer) and s->h2 (each
-// layer's attention input); the o and MLP updates accumulate as fixed-point
-// integers in dacc[0] / dacc[1] and are folded in by the next kernel that reads
-// the stream (which also writes the sum back for the one after):
-//   q/k/v(l):    x = h + dacc[1] (l > 0)  -> h2 = x; clear dacc[0]; RMSNorm, q/k/v, RoPE, KV append
-//   attn+o(l):   dacc[0] += rscale W_o attn; clear dacc[1]
-//   MLP(l):      x = h2 + dacc[0]         -> h = x; dacc[1] += rscale W_down (silu(gate) up)
-//   final norm:  h + dacc[1]
-void enqueue_decoder_step_fused(vxc_stream* s, int which, float* out, float* out2, int skip, StreamCtl* ctl,
-                                int advance) {
-    const vxc_device* dev = s->dev;
-    const vxc_model_desc& d = dev->desc;
-    const std::vector<LayerW>& layers = which == 0 ? dev->base : dev->res;
-    const __half* fnorm = which == 0 ? dev->base_norm : dev->res_norm;
-    const float rscale = which == 0 ? d.base_residual_scale : d.res_residual_scale;
-    const int H = d.hidden, hq = d.q_heads, hkv = d.kv_heads, hd = d.head_dim;
-    const size_t plane = static_cast<size_t>(hkv) * s->cap * hd;
-    long long* d_attn = s->dacc[which];
-    long long* d_mlp = s->dacc[which] + H;
-    for (size_t l = 0; l < layers.size(); ++l) {
-        const LayerW& L = layers[l];
-        GemvArgs qa;
-        qa.mode = GEMV_QKV;
-        qa.w = L.wqkv;
-        qa.x = s->h[which];
-        qa.delta = l > 0 ? d_mlp : nullptr;
-        qa.x_out = s->h2[which];
-        qa.zero = d_attn;
-        qa.norm_g = L.in_norm;
-        qa.eps = d.rms_eps;
-        qa.K = H;
-        qa.rows = (hq + 2 * hkv) * hd / 2;
-        qa.y = s->q;
-        qa.q_heads = hq;
-        qa.kv_heads = hkv;
-        qa.head_dim = hd;
-        qa.rope_cos = which == 0 ? s->rope_cos : nullptr;
-        qa.rope_sin = which == 0 ? s->rope_sin : nullptr;
-        qa.k_cache = s->kc[which] + l * plane;
-        qa.v_cache = s->vc[which] + l * plane;
-        qa.cap = s->cap;
-        qa.which = which;
-        qa.ctl = ctl;
-        qa.skip_if_stopped = skip;
-        launch_gemv(qa, s->cs, s->pdl);
-
-        AttnArgs aa;
-        aa.q = s->q;
-        aa.k0 = s->kc[which] + l * plane;
-        aa.v0 = s->vc[which] + l * plane;
-        aa.len0 = s->cap;
-        aa.stride0 = s->cap;
-        aa.q_heads = hq;
-        aa.kv_heads = hkv;
-        aa.head_dim = hd;
-        aa.scale = 1.0f / std::sqrt(static_cast<float>(hd));
-        aa.ctl = ctl;
-        aa.which = which;
-        aa.skip_if_stopped = skip;
-        AttnOArgs oa;
-        oa.wo_heads = L.wo_heads;
-        oa.hidden = H;
-        oa.rscale = rscale;
-        oa.delta = d_attn;
-        oa.zero = d_mlp;
-        launch_attn_o(aa, oa, s->cs, s->pdl);
-
-        FfnArgs fa;
-        fa.wgateup = L.wgateup;
-        fa.wdown_t = L.wdown_t;
-        fa.norm_g = L.post_norm;
-        fa.eps = d.rms_eps;
-        fa.hidden = H;
-        fa.ffn = d.ffn;
-        fa.rscale = rscale;
-        fa.h_in = s->h2[which];
-        fa.delta_in = d_attn;
-        fa.h_out = s->h[which];
-        fa.delta_out = d_mlp;
-        fa.ctl = ctl;
-        fa.skip_if_stopped = skip;
-        launch_ffn_fused(fa, s->cs, s->pdl);
-    }
-    launch_final_norm(s->h[which], fnorm, d.rms_eps, H, out, out2, ctl, which, advance, skip, s->cs, s->pdl,
-                      layers.empty() ? nullptr : d_mlp);
-}
-
 void enqueue_decoder_step(vxc_stream* s, int which, float* out, float* out2, int skip,
                           StreamCtl* ctl_override = nullptr, int advance = 1) {
     StreamCtl* ctl = ctl_override ? ctl_override : s->ctl;
-    const std::vector<LayerW>& fl = which == 0 ? s->dev->base : s->dev->res;
-    if (s->fused_layers && !fl.empty() && fl[0].wo_heads) {
-        enqueue_decoder_step_fused(s, which, out, out2, skip, ctl, advance);
-        return;
-    }
     auto gemv = s->bulk_gemv ? launch_gemv_bulk : launch_gemv;
     const vxc_device* dev = s->dev;
     const vxc_model_desc& d = dev->desc;
@@ -1875,33 +1772,8 @@ VXC_API void vxc_device_destroy(vxc_device* dev) {
         if (dev->dit_rope_sin) cudaFree(dev->dit_rope_sin);
         if (dev->dit_maps_dev) cudaFree(dev->dit_maps_dev);
         if (dev->dit_norms_dev) cudaFree(dev->dit_norms_dev);
-        for (__half* p : dev->fused_copies)
-            if (p) cudaFree(p);
     }
     delete dev;
-}
-
-// The fused decoder layer's weight layouts (W_o per head, W_down transposed),
-// derived on the device from a freshly uploaded decoder blob.
-bool fused_layers_ok(const vxc_model_desc& d) {
-    return attn_o_supported(d.hidden, d.q_heads, d.kv_heads, d.head_dim) && ffn_fused_supported(d.hidden, d.ffn);
-}
-
-void fused_layer_copies(vxc_device* dev, std::vector<LayerW>& layers, int which) {
-    const vxc_model_desc& d = dev->desc;
-    if (!fused_layers_ok(d) || layers.empty()) return;
-    const size_t H = d.hidden, F = d.ffn, Q = static_cast<size_t>(d.q_heads) * d.head_dim;
-    const size_t per = Q * H + F * H;
-    if (!dev->fused_copies[which]) dev->fused_copies[which] = dev_alloc<__half>(per * layers.size());
-    for (size_t l = 0; l < layers.size(); ++l) {
-        __half* wo_h = dev->fused_copies[which] + l * per;
-        __half* wd_t = wo_h + Q * H;
-        launch_split_heads(layers[l].wo, wo_h, d.hidden, d.q_heads, d.head_dim, nullptr);
-        launch_transpose_f16(layers[l].wdown, wd_t, d.hidden, d.ffn, nullptr);
-        layers[l].wo_heads = wo_h;
-        layers[l].wdown_t = wd_t;
-    }
-    ck(cudaDeviceSynchronize(), "fused layer layouts");
 }
 
 VXC_API int32_t vxc_load_weights(vxc_device* dev, int32_t component, const void* fp16, size_t count) {
@@ -1919,12 +1791,10 @@ VXC_API int32_t vxc_load_weights(vxc_device* dev, int32_t component, const void*
             dev->base = carve_decoder(dev->blob[component], base_shape(dev->desc), &fn);
             dev->base_norm = fn;
             dev->base_maps = decoder_maps(dev->desc, dev->base);
-            fused_layer_copies(dev, dev->base, 0);
         } else if (component == VXC_RESIDUAL_DECODER) {
             dev->res = carve_decoder(dev->blob[component], res_shape(dev->desc), &fn);
             dev->res_norm = fn;
             dev->res_maps = decoder_maps(dev->desc, dev->res);
-            fused_layer_copies(dev, dev->res, 1);
         } else if (component == VXC_DIT_ESTIMATOR) {
             const size_t Hd = dev->desc.dit_hidden, D = dev->desc.feat_dim;
             const __half* base = dev->blob[component] + 2 * (Hd * D + Hd) + 4 * (Hd * Hd + Hd);
@@ -1977,9 +1847,6 @@ VXC_API int32_t vxc_stream_create(vxc_device* dev, int32_t kv_capacity, vxc_stre
             ck(cudaMemset(s->kc[w], 0, n * sizeof(float)), "cache");
             ck(cudaMemset(s->vc[w], 0, n * sizeof(float)), "cache");
             s->h[w] = dev_alloc<float>(H);
-            s->h2[w] = dev_alloc<float>(H);
-            s->dacc[w] = dev_alloc<long long>(2 * H);
-            ck(cudaMemset(s->dacc[w], 0, 2 * H * sizeof(long long)), "accumulators");
             s->out[w] = dev_alloc<float>(H);
         }
         std::vector<float> c, sn;
@@ -2031,7 +1898,6 @@ VXC_API int32_t vxc_stream_create(vxc_device* dev, int32_t kv_capacity, vxc_stre
         if (const char* nk = std::getenv("VXC_NORM_KERNELS")) s->norm_kernels = std::string(nk) == "1";
         if (const char* rs = std::getenv("VXC_RECV_SHARED")) s->recv_shared = std::string(rs) == "1";
         if (const char* bg = std::getenv("VXC_BULK_GEMV")) s->bulk_gemv = std::string(bg) == "1";
-        if (const char* fl = std::getenv("VXC_FUSED_LAYERS")) s->fused_layers = std::string(fl) != "0";
         if (const char* tt = std::getenv("VXC_TC_TARGET")) {
             s->tc_target = std::atoi(tt);
             if (s->tc_target < 1 || s->tc_target > 4096) throw std::invalid_argument("VXC_TC_TARGET must be in [1, 4096]");
