@@ -137,6 +137,19 @@ VXC_API void vxc_device_destroy(vxc_device* dev);
  * in voxcpm2_b200/config.py) to the device (replaces ncnn::Net::load_model). */
 VXC_API int32_t vxc_load_weights(vxc_device* dev, int32_t component, const void* fp16, size_t count);
 
+/* The base decoder's LongRoPE factors, n >= head_dim / 2 values each (the first
+ * head_dim / 2 are used; shorter tables are rejected, synthesizer.cpp:949-951): model.json's
+ * setting.rope.short_factor and long_factor (src/model_manifest.cpp:92-106, kept by
+ * load_manifest, synthesizer.cpp:825-830). Until this is called every factor is 1.
+ * As make_rope_cache (synthesizer.cpp:940-974), a call covering positions
+ * [start, start + n) rotates with long_factor when start + n > rope_original_max and
+ * long_factor is set, else with short_factor; long_factor may be NULL. The patch
+ * loop stays below rope_original_max (synthesizer.cpp:542-544), so there only the
+ * short factors apply. Streams pick the factors up at their next prefill or
+ * decoder step. Every factor must be positive. */
+VXC_API int32_t vxc_set_rope_factors(vxc_device* dev, const float* short_factor, const float* long_factor,
+                                     int32_t n);
+
 /* One synthesis stream: its CUDA stream, KV caches of kv_capacity tokens for both
  * decoders (replaces HostDecoderKvCache, src/kvcache.h:18-40), scratch and graphs. */
 VXC_API int32_t vxc_stream_create(vxc_device* dev, int32_t kv_capacity, vxc_stream** out);

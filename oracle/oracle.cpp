@@ -389,7 +389,11 @@ struct orc_model {
     // HostDecoderKvCache equivalents: per decoder, per layer, [kv_heads][T][d]
     std::vector<std::vector<float>> cache_k[2], cache_v[2];
     int tokens[2] = {0, 0};
-    std::vector<float> short_factor;  // all ones (synthetic checkpoints carry no LongRoPE table)
+    // LongRoPE factors of the base decoder (setting.rope.short_factor / long_factor,
+    // src/model_manifest.cpp:92-106): all ones until orc_set_rope_factors; an empty
+    // long table means the short one is used at every position
+    std::vector<float> short_factor, long_factor;
+    std::vector<float> dit_factor;  // the estimator's rotary table: all ones
 };
 
 namespace {
@@ -415,8 +419,8 @@ void decoder_forward(orc_model* m, int which, const float* embed, int n, const f
     if (use_rope && (!cos_in || !sin_in)) {
         cos.resize(static_cast<std::size_t>(n) * hd);
         sin.resize(cos.size());
-        rope_cache(hd, d.rope_theta, d.rope_original_max, m->short_factor.data(), nullptr, past, n,
-                   cos.data(), sin.data());
+        rope_cache(hd, d.rope_theta, d.rope_original_max, m->short_factor.data(),
+                   m->long_factor.empty() ? nullptr : m->long_factor.data(), past, n, cos.data(), sin.data());
         cos_in = cos.data();
         sin_in = sin.data();
     }
@@ -484,7 +488,7 @@ void dit_decoder(const orc_model* m, float* hidden, int nseq, int seq, float* ou
     const int H = s.h, F = s.f, hq = s.hq, hkv = s.hkv, hd = s.d;
     const int n = nseq * seq;
     std::vector<float> cos(static_cast<std::size_t>(seq) * hd), sin(cos.size());
-    rope_cache(hd, d.rope_theta, d.rope_original_max, m->short_factor.data(), nullptr, 0, seq,
+    rope_cache(hd, d.rope_theta, d.rope_original_max, m->dit_factor.data(), nullptr, 0, seq,
                cos.data(), sin.data());
     const std::size_t N = n, S = seq;
     std::vector<float> normed(N * H), q(N * hq * hd), k(N * hkv * hd), v(N * hkv * hd),
@@ -706,13 +710,28 @@ orc_model* orc_model_create(const orc_desc* desc) {
     if (!desc) return nullptr;
     auto* m = new orc_model;
     m->desc = *desc;
-    m->short_factor.assign(static_cast<std::size_t>(std::max(desc->head_dim, desc->dit_hidden)), 1.0f);
+    m->short_factor.assign(static_cast<std::size_t>(desc->head_dim), 1.0f);
+    m->dit_factor.assign(static_cast<std::size_t>(std::max(desc->head_dim, desc->dit_hidden)), 1.0f);
     const int layers[2] = {desc->base_layers, desc->res_layers};
     for (int w = 0; w < 2; ++w) {
         m->cache_k[w].resize(static_cast<std::size_t>(layers[w]));
         m->cache_v[w].resize(static_cast<std::size_t>(layers[w]));
     }
     return m;
+}
+
+// Synthesizer::Impl::load_manifest keeps setting.rope.short_factor / long_factor
+// (synthesizer.cpp:825-830); make_rope_cache picks the long table for a call whose
+// last position reaches original_max_position_embeddings (synthesizer.cpp:945-948).
+int orc_set_rope_factors(orc_model* m, const float* short_factor, const float* long_factor, int n) {
+    const int half = m ? m->desc.head_dim / 2 : 0;
+    if (!m || !short_factor || n < half) return -1;  // "rope tables are missing or too short"
+    for (int j = 0; j < half; ++j)
+        if (!(short_factor[j] > 0.f) || (long_factor && !(long_factor[j] > 0.f))) return -1;
+    m->short_factor.assign(short_factor, short_factor + half);
+    if (long_factor) m->long_factor.assign(long_factor, long_factor + half);
+    else m->long_factor.clear();
+    return 0;
 }
 
 void orc_model_destroy(orc_model* model) { delete model; }

@@ -100,6 +100,11 @@ size_t orc_component_count(const orc_desc* desc, int component);
 /* The blob is referenced, not copied: it must outlive the model. */
 int orc_set_weights(orc_model* model, int component, const uint16_t* fp16, size_t count);
 
+/* LongRoPE factors of the base decoder (n >= head_dim / 2 each, the first head_dim / 2
+ * used; long may be NULL): setting.rope.short_factor / long_factor. Returns -1 on a
+ * short table or a factor <= 0. */
+int orc_set_rope_factors(orc_model* model, const float* short_factor, const float* long_factor, int n);
+
 /* KV caches of one utterance (HostDecoderKvCache, kvcache.cpp:39-93). */
 void orc_reset_caches(orc_model* model);
 int orc_token_count(const orc_model* model, int which);

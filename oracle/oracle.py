@@ -80,6 +80,8 @@ def _setup(L) -> None:
     L.orc_component_count.restype = C.c_size_t
     L.orc_set_weights.argtypes = [vp, i, vp, C.c_size_t]
     L.orc_set_weights.restype = i
+    L.orc_set_rope_factors.argtypes = [vp, vp, vp, i]
+    L.orc_set_rope_factors.restype = i
     L.orc_reset_caches.argtypes = [vp]
     L.orc_token_count.argtypes = [vp, i]
     L.orc_token_count.restype = i
@@ -227,6 +229,15 @@ class Oracle:
         if m:
             lib().orc_model_destroy(m)
             self._m = None
+
+    def set_rope_factors(self, short_factor, long_factor=None) -> None:
+        """The base decoder's LongRoPE factors (at least head_dim / 2 values each; long optional)."""
+        self._sf = np.ascontiguousarray(short_factor, dtype=np.float32)
+        self._lf = None if long_factor is None else np.ascontiguousarray(long_factor, dtype=np.float32)
+        rc = lib().orc_set_rope_factors(self._m, _p(self._sf), _p(self._lf) if self._lf is not None else None,
+                                        self._sf.size)
+        if rc != 0:
+            raise ValueError("rope factors: at least head_dim / 2 positive values each")
 
     def reset(self) -> None:
         lib().orc_reset_caches(self._m)

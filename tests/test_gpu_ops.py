@@ -5,6 +5,8 @@ CPU path restated) on the same seeded inputs and fp16 weights.
 """
 from __future__ import annotations
 
+import dataclasses
+
 import numpy as np
 import pytest
 
@@ -151,6 +153,49 @@ def test_decoder_prefill_row_blocks(rt, models, name, which, n):
     assert gk.shape == wk.shape == (cfg.kv_heads, n + 1, cfg.head_dim)
     assert np.abs(gk - wk).max() <= 1e-4 * max(1.0, np.abs(wk).max())
     s.close()
+
+
+def test_decoder_rope_factors(rt):
+    """vxc_set_rope_factors against the oracle on both sides of original_max (24
+    here): one-row steps at positions below it rotate with the short factors, at or
+    past it with the long ones, and a prefill whose range passes it rotates every
+    row with the long ones (make_rope_cache's rule). The rotated keys in the KV
+    cache are held to 1e-4. Factors set after a stream exists apply from its next call."""
+    cfg = dataclasses.replace(TINY, rope_original_max=24)
+    blobs = synthetic.model_blobs(cfg, 0)
+    dev = rt.Device(cfg, 0, blobs)
+    s = rt.Stream(dev, kv_capacity=64)  # built before the factors are set
+    rng = np.random.default_rng(5)
+    short = rng.uniform(0.5, 2.0, cfg.head_dim // 2).astype(np.float32)
+    long = rng.uniform(2.0, 8.0, cfg.head_dim // 2).astype(np.float32)
+    dev.set_rope_factors(short, long)
+    orc = oracle.Oracle(cfg, blobs)
+    orc.set_rope_factors(short, long)
+    x = rng.standard_normal((30, cfg.hidden), dtype=np.float32)
+    assert_parity(s.decoder_step(0, x[:10]), orc.decoder_forward(0, x[:10]), 2e-2, 0.999, "prefill of 10")
+    for p in range(10, 30):
+        assert_parity(s.decoder_step(0, x[p:p + 1]), orc.decoder_forward(0, x[p:p + 1]), 2e-2, 0.999,
+                      f"step at position {p}")
+
+    def same_keys(st, what):
+        for layer in (0, cfg.base_layers - 1):
+            gk, _ = st.read_cache(0, layer)
+            wk, _ = orc.read_cache(0, layer)
+            assert gk.shape == wk.shape, what
+            assert np.abs(gk - wk).max() <= 1e-4 * max(1.0, np.abs(wk).max()), f"{what}, layer {layer}"
+
+    same_keys(s, "steps across original_max")
+    s2 = rt.Stream(dev, kv_capacity=64)
+    orc.reset()
+    assert_parity(s2.decoder_step(0, x), orc.decoder_forward(0, x), 2e-2, 0.999, "prefill of 30 (long factors)")
+    same_keys(s2, "prefill past original_max")
+    with pytest.raises(rt.VxcError):
+        dev.set_rope_factors(short[:-1])
+    with pytest.raises(rt.VxcError):
+        dev.set_rope_factors(-short)
+    s.close()
+    s2.close()
+    dev.close()
 
 
 def test_decoder_capacity_checked_before_launch(rt, models):

@@ -1,6 +1,8 @@
 """The CPU oracle against the reference's known-answer tests and the torch restatement."""
 from __future__ import annotations
 
+import dataclasses
+
 import numpy as np
 import pytest
 
@@ -85,6 +87,32 @@ def test_rope_long_factor_switch():
     c2, _ = oracle.rope_cache(64, 10000.0, 100, 90, 11, short, long)
     assert np.allclose(c1[0, :32], np.cos(90 * np.power(10000.0, -2.0 * np.arange(32) / 64)), atol=1e-5)
     assert np.allclose(c2[0, :32], np.cos(90 / 4.0 * np.power(10000.0, -2.0 * np.arange(32) / 64)), atol=1e-5)
+
+
+def test_decoder_rope_factors(tiny_blobs):
+    """LongRoPE factors set on the model rotate the base decoder's q/k exactly as
+    the tables make_rope_cache builds for the call's range (short below original
+    max, long once start + n exceeds it); the residual decoder has no RoPE."""
+    cfg = dataclasses.replace(TINY, rope_original_max=12)
+    rng = np.random.default_rng(3)
+    short = rng.uniform(0.5, 2.0, cfg.head_dim // 2).astype(np.float32)
+    long = rng.uniform(2.0, 8.0, cfg.head_dim // 2).astype(np.float32)
+    x = rng.standard_normal((14, cfg.hidden), dtype=np.float32)
+    plain = oracle.Oracle(cfg, tiny_blobs)
+    o = oracle.Oracle(cfg, tiny_blobs)
+    o.set_rope_factors(short, long)
+    ref = oracle.Oracle(cfg, tiny_blobs)
+    for start, n in ((0, 8), (8, 1), (9, 5)):  # the last call ends at 14 > 12: long factors
+        rows = x[start:start + n]
+        cos, sin = oracle.rope_cache(cfg.head_dim, cfg.rope_theta, 12, start, n, short, long)
+        got = o.decoder_forward(0, rows)
+        assert np.array_equal(got, ref.decoder_forward(0, rows, cos=cos, sin=sin))
+        assert not np.allclose(got, plain.decoder_forward(0, rows), atol=1e-6)
+    assert np.array_equal(o.decoder_forward(1, x[:3]), plain.decoder_forward(1, x[:3]))
+    with pytest.raises(ValueError):
+        o.set_rope_factors(short[:-1])
+    with pytest.raises(ValueError):
+        o.set_rope_factors(-short)
 
 
 def test_noise_table_is_libstdcxx_stream():

@@ -19,8 +19,10 @@ the CPU oracle:
 * ``dit_proj``     lm_proj and res_proj each H -> Hd, concatenated to the two mu tokens
                    (export_components.py:571-578; mu is reshaped into 2 tokens of Hd at :674-681).
 
-RoPE uses the reference's host table (synthesizer.cpp:928-974) with all LongRoPE
-factors equal to 1, and the rotate_half convention of ``apply_rotary_pos_emb``.
+RoPE uses the reference's host table (synthesizer.cpp:928-974) and the rotate_half
+convention of ``apply_rotary_pos_emb``. The base decoder's LongRoPE factors are 1
+unless set from model.json (``Device.set_rope_factors`` / ``vxc_set_rope_factors``);
+the estimator's rotary table keeps factors of 1 (its graph is not available here).
 """
 from __future__ import annotations
 

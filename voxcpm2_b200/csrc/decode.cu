@@ -60,9 +60,11 @@ __device__ __forceinline__ void gemv_store(const GemvArgs& a, int item, const in
         float o0 = acc[0], o1 = acc[1];
         const bool is_v = hh >= a.q_heads + a.kv_heads;
         if (!is_v && a.rope_cos && pos < a.cap) {
-            // apply_rotary_pos_emb with rotate_half: x*cos + rotate_half(x)*sin
-            const float* c = a.rope_cos + static_cast<size_t>(pos) * d;
-            const float* s = a.rope_sin + static_cast<size_t>(pos) * d;
+            // apply_rotary_pos_emb with rotate_half: x*cos + rotate_half(x)*sin; a one-row
+            // call at pos takes the long-factor table when pos + 1 > original_max
+            const bool lng = a.rope_cos_long && pos + 1 > a.rope_long_from;
+            const float* c = (lng ? a.rope_cos_long : a.rope_cos) + static_cast<size_t>(pos) * d;
+            const float* s = (lng ? a.rope_sin_long : a.rope_sin) + static_cast<size_t>(pos) * d;
             o0 = acc[0] * c[j] + (-acc[1]) * s[j];
             o1 = acc[1] * c[j + half] + acc[0] * s[j + half];
         }

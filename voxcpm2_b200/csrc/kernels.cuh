@@ -47,6 +47,10 @@ struct GemvArgs {
     int q_heads = 0, kv_heads = 0, head_dim = 0;
     const float* rope_cos = nullptr;  // [capacity][head_dim] or null (no RoPE)
     const float* rope_sin = nullptr;
+    // LongRoPE: the row of position pos comes from these tables when pos + 1 > rope_long_from
+    const float* rope_cos_long = nullptr;
+    const float* rope_sin_long = nullptr;
+    int rope_long_from = 1 << 30;
     float* k_cache = nullptr;       // this layer: [kv_heads][cap][head_dim]
     float* v_cache = nullptr;
     int cap = 0;

@@ -189,9 +189,11 @@ void validate_desc(const vxc_model_desc& d) {
     require(d.audio_start_token >= 0 && d.audio_start_token < d.vocab, "audio_start_token out of range");
 }
 
-// RoPE tables of Synthesizer::Impl::make_rope_cache (synthesizer.cpp:928-974)
-// with all LongRoPE factors 1: one row per position.
-void rope_table(int head_dim, float theta, int positions, std::vector<float>& cos_t, std::vector<float>& sin_t) {
+// RoPE tables of Synthesizer::Impl::make_rope_cache (synthesizer.cpp:928-974):
+// one row per position, freq_j = (pos / factor_j) * theta^(-2j / head_dim), with
+// 'factor' the chosen LongRoPE table (head_dim / 2 values) or all ones when null.
+void rope_table(int head_dim, float theta, int positions, std::vector<float>& cos_t, std::vector<float>& sin_t,
+                const float* factor = nullptr) {
     const int half = head_dim / 2;
     std::vector<float> inv(half);
     for (int j = 0; j < half; ++j) {
@@ -202,7 +204,7 @@ void rope_table(int head_dim, float theta, int positions, std::vector<float>& co
     sin_t.assign(cos_t.size(), 0.f);
     for (int p = 0; p < positions; ++p) {
         for (int j = 0; j < half; ++j) {
-            const float freq = (static_cast<float>(p) / 1.0f) * inv[j];
+            const float freq = (static_cast<float>(p) / (factor ? factor[j] : 1.0f)) * inv[j];
             const float c = std::cos(freq), s = std::sin(freq);
             cos_t[static_cast<size_t>(p) * head_dim + j] = c;
             cos_t[static_cast<size_t>(p) * head_dim + j + half] = c;
@@ -269,6 +271,9 @@ struct vxc_device {
     vxc_model_desc desc{};
     __half* blob[9] = {};
     bool loaded[9] = {};
+    // the base decoder's LongRoPE factors (vxc_set_rope_factors); empty = all ones / none
+    std::vector<float> rope_short, rope_long;
+    uint64_t rope_epoch = 0;
     std::vector<LayerW> base, res, dit;
     const __half *base_norm = nullptr, *res_norm = nullptr, *dit_norm = nullptr;
     float *dit_rope_cos = nullptr, *dit_rope_sin = nullptr;  // positions 0..seq-1
@@ -325,7 +330,9 @@ struct vxc_stream {
     StreamCtl* ctl = nullptr;       // device
     StreamCtl* ctl_host = nullptr;  // pinned mirror
     float *kc[2] = {}, *vc[2] = {};  // fp32 KV caches [layers][kv_heads][cap][head_dim]
-    float *rope_cos = nullptr, *rope_sin = nullptr;
+    float *rope_cos = nullptr, *rope_sin = nullptr;          // short-factor rows [cap][head_dim]
+    float *rope_cos_l = nullptr, *rope_sin_l = nullptr;      // long-factor rows (= short when none is set)
+    uint64_t rope_epoch = ~0ull;                             // device factors the tables were built from
     // batch-1 step buffers
     float *h[2] = {}, *out[2] = {}, *q = nullptr, *attn = nullptr, *act = nullptr;
     float *lm_h = nullptr, *res_h = nullptr, *feat = nullptr, *mid = nullptr, *mid2 = nullptr;
@@ -410,7 +417,8 @@ namespace {
 void free_all(vxc_stream* s) {
     if (s->graph) cudaGraphExecDestroy(s->graph);
     s->graph = nullptr;
-    void* ptrs[] = {s->ctl, s->kc[0], s->kc[1], s->vc[0], s->vc[1], s->rope_cos, s->rope_sin, s->h[0], s->h[1],
+    void* ptrs[] = {s->ctl, s->kc[0], s->kc[1], s->vc[0], s->vc[1], s->rope_cos, s->rope_sin, s->rope_cos_l,
+                    s->rope_sin_l, s->h[0], s->h[1],
                     s->out[0], s->out[1], s->q, s->attn, s->act, s->lm_h, s->res_h, s->feat, s->mid, s->mid2,
                     s->partial, s->counters, s->mu, s->x, s->cond, s->cond0, s->noise, s->latents, s->temb,
                     s->tmid, s->ttok, s->dtemb, s->dtmid, s->dttok, s->dtemb1, s->dtmid1, s->dttok1, s->dh,
@@ -458,6 +466,36 @@ GemvArgs plain_gemv(const __half* w, const __half* b, const float* x, int K, int
 }
 
 // ----------------------------------------------------------- enqueue ------
+// The base decoder's RoPE tables from the device's LongRoPE factors: rebuilt when
+// the factors changed since the stream last built them (same device pointers, so
+// captured graphs stay valid). The stream's queue is drained first.
+void sync_rope(vxc_stream* s) {
+    const vxc_device* dev = s->dev;
+    if (s->rope_epoch == dev->rope_epoch) return;
+    const vxc_model_desc& d = dev->desc;
+    const int hd = d.head_dim;
+    std::vector<float> c, sn;
+    ck(cudaStreamSynchronize(s->cs), "rope tables");
+    rope_table(hd, d.rope_theta, s->cap, c, sn, dev->rope_short.empty() ? nullptr : dev->rope_short.data());
+    ck(cudaMemcpy(s->rope_cos, c.data(), sizeof(float) * c.size(), cudaMemcpyHostToDevice), "rope");
+    ck(cudaMemcpy(s->rope_sin, sn.data(), sizeof(float) * sn.size(), cudaMemcpyHostToDevice), "rope");
+    if (!dev->rope_long.empty())
+        rope_table(hd, d.rope_theta, s->cap, c, sn, dev->rope_long.data());
+    ck(cudaMemcpy(s->rope_cos_l, c.data(), sizeof(float) * c.size(), cudaMemcpyHostToDevice), "rope");
+    ck(cudaMemcpy(s->rope_sin_l, sn.data(), sizeof(float) * sn.size(), cudaMemcpyHostToDevice), "rope");
+    s->rope_epoch = dev->rope_epoch;
+}
+
+// RoPE of a one-row base-decoder q/k/v GEMV: the position (device side) picks the
+// short- or long-factor row as make_rope_cache(pos, 1) does.
+void set_decode_rope(GemvArgs& a, const vxc_stream* s) {
+    a.rope_cos = s->rope_cos;
+    a.rope_sin = s->rope_sin;
+    a.rope_cos_long = s->rope_cos_l;
+    a.rope_sin_long = s->rope_sin_l;
+    a.rope_long_from = s->dev->desc.rope_original_max;
+}
+
 // Batch-1 decoder step over s->h[which] (the residual stream, already holding
 // the input embedding); writes the final-norm output to out (+ out2) and bumps
 // kv_len[which] on the device (unless advance is 0). ctl_override replaces the
@@ -487,8 +525,7 @@ void enqueue_decoder_step(vxc_stream* s, int which, float* out, float* out2, int
         qa.q_heads = hq;
         qa.kv_heads = hkv;
         qa.head_dim = hd;
-        qa.rope_cos = which == 0 ? s->rope_cos : nullptr;
-        qa.rope_sin = which == 0 ? s->rope_sin : nullptr;
+        if (which == 0) set_decode_rope(qa, s);
         qa.k_cache = s->kc[which] + l * plane;
         qa.v_cache = s->vc[which] + l * plane;
         qa.cap = s->cap;
@@ -1031,6 +1068,10 @@ void run_decoder_rows(vxc_stream* s, int which, int n, float* out_dev) {
     const int W = (hq + 2 * hkv) * hd;
     const int past = s->kv_len[which];
     const size_t plane = static_cast<size_t>(hkv) * s->cap * hd;
+    // make_rope_cache(past, n): every row takes the long-factor table when past + n > original_max
+    const bool long_rows = past + n > d.rope_original_max;
+    const float* rope_c = long_rows ? s->rope_cos_l : s->rope_cos;
+    const float* rope_s = long_rows ? s->rope_sin_l : s->rope_sin;
     for (size_t l = 0; l < layers.size(); ++l) {
         const LayerW& L = layers[l];
         for (int r0 = 0; r0 < n; r0 += kRowBlock) {
@@ -1046,8 +1087,8 @@ void run_decoder_rows(vxc_stream* s, int which, int n, float* out_dev) {
             qa.ctl = s->ctl;
             launch_tc_rows(maps[l][0], s->map_xr_n, qa, s->cs);
         }
-        launch_qkv_rows_post(s->pqkv, n, hq, hkv, hd, past, 1 << 30, which == 0 ? s->rope_cos : nullptr,
-                             which == 0 ? s->rope_sin : nullptr, s->kc[which] + l * plane, s->vc[which] + l * plane,
+        launch_qkv_rows_post(s->pqkv, n, hq, hkv, hd, past, 1 << 30, which == 0 ? rope_c : nullptr,
+                             which == 0 ? rope_s : nullptr, s->kc[which] + l * plane, s->vc[which] + l * plane,
                              s->cap, s->ctl, s->cs, false);
         launch_attn_rows_cache(s->pqkv, n, hq, hkv, hd, past, s->kc[which] + l * plane, s->vc[which] + l * plane,
                                s->cap, 1.0f / std::sqrt(static_cast<float>(hd)), s->pattn, s->cs, false);
@@ -1258,6 +1299,7 @@ void prefill_rows(vxc_stream* s, const int32_t* ids_in, const int32_t* is_audio,
     const vxc_device* dev = s->dev;
     const vxc_model_desc& d = dev->desc;
     require(ids_in != nullptr && L > 0, "the prefix must not be empty");
+    sync_rope(s);
     std::vector<int> audio_rows;
     for (int i = 0; i < L; ++i)
         if (is_audio && is_audio[i]) audio_rows.push_back(i);
@@ -1457,8 +1499,7 @@ void enqueue_group_decoder_step(vxc_group* g, int which) {
         qa.q_heads = hq;
         qa.kv_heads = hkv;
         qa.head_dim = hd;
-        qa.rope_cos = which == 0 ? s0->rope_cos : nullptr;  // the members share a capacity, so the same table
-        qa.rope_sin = which == 0 ? s0->rope_sin : nullptr;
+        if (which == 0) set_decode_rope(qa, s0);  // the members share a capacity and the device's factors
         qa.cap = s0->cap;
         qa.which = which;
         qa.skip_if_stopped = 1;
@@ -1822,6 +1863,23 @@ VXC_API int32_t vxc_load_weights(vxc_device* dev, int32_t component, const void*
     });
 }
 
+VXC_API int32_t vxc_set_rope_factors(vxc_device* dev, const float* short_factor, const float* long_factor,
+                                     int32_t n) {
+    return guard([&] {
+        require(dev != nullptr && short_factor != nullptr, "device and short_factor must not be null");
+        // make_rope_cache reads the first head_dim / 2 entries and rejects shorter tables
+        // (synthesizer.cpp:949-951)
+        const int half = dev->desc.head_dim / 2;
+        require(n >= half, "VoxCPM2 rope tables are missing or too short");
+        for (int j = 0; j < half; ++j)
+            require(short_factor[j] > 0.f && (!long_factor || long_factor[j] > 0.f), "rope factors must be positive");
+        dev->rope_short.assign(short_factor, short_factor + half);
+        if (long_factor) dev->rope_long.assign(long_factor, long_factor + half);
+        else dev->rope_long.clear();
+        ++dev->rope_epoch;
+    });
+}
+
 VXC_API int32_t vxc_stream_create(vxc_device* dev, int32_t kv_capacity, vxc_stream** out) {
     return guard([&] {
         require(dev != nullptr && out != nullptr, "device and out must not be null");
@@ -1849,12 +1907,12 @@ VXC_API int32_t vxc_stream_create(vxc_device* dev, int32_t kv_capacity, vxc_stre
             s->h[w] = dev_alloc<float>(H);
             s->out[w] = dev_alloc<float>(H);
         }
-        std::vector<float> c, sn;
-        rope_table(static_cast<int>(hd), d.rope_theta, kv_capacity, c, sn);
-        s->rope_cos = dev_alloc<float>(c.size());
-        s->rope_sin = dev_alloc<float>(sn.size());
-        ck(cudaMemcpy(s->rope_cos, c.data(), sizeof(float) * c.size(), cudaMemcpyHostToDevice), "rope");
-        ck(cudaMemcpy(s->rope_sin, sn.data(), sizeof(float) * sn.size(), cudaMemcpyHostToDevice), "rope");
+        const size_t rope_n = static_cast<size_t>(kv_capacity) * hd;
+        s->rope_cos = dev_alloc<float>(rope_n);
+        s->rope_sin = dev_alloc<float>(rope_n);
+        s->rope_cos_l = dev_alloc<float>(rope_n);
+        s->rope_sin_l = dev_alloc<float>(rope_n);
+        sync_rope(s.get());
         s->q = dev_alloc<float>(hq * hd);
         s->attn = dev_alloc<float>(hq * hd);
         s->act = dev_alloc<float>(F);
@@ -2018,6 +2076,7 @@ VXC_API int32_t vxc_decoder_step(vxc_stream* s, int32_t which, const float* embe
         require(n > 0, "invalid decoder attention mask shape");
         std::lock_guard<std::mutex> lk(s->call_mutex);
         DeviceGuard g(s->dev->device);
+        sync_rope(s);
         decoder_call(s, which, embed, n, out);
     });
 }
@@ -2631,7 +2690,7 @@ std::vector<std::function<void(bool)>> profile_launches(vxc_stream* s, int kerne
                 GemvArgs a;
                 a.mode = GEMV_QKV; a.w = BL.wqkv; a.x = s->out[0]; a.norm_g = BL.in_norm; a.eps = d.rms_eps;
                 a.K = H; a.rows = (hq + 2 * hkv) * hd / 2; a.y = s->q; a.q_heads = hq; a.kv_heads = hkv;
-                a.head_dim = hd; a.rope_cos = s->rope_cos; a.rope_sin = s->rope_sin;
+                a.head_dim = hd; set_decode_rope(a, s);
                 a.k_cache = s->kc[0] + l * plane; a.v_cache = s->vc[0] + l * plane; a.cap = s->cap; a.which = 0;
                 a.ctl = pctl;
                 bytes = 2.0 * (hq + 2 * hkv) * hd * H + 4.0 * H + 4.0 * hq * hd + 4.0 * 2 * hkv * hd;

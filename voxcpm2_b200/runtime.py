@@ -75,6 +75,7 @@ def _signatures():
         "vxc_device_create": ([i, C.POINTER(Desc), C.POINTER(vp)], i),
         "vxc_device_destroy": ([vp], None),
         "vxc_load_weights": ([vp, i, vp, C.c_size_t], i),
+        "vxc_set_rope_factors": ([vp, vp, vp, i], i),
         "vxc_stream_create": ([vp, i, C.POINTER(vp)], i),
         "vxc_stream_destroy": ([vp], None),
         "vxc_stream_reset": ([vp], i),
@@ -166,6 +167,14 @@ class Device:
         if blob.size != component_count(self.cfg, component):
             raise ValueError(f"component {component}: {blob.size} values, expected {component_count(self.cfg, component)}")
         _check(lib().vxc_load_weights(self._h, component, _p(blob), blob.size))
+
+    def set_rope_factors(self, short_factor, long_factor=None) -> None:
+        """The base decoder's LongRoPE factors (model.json setting.rope.short_factor /
+        long_factor, at least head_dim / 2 values each; long optional). Streams pick them up at
+        their next prefill or decoder step."""
+        sf = np.ascontiguousarray(short_factor, dtype=np.float32)
+        lf = None if long_factor is None else np.ascontiguousarray(long_factor, dtype=np.float32)
+        _check(lib().vxc_set_rope_factors(self._h, _p(sf), _p(lf) if lf is not None else None, sf.size))
 
     def close(self) -> None:
         if getattr(self, "_h", None):
