@@ -263,6 +263,93 @@ def job_rate(world: int, streams_per_gpu: int, steps: int, seconds: float) -> fl
     return world * streams_per_gpu * steps / seconds
 
 
+# ----------------------------------------------------------- SDPA op ---
+def sdpa_op(rt, peak, rank, world):
+    """The VoxCPM2SDPA op alone, as its decode-shape test runs it: q [16][1][64], a
+    cached K/V of 511 rows per KV head plus the new row (GQA 8:1, scale 1/8), through
+    vxc_sdpa on device pointers. Each timed call reads its own input set; the sets
+    together exceed the L2, so every call reads K/V from HBM. Also the same call
+    with the layer's cache outputs (out_k / out_v, the concatenated caches), and the
+    oracle (the reference's CPU forward restated) on the same shapes."""
+    import torch
+    heads, groups, d, past, cur = 16, 2, 64, 511, 1
+    sets = 320  # 320 x ~0.53 MB > 126 MB L2
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=dev).manual_seed(11)
+    q = torch.randn(sets, heads, 1, d, device=dev, generator=g)
+    k = torch.randn(sets, groups, cur, d, device=dev, generator=g)
+    v = torch.randn(sets, groups, cur, d, device=dev, generator=g)
+    pk = torch.randn(sets, groups, past, d, device=dev, generator=g)
+    pv = torch.randn(sets, groups, past, d, device=dev, generator=g)
+    out = torch.empty(sets, heads, 1, d, device=dev)
+    ok = torch.empty(sets, groups, past + cur, d, device=dev)
+    ov = torch.empty_like(ok)
+    st = torch.cuda.current_stream().cuda_stream
+
+    def call(i, cache):
+        rt.sdpa_device(q[i].data_ptr(), heads, 1, d, k[i].data_ptr(), v[i].data_ptr(), groups, cur, d, 0, 0,
+                       pk[i].data_ptr(), pv[i].data_ptr(), past, 0.125, out[i].data_ptr(),
+                       ok[i].data_ptr() if cache else 0, ov[i].data_ptr() if cache else 0, st)
+
+    def timed(cache, graph):
+        """us per call: the calls replayed from one captured CUDA graph (device time),
+        or issued one by one from this Python loop (host-driven)."""
+        for i in range(8):
+            call(i, cache)
+        torch.cuda.synchronize()
+        if graph:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for i in range(sets):
+                    rt.sdpa_device(q[i].data_ptr(), heads, 1, d, k[i].data_ptr(), v[i].data_ptr(), groups, cur, d,
+                                   0, 0, pk[i].data_ptr(), pv[i].data_ptr(), past, 0.125, out[i].data_ptr(),
+                                   ok[i].data_ptr() if cache else 0, ov[i].data_ptr() if cache else 0,
+                                   torch.cuda.current_stream().cuda_stream)
+            g.replay()
+            torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        if graph:
+            g.replay()
+        else:
+            for i in range(sets):
+                call(i, cache)
+        e1.record()
+        e1.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / sets
+
+    us = timed(False, True)
+    us_cache = timed(True, True)
+    us_eager = timed(False, False)
+    nbytes = 4.0 * (heads * d + 2 * groups * (past + cur) * d + heads * d)
+    nbytes_cache = nbytes + 4.0 * 2 * groups * (past + cur) * d  # + the concatenated caches written
+    res = {"shape": "q [16][1][64], K/V [2][511 + 1][64], GQA 8:1, scale 1/8 (fp32)", "us": round(us, 2),
+           "bytes": nbytes, "GB/s": round(nbytes / us / 1e3, 1), "frac": nbytes / us / 1e3 / peak,
+           "us_with_cache_outputs": round(us_cache, 2),
+           "GB/s_with_cache_outputs": round(nbytes_cache / us_cache / 1e3, 1),
+           "us_host_loop": round(us_eager, 2),
+           "timing": f"{sets} calls replayed from one CUDA graph (device time per call); us_host_loop: the same "
+                     "calls issued one by one from Python (ctypes), which leaves the GPU idle between calls",
+           "inputs": f"{sets} distinct input sets cycled (> L2): K/V read from HBM each call"}
+    if rank == 0 and world == 1:
+        import oracle
+        rng = np.random.default_rng(11)
+        hq = rng.standard_normal((heads, 1, d), dtype=np.float32)
+        hk = rng.standard_normal((groups, cur, d), dtype=np.float32)
+        hv = rng.standard_normal((groups, cur, d), dtype=np.float32)
+        hpk = rng.standard_normal((groups, past, d), dtype=np.float32)
+        hpv = rng.standard_normal((groups, past, d), dtype=np.float32)
+        oracle.set_threads(os.cpu_count() or 1)
+        oracle.sdpa(hq, hk, hv, past_k=hpk, past_v=hpv, scale=0.125, want_cache=True)
+        t0 = time.perf_counter()
+        n = 200
+        for _ in range(n):
+            oracle.sdpa(hq, hk, hv, past_k=hpk, past_v=hpv, scale=0.125, want_cache=True)
+        res["cpu_us_with_cache_outputs"] = round((time.perf_counter() - t0) / n * 1e6, 1)
+        res["cpu"] = f"oracle (the layer's CPU forward restated), {os.cpu_count() or 1} threads, {n} calls"
+    return res
+
+
 # --------------------------------------------------------------- GPU arm ---
 def group_rate(rt, synthetic, dev, cfg, groups, members, K, W, min_patches, rank, barrier, max_over_ranks, world,
                peak):
@@ -559,6 +646,9 @@ def run_ours(args):
         group = group_rate(rt, synthetic, dev, cfg, args.groups, args.group_members, K, W, min_patches, rank,
                            barrier, max_over_ranks, world, peak)
 
+    # ---- config 1: the VoxCPM2SDPA op alone
+    sdpa = sdpa_op(rt, peak, rank, world)
+
     # ---- CPU baseline: the oracle port on this host, bounded sample (rank 0, N = 1)
     cpu = None
     if rank == 0 and world == 1:
@@ -589,7 +679,7 @@ def run_ours(args):
             "e2e_sync": {"value": e2e_sync_value, "unit": "patches/s", "h2d_bytes_per_step": h2d,
                          "d2h_bytes_per_step": d2h, "api": "vxc_patch_step (synchronous)"},
             "gpu_launches": graph_kernels * S * K, "roofline": roofline, "hbm_job": hbm_job, "kernels": kernels,
-            "decode_step": decode_step,
+            "decode_step": decode_step, "sdpa_op": sdpa,
             "cpu_baseline": cpu, "clocks": clk, "group": group,
         }
         print(json.dumps(line), flush=True)

@@ -789,18 +789,20 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    // combine the active splits of this KV head, staged with 8 loads in flight per thread
+    // combine the active splits of this KV head, staged with up to 72 loads in flight per
+    // thread: one L2 round trip for up to 72 x 128 floats (17 splits of 8 heads)
     const float* pk = a.partial + static_cast<size_t>(kvh) * a.splits * G * (D + 2);
     const int total = active * G * (D + 2);
-    for (int base = tid; base < total; base += kAttnThreads * 8) {
-        float v[8];
+    constexpr int kB = 72;
+    for (int base = tid; base < total; base += kAttnThreads * kB) {
+        float v[kB];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < kB; ++j) {
             const int i = base + j * kAttnThreads;
             v[j] = i < total ? __ldcg(pk + i) : 0.f;
         }
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < kB; ++j) {
             const int i = base + j * kAttnThreads;
             if (i < total) ps[i] = v[j];
         }

@@ -1,7 +1,7 @@
 // Single-query SDPA that never allocates device memory.
 //
-// vxc_sdpa's split-K decode path keeps its split partials in a scratch buffer it
-// allocates on first use. Some callers cannot let a library allocate: plugin
+// vxc_sdpa's split-K decode path (one query row over more than 512 keys) keeps its
+// split partials in a scratch buffer it allocates on first use. Some callers cannot let a library allocate: plugin
 // hosts that hand a layer pre-allocated tensors and a stream and forbid
 // allocation inside the enqueue call (cudaMalloc synchronises the device and
 // can fail against a budget the host manages), or real-time audio threads that

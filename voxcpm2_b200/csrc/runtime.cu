@@ -2305,6 +2305,9 @@ VXC_API int32_t vxc_generate(vxc_stream* s, const int32_t* text_ids, int32_t n_t
     });
 }
 
+// One-query SDPA calls of up to this many keys take the cluster-combined decode kernel.
+constexpr int kClusterDecodeKeys = 512;
+
 VXC_API int32_t vxc_sdpa(const float* q, int32_t heads, int32_t src, int32_t d, const float* k, const float* v,
                          int32_t groups, int32_t cur, int32_t dv, const float* mask, int32_t mask_c,
                          const float* past_k, const float* past_v, int32_t past, float scale, float* out,
@@ -2330,8 +2333,28 @@ VXC_API int32_t vxc_sdpa(const float* q, int32_t heads, int32_t src, int32_t d, 
                 ready.push_back(dev_id);
             }
         }
-        if (src == 1 && d == 64 && dv == 64 && G <= 16 && mask_c <= 1 && groups <= 64) {
-            // split-K flash decode over [past | cur] (fp32 rows). Its split partials
+        if (src == 1 && d == 64 && dv == 64 && G <= 16 && mask_c <= 1 && past + cur <= kClusterDecodeKeys) {
+            // up to 512 keys: one 8-CTA cluster per KV head (at most 2 key tiles per CTA),
+            // the splits combined through distributed shared memory; no scratch
+            AttnArgs aa;
+            aa.q = q;
+            aa.k0 = past > 0 ? past_k : k;
+            aa.v0 = past > 0 ? past_v : v;
+            aa.len0 = past > 0 ? past : cur;
+            aa.stride0 = past > 0 ? past : cur;
+            aa.k1 = past > 0 ? k : nullptr;
+            aa.v1 = past > 0 ? v : nullptr;
+            aa.len1 = past > 0 ? cur : 0;
+            aa.stride1 = cur;
+            aa.mask = mask;
+            aa.q_heads = heads;
+            aa.kv_heads = groups;
+            aa.head_dim = d;
+            aa.scale = rs;
+            aa.out = out;
+            launch_attn_decode_cluster(aa, cs, false);
+        } else if (src == 1 && d == 64 && dv == 64 && G <= 16 && mask_c <= 1 && groups <= 64) {
+            // longer: split-K flash decode over [past | cur] (fp32 rows). Its split partials
             // live in a scratch buffer kept per (device, CUDA stream): calls on one
             // stream run in order, calls on different streams never share it.
             int dev_id = 0;
