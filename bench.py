@@ -257,6 +257,13 @@ def stream_seeds(rank: int, streams_per_gpu: int):
     return [(1000 + rank * streams_per_gpu + i, rank * streams_per_gpu + i) for i in range(streams_per_gpu)]
 
 
+def gpu_bandwidth(job_value: float, world: int, bytes_per_patch: float, peak: float):
+    """(GB/s, fraction of the per-GPU peak) of one GPU: a whole-job patch rate over
+    'world' GPUs times the algorithmic bytes of a patch."""
+    gbs = job_value / world * bytes_per_patch / 1e9
+    return gbs, gbs / peak
+
+
 def job_rate(world: int, streams_per_gpu: int, steps: int, seconds: float) -> float:
     """Whole-job patches/s: every rank ran `steps` patches on each of its streams
     within `seconds` (the slowest rank's time)."""
@@ -410,10 +417,10 @@ def group_rate(rt, synthetic, dev, cfg, groups, members, K, W, min_patches, rank
     bpp = patch_bytes(cfg, TEXT_TOKENS + 1 + W + K / 2) - shared * (members - 1) / members
     return {"groups_per_gpu": groups, "members": members, "streams_per_gpu": groups * members,
             "value": value, "unit": "patches/s", "ms_per_step": ms / K,
-            "hbm_job": {"bytes_per_patch": bpp, "achieved": value * bpp / 1e9, "peak": peak, "unit": "GB/s",
-                        "frac": value * bpp / 1e9 / peak,
-                        "note": "algorithmic bytes per member patch (estimator and decoder weights shared by "
-                                "the group)"},
+            "hbm_job": {"bytes_per_patch": bpp, "achieved": gpu_bandwidth(value, world, bpp, peak)[0], "peak": peak,
+                        "unit": "GB/s", "frac": gpu_bandwidth(value, world, bpp, peak)[1],
+                        "note": "per GPU: algorithmic bytes per member patch (estimator and decoder weights shared "
+                                "by the group) x patches/s per GPU"},
             "group_patch_ms": float(np.median(lat)), "kernels_per_group_patch": kernels,
             "gpu_launches": groups * K * kernels,
             "note": "each group steps its members as one CUDA graph: the 9 estimator evaluations of all "
@@ -489,14 +496,15 @@ def run_ours(args):
         kname = "tc_linear_kernel gate/up (DiT, tcgen05 + TMA, 2x11 tokens, SiLU*up epilogue)"
         traffic = profiled_value("tc_linear_gateup_dit", "dram_bytes_per_launch")
     achieved = prof_bytes / (prof_ms / 1e3) / 1e9
-    # whole job: algorithmic bytes of all patches / the timed region (all streams together)
+    # per GPU: algorithmic bytes of all its streams' patches / the timed region
     bpp = patch_bytes(cfg, TEXT_TOKENS + 1 + W + K / 2)
-    hbm_job = {"bytes_per_patch": bpp, "achieved": value * bpp / 1e9, "peak": peak, "unit": "GB/s",
-               "frac": value * bpp / 1e9 / peak, "note": "patches/s x algorithmic bytes per patch, all streams"}
+    gbs, frac = gpu_bandwidth(value, world, bpp, peak)
+    hbm_job = {"bytes_per_patch": bpp, "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": frac,
+               "note": "per GPU: patches/s per GPU x algorithmic bytes per patch, all its streams"}
     dram_pp = profiled_value("patch_loop_16streams_dram_range", "dram_bytes_per_patch")
     if dram_pp:  # measured DRAM bytes: concurrent streams share weights through the L2
-        hbm_job.update({"dram_bytes_per_patch": dram_pp, "achieved_dram": value * dram_pp / 1e9,
-                        "frac_dram": value * dram_pp / 1e9 / peak,
+        gbs_d, frac_d = gpu_bandwidth(value, world, dram_pp, peak)
+        hbm_job.update({"dram_bytes_per_patch": dram_pp, "achieved_dram": gbs_d, "frac_dram": frac_d,
                         "dram_source": "profiles/patch_loop_16streams_dram_range.md (ncu app-range capture of "
                                        "16 streams; the L2-shared fraction varies with the streams' timing)"})
     roofline = {"kernel": kname, "bound": "hbm",
@@ -637,8 +645,8 @@ def run_ours(args):
     e2e_sync_value, per_call = e2e_run(False)
     e2e_value, _ = e2e_run(True)
     calls = np.concatenate([np.array(c) for c in per_call]) * 1e3
-    h2d = S * L * 4                   # each stream's noise patch
-    d2h = S * (L * 4 + 40)            # each stream's latent patch + its 40-byte control block
+    h2d = world * S * L * 4           # every stream's noise patch (whole job)
+    d2h = world * S * (L * 4 + 40)    # every stream's latent patch + its 40-byte control block
 
     # ---- stream groups: the same workload with each group's estimator passes batched
     group = None

@@ -57,3 +57,7 @@ def test_single_rank_helpers():
     assert bench.stream_seeds(0, 2) == [(1000, 0), (1001, 1)]
     assert bench.stream_seeds(3, 2) == [(1006, 6), (1007, 7)]
     assert bench.job_rate(8, 16, 20, 2.0) == 8 * 16 * 20 / 2.0
+    # bandwidth is per GPU: the whole-job rate of 2 GPUs counts each GPU's share once
+    gbs, frac = bench.gpu_bandwidth(2400.0, 2, 4.6e9, 6546.2)
+    assert abs(gbs - 1200.0 * 4.6) < 1e-6 and abs(frac - 1200.0 * 4.6 / 6546.2) < 1e-9
+    assert bench.gpu_bandwidth(1200.0, 1, 4.6e9, 6546.2) == (gbs, frac)
