@@ -274,6 +274,7 @@ struct vxc_device {
     // the base decoder's LongRoPE factors (vxc_set_rope_factors); empty = all ones / none
     std::vector<float> rope_short, rope_long;
     uint64_t rope_epoch = 0;
+    std::mutex rope_mu;  // guards the three above (set from any thread, read by stream calls)
     std::vector<LayerW> base, res, dit;
     const __half *base_norm = nullptr, *res_norm = nullptr, *dit_norm = nullptr;
     float *dit_rope_cos = nullptr, *dit_rope_sin = nullptr;  // positions 0..seq-1
@@ -470,20 +471,27 @@ GemvArgs plain_gemv(const __half* w, const __half* b, const float* x, int K, int
 // the factors changed since the stream last built them (same device pointers, so
 // captured graphs stay valid). The stream's queue is drained first.
 void sync_rope(vxc_stream* s) {
-    const vxc_device* dev = s->dev;
-    if (s->rope_epoch == dev->rope_epoch) return;
+    vxc_device* dev = s->dev;
+    std::vector<float> short_f, long_f;
+    uint64_t epoch = 0;
+    {
+        std::lock_guard<std::mutex> lk(dev->rope_mu);
+        if (s->rope_epoch == dev->rope_epoch) return;
+        short_f = dev->rope_short;
+        long_f = dev->rope_long;
+        epoch = dev->rope_epoch;
+    }
     const vxc_model_desc& d = dev->desc;
     const int hd = d.head_dim;
     std::vector<float> c, sn;
     ck(cudaStreamSynchronize(s->cs), "rope tables");
-    rope_table(hd, d.rope_theta, s->cap, c, sn, dev->rope_short.empty() ? nullptr : dev->rope_short.data());
+    rope_table(hd, d.rope_theta, s->cap, c, sn, short_f.empty() ? nullptr : short_f.data());
     ck(cudaMemcpy(s->rope_cos, c.data(), sizeof(float) * c.size(), cudaMemcpyHostToDevice), "rope");
     ck(cudaMemcpy(s->rope_sin, sn.data(), sizeof(float) * sn.size(), cudaMemcpyHostToDevice), "rope");
-    if (!dev->rope_long.empty())
-        rope_table(hd, d.rope_theta, s->cap, c, sn, dev->rope_long.data());
+    if (!long_f.empty()) rope_table(hd, d.rope_theta, s->cap, c, sn, long_f.data());
     ck(cudaMemcpy(s->rope_cos_l, c.data(), sizeof(float) * c.size(), cudaMemcpyHostToDevice), "rope");
     ck(cudaMemcpy(s->rope_sin_l, sn.data(), sizeof(float) * sn.size(), cudaMemcpyHostToDevice), "rope");
-    s->rope_epoch = dev->rope_epoch;
+    s->rope_epoch = epoch;
 }
 
 // RoPE of a one-row base-decoder q/k/v GEMV: the position (device side) picks the
@@ -1873,6 +1881,7 @@ VXC_API int32_t vxc_set_rope_factors(vxc_device* dev, const float* short_factor,
         require(n >= half, "VoxCPM2 rope tables are missing or too short");
         for (int j = 0; j < half; ++j)
             require(short_factor[j] > 0.f && (!long_factor || long_factor[j] > 0.f), "rope factors must be positive");
+        std::lock_guard<std::mutex> lk(dev->rope_mu);
         dev->rope_short.assign(short_factor, short_factor + half);
         if (long_factor) dev->rope_long.assign(long_factor, long_factor + half);
         else dev->rope_long.clear();
