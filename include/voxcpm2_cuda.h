@@ -139,7 +139,7 @@ VXC_API int32_t vxc_load_weights(vxc_device* dev, int32_t component, const void*
 
 /* The base decoder's LongRoPE factors, n >= head_dim / 2 values each (the first
  * head_dim / 2 are used; shorter tables are rejected, synthesizer.cpp:949-951): model.json's
- * setting.rope.short_factor and long_factor (src/model_manifest.cpp:92-106, kept by
+ * setting.rope.short_factor and long_factor (src/model_manifest.cpp:92-109, kept by
  * load_manifest, synthesizer.cpp:825-830). Until this is called every factor is 1.
  * As make_rope_cache (synthesizer.cpp:940-974), a call covering positions
  * [start, start + n) rotates with long_factor when start + n > rope_original_max and

@@ -390,7 +390,7 @@ struct orc_model {
     std::vector<std::vector<float>> cache_k[2], cache_v[2];
     int tokens[2] = {0, 0};
     // LongRoPE factors of the base decoder (setting.rope.short_factor / long_factor,
-    // src/model_manifest.cpp:92-106): all ones until orc_set_rope_factors; an empty
+    // src/model_manifest.cpp:92-109): all ones until orc_set_rope_factors; an empty
     // long table means the short one is used at every position
     std::vector<float> short_factor, long_factor;
     std::vector<float> dit_factor;  // the estimator's rotary table: all ones
