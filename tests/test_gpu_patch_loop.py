@@ -72,6 +72,26 @@ def test_generate_tiny_full_loop(rt, tiny):
     s.close()
 
 
+def test_generate_with_rope_factors(rt):
+    """LongRoPE short factors (model.json setting.rope) through the whole captured
+    patch loop: prefill rows and every decode step rotate as the oracle's
+    make_rope_cache restatement does."""
+    cfg = TINY
+    blobs = synthetic.model_blobs(cfg, 0)
+    dev = rt.Device(cfg, 0, blobs)
+    orc = oracle.Oracle(cfg, blobs)
+    short = np.random.default_rng(9).uniform(0.5, 3.0, cfg.head_dim // 2).astype(np.float32)
+    dev.set_rope_factors(short)
+    orc.set_rope_factors(short)
+    s = rt.Stream(dev, kv_capacity=128)
+    ids = synthetic.token_ids(cfg, 12, seed=2)
+    want = orc.generate(ids, min_patches=6, timesteps=10, cfg_value=2.0, max_patches_override=24, seed=1)
+    got = s.generate(ids, min_patches=6, timesteps=10, cfg_value=2.0, max_patches_override=24, seed=1)
+    compare_runs(got, want, "tiny with rope factors", 6)
+    s.close()
+    dev.close()
+
+
 def test_generate_bench_first_patches(rt, bench):
     """The benchmark model: 64 text tokens, the first 10 patches of the loop."""
     cfg, blobs, dev, orc = bench
