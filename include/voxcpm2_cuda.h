@@ -145,8 +145,8 @@ VXC_API int32_t vxc_load_weights(vxc_device* dev, int32_t component, const void*
  * [start, start + n) rotates with long_factor when start + n > rope_original_max and
  * long_factor is set, else with short_factor; long_factor may be NULL. The patch
  * loop stays below rope_original_max (synthesizer.cpp:542-544), so there only the
- * short factors apply. Streams pick the factors up at their next prefill or
- * decoder step; the call may come from any thread. Every factor must be positive. */
+ * short factors apply. Streams pick the factors up at their next prefill, decoder
+ * step or patch step; the call may come from any thread. Every factor must be positive. */
 VXC_API int32_t vxc_set_rope_factors(vxc_device* dev, const float* short_factor, const float* long_factor,
                                      int32_t n);
 

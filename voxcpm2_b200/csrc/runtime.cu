@@ -1218,6 +1218,7 @@ void check_patch_preconditions(vxc_stream* s, int T) {
         throw std::runtime_error("VoxCPM2 KV cache reached the exported RoPE range");
     if (s->kv_len[0] + 1 > s->cap || s->kv_len[1] + 1 > s->cap || s->patches >= s->cap)
         throw std::invalid_argument("KV cache capacity exceeded: create the stream with a larger kv_capacity");
+    sync_rope(s);  // factors set since the prefill apply from this patch on (every group member alike)
 }
 
 void patch_step(vxc_stream* s, const float* noise, int min_patches, float cfg, int T, float* out_latent,

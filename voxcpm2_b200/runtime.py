@@ -171,7 +171,7 @@ class Device:
     def set_rope_factors(self, short_factor, long_factor=None) -> None:
         """The base decoder's LongRoPE factors (model.json setting.rope.short_factor /
         long_factor, at least head_dim / 2 values each; long optional). Streams pick them up at
-        their next prefill or decoder step."""
+        their next prefill, decoder step or patch step."""
         sf = np.ascontiguousarray(short_factor, dtype=np.float32)
         lf = None if long_factor is None else np.ascontiguousarray(long_factor, dtype=np.float32)
         _check(lib().vxc_set_rope_factors(self._h, _p(sf), _p(lf) if lf is not None else None, sf.size))
