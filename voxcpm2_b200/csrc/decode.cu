@@ -617,7 +617,8 @@ void dispatch_gemv_batch(const GemvArgs& a, const GemvBatch& b, cudaStream_t s, 
 }
 
 // ------------------------------------------------------------ attention ---
-constexpr int kAttnThreads = 128;
+constexpr int kAttnThreads = 128;       // the cluster-combined decode (4 warps per CTA)
+constexpr int kAttnSplitThreads = 256;  // the split-K decode: more warps per scheduler to hide latency
 constexpr int kMaxGroup = 16;
 
 constexpr int kMinKeysPerSplit = 16;
@@ -668,13 +669,14 @@ struct AttnSmem {
 // Keys [t0, t0 + n) of KV head kvh against the group's G query heads: tiles of
 // kKeyTile rows staged by one batch of loads, online softmax per head. On
 // return S.m_s / S.l_s hold the running max and sum, acc[j] the P.V partial of
-// head g_lo + j at column e = tid % 64 (heads split between the two halves of
+// head g_lo + j at column e = tid % 64 (heads split over the NT / 64 thread groups of
 // the block).
-template <typename KV, int D>
+template <typename KV, int D, int NT>
 __device__ __forceinline__ void attend_keys(const AttnArgs& a, AttnSmem& S, int kvh, int G, int t0, int n, int len0,
                                             float* acc) {
+    constexpr int kGroups = NT / D;  // thread groups the query heads are split over
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    for (int i = tid; i < G * D; i += kAttnThreads) S.qs[i / D][i % D] = a.q[kvh * G * D + i] * a.scale;
+    for (int i = tid; i < G * D; i += NT) S.qs[i / D][i % D] = a.q[kvh * G * D + i] * a.scale;
     if (tid < G) {
         S.m_s[tid] = -1e30f;
         S.l_s[tid] = 0.f;
@@ -684,14 +686,14 @@ __device__ __forceinline__ void attend_keys(const AttnArgs& a, AttnSmem& S, int 
     const KV* k1 = a.k1 ? static_cast<const KV*>(a.k1) + static_cast<size_t>(kvh) * a.stride1 * D : nullptr;
     const KV* v1 = a.v1 ? static_cast<const KV*>(a.v1) + static_cast<size_t>(kvh) * a.stride1 * D : nullptr;
     const int e = tid & (D - 1), gh = tid / D;
-    const int hg = (G + 1) / 2, g_lo = gh * hg, g_hi = min(G, g_lo + hg);
+    const int hg = (G + kGroups - 1) / kGroups, g_lo = gh * hg, g_hi = min(G, g_lo + hg);
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = 0.f;
     for (int tb = 0; tb < n; tb += kKeyTile) {
         const int nt = min(kKeyTile, n - tb);
         __syncthreads();  // previous tile fully consumed (and q / stats initialised)
 #pragma unroll 4
-        for (int i = tid; i < nt * (D / 4); i += kAttnThreads) {
+        for (int i = tid; i < nt * (D / 4); i += NT) {
             const int r = i / (D / 4), c = (i % (D / 4)) * 4;
             const int row = t0 + tb + r;
             const KV* kp = row < len0 ? k0 + static_cast<size_t>(row) * D : k1 + static_cast<size_t>(row - len0) * D;
@@ -706,7 +708,7 @@ __device__ __forceinline__ void attend_keys(const AttnArgs& a, AttnSmem& S, int 
             }
         }
         __syncthreads();
-        for (int i = tid; i < G * nt; i += kAttnThreads) {
+        for (int i = tid; i < G * nt; i += NT) {
             const int g = i / nt, t = i - g * nt;
             float s = 0.f;
 #pragma unroll 16
@@ -714,7 +716,7 @@ __device__ __forceinline__ void attend_keys(const AttnArgs& a, AttnSmem& S, int 
             S.sc[g][t] = s + (a.mask ? a.mask[t0 + tb + t] : 0.f);
         }
         __syncthreads();
-        for (int g = warp; g < G; g += kAttnThreads / kWarp) {
+        for (int g = warp; g < G; g += NT / kWarp) {
             const float x = lane < nt ? S.sc[g][lane] : -1e30f;
             const float m_old = S.m_s[g];
             const float m_new = fmaxf(m_old, warp_max(x));
@@ -742,7 +744,8 @@ __device__ __forceinline__ void attend_keys(const AttnArgs& a, AttnSmem& S, int 
 }
 
 template <typename KV, int D>
-__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(kAttnSplitThreads) attn_decode_kernel(const AttnArgs a) {
+    constexpr int NT = kAttnSplitThreads;
     static_assert(D == 64, "head_dim 64");
     __shared__ AttnSmem S;
     __shared__ int s_last;
@@ -766,9 +769,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
     const int t0 = split * chunk;
     const int n = max(0, min(T, t0 + chunk) - t0);
     const int e = tid & (D - 1), gh = tid / D;
-    const int hg = (G + 1) / 2, g_lo = gh * hg, g_hi = min(G, g_lo + hg);
+    const int hg = (G + NT / D - 1) / (NT / D), g_lo = gh * hg, g_hi = min(G, g_lo + hg);
     float acc[8];
-    attend_keys<KV, D>(a, S, kvh, G, t0, n, len0, acc);
+    attend_keys<KV, D, NT>(a, S, kvh, G, t0, n, len0, acc);
     float* m_s = S.m_s;
     float* l_s = S.l_s;
     __syncthreads();
@@ -794,21 +797,21 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
     const float* pk = a.partial + static_cast<size_t>(kvh) * a.splits * G * (D + 2);
     const int total = active * G * (D + 2);
     constexpr int kB = 72;
-    for (int base = tid; base < total; base += kAttnThreads * kB) {
+    for (int base = tid; base < total; base += NT * kB) {
         float v[kB];
 #pragma unroll
         for (int j = 0; j < kB; ++j) {
-            const int i = base + j * kAttnThreads;
+            const int i = base + j * NT;
             v[j] = i < total ? __ldcg(pk + i) : 0.f;
         }
 #pragma unroll
         for (int j = 0; j < kB; ++j) {
-            const int i = base + j * kAttnThreads;
+            const int i = base + j * NT;
             if (i < total) ps[i] = v[j];
         }
     }
     __syncthreads();
-    for (int it = tid; it < G * D; it += kAttnThreads) {
+    for (int it = tid; it < G * D; it += NT) {
         const int g = it / D, c = it - g * D;
         float M = -1e30f;
         for (int sp = 0; sp < active; ++sp) M = fmaxf(M, ps[(sp * G + g) * (D + 2) + D]);
@@ -967,7 +970,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_cluster_kernel(const
     const int e = tid & (D - 1), gh = tid / D;
     const int hg = (G + 1) / 2, g_lo = gh * hg, g_hi = min(G, g_lo + hg);
     float acc[8];
-    attend_keys<KV, D>(a, S, kvh, G, t0, n, len0, acc);
+    attend_keys<KV, D, kAttnThreads>(a, S, kvh, G, t0, n, len0, acc);
     __syncthreads();
 #pragma unroll
     for (int j = 0; j < 8; ++j)
@@ -1047,7 +1050,7 @@ void launch_attn_decode(const AttnArgs& a, bool fp16_kv, cudaStream_t s, bool pd
     const size_t smem = static_cast<size_t>(a.splits) * G * (64 + 2) * sizeof(float);
     if (smem > 200 * 1024) throw std::invalid_argument("attention: sequence too long for one split");
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = make_cfg(dim3(a.splits, a.kv_heads), dim3(kAttnThreads), smem, s, pdl, attr);
+    cudaLaunchConfig_t cfg = make_cfg(dim3(a.splits, a.kv_heads), dim3(kAttnSplitThreads), smem, s, pdl, attr);
     if (fp16_kv) check_launch(cudaLaunchKernelEx(&cfg, attn_decode_kernel<__half, 64>, a));
     else check_launch(cudaLaunchKernelEx(&cfg, attn_decode_kernel<float, 64>, a));
 }
