@@ -46,18 +46,27 @@ def parse():
     p.add_argument("--group-members", type=int, default=4, help="streams per group (1..4)")
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--cpu-sample-patches", type=int, default=6)
-    p.add_argument("--range", choices=["patches", "profile", "group"], default=None,
-                   help="run one cudaProfilerStart/Stop range for an ncu app-range capture and exit: 'patches' = "
-                        "6 patches of every stream, 'profile' = the concurrent gate/up linear profile call "
-                        "(graph builds and warm-up replays included); 'group' = 3 patches of one stream group "
-                        "(--group-members streams), no profiler range")
+    p.add_argument("--range", choices=["stream", "group"], default=None,
+                   help="run a few patches and exit, for an ncu launch list (one metric, one pass): 'stream' = 3 "
+                        "patches of one lone stream, 'group' = 3 patches of one stream group (--group-members)")
     return p.parse_args()
+
+
+UTTERANCE_MID = 51  # the middle patch of the shortest utterance min_patches 100 allows (102 patches)
+
+
+def window(steps: int, warmup: int) -> int:
+    """Untimed patches before the K timed ones (warm-up included): the timed window
+    is centred on the middle of a 102-patch utterance, so its KV lengths average
+    those of the whole utterance instead of its short start."""
+    return max(warmup, UTTERANCE_MID - steps // 2)
 
 
 def workload(streams_per_gpu: int, steps: int, warmup: int):
     # min_patches stays at 100 unless a longer run needs it raised so the stop
     # head cannot end a stream inside the measured steps
-    min_patches = max(MIN_PATCHES, steps + warmup + 1)
+    first = window(steps, warmup)
+    min_patches = max(MIN_PATCHES, first + steps + 1)
     return {
         "workload": "full patch loop: base decode (24 layers) + residual decode (8) + 9 DiT evals (12 layers, "
                     "CFG 2x11 tokens) + dit_proj/stop/feat_encoder/fsq/fusion per patch; hidden 1024, 16/2 heads x 64, "
@@ -65,19 +74,17 @@ def workload(streams_per_gpu: int, steps: int, warmup: int):
         "min_patches": min_patches,
         "streams_per_gpu": streams_per_gpu,
         "batch_per_stream": 1,
+        "timed_patches": [first, first + steps - 1],
+        "kv_rows_timed": [TEXT_TOKENS + 1 + first, TEXT_TOKENS + 1 + first + steps - 1],
         "l2": "no flush: each patch streams ~4.7 GB of weights, far above the 126 MB L2",
     }, min_patches
 
 
-def profiled_value(name: str, key: str):
-    """A figure ('key: value' line) from the committed ncu summary profiles/<name>.md, or None."""
-    f = ROOT / "profiles" / f"{name}.md"
-    if not f.exists():
-        return None
-    for line in f.read_text().splitlines():
-        if line.startswith(key + ":"):
-            return float(line.split(":", 1)[1])
-    return None
+# DRAM bytes (ncu dram__bytes_read.sum + dram__bytes_write.sum) of one launch of the
+# dominant kernel, the DiT gate/up tcgen05 linear, from a capture of that kernel on
+# its own (the command is in profiles/tc_linear_gateup_dit.md); the algorithmic bytes
+# of the launch are 17,268,736.
+GATEUP_DRAM_BYTES_PER_LAUNCH = 16944896.0
 
 
 def dit_patch_bytes(cfg) -> float:
@@ -114,7 +121,10 @@ def patch_bytes(cfg, kv_tokens: float) -> float:
 
 # --------------------------------------------------------------- clocks ---
 class ClockSampler:
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+    """nvidia-smi sampling of one GPU's clocks every 200 ms, started once before any
+    timed work (its start-up never overlaps a timed region of this or another rank);
+    summary(t0, t1) keeps the samples taken within a host-time window."""
+    FIELDS = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
@@ -123,33 +133,49 @@ class ClockSampler:
         self.proc = None
         self.path = Path(f"/tmp/vxc_clocks_{os.getpid()}.csv")
 
-    def __enter__(self):
+    def start(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
-        time.sleep(0.3)
         return self
 
-    def __exit__(self, *exc):
+    def stop(self):
         if self.proc:
             self.proc.terminate()
             self.proc.wait(timeout=10)
+            self.proc = None
 
-    def summary(self):
+    def _rows(self):
+        from datetime import datetime
         if not self.path.exists():
-            return None
-        rows = [r.split(",") for r in self.path.read_text().strip().splitlines() if r.count(",") >= 6]
-        self.path.unlink(missing_ok=True)
+            return []
+        rows = []
+        for r in self.path.read_text().strip().splitlines():
+            f = [x.strip() for x in r.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                ts = datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append((ts, float(f[1]), float(f[2]), float(f[3]), f[4:8]))
+            except ValueError:
+                continue
+        return rows
+
+    def summary(self, t0: float, t1: float, pad: float = 0.25):
+        """Samples within [t0 - pad, t1 + pad] (host time.time() seconds)."""
+        rows = [r for r in self._rows() if t0 - pad <= r[0] <= t1 + pad]
         if not rows:
             return None
-        sm = [float(r[0]) for r in rows]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[3 + i].strip().lower() == "active"})
-        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": float(rows[0][1]), "samples": len(rows),
-                "power_w_max": max(float(r[2]) for r in rows), "reasons": reasons}
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[4][i].lower() == "active"})
+        return {"sm_mhz": float(np.median([r[1] for r in rows])), "sm_max_mhz": rows[0][2], "samples": len(rows),
+                "power_w_max": max(r[3] for r in rows), "reasons": reasons}
+
+    def cleanup(self):
+        self.path.unlink(missing_ok=True)
 
 
 def measured_peaks():
@@ -244,6 +270,15 @@ class Ranks:
         import torch.distributed as dist
         t = torch.tensor([x], dtype=torch.float64, device=self.device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, x: float) -> float:
+        if self.world == 1:
+            return x
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([float(x)], dtype=torch.float64, device=self.device)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
         return float(t.item())
 
     def close(self):
@@ -428,6 +463,112 @@ def group_rate(rt, synthetic, dev, cfg, groups, members, K, W, min_patches, rank
                     "decoder steps as batched GEMVs (one weight read, one dot product per member)"}
 
 
+def decoder_steps_at_config(rt, dev, cfg, ids_seed, peak):
+    """One whole base / residual KV-cache decode step at batch 1 at the lengths of
+    their configurations: the base decoder after 256 prefilled rows growing to 456
+    (past 256..455), the residual decoder growing from 256 to 512 (past 256..511).
+    Each point is 50 steps replayed in one graph at that KV length (vxc_profile_kernel);
+    the step time is affine in the length, so the mean over a configuration's range
+    is the mean of its two end points, reported beside the middle."""
+    from voxcpm2_b200 import synthetic
+    out = {}
+    for which, name, kind, lo, hi in ((0, "base_decoder", "base_step", 256, 455),
+                                      (1, "residual_decoder", "res_step", 256, 511)):
+        s = rt.Stream(dev, kv_capacity=520)
+        if which == 0:
+            rows = s.text_embed(synthetic.token_ids(cfg, 256, seed=ids_seed))
+        else:
+            rows = synthetic.normal((256, cfg.hidden), seed=ids_seed + 1)
+        s.decoder_step(which, rows)
+        points = {}
+        for past in (lo, (lo + hi) // 2, hi):
+            grow = past - s.token_count(which)
+            if grow > 0:
+                s.decoder_step(which, synthetic.normal((grow, cfg.hidden), seed=ids_seed + past))
+            ms, nb = s.profile_kernel(kind, 50)
+            points[past] = (ms, nb)
+        s.close()
+        us_lo, us_hi = 1e3 * points[lo][0], 1e3 * points[hi][0]
+        nb_mean = 0.5 * (points[lo][1] + points[hi][1])
+        us = 0.5 * (us_lo + us_hi)
+        gbs = nb_mean / (us / 1e6) / 1e9
+        out[name] = {"us": round(us, 2), "bytes": nb_mean, "GB/s": round(gbs, 1), "frac": gbs / peak,
+                     "kv_rows": [lo, hi + 1], "us_at_past": {str(k): round(1e3 * v[0], 2) for k, v in points.items()},
+                     "how": "mean of the first and last step of the configuration (the step time is affine in the KV "
+                            "length); each point 50 steps replayed in one graph, CUDA events"}
+    return out
+
+
+def utterance_run(rt, streams, ids, cfg, rank, world, barrier, max_over_ranks, clocks):
+    """Whole utterances: every stream prefilled with its 64-token prompt, then its patch
+    loop (min_patches 100) run until its stop decision, all streams at once. A first,
+    untimed pass learns each stream's utterance length (the loop is deterministic);
+    the timed pass replays exactly those patches from the device noise tables."""
+    import torch
+    cap = min(cfg.max_generation_patches, int(TEXT_TOKENS * 6.0 + 10.0))
+    S = len(streams)
+    noise = [synthetic_normal(cap, cfg.latent, 50_000 + 97 * (rank * S + i)) for i in range(S)]
+    for s, i, n in zip(streams, ids, noise):
+        s.prefill(i)
+        s.upload_noise(n)
+    # a stopped stream's later patch graphs skip their work: a stream's utterance
+    # length is the patch at which its stop flag first shows
+    lengths = [0] * S
+    for step in range(cap):
+        for s, n in zip(streams, lengths):
+            if not n:
+                s.patch_step_async(MIN_PATCHES, CFG, TIMESTEPS)
+        if step >= MIN_PATCHES:
+            for j, s in enumerate(streams):
+                if not lengths[j]:
+                    s.synchronize()
+                    if s.state().stopped:
+                        lengths[j] = step + 1
+        if all(lengths):
+            break
+    lengths = [n if n else cap for n in lengths]
+    # the timed pass: the same prompts and noise, exactly 'lengths' patches each
+    for s, i in zip(streams, ids):
+        s.prefill(i)
+    ext = [torch.cuda.ExternalStream(s.cuda_stream()) for s in streams]
+    main = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.time()
+    e0.record(main)
+    for st in ext:
+        st.wait_event(e0)
+    for step in range(max(lengths)):
+        for s, n in zip(streams, lengths):
+            if step < n:
+                s.patch_step_async(MIN_PATCHES, CFG, TIMESTEPS)
+    for st in ext:
+        ev = torch.cuda.Event()
+        ev.record(st)
+        main.wait_event(ev)
+    e1.record(main)
+    e1.synchronize()
+    t1 = time.time()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    for s, n in zip(streams, lengths):
+        st = s.state()
+        assert st.patches == n and st.stopped == (n < cap) and st.error == 0, "an utterance did not replay"
+    total = int(sum(lengths))
+    return {"value": None, "patches_this_rank": total, "unit": "patches/s",
+            "patches_per_stream": [int(n) for n in lengths], "timed_region_s": ms / 1e3,
+            "stop_decided": int(sum(n < cap for n in lengths)), "streams": S,
+            "clocks": clocks.summary(t0, t1),
+            "how": "each stream: prefill (untimed), then its whole patch loop until the stop head decides "
+                   f"(min_patches {MIN_PATCHES}, cap {cap}); all streams of the GPU at once, CUDA events"}
+
+
+def synthetic_normal(rows, cols, seed):
+    from voxcpm2_b200 import synthetic
+    return synthetic.normal((rows, cols), seed=seed)
+
+
 def run_ours(args):
     import torch
     from voxcpm2_b200 import runtime as rt
@@ -436,26 +577,29 @@ def run_ours(args):
 
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
+    clocks = ClockSampler(local).start()  # before any timed work, on every rank
     ranks = Ranks("nccl", torch.device("cuda", local))
     world, rank = ranks.world, ranks.rank
     barrier, max_over_ranks = ranks.barrier, ranks.max
 
     S, K, W = args.streams, args.steps, args.warmup
     cfg_info, min_patches = workload(S, K, W)
+    first = window(K, W)
     cfg = BENCH
     L = cfg.latent
     dev = rt.Device(cfg, local, synthetic.model_blobs(cfg, 0))
-    cap = TEXT_TOKENS + 1 + W + K + 8
-    streams = [rt.Stream(dev, kv_capacity=max(cap, 512)) for _ in range(S)]
+    cap = TEXT_TOKENS + 1 + first + K + 8
+    streams = [rt.Stream(dev, kv_capacity=512) for _ in range(S)]
     seeds = stream_seeds(rank, S)
     ids = [synthetic.token_ids(cfg, TEXT_TOKENS, seed=a) for a, _ in seeds]
-    noise = [synthetic.normal((W + K, L), seed=b) for _, b in seeds]
+    noise = [synthetic.normal((first + K, L), seed=b) for _, b in seeds]
 
-    # ---- value: device-resident, graphs replayed from the uploaded noise tables
+    # ---- value: device-resident, graphs replayed from the uploaded noise tables;
+    # 'first' untimed patches (warm-up included), then K timed ones
     for s, i, n in zip(streams, ids, noise):
         s.prefill(i)
         s.upload_noise(n)
-    for _ in range(W):
+    for _ in range(first):
         for s in streams:
             s.patch_step_async(min_patches, CFG, TIMESTEPS)
     for s in streams:
@@ -465,99 +609,93 @@ def run_ours(args):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local) as clocks:
-        e0.record(main)
-        for st in ext:
-            st.wait_event(e0)
-        for _ in range(K):
-            for s in streams:
-                s.patch_step_async(min_patches, CFG, TIMESTEPS)
-        for st in ext:
-            ev = torch.cuda.Event()
-            ev.record(st)
-            main.wait_event(ev)
-        e1.record(main)
-        e1.synchronize()
+    t0 = time.time()
+    e0.record(main)
+    for st in ext:
+        st.wait_event(e0)
+    h0 = time.perf_counter()
+    for _ in range(K):
+        for s in streams:
+            s.patch_step_async(min_patches, CFG, TIMESTEPS)
+    host_enqueue_ms = 1e3 * (time.perf_counter() - h0)
+    for st in ext:
+        ev = torch.cuda.Event()
+        ev.record(st)
+        main.wait_event(ev)
+    e1.record(main)
+    e1.synchronize()
+    t1 = time.time()
     barrier()
-    ms = max_over_ranks(e0.elapsed_time(e1))
+    ms_rank = e0.elapsed_time(e1)
+    ms = max_over_ranks(ms_rank)
+    host_enqueue_ms_max = max_over_ranks(host_enqueue_ms)
+    clk = clocks.summary(t0, t1)
     states = [s.state() for s in streams]
-    assert all(st.patches == W + K and st.error == 0 for st in states), "a stream did not complete its patches"
+    assert all(st.patches == first + K and st.error == 0 for st in states), "a stream did not complete its patches"
     graph_kernels = states[0].graph_kernels
     value = job_rate(world, S, K, ms / 1e3)
 
     # ---- dominant kernel, timed alone with CUDA events on the stream
     peak, peak_kind = measured_peaks()
-    try:  # the persistent DiT decoder when the stream runs that form (all 12 layers per launch)
-        prof_ms, prof_bytes = streams[0].profile_kernel("dit_layers", 20)
-        kname = "dit_layers_kernel (persistent DiT decoder, 12 layers, tcgen05 + TMA, one launch per evaluation)"
-        traffic = None
-    except rt.VxcError:  # the default form: per-layer tcgen05 linears
-        prof_ms, prof_bytes = streams[0].profile_kernel("dit_gateup", 100)
-        kname = "tc_linear_kernel gate/up (DiT, tcgen05 + TMA, 2x11 tokens, SiLU*up epilogue)"
-        traffic = profiled_value("tc_linear_gateup_dit", "dram_bytes_per_launch")
+    prof_ms, prof_bytes = streams[0].profile_kernel("dit_gateup", 100)
+    kname = "tc_linear_kernel gate/up (DiT, tcgen05 + TMA, 2x11 tokens, SiLU*up epilogue)"
     achieved = prof_bytes / (prof_ms / 1e3) / 1e9
     # per GPU: algorithmic bytes of all its streams' patches / the timed region
-    bpp = patch_bytes(cfg, TEXT_TOKENS + 1 + W + K / 2)
+    bpp = patch_bytes(cfg, TEXT_TOKENS + 1 + first + K / 2)
     gbs, frac = gpu_bandwidth(value, world, bpp, peak)
     hbm_job = {"bytes_per_patch": bpp, "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": frac,
                "note": "per GPU: patches/s per GPU x algorithmic bytes per patch, all its streams"}
-    dram_pp = profiled_value("patch_loop_16streams_dram_range", "dram_bytes_per_patch")
-    if dram_pp:  # measured DRAM bytes: concurrent streams share weights through the L2
-        gbs_d, frac_d = gpu_bandwidth(value, world, dram_pp, peak)
-        hbm_job.update({"dram_bytes_per_patch": dram_pp, "achieved_dram": gbs_d, "frac_dram": frac_d,
-                        "dram_source": "profiles/patch_loop_16streams_dram_range.md (ncu app-range capture of "
-                                       "16 streams; the L2-shared fraction varies with the streams' timing)"})
     roofline = {"kernel": kname, "bound": "hbm",
                 "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                 "peak_kind": f"{peak_kind} burst copy bandwidth", "bytes_per_launch": prof_bytes,
-                "us_per_launch": 1e3 * prof_ms, "traffic": traffic,
-                "traffic_source": "profiles/tc_linear_gateup_dit.md (ncu dram__bytes_read.sum + write, one launch)"
-                if traffic else None}
+                "us_per_launch": 1e3 * prof_ms, "traffic": GATEUP_DRAM_BYTES_PER_LAUNCH,
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of this kernel, "
+                                  "a constant in bench.py (not measured in this run)"}
     # the same kernel in the regime the bench runs it: every stream replays its own
     # graph of launches at once (aggregate algorithmic bytes / elapsed)
-    if not kname.startswith("dit_layers"):
-        iters_c = 100
-        cms, cbytes = rt.Stream.profile_kernel_concurrent(streams, "dit_gateup", iters_c)
-        agg = S * iters_c * cbytes / (cms / 1e3) / 1e9
-        roofline["concurrent"] = {"streams": S, "launches": S * iters_c, "achieved": agg, "frac": agg / peak,
-                                  "us_per_launch_avg": 1e3 * cms / (S * iters_c)}
-        roofline["concurrent"]["note"] = ("algorithmic bytes; the streams cycle through the same 12 layers' "
-                                          "weights and share part of them through the L2")
+    iters_c = 100
+    cms, cbytes = rt.Stream.profile_kernel_concurrent(streams, "dit_gateup", iters_c)
+    agg = S * iters_c * cbytes / (cms / 1e3) / 1e9
+    roofline["concurrent"] = {"streams": S, "launches": S * iters_c, "achieved": agg, "frac": agg / peak,
+                              "us_per_launch_avg": 1e3 * cms / (S * iters_c),
+                              "note": "algorithmic bytes; the streams cycle through the same 12 layers' weights "
+                                      "and share part of them through the L2"}
     kernels = {}
     for k in ("dit_qkv", "dit_o", "dit_down", "base_qkv", "base_attn", "base_gateup", "base_down"):
         km, kb = streams[0].profile_kernel(k, 50)
         kernels[k] = {"us": round(1e3 * km, 2), "GB/s": round(kb / (km / 1e3) / 1e9, 1)}
-    # one whole KV-cache decode step at batch 1 (configs 2 and 3: every weight of the
-    # decoder once + the K/V rows), replayed as a graph at the stream's KV length
-    decode_step = {}
-    for k, name in (("base_step", "base_decoder"), ("res_step", "residual_decoder"), ("dit_eval", "dit_estimator_eval")):
-        km, kb = streams[0].profile_kernel(k, 50)
-        gbs = kb / (km / 1e3) / 1e9
-        decode_step[name] = {"us": round(1e3 * km, 2), "bytes": kb, "GB/s": round(gbs, 1), "frac": gbs / peak,
-                             "kv_rows": TEXT_TOKENS + 1 + W + K}
+    # configs 2 and 3: one whole KV-cache decode step at batch 1 at their KV lengths;
+    # config 4: one estimator evaluation
+    decode_step = decoder_steps_at_config(rt, dev, cfg, 4242, peak)
+    km, kb = streams[0].profile_kernel("dit_eval", 50)
+    decode_step["dit_estimator_eval"] = {"us": round(1e3 * km, 2), "bytes": kb,
+                                         "GB/s": round(kb / (km / 1e3) / 1e9, 1), "frac": kb / (km / 1e3) / 1e9 / peak}
 
     # ---- prefill of the 64-token prompt (65 rows through both decoders; synchronous call)
     one = streams[0]
     pre_ms = []
     for _ in range(3):
-        t0 = time.perf_counter()
+        t_0 = time.perf_counter()
         one.prefill(ids[0])
-        pre_ms.append(1e3 * (time.perf_counter() - t0))
+        pre_ms.append(1e3 * (time.perf_counter() - t_0))
 
     # ---- single-stream per-patch latency (device time per patch)
-    one.prefill(ids[0])
-    one.upload_noise(noise[0])
-    ext0 = ext[0]
-    lat_ms = []
-    for step in range(W + min(K, 12)):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(ext0)
-        one.patch_step_async(min_patches, CFG, TIMESTEPS)
-        b.record(ext0)
-        b.synchronize()
-        if step >= W:
-            lat_ms.append(a.elapsed_time(b))
-    p50_single = float(np.median(lat_ms))
+    def lone_latency(st, n):
+        st.prefill(ids[0])
+        st.upload_noise(noise[0])
+        xs = torch.cuda.ExternalStream(st.cuda_stream())
+        lat = []
+        for step in range(n):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(xs)
+            st.patch_step_async(min_patches, CFG, TIMESTEPS)
+            b.record(xs)
+            b.synchronize()
+            if step >= W:
+                lat.append(a.elapsed_time(b))
+        return float(np.median(lat))
+
+    p50_single = lone_latency(one, W + min(K, 12))
 
     # ---- the same for a stream tuned for one utterance at a time: ~296 CTAs per tensor-core
     # launch and a 4-stage ring (the knobs are read when a stream is created)
@@ -568,18 +706,7 @@ def run_ours(args):
     finally:
         for k in LATENCY_TUNING:
             os.environ.pop(k, None)
-    solo.prefill(ids[0])
-    solo.upload_noise(noise[0])
-    ext_solo = torch.cuda.ExternalStream(solo.cuda_stream())
-    lat_solo = []
-    for step in range(W + min(K, 12)):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(ext_solo)
-        solo.patch_step_async(min_patches, CFG, TIMESTEPS)
-        b.record(ext_solo)
-        b.synchronize()
-        if step >= W:
-            lat_solo.append(a.elapsed_time(b))
+    p50_solo = lone_latency(solo, W + min(K, 12))
     solo_ms, solo_bytes = solo.profile_kernel("dit_gateup", 100)  # the dominant kernel at this tuning
     ev_ms, ev_bytes = solo.profile_kernel("dit_eval", 20)
     decode_step["dit_estimator_eval_latency_tuned"] = {"us": round(1e3 * ev_ms, 2), "bytes": ev_bytes,
@@ -587,44 +714,52 @@ def run_ours(args):
                                                         "frac": ev_bytes / (ev_ms / 1e3) / 1e9 / peak,
                                                         "tuning": LATENCY_TUNING}
     solo.close()
-    p50_solo = float(np.median(lat_solo))
+    ach = solo_bytes / (solo_ms / 1e3) / 1e9
+    roofline["latency_tuned"] = {"tuning": LATENCY_TUNING, "us_per_launch": 1e3 * solo_ms, "achieved": ach,
+                                 "frac": ach / peak, "note": "the same kernel in a stream tuned for one "
+                                 "utterance at a time (graph-cycled over the 12 layers, CUDA events)"}
 
     # ---- e2e: the public C ABI with host buffers (noise in, latent + stop flag out, every
-    # step), one thread per stream. Two driving patterns: the synchronous vxc_patch_step, and
-    # the pipelined vxc_patch_submit / vxc_patch_collect with one patch queued ahead (the
-    # headline e2e: the stream's GPU queue does not drain while the host handles a patch).
-    def e2e_run(pipelined: bool):
+    # step): vxc_patch_run drives all of this GPU's streams from one host thread in native
+    # code, two patches queued per stream. The same window of patches as 'value'.
+    def e2e_run():
         for s, i in zip(streams, ids):
             s.prefill(i)
-        per_call = [[] for _ in range(S)]
-        done_warm = [threading.Event() for _ in range(S)]  # warm-up steps done; wait for the timed start
+        nz = np.ascontiguousarray(np.stack(noise))            # [S][first + K][L]
+        rt.patch_run(streams, np.ascontiguousarray(nz[:, :first]), min_patches, CFG, TIMESTEPS)
+        timed = np.ascontiguousarray(nz[:, first:first + K])
+        out = np.empty_like(timed)
+        barrier()
+        torch.cuda.synchronize()
+        t_0 = time.perf_counter()
+        _, counts = rt.patch_run(streams, timed, min_patches, CFG, TIMESTEPS, out=out)
+        torch.cuda.synchronize()
+        secs = max_over_ranks(time.perf_counter() - t_0)
+        barrier()
+        assert (counts == K).all(), "a stream stopped inside the e2e window"
+        return job_rate(world, S, K, secs)
+
+    e2e_value = e2e_run()
+
+    # the synchronous vxc_patch_step, one host thread per stream
+    def e2e_sync_run():
+        for s, i in zip(streams, ids):
+            s.prefill(i)
+        done_warm = [threading.Event() for _ in range(S)]
         go = threading.Event()
+        per_call = [[] for _ in range(S)]
 
         def worker(j):
             s = streams[j]
-            out = np.empty(L, np.float32)  # the collected latent (a host buffer the caller owns)
-            if pipelined:
-                s.patch_submit(noise[j][0], min_patches, CFG, TIMESTEPS)
-                for step in range(1, W):
-                    s.patch_submit(noise[j][step], min_patches, CFG, TIMESTEPS)
-                    s.patch_collect(out)
-                s.patch_collect(out)
-            else:
-                for step in range(W):
-                    s.patch_step(noise[j][step], min_patches, step, CFG, TIMESTEPS)
+            out = np.empty(L, np.float32)
+            for step in range(first):
+                s.patch_step(noise[j][step], min_patches, step, CFG, TIMESTEPS, out=out)
             done_warm[j].set()
             go.wait()
-            if pipelined:
-                s.patch_submit(noise[j][W], min_patches, CFG, TIMESTEPS)
-                for step in range(W + 1, W + K):
-                    s.patch_submit(noise[j][step], min_patches, CFG, TIMESTEPS)
-                    _, stop = s.patch_collect(out)
-                s.patch_collect(out)
-            else:
-                for step in range(W, W + K):
-                    t0 = time.perf_counter()
-                    s.patch_step(noise[j][step], min_patches, step, CFG, TIMESTEPS, out=out)
-                    per_call[j].append(time.perf_counter() - t0)
+            for step in range(first, first + K):
+                t_0 = time.perf_counter()
+                s.patch_step(noise[j][step], min_patches, step, CFG, TIMESTEPS, out=out)
+                per_call[j].append(time.perf_counter() - t_0)
 
         threads = [threading.Thread(target=worker, args=(j,)) for j in range(S)]
         for t in threads:
@@ -633,20 +768,25 @@ def run_ours(args):
             ev.wait()
         barrier()
         torch.cuda.synchronize()
-        t0 = time.perf_counter()
+        t_0 = time.perf_counter()
         go.set()
         for t in threads:
             t.join()
         torch.cuda.synchronize()
-        secs = max_over_ranks(time.perf_counter() - t0)
+        secs = max_over_ranks(time.perf_counter() - t_0)
         barrier()
         return job_rate(world, S, K, secs), per_call
 
-    e2e_sync_value, per_call = e2e_run(False)
-    e2e_value, _ = e2e_run(True)
+    e2e_sync_value, per_call = e2e_sync_run()
     calls = np.concatenate([np.array(c) for c in per_call]) * 1e3
     h2d = world * S * L * 4           # every stream's noise patch (whole job)
     d2h = world * S * (L * 4 + 40)    # every stream's latent patch + its 40-byte control block
+
+    # ---- whole utterances (prefill to the stop decision) on every stream at once
+    utter = utterance_run(rt, streams, ids, cfg, rank, world, barrier, max_over_ranks, clocks)
+    utter_total = ranks.sum(utter.pop("patches_this_rank"))  # utterance lengths differ per rank
+    utter["patches_all_ranks"] = int(utter_total)
+    utter["value"] = utter_total / utter["timed_region_s"]  # whole job: all ranks' patches / the slowest rank
 
     # ---- stream groups: the same workload with each group's estimator passes batched
     group = None
@@ -656,6 +796,7 @@ def run_ours(args):
 
     # ---- config 1: the VoxCPM2SDPA op alone
     sdpa = sdpa_op(rt, peak, rank, world)
+    clocks.stop()
 
     # ---- CPU baseline: the oracle port on this host, bounded sample (rank 0, N = 1)
     cpu = None
@@ -666,12 +807,7 @@ def run_ours(args):
                "sample": f"{args.cpu_sample_patches} patches (after 1 untimed) of one stream, oracle (reference "
                          f"CPU math restated in C++), {threads_cpu} threads"}
 
-    if not kname.startswith("dit_layers"):
-        ach = solo_bytes / (solo_ms / 1e3) / 1e9
-        roofline["latency_tuned"] = {"tuning": LATENCY_TUNING, "us_per_launch": 1e3 * solo_ms, "achieved": ach,
-                                     "frac": ach / peak, "note": "the same kernel in a stream tuned for one "
-                                     "utterance at a time (graph-cycled over the 12 layers, CUDA events)"}
-    clk = clocks.summary()
+    clocks.cleanup()
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "patches/s", "n_gpus": world, "steps": K, "warmup": W,
@@ -682,12 +818,16 @@ def run_ours(args):
             "p50_patch_ms_latency_tuned": p50_solo, "latency_tuning": LATENCY_TUNING,
             "prefill_ms": float(np.median(pre_ms)),
             "per_gpu_patches_per_s": value / world,
+            "host_enqueue_ms": {"rank0": host_enqueue_ms, "max_over_ranks": host_enqueue_ms_max,
+                                "device_ms_rank0": ms_rank,
+                                "note": f"host time to enqueue the {S * K} patch graphs of the timed region"},
             "e2e": {"value": e2e_value, "unit": "patches/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "api": "vxc_patch_submit / vxc_patch_collect, one patch queued ahead per stream"},
+                    "api": "vxc_patch_run: every stream of the GPU driven from one host thread (native loop, two "
+                           "patches queued per stream; host noise in, host latent + stop flag out every patch)"},
             "e2e_sync": {"value": e2e_sync_value, "unit": "patches/s", "h2d_bytes_per_step": h2d,
-                         "d2h_bytes_per_step": d2h, "api": "vxc_patch_step (synchronous)"},
+                         "d2h_bytes_per_step": d2h, "api": "vxc_patch_step (synchronous), one host thread per stream"},
             "gpu_launches": graph_kernels * S * K, "roofline": roofline, "hbm_job": hbm_job, "kernels": kernels,
-            "decode_step": decode_step, "sdpa_op": sdpa,
+            "decode_step": decode_step, "utterance": utter, "sdpa_op": sdpa,
             "cpu_baseline": cpu, "clocks": clk, "group": group,
         }
         print(json.dumps(line), flush=True)
@@ -699,16 +839,14 @@ def run_ours(args):
 
 
 def run_range(args):
-    """The workload of an ncu app-range capture (DRAM bytes of concurrent streams)."""
-    import torch
+    """A few patches of one lone stream or one stream group, for an ncu launch list
+    (gpu__time_duration.sum alone: one pass per launch, nothing saved or restored).
+    Two warm-up patches, then one: the last graph_kernels launches are that patch."""
     from voxcpm2_b200 import runtime as rt
     from voxcpm2_b200 import synthetic
     from voxcpm2_b200.config import BENCH
-    S, K, W = args.streams, 6, 3
     dev = rt.Device(BENCH, 0, synthetic.model_blobs(BENCH, 0))
     if args.range == "group":
-        # one group of --group-members streams: 2 warm-up group patches, then 1
-        # (launch list: the last kernels_per_group_patch launches are that patch)
         g = rt.Group(dev, args.group_members, kv_capacity=512)
         for m, st in enumerate(g.streams):
             a = 7919 * m + 13
@@ -720,39 +858,15 @@ def run_range(args):
         print(json.dumps({"range": "group", "members": args.group_members,
                           "kernels_per_group_patch": g.graph_kernels()}))
         g.close()
-        dev.close()
-        return 0
-    streams = [rt.Stream(dev, kv_capacity=512) for _ in range(S)]
-    if args.range == "profile":
-        rt.Stream.profile_kernel_concurrent(streams, "dit_gateup", 100)
-        torch.cuda.synchronize()
-        torch.cuda.profiler.start()
-        ms, nb = rt.Stream.profile_kernel_concurrent(streams, "dit_gateup", 100)
-        torch.cuda.profiler.stop()
-        print(json.dumps({"range": "profile", "ms": ms, "algorithmic_bytes": S * 100 * nb}))
     else:
-        for i, (a, b) in enumerate(stream_seeds(0, S)):
-            streams[i].prefill(synthetic.token_ids(BENCH, TEXT_TOKENS, seed=a))
-            streams[i].upload_noise(synthetic.normal((W + K, BENCH.latent), seed=b))
-        for _ in range(W):
-            for s in streams:
-                s.patch_step_async(MIN_PATCHES, CFG, TIMESTEPS)
-        for s in streams:
-            s.synchronize()
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        torch.cuda.profiler.start()
-        for _ in range(K):
-            for s in streams:
-                s.patch_step_async(MIN_PATCHES, CFG, TIMESTEPS)
-        for s in streams:
-            s.synchronize()
-        torch.cuda.profiler.stop()
-        dt = time.perf_counter() - t0
-        print(json.dumps({"range": "patches", "patches": S * K, "wall_ms": 1e3 * dt,
-                          "algorithmic_bytes": S * K * patch_bytes(BENCH, TEXT_TOKENS + 1 + W + K / 2)}))
-    for s in streams:
-        s.close()
+        st = rt.Stream(dev, kv_capacity=512)
+        st.prefill(synthetic.token_ids(BENCH, TEXT_TOKENS, seed=13))
+        st.upload_noise(synthetic.normal((4, BENCH.latent), seed=14))
+        for _ in range(3):
+            st.patch_step_async(MIN_PATCHES, CFG, TIMESTEPS)
+        st.synchronize()
+        print(json.dumps({"range": "stream", "kernels_per_patch": st.state().graph_kernels}))
+        st.close()
     dev.close()
     return 0
 

@@ -112,7 +112,7 @@ enum {
     VXC_PROF_BASE_QKV = 5,     /* base decoder q/k/v GEMV + RoPE + KV append */
     VXC_PROF_BASE_ATTN = 6,    /* base decoder flash-decode attention */
     VXC_PROF_DIT_O = 7,        /* DiT attention + o projection + residual */
-    VXC_PROF_DIT_LAYERS = 8,   /* persistent DiT decoder: all layers of one evaluation (one launch) */
+    /* 8 is not used */
     VXC_PROF_BASE_STEP = 9,    /* one whole base decoder KV-cache step (24 layers + final norm) */
     VXC_PROF_RES_STEP = 10,    /* one whole residual decoder KV-cache step */
     VXC_PROF_DIT_EVAL = 11,    /* one whole DiT estimator evaluation (embed, 12 layers, out projection) */
@@ -267,6 +267,16 @@ VXC_API int32_t vxc_sdpa_host(const float* q, int32_t heads, int32_t src, int32_
                               int32_t mask_c, const float* past_k, const float* past_v, int32_t past,
                               float scale, float* out, float* out_k, float* out_v);
 
+/* VoxCPM2TimestepEmbedding::forward (src/ncnn_layers/timestep_embedding/
+ * voxcpm2_timestep_embedding.cpp:128-160; params half_dim, scale, max_period,
+ * schedule_mode from load_param) on HOST pointers, computed on the current
+ * CUDA device; synchronous. in [n_in]; out [n_in][2 * half_dim] =
+ * [sin(t f_i) | cos(t f_i)], f_i = exp(-ln(max_period) i / (half_dim - 1)),
+ * t = in[b] * scale (schedule_mode 0) or t(in[0] = step, in[1] = timesteps) *
+ * scale for every row (schedule_mode != 0, n_in >= 2). */
+VXC_API int32_t vxc_timestep_embedding(const float* in, int32_t n_in, int32_t half_dim, float scale,
+                                       float max_period, int32_t schedule_mode, float* out);
+
 /* ---- device-resident driving (benchmarks, multi-stream servers) ---------- */
 /* Uploads noise [patches][D*P] into the stream's device noise table. */
 VXC_API int32_t vxc_upload_noise(vxc_stream* s, const float* noise, int32_t patches);
@@ -284,6 +294,18 @@ VXC_API int32_t vxc_patch_step_async(vxc_stream* s, int32_t min_patches, float c
 VXC_API int32_t vxc_patch_submit(vxc_stream* s, const float* noise, int32_t min_patches, float cfg_value,
                                  int32_t timesteps);
 VXC_API int32_t vxc_patch_collect(vxc_stream* s, float* out_latent, int32_t* out_stop);
+/* The patch loop body (src/synthesizer.cpp:537-659, one vxc_patch_step per
+ * patch) for n independent streams of one device, driven from the calling
+ * thread with no per-stream host thread: each stream keeps two patches queued
+ * through vxc_patch_submit / vxc_patch_collect, visited round robin. noise
+ * [n][patches][D*P] and out_latents [n][patches][D*P] are host arrays; a
+ * stream ends at its stop decision or after 'patches' patches, and
+ * out_patches[i] is the number of latents written for stream i. Every stream
+ * must be prefilled, with nothing in flight; the call holds every stream's call
+ * lock until it returns. */
+VXC_API int32_t vxc_patch_run(vxc_stream* const* streams, int32_t n, const float* noise, int32_t patches,
+                              int32_t min_patches, float cfg_value, int32_t timesteps, float* out_latents,
+                              int32_t* out_patches);
 
 VXC_API int32_t vxc_stream_synchronize(vxc_stream* s);
 VXC_API int32_t vxc_read_state(vxc_stream* s, vxc_stream_state* out);
@@ -295,8 +317,7 @@ VXC_API int32_t vxc_read_latents(vxc_stream* s, int32_t first, int32_t count, fl
  * runs it: 'iters' launches cycling through the layers' weights (for the
  * benchmark model more than the L2 holds), captured in one CUDA graph with
  * programmatic dependent launch between them, timed with CUDA events on the
- * stream after one warm-up replay. VXC_PROF_DIT_LAYERS times each persistent
- * launch alone between two events. Writes the mean milliseconds per launch and
+ * stream after one warm-up replay. Writes the mean milliseconds per launch and
  * the algorithmic bytes one launch must move (weights + activations in + out).
  * Call it between patch steps: it leaves the stream's positions and valid KV
  * rows as they were, but overwrites scratch activations and the next free KV
@@ -306,7 +327,7 @@ VXC_API int32_t vxc_profile_kernel(vxc_stream* s, int32_t kernel, int32_t iters,
 /* The same kernel on n streams of one device at once: each stream replays its own
  * graph of 'iters' launches, all started after one event on streams[0] and joined
  * before a second; writes the elapsed milliseconds of the whole set (n * iters
- * launches) and the algorithmic bytes of one launch. Not for VXC_PROF_DIT_LAYERS. */
+ * launches) and the algorithmic bytes of one launch. */
 VXC_API int32_t vxc_profile_kernel_concurrent(vxc_stream** streams, int32_t n, int32_t kernel, int32_t iters,
                                               float* ms_total, double* bytes_per_launch);
 /* The stream's cudaStream_t, for callers timing it with CUDA events. */

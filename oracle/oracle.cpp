@@ -394,6 +394,14 @@ struct orc_model {
     // long table means the short one is used at every position
     std::vector<float> short_factor, long_factor;
     std::vector<float> dit_factor;  // the estimator's rotary table: all ones
+    // test hook (orc_trace_fsq): every FSQ row's values tanh(z) * scale before rounding,
+    // appended in call order while rows remain
+    mutable float* fsq_log = nullptr;
+    mutable int fsq_log_cap = 0, fsq_log_n = 0;
+    // test hook (orc_force_fsq): codes (integers in units of 1 / scale) that replace the
+    // rounding of the next FSQ rows, in call order while rows remain
+    const float* fsq_force = nullptr;
+    mutable int fsq_force_cap = 0, fsq_force_n = 0;
 };
 
 namespace {
@@ -796,7 +804,18 @@ int orc_fsq(const orc_model* m, const float* in, int rows, float* out) {
     const uint16_t *in_w = b, *in_b = b + Q * H, *out_w = in_b + Q, *out_b = out_w + H * Q;
     std::vector<float> z(static_cast<std::size_t>(rows) * Q);
     linear(in_w, in_b, static_cast<int>(Q), static_cast<int>(H), in, rows, z.data());
-    for (float& v : z) v = std::nearbyint(std::tanh(v) * d.fsq_scale) / d.fsq_scale;
+    for (float& v : z) v = std::tanh(v) * d.fsq_scale;
+    for (int r = 0; r < rows && m->fsq_log && m->fsq_log_n < m->fsq_log_cap; ++r, ++m->fsq_log_n)
+        std::memcpy(m->fsq_log + static_cast<std::size_t>(m->fsq_log_n) * Q, z.data() + r * Q, sizeof(float) * Q);
+    for (int r = 0; r < rows; ++r) {
+        const bool forced = m->fsq_force && m->fsq_force_n < m->fsq_force_cap;
+        const float* code = forced ? m->fsq_force + static_cast<std::size_t>(m->fsq_force_n) * Q : nullptr;
+        for (std::size_t j = 0; j < Q; ++j) {
+            float& v = z[r * Q + j];
+            v = (forced ? code[j] : std::nearbyint(v)) / d.fsq_scale;
+        }
+        if (forced) ++m->fsq_force_n;
+    }
     linear(out_w, out_b, static_cast<int>(H), static_cast<int>(Q), z.data(), rows, out);
     return 0;
 }
@@ -949,6 +968,28 @@ bool all_loaded(const orc_model* m) {
 }  // namespace
 
 extern "C" {
+
+// Test hook: record the pre-rounding FSQ values (tanh(z) * fsq_scale, [rows][fsq_dim])
+// of the next 'rows' FSQ rows the model computes into buf (NULL stops recording).
+// Returns the number of rows recorded so far by the previous call's buffer.
+int orc_trace_fsq(orc_model* m, float* buf, int rows) {
+    const int n = m->fsq_log_n;
+    m->fsq_log = buf;
+    m->fsq_log_cap = buf ? rows : 0;
+    m->fsq_log_n = 0;
+    return n;
+}
+
+// Test hook: the next 'rows' FSQ rows the model computes take their codes from
+// codes [rows][fsq_dim] (integers, the rounded tanh(z) * fsq_scale) instead of
+// rounding their own values; NULL stops. Returns the rows the previous buffer served.
+int orc_force_fsq(orc_model* m, const float* codes, int rows) {
+    const int n = m->fsq_force_n;
+    m->fsq_force = codes;
+    m->fsq_force_cap = codes ? rows : 0;
+    m->fsq_force_n = 0;
+    return n;
+}
 
 int orc_generate(orc_model* m, const int32_t* text_ids, int n_text, int min_patches,
                  int timesteps, float cfg, int max_patches_override, uint32_t seed,

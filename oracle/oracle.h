@@ -149,6 +149,18 @@ int orc_generate(orc_model* model, const int32_t* text_ids, int n_text, int min_
                  float* latents, float* lm_hidden, float* res_hidden, float* stop_logits,
                  int* out_patches);
 
+/* Test hook: record the pre-rounding FSQ values (tanh(z) * fsq_scale, [rows][fsq_dim])
+ * of the next 'rows' FSQ rows into buf (NULL stops); returns the rows recorded into
+ * the previous buffer. During orc_generate row p is the FSQ of patch p, whose output
+ * is the LM hidden state entering patch p + 1. */
+int orc_trace_fsq(orc_model* model, float* buf, int rows);
+
+/* Test hook: the next 'rows' FSQ rows take their codes from codes [rows][fsq_dim]
+ * (integers: the rounded tanh(z) * fsq_scale) instead of their own rounding, so the
+ * oracle can follow another implementation through a value that sits on a rounding
+ * boundary; NULL stops. Returns the rows the previous buffer served. */
+int orc_force_fsq(orc_model* model, const float* codes, int rows);
+
 /* The same from a prefix given row by row (synthesizer.cpp:43-47, 359-535): token
  * ids of every row, is_audio flags, the audio rows' latent patches in row order
  * ([n_audio][D*P], d-major); n_target_text sizes max_patches (the target text's

@@ -109,6 +109,10 @@ def _setup(L) -> None:
     L.orc_generate.restype = i
     L.orc_generate_rows.argtypes = [vp, vp, vp, vp, i, i, i, i, f, i, C.c_uint32, vp, vp, vp, vp, C.POINTER(C.c_int)]
     L.orc_generate_rows.restype = i
+    L.orc_trace_fsq.argtypes = [vp, vp, i]
+    L.orc_trace_fsq.restype = i
+    L.orc_force_fsq.argtypes = [vp, vp, i]
+    L.orc_force_fsq.restype = i
 
 
 def _p(a: Optional[np.ndarray]):
@@ -318,7 +322,10 @@ class Oracle:
         return out
 
     def generate(self, text_ids, min_patches: int = 2, timesteps: int = 10, cfg_value: float = 2.0,
-                 max_patches_override: int = 0, seed: int = 0) -> dict:
+                 max_patches_override: int = 0, seed: int = 0, fsq_codes=None) -> dict:
+        """generate_with_caches for a text-only prefix. fsq_codes [rows][fsq_dim]: codes
+        that replace the FSQ rounding of patches 0 .. rows - 1 (the test hook that lets
+        the oracle follow another run's rounding decisions; see orc_force_fsq)."""
         ids = np.ascontiguousarray(text_ids, dtype=np.int32)
         cap = max_patches(ids.size, self.cfg.max_generation_patches)
         if max_patches_override > 0:
@@ -327,9 +334,18 @@ class Oracle:
         lm = np.zeros((cap, self.cfg.hidden), np.float32)
         res = np.zeros((cap, self.cfg.hidden), np.float32)
         stop = np.zeros((cap, 2), np.float32)
+        fsq_pre = np.zeros((cap, self.cfg.fsq_dim), np.float32)
         n = C.c_int(0)
-        rc = lib().orc_generate(self._m, _p(ids), ids.size, min_patches, timesteps, cfg_value,
-                                max_patches_override, seed, _p(lat), _p(lm), _p(res), _p(stop), C.byref(n))
+        codes = None if fsq_codes is None else np.ascontiguousarray(fsq_codes, dtype=np.float32)
+        lib().orc_trace_fsq(self._m, _p(fsq_pre), cap)
+        if codes is not None:
+            lib().orc_force_fsq(self._m, _p(codes), codes.shape[0])
+        try:
+            rc = lib().orc_generate(self._m, _p(ids), ids.size, min_patches, timesteps, cfg_value,
+                                    max_patches_override, seed, _p(lat), _p(lm), _p(res), _p(stop), C.byref(n))
+        finally:
+            lib().orc_trace_fsq(self._m, None, 0)
+            lib().orc_force_fsq(self._m, None, 0)
         if rc == -2:
             raise RuntimeError("dit_estimator produced non-finite values")
         if rc == -3:
@@ -337,8 +353,10 @@ class Oracle:
         if rc != 0:
             raise ValueError("orc_generate failed")
         k = n.value
+        # fsq_pre[p]: the FSQ values of patch p before rounding (tanh(z) * fsq_scale); their
+        # rounded codes make the LM hidden state entering patch p + 1
         return {"patches": k, "latents": lat[:k], "lm_hidden": lm[:k], "res_hidden": res[:k],
-                "stop_logits": stop[:k]}
+                "stop_logits": stop[:k], "fsq_pre": fsq_pre[:k]}
 
     def generate_rows(self, token_ids, is_audio, audio_latents, n_target_text: int, min_patches: int = 2,
                       timesteps: int = 10, cfg_value: float = 2.0, max_patches_override: int = 0,

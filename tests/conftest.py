@@ -58,3 +58,33 @@ def assert_parity(got, want, atol=2e-2, cos_min=0.999, what=""):
     err, cos = close_stats(got, want)
     assert err <= atol and cos >= cos_min, f"{what}: max-abs {err:.3e} (<= {atol}), cosine {cos:.6f} (>= {cos_min})"
     return err, cos
+
+
+def fsq_codes_from_hidden(cfg, blobs, lm):
+    """The FSQ codes behind LM hidden states. An FSQ output is out_proj(codes / scale)
+    (+ bias) with integer codes, so least squares over out_proj's fsq_dim columns
+    recovers codes / scale; returns the rounded codes [rows][fsq_dim] and the largest
+    distance of the solution from those integers (near 0 for a real FSQ output)."""
+    from voxcpm2_b200.config import FSQ
+    H, Q = cfg.hidden, cfg.fsq_dim
+    b = np.asarray(blobs[FSQ], dtype=np.float16).astype(np.float64)
+    out_w = b[Q * H + Q: Q * H + Q + H * Q].reshape(H, Q)
+    out_b = b[Q * H + Q + H * Q: Q * H + Q + H * Q + H]
+    lm = np.atleast_2d(np.asarray(lm, np.float64))
+    sol, *_ = np.linalg.lstsq(out_w, (lm - out_b).T, rcond=None)
+    x = sol.T * cfg.fsq_scale
+    codes = np.rint(x)
+    return codes.astype(np.float32), float(np.abs(x - codes).max()) if x.size else 0.0
+
+
+def fsq_forced_disagreements(fsq_pre, codes):
+    """Codes that differ from the oracle's own rounding of its pre-rounding values:
+    [(patch, index, own code, forced code, distance of the value from the boundary
+    between the two codes)]."""
+    own = np.rint(fsq_pre[: codes.shape[0]])
+    out = []
+    for p, j in zip(*np.nonzero(own != codes)):
+        v, c = float(fsq_pre[p, j]), float(codes[p, j])
+        boundary = 0.5 * (float(own[p, j]) + c)
+        out.append((int(p), int(j), float(own[p, j]), c, abs(v - boundary)))
+    return out

@@ -1,0 +1,196 @@
+"""GPU parity at the benchmark configurations' own lengths, through the C ABI.
+
+- Base LM decode (24 layers): the KV cache prefilled from 256 random token ids,
+  then 200 one-token decode steps (KV 256 -> 456). Every step's output is held to
+  the oracle, and so is the final cache.
+- Residual decoder (8 layers): input = fusion_proj(LM hidden, feat_encoder(a
+  N(0,1) latent patch)); the cache grows from 256 to 512 rows over 256 steps.
+- The full synthesis loop: 64 random text tokens, min_patches 100, run until the
+  stop head decides (or the cap int(64 * 6 + 10) = 394): two lone streams at
+  once and one member of a stream group, each against the oracle's generate()
+  following the run's FSQ rounding at values that sit on a rounding boundary.
+
+The bar: per-step outputs and per-patch latents / hidden states within max-abs
+2e-2 and cosine >= 0.999; identical patch counts and stop decisions; cache rows
+within 1e-4 relative (tests/test_kvcache.cpp checks cache growth, src/kvcache.cpp:232-279
+grows it; src/synthesizer.cpp:584-586 is the stop rule, :216-220 the cap).
+"""
+from __future__ import annotations
+
+import threading
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import assert_parity, close_stats, fsq_codes_from_hidden, fsq_forced_disagreements
+from voxcpm2_b200 import synthetic
+from voxcpm2_b200.config import BENCH
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def rt():
+    from voxcpm2_b200 import runtime
+    return runtime
+
+
+@pytest.fixture(scope="module")
+def bench(rt):
+    blobs = synthetic.model_blobs(BENCH, 0)
+    dev = rt.Device(BENCH, 0, blobs)
+    yield BENCH, blobs, dev, oracle.Oracle(BENCH, blobs)
+    dev.close()
+
+
+def same_cache(s, orc, which, layers, rows):
+    for layer in (0, layers // 2, layers - 1):
+        gk, gv = s.read_cache(which, layer)
+        wk, wv = orc.read_cache(which, layer)
+        assert gk.shape == wk.shape == (BENCH.kv_heads, rows, BENCH.head_dim), layer
+        assert np.abs(gk - wk).max() <= 1e-4 * max(1.0, np.abs(wk).max()), f"K rows of layer {layer}"
+        assert np.abs(gv - wv).max() <= 1e-4 * max(1.0, np.abs(wv).max()), f"V rows of layer {layer}"
+
+
+def test_base_decoder_256_prefill_200_steps(rt, bench):
+    """Base LM decode step at its configuration: prefill 256 random token ids, then
+    200 decode steps on further random token embeddings (KV 256 -> 456)."""
+    cfg, blobs, dev, orc = bench
+    s = rt.Stream(dev, kv_capacity=512)
+    ids = synthetic.token_ids(cfg, 256 + 200, seed=202)
+    emb = orc.text_embed(ids)
+    orc.reset()
+    assert_parity(s.decoder_step(0, emb[:256]), orc.decoder_forward(0, emb[:256]), 2e-2, 0.999, "prefill of 256")
+    worst = (0.0, 1.0)
+    for step in range(200):
+        x = emb[256 + step: 257 + step]
+        err, cos = assert_parity(s.decoder_step(0, x), orc.decoder_forward(0, x), 2e-2, 0.999,
+                                 f"decode step {step} (KV {256 + step})")
+        worst = (max(worst[0], err), min(worst[1], cos))
+    print(f"base decoder, 200 steps: worst max-abs {worst[0]:.3e}, cosine {worst[1]:.6f}")
+    assert s.token_count(0) == orc.token_count(0) == 456
+    same_cache(s, orc, 0, cfg.base_layers, 456)
+    s.close()
+
+
+def test_residual_decoder_256_to_512(rt, bench):
+    """Residual decoder step at its configuration: the input is fusion_proj of an
+    LM hidden state and feat_encoder(latent N(0,1)); 256 rows prefilled, then 256
+    decode steps grow the cache to 512."""
+    cfg, blobs, dev, orc = bench
+    s = rt.Stream(dev, kv_capacity=512)
+    rng = np.random.default_rng(303)
+    lm = rng.standard_normal((512, cfg.hidden), dtype=np.float32)
+    lat = rng.standard_normal((512, cfg.latent), dtype=np.float32)
+    x = np.stack([orc.fusion_proj(lm[i], orc.feat_encoder(lat[i]))[0] for i in range(512)])
+    orc.reset()
+    assert_parity(s.decoder_step(1, x[:256]), orc.decoder_forward(1, x[:256]), 2e-2, 0.999, "prefill of 256")
+    worst = (0.0, 1.0)
+    for step in range(256):
+        xi = x[256 + step: 257 + step]
+        err, cos = assert_parity(s.decoder_step(1, xi), orc.decoder_forward(1, xi), 2e-2, 0.999,
+                                 f"decode step {step} (KV {256 + step})")
+        worst = (max(worst[0], err), min(worst[1], cos))
+    print(f"residual decoder, 256 steps: worst max-abs {worst[0]:.3e}, cosine {worst[1]:.6f}")
+    assert s.token_count(1) == orc.token_count(1) == 512
+    same_cache(s, orc, 1, cfg.res_layers, 512)
+    s.close()
+
+
+def compare_utterance(got, want, what, min_patches=100):
+    """Identical patch count and stop decisions; every per-patch latent (and hidden
+    state, where the run traced them) within max-abs 2e-2 and cosine >= 0.999."""
+    n = want["patches"]
+    assert got["patches"] == n, f"{what}: {got['patches']} patches, the oracle ran {n}"
+    worst = {}
+    for key in ("latents", "lm_hidden", "res_hidden"):
+        if key in got:
+            stats = [close_stats(got[key][i], want[key][i]) for i in range(n)]
+            worst[key] = (max(x[0] for x in stats), min(x[1] for x in stats))
+    print(f"{what}: {n} patches, worst {worst}")
+    for key, (err, cos) in worst.items():
+        assert err <= 2e-2 and cos >= 0.999, f"{what}: {key} max-abs {err:.3e}, cosine {cos:.6f}"
+    if "stop_logits" in got:
+        dg = [bool(l[1] > l[0]) for l in got["stop_logits"][:n]]
+        dw = [bool(l[1] > l[0]) for l in want["stop_logits"][:n]]
+        assert dg[min_patches + 1:] == dw[min_patches + 1:], f"{what}: stop decisions differ"
+
+
+def oracle_following_fsq(orc, cfg, blobs, ids, got, what):
+    """The oracle's run of the same utterance, following the GPU run's FSQ rounding.
+
+    FSQ rounds tanh(z) * 9 to integers. A value that lands within float rounding of a
+    half-integer can round one way on the GPU and the other on the CPU; from that
+    patch on the two trajectories are different utterances, and no pair of float
+    implementations avoids it over hundreds of thousands of roundings. So the GPU's
+    codes are recovered from its LM hidden states, the oracle is run with those
+    codes, and every code where the two roundings differ must be a +-1 step across
+    a boundary the oracle's own value sits within 2e-3 of (codes are spaced 1 apart).
+    Everything else (latents, hidden states, stop decisions, patch count) is then
+    compared over the whole utterance."""
+    n = got["patches"]
+    codes, resid = fsq_codes_from_hidden(cfg, blobs, got["lm_hidden"][1:n])
+    assert resid < 1e-2, f"{what}: the GPU's LM states are not FSQ outputs (distance {resid:.3e})"
+    want = orc.generate(ids, min_patches=100, timesteps=10, cfg_value=2.0, seed=0, fsq_codes=codes)
+    dis = fsq_forced_disagreements(want["fsq_pre"], codes)
+    print(f"{what}: {len(dis)} of {codes.size} FSQ codes rounded the other way on the GPU: "
+          + ", ".join(f"patch {p} code {j} ({own:+.0f} -> {c:+.0f}, {d:.1e} from the boundary)"
+                      for p, j, own, c, d in dis))
+    for p, j, own, c, d in dis:
+        assert abs(own - c) == 1.0 and d < 2e-3, f"{what}: patch {p} code {j}: {own} vs {c}, {d:.3e} from a boundary"
+    assert len(dis) <= max(1, codes.size // 1000), f"{what}: {len(dis)} codes differ"
+    return want
+
+
+def test_full_utterance_until_stop(rt, bench):
+    """The full loop at its configuration (64 random text tokens, min_patches 100,
+    10 timesteps, cfg 2.0) run until the stop rule or the cap, on two lone streams
+    at once and on member 0 of a two-member stream group (member 1 another prompt),
+    each against the oracle following that run's FSQ rounding (oracle_following_fsq)."""
+    cfg, blobs, dev, orc = bench
+    ids = synthetic.token_ids(cfg, 64, seed=1)
+    streams = [rt.Stream(dev, kv_capacity=512) for _ in range(2)]
+    got = [None, None]
+    errors = []
+
+    def run(i):
+        try:
+            got[i] = streams[i].generate(ids, min_patches=100, timesteps=10, cfg_value=2.0, seed=0)
+        except Exception as e:  # reported on the main thread
+            errors.append(e)
+
+    threads = [threading.Thread(target=run, args=(i,)) for i in range(2)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert not errors, errors
+    for st in streams:
+        st.close()
+    assert got[0]["patches"] >= 102
+    # concurrent streams do not disturb each other: bit-identical runs
+    assert got[0]["patches"] == got[1]["patches"] and np.array_equal(got[0]["latents"], got[1]["latents"])
+    want = oracle_following_fsq(orc, cfg, blobs, ids, got[0], "lone streams")
+    gaps = want["stop_logits"][:, 1] - want["stop_logits"][:, 0]
+    print(f"stop margin at the decisions after min_patches: min {np.abs(gaps[101:]).min():.3e}")
+    compare_utterance(got[0], want, "lone streams")
+
+    cap = 394
+    g = rt.Group(dev, 2, kv_capacity=512)
+    g.streams[0].prefill(ids)
+    g.streams[0].upload_noise(oracle.noise_table(0, cap, cfg.latent))
+    g.streams[1].prefill(synthetic.token_ids(cfg, 40, seed=77))
+    g.streams[1].upload_noise(oracle.noise_table(77, cap, cfg.latent))
+    lm_trace = []
+    for step in range(cap):
+        lm_trace.append(g.streams[0].hidden()[0])  # the LM state entering this patch
+        g.patch_step_async(100, 2.0, 10)
+        g.synchronize()
+        if g.streams[0].state().stopped:
+            break
+    n = len(lm_trace)
+    member = {"patches": n, "latents": g.streams[0].latents(0, n), "lm_hidden": np.stack(lm_trace)}
+    g.close()
+    want_g = oracle_following_fsq(orc, cfg, blobs, ids, member, "group member 0")
+    compare_utterance(member, want_g, "group member 0")

@@ -82,6 +82,45 @@ def test_sdpa_rows_masked(rt, past, src, per_head):
     assert np.abs(got - want).max() <= 1e-5
 
 
+@pytest.mark.parametrize("G", [1, 3, 5, 16])
+@pytest.mark.parametrize("past", [700, 1500])
+@pytest.mark.parametrize("masked", [False, True])
+def test_sdpa_split_path_head_groups(rt, G, past, masked):
+    """One query row over more than 512 keys takes the split-K flash decode, whose
+    CTAs spread a KV group's G query heads over four thread groups: G = 1 and 3
+    leave thread groups without a head, 5 and 16 give them uneven counts. Held to
+    the oracle at the reference test's 1e-5, with and without an additive mask."""
+    rng = np.random.default_rng(1000 * G + past + masked)
+    groups, d = 2, 64
+    heads = G * groups
+    q = rng.standard_normal((heads, 1, d), dtype=np.float32)
+    k = rng.standard_normal((groups, 1, d), dtype=np.float32)
+    v = rng.standard_normal((groups, 1, d), dtype=np.float32)
+    pk = rng.standard_normal((groups, past, d), dtype=np.float32)
+    pv = rng.standard_normal((groups, past, d), dtype=np.float32)
+    mask = (rng.standard_normal((1, past + 1)) * 2.0).astype(np.float32) if masked else None
+    want, wk, wv = oracle.sdpa(q, k, v, mask, pk, pv, 0.125, want_cache=True)
+    got, gk, gv = rt.sdpa(q, k, v, mask, pk, pv, 0.125, want_cache=True)
+    assert np.abs(got - want).max() <= 1e-5
+    assert np.array_equal(gk, wk) and np.array_equal(gv, wv)
+
+
+def test_timestep_embedding_known_answer(rt, kat):
+    """tests/test_voxcpm2_timestep_embedding.cpp:165-170: the layer's raw mode on
+    t = {0.70710677, 0.25} and schedule mode on (step 1, 10 timesteps), both at 1e-6
+    (half_dim 512, scale 1000, max_period 10000)."""
+    raw = rt.timestep_embedding(kat["ts_raw_in"], 512, 1000.0, 10000.0, 0)
+    assert raw.shape == kat["ts_raw_out"].shape
+    assert np.abs(raw - kat["ts_raw_out"]).max() <= 1e-6
+    sched = rt.timestep_embedding(kat["ts_sched_in"], 512, 1000.0, 10000.0, 1)
+    assert np.abs(sched - kat["ts_sched_out"]).max() <= 1e-6
+    # every step of a 10-step schedule, against the oracle
+    for step in range(10):
+        inp = np.array([step, 10], np.float32)
+        want = oracle.timestep_embedding(inp, 512, 1000.0, 10000.0, 1)
+        assert np.abs(rt.timestep_embedding(inp, 512, 1000.0, 10000.0, 1) - want).max() <= 1e-6, step
+
+
 def test_kvcache_toy_decoder(rt, kat):
     """tests/test_kvcache.cpp: two cached SDPA layers, prefill 2 then 2 decode steps."""
     caches = [(None, None), (None, None)]

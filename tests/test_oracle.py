@@ -211,3 +211,29 @@ def test_generate_rows_audio_prefix(tiny_blobs):
     assert not np.allclose(a["lm_hidden"][0], text["lm_hidden"][0])
     with pytest.raises(ValueError):
         o.generate_rows(rows, flags, None, ids.size, max_patches_override=2)  # audio rows without latents
+
+
+def test_fsq_trace_and_forced_codes_reproduce_the_loop():
+    """The FSQ test hooks: the codes recovered from the traced LM hidden states are
+    the oracle's own rounding of its traced pre-rounding values, and forcing those
+    codes back reproduces the loop bit for bit; forcing one other code changes the
+    patches after it."""
+    from conftest import fsq_codes_from_hidden, fsq_forced_disagreements
+    from voxcpm2_b200 import synthetic
+    blobs = synthetic.model_blobs(TINY, 0)
+    orc = oracle.Oracle(TINY, blobs)
+    ids = synthetic.token_ids(TINY, 8, seed=3)
+    a = orc.generate(ids, min_patches=100, timesteps=4, cfg_value=2.0, max_patches_override=8, seed=1)
+    codes, resid = fsq_codes_from_hidden(TINY, blobs, a["lm_hidden"][1:])
+    assert resid < 1e-3
+    assert np.array_equal(codes, np.rint(a["fsq_pre"][:7]))
+    b = orc.generate(ids, min_patches=100, timesteps=4, cfg_value=2.0, max_patches_override=8, seed=1, fsq_codes=codes)
+    assert np.array_equal(a["latents"], b["latents"]) and np.array_equal(a["lm_hidden"], b["lm_hidden"])
+    assert fsq_forced_disagreements(b["fsq_pre"], codes) == []
+    other = codes[:3].copy()  # patches 3 on round their own values
+    other[2, 5] += 1.0
+    c = orc.generate(ids, min_patches=100, timesteps=4, cfg_value=2.0, max_patches_override=8, seed=1, fsq_codes=other)
+    # the FSQ of patch 2 makes the LM state entering patch 3
+    assert np.array_equal(a["latents"][:3], c["latents"][:3]) and not np.array_equal(a["latents"][3], c["latents"][3])
+    d = fsq_forced_disagreements(c["fsq_pre"], other)
+    assert len(d) == 1 and d[0][:4] == (2, 5, codes[2, 5], codes[2, 5] + 1.0)

@@ -476,8 +476,6 @@ __global__ void __launch_bounds__(kEmbedThreads) dit_embed_kernel(const DitEmbed
         }
     }
     pdl_wait();
-    if (a.sync_reset && blockIdx.x == 0)
-        for (int i = threadIdx.x; i < a.sync_words; i += kEmbedThreads) a.sync_reset[i] = 0u;
     if (a.ctl && a.ctl->stopped) return;
     for (int i = threadIdx.x; i < DP; i += kEmbedThreads) {
         xs[i] = a.x[i];
@@ -537,25 +535,24 @@ __global__ void vec_add_kernel(const float* a, const float* b, float* out, int n
     if (i < n) out[i] = a[i] + b[i];
 }
 
-__global__ void timestep_embedding_kernel(float t_or_step, float timesteps, int schedule,
+// Sinusoidal timestep embedding rows [sin(t f_i) | cos(t f_i)]
+// (VoxCPM2TimestepEmbedding::forward, timestep_embedding.cpp:128-160). The
+// frequencies f_i = exp(-ln(max_period) i / (half - 1)) and the scaled t of every
+// row (schedule mode's t(step, T) included) come from the host, computed in float
+// with the C library as the layer does, so the only device rounding left is one
+// fp32 product and sinf / cosf. t_rows: one t per row in device memory, or null
+// for a single row of value t_val.
+__global__ void timestep_embedding_kernel(const float* t_rows, float t_val, int rows, const float* freq,
                                           int half_dim, float* out, StreamCtl* ctl) {
     pdl_launch_dependents();
     pdl_wait();
     if (ctl && ctl->stopped) return;
-    // VoxCPM2TimestepEmbedding::forward (timestep_embedding.cpp:128-160)
-    constexpr float kPi = 3.14159265358979323846f;
-    float t = t_or_step;
-    if (schedule) {
-        const float u = 1.0f - t_or_step / fmaxf(timesteps, 1.0f);
-        t = u + (cosf(kPi * 0.5f * u) - 1.0f + u);
-    }
-    t *= 1000.0f;
-    const float log_period = logf(10000.0f);
-    for (int i = threadIdx.x; i < half_dim; i += blockDim.x) {
-        const float inv_freq = expf(-log_period * static_cast<float>(i) / static_cast<float>(half_dim - 1));
-        const float phase = t * inv_freq;
-        out[i] = sinf(phase);
-        out[i + half_dim] = cosf(phase);
+    for (int u = blockIdx.x * blockDim.x + threadIdx.x; u < rows * half_dim; u += gridDim.x * blockDim.x) {
+        const int r = u / half_dim, i = u - r * half_dim;
+        const float t = t_rows ? t_rows[r] : t_val;
+        const float phase = t * freq[i];
+        out[static_cast<size_t>(r) * 2 * half_dim + i] = sinf(phase);
+        out[static_cast<size_t>(r) * 2 * half_dim + half_dim + i] = cosf(phase);
     }
 }
 
@@ -951,12 +948,13 @@ void launch_vec_add(const float* a, const float* b, float* out, int n, cudaStrea
     check_launch(cudaGetLastError());
 }
 
-void launch_timestep_embedding(float t_or_step, float timesteps, int schedule, int half_dim,
+void launch_timestep_embedding(const float* t_rows, float t_val, int rows, const float* freq, int half_dim,
                                float* out, StreamCtl* ctl, cudaStream_t s, bool pdl) {
+    if (rows <= 0 || half_dim <= 0 || !freq || !out) throw std::invalid_argument("timestep embedding: bad shape");
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = make_cfg(dim3(1), dim3(256), 0, s, pdl, attr);
-    check_launch(cudaLaunchKernelEx(&cfg, timestep_embedding_kernel, t_or_step, timesteps, schedule,
-                                    half_dim, out, ctl));
+    const int blocks = std::min(148, (rows * half_dim + 255) / 256);
+    cudaLaunchConfig_t cfg = make_cfg(dim3(blocks), dim3(256), 0, s, pdl, attr);
+    check_launch(cudaLaunchKernelEx(&cfg, timestep_embedding_kernel, t_rows, t_val, rows, freq, half_dim, out, ctl));
 }
 
 void launch_dit_out(const DitOutArgs& a, cudaStream_t s, bool pdl) {

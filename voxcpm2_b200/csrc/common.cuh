@@ -18,6 +18,39 @@ __device__ __forceinline__ void pdl_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Every mbarrier wait in these kernels gives up after this much wall time
+// (%globaltimer, nanoseconds) and reports failure instead of waiting on: a pipeline
+// wait normally completes within microseconds, so a wait that outlives one second
+// means a copy or MMA that never arrives.
+constexpr uint64_t kWaitNs = 1000000000ull;
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Wait for phase 'parity' of the shared-memory mbarrier at 'addr' (a shared-window
+// address); false if kWaitNs passed first. mbarrier.try_wait itself suspends the
+// thread for a hardware-chosen time before it returns false, so the clock is read
+// only between unsuccessful tries.
+__device__ __forceinline__ bool mbar_wait_addr(uint32_t addr, uint32_t parity) {
+    uint64_t start = 0;
+    for (uint32_t i = 0;; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(addr), "r"(parity)
+            : "memory");
+        if (done) return true;
+        const uint64_t now = global_ns();
+        if (i == 0) start = now;
+        else if (now - start > kWaitNs) return false;
+    }
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -387,21 +387,9 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
-// Bounded wait for phase 0 of a one-shot mbarrier; false on timeout.
+// Time-bounded wait (kWaitNs) for phase 0 of a one-shot mbarrier; false on timeout.
 __device__ __forceinline__ bool bulk_wait(uint64_t* bar) {
-    const uint32_t addr = static_cast<uint32_t>(__cvta_generic_to_shared(bar));
-    for (uint32_t i = 0; i < (1u << 22); ++i) {
-        uint32_t done;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(done)
-            : "r"(addr)
-            : "memory");
-        if (done) return true;
-    }
-    return false;
+    return mbar_wait_addr(static_cast<uint32_t>(__cvta_generic_to_shared(bar)), 0);
 }
 
 // Weight rows per output unit: gate + up, or the two rows of a RoPE pair.
@@ -1085,7 +1073,6 @@ void init_kernel_attributes() {
         check_launch(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kBulkSmemMax)));
     init_batched_attributes();
     init_tc_attributes();
-    init_dit_layers_attributes();
     init_tc_rows_attributes();
     init_tc_wide_attributes();
 }

@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <vector>
+
 #include "common.cuh"
 
 namespace vxc {
@@ -207,8 +209,6 @@ struct DitEmbedArgs {
     const float* cond_uncond;// [D*P] of CFG row 1, or null (same as cond)
     const float* tsum;       // [Hd] precomputed t_tok + dt_tok of both CFG rows, or null
     float* ssq_out;          // or null: per 32-feature block, row sums of squares [block][24]
-    unsigned* sync_reset;    // or null: words zeroed by block 0 (the next persistent launch's sync block)
-    int sync_words;
     // group members (grid y = member, 0 = none): member m replaces x, cond, mu and ctl,
     // and writes hidden + m * member_stride
     int members;
@@ -220,10 +220,14 @@ struct DitEmbedArgs {
 };
 void launch_dit_embed(const DitEmbedArgs& a, cudaStream_t s, bool pdl);
 
-// sinusoidal timestep embedding of one value (VoxCPM2TimestepEmbedding):
-// schedule != 0 derives t from (step_index, timesteps) like schedule mode 1.
-void launch_timestep_embedding(float t_or_step, float timesteps, int schedule, int half_dim,
+// sinusoidal timestep embedding rows (VoxCPM2TimestepEmbedding): t_rows[r] (or
+// t_val for one row when t_rows is null) times the host-computed frequencies
+// freq[half_dim]; out [rows][2 * half_dim].
+void launch_timestep_embedding(const float* t_rows, float t_val, int rows, const float* freq, int half_dim,
                                float* out, StreamCtl* ctl, cudaStream_t s, bool pdl);
+// the layer's host-side arithmetic (timestep_embedding.cpp:137-152), in float as the layer does it
+float timestep_scheduled_t(float step_index, float timesteps);
+std::vector<float> timestep_frequencies(int half_dim, float max_period);
 
 struct DitOutArgs {
     const float* hidden;    // [2][seq][Hd] pre-final-norm residual stream
@@ -288,28 +292,13 @@ struct TcLinearArgs {
     __half* yb = nullptr;  // GATEUP: split-fp16 [48][ldyb], the next linear's B operand
     int ldyb = 0;
     StreamCtl* ctl = nullptr;  // receives error 3 if a bounded wait gave up
-    // Where the B operand (the token rows) comes from:
-    //   TC_B_TMA:  TMA loads of a split-fp16 [48][K] buffer (map_b);
-    //   TC_B_NORM: RMSNorm of fp32 rows x [M][ldx] with weight g, built in shared
-    //              memory; the rows' sums of squares come as ssq_parts partial sums
-    //              ssq_in [part][24] written by the kernel that produced x;
-    //   TC_B_ATTN: per-head attention (RoPE, softmax, P.V) over the fp32 q/k/v
-    //              rows qkv [M][(q_heads + 2 kv_heads) * 64] of 2 sequences of
-    //              'seq' tokens, built in shared memory (K = q_heads * 64).
-    int bmode = 0;
-    const float* x = nullptr;
-    int ldx = 0;
-    const __half* g = nullptr;
+    // The B operand (the token rows) comes by TMA from a split-fp16 [48][K] buffer (map_b).
+    // row_scale: the producer's per-slice sums of squares of the rows, ssq_parts parts
+    // of ssq_in [part][24], and the RMSNorm eps
     float eps = 0.f;
     const float* ssq_in = nullptr;
     int ssq_parts = 0;
-    const float* qkv = nullptr;
-    int q_heads = 0, kv_heads = 0, seq = 0;
-    const float* rope_cos = nullptr;  // [seq][64]
-    const float* rope_sin = nullptr;
-    float scale = 1.f;
-    int attn_round = 2;  // heads computed together (scratch: ~20 KB each); see tc_attn_round
-    int max_stages = 8;  // shared-memory ring depth (1..8); fused token tiles need one stage per K chunk
+    int max_stages = 8;  // shared-memory ring depth (1..8)
     // residual epilogue: partial sums of squares of the updated rows, one part per
     // (tile, owner CTA) = tile * splits + rank, written to ssq_out [part][24]
     float* ssq_out = nullptr;
@@ -328,13 +317,9 @@ struct TcLinearArgs {
     // dedicated buffer behind it (smaller CTAs, more of them per SM)
     int recv_shared = 0;
 };
-enum { TC_B_TMA = 0, TC_B_NORM = 1, TC_B_ATTN = 2 };
 constexpr int kSsqStride = 24;  // floats per part in a sums-of-squares buffer
 CUtensorMap make_tensor_map_f16(const void* base, int rows, int cols, int box_rows);
-size_t tc_linear_smem_bytes(int K, int splits, int bmode, int attn_round = 1, int max_stages = 8,
-                            bool ssq_out = false, bool recv_shared = false);
-// heads per attention round that fit beside the stages of a TC_B_ATTN launch (2, else 1)
-int tc_attn_round(int K, int splits, int max_stages = 8);
+size_t tc_linear_smem_bytes(int K, int splits, int max_stages = 8, bool ssq_out = false, bool recv_shared = false);
 void launch_tc_linear(const CUtensorMap& map_a, const CUtensorMap& map_b, const TcLinearArgs& a, cudaStream_t s,
                       bool pdl);
 void init_tc_attributes();
@@ -383,31 +368,6 @@ struct TcWideArgs {
 void launch_tc_wide(const CUtensorMap& map_a, const CUtensorMap& map_b, const TcWideArgs& a, cudaStream_t s,
                     bool pdl);
 void init_tc_wide_attributes();
-
-// Persistent DiT decoder (all layers of one estimator evaluation, one
-// cooperative launch, one CTA per SM; dit_persist.cu).
-struct DitLayersArgs {
-    const CUtensorMap* maps;     // [layers][4] weight maps in device memory: q/k/v, o, gate|up, down
-    const __half* const* norms;  // [layers][2] device array: input and post-attention RMSNorm weights
-    int layers = 0, Hd = 0, F = 0, hq = 0, hkv = 0, seq = 0, M = 0;
-    float eps = 0.f, rscale = 1.f, scale = 1.f;
-    const float* rope_cos = nullptr;  // [seq][64]
-    const float* rope_sin = nullptr;
-    float* dh = nullptr;         // [M][Hd] residual stream, in and out
-    float* ssq = nullptr;        // [>= grid][24] per-slice row sums of squares of dh
-    int embed_parts = 0;         // slices dit_embed left in ssq for layer 0's input RMSNorm
-    float* qkv = nullptr;        // [M][(hq + 2 hkv) * 64]
-    __half* act = nullptr;       // [48][F] split-fp16 SiLU(gate) * up (pad rows zero)
-    float* part = nullptr;       // dit_layers_part_floats(grid)
-    unsigned* sync = nullptr;    // dit_layers_sync_words() words, zero at launch
-    StreamCtl* ctl = nullptr;    // receives error 3 if a bounded wait gave up
-};
-int dit_layers_grid();                       // CTAs of one launch (one per SM)
-size_t dit_layers_part_floats(int grid);
-int dit_layers_sync_words();
-void check_dit_layers(const DitLayersArgs& a, int grid);  // throws std::invalid_argument if unsupported
-void launch_dit_layers(const DitLayersArgs& a, int grid, cudaStream_t s);
-void init_dit_layers_attributes();
 
 // Raise the dynamic shared-memory limit of the kernels that need more than 48 KB
 // (call once per device, outside stream capture).

@@ -29,6 +29,27 @@
 
 using namespace vxc;
 
+namespace vxc {
+
+// VoxCPM2TimestepEmbedding's host arithmetic, in float with the C library as the
+// layer computes it (timestep_embedding.cpp:141-152): schedule mode's t from
+// (step_index, timesteps), and the frequencies exp(-ln(max_period) i / (half - 1)).
+float timestep_scheduled_t(float step_index, float timesteps) {
+    constexpr float kPi = 3.14159265358979323846f;
+    const float u = 1.0f - step_index / std::max(timesteps, 1.0f);
+    return u + (std::cos(kPi * 0.5f * u) - 1.0f + u);
+}
+
+std::vector<float> timestep_frequencies(int half_dim, float max_period) {
+    const float log_period = std::log(max_period);
+    std::vector<float> f(static_cast<size_t>(half_dim));
+    for (int i = 0; i < half_dim; ++i)
+        f[i] = std::exp(-log_period * static_cast<float>(i) / static_cast<float>(half_dim - 1));
+    return f;
+}
+
+}  // namespace vxc
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -278,12 +299,11 @@ struct vxc_device {
     std::vector<LayerW> base, res, dit;
     const __half *base_norm = nullptr, *res_norm = nullptr, *dit_norm = nullptr;
     float *dit_rope_cos = nullptr, *dit_rope_sin = nullptr;  // positions 0..seq-1
+    float* temb_freq = nullptr;  // the DiT timestep embedding's frequencies [dit_hidden / 2]
     // per DiT layer: TMA maps of W_qkv, W_o, W_gate|up, W_down (A operands)
     std::vector<std::array<CUtensorMap, 4>> dit_maps;
     // per decoder layer: TMA maps of W_qkv, W_o, W_gate|up, W_down for the prefill's row-block linears
     std::vector<std::array<CUtensorMap, 4>> base_maps, res_maps;
-    CUtensorMap* dit_maps_dev = nullptr;       // the same maps in device memory (persistent DiT kernel)
-    const __half** dit_norms_dev = nullptr;    // [layers][2] input / post-attention RMSNorm weights
     uint64_t epoch = 0;  // bumped by every weight upload (invalidates derived tables)
 };
 
@@ -381,10 +401,6 @@ struct vxc_stream {
     std::map<int, TimeTable> ttab;
     float* dest = nullptr;  // [2][D*P] estimator output scratch of dit_out
     float* dssq = nullptr;  // [parts][24] row sums of squares of s->dh, by slice
-    // DiT decoder form: 0 persistent (one cooperative launch per evaluation), 1 fused (4 tcgen05
-    // launches per layer), 2 split (7 launches per layer: RMSNorm and attention as their own kernels)
-    int dit_form = 0;
-    int dit_grid = 0;           // CTAs of the persistent launch
     // ring depth of the per-layer tensor-core launches (VXC_TC_STAGES): a shallow ring keeps a
     // CTA's shared memory small, so linears of several concurrent streams share an SM
     int tc_stages = 2;
@@ -403,8 +419,6 @@ struct vxc_stream {
     // VXC_BULK_GEMV=1 for the bulk-copy form (weight rows into shared memory before the
     // dependency wait; stream groups always use it, batched over their members)
     bool bulk_gemv = false;
-    float* dpart = nullptr;     // persistent launch: partial tiles
-    unsigned* dsync = nullptr;  // persistent launch: grid barrier and tile counters
     int* dcount = nullptr;  // dit_out arrival counter
     cudaGraphExec_t graph = nullptr;
     int graph_kernels = 0;
@@ -431,10 +445,8 @@ void free_all(vxc_stream* s) {
         if (kv.second.dev) cudaFree(kv.second.dev);
     if (s->dest) cudaFree(s->dest);
     if (s->dssq) cudaFree(s->dssq);
-    if (s->dpart) cudaFree(s->dpart);
     for (__half* p : {s->xr_n, s->xr_a, s->xr_act})
         if (p) cudaFree(p);
-    if (s->dsync) cudaFree(s->dsync);
     if (s->dcount) cudaFree(s->dcount);
     if (s->ctl_host) cudaFreeHost(s->ctl_host);
     if (s->pin) cudaFreeHost(s->pin);
@@ -612,118 +624,43 @@ int choose_splits(int tiles, int k, int target = 148) {
 
 // The tensor-core kernels split K over 1, 2, 4 or 8 CTAs.
 int pow2_floor(int v) { return v >= 8 ? 8 : v >= 4 ? 4 : v >= 2 ? 2 : 1; }
-int pow2_ceil(int v) { return v <= 1 ? 1 : v <= 2 ? 2 : v <= 4 ? 4 : 8; }
 
-// K split and ring depth of one tensor-core launch: about one CTA per SM, and
-// with an operand built in shared memory (fused) one stage per K chunk.
-TcLinearArgs tc_plan(const vxc_stream* s, int tiles, int K, bool fused_b) {
+// K split and ring depth of one tensor-core launch: about tc_target CTAs per launch.
+TcLinearArgs tc_plan(const vxc_stream* s, int tiles, int K) {
     TcLinearArgs a;
-    const int nch = K / 64;
     a.splits = pow2_floor(choose_splits(tiles, K, s->tc_target));
     a.max_stages = s->tc_stages;
     a.recv_shared = s->recv_shared ? 1 : 0;
-    if (fused_b)
-        a.splits = std::min(pow2_floor(std::min(8, nch)),
-                            pow2_ceil(std::max(a.splits, (nch + a.max_stages - 1) / a.max_stages)));
     return a;
 }
 
 // DiT decoder over the 2 x seq rows in s->dh (DitEstimator.decoder,
-// export_components.py:625-659), the four linears of each layer on tcgen05.
-// Fused form (4 launches per layer): each linear builds its token operand in
-// shared memory: q/k/v and gate/up from RMSNorm(dh) (row sums of squares left
-// by the kernel that last wrote dh), o from the attention over the q/k/v rows.
-// Shapes whose per-CTA K range exceeds 8 chunks take the 7-launch form with
-// separate RMSNorm and attention kernels.
-bool dit_fused_ok(const vxc_model_desc& d) {
-    const int Hd = d.dit_hidden, hq = d.dit_q_heads, hkv = d.dit_kv_heads;
-    const int seq = dit_tokens_per_seq(d.patch_size);
-    const int W = (hq + 2 * hkv) * (Hd / hq);
-    auto fits = [](int k, int splits) { return (k / 64 + splits - 1) / splits <= 8; };
-    return Hd / hq == 64 && seq <= 12 && hkv > 0 && hq % hkv == 0 &&
-           fits(Hd, choose_splits(W / 128, Hd)) && fits(Hd, choose_splits(d.dit_ffn / 64, Hd)) &&
-           fits(hq * 64, choose_splits(Hd / 128, hq * 64));
-}
-
-DitLayersArgs dit_layers_shape(const vxc_model_desc& d) {
-    DitLayersArgs a;
-    a.layers = d.dit_layers;
-    a.Hd = d.dit_hidden;
-    a.F = d.dit_ffn;
-    a.hq = d.dit_q_heads;
-    a.hkv = d.dit_kv_heads;
-    a.seq = dit_tokens_per_seq(d.patch_size);
-    a.M = 2 * a.seq;
-    a.eps = d.rms_eps;
-    a.rscale = d.dit_residual_scale;
-    a.scale = 1.0f / std::sqrt(static_cast<float>(d.dit_hidden / d.dit_q_heads));
-    return a;
-}
-
-bool dit_persistent_ok(const vxc_model_desc& d, int grid) {
-    try {
-        check_dit_layers(dit_layers_shape(d), grid);
-        return d.dit_hidden / d.dit_q_heads == 64;
-    } catch (const std::invalid_argument&) {
-        return false;
-    }
-}
-
-DitLayersArgs dit_layers_args(vxc_stream* s, StreamCtl* ctl) {
-    const vxc_device* dev = s->dev;
-    DitLayersArgs a = dit_layers_shape(dev->desc);
-    a.maps = dev->dit_maps_dev;
-    a.norms = dev->dit_norms_dev;
-    a.rope_cos = dev->dit_rope_cos;
-    a.rope_sin = dev->dit_rope_sin;
-    a.dh = s->dh;
-    a.ssq = s->dssq;
-    a.embed_parts = (a.Hd + 31) / 32;
-    a.qkv = s->dqkv;
-    a.act = s->xb_act;
-    a.part = s->dpart;
-    a.sync = s->dsync;
-    a.ctl = ctl;
-    for (const LayerW& L : dev->dit)  // the operand builders read the norm weights 4 at a time
-        if ((reinterpret_cast<uintptr_t>(L.in_norm) | reinterpret_cast<uintptr_t>(L.post_norm)) & 7)
-            throw std::invalid_argument("dit_layers: RMSNorm weights must be 8-byte aligned");
-    return a;
-}
-
+// export_components.py:625-659): per layer the four linears on tcgen05 and the
+// attention on CUDA cores. RMSNorm is folded into the linears: the residual
+// epilogues of o and down also write the next linear's split-fp16 operand of
+// dh * gain and per-slice sums of squares, and the consumer scales each token
+// row by 1 / rms (W (x g / rms) = (1 / rms) W (x g)); layer 0 (after the
+// embedding) and VXC_NORM_KERNELS=1 launch separate RMSNorm kernels instead.
 void enqueue_dit_layers(vxc_stream* s, StreamCtl* ctl) {
     const vxc_device* dev = s->dev;
     const vxc_model_desc& d = dev->desc;
     const int Hd = d.dit_hidden, F = d.dit_ffn, hq = d.dit_q_heads, hkv = d.dit_kv_heads, hd = Hd / hq;
     const int seq = dit_tokens_per_seq(d.patch_size), M = 2 * seq;
     const int W = (hq + 2 * hkv) * hd;
-    if (s->dit_form == 0) {
-        DitLayersArgs a = dit_layers_args(s, ctl);
-        launch_dit_layers(a, s->dit_grid, s->cs);
-        return;
-    }
-    const bool fused = s->dit_form == 1;
     const float scale = 1.0f / std::sqrt(static_cast<float>(hd));
     // sums-of-squares parts of s->dh: dit_embed leaves one per 32 features
     int parts = (Hd + 31) / 32;
     for (size_t l = 0; l < dev->dit.size(); ++l) {
         const LayerW& L = dev->dit[l];
         const std::array<CUtensorMap, 4>& maps = dev->dit_maps[l];
-        TcLinearArgs qa = tc_plan(s, W / 128, Hd, fused);
+        TcLinearArgs qa = tc_plan(s, W / 128, Hd);
         qa.K = Hd;
         qa.M = M;
         qa.rows = W;
         qa.y = s->dqkv;
         qa.ldy = W;
         qa.ctl = ctl;
-        if (fused) {
-            qa.bmode = TC_B_NORM;
-            qa.x = s->dh;
-            qa.ldx = Hd;
-            qa.g = L.in_norm;
-            qa.eps = d.rms_eps;
-            qa.ssq_in = s->dssq;
-            qa.ssq_parts = parts;
-        } else if (l == 0 || s->norm_kernels) {
+        if (l == 0 || s->norm_kernels) {
             launch_rmsnorm_rows_split(s->dh, Hd, L.in_norm, d.rms_eps, Hd, M, s->xb_n, ctl, s->cs, s->pdl);
         } else {  // the previous down projection left split(dh * in_norm) and its sums of squares
             qa.row_scale = 1;
@@ -732,7 +669,7 @@ void enqueue_dit_layers(vxc_stream* s, StreamCtl* ctl) {
             qa.eps = d.rms_eps;
         }
         launch_tc_linear(maps[0], s->map_xb_n, qa, s->cs, s->pdl);
-        TcLinearArgs oa = tc_plan(s, Hd / 128, hq * hd, fused);
+        TcLinearArgs oa = tc_plan(s, Hd / 128, hq * hd);
         oa.K = hq * hd;
         oa.M = M;
         oa.rows = Hd;
@@ -741,31 +678,18 @@ void enqueue_dit_layers(vxc_stream* s, StreamCtl* ctl) {
         oa.y = s->dh;
         oa.ldy = Hd;
         oa.ctl = ctl;
-        if (fused) {
-            oa.bmode = TC_B_ATTN;
-            oa.qkv = s->dqkv;
-            oa.q_heads = hq;
-            oa.kv_heads = hkv;
-            oa.seq = seq;
-            oa.rope_cos = dev->dit_rope_cos;
-            oa.rope_sin = dev->dit_rope_sin;
-            oa.scale = scale;
-            oa.attn_round = tc_attn_round(oa.K, oa.splits, oa.max_stages);
+        launch_dit_attention_split(s->dqkv, 2, seq, hq, hkv, hd, dev->dit_rope_cos, dev->dit_rope_sin, scale,
+                                   s->xb_a, ctl, s->cs, s->pdl);
+        if (!s->norm_kernels) {
+            // the residual epilogue also writes split(dh * post_norm) for gate/up, and the sums of squares
             oa.ssq_out = s->dssq;
-        } else {
-            launch_dit_attention_split(s->dqkv, 2, seq, hq, hkv, hd, dev->dit_rope_cos, dev->dit_rope_sin, scale,
-                                       s->xb_a, ctl, s->cs, s->pdl);
-            if (!s->norm_kernels) {
-                // the residual epilogue also writes split(dh * post_norm) for gate/up, and the sums of squares
-                oa.ssq_out = s->dssq;
-                oa.next_g = L.post_norm;
-                oa.next_b = s->xb_n;
-                oa.ldnb = Hd;
-            }
+            oa.next_g = L.post_norm;
+            oa.next_b = s->xb_n;
+            oa.ldnb = Hd;
         }
         launch_tc_linear(maps[1], s->map_xb_a, oa, s->cs, s->pdl);
         const int o_parts = (Hd / 128) * oa.splits;
-        TcLinearArgs ga = tc_plan(s, F / 64, Hd, fused);
+        TcLinearArgs ga = tc_plan(s, F / 64, Hd);
         ga.K = Hd;
         ga.M = M;
         ga.rows = F;
@@ -773,15 +697,7 @@ void enqueue_dit_layers(vxc_stream* s, StreamCtl* ctl) {
         ga.yb = s->xb_act;
         ga.ldyb = F;
         ga.ctl = ctl;
-        if (fused) {
-            ga.bmode = TC_B_NORM;
-            ga.x = s->dh;
-            ga.ldx = Hd;
-            ga.g = L.post_norm;
-            ga.eps = d.rms_eps;
-            ga.ssq_in = s->dssq;
-            ga.ssq_parts = o_parts;
-        } else if (s->norm_kernels) {
+        if (s->norm_kernels) {
             launch_rmsnorm_rows_split(s->dh, Hd, L.post_norm, d.rms_eps, Hd, M, s->xb_n, ctl, s->cs, s->pdl);
         } else {
             ga.row_scale = 1;
@@ -790,7 +706,7 @@ void enqueue_dit_layers(vxc_stream* s, StreamCtl* ctl) {
             ga.eps = d.rms_eps;
         }
         launch_tc_linear(maps[2], s->map_xb_n, ga, s->cs, s->pdl);
-        TcLinearArgs da = tc_plan(s, Hd / 128, F, false);
+        TcLinearArgs da = tc_plan(s, Hd / 128, F);
         da.K = F;
         da.M = M;
         da.rows = Hd;
@@ -799,8 +715,7 @@ void enqueue_dit_layers(vxc_stream* s, StreamCtl* ctl) {
         da.y = s->dh;
         da.ldy = Hd;
         da.ctl = ctl;
-        if (fused) da.ssq_out = s->dssq;
-        if (!fused && !s->norm_kernels && l + 1 < dev->dit.size()) {  // the next q/k/v operand, split(dh * in_norm)
+        if (!s->norm_kernels && l + 1 < dev->dit.size()) {  // the next q/k/v operand, split(dh * in_norm)
             da.ssq_out = s->dssq;
             da.next_g = dev->dit[l + 1].in_norm;
             da.next_b = s->xb_n;
@@ -818,14 +733,17 @@ void enqueue_time_tokens(vxc_stream* s, float step_index, float T, const float* 
     const DitPtrs w = dit_ptrs(s->dev);
     const int Hd = d.dit_hidden;
     const int sk = ctl ? 1 : 0;
-    launch_timestep_embedding(step_index, T, 1, Hd / 2, s->temb, ctl, s->cs, s->pdl);
+    const float* freq = s->dev->temb_freq;
+    // the estimator's time layers: scale 1000, schedule mode 1 for t and 0 for dt
+    const float t_sched = timestep_scheduled_t(step_index, T) * 1000.0f;
+    launch_timestep_embedding(nullptr, t_sched, 1, freq, Hd / 2, s->temb, ctl, s->cs, s->pdl);
     launch_gemv(plain_gemv(w.t1_w, w.t1_b, s->temb, Hd, Hd, s->tmid, ACT_SILU, ctl, sk), s->cs, s->pdl);
     launch_gemv(plain_gemv(w.t2_w, w.t2_b, s->tmid, Hd, Hd, s->ttok, ACT_NONE, ctl, sk), s->cs, s->pdl);
-    launch_timestep_embedding(dt_raw[0], 0.f, 0, Hd / 2, s->dtemb, ctl, s->cs, s->pdl);
+    launch_timestep_embedding(nullptr, dt_raw[0] * 1000.0f, 1, freq, Hd / 2, s->dtemb, ctl, s->cs, s->pdl);
     launch_gemv(plain_gemv(w.dt1_w, w.dt1_b, s->dtemb, Hd, Hd, s->dtmid, ACT_SILU, ctl, sk), s->cs, s->pdl);
     launch_gemv(plain_gemv(w.dt2_w, w.dt2_b, s->dtmid, Hd, Hd, s->dttok, ACT_NONE, ctl, sk), s->cs, s->pdl);
     if (dt_raw[1] != dt_raw[0]) {
-        launch_timestep_embedding(dt_raw[1], 0.f, 0, Hd / 2, s->dtemb1, ctl, s->cs, s->pdl);
+        launch_timestep_embedding(nullptr, dt_raw[1] * 1000.0f, 1, freq, Hd / 2, s->dtemb1, ctl, s->cs, s->pdl);
         launch_gemv(plain_gemv(w.dt1_w, w.dt1_b, s->dtemb1, Hd, Hd, s->dtmid1, ACT_SILU, ctl, sk), s->cs, s->pdl);
         launch_gemv(plain_gemv(w.dt2_w, w.dt2_b, s->dtmid1, Hd, Hd, s->dttok1, ACT_NONE, ctl, sk), s->cs, s->pdl);
     }
@@ -859,10 +777,6 @@ void enqueue_dit_eval(vxc_stream* s, const float* x, const float* x_unc, const f
     e.cond_uncond = cond_unc;
     e.tsum = tsum;
     e.ssq_out = s->dssq;
-    if (s->dit_form == 0) {  // the persistent launch that follows expects a zeroed sync block
-        e.sync_reset = s->dsync;
-        e.sync_words = dit_layers_sync_words();
-    }
     launch_dit_embed(e, s->cs, s->pdl);
     enqueue_dit_layers(s, ctl);
     DitOutArgs o{};
@@ -1808,6 +1722,9 @@ VXC_API int32_t vxc_device_create(int32_t device, const vxc_model_desc* desc, vx
         dev->dit_rope_sin = dev_alloc<float>(s.size());
         ck(cudaMemcpy(dev->dit_rope_cos, c.data(), sizeof(float) * c.size(), cudaMemcpyHostToDevice), "rope");
         ck(cudaMemcpy(dev->dit_rope_sin, s.data(), sizeof(float) * s.size(), cudaMemcpyHostToDevice), "rope");
+        const std::vector<float> f = timestep_frequencies(desc->dit_hidden / 2, 10000.0f);
+        dev->temb_freq = dev_alloc<float>(f.size());
+        ck(cudaMemcpy(dev->temb_freq, f.data(), sizeof(float) * f.size(), cudaMemcpyHostToDevice), "frequencies");
         *out = dev.release();
     });
 }
@@ -1820,8 +1737,7 @@ VXC_API void vxc_device_destroy(vxc_device* dev) {
             if (p) cudaFree(p);
         if (dev->dit_rope_cos) cudaFree(dev->dit_rope_cos);
         if (dev->dit_rope_sin) cudaFree(dev->dit_rope_sin);
-        if (dev->dit_maps_dev) cudaFree(dev->dit_maps_dev);
-        if (dev->dit_norms_dev) cudaFree(dev->dit_norms_dev);
+        if (dev->temb_freq) cudaFree(dev->temb_freq);
     }
     delete dev;
 }
@@ -1853,21 +1769,10 @@ VXC_API int32_t vxc_load_weights(vxc_device* dev, int32_t component, const void*
             const int dh = dev->desc.dit_hidden, df = dev->desc.dit_ffn;
             const int W = (dev->desc.dit_q_heads + 2 * dev->desc.dit_kv_heads) * 64;
             dev->dit_maps.clear();
-            std::vector<const __half*> norms;
-            for (const LayerW& L : dev->dit) {
+            for (const LayerW& L : dev->dit)
                 dev->dit_maps.push_back({make_tensor_map_f16(L.wqkv, W, dh, 64), make_tensor_map_f16(L.wo, dh, dh, 64),
                                          make_tensor_map_f16(L.wgateup, 2 * df, dh, 64),
                                          make_tensor_map_f16(L.wdown, dh, df, 64)});
-                norms.push_back(L.in_norm);
-                norms.push_back(L.post_norm);
-            }
-            const size_t nl = dev->dit.size();
-            if (!dev->dit_maps_dev) dev->dit_maps_dev = dev_alloc<CUtensorMap>(4 * nl);
-            if (!dev->dit_norms_dev) dev->dit_norms_dev = dev_alloc<const __half*>(2 * nl);
-            ck(cudaMemcpy(dev->dit_maps_dev, dev->dit_maps.data(), sizeof(CUtensorMap) * 4 * nl,
-                          cudaMemcpyHostToDevice), "tensor maps");
-            ck(cudaMemcpy(dev->dit_norms_dev, norms.data(), sizeof(const __half*) * 2 * nl, cudaMemcpyHostToDevice),
-               "norm pointers");
         }
     });
 }
@@ -1958,10 +1863,6 @@ VXC_API int32_t vxc_stream_create(vxc_device* dev, int32_t kv_capacity, vxc_stre
         s->dest = dev_alloc<float>(2 * L);
         s->dcount = dev_alloc<int>(1);
         ck(cudaMemset(s->dcount, 0, sizeof(int)), "cudaMemset");
-        // DiT decoder form: the 7-launch layers by default (separate RMSNorm and attention
-        // kernels around four tcgen05 linears; the fastest with several concurrent streams);
-        // VXC_DIT_FORM=persistent|fused|split picks one explicitly (an unsupported choice is an error)
-        s->dit_grid = dit_layers_grid();
         if (const char* np = std::getenv("VXC_NO_PDL")) s->pdl = std::string(np) != "1";
         if (const char* nk = std::getenv("VXC_NORM_KERNELS")) s->norm_kernels = std::string(nk) == "1";
         if (const char* rs = std::getenv("VXC_RECV_SHARED")) s->recv_shared = std::string(rs) == "1";
@@ -1974,25 +1875,9 @@ VXC_API int32_t vxc_stream_create(vxc_device* dev, int32_t kv_capacity, vxc_stre
             s->tc_stages = std::atoi(st);
             if (s->tc_stages < 1 || s->tc_stages > 8) throw std::invalid_argument("VXC_TC_STAGES must be in [1, 8]");
         }
-        const bool persist_ok = dit_persistent_ok(d, s->dit_grid), fused_ok = dit_fused_ok(d);
-        s->dit_form = 2;
-        if (const char* f = std::getenv("VXC_DIT_FORM")) {
-            const std::string form(f);
-            if (form == "persistent") s->dit_form = 0;
-            else if (form == "fused") s->dit_form = 1;
-            else if (form == "split") s->dit_form = 2;
-            else throw std::invalid_argument("VXC_DIT_FORM must be persistent, fused or split");
-            if ((s->dit_form == 0 && !persist_ok) || (s->dit_form == 1 && !fused_ok))
-                throw std::invalid_argument("VXC_DIT_FORM: that form does not support this model's shapes");
-        }
-        if (s->dit_form == 0) {
-            const size_t pf = dit_layers_part_floats(s->dit_grid);
-            s->dpart = dev_alloc<float>(pf);
-            const int sw = dit_layers_sync_words();
-            s->dsync = dev_alloc<unsigned>(sw);
-            ck(cudaMemset(s->dsync, 0, sizeof(unsigned) * sw), "cudaMemset");
-        }
-        const size_t ssq_n = static_cast<size_t>(std::max<int>(static_cast<int>(Hd / 16 + Hd / 32 + 1), s->dit_grid)) * kSsqStride;
+        // row sums of squares of dh, by slice: the embedding's Hd / 32 parts or a residual
+        // epilogue's (Hd / 128 tiles) x (K split <= 8) parts
+        const size_t ssq_n = static_cast<size_t>(Hd / 16 + Hd / 32 + 1) * kSsqStride;
         s->dssq = dev_alloc<float>(ssq_n);
         ck(cudaMemset(s->dssq, 0, ssq_n * sizeof(float)), "cudaMemset");
         for (__half** xb : {&s->xb_n, &s->xb_a, &s->xb_act}) {
@@ -2479,6 +2364,34 @@ VXC_API int32_t vxc_sdpa_host(const float* q, int32_t heads, int32_t src, int32_
     });
 }
 
+VXC_API int32_t vxc_timestep_embedding(const float* in, int32_t n_in, int32_t half_dim, float scale,
+                                       float max_period, int32_t schedule_mode, float* out) {
+    return guard([&] {
+        require(in != nullptr && out != nullptr, "null argument");
+        require(n_in > 0 && half_dim > 1 && max_period > 0.f, "bad timestep embedding shape");
+        require(schedule_mode == 0 || n_in >= 2, "schedule mode reads (step_index, timesteps) from two inputs");
+        // one t per input row; schedule mode gives every row t(step_index, timesteps)
+        std::vector<float> t(static_cast<size_t>(n_in));
+        const float sched = schedule_mode != 0 ? timestep_scheduled_t(in[0], in[1]) : 0.f;
+        for (int b = 0; b < n_in; ++b) t[b] = (schedule_mode != 0 ? sched : in[b]) * scale;
+        const std::vector<float> f = timestep_frequencies(half_dim, max_period);
+        const size_t n_out = static_cast<size_t>(n_in) * 2 * half_dim;
+        float* dt = dev_alloc<float>(t.size() + f.size() + n_out);
+        try {
+            float* dfreq = dt + t.size();
+            float* dout = dfreq + f.size();
+            ck(cudaMemcpy(dt, t.data(), sizeof(float) * t.size(), cudaMemcpyHostToDevice), "upload");
+            ck(cudaMemcpy(dfreq, f.data(), sizeof(float) * f.size(), cudaMemcpyHostToDevice), "upload");
+            launch_timestep_embedding(dt, 0.f, n_in, dfreq, half_dim, dout, nullptr, nullptr, false);
+            ck(cudaMemcpy(out, dout, sizeof(float) * n_out, cudaMemcpyDeviceToHost), "download");
+        } catch (...) {
+            cudaFree(dt);
+            throw;
+        }
+        cudaFree(dt);
+    });
+}
+
 VXC_API int32_t vxc_upload_noise(vxc_stream* s, const float* noise, int32_t patches) {
     return guard([&] {
         require(s && noise && patches > 0, "bad arguments");
@@ -2524,6 +2437,71 @@ VXC_API int32_t vxc_patch_collect(vxc_stream* s, float* out_latent, int32_t* out
         int stop = 0;
         patch_collect(s, out_latent, &stop);
         if (out_stop) *out_stop = stop;
+    });
+}
+
+VXC_API int32_t vxc_patch_run(vxc_stream* const* streams, int32_t n, const float* noise, int32_t patches,
+                              int32_t min_patches, float cfg_value, int32_t timesteps, float* out_latents,
+                              int32_t* out_patches) {
+    return guard([&] {
+        require(streams != nullptr && noise != nullptr && out_latents != nullptr && out_patches != nullptr,
+                "null argument");
+        require(n > 0 && patches > 0, "need at least one stream and one patch");
+        std::vector<vxc_stream*> order(streams, streams + n);
+        for (vxc_stream* s : order) require(s != nullptr, "stream must not be null");
+        std::sort(order.begin(), order.end());
+        require(std::adjacent_find(order.begin(), order.end()) == order.end(), "a stream is listed twice");
+        for (vxc_stream* s : order) require(s->dev->device == streams[0]->dev->device, "streams on different devices");
+        // every stream's call lock, taken in address order (no lock-order inversion with other such calls)
+        std::vector<std::unique_lock<std::mutex>> locks;
+        for (vxc_stream* s : order) locks.emplace_back(s->call_mutex);
+        DeviceGuard g(streams[0]->dev->device);
+        const int L = streams[0]->dev->desc.feat_dim * streams[0]->dev->desc.patch_size;
+        for (int i = 0; i < n; ++i) {
+            require(streams[i]->submitted == streams[i]->collected, "a stream has patches in flight");
+            out_patches[i] = 0;
+        }
+        // Each stream keeps kDepth patches queued: while the host copies one patch's
+        // latent out and the next one's noise in, the stream's GPU queue never drains.
+        constexpr int kDepth = 2;
+        std::vector<int> sub(n, 0), col(n, 0), done(n, 0);
+        auto submit = [&](int i) {
+            patch_submit(streams[i], noise + (static_cast<size_t>(i) * patches + sub[i]) * L, min_patches, cfg_value,
+                         timesteps);
+            sub[i] += 1;
+        };
+        auto drain = [&](int i) {  // patches queued after a stop (their kernels skip) or after an error
+            while (streams[i]->collected < streams[i]->submitted) {
+                try {
+                    patch_collect(streams[i], nullptr, nullptr);
+                } catch (...) {
+                }
+            }
+        };
+        try {
+            for (int k = 0; k < std::min(kDepth, static_cast<int>(patches)); ++k)
+                for (int i = 0; i < n; ++i) submit(i);
+            int live = n;
+            while (live > 0) {
+                for (int i = 0; i < n; ++i) {
+                    if (done[i]) continue;
+                    int stop = 0;
+                    patch_collect(streams[i], out_latents + (static_cast<size_t>(i) * patches + col[i]) * L, &stop);
+                    col[i] += 1;
+                    out_patches[i] = col[i];
+                    if (stop || col[i] == patches) {
+                        drain(i);
+                        done[i] = 1;
+                        --live;
+                    } else if (sub[i] < patches) {
+                        submit(i);
+                    }
+                }
+            }
+        } catch (...) {
+            for (int i = 0; i < n; ++i) drain(i);
+            throw;
+        }
     });
 }
 
@@ -2595,7 +2573,6 @@ std::vector<std::function<void(bool)>> profile_launches(vxc_stream* s, int kerne
     const int hq = d.q_heads, hkv = d.kv_heads, hd = d.head_dim;
     const int dq = d.dit_q_heads, dkv = d.dit_kv_heads;
     const size_t plane = static_cast<size_t>(hkv) * s->cap * hd;
-    const bool fused = s->dit_form != 2;
     const int Wd = (dq + 2 * dkv) * (Hd / dq);
     bytes = 0.0;
     // one launch per layer, in the form the patch graph runs it
@@ -2652,52 +2629,37 @@ std::vector<std::function<void(bool)>> profile_launches(vxc_stream* s, int kerne
     for (size_t l = 0; l < nl; ++l) {
         switch (kernel) {
             case VXC_PROF_DIT_GATEUP: {
-                TcLinearArgs a = tc_plan(s, Fd / 64, Hd, fused);
+                TcLinearArgs a = tc_plan(s, Fd / 64, Hd);
                 a.K = Hd; a.M = M; a.rows = Fd; a.gateup = 1;
                 a.yb = s->xb_act; a.ldyb = Fd; a.ctl = s->ctl;
-                if (fused) {
-                    a.bmode = TC_B_NORM; a.x = s->dh; a.ldx = Hd; a.g = dev->dit[l].post_norm; a.eps = d.rms_eps;
-                    a.ssq_in = s->dssq; a.ssq_parts = (Hd / 128) * tc_plan(s, Hd / 128, dq * 64, true).splits;
-                }
-                bytes = 2.0 * 2 * Fd * Hd + (fused ? 4.0 * M * Hd : 2.0 * 48 * Hd) + 2.0 * 48 * Fd;
+                bytes = 2.0 * 2 * Fd * Hd + 2.0 * 48 * Hd + 2.0 * 48 * Fd;
                 const CUtensorMap ma = dev->dit_maps[l][2], mb = s->map_xb_n;
                 launch.push_back([=](bool pdl) { launch_tc_linear(ma, mb, a, s->cs, pdl); });
                 break;
             }
             case VXC_PROF_DIT_DOWN: {
-                TcLinearArgs a = tc_plan(s, Hd / 128, Fd, false);
+                TcLinearArgs a = tc_plan(s, Hd / 128, Fd);
                 a.K = Fd; a.M = M; a.rows = Hd; a.resid = 1;
                 a.y = s->dxn; a.ldy = Hd; a.ctl = s->ctl;
-                if (fused) a.ssq_out = s->dssq + static_cast<size_t>(Hd / 16) * kSsqStride;  // spare parts
                 bytes = 2.0 * Hd * Fd + 2.0 * 48 * Fd + 8.0 * M * Hd;
                 const CUtensorMap ma = dev->dit_maps[l][3], mb = s->map_xb_act;
                 launch.push_back([=](bool pdl) { launch_tc_linear(ma, mb, a, s->cs, pdl); });
                 break;
             }
             case VXC_PROF_DIT_QKV: {
-                TcLinearArgs a = tc_plan(s, Wd / 128, Hd, fused);
+                TcLinearArgs a = tc_plan(s, Wd / 128, Hd);
                 a.K = Hd; a.M = M; a.rows = Wd;
                 a.y = s->dqkv; a.ldy = Wd; a.ctl = s->ctl;
-                if (fused) {
-                    a.bmode = TC_B_NORM; a.x = s->dh; a.ldx = Hd; a.g = dev->dit[l].in_norm; a.eps = d.rms_eps;
-                    a.ssq_in = s->dssq; a.ssq_parts = (Hd + 31) / 32;
-                }
-                bytes = 2.0 * Wd * Hd + (fused ? 4.0 * M * Hd : 2.0 * 48 * Hd) + 4.0 * M * Wd;
+                bytes = 2.0 * Wd * Hd + 2.0 * 48 * Hd + 4.0 * M * Wd;
                 const CUtensorMap ma = dev->dit_maps[l][0], mb = s->map_xb_n;
                 launch.push_back([=](bool pdl) { launch_tc_linear(ma, mb, a, s->cs, pdl); });
                 break;
             }
             case VXC_PROF_DIT_O: {
-                TcLinearArgs a = tc_plan(s, Hd / 128, dq * 64, fused);
+                TcLinearArgs a = tc_plan(s, Hd / 128, dq * 64);
                 a.K = dq * 64; a.M = M; a.rows = Hd; a.resid = 1;
                 a.y = s->dxn; a.ldy = Hd; a.ctl = s->ctl;
-                if (fused) {
-                    a.bmode = TC_B_ATTN; a.qkv = s->dqkv; a.q_heads = dq; a.kv_heads = dkv; a.seq = seq;
-                    a.rope_cos = dev->dit_rope_cos; a.rope_sin = dev->dit_rope_sin; a.scale = 0.125f;
-                    a.attn_round = tc_attn_round(a.K, a.splits, a.max_stages);
-                    a.ssq_out = s->dssq + static_cast<size_t>(Hd / 16) * kSsqStride;
-                }
-                bytes = 2.0 * Hd * dq * 64 + (fused ? 4.0 * M * Wd : 2.0 * 48 * dq * 64) + 8.0 * M * Hd;
+                bytes = 2.0 * Hd * dq * 64 + 2.0 * 48 * dq * 64 + 8.0 * M * Hd;
                 const CUtensorMap ma = dev->dit_maps[l][1], mb = s->map_xb_a;
                 launch.push_back([=](bool pdl) { launch_tc_linear(ma, mb, a, s->cs, pdl); });
                 break;
@@ -2781,49 +2743,7 @@ VXC_API int32_t vxc_profile_kernel(vxc_stream* s, int32_t kernel, int32_t iters,
         const vxc_model_desc& d = dev->desc;
         check_loaded(dev, {VXC_BASE_DECODER, VXC_DIT_ESTIMATOR});
         DeviceGuard g(dev->device);
-        if (kernel == VXC_PROF_DIT_LAYERS) {
-            // one persistent launch = every DiT layer of one evaluation; each launch timed
-            // alone between CUDA events (its sync block zeroed before it, outside the events)
-            require(s->dit_form == 0, "the stream does not use the persistent DiT form");
-            const DitLayersArgs a = dit_layers_args(s, s->ctl);
-            const size_t Hd = d.dit_hidden, F = d.dit_ffn;
-            const size_t W = static_cast<size_t>(d.dit_q_heads + 2 * d.dit_kv_heads) * (Hd / d.dit_q_heads);
-            const size_t M = 2 * static_cast<size_t>(dit_tokens_per_seq(d.patch_size));
-            const double per_layer = 2.0 * (W * Hd + Hd * Hd + 2 * F * Hd + Hd * F) + 4.0 * M * (2 * Hd + W);
-            const int sw = dit_layers_sync_words();
-            std::vector<cudaEvent_t> ev(2 * static_cast<size_t>(iters) + 2, nullptr);
-            cudaError_t err = cudaSuccess;
-            for (auto& e : ev)
-                if (err == cudaSuccess) err = cudaEventCreate(&e);
-            for (int i = -1; i < iters && err == cudaSuccess; ++i) {  // i = -1: warm-up
-                err = cudaMemsetAsync(s->dsync, 0, sizeof(unsigned) * sw, s->cs);
-                const size_t k = static_cast<size_t>(i + 1);
-                if (err == cudaSuccess) err = cudaEventRecord(ev[2 * k], s->cs);
-                if (err == cudaSuccess) {
-                    try {
-                        launch_dit_layers(a, s->dit_grid, s->cs);
-                    } catch (const std::exception&) {
-                        err = cudaErrorLaunchFailure;
-                    }
-                }
-                if (err == cudaSuccess) err = cudaEventRecord(ev[2 * k + 1], s->cs);
-            }
-            if (err == cudaSuccess) err = cudaStreamSynchronize(s->cs);
-            float total = 0.f;
-            for (int i = 0; i < iters && err == cudaSuccess; ++i) {
-                float ms = 0.f;
-                const size_t k = static_cast<size_t>(i + 1);
-                err = cudaEventElapsedTime(&ms, ev[2 * k], ev[2 * k + 1]);
-                total += ms;
-            }
-            for (auto& e : ev)
-                if (e) cudaEventDestroy(e);
-            ck(err, "persistent DiT profile");
-            sync_ctl(s);
-            *ms_per_launch = total / static_cast<float>(iters);
-            *bytes_per_launch = per_layer * d.dit_layers;
-            return;
-        }
+        require(kernel != 8, "kernel id 8 is not used");
         // iters launches cycling through the layers, captured in one graph with
         // programmatic dependent launch between them like the patch graph
         double bytes = 0.0;

@@ -12,6 +12,8 @@
 
 #include <cstdint>
 
+#include "common.cuh"
+
 namespace vxc {
 namespace tc {
 
@@ -21,7 +23,16 @@ constexpr int kBRows = 48;          // MMA N (hi tokens 0..23, lo tokens 24..47)
 constexpr int kLoOffset = 24;
 constexpr int kABytes = kTileRows * kKChunk * 2;  // 16 KiB
 constexpr int kBBytes = kBRows * kKChunk * 2;     // 6 KiB
-constexpr uint32_t kWaitLimit = 1u << 22;
+
+// TMEM budget. An SM has 512 TMEM columns and 233,472 bytes of shared memory,
+// 1 KiB of which every resident CTA reserves. A CTA that allocates 'cols' columns
+// asks for at least cols * 456 bytes of shared memory in all (dynamic + static +
+// the reserved 1 KiB): then the CTAs that fit on an SM by shared memory, from any
+// mix of these kernels and launches, hold at most 512 columns together, so
+// tcgen05.alloc never waits for another CTA to free columns (such a wait, with
+// CTAs of split-K clusters on both sides, could otherwise close a cycle across SMs).
+constexpr size_t kSmBytesPerTmemCol = (233472 + 511) / 512;  // 456
+inline size_t tmem_smem_floor(int cols) { return static_cast<size_t>(cols) * kSmBytesPerTmemCol - 1024; }
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -36,21 +47,9 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
                  : "memory");
 }
 
-// Bounded wait for phase 'parity' of an mbarrier; false on timeout.
+// Time-bounded wait for phase 'parity' of an mbarrier (kWaitNs); false on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    const uint32_t addr = smem_addr(bar);
-    for (uint32_t i = 0; i < kWaitLimit; ++i) {
-        uint32_t done;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(done)
-            : "r"(addr), "r"(parity)
-            : "memory");
-        if (done) return true;
-    }
-    return false;
+    return mbar_wait_addr(smem_addr(bar), parity);
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {

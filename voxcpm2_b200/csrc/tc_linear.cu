@@ -21,15 +21,16 @@
 //
 // Roles: thread 0 issues TMA (weights before griddepcontrol.wait, so weight
 // streaming overlaps the previous kernel), thread 32 issues tcgen05.mma, all
-// four warps drain TMEM. Every mbarrier wait is bounded; on timeout the kernel
-// records error 3 in the stream control block, still passes every cluster
-// barrier and frees its TMEM, and the host reports the failure.
+// four warps drain TMEM. Every mbarrier wait gives up after one second of
+// %globaltimer time; the failure path is written to record error 3 in the
+// stream control block, pass every cluster barrier and free its TMEM, but it
+// has not been exercised on a GPU (no injected failure runs there). The TMEM
+// allocation itself has no time bound: it relies on the kernels' shared-memory
+// sizes keeping every co-resident mix within the SM's 512 columns.
 #include <cuda.h>
 
 #include <algorithm>
-#include <cfloat>
 #include <stdexcept>
-#include <type_traits>
 #include <vector>
 
 #include "kernels.cuh"
@@ -53,189 +54,8 @@ __host__ __device__ constexpr bool shared_recv_fits(bool b_tma, int splits, int 
 }
 constexpr int kTmemCols = 64;
 
-// Zero token rows M..23 (and their residual rows) of 'cs' B tiles.
-__device__ __forceinline__ void zero_pad_rows(uint8_t* smem, int cs, int M) {
-    const int pad = kLoOffset - M;
-    for (int u = threadIdx.x; u < cs * pad * 16; u += kTcThreads) {
-        const int ch = u / (pad * 16), r = u - ch * pad * 16, m = M + r / 16, col = (r & 15) * 4;
-        put_split4(smem + ch * kStageBytes + kABytes, m, col, make_float4(0.f, 0.f, 0.f, 0.f));
-    }
-}
-
-// B = split-fp16 RMSNorm(x) for chunks c0 .. c0 + cs - 1 (RMSNorm as in
-// rmsnorm_rows_split_kernel: x * rsqrt(mean(x^2) + eps) * g). The row sums of
-// squares are the fixed-order sum of the producer's partials. Every thread
-// issues its loads in batches before it uses any (each global round trip costs
-// about a microsecond here).
-__device__ void build_b_norm(uint8_t* smem, const TcLinearArgs& a, int c0, int cs, float* inv_s, float4* red) {
-    const int tid = threadIdx.x;
-    // 120 threads = 20 part groups x 6 token quads, then a fixed-order sum over the groups
-    if (tid < 120) {
-        const int r = tid / 6, q = tid - r * 6;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int p0 = 0; p0 < a.ssq_parts; p0 += 160) {
-            float4 v[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int p = p0 + r + 20 * i;
-                v[i] = p < a.ssq_parts ? __ldcg(reinterpret_cast<const float4*>(a.ssq_in + p * kSsqStride) + q)
-                                       : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                acc.x += v[i].x;
-                acc.y += v[i].y;
-                acc.z += v[i].z;
-                acc.w += v[i].w;
-            }
-        }
-        red[r * 6 + q] = acc;
-    }
-    __syncthreads();
-    if (tid < kLoOffset) {
-        const float* rf = reinterpret_cast<const float*>(red);
-        float t = 0.f;
-        for (int r = 0; r < 20; ++r) t += rf[r * 24 + tid];
-        inv_s[tid] = rsqrtf(t / static_cast<float>(a.K) + a.eps);
-    }
-    __syncthreads();
-    const int per = cs * 16, total = a.M * per;  // float4 units per token row, in all
-    constexpr int kB = 8;
-    for (int base = 0; base < total; base += kTcThreads * kB) {
-        float4 xv[kB];
-        uint2 gw[kB];
-#pragma unroll
-        for (int i = 0; i < kB; ++i) {
-            const int u = base + tid + kTcThreads * i;
-            if (u < total) {
-                const int m = u / per, q = u - m * per, k = (c0 + (q >> 4)) * kKChunk + (q & 15) * 4;
-                xv[i] = __ldcg(reinterpret_cast<const float4*>(a.x + static_cast<size_t>(m) * a.ldx + k));
-                gw[i] = __ldg(reinterpret_cast<const uint2*>(a.g + k));
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < kB; ++i) {
-            const int u = base + tid + kTcThreads * i;
-            if (u < total) {
-                const int m = u / per, q = u - m * per, ch = q >> 4, col = (q & 15) * 4;
-                const float2 g01 = __half22float2(*reinterpret_cast<const __half2*>(&gw[i].x));
-                const float2 g23 = __half22float2(*reinterpret_cast<const __half2*>(&gw[i].y));
-                const float iv = inv_s[m];
-                put_split4(smem + ch * kStageBytes + kABytes, m, col,
-                           make_float4(xv[i].x * iv * g01.x, xv[i].y * iv * g01.y, xv[i].z * iv * g23.x,
-                                       xv[i].w * iv * g23.y));
-            }
-        }
-    }
-    zero_pad_rows(smem, cs, a.M);
-}
-
-// Attention scratch per head of a round (floats): q and k [24][65], v [24][64],
-// probabilities [2 sequences][12][13].
-constexpr int kAttnRow = 65;
-constexpr int kAttnHeadFloats = 2 * 24 * kAttnRow + 24 * 64 + 2 * 12 * 13;
 constexpr size_t kSmemOptin = 232448;  // B200: opt-in shared memory per CTA (227 KB)
 size_t g_dyn_limit = 0;                // kSmemOptin less the kernel's static shared memory (set once)
-
-// B = split-fp16 attention output of heads c0 .. c0 + cs - 1 (one 64-wide head
-// per K chunk), the math of dit_attention_split_kernel: RoPE (rotate_half) on q
-// and k, scores * scale, softmax, P.V, both sequences, 'round' heads at a time.
-__device__ void build_b_attn(uint8_t* smem, const TcLinearArgs& a, int c0, int cs, int round, float* scratch) {
-    constexpr int D = 64, HALF = 32;
-    const int tid = threadIdx.x, M = a.M, seq = a.seq;
-    const int W = (a.q_heads + 2 * a.kv_heads) * D, grp = a.q_heads / a.kv_heads;
-    float* qs = scratch;
-    float* ks = qs + round * 24 * kAttnRow;
-    float* vs = ks + round * 24 * kAttnRow;
-    float* ps = vs + round * 24 * D;
-    for (int h0 = 0; h0 < cs; h0 += round) {
-        const int nh = min(round, cs - h0);
-        // raw q / k / v rows of the round's heads (nh x M x 3 x 16 float4), loads in batches
-        constexpr int kB = 9;
-        const int total = nh * M * 48;
-        for (int base = 0; base < total; base += kTcThreads * kB) {
-            float4 v[kB];
-#pragma unroll
-            for (int i = 0; i < kB; ++i) {
-                const int u = base + tid + kTcThreads * i;
-                if (u < total) {
-                    const int hl = u / (M * 48), r2 = u - hl * M * 48, i2 = r2 / 48, w = r2 - i2 * 48;
-                    const int kind = w >> 4, e4 = (w & 15) * 4, h = c0 + h0 + hl, kvh = h / grp;
-                    const int col = kind == 0 ? h * D : kind == 1 ? (a.q_heads + kvh) * D
-                                                                  : (a.q_heads + a.kv_heads + kvh) * D;
-                    v[i] = __ldcg(reinterpret_cast<const float4*>(a.qkv + static_cast<size_t>(i2) * W + col + e4));
-                }
-            }
-#pragma unroll
-            for (int i = 0; i < kB; ++i) {
-                const int u = base + tid + kTcThreads * i;
-                if (u < total) {
-                    const int hl = u / (M * 48), r2 = u - hl * M * 48, i2 = r2 / 48, w = r2 - i2 * 48;
-                    const int kind = w >> 4, e4 = (w & 15) * 4;
-                    float* dst = kind == 0 ? qs + (hl * 24 + i2) * kAttnRow
-                                           : kind == 1 ? ks + (hl * 24 + i2) * kAttnRow : vs + (hl * 24 + i2) * D;
-                    dst[e4] = v[i].x;
-                    dst[e4 + 1] = v[i].y;
-                    dst[e4 + 2] = v[i].z;
-                    dst[e4 + 3] = v[i].w;
-                }
-            }
-        }
-        __syncthreads();
-        // RoPE (rotate_half) on q and k in place: each unit owns the pair (e, e + 32)
-        for (int u = tid; u < nh * 2 * M * HALF; u += kTcThreads) {
-            const int hl = u / (2 * M * HALF), r2 = u - hl * 2 * M * HALF, which = r2 / (M * HALF);
-            const int r3 = r2 - which * M * HALF, i = r3 / HALF, e = r3 - i * HALF, pos = i % seq;
-            float* row = (which == 0 ? qs : ks) + (hl * 24 + i) * kAttnRow;
-            const float c1 = __ldg(a.rope_cos + pos * D + e), c2 = __ldg(a.rope_cos + pos * D + e + HALF);
-            const float s1 = __ldg(a.rope_sin + pos * D + e), s2 = __ldg(a.rope_sin + pos * D + e + HALF);
-            const float v1 = row[e], v2 = row[e + HALF];
-            row[e] = v1 * c1 + (-v2) * s1;
-            row[e + HALF] = v2 * c2 + v1 * s2;
-        }
-        __syncthreads();
-        for (int u = tid; u < nh * 2 * seq * seq; u += kTcThreads) {
-            const int hl = u / (2 * seq * seq), r = u - hl * 2 * seq * seq, b = r / (seq * seq);
-            const int r2 = r - b * seq * seq, i = r2 / seq, j = r2 - i * seq;
-            const float* q = qs + (hl * 24 + b * seq + i) * kAttnRow;
-            const float* k = ks + (hl * 24 + b * seq + j) * kAttnRow;
-            float sum = 0.f;
-#pragma unroll 16
-            for (int e = 0; e < D; ++e) sum = fmaf(q[e], k[e], sum);
-            ps[((hl * 2 + b) * 12 + i) * 13 + j] = sum * a.scale;
-        }
-        __syncthreads();
-        for (int u = tid; u < nh * 2 * seq; u += kTcThreads) {
-            float* pr = ps + ((u / seq) * 12 + (u % seq)) * 13;  // u = (head * 2 + b) * seq + i
-            float mx = -FLT_MAX;
-            for (int j = 0; j < seq; ++j) mx = fmaxf(mx, pr[j]);
-            float sum = 0.f;
-            for (int j = 0; j < seq; ++j) {
-                pr[j] = expf(pr[j] - mx);
-                sum += pr[j];
-            }
-            for (int j = 0; j < seq; ++j) pr[j] /= sum;
-        }
-        __syncthreads();
-        for (int u = tid; u < nh * M * 16; u += kTcThreads) {
-            const int hl = u / (M * 16), r = u - hl * M * 16, m = r >> 4, col = (r & 15) * 4;
-            const int b = m / seq, i = m - b * seq;
-            const float* pr = ps + ((hl * 2 + b) * 12 + i) * 13;
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int j = 0; j < seq; ++j) {
-                const float p = pr[j];
-                const float* vr = vs + (hl * 24 + b * seq + j) * D + col;
-                acc.x = fmaf(p, vr[0], acc.x);
-                acc.y = fmaf(p, vr[1], acc.y);
-                acc.z = fmaf(p, vr[2], acc.z);
-                acc.w = fmaf(p, vr[3], acc.w);
-            }
-            put_split4(smem + (h0 + hl) * kStageBytes + kABytes, m, col, acc);
-        }
-        __syncthreads();  // the next head pair reuses the scratch
-    }
-    zero_pad_rows(smem, cs, M);
-}
 
 // The receive buffer can share the stage area when nothing else needs it there:
 // TMA-fed token tiles, no K split (no remote pushes), no squares scratch.
@@ -243,11 +63,9 @@ __host__ __device__ constexpr bool recv_in_stage_area(bool b_tma, int splits, bo
     return b_tma && splits == 1 && !ssq_out;
 }
 
-// BM: where the token operand comes from (TC_B_TMA / TC_B_NORM / TC_B_ATTN); one
-// instantiation each, so the TMA form does not carry the builders' registers.
 // S: the K split (cluster size, 1, 2, 4 or 8), a template parameter so that the
 // rank-order sums of the partials unroll and their loads issue together.
-template <int BM, int S>
+template <int S>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_linear_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                      const TcLinearArgs a) {
@@ -256,14 +74,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __shared__ uint32_t tmem_base_s;
     __shared__ int failed_s;
     __shared__ float inv_s[kLoOffset];
-    __shared__ float4 red_s[120];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int split = blockIdx.x, tile = blockIdx.y;
     // 1 KiB aligned, derived from smem_raw by pointer arithmetic so that the
     // compiler keeps shared-memory addressing for everything carved from it
     uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
-    constexpr bool b_tma = BM == TC_B_TMA;
+    constexpr bool b_tma = true;  // the token tiles arrive by TMA beside the weight tiles
 
     const int nch = a.K / kKChunk;
     const int c0 = split * nch / S, c1 = (split + 1) * nch / S, cs = c1 - c0;
@@ -331,7 +148,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         umma_commit(&done_bar);  // arrives when every MMA issued above has completed
     };
 
-    if constexpr (b_tma) {
+    {
         if (tid == 0) {
             pdl_wait();
             for (int i = 0; i < pre; ++i)
@@ -355,20 +172,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         } else {
             pdl_wait();
         }
-    } else {
-        // all chunks have their own stage (cs <= stages, checked by the launcher):
-        // every thread builds the token tiles next to the weight tiles in flight
-        pdl_wait();
-        if constexpr (BM == TC_B_NORM) {
-            build_b_norm(smem, a, c0, cs, inv_s, red_s);
-        } else {
-            float* scratch = reinterpret_cast<float*>(smem + static_cast<size_t>(stage_area) * kStageBytes) +
-                             kRecvFloats;
-            build_b_attn(smem, a, c0, cs, a.attn_round, scratch);
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic-proxy writes -> tensor core
-        __syncthreads();
-        if (tid == 32) mma_loop();
     }
 
     // row_scale: each token row's 1 / rms from the producer's sums of squares (warp 2,
@@ -436,6 +239,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // barrier; then owners sum the splits in rank order (deterministic).
         // recv[((p * halves + half) * M + m) * nu + lu]. Without a K split it lives in
         // the (then idle) stage area, so more CTAs of concurrent streams fit on an SM.
+        // 'shared' and S depend only on launch arguments, never on this CTA's data or on a
+        // failed wait, so every CTA of the cluster passes the same cluster barriers
         const bool shared = shared_recv_fits(b_tma, S, a.recv_shared, static_cast<size_t>(stage_area) * kStageBytes);
         const bool recv_in_stages = recv_in_stage_area(b_tma, S, a.ssq_out != nullptr) || shared;
         float* recv =
@@ -542,45 +347,31 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
 }  // namespace
 
-size_t tc_linear_smem_bytes(int K, int splits, int bmode, int attn_round, int max_stages, bool ssq_out,
-                            bool recv_shared) {
+size_t tc_linear_smem_bytes(int K, int splits, int max_stages, bool ssq_out, bool recv_shared) {
     const int nch = K / kKChunk;
     const int cs = (nch + splits - 1) / splits;
     const int stages = std::min(std::min(max_stages, kMaxStages), std::max(cs, 1));
     const size_t stage_bytes = static_cast<size_t>(stages) * kStageBytes;
-    if (recv_in_stage_area(bmode == TC_B_TMA, splits, ssq_out) ||
-        shared_recv_fits(bmode == TC_B_TMA, splits, recv_shared, stage_bytes))
+    if (recv_in_stage_area(true, splits, ssq_out) || shared_recv_fits(true, splits, recv_shared, stage_bytes))
         return stage_bytes + 1024;  // + alignment slack
     const size_t recv_bytes = static_cast<size_t>(kRecvFloats) * sizeof(float);
-    const size_t scratch = bmode == TC_B_ATTN ? static_cast<size_t>(attn_round) * kAttnHeadFloats * sizeof(float) : 0;
-    return stage_bytes + recv_bytes + scratch + 1024;  // + alignment slack
+    return stage_bytes + recv_bytes + 1024;  // + alignment slack
 }
 
-template <int BM>
 cudaError_t launch_split(cudaLaunchConfig_t& cfg, const CUtensorMap& map_a, const CUtensorMap& map_b,
                          const TcLinearArgs& a) {
     switch (a.splits) {
-        case 1: return cudaLaunchKernelEx(&cfg, tc_linear_kernel<BM, 1>, map_a, map_b, a);
-        case 2: return cudaLaunchKernelEx(&cfg, tc_linear_kernel<BM, 2>, map_a, map_b, a);
-        case 4: return cudaLaunchKernelEx(&cfg, tc_linear_kernel<BM, 4>, map_a, map_b, a);
-        default: return cudaLaunchKernelEx(&cfg, tc_linear_kernel<BM, 8>, map_a, map_b, a);
+        case 1: return cudaLaunchKernelEx(&cfg, tc_linear_kernel<1>, map_a, map_b, a);
+        case 2: return cudaLaunchKernelEx(&cfg, tc_linear_kernel<2>, map_a, map_b, a);
+        case 4: return cudaLaunchKernelEx(&cfg, tc_linear_kernel<4>, map_a, map_b, a);
+        default: return cudaLaunchKernelEx(&cfg, tc_linear_kernel<8>, map_a, map_b, a);
     }
 }
 
-// every instantiation (token-operand mode x split)
+// every instantiation (one per K split)
 std::vector<const void*> tc_linear_kernels() {
-    std::vector<const void*> k;
-    auto add = [&k](auto bm) {
-        constexpr int B = decltype(bm)::value;
-        k.push_back(reinterpret_cast<const void*>(tc_linear_kernel<B, 1>));
-        k.push_back(reinterpret_cast<const void*>(tc_linear_kernel<B, 2>));
-        k.push_back(reinterpret_cast<const void*>(tc_linear_kernel<B, 4>));
-        k.push_back(reinterpret_cast<const void*>(tc_linear_kernel<B, 8>));
-    };
-    add(std::integral_constant<int, TC_B_TMA>{});
-    add(std::integral_constant<int, TC_B_NORM>{});
-    add(std::integral_constant<int, TC_B_ATTN>{});
-    return k;
+    return {reinterpret_cast<const void*>(tc_linear_kernel<1>), reinterpret_cast<const void*>(tc_linear_kernel<2>),
+            reinterpret_cast<const void*>(tc_linear_kernel<4>), reinterpret_cast<const void*>(tc_linear_kernel<8>)};
 }
 
 size_t dyn_limit() {
@@ -597,10 +388,6 @@ size_t dyn_limit() {
     return g_dyn_limit;
 }
 
-int tc_attn_round(int K, int splits, int max_stages) {
-    return tc_linear_smem_bytes(K, splits, TC_B_ATTN, 2, max_stages) <= dyn_limit() ? 2 : 1;
-}
-
 void launch_tc_linear(const CUtensorMap& map_a, const CUtensorMap& map_b, const TcLinearArgs& a, cudaStream_t s,
                       bool pdl) {
     if (a.K % kKChunk != 0 || a.K <= 0) throw std::invalid_argument("tc_linear: K must be a multiple of 64");
@@ -609,30 +396,18 @@ void launch_tc_linear(const CUtensorMap& map_a, const CUtensorMap& map_b, const 
         throw std::invalid_argument("tc_linear: splits must be 1, 2, 4 or 8 and at most K / 64");
     const int n_tiles = a.gateup ? a.rows / 64 : a.rows / kTileRows;
     if ((a.gateup ? a.rows % 64 : a.rows % kTileRows) != 0) throw std::invalid_argument("tc_linear: rows");
-    if (a.bmode != TC_B_TMA) {
-        const int nch = a.K / kKChunk;
-        if ((nch + a.splits - 1) / a.splits > a.max_stages)
-            throw std::invalid_argument("tc_linear: a fused token tile needs a stage per K chunk of the CTA");
-    }
-    if (a.bmode == TC_B_NORM && (!a.x || !a.g || !a.ssq_in || a.ssq_parts <= 0 || a.ldx % 4 != 0 ||
-                                 (reinterpret_cast<uintptr_t>(a.x) & 15) != 0 ||
-                                 (reinterpret_cast<uintptr_t>(a.g) & 7) != 0))
-        throw std::invalid_argument("tc_linear: bad RMSNorm operand");
-    if (a.bmode == TC_B_ATTN &&
-        (!a.qkv || !a.rope_cos || !a.rope_sin || a.kv_heads <= 0 || a.q_heads % a.kv_heads != 0 ||
-         a.K != a.q_heads * 64 || a.seq <= 0 || a.seq > 12 || a.M != 2 * a.seq || a.attn_round < 1))
-        throw std::invalid_argument("tc_linear: bad attention operand");
     if (a.ssq_out && (a.gateup || a.M > kSsqStride)) throw std::invalid_argument("tc_linear: bad ssq_out");
     if (a.next_b && (!a.ssq_out || !a.next_g || !a.resid || a.ldnb < a.rows))
         throw std::invalid_argument("tc_linear: next_b needs a residual launch with ssq_out and next_g");
-    if (a.row_scale && (!a.ssq_in || a.ssq_parts <= 0 || a.bmode != TC_B_TMA))
-        throw std::invalid_argument("tc_linear: row_scale needs ssq_in parts and a TMA-fed operand");
+    if (a.row_scale && (!a.ssq_in || a.ssq_parts <= 0))
+        throw std::invalid_argument("tc_linear: row_scale needs ssq_in parts");
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.splits, n_tiles);
     cfg.blockDim = dim3(kTcThreads);
     if (a.max_stages < 1 || a.max_stages > kMaxStages) throw std::invalid_argument("tc_linear: max_stages in [1, 8]");
-    cfg.dynamicSmemBytes = tc_linear_smem_bytes(a.K, a.splits, a.bmode, a.attn_round, a.max_stages, a.ssq_out != nullptr,
-                                                a.recv_shared != 0);
+    cfg.dynamicSmemBytes = std::max(tc_linear_smem_bytes(a.K, a.splits, a.max_stages, a.ssq_out != nullptr,
+                                                         a.recv_shared != 0),
+                                    tmem_smem_floor(kTmemCols));
     if (cfg.dynamicSmemBytes > dyn_limit()) throw std::invalid_argument("tc_linear: shared memory over 227 KB");
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
@@ -644,9 +419,7 @@ void launch_tc_linear(const CUtensorMap& map_a, const CUtensorMap& map_b, const 
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
-    const cudaError_t e = a.bmode == TC_B_TMA    ? launch_split<TC_B_TMA>(cfg, map_a, map_b, a)
-                          : a.bmode == TC_B_NORM ? launch_split<TC_B_NORM>(cfg, map_a, map_b, a)
-                                                 : launch_split<TC_B_ATTN>(cfg, map_a, map_b, a);
+    const cudaError_t e = launch_split(cfg, map_a, map_b, a);
     if (e != cudaSuccess) throw std::runtime_error(std::string("tc_linear launch: ") + cudaGetErrorString(e));
 }
 

@@ -181,7 +181,7 @@ void launch_tc_rows(const CUtensorMap& map_a, const CUtensorMap& map_b, const Tc
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(n_tiles);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = smem_bytes(stages);
+    cfg.dynamicSmemBytes = std::max(smem_bytes(stages), tmem_smem_floor(kTmem));
     cfg.stream = s;
     check_launch(cudaLaunchKernelEx(&cfg, tc_rows_kernel, map_a, map_b, a));
 }

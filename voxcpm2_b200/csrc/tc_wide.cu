@@ -321,7 +321,7 @@ void launch_tc_wide(const CUtensorMap& map_a, const CUtensorMap& map_b, const Tc
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.splits, n_tiles);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = smem_bytes(a.K, a.splits, a.stages, a.recv_shared != 0);
+    cfg.dynamicSmemBytes = std::max(smem_bytes(a.K, a.splits, a.stages, a.recv_shared != 0), tmem_smem_floor(kTmem));
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;

@@ -55,7 +55,7 @@ class StreamState(C.Structure):
 
 
 PROFILE_KERNELS = {"dit_gateup": 0, "dit_down": 1, "dit_qkv": 2, "base_gateup": 3, "base_down": 4,
-                   "base_qkv": 5, "base_attn": 6, "dit_o": 7, "dit_layers": 8, "base_step": 9, "res_step": 10,
+                   "base_qkv": 5, "base_attn": 6, "dit_o": 7, "base_step": 9, "res_step": 10,
                    "dit_eval": 11}
 
 
@@ -94,11 +94,13 @@ def _signatures():
         "vxc_sdpa": ([vp, i, i, i, vp, vp, i, i, i, vp, i, vp, vp, i, f, vp, vp, vp, vp], i),
         "vxc_sdpa_host": ([vp, i, i, i, vp, vp, i, i, i, vp, i, vp, vp, i, f, vp, vp, vp], i),
         "vxc_sdpa_decode_noalloc": ([vp, i, i, vp, vp, i, i, vp, vp, vp, i, f, vp, vp, vp, vp], i),
+        "vxc_timestep_embedding": ([vp, i, i, f, f, i, vp], i),
         "vxc_upload_noise": ([vp, vp, i], i),
         "vxc_patch_step_async": ([vp, i, f, i], i),
         "vxc_stream_synchronize": ([vp], i),
         "vxc_patch_submit": ([vp, vp, i, f, i], i),
         "vxc_patch_collect": ([vp, vp, C.POINTER(i)], i),
+        "vxc_patch_run": ([C.POINTER(vp), i, vp, i, i, f, i, vp, vp], i),
         "vxc_read_state": ([vp, C.POINTER(StreamState)], i),
         "vxc_read_hidden": ([vp, vp, vp], i),
         "vxc_read_latents": ([vp, i, i, vp], i),
@@ -404,6 +406,26 @@ class Stream:
         return h.value or 0
 
 
+def patch_run(streams, noise, min_patches: int, cfg_value: float = 2.0, timesteps: int = 10, out=None):
+    """vxc_patch_run: the patch loop of several streams driven from this thread in
+    native code. noise [n][patches][D*P] float32; returns (latents [n][patches][D*P],
+    patches run per stream). out: an optional float32 array of the latents' shape."""
+    n = len(streams)
+    if not (isinstance(noise, np.ndarray) and noise.dtype == np.float32 and noise.flags.c_contiguous):
+        noise = _f32(noise)
+    patches = noise.shape[1]
+    lat = np.empty(noise.shape, np.float32) if out is None else out
+    if lat.shape != noise.shape or lat.dtype != np.float32 or not lat.flags.c_contiguous:
+        raise ValueError("out must be a contiguous float32 array shaped like noise")
+    counts = np.zeros(n, np.int32)
+    arr = (C.c_void_p * n)(*[st._h for st in streams])
+    rc = _lib.vxc_patch_run(arr, n, noise.ctypes.data, patches, min_patches, cfg_value, timesteps, lat.ctypes.data,
+                            counts.ctypes.data)
+    if rc:
+        _check(rc)
+    return lat, counts
+
+
 class Group:
     """Up to 4 streams stepped together: one CUDA graph per group patch, with the
     estimator evaluations of all members batched into one pass over the DiT
@@ -480,3 +502,13 @@ def sdpa_decode_noalloc(q_ptr: int, heads: int, d: int, k_ptr: int, v_ptr: int, 
     _check(lib().vxc_sdpa_decode_noalloc(q_ptr, heads, d, k_ptr, v_ptr, groups, cur, mask_ptr or None,
                                          pk_ptr or None, pv_ptr or None, past, scale, out_ptr, ok_ptr or None,
                                          ov_ptr or None, stream or None))
+
+
+def timestep_embedding(inp, half_dim: int = 512, scale: float = 1000.0, max_period: float = 10000.0,
+                       schedule_mode: int = 0) -> np.ndarray:
+    """VoxCPM2TimestepEmbedding forward on host arrays, computed on the GPU: [n][2 * half_dim]."""
+    x = _f32(inp).ravel()
+    out = np.empty((x.size, 2 * half_dim), np.float32)
+    _check(lib().vxc_timestep_embedding(_p(x), x.size, half_dim, float(scale), float(max_period), schedule_mode,
+                                        _p(out)))
+    return out
