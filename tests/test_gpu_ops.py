@@ -105,6 +105,27 @@ def test_sdpa_split_path_head_groups(rt, G, past, masked):
     assert np.array_equal(gk, wk) and np.array_equal(gv, wv)
 
 
+@pytest.mark.parametrize("keys", [1, 7, 64, 65, 300, 512])
+@pytest.mark.parametrize("G", [1, 8, 16])
+def test_sdpa_single_query_op(rt, keys, G):
+    """One query row over at most 512 keys (the layer's decode shape, config 1 at 512):
+    the load-all-first cluster kernel, [past | cur] rows, with and without a mask,
+    against the oracle at 1e-5."""
+    rng = np.random.default_rng(7 * keys + G)
+    groups, d = 2, 64
+    heads = G * groups
+    past, cur = keys - 1, 1
+    q = rng.standard_normal((heads, 1, d), dtype=np.float32)
+    k = rng.standard_normal((groups, cur, d), dtype=np.float32)
+    v = rng.standard_normal((groups, cur, d), dtype=np.float32)
+    pk = rng.standard_normal((groups, past, d), dtype=np.float32) if past else None
+    pv = rng.standard_normal((groups, past, d), dtype=np.float32) if past else None
+    for mask in (None, (rng.standard_normal((1, keys)) * 2.0).astype(np.float32)):
+        want = oracle.sdpa(q, k, v, mask, pk, pv, 0.125)
+        got = rt.sdpa(q, k, v, mask, pk, pv, 0.125)
+        assert np.abs(got - want).max() <= 1e-5, (keys, G, mask is not None)
+
+
 def test_timestep_embedding_known_answer(rt, kat):
     """tests/test_voxcpm2_timestep_embedding.cpp:165-170: the layer's raw mode on
     t = {0.70710677, 0.25} and schedule mode on (step 1, 10 timesteps), both at 1e-6

@@ -1075,6 +1075,7 @@ void init_kernel_attributes() {
     init_tc_attributes();
     init_tc_rows_attributes();
     init_decode_step_attributes();
+    init_sdpa_op_attributes();
     init_tc_wide_attributes();
 }
 

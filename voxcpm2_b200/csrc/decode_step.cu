@@ -25,8 +25,9 @@
 // spins on each word until its tag appears. A word is written by one 64-bit
 // store and read by one 64-bit load (single-copy atomic), so value and tag always
 // arrive together: no fences, no grid barriers, one round trip per hand-off.
-// Every spin gives up after kWaitNs (%globaltimer) or as soon as another CTA has
-// reported a failure; the kernel then records error 4 and runs to its end.
+// Every spin gives up after about a second (2^31 SM cycles; the bulk-copy waits after
+// kWaitNs of %globaltimer) or as soon as another CTA has reported a failure; the kernel
+// then records error 4 and runs to its end.
 //
 // Sums are in a fixed order (warp butterflies, fixed part orders), so results
 // are bit-reproducible from run to run.
@@ -50,6 +51,8 @@ constexpr int kMaxG = 8;        // query heads per KV head
 constexpr int kMaxChunks = 4;   // 256-element chunks of a lane's slice (K <= 1024 per dot)
 constexpr int kHd = 64;         // head_dim
 constexpr int kScStride = kKvRows + 4;
+// a hand-off spin gives up after 2^31 SM cycles (about a second at the B200's clocks)
+constexpr long long kSpinCycles = 1ll << 31;
 
 void check_launch(cudaError_t e) {
     if (e != cudaSuccess) throw std::runtime_error(std::string("decode step: ") + cudaGetErrorString(e));
@@ -64,6 +67,7 @@ struct StepPlan {
     int x_qkv = 0, x_part = 0, x_hm = 0, x_act = 0, x_h = 0, x_words = 0;
     // shared-memory byte offsets
     int s_wq = 0, s_wo = 0, s_wd = 0, s_xs = 0, s_hs = 0, s_red = 0, s_red2 = 0, s_dpart = 0, s_u = 0;
+    int s_gin = 0, s_gpost = 0, s_rope = 0;  // input-norm gain, post-norm gains [2][H] (by layer parity), RoPE row
     // attention CTAs, inside the U region
     int s_kb = 0, s_vb = 0, s_qs = 0, s_kn = 0, s_vn = 0, s_sc = 0, s_accq = 0, s_accr = 0, s_ml = 0, s_act = 0;
     int smem = 0;
@@ -96,7 +100,7 @@ __device__ bool xgather(const u64* const (&ptr)[N], int cnt, uint32_t tag, float
 #pragma unroll
     for (int k = 0; k < N; ++k)
         if (k < cnt) pending |= 1u << k;
-    uint64_t start = 0;
+    long long start = 0;
     bool timing = false;
     while (pending) {
         u64 w[N];
@@ -110,11 +114,47 @@ __device__ bool xgather(const u64* const (&ptr)[N], int cnt, uint32_t tag, float
                 pending &= ~(1u << k);
             }
         if (pending) {
-            const uint64_t now = global_ns();
+            // the SM cycle counter (cheap to read, unlike %globaltimer) bounds the spin
+            const long long now = clock64();
             if (!timing) {
                 start = now;
                 timing = true;
-            } else if (now - start > kWaitNs || ab.raised()) {
+            } else if (now - start > kSpinCycles || ab.raised()) {
+                ab.raise();
+                return false;
+            }
+        }
+    }
+    return true;
+}
+
+// The same for words base[idx[k]] (offsets instead of pointers: fewer registers).
+template <int N>
+__device__ bool xgather_at(const u64* base, const int (&idx)[N], int cnt, uint32_t tag, float (&v)[N], const Abort& ab) {
+    uint32_t pending = 0;
+#pragma unroll
+    for (int k = 0; k < N; ++k)
+        if (k < cnt) pending |= 1u << k;
+    long long start = 0;
+    bool timing = false;
+    while (pending) {
+        u64 w[N];
+#pragma unroll
+        for (int k = 0; k < N; ++k)
+            if ((pending >> k) & 1u) w[k] = xld(base + idx[k]);
+#pragma unroll
+        for (int k = 0; k < N; ++k)
+            if (((pending >> k) & 1u) && static_cast<uint32_t>(w[k] >> 32) == tag) {
+                v[k] = __uint_as_float(static_cast<uint32_t>(w[k]));
+                pending &= ~(1u << k);
+            }
+        if (pending) {
+            // the SM cycle counter (cheap to read, unlike %globaltimer) bounds the spin
+            const long long now = clock64();
+            if (!timing) {
+                start = now;
+                timing = true;
+            } else if (now - start > kSpinCycles || ab.raised()) {
                 ab.raise();
                 return false;
             }
@@ -186,17 +226,35 @@ __device__ __forceinline__ void load_slice(const float* src, int nc, int lane, f
     }
 }
 
-// A weight row slice (fp16 in shared memory) . the lane's slice, summed over the warp.
-__device__ __forceinline__ float row_dot(const __half* w, const float (&xr)[kMaxChunks][8], int nc, int lane) {
-    float acc = 0.f;
+// n <= R weight rows (fp16 in shared memory, w[r]) . the lane's slice, each summed over
+// the warp: every load of all rows issued first, one FMA chain per (row, chunk), and
+// the rows' butterflies interleaved, so the warp waits on one latency, not R x 4.
+template <int R>
+__device__ __forceinline__ void rows_dot(const __half* const (&w)[R], int n, const float (&xr)[kMaxChunks][8], int nc,
+                                         int lane, float (&out)[R]) {
+    uint4 wv[R][kMaxChunks];
 #pragma unroll
-    for (int c = 0; c < kMaxChunks; ++c)
-        if (c < nc) {
-            const uint4 wv = *reinterpret_cast<const uint4*>(w + (c * 32 + lane) * 8);
-            acc = dot8(wv, make_float4(xr[c][0], xr[c][1], xr[c][2], xr[c][3]),
-                       make_float4(xr[c][4], xr[c][5], xr[c][6], xr[c][7]), acc);
-        }
-    return warp_sum(acc);
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int c = 0; c < kMaxChunks; ++c)
+            wv[r][c] = (r < n && c < nc) ? *reinterpret_cast<const uint4*>(w[r] + (c * 32 + lane) * 8)
+                                         : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        float part[kMaxChunks];
+#pragma unroll
+        for (int c = 0; c < kMaxChunks; ++c)
+            part[c] = dot8(wv[r][c], make_float4(xr[c][0], xr[c][1], xr[c][2], xr[c][3]),
+                           make_float4(xr[c][4], xr[c][5], xr[c][6], xr[c][7]), 0.f);
+        float acc = part[0];
+#pragma unroll
+        for (int c = 1; c < kMaxChunks; ++c) acc += part[c];
+        out[r] = acc;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int r = 0; r < R; ++r) out[r] += __shfl_xor_sync(0xffffffffu, out[r], o);
 }
 
 // Sum over the CTA in a fixed order; every thread gets the total. red: kWarps floats.
@@ -271,10 +329,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecodeSt
                              static_cast<uint32_t>(__cvta_generic_to_shared(&bar[k])))
                          : "memory");
     };
-    auto fill_q = [&](int l) {
+    auto fill_q = [&](int l) {  // q/k/v rows, and layer l's two RMSNorm gains
         const __half* w = a.lw[l * 6 + 0];
-        const uint32_t rowb = static_cast<uint32_t>(H) * 2, bytes = 2u * nq * rowb;
-        if (bytes) bar_expect(&bar[0], bytes);
+        const uint32_t rowb = static_cast<uint32_t>(H) * 2, bytes = 2u * nq * rowb + 2u * rowb;
+        bar_expect(&bar[0], bytes);
+        bulk_copy(sm + p.s_gin, a.lw[l * 6 + 4], rowb, &bar[0]);
+        bulk_copy(sm + p.s_gpost + (l & 1) * rowb, a.lw[l * 6 + 5], rowb, &bar[0]);
         for (int i = 0; i < nq; ++i) {
             const int u = u0 + i, hh = u / (kHd / 2), j = u - hh * (kHd / 2);
             const size_t r0 = static_cast<size_t>(hh) * kHd + j;
@@ -346,9 +406,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecodeSt
     __syncthreads();
 
     const int nch = H / 256, ncho = Ko / 256;
+    float* rope_s = reinterpret_cast<float*>(sm + p.s_rope);  // cos [64] | sin [64] of position pos
+    if (a.rope_cos && tid < 2 * kHd) {
+        const bool lng = a.rope_cos_long && pos + 1 > a.rope_long_from;  // make_rope_cache's rule for one row
+        const float* c = (lng ? a.rope_cos_long : a.rope_cos) + static_cast<size_t>(pos) * kHd;
+        const float* sn = (lng ? a.rope_sin_long : a.rope_sin) + static_cast<size_t>(pos) * kHd;
+        rope_s[tid] = tid < kHd ? c[tid] : sn[tid - kHd];
+    }
+    const __half* gin = reinterpret_cast<const __half*>(sm + p.s_gin);
     for (int l = 0; l < L; ++l) {
-        const __half* in_norm = a.lw[l * 6 + 4];
-        const __half* post_norm = a.lw[l * 6 + 5];
+        const __half* post_norm = reinterpret_cast<const __half*>(sm + p.s_gpost) + (l & 1) * H;
         const bool last = l + 1 == L;
 
         // ---------------- phase 1: RMSNorm(h) -> q/k/v rows, RoPE, KV append
@@ -357,21 +424,26 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecodeSt
         } else {
             ok &= xget1(X + p.x_h, H, tag(l - 1, 4), hs, ab);
         }
+        wait_fill(0);
         __syncthreads();
         {
             float ss = 0.f;
             for (int i = tid; i < H; i += kThreads) ss += hs[i] * hs[i];
             const float inv_rms = rsqrtf(block_sum(ss, red) / static_cast<float>(H) + a.eps);
-            for (int i = tid; i < H; i += kThreads) xs[i] = hs[i] * inv_rms * __half2float(in_norm[i]);
+            for (int i = tid; i < H; i += kThreads) xs[i] = hs[i] * inv_rms * __half2float(gin[i]);
         }
         __syncthreads();
-        wait_fill(0);
         {
             float xr[kMaxChunks][8];
             load_slice(xs, nch, lane, xr);
-            for (int r = warp; r < 2 * nq; r += kWarps) {
-                const float d = row_dot(wq + static_cast<size_t>(r) * H, xr, nch, lane);
-                if (lane == 0) red2[r] = d;
+            for (int r0 = warp * 2; r0 < 2 * nq; r0 += kWarps * 2) {
+                const __half* w2[2] = {wq + static_cast<size_t>(r0) * H, wq + static_cast<size_t>(r0 + 1) * H};
+                float d2[2];
+                rows_dot<2>(w2, min(2, 2 * nq - r0), xr, nch, lane, d2);
+                if (lane == 0) {
+                    red2[r0] = d2[0];
+                    if (r0 + 1 < 2 * nq) red2[r0 + 1] = d2[1];
+                }
             }
         }
         __syncthreads();
@@ -381,9 +453,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecodeSt
             float v0 = a0, v1 = a1;
             const bool is_v = hh >= hq + hkv;
             if (!is_v && a.rope_cos) {  // apply_rotary_pos_emb (rotate_half) at position pos
-                const bool lng = a.rope_cos_long && pos + 1 > a.rope_long_from;
-                const float* c = (lng ? a.rope_cos_long : a.rope_cos) + static_cast<size_t>(pos) * kHd;
-                const float* s = (lng ? a.rope_sin_long : a.rope_sin) + static_cast<size_t>(pos) * kHd;
+                const float* c = rope_s;
+                const float* s = rope_s + kHd;
                 v0 = a0 * c[j] + (-a1) * s[j];
                 v1 = a1 * c[j + half] + a0 * s[j + half];
             }
@@ -399,9 +470,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecodeSt
             }
         }
         __syncthreads();
-        if (tid == 0 && !last) {
+        if (tid == 0) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            fill_q(l + 1);
+            if (!last) fill_q(l + 1);
+            if (l > 0) {
+                // this layer's down and gate/up slices: issued only now, after the hand-off at the
+                // layer's start, so their bursts do not queue that hand-off's loads
+                fill_d(l);
+                if (!attn) fill_u(l, 0);
+            }
         }
 
         // ---------------- phase 2: attention over this split's keys (attention CTAs)
@@ -440,6 +517,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecodeSt
 #pragma unroll
                         for (int i = 0; i < 8; ++i)
                             qr[h][i] = hg0 + h < G ? qs[(hg0 + h) * kHd + l8 * 8 + i] * a.scale : 0.f;
+#pragma unroll 2
                     for (int tb = warp * 4; tb < n; tb += kWarps * 4) {
                         const int t = tb + kk;
                         const bool valid = t < n;
@@ -453,16 +531,26 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecodeSt
 #pragma unroll
                             for (int i = 0; i < 8; ++i) kv[i] = 0.f;
                         }
+                        float dv[4];
 #pragma unroll
                         for (int h = 0; h < 4; ++h) {
                             float d = 0.f;
 #pragma unroll
                             for (int i = 0; i < 8; ++i) d = fmaf(qr[h][i], kv[i], d);
-                            d += __shfl_xor_sync(0xffffffffu, d, 4);
-                            d += __shfl_xor_sync(0xffffffffu, d, 2);
-                            d += __shfl_xor_sync(0xffffffffu, d, 1);
-                            if (valid && l8 == 0 && hg0 + h < G) sc[(hg0 + h) * kScStride + t] = d;
+                            dv[h] = d;
                         }
+                        // transposed butterfly over the key's 8 lanes: 4 shuffles for 4 heads;
+                        // lanes 2h' and 2h' + 1 of each half end with head (hi ? 2 : 0) + b1
+                        const bool hi = (lane & 4) != 0, b1 = (lane & 2) != 0;
+                        float s0 = hi ? dv[2] : dv[0], s1 = hi ? dv[3] : dv[1];
+                        const float o0 = hi ? dv[0] : dv[2], o1 = hi ? dv[1] : dv[3];
+                        s0 += __shfl_xor_sync(0xffffffffu, o0, 4);
+                        s1 += __shfl_xor_sync(0xffffffffu, o1, 4);
+                        float tsum = b1 ? s1 : s0;
+                        tsum += __shfl_xor_sync(0xffffffffu, b1 ? s0 : s1, 2);
+                        tsum += __shfl_xor_sync(0xffffffffu, tsum, 1);
+                        const int hh = hg0 + (hi ? 2 : 0) + (b1 ? 1 : 0);
+                        if (valid && (lane & 1) == 0 && hh < G) sc[hh * kScStride + t] = tsum;
                     }
                 }
                 __syncthreads();
@@ -495,6 +583,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecodeSt
                     const int qi = tid / per, r = tid - qi * per, h = r / 16, d4 = r - h * 16;
                     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
                     if (qi < groups)
+#pragma unroll 4
                         for (int t = qi; t < n; t += groups) {
                             const float pr = sc[h * kScStride + t];
                             const float4 v = *reinterpret_cast<const float4*>(vb + t * kHd + d4 * 4);
@@ -527,35 +616,35 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecodeSt
         }
 
         // ---------------- phase 3: combine the splits -> attention vector -> o rows + residual
-        // thread: elements (e, e + 1) of one head, e = 2 tid + 2 kThreads i: per split
-        // its m, l and the two P.V values, all loads in flight together
-        for (int e = 2 * tid; e < Ko; e += 2 * kThreads) {
+        // thread: elements e .. e + 3 of one head, e = 4 tid (+ 4 kThreads i): per split its m,
+        // l and the four P.V values, one gather with all loads in flight
+        for (int e = 4 * tid; e < Ko; e += 4 * kThreads) {
             const uint32_t tp = tag(l, 1);
             const int h = e / kHd, d = e - h * kHd, kh = h / G, hg = h - kh * G;
-            const u64* ptr[4 * kSplits];
-            float v[4 * kSplits];
+            int idx[6 * kSplits];
+            float v[6 * kSplits];
 #pragma unroll
             for (int sp2 = 0; sp2 < kSplits; ++sp2) {
-                const u64* base = X + p.x_part + static_cast<size_t>((kh * kSplits + sp2) * G) * (kHd + 2);
-                ptr[4 * sp2] = base + hg;
-                ptr[4 * sp2 + 1] = base + G + hg;
-                ptr[4 * sp2 + 2] = base + 2 * G + hg * kHd + d;
-                ptr[4 * sp2 + 3] = base + 2 * G + hg * kHd + d + 1;
+                const int base = (kh * kSplits + sp2) * G * (kHd + 2);
+                idx[6 * sp2] = base + hg;
+                idx[6 * sp2 + 1] = base + G + hg;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) idx[6 * sp2 + 2 + j] = base + 2 * G + hg * kHd + d + j;
             }
-            ok &= xgather<4 * kSplits>(ptr, 4 * kSplits, tp, v, ab);
+            ok &= xgather_at<6 * kSplits>(X + p.x_part, idx, 6 * kSplits, tp, v, ab);
             float M = -1e30f;
 #pragma unroll
-            for (int sp2 = 0; sp2 < kSplits; ++sp2) M = fmaxf(M, v[4 * sp2]);
-            float den = 0.f, n0 = 0.f, n1 = 0.f;
+            for (int sp2 = 0; sp2 < kSplits; ++sp2) M = fmaxf(M, v[6 * sp2]);
+            float den = 0.f, num[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int sp2 = 0; sp2 < kSplits; ++sp2) {
-                const float c = expf(v[4 * sp2] - M);
-                den = fmaf(c, v[4 * sp2 + 1], den);
-                n0 = fmaf(c, v[4 * sp2 + 2], n0);
-                n1 = fmaf(c, v[4 * sp2 + 3], n1);
+                const float c = expf(v[6 * sp2] - M);
+                den = fmaf(c, v[6 * sp2 + 1], den);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) num[j] = fmaf(c, v[6 * sp2 + 2 + j], num[j]);
             }
-            xs[e] = n0 / den;
-            xs[e + 1] = n1 / den;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) xs[e + j] = num[j] / den;
         }
         __syncthreads();
         wait_fill(1);
@@ -564,8 +653,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecodeSt
             load_slice(xs, ncho, lane, xr);
             const uint32_t tg = tag(l, 2);
             for (int r = warp; r < no; r += kWarps) {
-                const float d = row_dot(wo + static_cast<size_t>(r) * Ko, xr, ncho, lane);
-                if (lane == 0) xput(X + p.x_hm + o0 + r, hs[o0 + r] + (a.rscale == 1.f ? d : d * a.rscale), tg);
+                const __half* w1[1] = {wo + static_cast<size_t>(r) * Ko};
+                float d1[1];
+                rows_dot<1>(w1, 1, xr, ncho, lane, d1);
+                if (lane == 0) xput(X + p.x_hm + o0 + r, hs[o0 + r] + (a.rscale == 1.f ? d1[0] : d1[0] * a.rscale), tg);
             }
         }
         __syncthreads();
@@ -587,10 +678,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecodeSt
             float xr[kMaxChunks][8];
             load_slice(xs, nch, lane, xr);
             const uint32_t tg = tag(l, 3);
-            for (int i = warp; i < ngu; i += kWarps) {
-                const float g = row_dot(wu + static_cast<size_t>(i) * H, xr, nch, lane);
-                const float u = row_dot(wu + static_cast<size_t>(ngu + i) * H, xr, nch, lane);
-                if (lane == 0) xput(X + p.x_act + g0 + i, silu(g) * u, tg);
+            for (int i = warp * 2; i < ngu; i += kWarps * 2) {
+                const int i1 = min(i + 1, ngu - 1);
+                const __half* w4[4] = {wu + static_cast<size_t>(i) * H, wu + static_cast<size_t>(ngu + i) * H,
+                                       wu + static_cast<size_t>(i1) * H, wu + static_cast<size_t>(ngu + i1) * H};
+                float d4[4];
+                rows_dot<4>(w4, i + 1 < ngu ? 4 : 2, xr, nch, lane, d4);
+                if (lane == 0) {
+                    xput(X + p.x_act + g0 + i, silu(d4[0]) * d4[1], tg);
+                    if (i + 1 < ngu) xput(X + p.x_act + g0 + i + 1, silu(d4[2]) * d4[3], tg);
+                }
             }
         }
         __syncthreads();  // gate/up CTAs: the slice is consumed; 'act' may overwrite it
@@ -600,17 +697,32 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecodeSt
         __syncthreads();
         wait_fill(3);
         {
+            // task t = (row t / np, K part t % np); a warp takes tasks warp, warp + 8, ...
             const int tasks = no * p.np, kc = p.kp / 256;
             float xr[kMaxChunks][8];
             int loaded = -1;
-            for (int t = warp; t < tasks; t += kWarps) {
-                const int r = t / p.np, q = t - r * p.np;
+            for (int t0 = warp; t0 < tasks;) {
+                const int q = t0 % p.np;
+                // this warp's next tasks of the same K part (up to 4), one batch
+                int tk[4], n = 0;
+                int t = t0;
+                for (; t < tasks && n < 4; t += kWarps) {
+                    if (t % p.np != q) break;
+                    tk[n++] = t;
+                }
+                for (int k = n; k < 4; ++k) tk[k] = tk[0];
                 if (q != loaded) {
                     load_slice(act + q * p.kp, kc, lane, xr);
                     loaded = q;
                 }
-                const float d = row_dot(wd + static_cast<size_t>(r) * F + q * p.kp, xr, kc, lane);
-                if (lane == 0) dpart[t] = d;
+                const __half* w4[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) w4[k] = wd + static_cast<size_t>(tk[k] / p.np) * F + q * p.kp;
+                float d4[4];
+                rows_dot<4>(w4, n, xr, kc, lane, d4);
+                if (lane == 0)
+                    for (int k = 0; k < n; ++k) dpart[tk[k]] = d4[k];
+                t0 = t;
             }
         }
         __syncthreads();
@@ -621,12 +733,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecodeSt
             xput(X + p.x_h + o0 + tid, hn, tag(l, 4));
             if (last) a.h[o0 + tid] = hn;
         }
-        __syncthreads();
-        if (tid == 0 && !last) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            fill_d(l + 1);
-            if (!attn) fill_u(l + 1, 0);
-        }
+        __syncthreads();  // the down and gate/up slices (and act) are consumed: layer l + 1 refills them
     }
 
     // ---------------- final RMSNorm of the CTA's rows
@@ -691,6 +798,9 @@ StepPlan make_plan(const DecodeStepArgs& a, int nb) {
     p.s_red = take(kWarps * 4);
     p.s_red2 = take(2 * p.nq * 4);
     p.s_dpart = take(std::max(1, p.no * p.np) * 4);
+    p.s_gin = take(H * 2);
+    p.s_gpost = take(2 * H * 2);
+    p.s_rope = take(2 * kHd * 4);
     p.s_u = off;
     // the U region: gate/up slice (and SiLU * up after it), or the attention CTAs' buffers
     int u = 0;

@@ -124,6 +124,12 @@ struct AttnBatch {
     StreamCtl* ctl[4] = {};
 };
 void launch_attn_decode_cluster_batch(const AttnArgs& a, const AttnBatch& b, cudaStream_t s, bool pdl);
+// The layer-contract op (sdpa_op.cu): one query row over at most 512 fp32 keys given as
+// [k0 rows | k1 rows] per KV head, no control block; every load issued up front, one
+// 8-CTA cluster per KV head combining through shared memory.
+bool sdpa_op_supported(const AttnArgs& a);
+void launch_sdpa_op(const AttnArgs& a, cudaStream_t s, bool pdl);
+void init_sdpa_op_attributes();
 
 // final RMSNorm of a decoder step: out = norm(h) * g; optionally bump kv_len.
 void launch_final_norm(const float* h, const __half* g, float eps, int H, float* out, float* out2,

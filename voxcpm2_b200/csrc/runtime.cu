@@ -2339,7 +2339,17 @@ VXC_API int32_t vxc_sdpa(const float* q, int32_t heads, int32_t src, int32_t d, 
             aa.head_dim = d;
             aa.scale = rs;
             aa.out = out;
-            launch_attn_decode_cluster(aa, cs, false);
+            // programmatic dependent launch: the kernel waits (griddepcontrol.wait) before it
+            // reads anything, so its launch overlaps the tail of the stream's previous kernel.
+            // Rows on 16-byte boundaries (always, from vxc_sdpa_host) take the load-all-first
+            // op kernel; others the cluster decode kernel, which loads q by element.
+            const bool aligned = ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(aa.k0) |
+                                   reinterpret_cast<uintptr_t>(aa.v0) | reinterpret_cast<uintptr_t>(aa.k1) |
+                                   reinterpret_cast<uintptr_t>(aa.v1)) & 15) == 0;
+            if (aligned && sdpa_op_supported(aa))
+                launch_sdpa_op(aa, cs, true);
+            else
+                launch_attn_decode_cluster(aa, cs, true);
         } else if (src == 1 && d == 64 && dv == 64 && G <= 16 && mask_c <= 1 && groups <= 64) {
             // longer: split-K flash decode over [past | cur] (fp32 rows). Its split partials
             // live in a scratch buffer kept per (device, CUDA stream): calls on one
@@ -2387,7 +2397,7 @@ VXC_API int32_t vxc_sdpa(const float* q, int32_t heads, int32_t src, int32_t d, 
             aa.partial = sc.partial;
             aa.counters = sc.counters;
             aa.out = out;
-            launch_attn_decode(aa, false, cs, false);
+            launch_attn_decode(aa, false, cs, true);
         } else {
             launch_sdpa_rows_f32(q, heads, src, d, k, v, groups, cur, dv, mask, mask_c, past_k, past_v, past, rs, out, cs);
         }
