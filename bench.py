@@ -46,10 +46,9 @@ def parse():
     p.add_argument("--group-members", type=int, default=4, help="streams per group (1..4)")
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--cpu-sample-patches", type=int, default=6)
-    p.add_argument("--range", choices=["stream", "group", "step"], default=None,
+    p.add_argument("--range", choices=["stream", "group"], default=None,
                    help="run a few patches and exit, for an ncu launch list (one metric, one pass): 'stream' = 3 "
-                        "patches of one lone stream, 'group' = 3 patches of one stream group (--group-members), "
-                        "'step' = 256 prefilled rows then 3 persistent base-decoder steps")
+                        "patches of one lone stream, 'group' = 3 patches of one stream group (--group-members)")
     return p.parse_args()
 
 
@@ -464,7 +463,7 @@ def group_rate(rt, synthetic, dev, cfg, groups, members, K, W, min_patches, rank
                     "decoder steps as batched GEMVs (one weight read, one dot product per member)"}
 
 
-def decoder_steps_at_config(rt, dev, cfg, ids_seed, peak, persistent=False):
+def decoder_steps_at_config(rt, dev, cfg, ids_seed, peak):
     """One whole base / residual KV-cache decode step at batch 1 at the lengths of
     their configurations: the base decoder after 256 prefilled rows growing to 456
     (past 256..455), the residual decoder growing from 256 to 512 (past 256..511).
@@ -475,14 +474,7 @@ def decoder_steps_at_config(rt, dev, cfg, ids_seed, peak, persistent=False):
     out = {}
     for which, name, kind, lo, hi in ((0, "base_decoder", "base_step", 256, 455),
                                       (1, "residual_decoder", "res_step", 256, 511)):
-        if persistent:
-            os.environ["VXC_DECODE_STEP"] = "persistent"
-        try:
-            s = rt.Stream(dev, kv_capacity=520)
-        finally:
-            os.environ.pop("VXC_DECODE_STEP", None)
-        if persistent:
-            name += "_persistent"
+        s = rt.Stream(dev, kv_capacity=520)
         if which == 0:
             rows = s.text_embed(synthetic.token_ids(cfg, 256, seed=ids_seed))
         else:
@@ -503,9 +495,7 @@ def decoder_steps_at_config(rt, dev, cfg, ids_seed, peak, persistent=False):
         out[name] = {"us": round(us, 2), "bytes": nb_mean, "GB/s": round(gbs, 1), "frac": gbs / peak,
                      "kv_rows": [lo, hi + 1], "us_at_past": {str(k): round(1e3 * v[0], 2) for k, v in points.items()},
                      "how": "mean of the first and last step of the configuration (the step time is affine in the KV "
-                            "length); each point 50 steps replayed in one graph, CUDA events",
-                     "form": "one cooperative launch per step (VXC_DECODE_STEP=persistent)" if persistent else
-                             "five kernels per layer + final norm, PDL chain"}
+                            "length); each point 50 steps replayed in one graph, CUDA events"}
     return out
 
 
@@ -677,7 +667,6 @@ def run_ours(args):
     # configs 2 and 3: one whole KV-cache decode step at batch 1 at their KV lengths;
     # config 4: one estimator evaluation
     decode_step = decoder_steps_at_config(rt, dev, cfg, 4242, peak)
-    decode_step.update(decoder_steps_at_config(rt, dev, cfg, 4242, peak, persistent=True))
     km, kb = streams[0].profile_kernel("dit_eval", 50)
     decode_step["dit_estimator_eval"] = {"us": round(1e3 * km, 2), "bytes": kb,
                                          "GB/s": round(kb / (km / 1e3) / 1e9, 1), "frac": kb / (km / 1e3) / 1e9 / peak}
@@ -709,9 +698,8 @@ def run_ours(args):
     p50_single = lone_latency(one, W + min(K, 12))
 
     # ---- the same for a stream tuned for one utterance at a time: ~296 CTAs per tensor-core
-    # launch, a 4-stage ring, and decoder steps as one persistent launch each (the knobs are
-    # read when a stream is created)
-    LATENCY_TUNING = {"VXC_TC_TARGET": "296", "VXC_TC_STAGES": "4", "VXC_DECODE_STEP": "persistent"}
+    # launch and a 4-stage ring (the knobs are read when a stream is created)
+    LATENCY_TUNING = {"VXC_TC_TARGET": "296", "VXC_TC_STAGES": "4"}
     os.environ.update(LATENCY_TUNING)
     try:
         solo = rt.Stream(dev, kv_capacity=max(cap, 512))
@@ -858,17 +846,6 @@ def run_range(args):
     from voxcpm2_b200 import synthetic
     from voxcpm2_b200.config import BENCH
     dev = rt.Device(BENCH, 0, synthetic.model_blobs(BENCH, 0))
-    if args.range == "step":
-        os.environ["VXC_DECODE_STEP"] = "persistent"
-        st = rt.Stream(dev, kv_capacity=512)
-        os.environ.pop("VXC_DECODE_STEP", None)
-        st.decoder_step(0, st.text_embed(synthetic.token_ids(BENCH, 256, seed=5)))
-        for i in range(3):
-            st.decoder_step(0, synthetic.normal((1, BENCH.hidden), seed=6 + i))
-        print(json.dumps({"range": "step", "kv_rows": st.token_count(0)}))
-        st.close()
-        dev.close()
-        return 0
     if args.range == "group":
         g = rt.Group(dev, args.group_members, kv_capacity=512)
         for m, st in enumerate(g.streams):

@@ -1074,7 +1074,6 @@ void init_kernel_attributes() {
     init_batched_attributes();
     init_tc_attributes();
     init_tc_rows_attributes();
-    init_decode_step_attributes();
     init_sdpa_op_attributes();
     init_tc_wide_attributes();
 }

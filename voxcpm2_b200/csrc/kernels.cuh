@@ -375,36 +375,6 @@ void launch_tc_wide(const CUtensorMap& map_a, const CUtensorMap& map_b, const Tc
                     bool pdl);
 void init_tc_wide_attributes();
 
-// Persistent batch-1 decoder step (decode_step.cu): every layer of one KV-cache
-// step in one cooperative launch (one CTA per SM), weight slices streamed into
-// shared memory a layer ahead, vectors handed between phases as tagged words.
-struct DecodeStepArgs {
-    const __half* const* lw = nullptr;  // device array [layers][6]: wqkv, wo, wgateup, wdown, in_norm, post_norm
-    const __half* final_norm = nullptr;
-    int layers = 0, H = 0, F = 0, hq = 0, hkv = 0, hd = 64;
-    float eps = 1e-5f, rscale = 1.f, scale = 0.125f;
-    float* h = nullptr;                 // [H] the step's input embedding; the final residual stream on exit
-    float* out = nullptr;               // [H] final RMSNorm output
-    float* out2 = nullptr;              // optional second copy of out
-    float* k_cache = nullptr;           // [layers][hkv][cap][hd] fp32
-    float* v_cache = nullptr;
-    int cap = 0;
-    const float* rope_cos = nullptr;    // [cap][hd] or null (no RoPE)
-    const float* rope_sin = nullptr;
-    const float* rope_cos_long = nullptr;
-    const float* rope_sin_long = nullptr;
-    int rope_long_from = 1 << 30;
-    StreamCtl* ctl = nullptr;
-    int which = 0, advance = 1, skip_if_stopped = 0;
-    unsigned long long* xbuf = nullptr;  // decode_step_words() exchange words, zeroed once before first use
-    unsigned* seq = nullptr;             // 2 words, zeroed once: invocation counter, failure flag
-};
-int decode_step_grid();                              // CTAs of one launch (the SM count)
-size_t decode_step_words(const DecodeStepArgs& a);   // exchange words for these shapes
-void check_decode_step(const DecodeStepArgs& a);     // shapes only; throws std::invalid_argument if unsupported
-void launch_decode_step(const DecodeStepArgs& a, cudaStream_t s);
-void init_decode_step_attributes();
-
 // Raise the dynamic shared-memory limit of the kernels that need more than 48 KB
 // (call once per device, outside stream capture).
 void init_kernel_attributes();

@@ -305,27 +305,9 @@ struct vxc_device {
     // per decoder layer: TMA maps of W_qkv, W_o, W_gate|up, W_down for the prefill's row-block linears
     std::vector<std::array<CUtensorMap, 4>> base_maps, res_maps;
     uint64_t epoch = 0;  // bumped by every weight upload (invalidates derived tables)
-    // per decoder: device array [layers][6] of wqkv, wo, wgateup, wdown, in_norm, post_norm
-    // (the persistent decoder step's weight table)
-    const __half** step_lw[2] = {};
 };
 
 namespace {
-
-// The persistent decoder step's per-layer weight table of one decoder, on the device.
-void upload_step_table(vxc_device* dev, int which) {
-    const std::vector<LayerW>& layers = which == 0 ? dev->base : dev->res;
-    std::vector<const __half*> t;
-    for (const LayerW& L : layers) {
-        for (const __half* w : {L.wqkv, L.wo, L.wgateup, L.wdown, L.in_norm, L.post_norm}) {
-            if (reinterpret_cast<uintptr_t>(w) & 15) throw std::invalid_argument("decoder weights must be 16-byte aligned");
-            t.push_back(w);
-        }
-    }
-    if (!dev->step_lw[which]) dev->step_lw[which] = dev_alloc<const __half*>(t.size());
-    ck(cudaMemcpy(dev->step_lw[which], t.data(), sizeof(const __half*) * t.size(), cudaMemcpyHostToDevice),
-       "decoder step table");
-}
 
 struct DitPtrs {
     const __half *in_w, *in_b, *cond_w, *cond_b, *t1_w, *t1_b, *t2_w, *t2_b, *dt1_w, *dt1_b, *dt2_w, *dt2_b;
@@ -437,12 +419,6 @@ struct vxc_stream {
     // VXC_BULK_GEMV=1 for the bulk-copy form (weight rows into shared memory before the
     // dependency wait; stream groups always use it, batched over their members)
     bool bulk_gemv = false;
-    // decoder steps as one persistent cooperative launch (VXC_DECODE_STEP=persistent): every SM
-    // streams its slice of the next layer's weights while the current layer computes; for a
-    // stream that has the GPU to itself (it occupies every SM for the step)
-    bool step_persist = false;
-    unsigned long long* xstep[2] = {};  // per decoder: the step's exchange words
-    unsigned* xseq = nullptr;           // per decoder: invocation counter, failure flag
     int* dcount = nullptr;  // dit_out arrival counter
     cudaGraphExec_t graph = nullptr;
     int graph_kernels = 0;
@@ -464,8 +440,6 @@ void free_all(vxc_stream* s) {
                     s->dxn, s->dqkv, s->dattn, s->dact, s->est, s->gen_in, s->ph, s->pxn, s->pqkv, s->pattn,
                     s->pact, s->pcat, s->pids, s->xb_n, s->xb_a, s->xb_act};
     for (void* p : ptrs)
-        if (p) cudaFree(p);
-    for (void* p : {static_cast<void*>(s->xstep[0]), static_cast<void*>(s->xstep[1]), static_cast<void*>(s->xseq)})
         if (p) cudaFree(p);
     for (auto& kv : s->ttab)
         if (kv.second.dev) cudaFree(kv.second.dev);
@@ -546,52 +520,10 @@ void set_decode_rope(GemvArgs& a, const vxc_stream* s) {
 // the input embedding); writes the final-norm output to out (+ out2) and bumps
 // kv_len[which] on the device (unless advance is 0). ctl_override replaces the
 // stream's control block (the step profile runs on a private one).
-DecodeStepArgs decode_step_args(const vxc_stream* s, int which) {
-    const vxc_device* dev = s->dev;
-    const vxc_model_desc& d = dev->desc;
-    DecodeStepArgs a;
-    a.lw = dev->step_lw[which];
-    a.final_norm = which == 0 ? dev->base_norm : dev->res_norm;
-    a.layers = which == 0 ? d.base_layers : d.res_layers;
-    a.H = d.hidden;
-    a.F = d.ffn;
-    a.hq = d.q_heads;
-    a.hkv = d.kv_heads;
-    a.hd = d.head_dim;
-    a.eps = d.rms_eps;
-    a.rscale = which == 0 ? d.base_residual_scale : d.res_residual_scale;
-    a.scale = 1.0f / std::sqrt(static_cast<float>(d.head_dim));
-    a.h = s->h[which];
-    a.k_cache = s->kc[which];
-    a.v_cache = s->vc[which];
-    a.cap = s->cap;
-    if (which == 0) {
-        a.rope_cos = s->rope_cos;
-        a.rope_sin = s->rope_sin;
-        a.rope_cos_long = s->rope_cos_l;
-        a.rope_sin_long = s->rope_sin_l;
-        a.rope_long_from = d.rope_original_max;
-    }
-    a.ctl = s->ctl;
-    a.which = which;
-    a.xbuf = s->xstep[which];
-    a.seq = s->xseq ? s->xseq + 2 * which : nullptr;
-    return a;
-}
-
 void enqueue_decoder_step(vxc_stream* s, int which, float* out, float* out2, int skip,
                           StreamCtl* ctl_override = nullptr, int advance = 1) {
     StreamCtl* ctl = ctl_override ? ctl_override : s->ctl;
-    if (s->step_persist) {
-        DecodeStepArgs a = decode_step_args(s, which);
-        a.out = out;
-        a.out2 = out2;
-        a.ctl = ctl;
-        a.advance = advance;
-        a.skip_if_stopped = skip;
-        launch_decode_step(a, s->cs);
-        return;
-    }
+
     auto gemv = s->bulk_gemv ? launch_gemv_bulk : launch_gemv;
     const vxc_device* dev = s->dev;
     const vxc_model_desc& d = dev->desc;
@@ -1807,8 +1739,6 @@ VXC_API void vxc_device_destroy(vxc_device* dev) {
         if (dev->dit_rope_cos) cudaFree(dev->dit_rope_cos);
         if (dev->dit_rope_sin) cudaFree(dev->dit_rope_sin);
         if (dev->temb_freq) cudaFree(dev->temb_freq);
-        for (const __half** t : dev->step_lw)
-            if (t) cudaFree(t);
     }
     delete dev;
 }
@@ -1828,12 +1758,10 @@ VXC_API int32_t vxc_load_weights(vxc_device* dev, int32_t component, const void*
             dev->base = carve_decoder(dev->blob[component], base_shape(dev->desc), &fn);
             dev->base_norm = fn;
             dev->base_maps = decoder_maps(dev->desc, dev->base);
-            upload_step_table(dev, 0);
         } else if (component == VXC_RESIDUAL_DECODER) {
             dev->res = carve_decoder(dev->blob[component], res_shape(dev->desc), &fn);
             dev->res_norm = fn;
             dev->res_maps = decoder_maps(dev->desc, dev->res);
-            upload_step_table(dev, 1);
         } else if (component == VXC_DIT_ESTIMATOR) {
             const size_t Hd = dev->desc.dit_hidden, D = dev->desc.feat_dim;
             const __half* base = dev->blob[component] + 2 * (Hd * D + Hd) + 4 * (Hd * Hd + Hd);
@@ -1940,25 +1868,6 @@ VXC_API int32_t vxc_stream_create(vxc_device* dev, int32_t kv_capacity, vxc_stre
         if (const char* nk = std::getenv("VXC_NORM_KERNELS")) s->norm_kernels = std::string(nk) == "1";
         if (const char* rs = std::getenv("VXC_RECV_SHARED")) s->recv_shared = std::string(rs) == "1";
         if (const char* bg = std::getenv("VXC_BULK_GEMV")) s->bulk_gemv = std::string(bg) == "1";
-        if (const char* ds = std::getenv("VXC_DECODE_STEP")) {
-            const std::string form(ds);
-            if (form != "persistent" && form != "chain") throw std::invalid_argument("VXC_DECODE_STEP must be persistent or chain");
-            s->step_persist = form == "persistent";
-        }
-        if (s->step_persist) {
-            size_t words = 0;
-            for (int w = 0; w < 2; ++w) {
-                const DecodeStepArgs a = decode_step_args(s.get(), w);
-                check_decode_step(a);
-                words = std::max(words, decode_step_words(a));
-            }
-            for (int w = 0; w < 2; ++w) {
-                s->xstep[w] = dev_alloc<unsigned long long>(words);
-                ck(cudaMemset(s->xstep[w], 0, words * sizeof(unsigned long long)), "cudaMemset");
-            }
-            s->xseq = dev_alloc<unsigned>(4);
-            ck(cudaMemset(s->xseq, 0, 4 * sizeof(unsigned)), "cudaMemset");
-        }
         if (const char* tt = std::getenv("VXC_TC_TARGET")) {
             s->tc_target = std::atoi(tt);
             if (s->tc_target < 1 || s->tc_target > 4096) throw std::invalid_argument("VXC_TC_TARGET must be in [1, 4096]");
