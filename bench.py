@@ -46,9 +46,10 @@ def parse():
     p.add_argument("--group-members", type=int, default=4, help="streams per group (1..4)")
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--cpu-sample-patches", type=int, default=6)
-    p.add_argument("--range", choices=["stream", "group"], default=None,
-                   help="run a few patches and exit, for an ncu launch list (one metric, one pass): 'stream' = 3 "
-                        "patches of one lone stream, 'group' = 3 patches of one stream group (--group-members)")
+    p.add_argument("--range", choices=["stream", "group", "sdpa"], default=None,
+                   help="run a small case and exit, for ncu: 'stream' = 3 patches of one lone stream, 'group' = 3 "
+                        "patches of one stream group (--group-members), 'sdpa' = 8 calls of the VoxCPM2SDPA op at "
+                        "config 1's shape (q [16][1][64], K/V [2][511 + 1][64])")
     return p.parse_args()
 
 
@@ -845,6 +846,20 @@ def run_range(args):
     from voxcpm2_b200 import runtime as rt
     from voxcpm2_b200 import synthetic
     from voxcpm2_b200.config import BENCH
+    if args.range == "sdpa":
+        import torch
+        dv = torch.device("cuda", 0)
+        g = torch.Generator(device=dv).manual_seed(11)
+        heads, groups, d, past = 16, 2, 64, 511
+        bufs = [torch.randn(n, device=dv, generator=g) for n in (heads * d, groups * d, groups * d, groups * past * d,
+                                                                 groups * past * d)]
+        out = torch.empty(heads * d, device=dv)
+        for _ in range(8):
+            rt.sdpa_device(bufs[0].data_ptr(), heads, 1, d, bufs[1].data_ptr(), bufs[2].data_ptr(), groups, 1, d, 0,
+                           0, bufs[3].data_ptr(), bufs[4].data_ptr(), past, 0.125, out.data_ptr())
+        torch.cuda.synchronize()
+        print(json.dumps({"range": "sdpa", "calls": 8}))
+        return 0
     dev = rt.Device(BENCH, 0, synthetic.model_blobs(BENCH, 0))
     if args.range == "group":
         g = rt.Group(dev, args.group_members, kv_capacity=512)
