@@ -258,6 +258,16 @@ class Ranks:
             from datetime import timedelta
             kw = {"device_id": device} if backend == "nccl" else {}
             dist.init_process_group(backend, timeout=timedelta(seconds=timeout_s), **kw)
+            # NCCL sets up its connections at the first collective, and the GPU runs 6-8 %
+            # slower for a few hundred ms after it (measured on B200: only the first timed
+            # window after the first collective lost, gloo ranks none). Take those
+            # collectives here, seconds before any timed work.
+            for _ in range(3):
+                self.barrier()
+                self.max(0.0)
+            if backend == "nccl":
+                import torch
+                torch.cuda.synchronize()
 
     def barrier(self):
         if self.world > 1:
@@ -787,6 +797,10 @@ def run_ours(args):
     utter = utterance_run(rt, streams, ids, cfg, rank, world, barrier, max_over_ranks, clocks)
     utter_total = ranks.sum(utter.pop("patches_this_rank"))  # utterance lengths differ per rank
     utter["patches_all_ranks"] = int(utter_total)
+    # the region lasts as long as the longest utterance of any rank: a stream whose stop
+    # head never decides runs alone to the cap at the end
+    utter["longest_stream_all_ranks"] = int(max_over_ranks(float(max(utter["patches_per_stream"]))))
+    utter["stop_decided_all_ranks"] = int(ranks.sum(utter["stop_decided"]))
     utter["value"] = utter_total / utter["timed_region_s"]  # whole job: all ranks' patches / the slowest rank
 
     # ---- stream groups: the same workload with each group's estimator passes batched
