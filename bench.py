@@ -43,7 +43,7 @@ def parse():
     p.add_argument("--streams", type=int, default=16, help="independent batch-1 streams per GPU")
     p.add_argument("--groups", type=int, default=12,
                    help="stream groups per GPU for the group measurement (0 skips it)")
-    p.add_argument("--group-members", type=int, default=4, help="streams per group (1..4)")
+    p.add_argument("--group-members", type=int, default=4, help="streams per group (1..8)")
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--cpu-sample-patches", type=int, default=6)
     p.add_argument("--range", choices=["stream", "group", "sdpa"], default=None,

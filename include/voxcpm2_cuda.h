@@ -331,7 +331,7 @@ VXC_API int32_t vxc_profile_kernel(vxc_stream* s, int32_t kernel, int32_t iters,
 VXC_API int32_t vxc_profile_kernel_concurrent(vxc_stream** streams, int32_t n, int32_t kernel, int32_t iters,
                                               float* ms_total, double* bytes_per_launch);
 /* The stream's cudaStream_t, for callers timing it with CUDA events. */
-/* Groups: up to 4 streams whose patch steps run together as one CUDA graph. Each
+/* Groups: up to 8 streams whose patch steps run together as one CUDA graph. Each
  * member keeps its own prompt, KV caches, noise, stop state and latents (use the
  * stream calls above on vxc_group_stream's handle: vxc_prefill, vxc_upload_noise,
  * vxc_read_state, vxc_read_latents ...); the 9 estimator evaluations of all

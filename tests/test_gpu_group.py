@@ -13,7 +13,7 @@ import numpy as np
 import pytest
 
 import oracle
-from conftest import close_stats
+from conftest import close_stats, fsq_codes_from_hidden, fsq_forced_disagreements
 from voxcpm2_b200 import synthetic
 from voxcpm2_b200.config import BENCH, TINY
 
@@ -56,10 +56,12 @@ def check_members(orc, prompts, seeds, got, patches, timesteps=10, cfg_value=2.0
         assert err <= 2e-2 and cos >= 0.999, (m, err, cos)
 
 
-@pytest.mark.parametrize("members,bulk", [(1, "0"), (4, "0"), (4, "1")])
+@pytest.mark.parametrize("members,bulk", [(1, "0"), (4, "0"), (4, "1"), (6, "0"), (8, "0"), (8, "1")])
 def test_group_tiny_matches_oracle(rt, members, bulk, monkeypatch):
-    """TINY groups of 1 and 4 members; the decoder GEMVs in the register-streaming
-    batch form (the default) and in the bulk-copy form (VXC_GROUP_BULK_GEMV=1)."""
+    """TINY groups of 1 to 8 members; the decoder GEMVs in the register-streaming
+    batch form (the default) and in the bulk-copy form (VXC_GROUP_BULK_GEMV=1).
+    Groups of 5 to 8 members run the wide linears on a 144- or 176-row block (256
+    TMEM columns, N = 144 / 176 MMAs) and the 8-slot member batches."""
     monkeypatch.setenv("VXC_GROUP_BULK_GEMV", bulk)
     blobs = synthetic.model_blobs(TINY, 0)
     dev = rt.Device(TINY, 0, blobs)
@@ -69,6 +71,52 @@ def test_group_tiny_matches_oracle(rt, members, bulk, monkeypatch):
     got, kernels = run_group(rt, TINY, dev, prompts, seeds, patches=8, timesteps=6)
     check_members(orc, prompts, seeds, got, 8, timesteps=6)
     assert kernels > 0
+    dev.close()
+
+
+def test_group_bench_eight_members_match_oracle(rt):
+    """The benchmark model, a group of 8 members (176 estimator rows per pass), 3
+    patches, every member against its own oracle run.
+
+    FSQ rounds tanh(z) * 9 to integers, and a value within float rounding of a
+    half-integer can round one way on the GPU and the other on the CPU; the next
+    patches then belong to different utterances. So each member is held to the
+    oracle following the GPU's FSQ codes (recovered from the member's LM states),
+    and every code the oracle would have rounded the other way must be a one-step
+    change within 1e-3 of the rounding boundary."""
+    cfg = BENCH
+    blobs = synthetic.model_blobs(cfg, 0)
+    dev = rt.Device(cfg, 0, blobs)
+    orc = oracle.Oracle(cfg, blobs)
+    patches = 3
+    prompts = [synthetic.token_ids(cfg, 16 + 6 * m, seed=130 + m) for m in range(8)]
+    seeds = [170 + m for m in range(8)]
+    g = rt.Group(dev, 8, kv_capacity=256)
+    for st, ids, seed in zip(g.streams, prompts, seeds):
+        st.prefill(ids)
+        st.upload_noise(oracle.noise_table(seed, patches, cfg.latent))
+    lm = [[] for _ in range(8)]
+    for _ in range(patches):
+        for m, st in enumerate(g.streams):
+            lm[m].append(st.hidden()[0])  # the LM state entering this patch
+        g.patch_step_async(10 * patches, 2.0, 10)
+        g.synchronize()
+    for m, (st, ids, seed) in enumerate(zip(g.streams, prompts, seeds)):
+        s = st.state()
+        assert s.patches == patches and s.kv_len[0] == s.kv_len[1] == len(ids) + 1 + patches
+        got = st.latents(0, patches)
+        codes, resid = fsq_codes_from_hidden(cfg, blobs, lm[m][1:patches])
+        assert resid < 1e-2, (m, resid)
+        want = orc.generate(ids, min_patches=10 * patches, timesteps=10, cfg_value=2.0,
+                            max_patches_override=patches, seed=seed, fsq_codes=codes)
+        dis = fsq_forced_disagreements(want["fsq_pre"], codes)
+        for p, j, own, c, d in dis:
+            assert abs(own - c) == 1 and d < 1e-3, (m, p, j, own, c, d)
+        stats = [close_stats(got[i], want["latents"][i]) for i in range(patches)]
+        err, cos = max(x[0] for x in stats), min(x[1] for x in stats)
+        print(f"member {m}: {len(dis)} FSQ codes rounded the other way, worst max-abs {err:.3e}, cosine {cos:.6f}")
+        assert err <= 2e-2 and cos >= 0.999, (m, err, cos)
+    g.close()
     dev.close()
 
 
@@ -110,7 +158,7 @@ def test_group_orders_with_member_calls(rt):
         assert np.array_equal(st.latents(0, 3), ref[m])
     g.close()
     with pytest.raises(rt.VxcError):
-        rt.Group(dev, 5, kv_capacity=64)
+        rt.Group(dev, 9, kv_capacity=64)
     dev.close()
 
 
@@ -130,22 +178,24 @@ def stop_prone_blobs():
     return blobs
 
 
-def test_group_members_stop_independently(rt):
+@pytest.mark.parametrize("members", [4, 8])
+def test_group_members_stop_independently(rt, members):
     """Small min_patches: members reach the stop rule at their own patches (their
     decoder steps inside the batched kernels skip once their own flag is set).
     Each member's stop patch and latents up to it match the oracle's generate()
-    (with these weights the oracle stops the members after 5, never, 6 and 8 patches)."""
+    (with these weights the oracle stops the first four members after 5, never, 6
+    and 8 patches)."""
     blobs = stop_prone_blobs()
     dev = rt.Device(TINY, 0, blobs)
     orc = oracle.Oracle(TINY, blobs)
     cap_patches = 24
-    prompts = [synthetic.token_ids(TINY, 5 + 2 * m, seed=60 + m) for m in range(4)]
-    seeds = [300 + m for m in range(4)]
-    g = rt.Group(dev, 4, kv_capacity=128)
+    prompts = [synthetic.token_ids(TINY, 5 + 2 * m, seed=60 + m) for m in range(members)]
+    seeds = [300 + m for m in range(members)]
+    g = rt.Group(dev, members, kv_capacity=128)
     for st, ids, seed in zip(g.streams, prompts, seeds):
         st.prefill(ids)
         st.upload_noise(oracle.noise_table(seed, cap_patches, TINY.latent))
-    first_stop = [None] * 4
+    first_stop = [None] * members
     for step in range(cap_patches):
         g.patch_step_async(2, 2.0, 6)
         g.synchronize()
@@ -194,16 +244,18 @@ def test_group_rejects_bad_use(rt):
     dev.close()
 
 
-def test_group_receive_buffer_forms_bit_identical(rt, monkeypatch):
+@pytest.mark.parametrize("members", [4, 8])
+def test_group_receive_buffer_forms_bit_identical(rt, monkeypatch, members):
     """The wide linears' split-K partials in the stage area (the default) or in a
-    dedicated buffer (VXC_GROUP_RECV_SHARED=0): same sums, identical latents."""
+    dedicated buffer (VXC_GROUP_RECV_SHARED=0, where it fits beside the ring):
+    same sums, identical latents."""
     blobs = synthetic.model_blobs(TINY, 0)
     dev = rt.Device(TINY, 0, blobs)
-    prompts = [synthetic.token_ids(TINY, 6 + m, seed=80 + m) for m in range(4)]
+    prompts = [synthetic.token_ids(TINY, 6 + m, seed=80 + m) for m in range(members)]
     got = []
     for env in ("1", "0"):
         monkeypatch.setenv("VXC_GROUP_RECV_SHARED", env)
-        lat, _ = run_group(rt, TINY, dev, prompts, [90, 91, 92, 93], patches=4, timesteps=6)
+        lat, _ = run_group(rt, TINY, dev, prompts, [90 + m for m in range(members)], patches=4, timesteps=6)
         got.append(lat)
     for a, b in zip(*got):
         assert np.array_equal(a, b)

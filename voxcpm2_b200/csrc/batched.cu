@@ -936,7 +936,7 @@ void launch_dit_embed(const DitEmbedArgs& a, cudaStream_t s, bool pdl) {
     cudaLaunchAttribute attr[1];
     const size_t smem = static_cast<size_t>(kEmbedFeatures * (2 * a.D + 1) + 4 * a.D * a.P) * sizeof(float);
     if (smem > 200 * 1024) throw std::invalid_argument("dit_embed: patch too large");
-    if (a.members < 0 || a.members > 4) throw std::invalid_argument("dit_embed: 0 to 4 members");
+    if (a.members < 0 || a.members > kGroupMembers) throw std::invalid_argument("dit_embed: 0 to 8 members");
     cudaLaunchConfig_t cfg = make_cfg(dim3((a.Hd + kEmbedFeatures - 1) / kEmbedFeatures, a.members > 0 ? a.members : 1),
                                       dim3(kEmbedThreads), smem,
                                       s, pdl, attr);
@@ -962,7 +962,7 @@ void launch_dit_out(const DitOutArgs& a, cudaStream_t s, bool pdl) {
     const size_t smem = static_cast<size_t>(2 * a.P + kOutFeatures) * a.Hd * sizeof(float);
     if (smem > 200 * 1024) throw std::invalid_argument("dit_out: hidden too large");
     cudaLaunchAttribute attr[1];
-    if (a.members < 0 || a.members > 4) throw std::invalid_argument("dit_out: 0 to 4 members");
+    if (a.members < 0 || a.members > kGroupMembers) throw std::invalid_argument("dit_out: 0 to 8 members");
     cudaLaunchConfig_t cfg = make_cfg(dim3((a.D + kOutFeatures - 1) / kOutFeatures, a.members > 0 ? a.members : 1),
                                       dim3(kOutThreads), smem, s, pdl,
                                       attr);

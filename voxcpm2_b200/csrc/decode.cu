@@ -202,9 +202,9 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
 // each warp's weight rows are loaded once into registers, every member's input is
 // staged (and RMS-normalised) in shared memory, and the warp forms one dot product
 // per member; lane m stores member m. IN_PLAIN inputs only.
-template <int MODE, int MAXCH, int RPW>
+template <int MODE, int MAXCH, int RPW, int NB>
 __global__ void __launch_bounds__(kGemvThreads) gemv_batch_kernel(const GemvArgs a, const GemvBatch b) {
-    constexpr int NB = kGemvBatch;
+    static_assert(NB <= kGemvBatch && NB <= kWarp, "lane m stores member m");
     extern __shared__ float xs[];  // [nb][K]
     __shared__ float red[NB][kGemvWarps];
     pdl_launch_dependents();
@@ -589,19 +589,26 @@ void dispatch_gemv_bulk(const GemvArgs& a, const GemvBatch& b, cudaStream_t s, b
     check_launch(cudaLaunchKernelEx(&cfg, gemv_bulk_kernel<MODE>, a, b, upb));
 }
 
-template <int MODE, int RPW>
-void dispatch_gemv_batch(const GemvArgs& a, const GemvBatch& b, cudaStream_t s, bool pdl) {
+// NB: the member slots a launch unrolls (4 for groups of up to 4, else 8)
+template <int MODE, int RPW, int NB>
+void dispatch_gemv_batch_nb(const GemvArgs& a, const GemvBatch& b, cudaStream_t s, bool pdl) {
     const int nch = (a.K + 255) / 256;
     const int blocks = (a.rows + kGemvWarps - 1) / kGemvWarps;
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = make_cfg(dim3(blocks), dim3(kGemvThreads),
                                       static_cast<size_t>(b.n) * ((a.K + 7) / 8) * 8 * sizeof(float), s, pdl, attr);
-    if (nch <= 1) check_launch(cudaLaunchKernelEx(&cfg, gemv_batch_kernel<MODE, 1, RPW>, a, b));
-    else if (nch <= 2) check_launch(cudaLaunchKernelEx(&cfg, gemv_batch_kernel<MODE, 2, RPW>, a, b));
-    else if (nch <= 4) check_launch(cudaLaunchKernelEx(&cfg, gemv_batch_kernel<MODE, 4, RPW>, a, b));
-    else if (nch <= 8) check_launch(cudaLaunchKernelEx(&cfg, gemv_batch_kernel<MODE, 8, RPW>, a, b));
-    else if (RPW == 1 && nch <= 16) check_launch(cudaLaunchKernelEx(&cfg, gemv_batch_kernel<MODE, 16, 1>, a, b));
+    if (nch <= 1) check_launch(cudaLaunchKernelEx(&cfg, gemv_batch_kernel<MODE, 1, RPW, NB>, a, b));
+    else if (nch <= 2) check_launch(cudaLaunchKernelEx(&cfg, gemv_batch_kernel<MODE, 2, RPW, NB>, a, b));
+    else if (nch <= 4) check_launch(cudaLaunchKernelEx(&cfg, gemv_batch_kernel<MODE, 4, RPW, NB>, a, b));
+    else if (nch <= 8) check_launch(cudaLaunchKernelEx(&cfg, gemv_batch_kernel<MODE, 8, RPW, NB>, a, b));
+    else if (RPW == 1 && nch <= 16) check_launch(cudaLaunchKernelEx(&cfg, gemv_batch_kernel<MODE, 16, 1, NB>, a, b));
     else throw std::invalid_argument("gemv_batch: input dimension too large");
+}
+
+template <int MODE, int RPW>
+void dispatch_gemv_batch(const GemvArgs& a, const GemvBatch& b, cudaStream_t s, bool pdl) {
+    if (b.n <= 4) dispatch_gemv_batch_nb<MODE, RPW, 4>(a, b, s, pdl);
+    else dispatch_gemv_batch_nb<MODE, RPW, kGemvBatch>(a, b, s, pdl);
 }
 
 // ------------------------------------------------------------ attention ---
@@ -998,7 +1005,7 @@ void launch_attn_decode_cluster_batch(const AttnArgs& a, const AttnBatch& b, cud
     if (a.kv_heads <= 0 || a.q_heads % a.kv_heads != 0) throw std::invalid_argument("attention: bad head grouping");
     const int G = a.q_heads / a.kv_heads;
     if (G < 1 || G > kMaxGroup) throw std::invalid_argument("attention: more than 16 query heads per KV head");
-    if (b.n < 0 || b.n > 4) throw std::invalid_argument("attention: 1 to 4 members");
+    if (b.n < 0 || b.n > kGroupMembers) throw std::invalid_argument("attention: 1 to 8 members");
     for (const void* p : {a.k0, a.v0, a.k1, a.v1})
         if (reinterpret_cast<uintptr_t>(p) % 16 != 0)
             throw std::invalid_argument("attention: key/value rows must start on 16-byte boundaries");
@@ -1045,17 +1052,22 @@ void launch_attn_decode(const AttnArgs& a, bool fp16_kv, cudaStream_t s, bool pd
 
 void init_batched_attributes();
 
-template <int MODE, int RPW>
-void set_gemv_batch_attributes() {
+template <int MODE, int RPW, int NB>
+void set_gemv_batch_attributes_nb() {
     constexpr int kSmem = 160 * 1024;  // up to kGemvBatch inputs of K <= 4096 (+ slack)
-    for (const void* f : {reinterpret_cast<const void*>(gemv_batch_kernel<MODE, 1, RPW>),
-                          reinterpret_cast<const void*>(gemv_batch_kernel<MODE, 2, RPW>),
-                          reinterpret_cast<const void*>(gemv_batch_kernel<MODE, 4, RPW>),
-                          reinterpret_cast<const void*>(gemv_batch_kernel<MODE, 8, RPW>)})
+    for (const void* f : {reinterpret_cast<const void*>(gemv_batch_kernel<MODE, 1, RPW, NB>),
+                          reinterpret_cast<const void*>(gemv_batch_kernel<MODE, 2, RPW, NB>),
+                          reinterpret_cast<const void*>(gemv_batch_kernel<MODE, 4, RPW, NB>),
+                          reinterpret_cast<const void*>(gemv_batch_kernel<MODE, 8, RPW, NB>)})
         check_launch(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
     if constexpr (RPW == 1)
-        check_launch(cudaFuncSetAttribute(gemv_batch_kernel<MODE, 16, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          kSmem));
+        check_launch(cudaFuncSetAttribute(gemv_batch_kernel<MODE, 16, 1, NB>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
+}
+template <int MODE, int RPW>
+void set_gemv_batch_attributes() {
+    set_gemv_batch_attributes_nb<MODE, RPW, 4>();
+    set_gemv_batch_attributes_nb<MODE, RPW, kGemvBatch>();
 }
 
 void init_kernel_attributes() {

@@ -67,11 +67,12 @@ void launch_gemv(const GemvArgs& a, cudaStream_t s, bool pdl);
 // into shared memory by the bulk-copy engine before the dependency wait (the
 // decoder-step form); IN_PLAIN input, K <= 4096.
 void launch_gemv_bulk(const GemvArgs& a, cudaStream_t s, bool pdl);
+constexpr int kGroupMembers = 8;  // most streams in a group (the member-indexed argument arrays)
 // Up to kGemvBatch members (streams of a group) through the same weights: one read
 // of each weight row, one dot product per member. Member m replaces a's x, y,
 // resid, k_cache, v_cache and ctl; each member skips (and appends no KV row) when
 // a.skip_if_stopped and its own ctl->stopped are set.
-constexpr int kGemvBatch = 4;
+constexpr int kGemvBatch = kGroupMembers;
 struct GemvBatch {
     int n = 0;
     const float* x[kGemvBatch] = {};
@@ -113,15 +114,15 @@ void launch_attn_decode(const AttnArgs& a, bool fp16_kv, cudaStream_t s, bool pd
 // The same (fp32 KV) with the split-K combine inside one 8-CTA cluster per KV head
 // (distributed shared memory; no scratch, no atomics). Ignores splits/partial/counters.
 void launch_attn_decode_cluster(const AttnArgs& a, cudaStream_t s, bool pdl);
-// The same for up to 4 members (grid z = member): member m replaces a's q, k0, v0,
-// out and ctl (its own KV length and stop flag).
+// The same for up to kGroupMembers members (grid z = member): member m replaces a's
+// q, k0, v0, out and ctl (its own KV length and stop flag).
 struct AttnBatch {
     int n = 0;
-    const float* q[4] = {};
-    const void* k0[4] = {};
-    const void* v0[4] = {};
-    float* out[4] = {};
-    StreamCtl* ctl[4] = {};
+    const float* q[kGroupMembers] = {};
+    const void* k0[kGroupMembers] = {};
+    const void* v0[kGroupMembers] = {};
+    float* out[kGroupMembers] = {};
+    StreamCtl* ctl[kGroupMembers] = {};
 };
 void launch_attn_decode_cluster_batch(const AttnArgs& a, const AttnBatch& b, cudaStream_t s, bool pdl);
 // The layer-contract op (sdpa_op.cu): one query row over at most 512 fp32 keys given as
@@ -218,10 +219,10 @@ struct DitEmbedArgs {
     // group members (grid y = member, 0 = none): member m replaces x, cond, mu and ctl,
     // and writes hidden + m * member_stride
     int members;
-    const float* mx[4];
-    const float* mcond[4];
-    const float* mmu[4];
-    StreamCtl* mctl[4];
+    const float* mx[kGroupMembers];
+    const float* mcond[kGroupMembers];
+    const float* mmu[kGroupMembers];
+    StreamCtl* mctl[kGroupMembers];
     size_t member_stride;
 };
 void launch_dit_embed(const DitEmbedArgs& a, cudaStream_t s, bool pdl);
@@ -249,10 +250,10 @@ struct DitOutArgs {
     // group members (grid y = member, 0 = none): member m reads hidden + m * member_stride
     // and replaces x, ctl, est_buf and counter
     int members = 0;
-    float* mx[4] = {};
-    StreamCtl* mctl[4] = {};
-    float* mest[4] = {};
-    int* mcounter[4] = {};
+    float* mx[kGroupMembers] = {};
+    StreamCtl* mctl[kGroupMembers] = {};
+    float* mest[kGroupMembers] = {};
+    int* mcounter[kGroupMembers] = {};
     size_t member_stride = 0;
 };
 void launch_dit_out(const DitOutArgs& a, cudaStream_t s, bool pdl);
@@ -351,24 +352,27 @@ void launch_tc_rows(const CUtensorMap& map_a, const CUtensorMap& map_b, const Tc
 void init_tc_rows_attributes();
 
 // Wide-token tcgen05 linear (the DiT of a group of streams): Y[m][r] for
-// m < M <= kWideTokens rows, K split across a cluster of 'splits' CTAs
-// (tc_wide.cu). The token operand is split fp16 [2 * kWideTokens][K] (map_b, box
-// rows 2 * kWideTokens): fp16(x) in rows 0.., the residuals in rows kWideTokens...
-constexpr int kWideTokens = 96;
+// m < M <= lo rows, K split across a cluster of 'splits' CTAs (tc_wide.cu). The
+// token operand is split fp16 [2 lo][K] (map_b, box rows lo): fp16(x) in rows
+// 0..lo-1, the residuals in rows lo..2 lo-1; lo is a multiple of 16, at most
+// kWideTokens (8 members x 22 rows).
+constexpr int kWideTokens = 176;
 struct TcWideArgs {
     int K = 0, M = 0, rows = 0;
+    int lo = 0;                // the token operand's row block (a multiple of 16, M <= lo <= kWideTokens)
     int splits = 1;
-    int gateup = 0;            // out = SiLU(gate) * up, as split fp16 into yb [2 * kWideTokens][ldyb]
+    int gateup = 0;            // out = SiLU(gate) * up, as split fp16 into yb [2 lo][ldyb]
     int resid = 0;             // y += rscale * out (else y = out)
     float rscale = 1.f;
     float* y = nullptr;        // fp32 [M][ldy]
     int ldy = 0;
     __half* yb = nullptr;
     int ldyb = 0;
-    int stages = 2;            // shared-memory ring depth (1..4)
+    int stages = 2;            // shared-memory ring depth (1..4; lowered where the block does not fit)
     StreamCtl* ctl = nullptr;  // receives error 3 if a bounded wait gave up
     // K split: receive the cluster's partials in the (by then idle) stage area after one
-    // more cluster barrier, instead of a dedicated 48 KB buffer (more CTAs per SM)
+    // more cluster barrier, instead of a dedicated buffer (more CTAs per SM; always
+    // so where the dedicated buffer would not fit beside the ring)
     int recv_shared = 0;
 };
 void launch_tc_wide(const CUtensorMap& map_a, const CUtensorMap& map_b, const TcWideArgs& a, cudaStream_t s,

@@ -1336,7 +1336,7 @@ void vxc_internal_set_error(const char* msg) { g_last_error = msg; }
 
 // ==================================================================== C ABI ==
 // ------------------------------------------------------------- groups ----
-// A group of up to 4 streams whose patch steps run as one CUDA graph: each
+// A group of up to 8 streams whose patch steps run as one CUDA graph: each
 // member's decoder steps and small graphs on its own stream (forked branches),
 // and the 9 estimator evaluations of all members batched into one pass over
 // 22 rows per member, so every DiT weight byte is read once per group patch.
@@ -1348,7 +1348,8 @@ struct vxc_group {
     std::mutex call_mutex;
     float* gdh = nullptr;   // [22 n][Hd] residual stream of all members' DiT rows
     float* gqkv = nullptr;  // [22 n][(Hq + 2 Hkv) d]
-    __half *xw_n = nullptr, *xw_a = nullptr, *xw_act = nullptr;  // [2 kWideTokens][K] split operands
+    int lo = 0;  // the split operands' row block: 22 rows per member rounded up to 16
+    __half *xw_n = nullptr, *xw_a = nullptr, *xw_act = nullptr;  // [2 lo][K] split operands
     CUtensorMap map_xw_n{}, map_xw_a{}, map_xw_act{};
     int tc_target = 32;              // CTAs aimed at per wide linear (VXC_GROUP_TC_TARGET; 32 suits
                                      // several groups at once, 148 a lone group's latency)
@@ -1494,6 +1495,7 @@ void enqueue_group_layers(vxc_group* g) {
         a.splits = pow2_floor(choose_splits(tiles, K, g->tc_target));
         a.stages = g->tc_stages;
         a.M = M;
+        a.lo = g->lo;
         a.K = K;
         a.ctl = g->gctl;
         a.recv_shared = g->recv_shared ? 1 : 0;
@@ -1502,14 +1504,14 @@ void enqueue_group_layers(vxc_group* g) {
     for (size_t l = 0; l < dev->dit.size(); ++l) {
         const LayerW& L = dev->dit[l];
         const std::array<CUtensorMap, 4>& maps = dev->dit_maps[l];
-        launch_rmsnorm_rows_split(g->gdh, Hd, L.in_norm, d.rms_eps, Hd, M, g->xw_n, nullptr, cs, pdl, kWideTokens);
+        launch_rmsnorm_rows_split(g->gdh, Hd, L.in_norm, d.rms_eps, Hd, M, g->xw_n, nullptr, cs, pdl, g->lo);
         TcWideArgs qa = plan(W / 128, Hd);
         qa.rows = W;
         qa.y = g->gqkv;
         qa.ldy = W;
         launch_tc_wide(maps[0], g->map_xw_n, qa, cs, pdl);
         launch_dit_attention_split(g->gqkv, 2 * n, seq, hq, hkv, hd, dev->dit_rope_cos, dev->dit_rope_sin, scale,
-                                   g->xw_a, nullptr, cs, pdl, kWideTokens);
+                                   g->xw_a, nullptr, cs, pdl, g->lo);
         TcWideArgs oa = plan(Hd / 128, hq * hd);
         oa.rows = Hd;
         oa.resid = 1;
@@ -1517,8 +1519,7 @@ void enqueue_group_layers(vxc_group* g) {
         oa.y = g->gdh;
         oa.ldy = Hd;
         launch_tc_wide(maps[1], g->map_xw_a, oa, cs, pdl);
-        launch_rmsnorm_rows_split(g->gdh, Hd, L.post_norm, d.rms_eps, Hd, M, g->xw_n, nullptr, cs, pdl,
-                                  kWideTokens);
+        launch_rmsnorm_rows_split(g->gdh, Hd, L.post_norm, d.rms_eps, Hd, M, g->xw_n, nullptr, cs, pdl, g->lo);
         TcWideArgs ga = plan(F / 64, Hd);
         ga.rows = F;
         ga.gateup = 1;
@@ -2855,7 +2856,7 @@ VXC_API int32_t vxc_group_create(vxc_device* dev, int32_t n_streams, int32_t kv_
     return guard([&] {
         require(dev != nullptr && out != nullptr, "device and out must not be null");
         *out = nullptr;
-        require(n_streams >= 1 && n_streams <= kGroupMax, "a group holds 1 to 4 streams");
+        require(n_streams >= 1 && n_streams <= kGroupMax, "a group holds 1 to 8 streams");
         const vxc_model_desc& d = dev->desc;
         require(dit_tokens_per_seq(d.patch_size) == 11 && d.dit_hidden / d.dit_q_heads == 64,
                 "groups need the 2 x 11-token DiT with 64-wide heads");
@@ -2884,15 +2885,18 @@ VXC_API int32_t vxc_group_create(vxc_device* dev, int32_t n_streams, int32_t kv_
             const size_t M = 22 * static_cast<size_t>(n_streams);
             grp->gdh = dev_alloc<float>(M * Hd);
             grp->gqkv = dev_alloc<float>(M * W);
-            grp->xw_n = dev_alloc<__half>(2 * kWideTokens * Hd);
-            grp->xw_a = dev_alloc<__half>(2 * kWideTokens * Q);
-            grp->xw_act = dev_alloc<__half>(2 * kWideTokens * F);
-            ck(cudaMemset(grp->xw_n, 0, 2 * kWideTokens * Hd * sizeof(__half)), "cudaMemset");
-            ck(cudaMemset(grp->xw_a, 0, 2 * kWideTokens * Q * sizeof(__half)), "cudaMemset");
-            ck(cudaMemset(grp->xw_act, 0, 2 * kWideTokens * F * sizeof(__half)), "cudaMemset");
-            grp->map_xw_n = make_tensor_map_f16(grp->xw_n, 2 * kWideTokens, static_cast<int>(Hd), 2 * kWideTokens);
-            grp->map_xw_a = make_tensor_map_f16(grp->xw_a, 2 * kWideTokens, static_cast<int>(Q), 2 * kWideTokens);
-            grp->map_xw_act = make_tensor_map_f16(grp->xw_act, 2 * kWideTokens, static_cast<int>(F), 2 * kWideTokens);
+            const int lo = (static_cast<int>(M) + 15) / 16 * 16;
+            const size_t rows = 2 * static_cast<size_t>(lo);
+            grp->lo = lo;
+            grp->xw_n = dev_alloc<__half>(rows * Hd);
+            grp->xw_a = dev_alloc<__half>(rows * Q);
+            grp->xw_act = dev_alloc<__half>(rows * F);
+            ck(cudaMemset(grp->xw_n, 0, rows * Hd * sizeof(__half)), "cudaMemset");
+            ck(cudaMemset(grp->xw_a, 0, rows * Q * sizeof(__half)), "cudaMemset");
+            ck(cudaMemset(grp->xw_act, 0, rows * F * sizeof(__half)), "cudaMemset");
+            grp->map_xw_n = make_tensor_map_f16(grp->xw_n, static_cast<int>(rows), static_cast<int>(Hd), lo);
+            grp->map_xw_a = make_tensor_map_f16(grp->xw_a, static_cast<int>(rows), static_cast<int>(Q), lo);
+            grp->map_xw_act = make_tensor_map_f16(grp->xw_act, static_cast<int>(rows), static_cast<int>(F), lo);
             grp->gctl = dev_alloc<StreamCtl>(1);
             ck(cudaMemset(grp->gctl, 0, sizeof(StreamCtl)), "cudaMemset");
             ck(cudaMallocHost(&grp->gctl_host, sizeof(StreamCtl)), "cudaMallocHost");

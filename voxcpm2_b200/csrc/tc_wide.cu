@@ -1,24 +1,28 @@
-// tcgen05 linear over a wide token block: up to kWideTokens = 96 rows, for the
-// DiT estimator of a group of streams evaluated together (DitEstimator.decoder,
-// tools/export_components.py:625-659, over 22 rows per stream).
+// tcgen05 linear over a wide token block: up to kWideTokens = 176 rows, for the
+// DiT estimator of a group of up to 8 streams evaluated together
+// (DitEstimator.decoder, tools/export_components.py:625-659, over 22 rows per
+// stream).
 //
 // The weight tile is the MMA A operand (128 output features, K-major, 128-byte
-// swizzle, TMA); the token rows are the B operand, fp16(x) in rows 0..95 and
-// fp16(x - fp16(x)) in rows 96..191 of each K chunk. Both halves accumulate into
-// the same 96 fp32 TMEM columns (two N = 96 MMAs per K step), so the
-// accumulator already holds W (x_hi + x_lo). K is split across a thread-block
-// cluster of 1, 2, 4 or 8 CTAs: after the MMAs each CTA pushes its partials,
-// token-major, to the CTA that owns those output features (a warp's store is
-// one contiguous run in the owner's shared memory), one cluster barrier, then
-// the owner sums the partials in rank order and writes the epilogue: plain,
-// residual (y += rscale * v), or SiLU(gate) * up into the next linear's split
-// operand (residual half at row offset 96).
+// swizzle, TMA); the token rows are the B operand. The operand buffer holds a
+// row block of 'lo' rows (a multiple of 16, at least M): fp16(x) in rows
+// 0..lo-1 and fp16(x - fp16(x)) in rows lo..2 lo-1. A K chunk brings both halves
+// with two TMA copies of one lo-row box; both accumulate into the same lo fp32
+// TMEM columns (two N = lo MMAs per K step), so the accumulator already holds
+// W (x_hi + x_lo). K is split across a thread-block cluster of 1, 2, 4 or 8 CTAs:
+// after the MMAs each CTA pushes its partials, token-major, to the CTA that owns
+// those output features (a warp's store is one contiguous run in the owner's
+// shared memory), one cluster barrier, then the owner sums the partials in rank
+// order and writes the epilogue: plain, residual (y += rscale * v), or
+// SiLU(gate) * up into the next linear's split operand (residual half at row
+// offset lo). The accumulator is read from TMEM 32 token columns at a time.
 //
-// Shared memory never drops below kFloor, so an SM holds at most two of these
-// CTAs (2 x 128 TMEM columns) and no 24-token linear beside them: the SM's 512
-// TMEM columns are never oversubscribed, and a cluster CTA never waits for TMEM.
-// Every wait is bounded; on timeout the kernel records error 3, still passes the
-// cluster barrier, drains its loads and frees its TMEM.
+// TMEM: 128 columns for lo <= 128, else 256. Shared memory never drops below
+// tmem_smem_floor of that count (and kFloor), so the SM's 512 TMEM columns are
+// never oversubscribed by co-resident CTAs and a cluster CTA never waits for
+// TMEM. Every mbarrier wait is time-bounded; on timeout the kernel records
+// error 3, still passes the cluster barriers, drains its loads and frees its TMEM
+// (this failure path has not been exercised on a GPU).
 #include <cuda.h>
 
 #include <algorithm>
@@ -34,14 +38,11 @@ namespace {
 using namespace tc;
 
 constexpr int kThreads = 128;
-constexpr int kN = kWideTokens;                       // MMA N: hi and lo rows share the columns
-constexpr int kLoBytes = kWideTokens * kKChunk * 2;   // offset of the lo rows in a B tile (12 KiB)
-constexpr int kBTile = 2 * kLoBytes;                  // 24 KiB
-constexpr int kStage = kABytes + kBTile;              // 40 KiB (1 KiB aligned)
 constexpr int kMaxRing = 4;
-constexpr int kTmem = 128;
-constexpr size_t kRecvBytes = static_cast<size_t>(kTileRows) * kWideTokens * 4;  // 48 KiB
 constexpr size_t kFloor = 92 * 1024;
+// dynamic shared memory a launch may ask for: the 227 KiB opt-in limit covers the
+// static barriers too, so 1 KiB is left for them
+constexpr size_t kSmemMax = 226 * 1024;
 
 void check_launch(cudaError_t e) {
     if (e != cudaSuccess) throw std::runtime_error(std::string("tc_wide: ") + cudaGetErrorString(e));
@@ -51,10 +52,14 @@ __device__ __forceinline__ void cluster_barrier() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// Shared-memory layout of a launch, the same on the host and in every CTA.
+__host__ __device__ constexpr int stage_bytes(int lo) { return kABytes + lo * kKChunk * 2 * 2; }
+__host__ __device__ constexpr size_t recv_bytes(int lo) { return static_cast<size_t>(kTileRows) * lo * 4; }
+__host__ __device__ constexpr int tmem_cols(int lo) { return lo <= 128 ? 128 : 256; }
 // The receive buffer lives in the (then idle) stage area when the CTA has no
 // K split and the stage area is large enough for it.
-__host__ __device__ constexpr bool recv_in_stages(int splits, int stages) {
-    return splits == 1 && static_cast<size_t>(stages) * kStage >= kRecvBytes;
+__host__ __device__ constexpr bool recv_in_stages(int splits, int stages, int lo) {
+    return splits == 1 && static_cast<size_t>(stages) * stage_bytes(lo) >= recv_bytes(lo);
 }
 
 // S = K split (cluster size): a template parameter so the partial sums unroll.
@@ -68,7 +73,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __shared__ int failed_s;
 
     const int tid = threadIdx.x, warp = tid >> 5;
-    const int split = blockIdx.x, tile = blockIdx.y, M = a.M;
+    const int split = blockIdx.x, tile = blockIdx.y, M = a.M, lo = a.lo;
+    const int kstage = stage_bytes(lo), tcols = tmem_cols(lo);
+    const uint32_t lo_bytes = static_cast<uint32_t>(lo) * kKChunk * 2;  // offset of the lo rows in a B tile
     // 1 KiB aligned, derived from smem_raw by pointer arithmetic so that the
     // compiler keeps shared-memory addressing for everything carved from it
     uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
@@ -96,8 +103,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < kMaxRing; ++i) issued[i] = 0;
         // weights first: they depend on no earlier kernel
         for (int i = 0; i < pre; ++i) {
-            uint8_t* st = smem + i * kStage;
-            mbar_expect_tx(&full_bar[i], kStage);
+            uint8_t* st = smem + i * kstage;
+            mbar_expect_tx(&full_bar[i], kstage);
             tma_load_2d(st, &map_a, (c0 + i) * kKChunk, r0, &full_bar[i]);
             tma_load_2d(st + kABytes / 2, &map_a, (c0 + i) * kKChunk, r1, &full_bar[i]);
             issued[i] = 1;
@@ -105,7 +112,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                         smem_addr(&tmem_base_s)), "r"(kTmem)
+                         smem_addr(&tmem_base_s)), "r"(tcols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -117,24 +124,28 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (tid == 0) {
         pdl_wait();
-        for (int i = 0; i < pre; ++i)
-            tma_load_2d(smem + i * kStage + kABytes, &map_b, (c0 + i) * kKChunk, 0, &full_bar[i]);
+        for (int i = 0; i < pre; ++i) {
+            uint8_t* sb = smem + i * kstage + kABytes;
+            tma_load_2d(sb, &map_b, (c0 + i) * kKChunk, 0, &full_bar[i]);
+            tma_load_2d(sb + lo_bytes, &map_b, (c0 + i) * kKChunk, lo, &full_bar[i]);
+        }
         for (int i = pre; i < cs; ++i) {
             const int s = i % stages;
             if (!mbar_wait(&empty_bar[s], ((i / stages) - 1) & 1)) {
                 failed_s = 1;
                 break;
             }
-            uint8_t* st = smem + s * kStage;
-            mbar_expect_tx(&full_bar[s], kStage);
+            uint8_t* st = smem + s * kstage;
+            mbar_expect_tx(&full_bar[s], kstage);
             tma_load_2d(st, &map_a, (c0 + i) * kKChunk, r0, &full_bar[s]);
             tma_load_2d(st + kABytes / 2, &map_a, (c0 + i) * kKChunk, r1, &full_bar[s]);
             tma_load_2d(st + kABytes, &map_b, (c0 + i) * kKChunk, 0, &full_bar[s]);
+            tma_load_2d(st + kABytes + lo_bytes, &map_b, (c0 + i) * kKChunk, lo, &full_bar[s]);
             issued[s] += 1;
         }
     } else if (tid == 32) {
         pdl_wait();
-        const uint32_t idesc = umma_idesc(kTileRows, kN);
+        const uint32_t idesc = umma_idesc(kTileRows, lo);
         for (int i = 0; i < cs; ++i) {
             const int s = i % stages;
             if (!mbar_wait(&full_bar[s], (i / stages) & 1)) {
@@ -142,11 +153,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t sa = smem_addr(smem + s * kStage), sb = sa + kABytes;
+            const uint32_t sa = smem_addr(smem + s * kstage), sb = sa + kABytes;
 #pragma unroll
             for (int kk = 0; kk < kKChunk / 16; ++kk) {
                 umma_f16(tmem, umma_desc(sa + kk * 32), umma_desc(sb + kk * 32), idesc, (i | kk) != 0);
-                umma_f16(tmem, umma_desc(sa + kk * 32), umma_desc(sb + kLoBytes + kk * 32), idesc, 1);
+                umma_f16(tmem, umma_desc(sa + kk * 32), umma_desc(sb + lo_bytes + kk * 32), idesc, 1);
             }
             umma_commit(&empty_bar[s]);
         }
@@ -158,72 +169,78 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool ok = mbar_wait(&done_bar, 0);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (!ok) failed_s = 1;
+    // tcgen05.ld is warp-collective: read the accumulator only if the whole warp saw it complete
+    const bool wok = __all_sync(0xffffffffu, ok);
     // output features of the tile: 128 (or 64 gate + 64 up); CTA p of the
     // cluster owns features [p nu, (p + 1) nu) of each half
     const int units = a.gateup ? 64 : kTileRows, halves = a.gateup ? 2 : 1;
     const int nu = units / S;
     // split launches may receive in the stage area too, once every CTA of the cluster is done with its own
-    const bool shared_recv = S > 1 && a.recv_shared && static_cast<size_t>(stage_area) * kStage >= kRecvBytes;
-    const bool local_recv = recv_in_stages(S, stages) || shared_recv;
+    const bool shared_recv = S > 1 && a.recv_shared && static_cast<size_t>(stage_area) * kstage >= recv_bytes(lo);
+    const bool local_recv = recv_in_stages(S, stages, lo) || shared_recv;
     if (tid == 0) {
         // no copy may still be landing in this CTA's shared memory (bounded when something failed)
         for (int i = 0; i < stages; ++i)
             if (issued[i] > 0 && !mbar_wait(&full_bar[i], (issued[i] - 1) & 1)) failed_s = 1;
     }
     __syncthreads();
-    float v[kWideTokens];  // this thread's accumulator row: output feature tid, token rows 0..M-1
-    {
-        const uint32_t lanes = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-        if (ok) {
-#pragma unroll
-            for (int c = 0; c < kWideTokens; c += 16)
-                if (c < M) tmem_ld16(lanes + c, v + c);
+    // this thread's accumulator row (output feature tid), token columns mb .. mb + 31
+    const uint32_t lanes = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    auto acc32 = [&](int mb, float* v) {
+        if (wok) {
+            tmem_ld16(lanes + mb, v);
+            if (mb + 16 < M) tmem_ld16(lanes + mb + 16, v + 16);
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
         } else {
 #pragma unroll
-            for (int m = 0; m < kWideTokens; ++m) v[m] = 0.f;
+            for (int i = 0; i < 32; ++i) v[i] = 0.f;
         }
-    }
+    };
     if (S == 1 && !a.gateup) {
-        // no split, one feature per thread: straight from registers, coalesced
-        // across the warp (consecutive features of one token row)
+        // no split, one feature per thread: straight from TMEM, coalesced across
+        // the warp (consecutive features of one token row)
         float* yc = a.y + tile * kTileRows + tid;
+        for (int mb = 0; mb < M; mb += 32) {
+            float v[32];
+            acc32(mb, v);
 #pragma unroll
-        for (int mb = 0; mb < kWideTokens; mb += 16) {
-            if (mb < M) {
+            for (int h = 0; h < 32; h += 16) {
                 float r[16];
 #pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    r[j] = (a.resid && mb + j < M) ? yc[static_cast<size_t>(mb + j) * a.ldy] : 0.f;
+                for (int j = 0; j < 16; ++j) {
+                    const int m = mb + h + j;
+                    r[j] = (a.resid && m < M) ? yc[static_cast<size_t>(m) * a.ldy] : 0.f;
+                }
 #pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    if (mb + j < M)
-                        yc[static_cast<size_t>(mb + j) * a.ldy] =
-                            a.resid ? r[j] + (a.rscale == 1.f ? v[mb + j] : v[mb + j] * a.rscale) : v[mb + j];
+                for (int j = 0; j < 16; ++j) {
+                    const int m = mb + h + j;
+                    if (m < M)
+                        yc[static_cast<size_t>(m) * a.ldy] =
+                            a.resid ? r[j] + (a.rscale == 1.f ? v[h + j] : v[h + j] * a.rscale) : v[h + j];
+                }
             }
         }
     } else {
         // partials, token-major per owner: recv[((p * halves + half) * M + m) * nu + lu]
-        float* recv = reinterpret_cast<float*>(local_recv ? smem : smem + static_cast<size_t>(stage_area) * kStage);
+        float* recv = reinterpret_cast<float*>(local_recv ? smem : smem + static_cast<size_t>(stage_area) * kstage);
         if (shared_recv) cluster_barrier();  // every CTA's loads have landed: the stage areas are free
         {
             const int u = a.gateup ? (tid & 63) : tid, half = a.gateup ? (tid >> 6) : 0;
             const int owner = u / nu, lu = u - owner * nu;
             float* dst = recv + static_cast<size_t>((split * halves + half) * M) * nu + lu;
-            if (owner == split) {
+            const uint32_t remote = owner == split ? 0u : peer_addr(dst, static_cast<uint32_t>(owner));
+            for (int mb = 0; mb < M; mb += 32) {
+                float v[32];
+                acc32(mb, v);
+                if (owner == split) {
 #pragma unroll
-                for (int m = 0; m < kWideTokens; ++m)
-                    if (m < M) dst[m * nu] = v[m];
-            } else {
-                uint32_t remote;
-                asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
-                             : "=r"(remote)
-                             : "r"(smem_addr(dst)), "r"(static_cast<uint32_t>(owner)));
+                    for (int j = 0; j < 32; ++j)
+                        if (mb + j < M) dst[static_cast<size_t>(mb + j) * nu] = v[j];
+                } else {
 #pragma unroll
-                for (int m = 0; m < kWideTokens; ++m)
-                    if (m < M)
-                        asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote + 4u * m * nu), "f"(v[m])
-                                     : "memory");
+                    for (int j = 0; j < 32; ++j)
+                        if (mb + j < M) st_peer(remote + 4u * static_cast<uint32_t>((mb + j) * nu), v[j]);
+                }
             }
         }
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -260,8 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const float o = silu(gs) * us;
                         const __half h = __float2half_rn(o);
                         a.yb[static_cast<size_t>(m) * a.ldyb + ocol] = h;
-                        a.yb[static_cast<size_t>(kWideTokens + m) * a.ldyb + ocol] =
-                            __float2half_rn(o - __half2float(h));
+                        a.yb[static_cast<size_t>(lo + m) * a.ldyb + ocol] = __float2half_rn(o - __half2float(h));
                     }
                 }
             }
@@ -294,34 +310,67 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     if (tid == 0 && failed_s && a.ctl) a.ctl->error = 3;
     if (warp == 1)
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmem) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tcols) : "memory");
 }
 
-size_t smem_bytes(int K, int splits, int stages_cap, bool recv_shared = false) {
-    const int nch = K / kKChunk;
-    const int cs = (nch + splits - 1) / splits;
-    const int stages = std::min(stages_cap, std::max(cs, 1));
-    size_t bytes = static_cast<size_t>(stages) * kStage + 1024;
-    const bool shared = splits > 1 && recv_shared && static_cast<size_t>(stages) * kStage >= kRecvBytes;
-    if (!recv_in_stages(splits, stages) && !shared) bytes += kRecvBytes;  // (unused by an unsplit plain/residual launch)
-    return std::max(bytes, kFloor);
+}  // namespace
+}  // namespace vxc
+
+namespace vxc {
+namespace {
+
+// The launch's ring depth, receive placement and dynamic shared memory: the
+// deepest ring (up to a.stages) whose layout fits; a split launch whose separate
+// receive buffer would not fit beside its ring receives in the stage area.
+struct WidePlan {
+    int stages = 1;
+    int recv_shared = 0;
+    size_t bytes = 0;
+};
+
+WidePlan plan_smem(const TcWideArgs& a) {
+    const int nch = a.K / kKChunk, S = a.splits, lo = a.lo;
+    const size_t kstage = static_cast<size_t>(stage_bytes(lo)), recv = recv_bytes(lo);
+    const bool needs_recv = S > 1 || a.gateup;  // an unsplit plain / residual launch writes from TMEM
+    for (int st = a.stages; st >= 1; --st) {
+        const size_t area = static_cast<size_t>(std::min(st, std::max((nch + S - 1) / S, 1))) * kstage;
+        int rs = a.recv_shared;
+        if (S > 1 && !rs && area + recv + 1024 > kSmemMax && area >= recv) rs = 1;
+        const bool in_stages = (S == 1 && area >= recv) || (S > 1 && rs && area >= recv);
+        const size_t bytes = area + 1024 + ((needs_recv && !in_stages) ? recv : 0);
+        if (bytes <= kSmemMax) {
+            WidePlan p;
+            p.stages = st;
+            p.recv_shared = rs;
+            p.bytes = std::max({bytes, kFloor, tmem_smem_floor(tmem_cols(lo))});
+            return p;
+        }
+    }
+    throw std::invalid_argument("tc_wide: the token block does not fit in shared memory");
 }
 
 }  // namespace
 
-void launch_tc_wide(const CUtensorMap& map_a, const CUtensorMap& map_b, const TcWideArgs& a, cudaStream_t s,
+void launch_tc_wide(const CUtensorMap& map_a, const CUtensorMap& map_b, const TcWideArgs& args, cudaStream_t s,
                     bool pdl) {
-    if (a.K % kKChunk != 0 || a.K <= 0) throw std::invalid_argument("tc_wide: K must be a multiple of 64");
-    if (a.M <= 0 || a.M > kWideTokens) throw std::invalid_argument("tc_wide: 1..96 token rows");
-    if ((a.splits != 1 && a.splits != 2 && a.splits != 4 && a.splits != 8) || a.splits > a.K / kKChunk)
+    if (args.K % kKChunk != 0 || args.K <= 0) throw std::invalid_argument("tc_wide: K must be a multiple of 64");
+    if (args.lo < 16 || args.lo > kWideTokens || args.lo % 16 != 0)
+        throw std::invalid_argument("tc_wide: the row block must be a multiple of 16 in [16, 176]");
+    if (args.M <= 0 || args.M > args.lo) throw std::invalid_argument("tc_wide: 1 to lo token rows");
+    if ((args.splits != 1 && args.splits != 2 && args.splits != 4 && args.splits != 8) ||
+        args.splits > args.K / kKChunk)
         throw std::invalid_argument("tc_wide: splits must be 1, 2, 4 or 8 and at most K / 64");
-    if (a.stages < 1 || a.stages > kMaxRing) throw std::invalid_argument("tc_wide: stages in [1, 4]");
-    if ((a.gateup ? a.rows % 64 : a.rows % kTileRows) != 0) throw std::invalid_argument("tc_wide: rows");
+    if (args.stages < 1 || args.stages > kMaxRing) throw std::invalid_argument("tc_wide: stages in [1, 4]");
+    if ((args.gateup ? args.rows % 64 : args.rows % kTileRows) != 0) throw std::invalid_argument("tc_wide: rows");
+    const WidePlan p = plan_smem(args);
+    TcWideArgs a = args;
+    a.stages = p.stages;
+    a.recv_shared = p.recv_shared;
     const int n_tiles = a.gateup ? a.rows / 64 : a.rows / kTileRows;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.splits, n_tiles);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = std::max(smem_bytes(a.K, a.splits, a.stages, a.recv_shared != 0), tmem_smem_floor(kTmem));
+    cfg.dynamicSmemBytes = p.bytes;
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -341,11 +390,9 @@ void launch_tc_wide(const CUtensorMap& map_a, const CUtensorMap& map_b, const Tc
 }
 
 void init_tc_wide_attributes() {
-    size_t most = kFloor;
-    for (int sp = 1; sp <= 8; ++sp) most = std::max(most, smem_bytes(64 * kMaxRing * sp, sp, kMaxRing));
     for (const void* f : {reinterpret_cast<const void*>(tc_wide_kernel<1>), reinterpret_cast<const void*>(tc_wide_kernel<2>),
                           reinterpret_cast<const void*>(tc_wide_kernel<4>), reinterpret_cast<const void*>(tc_wide_kernel<8>)})
-        check_launch(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(most)));
+        check_launch(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemMax)));
 }
 
 }  // namespace vxc

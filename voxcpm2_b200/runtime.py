@@ -427,7 +427,7 @@ def patch_run(streams, noise, min_patches: int, cfg_value: float = 2.0, timestep
 
 
 class Group:
-    """Up to 4 streams stepped together: one CUDA graph per group patch, with the
+    """Up to 8 streams stepped together: one CUDA graph per group patch, with the
     estimator evaluations of all members batched into one pass over the DiT
     weights. Members are ordinary streams (prefill, noise, state, latents)."""
 
