@@ -279,7 +279,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_rows_split_kernel(const 
         gw[i] = u < n4 && g ? __ldg(reinterpret_cast<const uint2*>(g) + u) : make_uint2(0x3c003c00u, 0x3c003c00u);
     }
     pdl_wait();
-    if (ctl && ctl->stopped) return;
+    const bool stop = ctl && ctl->stopped;  // read beside the row; nothing is written before the check
     const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(m) * ldx);
     float4 v[kNormBatch];
 #pragma unroll
@@ -292,6 +292,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_rows_split_kernel(const 
     for (int i = 0; i < kNormBatch; ++i) ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
     ss = warp_sum(ss);
     if ((tid & 31) == 0) red[tid >> 5] = ss;
+    if (stop) return;
     __syncthreads();
     float t = 0.f;
 #pragma unroll
@@ -314,18 +315,24 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_rows_split_kernel(const 
 // One CTA per (head, sequence): RoPE on q/k (apply_rotary_pos_emb, rotate_half),
 // scores, softmax and P.V for the sequence's rows (VoxCPM2SDPA without mask or
 // cache, voxcpm2_sdpa.cpp:187-252), written as the o projection's split operand.
-// The q/k/v rows and the RoPE tables arrive in one batch of loads.
+// Every load after the dependency wait (the stop flag and the head's q/k/v rows)
+// is issued in one batch; each thread rotates the (e, e + 32) column pairs it
+// loaded in registers before staging them. A warp owns a query row's scores and
+// softmax (lane j scores key j), and the P.V outputs leave as fp16 pairs.
 constexpr int kDitMaxSeq = 16;
+constexpr int kDitRow = 68;     // staged q/k/v row: 16-byte aligned, at most two-way bank conflicts
+constexpr int kDitUnits = 3;    // (row, q|k|v, 4-column pair) units per thread: 16 rows x 24 <= 3 x 128
 __global__ void __launch_bounds__(128) dit_attention_split_kernel(const float* qkv, int seq, int q_heads,
                                                                   int kv_heads, const float* rope_cos,
                                                                   const float* rope_sin, float scale, __half* xb,
                                                                   StreamCtl* ctl, int lo) {
     constexpr int D = 64, H = 32;
-    // q and k rows padded to 65 floats: the score loop reads 11 different rows per warp
-    __shared__ float qs[kDitMaxSeq][D + 1], ks[kDitMaxSeq][D + 1], vs[kDitMaxSeq][D], ps[kDitMaxSeq][kDitMaxSeq + 1];
-    __shared__ float cs_[kDitMaxSeq][D], sn_[kDitMaxSeq][D];
+    __shared__ __align__(16) float qs[kDitMaxSeq][kDitRow], ks[kDitMaxSeq][kDitRow], vs[kDitMaxSeq][kDitRow];
+    __shared__ float ps[kDitMaxSeq][kDitMaxSeq + 1];
+    __shared__ __align__(16) float cs_[kDitMaxSeq][D], sn_[kDitMaxSeq][D];
     pdl_launch_dependents();
     const int h = blockIdx.x, sq = blockIdx.y, kvh = h / (q_heads / kv_heads), tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
     const int width = (q_heads + 2 * kv_heads) * D;
     // RoPE tables first: they do not depend on the previous kernel
     for (int u = tid; u < seq * 16; u += 128) {
@@ -334,68 +341,86 @@ __global__ void __launch_bounds__(128) dit_attention_split_kernel(const float* q
         *reinterpret_cast<float4*>(&sn_[i][e4]) = __ldg(reinterpret_cast<const float4*>(rope_sin + i * D + e4));
     }
     pdl_wait();
-    if (ctl && ctl->stopped) return;
-    {
-        constexpr int kB = 7;  // seq * 48 float4 (<= 768) over 128 threads
-        const int total = seq * 48;
-        float4 v[kB];
+    const bool stop = ctl && ctl->stopped;  // read beside the rows; nothing is written before the check
+    // unit u: row r = u / 24, kind (q, k, v) = (u % 24) / 8, columns 4c .. 4c + 3 and 32 + 4c .. 32 + 4c + 3
+    float4 va[kDitUnits], vb[kDitUnits];
 #pragma unroll
-        for (int i = 0; i < kB; ++i) {
-            const int u = tid + 128 * i;
-            if (u < total) {
-                const int r = u / 48, w = u - r * 48, kind = w >> 4, e4 = (w & 15) * 4;
-                const int col = kind == 0 ? h * D : kind == 1 ? (q_heads + kvh) * D : (q_heads + kv_heads + kvh) * D;
-                v[i] = *reinterpret_cast<const float4*>(qkv + static_cast<size_t>(sq * seq + r) * width + col + e4);
-            }
+    for (int i = 0; i < kDitUnits; ++i) {
+        const int u = tid + 128 * i;
+        if (u < seq * 24) {
+            const int r = u / 24, w = u - r * 24, kind = w >> 3, c4 = (w & 7) * 4;
+            const int col = kind == 0 ? h * D : kind == 1 ? (q_heads + kvh) * D : (q_heads + kv_heads + kvh) * D;
+            const float* src = qkv + static_cast<size_t>(sq * seq + r) * width + col + c4;
+            va[i] = *reinterpret_cast<const float4*>(src);
+            vb[i] = *reinterpret_cast<const float4*>(src + H);
         }
+    }
+    __syncthreads();  // RoPE tables staged
+    if (stop) return;
 #pragma unroll
-        for (int i = 0; i < kB; ++i) {
-            const int u = tid + 128 * i;
-            if (u < total) {
-                const int r = u / 48, w = u - r * 48, kind = w >> 4, e4 = (w & 15) * 4;
-                float* dst = kind == 0 ? &qs[r][e4] : kind == 1 ? &ks[r][e4] : &vs[r][e4];
-                dst[0] = v[i].x;
-                dst[1] = v[i].y;
-                dst[2] = v[i].z;
-                dst[3] = v[i].w;
+    for (int i = 0; i < kDitUnits; ++i) {
+        const int u = tid + 128 * i;
+        if (u < seq * 24) {
+            const int r = u / 24, w = u - r * 24, kind = w >> 3, c4 = (w & 7) * 4;
+            float4 a = va[i], b = vb[i];
+            if (kind < 2) {  // rotate_half: x[e] cos[e] - x[e + 32] sin[e]; x[e + 32] cos[e + 32] + x[e] sin[e + 32]
+                const float4 c0 = *reinterpret_cast<const float4*>(&cs_[r][c4]);
+                const float4 s0 = *reinterpret_cast<const float4*>(&sn_[r][c4]);
+                const float4 c1 = *reinterpret_cast<const float4*>(&cs_[r][c4 + H]);
+                const float4 s1 = *reinterpret_cast<const float4*>(&sn_[r][c4 + H]);
+                const float4 ra = make_float4(a.x * c0.x + (-b.x) * s0.x, a.y * c0.y + (-b.y) * s0.y,
+                                              a.z * c0.z + (-b.z) * s0.z, a.w * c0.w + (-b.w) * s0.w);
+                const float4 rb = make_float4(b.x * c1.x + a.x * s1.x, b.y * c1.y + a.y * s1.y, b.z * c1.z + a.z * s1.z,
+                                              b.w * c1.w + a.w * s1.w);
+                a = ra;
+                b = rb;
             }
+            float* dst = kind == 0 ? qs[r] : kind == 1 ? ks[r] : vs[r];
+            *reinterpret_cast<float4*>(dst + c4) = a;
+            *reinterpret_cast<float4*>(dst + c4 + H) = b;
         }
     }
     __syncthreads();
-    // rotate_half RoPE in place: each unit owns the pair (e, e + 32) of a q or k row
-    for (int u = tid; u < 2 * seq * H; u += 128) {
-        const int which = u / (seq * H), r = u - which * seq * H, i = r / H, e = r - i * H;
-        float* row = which == 0 ? qs[i] : ks[i];
-        const float v1 = row[e], v2 = row[e + H];
-        row[e] = v1 * cs_[i][e] + (-v2) * sn_[i][e];
-        row[e + H] = v2 * cs_[i][e + H] + v1 * sn_[i][e + H];
-    }
-    __syncthreads();
-    for (int idx = tid; idx < seq * seq; idx += 128) {
-        const int i = idx / seq, j = idx - i * seq;
-        float sum = 0.f;
-        for (int e = 0; e < D; ++e) sum = fmaf(qs[i][e], ks[j][e], sum);
-        ps[i][j] = sum * scale;
-    }
-    __syncthreads();
-    if (tid < seq) {
-        const int i = tid;
-        float mx = -FLT_MAX;
-        for (int j = 0; j < seq; ++j) mx = fmaxf(mx, ps[i][j]);
-        float sum = 0.f;
-        for (int j = 0; j < seq; ++j) {
-            ps[i][j] = expf(ps[i][j] - mx);
-            sum += ps[i][j];
+    // warp w: query rows w, w + 4, ...; lane j < seq scores key j (four FMA chains), then
+    // the row's softmax across the lanes
+    for (int i = warp; i < seq; i += 4) {
+        float x = -FLT_MAX;
+        if (lane < seq) {
+            float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int c = 0; c < D; c += 4) {
+                const float4 q4 = *reinterpret_cast<const float4*>(&qs[i][c]);
+                const float4 k4 = *reinterpret_cast<const float4*>(&ks[lane][c]);
+                s4[0] = fmaf(q4.x, k4.x, s4[0]);
+                s4[1] = fmaf(q4.y, k4.y, s4[1]);
+                s4[2] = fmaf(q4.z, k4.z, s4[2]);
+                s4[3] = fmaf(q4.w, k4.w, s4[3]);
+            }
+            x = ((s4[0] + s4[1]) + (s4[2] + s4[3])) * scale;
         }
-        for (int j = 0; j < seq; ++j) ps[i][j] /= sum;
+        const float mx = warp_max(x);
+        const float p = lane < seq ? expf(x - mx) : 0.f;
+        const float sum = warp_sum(p);
+        if (lane < seq) ps[i][lane] = p / sum;
     }
     __syncthreads();
+    // P.V: thread -> (row i, column pair e); hi and lo halves stored as fp16 pairs
     const int ld = q_heads * D;
-    for (int idx = tid; idx < seq * D; idx += 128) {
-        const int i = idx / D, e = idx - i * D;
-        float acc = 0.f;
-        for (int j = 0; j < seq; ++j) acc = fmaf(ps[i][j], vs[j][e], acc);
-        split_store(xb, ld, sq * seq + i, h * D + e, acc, lo);
+    for (int u = tid; u < seq * H; u += 128) {
+        const int i = u / H, e = (u - i * H) * 2;
+        float a0 = 0.f, a1 = 0.f;
+        for (int j = 0; j < seq; ++j) {
+            const float pj = ps[i][j];
+            const float2 v2 = *reinterpret_cast<const float2*>(&vs[j][e]);
+            a0 = fmaf(pj, v2.x, a0);
+            a1 = fmaf(pj, v2.y, a1);
+        }
+        const __half2 hi = __floats2half2_rn(a0, a1);
+        const float2 hf = __half22float2(hi);
+        const __half2 lw = __floats2half2_rn(a0 - hf.x, a1 - hf.y);
+        const size_t row = static_cast<size_t>(sq * seq + i), col = static_cast<size_t>(h * D + e);
+        *reinterpret_cast<__half2*>(xb + row * ld + col) = hi;
+        *reinterpret_cast<__half2*>(xb + (lo + row) * ld + col) = lw;
     }
 }
 
@@ -476,27 +501,32 @@ __global__ void __launch_bounds__(kEmbedThreads) dit_embed_kernel(const DitEmbed
         }
     }
     pdl_wait();
-    if (a.ctl && a.ctl->stopped) return;
+    // the stop flag, the x / cond rows and (threads of the first two feature rows)
+    // the mu and time rows are read in one batch; nothing is written before the check
+    const bool stop = a.ctl && a.ctl->stopped;
+    const int fl = threadIdx.x & (kEmbedFeatures - 1), j = threadIdx.x / kEmbedFeatures;
+    const int f = f0 + fl;
+    const bool live = f < a.Hd;
+    float v0 = 0.f, v1 = 0.f, v2 = 0.f;
+    if (j < 2 && live) {  // mu tokens and the time token of sequence j
+        const float* mu = j == 0 ? a.mu : a.mu_uncond;
+        v0 = mu ? mu[f] : 0.f;
+        v1 = mu ? mu[a.Hd + f] : 0.f;
+        v2 = a.tsum ? a.tsum[f] : (j == 0 ? a.t_tok0 : a.t_tok1)[f] + (j == 0 ? a.dt_tok0 : a.dt_tok1)[f];
+    }
     for (int i = threadIdx.x; i < DP; i += kEmbedThreads) {
         xs[i] = a.x[i];
         xs[DP + i] = a.x_uncond ? a.x_uncond[i] : a.x[i];
         cs[i] = a.cond[i];
         cs[DP + i] = a.cond_uncond ? a.cond_uncond[i] : a.cond[i];
     }
+    if (stop) return;
     __syncthreads();
-    const int fl = threadIdx.x & (kEmbedFeatures - 1), j = threadIdx.x / kEmbedFeatures;
-    const int f = f0 + fl;
-    const bool live = f < a.Hd;
     const int seq = 3 + 2 * P;
     __shared__ float vals[24][kEmbedFeatures + 1];  // this block's outputs, for the sums of squares
-    if (j < 2) {  // mu tokens and the time token of sequence j
+    if (j < 2) {
         const int b = j;
-        const float* mu = b == 0 ? a.mu : a.mu_uncond;
-        float v0 = 0.f, v1 = 0.f, v2 = 0.f;
         if (live) {
-            v0 = mu ? mu[f] : 0.f;
-            v1 = mu ? mu[a.Hd + f] : 0.f;
-            v2 = a.tsum ? a.tsum[f] : (b == 0 ? a.t_tok0 : a.t_tok1)[f] + (b == 0 ? a.dt_tok0 : a.dt_tok1)[f];
             float* h = a.hidden + static_cast<size_t>(b) * seq * a.Hd;
             h[f] = v0;
             h[a.Hd + f] = v1;
@@ -618,7 +648,7 @@ __global__ void __launch_bounds__(kOutThreads) dit_out_kernel(const DitOutArgs a
         }
     }
     pdl_wait();
-    if (a.ctl && a.ctl->stopped) return;
+    const bool stop = a.ctl && a.ctl->stopped;  // read beside the rows; nothing is written before the check
     // warp r normalises row r (the row read once, as float4, into registers)
     for (int r = warp; r < R; r += nw) {
         const int b = r / a.P, p = r - b * a.P;
@@ -656,6 +686,7 @@ __global__ void __launch_bounds__(kOutThreads) dit_out_kernel(const DitOutArgs a
             for (int k = lane; k < a.Hd; k += 32) xn[r * a.Hd + k] = h[k] * inv * __half2float(a.norm_g[k]);
         }
     }
+    if (stop) return;
     __syncthreads();
     // (feature, row) pairs: warp w takes pairs w, w + 8, ...
     for (int q = warp; q < kOutFeatures * R; q += nw) {
@@ -916,7 +947,7 @@ void launch_rmsnorm_rows_split(const float* x, int ldx, const __half* g, float e
 void launch_dit_attention_split(const float* qkv, int nseq, int seq, int q_heads, int kv_heads, int d,
                                 const float* rope_cos, const float* rope_sin, float scale, __half* xb,
                                 StreamCtl* ctl, cudaStream_t s, bool pdl, int lo) {
-    if (d != 64 || seq > kDitMaxSeq || seq * 48 > 128 * 7 || nseq * seq > lo ||
+    if (d != 64 || seq > kDitMaxSeq || seq * 24 > 128 * kDitUnits || nseq * seq > lo || (q_heads * d) % 2 != 0 ||
         (reinterpret_cast<uintptr_t>(qkv) & 15) || (reinterpret_cast<uintptr_t>(rope_cos) & 15) ||
         (reinterpret_cast<uintptr_t>(rope_sin) & 15))
         throw std::invalid_argument("dit attention: unsupported shape");

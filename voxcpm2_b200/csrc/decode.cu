@@ -120,9 +120,11 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
         }
     }
 
-    // 2) wait for the producer of the input vector
+    // 2) wait for the producer of the input vector. The stop flag is read together
+    // with the input (one L2 round trip, not two) and acted on once the input is
+    // staged; nothing is written to global memory before the check.
     pdl_wait();
-    if (a.skip_if_stopped && a.ctl && a.ctl->stopped) return;
+    const bool stop = a.skip_if_stopped && a.ctl && a.ctl->stopped;
 
     // 3) stage the (optionally RMS-normalised) input in shared memory. A plain
     // input is read as float4 (and its gain as 4 x fp16), every load of the thread
@@ -174,7 +176,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
     } else {
         __syncthreads();
     }
-    if (!active) return;
+    if (stop || !active) return;
 
     // 4) dot products
     float acc[RPW];
@@ -661,7 +663,16 @@ struct AttnSmem {
     float m_s[kMaxGroup], l_s[kMaxGroup], alpha_s[kMaxGroup];
 };
 
-// Keys [t0, t0 + n) of KV head kvh against the group's G query heads: tiles of
+// The G query rows of KV head kvh, scaled, into S.qs (the caller's first loads
+// after the dependency wait, issued beside its reads of the control block).
+template <int NT>
+__device__ __forceinline__ void stage_q(const AttnArgs& a, AttnSmem& S, int kvh, int G) {
+    constexpr int D = 64;
+    for (int i = threadIdx.x; i < G * D; i += NT) S.qs[i / D][i % D] = a.q[kvh * G * D + i] * a.scale;
+}
+
+// Keys [t0, t0 + n) of KV head kvh against the group's G query heads (rows staged
+// by stage_q before the call): tiles of
 // kKeyTile rows staged by one batch of loads, online softmax per head. On
 // return S.m_s / S.l_s hold the running max and sum, acc[j] the P.V partial of
 // head g_lo + j at column e = tid % 64 (heads split over the NT / 64 thread groups of
@@ -671,7 +682,6 @@ __device__ __forceinline__ void attend_keys(const AttnArgs& a, AttnSmem& S, int 
                                             float* acc) {
     constexpr int kGroups = NT / D;  // thread groups the query heads are split over
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    for (int i = tid; i < G * D; i += NT) S.qs[i / D][i % D] = a.q[kvh * G * D + i] * a.scale;
     if (tid < G) {
         S.m_s[tid] = -1e30f;
         S.l_s[tid] = 0.f;
@@ -747,14 +757,21 @@ __global__ void __launch_bounds__(kAttnSplitThreads) attn_decode_kernel(const At
     extern __shared__ float ps[];  // combine staging: [splits][G][D + 2]
     pdl_launch_dependents();
     pdl_wait();
-    if (a.skip_if_stopped && a.ctl && a.ctl->stopped) return;
-
+    // the control block and the query rows are read in one batch of loads; nothing
+    // is written to global memory before the stop flag is acted on
+    int stop = 0, kv_len = 0;
+    if (a.ctl) {
+        stop = a.skip_if_stopped ? a.ctl->stopped : 0;
+        kv_len = a.ctl->kv_len[a.which];
+    }
     const int G = a.q_heads / a.kv_heads;
     const int split = blockIdx.x, kvh = blockIdx.y;
     const int tid = threadIdx.x;
+    stage_q<NT>(a, S, kvh, G);
+    if (stop) return;
     int len0 = a.len0, len1 = a.len1;
     if (a.ctl) {
-        len0 = min(a.ctl->kv_len[a.which] + 1, a.len0);  // len0 holds the capacity here
+        len0 = min(kv_len + 1, a.len0);  // len0 holds the capacity here
         len1 = 0;
     }
     const int T = len0 + len1;
@@ -822,26 +839,48 @@ __global__ void __launch_bounds__(kAttnSplitThreads) attn_decode_kernel(const At
     if (tid == 0) a.counters[kvh] = 0;
 }
 
+constexpr int kFinalNormThreads = 256, kFinalNormPer = 16;  // H <= 4096
+
 __global__ void final_norm_kernel(const float* h, const __half* g, float eps, int H, float* out,
                                   float* out2, StreamCtl* ctl, int which, int bump, int skip) {
-    __shared__ float red[32];
+    __shared__ float red[kFinalNormThreads / 32];
     pdl_launch_dependents();
-    pdl_wait();
-    if (skip && ctl && ctl->stopped) return;
-    float ss = 0.f;
-    for (int k = threadIdx.x; k < H; k += blockDim.x) ss += h[k] * h[k];
-    ss = warp_sum(ss);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-    __syncthreads();
-    float t = 0.f;
-    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += red[w];
-    const float a = rsqrtf(t / static_cast<float>(H) + eps);
-    for (int k = threadIdx.x; k < H; k += blockDim.x) {
-        const float v = h[k] * a * __half2float(g[k]);
-        out[k] = v;
-        if (out2) out2[k] = v;
+    const int tid = threadIdx.x;
+    float gv[kFinalNormPer], hv[kFinalNormPer];
+#pragma unroll
+    for (int j = 0; j < kFinalNormPer; ++j) {  // the gain does not depend on the previous kernel
+        const int k = tid + j * kFinalNormThreads;
+        gv[j] = k < H ? __half2float(g[k]) : 0.f;
     }
-    if (bump && ctl && threadIdx.x == 0) ctl->kv_len[which] += bump;
+    pdl_wait();
+    // the stop flag and the hidden row in one batch of loads; nothing is written before the check
+    const bool stop = skip && ctl && ctl->stopped;
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < kFinalNormPer; ++j) {
+        const int k = tid + j * kFinalNormThreads;
+        hv[j] = k < H ? h[k] : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < kFinalNormPer; ++j) ss += hv[j] * hv[j];
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    if (stop) return;
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < kFinalNormThreads / 32; ++w) t += red[w];
+    const float a = rsqrtf(t / static_cast<float>(H) + eps);
+#pragma unroll
+    for (int j = 0; j < kFinalNormPer; ++j) {
+        const int k = tid + j * kFinalNormThreads;
+        if (k < H) {
+            const float v = hv[j] * a * gv[j];
+            out[k] = v;
+            if (out2) out2[k] = v;
+        }
+    }
+    if (bump && ctl && tid == 0) ctl->kv_len[which] += bump;
 }
 
 }  // namespace
@@ -951,13 +990,21 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_cluster_kernel(const
         a.ctl = b.ctl[m];
     }
     pdl_wait();
-    // uniform over the grid: the flag cannot change while the kernel runs
-    if (a.skip_if_stopped && a.ctl && a.ctl->stopped) return;
+    // the control block and the query rows are read in one batch of loads. The stop
+    // flag is uniform over the grid (it cannot change while the kernel runs), so every
+    // CTA of a cluster takes the same branch
+    int stop = 0, kv_len = 0;
+    if (a.ctl) {
+        stop = a.skip_if_stopped ? a.ctl->stopped : 0;
+        kv_len = a.ctl->kv_len[a.which];
+    }
     const int G = a.q_heads / a.kv_heads, C = kAttnCluster;
     const int rank = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x;
+    stage_q<kAttnThreads>(a, S, kvh, G);
+    if (stop) return;
     int len0 = a.len0, len1 = a.len1;
     if (a.ctl) {
-        len0 = min(a.ctl->kv_len[a.which] + 1, a.len0);  // len0 holds the capacity here
+        len0 = min(kv_len + 1, a.len0);  // len0 holds the capacity here
         len1 = 0;
     }
     const int T = len0 + len1;
@@ -1093,8 +1140,9 @@ void init_kernel_attributes() {
 void launch_final_norm(const float* h, const __half* g, float eps, int H, float* out, float* out2,
                        StreamCtl* ctl, int which, int bump, int skip_if_stopped, cudaStream_t s,
                        bool pdl) {
+    if (H <= 0 || H > kFinalNormThreads * kFinalNormPer) throw std::invalid_argument("final norm: hidden in [1, 4096]");
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = make_cfg(dim3(1), dim3(256), 0, s, pdl, attr);
+    cudaLaunchConfig_t cfg = make_cfg(dim3(1), dim3(kFinalNormThreads), 0, s, pdl, attr);
     check_launch(cudaLaunchKernelEx(&cfg, final_norm_kernel, h, g, eps, H, out, out2, ctl, which, bump,
                                     skip_if_stopped));
 }

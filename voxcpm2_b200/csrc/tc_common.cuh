@@ -59,6 +59,13 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
+// Prefetch a tile of a tensor map into the L2 (no shared memory, no completion).
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int x, int y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y)
+                 : "memory");
+}
+
 // K-major, 128-byte-swizzle UMMA shared-memory descriptor: start address >> 4,
 // leading offset 1 (unused for swizzled K-major), stride offset 1024 B between
 // 8-row groups, descriptor version 1, layout type 2 (SWIZZLE_128B).
@@ -111,6 +118,11 @@ __device__ __forceinline__ uint32_t peer_addr(const void* local, uint32_t rank) 
 }
 __device__ __forceinline__ void st_peer(uint32_t remote, float v) {  // fire and forget
     asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
+}
+// four floats to a 16-byte aligned address in a cluster peer's shared memory
+__device__ __forceinline__ void st_peer4(uint32_t remote, float a, float b, float c, float d) {
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(remote), "f"(a), "f"(b), "f"(c), "f"(d)
+                 : "memory");
 }
 
 __device__ __forceinline__ void store_split(__half* yb, int ld, int m, int col, float v) {

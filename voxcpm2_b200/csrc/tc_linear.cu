@@ -44,7 +44,12 @@ using namespace tc;
 constexpr int kTcThreads = 128;
 constexpr int kStageBytes = kABytes + kBBytes;    // 22 KiB, keeps 1 KiB alignment
 constexpr int kMaxStages = 8;
-constexpr int kRecvFloats = kTileRows * kLoOffset;  // split-K receive buffer: every partial of one tile
+// split-K receive buffer: every partial of one tile, [part][unit][token] with the token
+// run of a unit padded from 24 to 28 floats (16-byte stores; two- to four-way bank
+// conflicts on the owner's reads instead of eight)
+constexpr int kRecvStride = 28;
+constexpr int kRecvFloats = kTileRows * kRecvStride;
+constexpr int kMaxSsqParts = 64;  // sums-of-squares parts read in one batch (more: a serial loop)
 constexpr int kSqFloats = kTileRows * kLoOffset;    // squares of the updated rows (at most 128 x 24)
 
 // A split launch can receive in its stage area when the area holds the partials and,
@@ -74,6 +79,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __shared__ uint32_t tmem_base_s;
     __shared__ int failed_s;
     __shared__ float inv_s[kLoOffset];
+    __shared__ __align__(16) float ssq_s[kMaxSsqParts * kSsqStride];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int split = blockIdx.x, tile = blockIdx.y;
@@ -116,6 +122,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tma_load_2d(st + kABytes / 2, &map_a, (c0 + i) * kKChunk, r1, &full_bar[i]);
             issued[i] = 1;
         }
+        // the weight chunks beyond the ring: into the L2 now, so that the refills after
+        // the dependency wait are L2 hits rather than DRAM round trips
+        if (a.l2_prefetch)
+            for (int i = pre; i < cs; ++i) {
+                tma_prefetch_2d(&map_a, (c0 + i) * kKChunk, r0);
+                tma_prefetch_2d(&map_a, (c0 + i) * kKChunk, r1);
+            }
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -174,14 +187,61 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
     }
 
-    // row_scale: each token row's 1 / rms from the producer's sums of squares (warp 2,
-    // idle until the epilogue; parts summed in order)
-    if (a.row_scale && warp == 2) {
-        if (lane < a.M) {
-            float t = 0.f;
+    // Epilogue operands that do not wait for the MMAs, read now in one batch per
+    // thread: the residual rows this thread updates and (weights) the next operand's
+    // gain. Every thread has passed griddepcontrol.wait above.
+    // Thread -> output unit lu of this CTA and token rows m0, m0 + per, ... (split path),
+    // or accumulator row tid and every token row (direct path).
+    const bool direct = S == 1 && !a.gateup && !a.ssq_out;
+    const int units = a.gateup ? 64 : kTileRows, halves = a.gateup ? 2 : 1;
+    const int nu = units / S;
+    const int per = kTcThreads / nu, lu = tid % nu, m0 = tid / nu;  // per == S (== 2 S for gate/up)
+    const int col = split * nu + lu;
+    constexpr int kRows = (kLoOffset + S - 1) / S;  // token rows per thread, residual split path
+    float rres[kRows];
+    float rdir[kLoOffset];
+    float gn = 0.f;
+    if (direct) {
+        if (a.resid) {
+            const float* yc = a.y + tile * kTileRows + tid;
+#pragma unroll
+            for (int m = 0; m < kLoOffset; ++m) rdir[m] = m < a.M ? yc[static_cast<size_t>(m) * a.ldy] : 0.f;
+        }
+    } else if (!a.gateup) {
+        const float* yc = a.y + tile * kTileRows + col;
+        if (a.next_b) gn = __half2float(a.next_g[tile * kTileRows + col]);
+#pragma unroll
+        for (int j = 0; j < kRows; ++j) {
+            const int m = m0 + j * S;
+            rres[j] = (a.resid && m < a.M) ? yc[static_cast<size_t>(m) * a.ldy] : 0.f;
+        }
+    }
+
+    // row_scale: each token row's 1 / rms from the producer's sums of squares. Warps 2
+    // and 3 (idle until the epilogue) read all parts in one batch of 16-byte loads into
+    // shared memory; lane m of warp 2 then sums row m's parts in order.
+    if (a.row_scale && warp >= 2) {
+        if (a.ssq_parts <= kMaxSsqParts) {
+            const int n4 = a.ssq_parts * kSsqStride / 4, t = tid - 64;
+            const float4* src = reinterpret_cast<const float4*>(a.ssq_in);
+            constexpr int kL = kMaxSsqParts * kSsqStride / 4 / 64;
+            float4 q4[kL];
+#pragma unroll
+            for (int j = 0; j < kL; ++j) q4[j] = t + 64 * j < n4 ? __ldcg(src + t + 64 * j) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int j = 0; j < kL; ++j)
+                if (t + 64 * j < n4) reinterpret_cast<float4*>(ssq_s)[t + 64 * j] = q4[j];
+            asm volatile("bar.sync 1, 64;" ::: "memory");  // warps 2 and 3 only
+            if (warp == 2 && lane < a.M) {
+                float tsum = 0.f;
+                for (int p = 0; p < a.ssq_parts; ++p) tsum += ssq_s[p * kSsqStride + lane];
+                inv_s[lane] = rsqrtf(tsum / static_cast<float>(a.K) + a.eps);
+            }
+        } else if (warp == 2 && lane < a.M) {
+            float tsum = 0.f;
 #pragma unroll 8
-            for (int p = 0; p < a.ssq_parts; ++p) t += __ldcg(a.ssq_in + p * kSsqStride + lane);
-            inv_s[lane] = rsqrtf(t / static_cast<float>(a.K) + a.eps);
+            for (int p = 0; p < a.ssq_parts; ++p) tsum += __ldcg(a.ssq_in + p * kSsqStride + lane);
+            inv_s[lane] = rsqrtf(tsum / static_cast<float>(a.K) + a.eps);
         }
     }
 
@@ -192,8 +252,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // Output units of the tile: 128 rows, or 64 gate/up pairs; CTA p of the cluster
     // owns units [p nu, (p + 1) nu). Each thread holds one accumulator row
     // (tile row tid): v[m] = hi + lo columns of token m.
-    const int units = a.gateup ? 64 : kTileRows, halves = a.gateup ? 2 : 1;
-    const int nu = units / S;
     float v[kLoOffset];
     {
         float d[kBRows];
@@ -217,28 +275,26 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (issued[i] > 0 && !mbar_wait(&full_bar[i], (issued[i] - 1) & 1)) failed_s = 1;
     }
     if (a.row_scale) __syncthreads();  // inv_s is complete
-    if (S == 1 && !a.gateup && !a.ssq_out) {
+    if (direct) {
         // no split: straight from registers, coalesced across the warp
         if (a.row_scale) {
 #pragma unroll
             for (int m = 0; m < kLoOffset; ++m) v[m] *= inv_s[m];
         }
         float* yc = a.y + tile * kTileRows + tid;
-        float r[kLoOffset];
-#pragma unroll
-        for (int m = 0; m < kLoOffset; ++m) r[m] = (a.resid && m < a.M) ? yc[static_cast<size_t>(m) * a.ldy] : 0.f;
 #pragma unroll
         for (int m = 0; m < kLoOffset; ++m)
             if (m < a.M)
-                yc[static_cast<size_t>(m) * a.ldy] = a.resid ? r[m] + (a.rscale == 1.f ? v[m] : v[m] * a.rscale) : v[m];
+                yc[static_cast<size_t>(m) * a.ldy] =
+                    a.resid ? rdir[m] + (a.rscale == 1.f ? v[m] : v[m] * a.rscale) : v[m];
         __syncthreads();
     } else {
-        // Split-K exchange by push: each CTA stores its partials straight into the
-        // receive buffer of the CTA that owns them (non-blocking remote stores),
-        // token-major so that a warp's store is one contiguous run; one cluster
-        // barrier; then owners sum the splits in rank order (deterministic).
-        // recv[((p * halves + half) * M + m) * nu + lu]. Without a K split it lives in
-        // the (then idle) stage area, so more CTAs of concurrent streams fit on an SM.
+        // Split-K exchange by push: each CTA stores its accumulator rows straight into
+        // the receive buffer of the CTA that owns them, as 16-byte remote stores (a
+        // thread's kLoOffset tokens are one contiguous run, recv[part][unit][token]
+        // with a padded token stride); one cluster barrier; then owners sum the splits
+        // in rank order (deterministic). Without a K split it lives in the (then idle)
+        // stage area, so more CTAs of concurrent streams fit on an SM.
         // 'shared' and S depend only on launch arguments, never on this CTA's data or on a
         // failed wait, so every CTA of the cluster passes the same cluster barriers
         const bool shared = shared_recv_fits(b_tma, S, a.recv_shared, static_cast<size_t>(stage_area) * kStageBytes);
@@ -249,26 +305,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (shared) cluster_sync();  // ... in every CTA of the cluster: partials may land in it
         {
             const int u = a.gateup ? (tid & 63) : tid, half = a.gateup ? (tid >> 6) : 0;
-            const int owner = u / nu, lu = u - owner * nu;
-            float* dst = recv + static_cast<size_t>((split * halves + half) * a.M) * nu + lu;
+            const int owner = u / nu, ou = u - owner * nu;
+            float* dst = recv + static_cast<size_t>((split * halves + half) * nu + ou) * kRecvStride;
             if (owner == split) {
 #pragma unroll
-                for (int m = 0; m < kLoOffset; ++m)
-                    if (m < a.M) dst[m * nu] = v[m];
+                for (int c = 0; c < kLoOffset / 4; ++c)
+                    reinterpret_cast<float4*>(dst)[c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
             } else {
                 const uint32_t remote = peer_addr(dst, owner);
 #pragma unroll
-                for (int m = 0; m < kLoOffset; ++m)
-                    if (m < a.M) st_peer(remote + 4u * m * nu, v[m]);
+                for (int c = 0; c < kLoOffset / 4; ++c)
+                    st_peer4(remote + 16u * c, v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
             }
         }
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         if (S > 1) cluster_sync();  // every partial has landed in its owner's buffer
         else __syncthreads();
-        // this CTA's units: thread -> (unit lu, token rows m0, m0 + per, ...);
-        // each batch issues all its loads before any of its stores
-        const int per = kTcThreads / nu, lu = tid % nu, m0 = tid / nu;
-        const int col = split * nu + lu;
+        // this CTA's units: thread -> (unit lu, token rows m0, m0 + per, ...); all of a
+        // thread's partials are read before any result is stored
         // the stage area is idle now: squares of updated rows (behind the partials when those share it)
         float* sq = reinterpret_cast<float*>(smem) + (shared ? kRecvFloats : 0);
         if (a.gateup) {
@@ -280,8 +334,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     const int mc = min(mb + j * per, a.M - 1);
 #pragma unroll
                     for (int p = 0; p < S; ++p) {
-                        g[j][p] = recv[static_cast<size_t>((p * 2 + 0) * a.M + mc) * nu + lu];
-                        up[j][p] = recv[static_cast<size_t>((p * 2 + 1) * a.M + mc) * nu + lu];
+                        g[j][p] = recv[static_cast<size_t>((p * 2 + 0) * nu + lu) * kRecvStride + mc];
+                        up[j][p] = recv[static_cast<size_t>((p * 2 + 1) * nu + lu) * kRecvStride + mc];
                     }
                 }
 #pragma unroll
@@ -303,32 +357,26 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
             }
         } else {
-            constexpr int kBatch = 8;
             float* yc = a.y + tile * kTileRows + col;
-            const float gn = a.next_b ? __half2float(a.next_g[tile * kTileRows + col]) : 0.f;
-            for (int mb = m0; mb < a.M; mb += per * kBatch) {
-                float part[kBatch][S], r[kBatch];
+            float part[kRows][S];
 #pragma unroll
-                for (int j = 0; j < kBatch; ++j) {
-                    const int m = mb + j * per;
-                    const int mc = min(m, a.M - 1);
+            for (int j = 0; j < kRows; ++j) {
+                const int mc = min(m0 + j * S, a.M - 1);
 #pragma unroll
-                    for (int p = 0; p < S; ++p) part[j][p] = recv[static_cast<size_t>(p * a.M + mc) * nu + lu];
-                    r[j] = (a.resid && m < a.M) ? yc[static_cast<size_t>(m) * a.ldy] : 0.f;
-                }
+                for (int p = 0; p < S; ++p) part[j][p] = recv[static_cast<size_t>(p * nu + lu) * kRecvStride + mc];
+            }
 #pragma unroll
-                for (int j = 0; j < kBatch; ++j) {
-                    const int m = mb + j * per;
-                    if (m < a.M) {
-                        float sum = 0.f;
+            for (int j = 0; j < kRows; ++j) {
+                const int m = m0 + j * S;
+                if (m < a.M) {
+                    float sum = 0.f;
 #pragma unroll
-                        for (int p = 0; p < S; ++p) sum += part[j][p];
-                        if (a.row_scale) sum *= inv_s[m];
-                        const float nv = a.resid ? r[j] + (a.rscale == 1.f ? sum : sum * a.rscale) : sum;
-                        yc[static_cast<size_t>(m) * a.ldy] = nv;
-                        if (a.ssq_out) sq[m * nu + lu] = nv * nv;
-                        if (a.next_b) store_split(a.next_b, a.ldnb, m, tile * kTileRows + col, nv * gn);
-                    }
+                    for (int p = 0; p < S; ++p) sum += part[j][p];
+                    if (a.row_scale) sum *= inv_s[m];
+                    const float nv = a.resid ? rres[j] + (a.rscale == 1.f ? sum : sum * a.rscale) : sum;
+                    yc[static_cast<size_t>(m) * a.ldy] = nv;
+                    if (a.ssq_out) sq[m * nu + lu] = nv * nv;
+                    if (a.next_b) store_split(a.next_b, a.ldnb, m, tile * kTileRows + col, nv * gn);
                 }
             }
         }
@@ -399,8 +447,8 @@ void launch_tc_linear(const CUtensorMap& map_a, const CUtensorMap& map_b, const 
     if (a.ssq_out && (a.gateup || a.M > kSsqStride)) throw std::invalid_argument("tc_linear: bad ssq_out");
     if (a.next_b && (!a.ssq_out || !a.next_g || !a.resid || a.ldnb < a.rows))
         throw std::invalid_argument("tc_linear: next_b needs a residual launch with ssq_out and next_g");
-    if (a.row_scale && (!a.ssq_in || a.ssq_parts <= 0))
-        throw std::invalid_argument("tc_linear: row_scale needs ssq_in parts");
+    if (a.row_scale && (!a.ssq_in || a.ssq_parts <= 0 || (reinterpret_cast<uintptr_t>(a.ssq_in) & 15) != 0))
+        throw std::invalid_argument("tc_linear: row_scale needs 16-byte aligned ssq_in parts");
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.splits, n_tiles);
     cfg.blockDim = dim3(kTcThreads);
