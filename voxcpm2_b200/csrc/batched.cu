@@ -317,111 +317,93 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_rows_split_kernel(const 
 // cache, voxcpm2_sdpa.cpp:187-252), written as the o projection's split operand.
 // Every load after the dependency wait (the stop flag and the head's q/k/v rows)
 // is issued in one batch; each thread rotates the (e, e + 32) column pairs it
-// loaded in registers before staging them. A warp owns a query row's scores and
-// softmax (lane j scores key j), and the P.V outputs leave as fp16 pairs.
+// loaded in registers before staging them. Warp i then owns query row i from
+// end to end (lane j scores key j, the softmax across the lanes, lane c forms
+// output columns 2c and 2c + 1), so only one block barrier follows the staging,
+// and the outputs leave as fp16 pairs.
 constexpr int kDitMaxSeq = 16;
-constexpr int kDitRow = 68;     // staged q/k/v row: 16-byte aligned, at most two-way bank conflicts
-constexpr int kDitUnits = 3;    // (row, q|k|v, 4-column pair) units per thread: 16 rows x 24 <= 3 x 128
-__global__ void __launch_bounds__(128) dit_attention_split_kernel(const float* qkv, int seq, int q_heads,
-                                                                  int kv_heads, const float* rope_cos,
-                                                                  const float* rope_sin, float scale, __half* xb,
-                                                                  StreamCtl* ctl, int lo) {
+constexpr int kDitThreads = 32 * kDitMaxSeq;  // a warp per query row
+constexpr int kDitRow = 68;  // staged q/k/v row: 16-byte aligned, at most two-way bank conflicts
+__global__ void __launch_bounds__(kDitThreads) dit_attention_split_kernel(const float* qkv, int seq, int q_heads,
+                                                                          int kv_heads, const float* rope_cos,
+                                                                          const float* rope_sin, float scale,
+                                                                          __half* xb, StreamCtl* ctl, int lo) {
     constexpr int D = 64, H = 32;
     __shared__ __align__(16) float qs[kDitMaxSeq][kDitRow], ks[kDitMaxSeq][kDitRow], vs[kDitMaxSeq][kDitRow];
-    __shared__ float ps[kDitMaxSeq][kDitMaxSeq + 1];
-    __shared__ __align__(16) float cs_[kDitMaxSeq][D], sn_[kDitMaxSeq][D];
+    __shared__ float ps[kDitMaxSeq][kDitMaxSeq];
     pdl_launch_dependents();
     const int h = blockIdx.x, sq = blockIdx.y, kvh = h / (q_heads / kv_heads), tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
     const int width = (q_heads + 2 * kv_heads) * D;
-    // RoPE tables first: they do not depend on the previous kernel
-    for (int u = tid; u < seq * 16; u += 128) {
-        const int i = u >> 4, e4 = (u & 15) * 4;
-        *reinterpret_cast<float4*>(&cs_[i][e4]) = __ldg(reinterpret_cast<const float4*>(rope_cos + i * D + e4));
-        *reinterpret_cast<float4*>(&sn_[i][e4]) = __ldg(reinterpret_cast<const float4*>(rope_sin + i * D + e4));
+    // unit tid: row r = tid / 24, kind (q, k, v) = (tid % 24) / 8, columns 4c .. 4c + 3 and
+    // 32 + 4c .. 32 + 4c + 3. Its RoPE factors do not depend on the previous kernel.
+    const bool unit = tid < seq * 24;
+    const int r = tid / 24, w = tid - r * 24, kind = w >> 3, c4 = (w & 7) * 4;
+    float4 c0 = {}, s0 = {}, c1 = {}, s1 = {};
+    if (unit && kind < 2) {
+        c0 = __ldg(reinterpret_cast<const float4*>(rope_cos + r * D + c4));
+        s0 = __ldg(reinterpret_cast<const float4*>(rope_sin + r * D + c4));
+        c1 = __ldg(reinterpret_cast<const float4*>(rope_cos + r * D + c4 + H));
+        s1 = __ldg(reinterpret_cast<const float4*>(rope_sin + r * D + c4 + H));
     }
     pdl_wait();
     const bool stop = ctl && ctl->stopped;  // read beside the rows; nothing is written before the check
-    // unit u: row r = u / 24, kind (q, k, v) = (u % 24) / 8, columns 4c .. 4c + 3 and 32 + 4c .. 32 + 4c + 3
-    float4 va[kDitUnits], vb[kDitUnits];
-#pragma unroll
-    for (int i = 0; i < kDitUnits; ++i) {
-        const int u = tid + 128 * i;
-        if (u < seq * 24) {
-            const int r = u / 24, w = u - r * 24, kind = w >> 3, c4 = (w & 7) * 4;
-            const int col = kind == 0 ? h * D : kind == 1 ? (q_heads + kvh) * D : (q_heads + kv_heads + kvh) * D;
-            const float* src = qkv + static_cast<size_t>(sq * seq + r) * width + col + c4;
-            va[i] = *reinterpret_cast<const float4*>(src);
-            vb[i] = *reinterpret_cast<const float4*>(src + H);
+    if (unit) {
+        const int col = kind == 0 ? h * D : kind == 1 ? (q_heads + kvh) * D : (q_heads + kv_heads + kvh) * D;
+        const float* src = qkv + static_cast<size_t>(sq * seq + r) * width + col + c4;
+        float4 a = *reinterpret_cast<const float4*>(src);
+        float4 b = *reinterpret_cast<const float4*>(src + H);
+        if (kind < 2) {  // rotate_half: x[e] cos[e] - x[e + 32] sin[e]; x[e + 32] cos[e + 32] + x[e] sin[e + 32]
+            const float4 ra = make_float4(a.x * c0.x + (-b.x) * s0.x, a.y * c0.y + (-b.y) * s0.y,
+                                          a.z * c0.z + (-b.z) * s0.z, a.w * c0.w + (-b.w) * s0.w);
+            const float4 rb = make_float4(b.x * c1.x + a.x * s1.x, b.y * c1.y + a.y * s1.y, b.z * c1.z + a.z * s1.z,
+                                          b.w * c1.w + a.w * s1.w);
+            a = ra;
+            b = rb;
         }
+        float* dst = kind == 0 ? qs[r] : kind == 1 ? ks[r] : vs[r];
+        *reinterpret_cast<float4*>(dst + c4) = a;
+        *reinterpret_cast<float4*>(dst + c4 + H) = b;
     }
-    __syncthreads();  // RoPE tables staged
     if (stop) return;
-#pragma unroll
-    for (int i = 0; i < kDitUnits; ++i) {
-        const int u = tid + 128 * i;
-        if (u < seq * 24) {
-            const int r = u / 24, w = u - r * 24, kind = w >> 3, c4 = (w & 7) * 4;
-            float4 a = va[i], b = vb[i];
-            if (kind < 2) {  // rotate_half: x[e] cos[e] - x[e + 32] sin[e]; x[e + 32] cos[e + 32] + x[e] sin[e + 32]
-                const float4 c0 = *reinterpret_cast<const float4*>(&cs_[r][c4]);
-                const float4 s0 = *reinterpret_cast<const float4*>(&sn_[r][c4]);
-                const float4 c1 = *reinterpret_cast<const float4*>(&cs_[r][c4 + H]);
-                const float4 s1 = *reinterpret_cast<const float4*>(&sn_[r][c4 + H]);
-                const float4 ra = make_float4(a.x * c0.x + (-b.x) * s0.x, a.y * c0.y + (-b.y) * s0.y,
-                                              a.z * c0.z + (-b.z) * s0.z, a.w * c0.w + (-b.w) * s0.w);
-                const float4 rb = make_float4(b.x * c1.x + a.x * s1.x, b.y * c1.y + a.y * s1.y, b.z * c1.z + a.z * s1.z,
-                                              b.w * c1.w + a.w * s1.w);
-                a = ra;
-                b = rb;
-            }
-            float* dst = kind == 0 ? qs[r] : kind == 1 ? ks[r] : vs[r];
-            *reinterpret_cast<float4*>(dst + c4) = a;
-            *reinterpret_cast<float4*>(dst + c4 + H) = b;
-        }
-    }
     __syncthreads();
-    // warp w: query rows w, w + 4, ...; lane j < seq scores key j (four FMA chains), then
-    // the row's softmax across the lanes
-    for (int i = warp; i < seq; i += 4) {
-        float x = -FLT_MAX;
-        if (lane < seq) {
-            float s4[4] = {0.f, 0.f, 0.f, 0.f};
+    const int i = warp;  // query row
+    if (i >= seq) return;
+    float x = -FLT_MAX;
+    if (lane < seq) {
+        float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int c = 0; c < D; c += 4) {
-                const float4 q4 = *reinterpret_cast<const float4*>(&qs[i][c]);
-                const float4 k4 = *reinterpret_cast<const float4*>(&ks[lane][c]);
-                s4[0] = fmaf(q4.x, k4.x, s4[0]);
-                s4[1] = fmaf(q4.y, k4.y, s4[1]);
-                s4[2] = fmaf(q4.z, k4.z, s4[2]);
-                s4[3] = fmaf(q4.w, k4.w, s4[3]);
-            }
-            x = ((s4[0] + s4[1]) + (s4[2] + s4[3])) * scale;
+        for (int c = 0; c < D; c += 4) {
+            const float4 q4 = *reinterpret_cast<const float4*>(&qs[i][c]);
+            const float4 k4 = *reinterpret_cast<const float4*>(&ks[lane][c]);
+            s4[0] = fmaf(q4.x, k4.x, s4[0]);
+            s4[1] = fmaf(q4.y, k4.y, s4[1]);
+            s4[2] = fmaf(q4.z, k4.z, s4[2]);
+            s4[3] = fmaf(q4.w, k4.w, s4[3]);
         }
-        const float mx = warp_max(x);
-        const float p = lane < seq ? expf(x - mx) : 0.f;
-        const float sum = warp_sum(p);
-        if (lane < seq) ps[i][lane] = p / sum;
+        x = ((s4[0] + s4[1]) + (s4[2] + s4[3])) * scale;
     }
-    __syncthreads();
-    // P.V: thread -> (row i, column pair e); hi and lo halves stored as fp16 pairs
-    const int ld = q_heads * D;
-    for (int u = tid; u < seq * H; u += 128) {
-        const int i = u / H, e = (u - i * H) * 2;
-        float a0 = 0.f, a1 = 0.f;
-        for (int j = 0; j < seq; ++j) {
-            const float pj = ps[i][j];
-            const float2 v2 = *reinterpret_cast<const float2*>(&vs[j][e]);
-            a0 = fmaf(pj, v2.x, a0);
-            a1 = fmaf(pj, v2.y, a1);
-        }
-        const __half2 hi = __floats2half2_rn(a0, a1);
-        const float2 hf = __half22float2(hi);
-        const __half2 lw = __floats2half2_rn(a0 - hf.x, a1 - hf.y);
-        const size_t row = static_cast<size_t>(sq * seq + i), col = static_cast<size_t>(h * D + e);
-        *reinterpret_cast<__half2*>(xb + row * ld + col) = hi;
-        *reinterpret_cast<__half2*>(xb + (lo + row) * ld + col) = lw;
+    const float mx = warp_max(x);
+    const float p = lane < seq ? expf(x - mx) : 0.f;
+    const float sum = warp_sum(p);
+    if (lane < seq) ps[i][lane] = p / sum;
+    __syncwarp();
+    // P.V: lane c -> output columns 2c, 2c + 1; hi and lo halves stored as fp16 pairs
+    const int e = lane * 2;
+    float a0 = 0.f, a1 = 0.f;
+    for (int j = 0; j < seq; ++j) {
+        const float pj = ps[i][j];
+        const float2 v2 = *reinterpret_cast<const float2*>(&vs[j][e]);
+        a0 = fmaf(pj, v2.x, a0);
+        a1 = fmaf(pj, v2.y, a1);
     }
+    const __half2 hi = __floats2half2_rn(a0, a1);
+    const float2 hf = __half22float2(hi);
+    const __half2 lw = __floats2half2_rn(a0 - hf.x, a1 - hf.y);
+    const size_t ld = static_cast<size_t>(q_heads) * D, row = static_cast<size_t>(sq * seq + i);
+    const size_t col = static_cast<size_t>(h * D + e);
+    *reinterpret_cast<__half2*>(xb + row * ld + col) = hi;
+    *reinterpret_cast<__half2*>(xb + (lo + row) * ld + col) = lw;
 }
 
 __global__ void embed_gather_kernel(const __half* table, const int32_t* ids, int H, float scale,
@@ -947,12 +929,12 @@ void launch_rmsnorm_rows_split(const float* x, int ldx, const __half* g, float e
 void launch_dit_attention_split(const float* qkv, int nseq, int seq, int q_heads, int kv_heads, int d,
                                 const float* rope_cos, const float* rope_sin, float scale, __half* xb,
                                 StreamCtl* ctl, cudaStream_t s, bool pdl, int lo) {
-    if (d != 64 || seq > kDitMaxSeq || seq * 24 > 128 * kDitUnits || nseq * seq > lo || (q_heads * d) % 2 != 0 ||
+    if (d != 64 || seq > kDitMaxSeq || nseq * seq > lo ||
         (reinterpret_cast<uintptr_t>(qkv) & 15) || (reinterpret_cast<uintptr_t>(rope_cos) & 15) ||
         (reinterpret_cast<uintptr_t>(rope_sin) & 15))
         throw std::invalid_argument("dit attention: unsupported shape");
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = make_cfg(dim3(q_heads, nseq), dim3(128), 0, s, pdl, attr);
+    cudaLaunchConfig_t cfg = make_cfg(dim3(q_heads, nseq), dim3(kDitThreads), 0, s, pdl, attr);
     check_launch(cudaLaunchKernelEx(&cfg, dit_attention_split_kernel, qkv, seq, q_heads, kv_heads, rope_cos, rope_sin,
                                     scale, xb, ctl, lo));
 }

@@ -203,15 +203,28 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
 // The register-streaming GEMV for up to kGemvBatch members (streams of a group):
 // each warp's weight rows are loaded once into registers, every member's input is
 // staged (and RMS-normalised) in shared memory, and the warp forms one dot product
-// per member; lane m stores member m. IN_PLAIN inputs only.
-template <int MODE, int MAXCH, int RPW, int NB>
-__global__ void __launch_bounds__(kGemvThreads) gemv_batch_kernel(const GemvArgs a, const GemvBatch b) {
+// per member; lane m stores member m. IN_PLAIN inputs only. W warps per CTA: a
+// CTA stages all members' inputs once for its W weight rows (16 warps for 8-member
+// batches, whose staged inputs are up to 128 KB). The inputs arrive by cp.async,
+// every member's in one batch (one L2 round trip), with the stop flags beside them.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(
+                     smem_dst))),
+                 "l"(gsrc)
+                 : "memory");
+}
+
+template <int MODE, int MAXCH, int RPW, int NB, int W>
+__global__ void __launch_bounds__(W * 32, (W > 4 && MAXCH <= 8) ? 2 : 1)
+    gemv_batch_kernel(const GemvArgs a, const GemvBatch b) {
     static_assert(NB <= kGemvBatch && NB <= kWarp, "lane m stores member m");
-    extern __shared__ float xs[];  // [nb][K]
-    __shared__ float red[NB][kGemvWarps];
+    constexpr int T = W * 32;
+    constexpr int kV = (MAXCH * 64 + T - 1) / T;  // float4 of one member's input per thread (K <= 256 MAXCH)
+    extern __shared__ float xs[];                 // [nb][K]
+    __shared__ float red[NB][W];
     pdl_launch_dependents();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int item = blockIdx.x * kGemvWarps + warp;
+    const int item = blockIdx.x * W + warp;
     const bool active = item < a.rows;
     const int K = a.K;
     int row[RPW];
@@ -237,7 +250,26 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_batch_kernel(const GemvArgs
             wr[r][c] = (active && e < K) ? ld_stream(wrow + e) : make_uint4(0, 0, 0, 0);
         }
     }
+    const int n4 = K >> 2;
+    uint2 gv[kV];  // the RMSNorm gain: a weight, read before the dependency wait
+#pragma unroll
+    for (int j = 0; j < kV; ++j) {
+        const int i = threadIdx.x + j * T;
+        gv[j] = (a.norm_g && i < n4) ? reinterpret_cast<const uint2*>(a.norm_g)[i] : make_uint2(0u, 0u);
+    }
     pdl_wait();
+    // every member's input and stop flag in one batch (a stopped member's input is still
+    // valid memory; its results are simply not stored)
+#pragma unroll
+    for (int m = 0; m < NB; ++m) {
+        if (m >= b.n) break;
+#pragma unroll
+        for (int j = 0; j < kV; ++j) {
+            const int i = threadIdx.x + j * T;
+            if (i < n4) cp_async16(xs + static_cast<size_t>(m) * K + 4 * i, b.x[m] + 4 * i);
+        }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
     bool live[NB];
     bool any = false;
 #pragma unroll
@@ -245,37 +277,26 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_batch_kernel(const GemvArgs
         live[m] = m < b.n && !(a.skip_if_stopped && b.ctl[m] && b.ctl[m]->stopped);
         any = any || live[m];
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
     if (!any) return;
-    constexpr int kV = MAXCH >= 2 ? MAXCH / 2 : 1;
-    const int n4 = K >> 2;
-    uint2 gv[kV];
-#pragma unroll
-    for (int j = 0; j < kV; ++j) {
-        const int i = threadIdx.x + j * kGemvThreads;
-        gv[j] = (a.norm_g && i < n4) ? reinterpret_cast<const uint2*>(a.norm_g)[i] : make_uint2(0u, 0u);
-    }
+    // each thread normalises the float4 it staged (its own copies: no barrier needed)
 #pragma unroll
     for (int m = 0; m < NB; ++m) {
         if (!live[m]) continue;
-        float4 xv[kV];
-#pragma unroll
-        for (int j = 0; j < kV; ++j) {
-            const int i = threadIdx.x + j * kGemvThreads;
-            xv[j] = i < n4 ? reinterpret_cast<const float4*>(b.x[m])[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
         float ss = 0.f;
 #pragma unroll
         for (int j = 0; j < kV; ++j) {
-            const int i = threadIdx.x + j * kGemvThreads;
+            const int i = threadIdx.x + j * T;
             if (i < n4) {
-                float4 v = xv[j];
+                float4* p4 = reinterpret_cast<float4*>(xs + static_cast<size_t>(m) * K) + i;
+                float4 v = *p4;
                 ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
                 if (a.norm_g) {
                     const float2 g01 = __half22float2(*reinterpret_cast<const __half2*>(&gv[j].x));
                     const float2 g23 = __half22float2(*reinterpret_cast<const __half2*>(&gv[j].y));
                     v = make_float4(v.x * g01.x, v.y * g01.y, v.z * g23.x, v.w * g23.y);
+                    *p4 = v;
                 }
-                reinterpret_cast<float4*>(xs + static_cast<size_t>(m) * K)[i] = v;
             }
         }
         if (a.norm_g) {
@@ -291,7 +312,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_batch_kernel(const GemvArgs
         if (a.norm_g && live[m]) {
             float t = 0.f;
 #pragma unroll
-            for (int w = 0; w < kGemvWarps; ++w) t += red[m][w];
+            for (int w = 0; w < W; ++w) t += red[m][w];
             inv_rms[m] = rsqrtf(t / static_cast<float>(K) + a.eps);
         }
     }
@@ -591,19 +612,24 @@ void dispatch_gemv_bulk(const GemvArgs& a, const GemvBatch& b, cudaStream_t s, b
     check_launch(cudaLaunchKernelEx(&cfg, gemv_bulk_kernel<MODE>, a, b, upb));
 }
 
-// NB: the member slots a launch unrolls (4 for groups of up to 4, else 8)
+// NB: the member slots a launch unrolls (4 for groups of up to 4, else 8); W: warps per
+// CTA (4, or 16 for 8-member batches)
+template <int NB>
+constexpr int batch_warps() { return NB > 4 ? 16 : 4; }
+
 template <int MODE, int RPW, int NB>
 void dispatch_gemv_batch_nb(const GemvArgs& a, const GemvBatch& b, cudaStream_t s, bool pdl) {
+    constexpr int W = batch_warps<NB>();
     const int nch = (a.K + 255) / 256;
-    const int blocks = (a.rows + kGemvWarps - 1) / kGemvWarps;
+    const int blocks = (a.rows + W - 1) / W;
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = make_cfg(dim3(blocks), dim3(kGemvThreads),
+    cudaLaunchConfig_t cfg = make_cfg(dim3(blocks), dim3(W * 32),
                                       static_cast<size_t>(b.n) * ((a.K + 7) / 8) * 8 * sizeof(float), s, pdl, attr);
-    if (nch <= 1) check_launch(cudaLaunchKernelEx(&cfg, gemv_batch_kernel<MODE, 1, RPW, NB>, a, b));
-    else if (nch <= 2) check_launch(cudaLaunchKernelEx(&cfg, gemv_batch_kernel<MODE, 2, RPW, NB>, a, b));
-    else if (nch <= 4) check_launch(cudaLaunchKernelEx(&cfg, gemv_batch_kernel<MODE, 4, RPW, NB>, a, b));
-    else if (nch <= 8) check_launch(cudaLaunchKernelEx(&cfg, gemv_batch_kernel<MODE, 8, RPW, NB>, a, b));
-    else if (RPW == 1 && nch <= 16) check_launch(cudaLaunchKernelEx(&cfg, gemv_batch_kernel<MODE, 16, 1, NB>, a, b));
+    if (nch <= 1) check_launch(cudaLaunchKernelEx(&cfg, gemv_batch_kernel<MODE, 1, RPW, NB, W>, a, b));
+    else if (nch <= 2) check_launch(cudaLaunchKernelEx(&cfg, gemv_batch_kernel<MODE, 2, RPW, NB, W>, a, b));
+    else if (nch <= 4) check_launch(cudaLaunchKernelEx(&cfg, gemv_batch_kernel<MODE, 4, RPW, NB, W>, a, b));
+    else if (nch <= 8) check_launch(cudaLaunchKernelEx(&cfg, gemv_batch_kernel<MODE, 8, RPW, NB, W>, a, b));
+    else if (RPW == 1 && nch <= 16) check_launch(cudaLaunchKernelEx(&cfg, gemv_batch_kernel<MODE, 16, 1, NB, W>, a, b));
     else throw std::invalid_argument("gemv_batch: input dimension too large");
 }
 
@@ -959,7 +985,12 @@ void launch_gemv(const GemvArgs& a, cudaStream_t s, bool pdl) {
 // g = r, r + C, ... reading the others' partials through distributed shared
 // memory. A second barrier keeps every CTA's shared memory alive until the
 // readers are done. No global scratch, no atomics.
-constexpr int kAttnCluster = 8;
+// The cluster has 16 CTAs (a non-portable size); the key range is spread over
+// max(8, ceil(T / 32)) of them, so up to 512 keys every working CTA walks one
+// 32-key tile, and short rows do not pay for a 16-way combine's idle ranks beyond
+// their barriers.
+constexpr int kAttnCluster = 16;
+constexpr int kAttnMinActive = 8;
 
 __device__ __forceinline__ float ld_peer(const float* local, uint32_t rank) {
     uint32_t addr;
@@ -1008,7 +1039,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_cluster_kernel(const
         len1 = 0;
     }
     const int T = len0 + len1;
-    const int chunk = (T + C - 1) / C, t0 = rank * chunk, n = max(0, min(T, t0 + chunk) - t0);
+    const int act = min(C, max(kAttnMinActive, (T + kKeyTile - 1) / kKeyTile));  // working CTAs
+    const int chunk = (T + act - 1) / act, t0 = rank * chunk;
+    const int n = rank < act ? max(0, min(T, t0 + chunk) - t0) : 0;
     const int e = tid & (D - 1), gh = tid / D;
     const int hg = (G + 1) / 2, g_lo = gh * hg, g_hi = min(G, g_lo + hg);
     float acc[8];
@@ -1026,10 +1059,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_cluster_kernel(const
         if (tid < D) {
             float mr[kAttnCluster], lr[kAttnCluster], ar[kAttnCluster];
 #pragma unroll
-            for (int r = 0; r < kAttnCluster; ++r) {
-                mr[r] = ld_peer(&pm[g], r);
-                lr[r] = ld_peer(&pl[g], r);
-                ar[r] = ld_peer(&pacc[g][tid], r);
+            for (int r = 0; r < kAttnCluster; ++r) {  // ranks past 'act' hold no keys: weight 0
+                mr[r] = r < act ? ld_peer(&pm[g], r) : -1e30f;
+                lr[r] = r < act ? ld_peer(&pl[g], r) : 0.f;
+                ar[r] = r < act ? ld_peer(&pacc[g][tid], r) : 0.f;
             }
             float M = -1e30f;
 #pragma unroll
@@ -1102,13 +1135,14 @@ void init_batched_attributes();
 template <int MODE, int RPW, int NB>
 void set_gemv_batch_attributes_nb() {
     constexpr int kSmem = 160 * 1024;  // up to kGemvBatch inputs of K <= 4096 (+ slack)
-    for (const void* f : {reinterpret_cast<const void*>(gemv_batch_kernel<MODE, 1, RPW, NB>),
-                          reinterpret_cast<const void*>(gemv_batch_kernel<MODE, 2, RPW, NB>),
-                          reinterpret_cast<const void*>(gemv_batch_kernel<MODE, 4, RPW, NB>),
-                          reinterpret_cast<const void*>(gemv_batch_kernel<MODE, 8, RPW, NB>)})
+    constexpr int W = batch_warps<NB>();
+    for (const void* f : {reinterpret_cast<const void*>(gemv_batch_kernel<MODE, 1, RPW, NB, W>),
+                          reinterpret_cast<const void*>(gemv_batch_kernel<MODE, 2, RPW, NB, W>),
+                          reinterpret_cast<const void*>(gemv_batch_kernel<MODE, 4, RPW, NB, W>),
+                          reinterpret_cast<const void*>(gemv_batch_kernel<MODE, 8, RPW, NB, W>)})
         check_launch(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
     if constexpr (RPW == 1)
-        check_launch(cudaFuncSetAttribute(gemv_batch_kernel<MODE, 16, 1, NB>,
+        check_launch(cudaFuncSetAttribute(gemv_batch_kernel<MODE, 16, 1, NB, W>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
 }
 template <int MODE, int RPW>
@@ -1130,6 +1164,8 @@ void init_kernel_attributes() {
                           reinterpret_cast<const void*>(gemv_bulk_kernel<GEMV_GATEUP>),
                           reinterpret_cast<const void*>(gemv_bulk_kernel<GEMV_QKV>)})
         check_launch(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kBulkSmemMax)));
+    check_launch(cudaFuncSetAttribute(attn_decode_cluster_kernel<float, 64>,
+                                      cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     init_batched_attributes();
     init_tc_attributes();
     init_tc_rows_attributes();
