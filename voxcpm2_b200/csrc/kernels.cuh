@@ -323,10 +323,6 @@ struct TcLinearArgs {
     // squares) in the idle stage area after one more cluster barrier, instead of a
     // dedicated buffer behind it (smaller CTAs, more of them per SM)
     int recv_shared = 0;
-    // prefetch the weight chunks that do not fit the ring into the L2 at kernel start
-    // (a single stream's latency setting: with many concurrent streams the prefetched
-    // lines would compete for the L2)
-    int l2_prefetch = 0;
 };
 constexpr int kSsqStride = 24;  // floats per part in a sums-of-squares buffer
 CUtensorMap make_tensor_map_f16(const void* base, int rows, int cols, int box_rows);

@@ -408,9 +408,6 @@ struct vxc_stream {
     // linears run without a K split (no cluster exchange) and concurrent streams share the SMs;
     // 148 (one per SM) trades ~45% of the multi-stream throughput for ~8% lower single-stream latency
     int tc_target = 32;
-    // prefetch each tensor-core CTA's weight chunks beyond its ring into the L2 at kernel
-    // start (VXC_TC_L2_PREFETCH=1): a single-stream latency setting
-    bool l2_prefetch = false;
     // programmatic dependent launch between the patch graph's kernels (VXC_NO_PDL=1 turns it off)
     bool pdl = true;
     // split tcgen05 linears receive their partials in the idle stage area (VXC_RECV_SHARED=1)
@@ -634,7 +631,6 @@ TcLinearArgs tc_plan(const vxc_stream* s, int tiles, int K) {
     TcLinearArgs a;
     a.splits = pow2_floor(choose_splits(tiles, K, s->tc_target));
     a.max_stages = s->tc_stages;
-    a.l2_prefetch = s->l2_prefetch ? 1 : 0;
     a.recv_shared = s->recv_shared ? 1 : 0;
     return a;
 }
@@ -1873,7 +1869,6 @@ VXC_API int32_t vxc_stream_create(vxc_device* dev, int32_t kv_capacity, vxc_stre
         if (const char* nk = std::getenv("VXC_NORM_KERNELS")) s->norm_kernels = std::string(nk) == "1";
         if (const char* rs = std::getenv("VXC_RECV_SHARED")) s->recv_shared = std::string(rs) == "1";
         if (const char* bg = std::getenv("VXC_BULK_GEMV")) s->bulk_gemv = std::string(bg) == "1";
-        if (const char* lp = std::getenv("VXC_TC_L2_PREFETCH")) s->l2_prefetch = std::string(lp) == "1";
         if (const char* tt = std::getenv("VXC_TC_TARGET")) {
             s->tc_target = std::atoi(tt);
             if (s->tc_target < 1 || s->tc_target > 4096) throw std::invalid_argument("VXC_TC_TARGET must be in [1, 4096]");

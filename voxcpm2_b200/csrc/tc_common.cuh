@@ -59,13 +59,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
-// Prefetch a tile of a tensor map into the L2 (no shared memory, no completion).
-__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int x, int y) {
-    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
-                     reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y)
-                 : "memory");
-}
-
 // K-major, 128-byte-swizzle UMMA shared-memory descriptor: start address >> 4,
 // leading offset 1 (unused for swizzled K-major), stride offset 1024 B between
 // 8-row groups, descriptor version 1, layout type 2 (SWIZZLE_128B).

@@ -122,13 +122,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tma_load_2d(st + kABytes / 2, &map_a, (c0 + i) * kKChunk, r1, &full_bar[i]);
             issued[i] = 1;
         }
-        // the weight chunks beyond the ring: into the L2 now, so that the refills after
-        // the dependency wait are L2 hits rather than DRAM round trips
-        if (a.l2_prefetch)
-            for (int i = pre; i < cs; ++i) {
-                tma_prefetch_2d(&map_a, (c0 + i) * kKChunk, r0);
-                tma_prefetch_2d(&map_a, (c0 + i) * kKChunk, r1);
-            }
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(

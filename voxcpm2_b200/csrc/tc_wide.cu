@@ -54,7 +54,9 @@ __device__ __forceinline__ void cluster_barrier() {
 
 // Shared-memory layout of a launch, the same on the host and in every CTA.
 __host__ __device__ constexpr int stage_bytes(int lo) { return kABytes + lo * kKChunk * 2 * 2; }
-__host__ __device__ constexpr size_t recv_bytes(int lo) { return static_cast<size_t>(kTileRows) * lo * 4; }
+// the receive buffer: every (split, half, unit) of a tile, a token run of lo + 4 floats each
+__host__ __device__ constexpr int recv_stride(int lo) { return lo + 4; }
+__host__ __device__ constexpr size_t recv_bytes(int lo) { return static_cast<size_t>(kTileRows) * recv_stride(lo) * 4; }
 __host__ __device__ constexpr int tmem_cols(int lo) { return lo <= 128 ? 128 : 256; }
 // The receive buffer lives in the (then idle) stage area when the CTA has no
 // K split and the stage area is large enough for it.
@@ -166,15 +168,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         pdl_wait();
     }
 
+    // output features of the tile: 128 (or 64 gate + 64 up); CTA p of the
+    // cluster owns features [p nu, (p + 1) nu) of each half. After the exchange, thread ->
+    // (feature lu, token chunks q0, q0 + per, ... of four rows each).
+    const int units = a.gateup ? 64 : kTileRows, halves = a.gateup ? 2 : 1;
+    const int nu = units / S;
+    const int per = kThreads / nu, lu = tid % nu, q0 = tid / nu;
+    const int col = split * nu + lu;
+    const int nq = (M + 3) / 4;
+    // A residual launch split 4 or 8 ways reads this thread's residual rows now, in one
+    // batch, instead of after the exchange (at most 11 chunks of four rows per thread).
+    constexpr int kPreQ = S >= 4 ? (kWideTokens / 4 + S - 1) / S : 1;
+    float rpre[kPreQ][4];
+    if constexpr (S >= 4) {
+        if (!a.gateup && a.resid) {
+            const float* yc = a.y + tile * kTileRows + col;
+#pragma unroll
+            for (int jj = 0; jj < kPreQ; ++jj)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int m = 4 * (q0 + jj * per) + i;
+                    rpre[jj][i] = m < M ? yc[static_cast<size_t>(m) * a.ldy] : 0.f;
+                }
+        }
+    }
+
     const bool ok = mbar_wait(&done_bar, 0);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (!ok) failed_s = 1;
     // tcgen05.ld is warp-collective: read the accumulator only if the whole warp saw it complete
     const bool wok = __all_sync(0xffffffffu, ok);
-    // output features of the tile: 128 (or 64 gate + 64 up); CTA p of the
-    // cluster owns features [p nu, (p + 1) nu) of each half
-    const int units = a.gateup ? 64 : kTileRows, halves = a.gateup ? 2 : 1;
-    const int nu = units / S;
     // split launches may receive in the stage area too, once every CTA of the cluster is done with its own
     const bool shared_recv = S > 1 && a.recv_shared && static_cast<size_t>(stage_area) * kstage >= recv_bytes(lo);
     const bool local_recv = recv_in_stages(S, stages, lo) || shared_recv;
@@ -221,58 +244,64 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else {
-        // partials, token-major per owner: recv[((p * halves + half) * M + m) * nu + lu]
+        // partials, one contiguous token run per (split, half, unit):
+        // recv[((p * halves + half) * nu + lu) * rs + m], rs = lo + 4. Pushes are 16-byte
+        // stores, and the owner reads four token rows per 16-byte load (row stride of 4
+        // banks modulo 32: each quarter-warp phase touches all 32 banks once).
+        const int rs = recv_stride(lo);
         float* recv = reinterpret_cast<float*>(local_recv ? smem : smem + static_cast<size_t>(stage_area) * kstage);
         if (shared_recv) cluster_barrier();  // every CTA's loads have landed: the stage areas are free
         {
             const int u = a.gateup ? (tid & 63) : tid, half = a.gateup ? (tid >> 6) : 0;
-            const int owner = u / nu, lu = u - owner * nu;
-            float* dst = recv + static_cast<size_t>((split * halves + half) * M) * nu + lu;
+            const int owner = u / nu, ou = u - owner * nu;
+            float* dst = recv + static_cast<size_t>((split * halves + half) * nu + ou) * rs;
             const uint32_t remote = owner == split ? 0u : peer_addr(dst, static_cast<uint32_t>(owner));
             for (int mb = 0; mb < M; mb += 32) {
                 float v[32];
                 acc32(mb, v);
-                if (owner == split) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (mb + j < M) dst[static_cast<size_t>(mb + j) * nu] = v[j];
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (mb + j < M) st_peer(remote + 4u * static_cast<uint32_t>((mb + j) * nu), v[j]);
+                for (int c = 0; c < 8; ++c) {
+                    if (mb + 4 * c >= M) break;
+                    if (owner == split)
+                        *reinterpret_cast<float4*>(dst + mb + 4 * c) =
+                            make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+                    else
+                        st_peer4(remote + 4u * static_cast<uint32_t>(mb + 4 * c), v[4 * c], v[4 * c + 1],
+                                 v[4 * c + 2], v[4 * c + 3]);
                 }
             }
         }
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         if (S > 1) cluster_barrier();  // every partial has landed in its owner's buffer
         else __syncthreads();
-        // this CTA's features: thread -> (feature lu, token rows m0, m0 + per, ...);
-        // each batch issues all its loads before any of its stores
-        const int per = kThreads / nu, lu = tid % nu, m0 = tid / nu;
-        const int col = split * nu + lu;
+        // this CTA's features; each batch issues all its loads (partials and residual rows) first
         if (a.gateup) {
-            constexpr int kBatch = 4;
+            constexpr int kBatch = S >= 4 ? 1 : 4 / S;
             const size_t ocol = static_cast<size_t>(tile) * 64 + col;
-            for (int mb = m0; mb < M; mb += per * kBatch) {
-                float g[kBatch][S], up[kBatch][S];
+            for (int qb = q0; qb < nq; qb += per * kBatch) {
+                float4 g[kBatch][S], up[kBatch][S];
 #pragma unroll
                 for (int j = 0; j < kBatch; ++j) {
-                    const int m = min(mb + j * per, M - 1);
+                    const int q = min(qb + j * per, nq - 1);
 #pragma unroll
                     for (int p = 0; p < S; ++p) {
-                        g[j][p] = recv[static_cast<size_t>((p * 2 + 0) * M + m) * nu + lu];
-                        up[j][p] = recv[static_cast<size_t>((p * 2 + 1) * M + m) * nu + lu];
+                        g[j][p] = *reinterpret_cast<const float4*>(recv + static_cast<size_t>((p * 2 + 0) * nu + lu) * rs + 4 * q);
+                        up[j][p] = *reinterpret_cast<const float4*>(recv + static_cast<size_t>((p * 2 + 1) * nu + lu) * rs + 4 * q);
                     }
                 }
 #pragma unroll
                 for (int j = 0; j < kBatch; ++j) {
-                    const int m = mb + j * per;
-                    if (m < M) {
+                    const int q = qb + j * per;
+                    if (q >= nq) break;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int m = 4 * q + i;
+                        if (m >= M) break;
                         float gs = 0.f, us = 0.f;
 #pragma unroll
                         for (int p = 0; p < S; ++p) {
-                            gs += g[j][p];
-                            us += up[j][p];
+                            gs += reinterpret_cast<const float*>(&g[j][p])[i];
+                            us += reinterpret_cast<const float*>(&up[j][p])[i];
                         }
                         const float o = silu(gs) * us;
                         const __half h = __float2half_rn(o);
@@ -281,27 +310,62 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
-        } else {
-            constexpr int kBatch = 8;
+        } else if constexpr (S >= 4) {
+            // residual rows already in registers: partials summed straight from shared memory
             float* yc = a.y + tile * kTileRows + col;
-            for (int mb = m0; mb < M; mb += per * kBatch) {
-                float part[kBatch][S], r[kBatch];
+#pragma unroll
+            for (int jj = 0; jj < kPreQ; ++jj) {
+                const int q = q0 + jj * per;
+                if (q >= nq) break;
+                float4 sum4 = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int p = 0; p < S; ++p) {
+                    const float4 v = *reinterpret_cast<const float4*>(recv + static_cast<size_t>(p * nu + lu) * rs + 4 * q);
+                    sum4.x += v.x;
+                    sum4.y += v.y;
+                    sum4.z += v.z;
+                    sum4.w += v.w;
+                }
+                const float sm[4] = {sum4.x, sum4.y, sum4.z, sum4.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int m = 4 * q + i;
+                    if (m >= M) break;
+                    yc[static_cast<size_t>(m) * a.ldy] =
+                        a.resid ? rpre[jj][i] + (a.rscale == 1.f ? sm[i] : sm[i] * a.rscale) : sm[i];
+                }
+            }
+        } else {
+            constexpr int kBatch = 4;
+            float* yc = a.y + tile * kTileRows + col;
+            for (int qb = q0; qb < nq; qb += per * kBatch) {
+                float4 part[kBatch][S];
+                float r[kBatch][4];
 #pragma unroll
                 for (int j = 0; j < kBatch; ++j) {
-                    const int m = mb + j * per;
-                    const int mc = min(m, M - 1);
+                    const int q = qb + j * per, qc = min(q, nq - 1);
 #pragma unroll
-                    for (int p = 0; p < S; ++p) part[j][p] = recv[static_cast<size_t>(p * M + mc) * nu + lu];
-                    r[j] = (a.resid && m < M) ? yc[static_cast<size_t>(m) * a.ldy] : 0.f;
+                    for (int p = 0; p < S; ++p)
+                        part[j][p] = *reinterpret_cast<const float4*>(recv + static_cast<size_t>(p * nu + lu) * rs + 4 * qc);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int m = 4 * q + i;
+                        r[j][i] = (a.resid && q < nq && m < M) ? yc[static_cast<size_t>(m) * a.ldy] : 0.f;
+                    }
                 }
 #pragma unroll
                 for (int j = 0; j < kBatch; ++j) {
-                    const int m = mb + j * per;
-                    if (m < M) {
-                        float s = 0.f;
+                    const int q = qb + j * per;
+                    if (q >= nq) break;
 #pragma unroll
-                        for (int p = 0; p < S; ++p) s += part[j][p];
-                        yc[static_cast<size_t>(m) * a.ldy] = a.resid ? r[j] + (a.rscale == 1.f ? s : s * a.rscale) : s;
+                    for (int i = 0; i < 4; ++i) {
+                        const int m = 4 * q + i;
+                        if (m >= M) break;
+                        float sum = 0.f;
+#pragma unroll
+                        for (int p = 0; p < S; ++p) sum += reinterpret_cast<const float*>(&part[j][p])[i];
+                        yc[static_cast<size_t>(m) * a.ldy] =
+                            a.resid ? r[j][i] + (a.rscale == 1.f ? sum : sum * a.rscale) : sum;
                     }
                 }
             }
