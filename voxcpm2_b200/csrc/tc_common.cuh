@@ -112,6 +112,45 @@ __device__ __forceinline__ uint32_t peer_addr(const void* local, uint32_t rank) 
 __device__ __forceinline__ void st_peer(uint32_t remote, float v) {  // fire and forget
     asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
 }
+// Four floats to a 16-byte aligned address in a cluster peer's shared memory, as an
+// asynchronous store that completes 16 bytes of transaction count on the peer's
+// mbarrier 'remote_bar' (both addresses from peer_addr): the peer learns of the data
+// by waiting on its own barrier, with no cluster-wide barrier.
+__device__ __forceinline__ void st_async4(uint32_t remote, float a, float b, float c, float d, uint32_t remote_bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                     remote),
+                 "f"(a), "f"(b), "f"(c), "f"(d), "r"(remote_bar)
+                 : "memory");
+}
+
+// Time-bounded wait (kWaitNs) for phase 'parity' of a local mbarrier whose
+// transactions come from other CTAs of the cluster: acquire at cluster scope.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
+    const uint32_t addr = smem_addr(bar);
+    uint64_t start = 0;
+    for (uint32_t i = 0;; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(addr), "r"(parity)
+            : "memory");
+        if (done) return true;
+        const uint64_t now = global_ns();
+        if (i == 0) start = now;
+        else if (now - start > kWaitNs) return false;
+    }
+}
+
+// The two halves of a cluster barrier, for a barrier whose wait can come long after
+// its arrival (relaxed: orders nothing by itself; see its callers).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+
 // four floats to a 16-byte aligned address in a cluster peer's shared memory
 __device__ __forceinline__ void st_peer4(uint32_t remote, float a, float b, float c, float d) {
     asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(remote), "f"(a), "f"(b), "f"(c), "f"(d)

@@ -76,6 +76,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                      const TcLinearArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ uint64_t full_bar[kMaxStages], empty_bar[kMaxStages], done_bar;
+    __shared__ uint64_t recv_bar;  // split-K: the peers' partials for this CTA have landed
     __shared__ uint32_t tmem_base_s;
     __shared__ int failed_s;
     __shared__ float inv_s[kLoOffset];
@@ -109,8 +110,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_init(&empty_bar[i], 1);
         }
         mbar_init(&done_bar, 1);
+        if (S > 1) mbar_init(&recv_bar, 1);
         failed_s = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        // the peers' partials: kTcThreads / S accumulator rows from each of the S - 1 peers,
+        // kLoOffset floats each
+        if (S > 1) mbar_expect_tx(&recv_bar, (S - 1) * (kTcThreads / S) * kLoOffset * 4);
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
         if (b_tma) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b)) : "memory");
 #pragma unroll
@@ -133,6 +138,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem_d = tmem_base_s;
+    // split-K: announce that this CTA's barriers are initialised (after thread 0's
+    // fence.mbarrier_init, ordered by the block barrier above); the matching wait comes
+    // right before the first push into a peer, long after every CTA has arrived
+    if (S > 1) cluster_arrive_relaxed();
     pdl_launch_dependents();
 
     // tensor-core issue: thread 32, one 128 x 48 x 16 MMA per 16 fp16 of K
@@ -295,6 +304,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         float* recv =
             reinterpret_cast<float*>(recv_in_stages ? smem : smem + static_cast<size_t>(stage_area) * kStageBytes);
         __syncthreads();  // the stage area is idle
+        if (S > 1) cluster_wait();   // every peer's receive barrier is initialised
         if (shared) cluster_sync();  // ... in every CTA of the cluster: partials may land in it
         {
             const int u = a.gateup ? (tid & 63) : tid, half = a.gateup ? (tid >> 6) : 0;
@@ -305,15 +315,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 for (int c = 0; c < kLoOffset / 4; ++c)
                     reinterpret_cast<float4*>(dst)[c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
             } else {
-                const uint32_t remote = peer_addr(dst, owner);
+                const uint32_t remote = peer_addr(dst, owner), rbar = peer_addr(&recv_bar, owner);
 #pragma unroll
                 for (int c = 0; c < kLoOffset / 4; ++c)
-                    st_peer4(remote + 16u * c, v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+                    st_async4(remote + 16u * c, v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3], rbar);
             }
         }
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        if (S > 1) cluster_sync();  // every partial has landed in its owner's buffer
-        else __syncthreads();
+        __syncthreads();  // this CTA's own partials are in place
+        // the peers' partials: every byte counted on the receive barrier. After the wait no
+        // peer writes into this CTA's shared memory again, so it may exit without a cluster
+        // barrier; its own asynchronous stores complete at peers that wait for them.
+        if (S > 1 && !mbar_wait_cluster(&recv_bar, 0)) failed_s = 1;
         // this CTA's units: thread -> (unit lu, token rows m0, m0 + per, ...); all of a
         // thread's partials are read before any result is stored
         // the stage area is idle now: squares of updated rows (behind the partials when those share it)
