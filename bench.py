@@ -83,9 +83,10 @@ def workload(streams_per_gpu: int, steps: int, warmup: int):
 
 # DRAM bytes (ncu dram__bytes_read.sum + dram__bytes_write.sum) of one launch of the
 # dominant kernel, the DiT gate/up tcgen05 linear, from a capture of that kernel on
-# its own (the command is in profiles/tc_linear_gateup_dit.md); the algorithmic bytes
-# of the launch are 17,268,736.
-GATEUP_DRAM_BYTES_PER_LAUNCH = 16944896.0
+# its own: ncu --set full --clock-control none -k regex:tc_linear_kernel -s 44 -c 4
+# python bench.py --range stream (the third of the four launches). The algorithmic
+# bytes of the launch are 17,268,736.
+GATEUP_DRAM_BYTES_PER_LAUNCH = 16948992.0
 
 
 def dit_patch_bytes(cfg) -> float:
