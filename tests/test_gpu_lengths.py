@@ -225,10 +225,14 @@ def test_full_utterance_until_stop(rt, bench):
             print(f"{what}: {nr} patches against the oracle's {own['patches']}: the decision at patch {k} has an "
                   f"oracle logit gap of {gaps[k]:.2e}")
         if "stop_logits" in run_:
+            # every decision the oracle takes with a margin above the loop's drift must agree;
+            # an ambiguous one (gap under 1e-2) may go either way, as between the oracle and its
+            # own one-ulp-perturbed run
             c = min(nr, own["patches"])
             dg = [bool(l[1] > l[0]) for l in run_["stop_logits"][:c]]
             dw = [bool(l[1] > l[0]) for l in own["stop_logits"][:c]]
-            assert dg[101:] == dw[101:], f"{what}: stop decisions differ"
+            for i in range(101, c):
+                assert dg[i] == dw[i] or abs(gaps[i]) < 1e-2, f"{what}: stop decision {i} differs (gap {gaps[i]:.2e})"
         follow, dis = oracle_following_fsq(orc, cfg, blobs, ids, run_, what)
         first_flip = min([p for p, *_ in dis], default=nr - 1)
         for i in range(first_flip + 1):  # the strict bar up to the first rounding difference

@@ -640,7 +640,6 @@ void dispatch_gemv_batch(const GemvArgs& a, const GemvBatch& b, cudaStream_t s, 
 }
 
 // ------------------------------------------------------------ attention ---
-constexpr int kAttnThreads = 128;       // the cluster-combined decode (4 warps per CTA)
 constexpr int kAttnSplitThreads = 256;  // the split-K decode: more warps per scheduler to hide latency
 constexpr int kMaxGroup = 16;
 
@@ -1005,10 +1004,26 @@ __device__ __forceinline__ void cluster_barrier() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// One cluster CTA: 8 warps, warp w owns query heads w and w + 8 of the KV group.
+// Its key range is walked in 32-key tiles staged in shared memory by cp.async (K
+// rows padded to 68 floats: a quarter-warp's 16-byte reads of 8 rows hit 32
+// distinct banks), two buffers so the next tile's copies are in flight while the
+// current one is scored.
+// Per tile and head, lane j scores key j, the online softmax runs across the lanes,
+// and lane l accumulates output columns 2l and 2l + 1 (P.V with the probabilities
+// broadcast by shuffles): no block barrier between the phases of a tile.
+constexpr int kClThreads = 256;
+constexpr int kClWarps = kClThreads / 32;
+constexpr int kClKeys = 32;
+constexpr int kClKRow = 68;
+
 template <typename KV, int D>
-__global__ void __launch_bounds__(kAttnThreads) attn_decode_cluster_kernel(const AttnArgs a0, const AttnBatch b) {
+__global__ void __launch_bounds__(kClThreads) attn_decode_cluster_kernel(const AttnArgs a0, const AttnBatch b) {
     static_assert(D == 64, "head_dim 64");
-    __shared__ AttnSmem S;
+    static_assert(sizeof(KV) == 4, "fp32 key/value rows");
+    __shared__ __align__(16) float ks[2][kClKeys][kClKRow];
+    __shared__ __align__(16) float vs[2][kClKeys][D];
+    __shared__ __align__(16) float qs[kMaxGroup][D];
     __shared__ float pacc[kMaxGroup][D], pm[kMaxGroup], pl[kMaxGroup];
     pdl_launch_dependents();
     AttnArgs a = a0;
@@ -1030,8 +1045,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_cluster_kernel(const
         kv_len = a.ctl->kv_len[a.which];
     }
     const int G = a.q_heads / a.kv_heads, C = kAttnCluster;
-    const int rank = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x;
-    stage_q<kAttnThreads>(a, S, kvh, G);
+    const int rank = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int i = tid; i < G * D; i += kClThreads) qs[i / D][i % D] = a.q[kvh * G * D + i] * a.scale;
     if (stop) return;
     int len0 = a.len0, len1 = a.len1;
     if (a.ctl) {
@@ -1042,17 +1057,92 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_cluster_kernel(const
     const int act = min(C, max(kAttnMinActive, (T + kKeyTile - 1) / kKeyTile));  // working CTAs
     const int chunk = (T + act - 1) / act, t0 = rank * chunk;
     const int n = rank < act ? max(0, min(T, t0 + chunk) - t0) : 0;
-    const int e = tid & (D - 1), gh = tid / D;
-    const int hg = (G + 1) / 2, g_lo = gh * hg, g_hi = min(G, g_lo + hg);
-    float acc[8];
-    attend_keys<KV, D, kAttnThreads>(a, S, kvh, G, t0, n, len0, acc);
-    __syncthreads();
+    const KV* k0 = static_cast<const KV*>(a.k0) + static_cast<size_t>(kvh) * a.stride0 * D;
+    const KV* v0 = static_cast<const KV*>(a.v0) + static_cast<size_t>(kvh) * a.stride0 * D;
+    const KV* k1 = a.k1 ? static_cast<const KV*>(a.k1) + static_cast<size_t>(kvh) * a.stride1 * D : nullptr;
+    const KV* v1 = a.v1 ? static_cast<const KV*>(a.v1) + static_cast<size_t>(kvh) * a.stride1 * D : nullptr;
+    // tile copies: 2 x 32 rows x 16 float4 over 256 threads, 4 cp.async each, one group
+    auto stage = [&](int buf, int tb) {
+        const int nt = min(kClKeys, n - tb);
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-        if (g_lo + j < g_hi) pacc[g_lo + j][e] = acc[j];
-    if (tid < G) {
-        pm[tid] = n > 0 ? S.m_s[tid] : -1e30f;
-        pl[tid] = S.l_s[tid];
+        for (int j = 0; j < 4; ++j) {
+            const int i = tid + j * kClThreads;  // 0 .. 1023
+            const int kv = i >> 9, r = (i >> 4) & 31, c = (i & 15) * 4;
+            if (r < nt) {
+                const int row = t0 + tb + r;
+                const KV* base = kv == 0 ? (row < len0 ? k0 : k1) : (row < len0 ? v0 : v1);
+                const KV* p = base + static_cast<size_t>(row < len0 ? row : row - len0) * D + c;
+                cp_async16(kv == 0 ? &ks[buf][r][c] : &vs[buf][r][c], p);
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    float m_run[2] = {-1e30f, -1e30f}, l_run[2] = {0.f, 0.f};
+    float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+    if (n > 0) stage(0, 0);
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();  // q rows and the first tile staged
+    for (int tb = 0, buf = 0; tb < n; tb += kClKeys, buf ^= 1) {
+        if (tb + kClKeys < n) stage(buf ^ 1, tb + kClKeys);  // the next tile's loads in flight
+        const int nt = min(kClKeys, n - tb);
+        float kr[D];  // lane j's key row
+        if (lane < nt) {
+#pragma unroll
+            for (int c = 0; c < D; c += 4) {
+                const float4 k4 = *reinterpret_cast<const float4*>(&ks[buf][lane][c]);
+                kr[c] = k4.x;
+                kr[c + 1] = k4.y;
+                kr[c + 2] = k4.z;
+                kr[c + 3] = k4.w;
+            }
+        }
+        const float mk = (a.mask && lane < nt) ? a.mask[t0 + tb + lane] : 0.f;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            const int g = warp + hh * kClWarps;
+            if (g >= G) break;
+            float x = -1e30f;
+            if (lane < nt) {
+                float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int c = 0; c < D; c += 4) {
+                    const float4 q4 = *reinterpret_cast<const float4*>(&qs[g][c]);
+                    s4[0] = fmaf(q4.x, kr[c], s4[0]);
+                    s4[1] = fmaf(q4.y, kr[c + 1], s4[1]);
+                    s4[2] = fmaf(q4.z, kr[c + 2], s4[2]);
+                    s4[3] = fmaf(q4.w, kr[c + 3], s4[3]);
+                }
+                x = ((s4[0] + s4[1]) + (s4[2] + s4[3])) + mk;
+            }
+            const float m_new = fmaxf(m_run[hh], warp_max(x));
+            const float p = lane < nt ? __expf(x - m_new) : 0.f;
+            const float alpha = __expf(m_run[hh] - m_new);
+            l_run[hh] = l_run[hh] * alpha + warp_sum(p);
+            m_run[hh] = m_new;
+            float o0 = acc[hh][0] * alpha, o1 = acc[hh][1] * alpha;
+            for (int j = 0; j < nt; ++j) {
+                const float pj = __shfl_sync(0xffffffffu, p, j);
+                const float2 v2 = *reinterpret_cast<const float2*>(&vs[buf][j][2 * lane]);
+                o0 = fmaf(pj, v2.x, o0);
+                o1 = fmaf(pj, v2.y, o1);
+            }
+            acc[hh][0] = o0;
+            acc[hh][1] = o1;
+        }
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        __syncthreads();  // this tile consumed, the next one staged
+    }
+    // this CTA's partial (max, sum, P.V) per head
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+        const int g = warp + hh * kClWarps;
+        if (g < G) {
+            *reinterpret_cast<float2*>(&pacc[g][2 * lane]) = make_float2(acc[hh][0], acc[hh][1]);
+            if (lane == 0) {
+                pm[g] = n > 0 ? m_run[hh] : -1e30f;
+                pl[g] = l_run[hh];
+            }
+        }
     }
     cluster_barrier();  // every CTA's partial is visible cluster-wide
     for (int g = rank; g < G; g += C) {
@@ -1094,7 +1184,7 @@ void launch_attn_decode_cluster_batch(const AttnArgs& a, const AttnBatch& b, cud
             throw std::invalid_argument("attention: key/value rows must start on 16-byte boundaries");
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(kAttnCluster, a.kv_heads, b.n > 0 ? b.n : 1);
-    cfg.blockDim = dim3(kAttnThreads);
+    cfg.blockDim = dim3(kClThreads);
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
