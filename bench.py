@@ -709,15 +709,11 @@ def run_ours(args):
 
     p50_single = lone_latency(one, W + min(K, 12))
 
-    # ---- the same for a stream tuned for one utterance at a time: ~296 CTAs per tensor-core
-    # launch and a 4-stage ring (the knobs are read when a stream is created)
-    LATENCY_TUNING = {"VXC_TC_TARGET": "296", "VXC_TC_STAGES": "4"}
-    os.environ.update(LATENCY_TUNING)
-    try:
-        solo = rt.Stream(dev, kv_capacity=max(cap, 512))
-    finally:
-        for k in LATENCY_TUNING:
-            os.environ.pop(k, None)
+    # ---- the same for a stream planned for one utterance at a time (vxc_stream_set_plan:
+    # ~296 CTAs per tensor-core launch and a 4-stage ring)
+    LATENCY_TUNING = {"plan": "VXC_PLAN_LATENCY", "ctas_per_linear": 296, "ring_stages": 4}
+    solo = rt.Stream(dev, kv_capacity=max(cap, 512))
+    solo.set_plan(rt.PLAN_LATENCY)
     p50_solo = lone_latency(solo, W + min(K, 12))
     solo_ms, solo_bytes = solo.profile_kernel("dit_gateup", 100)  # the dominant kernel at this tuning
     ev_ms, ev_bytes = solo.profile_kernel("dit_eval", 20)

@@ -154,6 +154,17 @@ VXC_API int32_t vxc_set_rope_factors(vxc_device* dev, const float* short_factor,
  * decoders (replaces HostDecoderKvCache, src/kvcache.h:18-40), scratch and graphs. */
 VXC_API int32_t vxc_stream_create(vxc_device* dev, int32_t kv_capacity, vxc_stream** out);
 VXC_API void vxc_stream_destroy(vxc_stream* s);
+/* How a stream's estimator linears spread over the GPU (no counterpart in the
+ * reference, which runs the estimator on the CPU). VXC_PLAN_THROUGHPUT, the default:
+ * ~32 CTAs and a 2-stage shared-memory ring per tcgen05 linear, the highest rate when
+ * many streams share the GPU. VXC_PLAN_LATENCY: ~296 CTAs and a 4-stage ring, the
+ * lowest per-patch latency for a stream that runs alone. The plans split the linears'
+ * K range differently, so latents differ in the last bits between them. Takes effect
+ * at the next patch (its graph is captured again); INVALID_STATE while a submitted
+ * patch has not been collected. */
+#define VXC_PLAN_THROUGHPUT 0
+#define VXC_PLAN_LATENCY 1
+VXC_API int32_t vxc_stream_set_plan(vxc_stream* s, int32_t plan);
 /* Empties both KV caches (a new HostDecoderKvCache pair, synthesizer.cpp:348-350). */
 VXC_API int32_t vxc_stream_reset(vxc_stream* s);
 /* Cancels the active vxc_generate at its next patch boundary (thread-safe;

@@ -56,6 +56,7 @@ def test_null_arguments_are_invalid_argument(rt):
     assert b"null" in rt.lib().vxc_last_error()
     assert rt.lib().vxc_stream_create(None, 16, C.byref(h)) == 1
     assert rt.lib().vxc_set_rope_factors(None, None, None, 32) == 1
+    assert rt.lib().vxc_stream_set_plan(None, 1) == 1
     # stream groups
     assert rt.lib().vxc_group_create(None, 2, 16, C.byref(h)) == 1
     assert rt.lib().vxc_group_stream(None, 0, C.byref(h)) == 1

@@ -106,6 +106,39 @@ def test_generate_bench_first_patches(rt, bench):
     s.close()
 
 
+def test_latency_plan_matches_oracle(rt, bench):
+    """vxc_stream_set_plan(VXC_PLAN_LATENCY) mid-utterance: the next patches run on ~296
+    CTAs per estimator linear with a 4-stage ring and still meet the bar against the
+    oracle; switching back is allowed; the plan cannot change with a patch in flight."""
+    cfg, blobs, dev, orc = bench
+    ids = synthetic.token_ids(cfg, 64, seed=1)
+    want = orc.generate(ids, min_patches=100, timesteps=10, cfg_value=2.0, max_patches_override=6, seed=0)
+    s = rt.Stream(dev, kv_capacity=512)
+    s.prefill(ids)
+    noise = oracle.noise_table(0, 6, cfg.latent)
+    lat = []
+    for step in range(6):
+        if step == 2:
+            s.set_plan(rt.PLAN_LATENCY)
+        if step == 4:
+            s.set_plan(rt.PLAN_THROUGHPUT)
+        x, stop = s.patch_step(noise[step], min_patches=100, step=step, cfg_value=2.0, timesteps=10)
+        lat.append(x)
+        assert not stop
+    for i in range(6):
+        err = float(np.abs(lat[i] - want["latents"][i]).max())
+        assert err <= 2e-2, f"patch {i}: max-abs {err:.3e}"
+    with pytest.raises(rt.VxcError) as e:
+        s.set_plan(7)
+    assert e.value.status == 1
+    s.patch_submit(noise[0], 100, 2.0, 10)
+    with pytest.raises(rt.VxcError) as e:
+        s.set_plan(rt.PLAN_LATENCY)  # a submitted patch is not collected yet
+    assert e.value.status == 2
+    s.patch_collect()
+    s.close()
+
+
 def test_patch_step_matches_generate(rt, tiny):
     cfg, blobs, dev, orc = tiny
     ids = synthetic.token_ids(cfg, 8, seed=2)

@@ -1916,6 +1916,21 @@ VXC_API void vxc_stream_cancel(vxc_stream* s) {
     if (s) s->cancel.store(true, std::memory_order_release);
 }
 
+VXC_API int32_t vxc_stream_set_plan(vxc_stream* s, int32_t plan) {
+    return guard([&] {
+        require(s != nullptr, "stream must not be null");
+        require(plan == VXC_PLAN_THROUGHPUT || plan == VXC_PLAN_LATENCY, "plan must be VXC_PLAN_THROUGHPUT or VXC_PLAN_LATENCY");
+        std::lock_guard<std::mutex> lk(s->call_mutex);
+        if (s->submitted != s->collected) throw InvalidState("collect the submitted patches before changing the plan");
+        DeviceGuard g(s->dev->device);
+        ck(cudaStreamSynchronize(s->cs), "cudaStreamSynchronize");
+        s->tc_target = plan == VXC_PLAN_LATENCY ? 296 : 32;
+        s->tc_stages = plan == VXC_PLAN_LATENCY ? 4 : 2;
+        if (s->graph) cudaGraphExecDestroy(s->graph);
+        s->graph = nullptr;  // the next patch captures its graph with the new plan
+    });
+}
+
 VXC_API int32_t vxc_stream_reset(vxc_stream* s) {
     return guard([&] {
         require(s != nullptr, "stream must not be null");

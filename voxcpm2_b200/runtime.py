@@ -25,6 +25,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libvoxcpm2_cuda.so"
 STATUS = {0: "OK", 1: "INVALID_ARGUMENT", 2: "INVALID_STATE", 3: "CANCELLED", 4: "OUT_OF_MEMORY",
           5: "RUNTIME_ERROR"}
 BASE, RESIDUAL = 0, 1
+PLAN_THROUGHPUT, PLAN_LATENCY = 0, 1  # vxc_stream_set_plan
 
 
 class VxcError(RuntimeError):
@@ -79,6 +80,7 @@ def _signatures():
         "vxc_stream_create": ([vp, i, C.POINTER(vp)], i),
         "vxc_stream_destroy": ([vp], None),
         "vxc_stream_reset": ([vp], i),
+        "vxc_stream_set_plan": ([vp, i], i),
         "vxc_stream_cancel": ([vp], None),
         "vxc_token_count": ([vp, i, C.POINTER(i)], i),
         "vxc_read_cache": ([vp, i, i, vp, vp], i),
@@ -224,6 +226,11 @@ class Stream:
             self.close()
         except Exception:  # interpreter shutdown: module globals may already be gone
             pass
+
+    def set_plan(self, plan: int) -> None:
+        """PLAN_THROUGHPUT (the default) or PLAN_LATENCY for a stream that runs alone;
+        takes effect at the next patch."""
+        _check(lib().vxc_stream_set_plan(self._h, plan))
 
     # -- KV cache runner ---------------------------------------------------
     def reset(self) -> None:
