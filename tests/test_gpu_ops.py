@@ -194,6 +194,32 @@ def test_decoder_prefill_then_decode(rt, models, name, which):
     s.close()
 
 
+@pytest.mark.parametrize("name,which", [("small", 0), ("small", 1)])
+def test_decoder_decode_past_512_keys(rt, models, name, which):
+    """One-row steps over 900-1000 cached keys: the decode attention's CTAs walk
+    several 32-key tiles each (the double-buffered path), against the oracle."""
+    cfg, blobs, dev, orc = models(name)
+    s = rt.Stream(dev, kv_capacity=1100)
+    rng = np.random.default_rng(31 + which)
+    pre = rng.standard_normal((900, cfg.hidden), dtype=np.float32) * 0.5
+    orc.reset()
+    orc.decoder_forward(which, pre)
+    s.decoder_step(which, pre)
+    for step in range(3):
+        x = rng.standard_normal((1, cfg.hidden), dtype=np.float32)
+        want = orc.decoder_forward(which, x)
+        got = s.decoder_step(which, x)
+        assert_parity(got, want, 2e-2, 0.999, f"{name} decode step {step} over {901 + step} keys")
+    # and a jump to 1000 keys
+    grow = rng.standard_normal((96, cfg.hidden), dtype=np.float32) * 0.5
+    orc.decoder_forward(which, grow)
+    s.decoder_step(which, grow)
+    x = rng.standard_normal((1, cfg.hidden), dtype=np.float32)
+    assert_parity(s.decoder_step(which, x), orc.decoder_forward(which, x), 2e-2, 0.999, f"{name} step at 1000 keys")
+    assert s.token_count(which) == 1000
+    s.close()
+
+
 @pytest.mark.parametrize("name,which,n", [("tiny", 0, 128), ("tiny", 1, 129), ("small", 0, 200), ("bench", 0, 200)])
 def test_decoder_prefill_row_blocks(rt, models, name, which, n):
     """Prefill longer than one 128-row block of the tensor-core linears (full block,
