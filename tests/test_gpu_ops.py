@@ -194,6 +194,23 @@ def test_decoder_prefill_then_decode(rt, models, name, which):
     s.close()
 
 
+@pytest.mark.parametrize("which", [0, 1])
+def test_decoder_steps_bulk_copy_gemv(rt, models, which, monkeypatch):
+    """A lone stream's decoder GEMVs in the bulk-copy form (VXC_BULK_GEMV=1: weight rows
+    into shared memory before the dependency wait, one member slot) against the oracle."""
+    monkeypatch.setenv("VXC_BULK_GEMV", "1")
+    cfg, blobs, dev, orc = models("bench")
+    s = rt.Stream(dev, kv_capacity=64)
+    rng = np.random.default_rng(57 + which)
+    pre = rng.standard_normal((9, cfg.hidden), dtype=np.float32)
+    orc.reset()
+    assert_parity(s.decoder_step(which, pre), orc.decoder_forward(which, pre), 2e-2, 0.999, "bulk prefill")
+    for step in range(3):
+        x = rng.standard_normal((1, cfg.hidden), dtype=np.float32)
+        assert_parity(s.decoder_step(which, x), orc.decoder_forward(which, x), 2e-2, 0.999, f"bulk step {step}")
+    s.close()
+
+
 @pytest.mark.parametrize("name,which", [("small", 0), ("small", 1)])
 def test_decoder_decode_past_512_keys(rt, models, name, which):
     """One-row steps over 900-1000 cached keys: the decode attention's CTAs walk

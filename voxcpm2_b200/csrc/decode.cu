@@ -422,10 +422,9 @@ constexpr int bulk_rows() {
 }
 
 // Output units [blockIdx.x * upb, + upb) of a.rows for the b.n members; IN_PLAIN input only.
-template <int MODE>
+template <int MODE, int NB>
 __global__ void __launch_bounds__(kBulkThreads) gemv_bulk_kernel(const GemvArgs a, const GemvBatch b, int upb) {
     constexpr int R = bulk_rows<MODE>();
-    constexpr int NB = kGemvBatch;
     extern __shared__ __align__(16) uint8_t bulk_sm[];
     __shared__ uint64_t bar;
     __shared__ float red[NB][kBulkWarps];
@@ -609,7 +608,9 @@ void dispatch_gemv_bulk(const GemvArgs& a, const GemvBatch& b, cudaStream_t s, b
     const int blocks = (a.rows + upb - 1) / upb;
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = make_cfg(dim3(blocks), dim3(kBulkThreads), smem, s, pdl, attr);
-    check_launch(cudaLaunchKernelEx(&cfg, gemv_bulk_kernel<MODE>, a, b, upb));
+    // a lone stream's launch unrolls one member slot (fewer registers), a group's all of them
+    if (b.n == 1) check_launch(cudaLaunchKernelEx(&cfg, gemv_bulk_kernel<MODE, 1>, a, b, upb));
+    else check_launch(cudaLaunchKernelEx(&cfg, gemv_bulk_kernel<MODE, kGemvBatch>, a, b, upb));
 }
 
 // NB: the member slots a launch unrolls (4 for groups of up to 4, else 8); W: warps per
@@ -1249,10 +1250,14 @@ void init_kernel_attributes() {
     set_gemv_batch_attributes<GEMV_QKV, 2>();
     check_launch(cudaFuncSetAttribute(attn_decode_kernel<__half, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax));
     check_launch(cudaFuncSetAttribute(attn_decode_kernel<float, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax));
-    for (const void* f : {reinterpret_cast<const void*>(gemv_bulk_kernel<GEMV_PLAIN>),
-                          reinterpret_cast<const void*>(gemv_bulk_kernel<GEMV_RESID>),
-                          reinterpret_cast<const void*>(gemv_bulk_kernel<GEMV_GATEUP>),
-                          reinterpret_cast<const void*>(gemv_bulk_kernel<GEMV_QKV>)})
+    for (const void* f : {reinterpret_cast<const void*>(gemv_bulk_kernel<GEMV_PLAIN, 1>),
+                          reinterpret_cast<const void*>(gemv_bulk_kernel<GEMV_RESID, 1>),
+                          reinterpret_cast<const void*>(gemv_bulk_kernel<GEMV_GATEUP, 1>),
+                          reinterpret_cast<const void*>(gemv_bulk_kernel<GEMV_QKV, 1>),
+                          reinterpret_cast<const void*>(gemv_bulk_kernel<GEMV_PLAIN, kGemvBatch>),
+                          reinterpret_cast<const void*>(gemv_bulk_kernel<GEMV_RESID, kGemvBatch>),
+                          reinterpret_cast<const void*>(gemv_bulk_kernel<GEMV_GATEUP, kGemvBatch>),
+                          reinterpret_cast<const void*>(gemv_bulk_kernel<GEMV_QKV, kGemvBatch>)})
         check_launch(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kBulkSmemMax)));
     check_launch(cudaFuncSetAttribute(attn_decode_cluster_kernel<float, 64>,
                                       cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
