@@ -710,8 +710,8 @@ def run_ours(args):
     p50_single = lone_latency(one, W + min(K, 12))
 
     # ---- the same for a stream planned for one utterance at a time (vxc_stream_set_plan:
-    # ~296 CTAs per tensor-core launch and a 4-stage ring)
-    LATENCY_TUNING = {"plan": "VXC_PLAN_LATENCY", "ctas_per_linear": 296, "ring_stages": 4}
+    # ~296 CTAs per tensor-core launch and a 3-stage ring)
+    LATENCY_TUNING = {"plan": "VXC_PLAN_LATENCY", "ctas_per_linear": 296, "ring_stages": 3}
     solo = rt.Stream(dev, kv_capacity=max(cap, 512))
     solo.set_plan(rt.PLAN_LATENCY)
     p50_solo = lone_latency(solo, W + min(K, 12))

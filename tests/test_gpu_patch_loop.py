@@ -108,7 +108,7 @@ def test_generate_bench_first_patches(rt, bench):
 
 def test_latency_plan_matches_oracle(rt, bench):
     """vxc_stream_set_plan(VXC_PLAN_LATENCY) mid-utterance: the next patches run on ~296
-    CTAs per estimator linear with a 4-stage ring and still meet the bar against the
+    CTAs per estimator linear with a 3-stage ring and still meet the bar against the
     oracle; switching back is allowed; the plan cannot change with a patch in flight."""
     cfg, blobs, dev, orc = bench
     ids = synthetic.token_ids(cfg, 64, seed=1)

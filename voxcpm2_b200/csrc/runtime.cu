@@ -1925,7 +1925,7 @@ VXC_API int32_t vxc_stream_set_plan(vxc_stream* s, int32_t plan) {
         DeviceGuard g(s->dev->device);
         ck(cudaStreamSynchronize(s->cs), "cudaStreamSynchronize");
         s->tc_target = plan == VXC_PLAN_LATENCY ? 296 : 32;
-        s->tc_stages = plan == VXC_PLAN_LATENCY ? 4 : 2;
+        s->tc_stages = plan == VXC_PLAN_LATENCY ? 3 : 2;
         if (s->graph) cudaGraphExecDestroy(s->graph);
         s->graph = nullptr;  // the next patch captures its graph with the new plan
     });
