@@ -15,6 +15,7 @@
 #include <stdexcept>
 
 #include "kernels.cuh"
+#include "tc_common.cuh"
 
 namespace vxc {
 namespace {
@@ -1025,8 +1026,14 @@ __global__ void __launch_bounds__(kClThreads) attn_decode_cluster_kernel(const A
     __shared__ __align__(16) float ks[2][kClKeys][kClKRow];
     __shared__ __align__(16) float vs[2][kClKeys][D];
     __shared__ __align__(16) float qs[kMaxGroup][D];
-    __shared__ float pacc[kMaxGroup][D], pm[kMaxGroup], pl[kMaxGroup];
+    // combiner of head g = rank: every working CTA's (P.V, max, sum) for it, 66 floats each
+    __shared__ __align__(16) float rbuf[kAttnCluster][D + 2];
+    __shared__ uint64_t rbar;
     pdl_launch_dependents();
+    if (threadIdx.x == 0) {
+        tc::mbar_init(&rbar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
     AttnArgs a = a0;
     if (b.n > 0) {  // member blockIdx.z of a group (a cluster spans x only: one member per cluster)
         const int m = blockIdx.z;
@@ -1058,6 +1065,13 @@ __global__ void __launch_bounds__(kClThreads) attn_decode_cluster_kernel(const A
     const int act = min(C, max(kAttnMinActive, (T + kKeyTile - 1) / kKeyTile));  // working CTAs
     const int chunk = (T + act - 1) / act, t0 = rank * chunk;
     const int n = rank < act ? max(0, min(T, t0 + chunk) - t0) : 0;
+    // The combiner of head g (CTA g, g < G) expects act partials of 264 bytes. The
+    // cluster-barrier arrival (release) orders this CTA's barrier set-up before any peer's
+    // push, which waits for every arrival; the wait comes after the key tiles.
+    constexpr uint32_t kPartBytes = (D + 2) * 4;
+    __syncthreads();  // thread 0's barrier initialisation is done
+    if (rank < G && tid == 0) tc::mbar_expect_tx(&rbar, static_cast<uint32_t>(act) * kPartBytes);
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
     const KV* k0 = static_cast<const KV*>(a.k0) + static_cast<size_t>(kvh) * a.stride0 * D;
     const KV* v0 = static_cast<const KV*>(a.v0) + static_cast<size_t>(kvh) * a.stride0 * D;
     const KV* k1 = a.k1 ? static_cast<const KV*>(a.k1) + static_cast<size_t>(kvh) * a.stride1 * D : nullptr;
@@ -1133,27 +1147,35 @@ __global__ void __launch_bounds__(kClThreads) attn_decode_cluster_kernel(const A
         asm volatile("cp.async.wait_group 0;" ::: "memory");
         __syncthreads();  // this tile consumed, the next one staged
     }
-    // this CTA's partial (max, sum, P.V) per head
+    // Combine: CTA g (g < G) combines head g. Every working CTA (rank < act) sends its
+    // (P.V, max, sum) for head g into CTA g's rbuf[rank] as asynchronous 8-byte stores that
+    // complete on CTA g's barrier; a combiner waits for its own bytes only, and no CTA reads
+    // another's shared memory, so none waits for the others before it exits.
+    tc::cluster_wait();  // every CTA's receive barrier is set up
+    if (rank < act) {
 #pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-        const int g = warp + hh * kClWarps;
-        if (g < G) {
-            *reinterpret_cast<float2*>(&pacc[g][2 * lane]) = make_float2(acc[hh][0], acc[hh][1]);
-            if (lane == 0) {
-                pm[g] = n > 0 ? m_run[hh] : -1e30f;
-                pl[g] = l_run[hh];
+        for (int hh = 0; hh < 2; ++hh) {
+            const int g = warp + hh * kClWarps;
+            if (g < G) {
+                float* dst = &rbuf[rank][0];
+                const uint32_t base = tc::peer_addr(dst, static_cast<uint32_t>(g));
+                const uint32_t bar = tc::peer_addr(&rbar, static_cast<uint32_t>(g));
+                tc::st_async2(base + 8u * lane, acc[hh][0], acc[hh][1], bar);
+                if (lane == 0) tc::st_async2(base + 4u * D, n > 0 ? m_run[hh] : -1e30f, l_run[hh], bar);
             }
         }
     }
-    cluster_barrier();  // every CTA's partial is visible cluster-wide
-    for (int g = rank; g < G; g += C) {
-        if (tid < D) {
+    if (rank < G) {
+        const bool got = tc::mbar_wait_cluster(&rbar, 0);
+        if (!got && tid == 0 && a.ctl) a.ctl->error = 3;
+        if (got && tid < D) {
+            const int g = rank;
             float mr[kAttnCluster], lr[kAttnCluster], ar[kAttnCluster];
 #pragma unroll
             for (int r = 0; r < kAttnCluster; ++r) {  // ranks past 'act' hold no keys: weight 0
-                mr[r] = r < act ? ld_peer(&pm[g], r) : -1e30f;
-                lr[r] = r < act ? ld_peer(&pl[g], r) : 0.f;
-                ar[r] = r < act ? ld_peer(&pacc[g][tid], r) : 0.f;
+                mr[r] = r < act ? rbuf[r][D] : -1e30f;
+                lr[r] = r < act ? rbuf[r][D + 1] : 0.f;
+                ar[r] = r < act ? rbuf[r][tid] : 0.f;
             }
             float M = -1e30f;
 #pragma unroll
@@ -1168,7 +1190,6 @@ __global__ void __launch_bounds__(kClThreads) attn_decode_cluster_kernel(const A
             a.out[(kvh * G + g) * D + tid] = num / den;
         }
     }
-    cluster_barrier();  // no CTA leaves while another still reads its shared memory
 }
 
 void launch_attn_decode_cluster_batch(const AttnArgs& a, const AttnBatch& b, cudaStream_t s, bool pdl) {

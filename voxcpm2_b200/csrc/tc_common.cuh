@@ -123,6 +123,13 @@ __device__ __forceinline__ void st_async4(uint32_t remote, float a, float b, flo
                  : "memory");
 }
 
+// Two floats, the same way (an 8-byte aligned address; 8 bytes of transaction count).
+__device__ __forceinline__ void st_async2(uint32_t remote, float a, float b, uint32_t remote_bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(remote),
+                 "f"(a), "f"(b), "r"(remote_bar)
+                 : "memory");
+}
+
 // Time-bounded wait (kWaitNs) for phase 'parity' of a local mbarrier whose
 // transactions come from other CTAs of the cluster: acquire at cluster scope.
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
