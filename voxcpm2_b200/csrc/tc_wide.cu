@@ -71,6 +71,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const TcWideArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ uint64_t full_bar[kMaxRing], empty_bar[kMaxRing], done_bar;
+    __shared__ uint64_t recv_bar;  // split-K: the peers' partials for this CTA have landed
     __shared__ uint32_t tmem_base_s;
     __shared__ int failed_s;
 
@@ -97,8 +98,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&empty_bar[i], 1);
         }
         mbar_init(&done_bar, 1);
+        if (S > 1) mbar_init(&recv_bar, 1);
         failed_s = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        // the peers' partials: kThreads / S accumulator rows from each of the S - 1 peers,
+        // ceil(M / 4) 16-byte stores each
+        if (S > 1) mbar_expect_tx(&recv_bar, (S - 1) * (kThreads / S) * 16 * ((M + 3) / 4));
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b)) : "memory");
 #pragma unroll
@@ -122,6 +127,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = tmem_base_s;
+    // split-K: this CTA's receive barrier is set up (thread 0's init and expect_tx, ordered by
+    // the block barrier above); the matching wait comes right before the first push
+    if (S > 1) asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
     pdl_launch_dependents();
 
     if (tid == 0) {
@@ -250,12 +258,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         // banks modulo 32: each quarter-warp phase touches all 32 banks once).
         const int rs = recv_stride(lo);
         float* recv = reinterpret_cast<float*>(local_recv ? smem : smem + static_cast<size_t>(stage_area) * kstage);
+        if (S > 1) cluster_wait();           // every peer's receive barrier is set up
         if (shared_recv) cluster_barrier();  // every CTA's loads have landed: the stage areas are free
         {
             const int u = a.gateup ? (tid & 63) : tid, half = a.gateup ? (tid >> 6) : 0;
             const int owner = u / nu, ou = u - owner * nu;
             float* dst = recv + static_cast<size_t>((split * halves + half) * nu + ou) * rs;
             const uint32_t remote = owner == split ? 0u : peer_addr(dst, static_cast<uint32_t>(owner));
+            const uint32_t rbar = owner == split ? 0u : peer_addr(&recv_bar, static_cast<uint32_t>(owner));
             for (int mb = 0; mb < M; mb += 32) {
                 float v[32];
                 acc32(mb, v);
@@ -266,14 +276,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                         *reinterpret_cast<float4*>(dst + mb + 4 * c) =
                             make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
                     else
-                        st_peer4(remote + 4u * static_cast<uint32_t>(mb + 4 * c), v[4 * c], v[4 * c + 1],
-                                 v[4 * c + 2], v[4 * c + 3]);
+                        st_async4(remote + 4u * static_cast<uint32_t>(mb + 4 * c), v[4 * c], v[4 * c + 1],
+                                  v[4 * c + 2], v[4 * c + 3], rbar);
                 }
             }
         }
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        if (S > 1) cluster_barrier();  // every partial has landed in its owner's buffer
-        else __syncthreads();
+        __syncthreads();  // this CTA's own partials are in place
+        // the peers' partials: every byte counted on the receive barrier; after the wait no peer
+        // writes into this CTA's shared memory again, so it may exit without a cluster barrier
+        if (S > 1 && !mbar_wait_cluster(&recv_bar, 0)) failed_s = 1;
         // this CTA's features; each batch issues all its loads (partials and residual rows) first
         if (a.gateup) {
             constexpr int kBatch = S >= 4 ? 1 : 4 / S;
