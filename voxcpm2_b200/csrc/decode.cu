@@ -981,30 +981,15 @@ void launch_gemv(const GemvArgs& a, cudaStream_t s, bool pdl) {
 }
 
 // The same decode with the split-K combine inside a thread-block cluster: the
-// cluster's CTAs take one contiguous key range each, publish (max, sum, P.V) in
-// their own shared memory, and after one cluster barrier CTA r combines heads
-// g = r, r + C, ... reading the others' partials through distributed shared
-// memory. A second barrier keeps every CTA's shared memory alive until the
-// readers are done. No global scratch, no atomics.
+// cluster's CTAs take one contiguous key range each and send their (P.V, max, sum)
+// for head g into CTA g's shared memory as asynchronous stores counted on CTA g's
+// mbarrier; CTA g combines head g in rank order. No global scratch, no atomics, no
+// remote loads.
 // The cluster has 16 CTAs (a non-portable size); the key range is spread over
 // max(8, ceil(T / 32)) of them, so up to 512 keys every working CTA walks one
-// 32-key tile, and short rows do not pay for a 16-way combine's idle ranks beyond
-// their barriers.
+// 32-key tile, and short rows do not pay for a 16-way combine.
 constexpr int kAttnCluster = 16;
 constexpr int kAttnMinActive = 8;
-
-__device__ __forceinline__ float ld_peer(const float* local, uint32_t rank) {
-    uint32_t addr;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
-                 : "=r"(addr)
-                 : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(local))), "r"(rank));
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-    return v;
-}
-__device__ __forceinline__ void cluster_barrier() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
 
 // One cluster CTA: 8 warps, warp w owns query heads w and w + 8 of the KV group.
 // Its key range is walked in 32-key tiles staged in shared memory by cp.async (K
