@@ -347,8 +347,15 @@ struct TcRowsArgs {
     int ldyb = 0;
     int stages = 4;            // shared-memory ring depth (1..4)
     StreamCtl* ctl = nullptr;  // receives error 3 if a bounded wait gave up
+    // K split over 'splits' CTAs per output tile: each writes its fp32 partial tile into
+    // part [splits][M][rows] (gate/up: [splits][M][2 rows], the gate then the up features)
+    // and a second kernel sums the partials in order and applies the epilogue
+    int splits = 1;
+    float* part = nullptr;
 };
 void launch_tc_rows(const CUtensorMap& map_a, const CUtensorMap& map_b, const TcRowsArgs& a, cudaStream_t s);
+// K split of a prefill linear: about 128 CTAs per launch, at most 8 per output tile.
+int tc_rows_splits(int rows, int gateup, int K);
 void init_tc_rows_attributes();
 
 // Wide-token tcgen05 linear (the DiT of a group of streams): Y[m][r] for

@@ -383,6 +383,7 @@ struct vxc_stream {
     // row-block split-fp16 operands of the prefill's tcgen05 linears ([2 * kRowBlock][K]) and their maps
     __half *xr_n = nullptr, *xr_a = nullptr, *xr_act = nullptr;
     CUtensorMap map_xr_n{}, map_xr_a{}, map_xr_act{};
+    float* xr_part = nullptr;  // K-split partial tiles of the prefill linears
     int32_t* pids = nullptr;
 
     // host mirror
@@ -447,6 +448,7 @@ void free_all(vxc_stream* s) {
     if (s->dssq) cudaFree(s->dssq);
     for (__half* p : {s->xr_n, s->xr_a, s->xr_act})
         if (p) cudaFree(p);
+    if (s->xr_part) cudaFree(s->xr_part);
     if (s->dcount) cudaFree(s->dcount);
     if (s->ctl_host) cudaFreeHost(s->ctl_host);
     if (s->pin) cudaFreeHost(s->pin);
@@ -973,6 +975,13 @@ void ensure_prefill_rows(vxc_stream* s, int n) {
         s->map_xr_n = make_tensor_map_f16(s->xr_n, 2 * kRowBlock, static_cast<int>(H), 2 * kRowBlock);
         s->map_xr_a = make_tensor_map_f16(s->xr_a, 2 * kRowBlock, static_cast<int>(Q), 2 * kRowBlock);
         s->map_xr_act = make_tensor_map_f16(s->xr_act, 2 * kRowBlock, static_cast<int>(F), 2 * kRowBlock);
+        // the largest split partial buffer of the four linears: splits x kRowBlock x outputs
+        const int Hi = static_cast<int>(H), Fi = static_cast<int>(F), Wi = static_cast<int>(W), Qi = static_cast<int>(Q);
+        const size_t part = std::max({static_cast<size_t>(tc_rows_splits(Wi, 0, Hi)) * Wi,
+                                      static_cast<size_t>(tc_rows_splits(Hi, 0, Qi)) * Hi,
+                                      static_cast<size_t>(tc_rows_splits(Fi, 1, Hi)) * 2 * Fi,
+                                      static_cast<size_t>(tc_rows_splits(Hi, 0, Fi)) * Hi}) * kRowBlock;
+        s->xr_part = dev_alloc<float>(part);
     }
 }
 
@@ -1008,6 +1017,8 @@ void run_decoder_rows(vxc_stream* s, int which, int n, float* out_dev) {
             qa.y = s->pqkv + static_cast<size_t>(r0) * W;
             qa.ldy = W;
             qa.ctl = s->ctl;
+            qa.splits = tc_rows_splits(qa.rows, 0, qa.K);
+            qa.part = s->xr_part;
             launch_tc_rows(maps[l][0], s->map_xr_n, qa, s->cs);
         }
         launch_qkv_rows_post(s->pqkv, n, hq, hkv, hd, past, 1 << 30, which == 0 ? rope_c : nullptr,
@@ -1029,6 +1040,8 @@ void run_decoder_rows(vxc_stream* s, int which, int n, float* out_dev) {
             oa.y = hb;
             oa.ldy = H;
             oa.ctl = s->ctl;
+            oa.splits = tc_rows_splits(oa.rows, 0, oa.K);
+            oa.part = s->xr_part;
             launch_tc_rows(maps[l][1], s->map_xr_a, oa, s->cs);
             launch_rmsnorm_rows_split(hb, H, L.post_norm, d.rms_eps, H, mb, s->xr_n, nullptr, s->cs, false, kRowBlock);
             TcRowsArgs ga;
@@ -1039,6 +1052,8 @@ void run_decoder_rows(vxc_stream* s, int which, int n, float* out_dev) {
             ga.yb = s->xr_act;
             ga.ldyb = F;
             ga.ctl = s->ctl;
+            ga.splits = tc_rows_splits(ga.rows, 1, ga.K);
+            ga.part = s->xr_part;
             launch_tc_rows(maps[l][2], s->map_xr_n, ga, s->cs);
             TcRowsArgs da;
             da.K = F;
@@ -1049,6 +1064,8 @@ void run_decoder_rows(vxc_stream* s, int which, int n, float* out_dev) {
             da.y = hb;
             da.ldy = H;
             da.ctl = s->ctl;
+            da.splits = tc_rows_splits(da.rows, 0, da.K);
+            da.part = s->xr_part;
             launch_tc_rows(maps[l][3], s->map_xr_act, da, s->cs);
         }
     }
