@@ -250,6 +250,127 @@ __global__ void attn_rows_kernel(const float* qkv, int q_heads, int kv_heads, in
     }
 }
 
+// Prefill attention over the cached keys (the rows' own K/V already appended by
+// qkv_rows_post): query row m sees keys 0 .. past + m (causal, kvcache.cpp:216-230).
+// One CTA per (KV head, block of rb query rows): its rb x G query vectors (at most
+// 32) spread over 8 warps. Keys are walked in 32-key tiles staged by cp.async into
+// two buffers; lane j holds key j's row in registers and scores it against each of
+// its warp's vectors; each vector keeps an online softmax (running max and sum) and
+// two output columns per lane, the probabilities broadcast by shuffles.
+constexpr int kPfThreads = 256, kPfWarps = 8, kPfVectors = 32, kPfPer = kPfVectors / kPfWarps, kPfMaxGroup = 16;
+constexpr int kPfKeys = 32, kPfKRow = 68;
+
+__device__ __forceinline__ void pf_cp_async16(void* smem_dst, const void* gsrc) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(
+                     smem_dst))),
+                 "l"(gsrc)
+                 : "memory");
+}
+
+__global__ void __launch_bounds__(kPfThreads) attn_prefill_kernel(const float* qkv, int M, int q_heads, int kv_heads,
+                                                                 int past, const float* k_cache, const float* v_cache,
+                                                                 int cap, float scale, float* out, int rb) {
+    constexpr int D = 64;
+    __shared__ __align__(16) float ks[2][kPfKeys][kPfKRow];
+    __shared__ __align__(16) float vs[2][kPfKeys][D];
+    __shared__ __align__(16) float qs[kPfVectors][D];
+    const int kvh = blockIdx.x, r0 = blockIdx.y * rb, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int G = q_heads / kv_heads, nv = min(rb, M - r0) * G;  // this CTA's query vectors: v -> (row v / G, head v % G)
+    const int width = (q_heads + 2 * kv_heads) * D;
+    for (int i = tid; i < nv * D; i += kPfThreads) {
+        const int v = i / D, e = i - v * D;
+        const int m = r0 + v / G, hh = kvh * G + v % G;
+        qs[v][e] = qkv[static_cast<size_t>(m) * width + hh * D + e] * scale;
+    }
+    const int T = past + min(M, r0 + rb);  // keys of the block's last row
+    const float* kb = k_cache + static_cast<size_t>(kvh) * cap * D;
+    const float* vb = v_cache + static_cast<size_t>(kvh) * cap * D;
+    auto stage = [&](int buf, int tb) {
+        const int nt = min(kPfKeys, T - tb);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int i = tid + j * kPfThreads;  // 0 .. 1023
+            const int kv = i >> 9, r = (i >> 4) & 31, c = (i & 15) * 4;
+            if (r < nt) {
+                const float* src = (kv == 0 ? kb : vb) + static_cast<size_t>(tb + r) * D + c;
+                pf_cp_async16(kv == 0 ? &ks[buf][r][c] : &vs[buf][r][c], src);
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    float m_run[kPfPer], l_run[kPfPer], acc[kPfPer][2];
+#pragma unroll
+    for (int i = 0; i < kPfPer; ++i) {
+        m_run[i] = -1e30f;
+        l_run[i] = 0.f;
+        acc[i][0] = acc[i][1] = 0.f;
+    }
+    stage(0, 0);
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();  // query vectors and the first tile staged
+    for (int tb = 0, buf = 0; tb < T; tb += kPfKeys, buf ^= 1) {
+        if (tb + kPfKeys < T) stage(buf ^ 1, tb + kPfKeys);
+        const int nt = min(kPfKeys, T - tb);
+        float kr[D];
+        if (lane < nt) {
+#pragma unroll
+            for (int c = 0; c < D; c += 4) {
+                const float4 k4 = *reinterpret_cast<const float4*>(&ks[buf][lane][c]);
+                kr[c] = k4.x;
+                kr[c + 1] = k4.y;
+                kr[c + 2] = k4.z;
+                kr[c + 3] = k4.w;
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < kPfPer; ++i) {
+            const int v = warp + i * kPfWarps;
+            if (v >= nv) break;
+            const int lim = past + r0 + v / G;  // the last key this row sees
+            if (tb > lim) continue;             // (warp-uniform) a fully masked tile
+            float x = -1e30f;
+            if (lane < nt && tb + lane <= lim) {
+                float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int c = 0; c < D; c += 4) {
+                    const float4 q4 = *reinterpret_cast<const float4*>(&qs[v][c]);
+                    s4[0] = fmaf(q4.x, kr[c], s4[0]);
+                    s4[1] = fmaf(q4.y, kr[c + 1], s4[1]);
+                    s4[2] = fmaf(q4.z, kr[c + 2], s4[2]);
+                    s4[3] = fmaf(q4.w, kr[c + 3], s4[3]);
+                }
+                x = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+            }
+            const float m_new = fmaxf(m_run[i], warp_max(x));
+            const float p = x > -1e29f ? __expf(x - m_new) : 0.f;
+            const float alpha = __expf(m_run[i] - m_new);
+            l_run[i] = l_run[i] * alpha + warp_sum(p);
+            m_run[i] = m_new;
+            float o0 = acc[i][0] * alpha, o1 = acc[i][1] * alpha;
+            const int nk = min(nt, lim - tb + 1);
+            for (int j = 0; j < nk; ++j) {
+                const float pj = __shfl_sync(0xffffffffu, p, j);
+                const float2 v2 = *reinterpret_cast<const float2*>(&vs[buf][j][2 * lane]);
+                o0 = fmaf(pj, v2.x, o0);
+                o1 = fmaf(pj, v2.y, o1);
+            }
+            acc[i][0] = o0;
+            acc[i][1] = o1;
+        }
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        __syncthreads();  // this tile consumed, the next one staged
+    }
+#pragma unroll
+    for (int i = 0; i < kPfPer; ++i) {
+        const int v = warp + i * kPfWarps;
+        if (v >= nv) break;
+        const int m = r0 + v / G, hh = kvh * G + v % G;
+        const float inv = 1.f / l_run[i];
+        *reinterpret_cast<float2*>(out + static_cast<size_t>(m) * q_heads * D + hh * D + 2 * lane) =
+            make_float2(acc[i][0] * inv, acc[i][1] * inv);
+    }
+}
+
 // split-fp16 operand row m: fp16(v) in row m, fp16(v - fp16(v)) in row lo + m
 __device__ __forceinline__ void split_store(__half* xb, int ld, int m, int col, float v, int lo = 24) {
     const __half hi = __float2half_rn(v);
@@ -897,12 +1018,15 @@ void launch_attn_rows_cache(const float* qkv, int M, int q_heads, int kv_heads, 
                             const float* k_cache, const float* v_cache, int cap, float scale,
                             float* out, cudaStream_t s, bool pdl) {
     if (past + M > cap) throw std::invalid_argument("prefill attention: rows beyond the cache capacity");
-    const size_t smem = static_cast<size_t>(d + past + M) * sizeof(float);
-    if (smem > 200 * 1024) throw std::invalid_argument("prefill attention: sequence too long");
+    if (d != 64 || kv_heads <= 0 || q_heads % kv_heads != 0 || q_heads / kv_heads > kPfMaxGroup ||
+        (reinterpret_cast<uintptr_t>(k_cache) & 15) || (reinterpret_cast<uintptr_t>(v_cache) & 15))
+        throw std::invalid_argument("prefill attention: head_dim 64, at most 16 query heads per KV head");
+    const int G = q_heads / kv_heads;
+    const int rb = std::max(1, kPfVectors / G);  // query rows per CTA
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = make_cfg(dim3(q_heads, M), dim3(128), smem, s, pdl, attr);
-    check_launch(cudaLaunchKernelEx(&cfg, attn_rows_kernel<0>, qkv, q_heads, kv_heads, d, past, 0, k_cache,
-                                    v_cache, cap, scale, out, static_cast<StreamCtl*>(nullptr)));
+    cudaLaunchConfig_t cfg = make_cfg(dim3(kv_heads, (M + rb - 1) / rb), dim3(kPfThreads), 0, s, pdl, attr);
+    check_launch(cudaLaunchKernelEx(&cfg, attn_prefill_kernel, qkv, M, q_heads, kv_heads, past, k_cache, v_cache, cap,
+                                    scale, out, rb));
 }
 
 void launch_dit_attention(const float* qkv, int nseq, int seq, int q_heads, int kv_heads, int d,
