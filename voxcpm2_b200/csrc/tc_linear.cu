@@ -14,16 +14,17 @@
 // A * (hi + lo) reproduces the fp32 activations to ~2^-22 and the result keeps
 // fp32-level accuracy; the extra N costs nothing at this arithmetic
 // intensity). Accumulators live in TMEM (48 fp32 columns). K is split across
-// the CTAs of a thread-block cluster; the partial tiles are reduced through
-// distributed shared memory in a fixed order (deterministic), then the
-// epilogue (plain store, residual add, or SiLU(gate) * up written straight
-// into the next layer's split-fp16 B operand) runs on the reducing CTA.
+// the CTAs of a thread-block cluster: each CTA sends the partial rows another CTA
+// owns into that CTA's shared memory as asynchronous stores counted on its
+// mbarrier, the owner sums the partials in a fixed order (deterministic), then
+// the epilogue (plain store, residual add, or SiLU(gate) * up written straight
+// into the next layer's split-fp16 B operand) runs on the owning CTA.
 //
 // Roles: thread 0 issues TMA (weights before griddepcontrol.wait, so weight
 // streaming overlaps the previous kernel), thread 32 issues tcgen05.mma, all
 // four warps drain TMEM. Every mbarrier wait gives up after one second of
 // %globaltimer time; the failure path is written to record error 3 in the
-// stream control block, pass every cluster barrier and free its TMEM, but it
+// stream control block, keep to its cluster barriers and free its TMEM, but it
 // has not been exercised on a GPU (no injected failure runs there). The TMEM
 // allocation itself has no time bound: it relies on the kernels' shared-memory
 // sizes keeping every co-resident mix within the SM's 512 columns.

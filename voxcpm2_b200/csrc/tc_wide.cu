@@ -10,12 +10,13 @@
 // with two TMA copies of one lo-row box; both accumulate into the same lo fp32
 // TMEM columns (two N = lo MMAs per K step), so the accumulator already holds
 // W (x_hi + x_lo). K is split across a thread-block cluster of 1, 2, 4 or 8 CTAs:
-// after the MMAs each CTA pushes its partials, token-major, to the CTA that owns
-// those output features (a warp's store is one contiguous run in the owner's
-// shared memory), one cluster barrier, then the owner sums the partials in rank
-// order and writes the epilogue: plain, residual (y += rscale * v), or
-// SiLU(gate) * up into the next linear's split operand (residual half at row
-// offset lo). The accumulator is read from TMEM 32 token columns at a time.
+// after the MMAs each CTA sends its partial rows, one contiguous token run per
+// output feature, to the CTA that owns those features as 16-byte asynchronous
+// stores counted on the owner's mbarrier; the owner waits for its bytes, sums the
+// partials in rank order and writes the epilogue: plain, residual
+// (y += rscale * v), or SiLU(gate) * up into the next linear's split operand
+// (residual half at row offset lo). The accumulator is read from TMEM 32 token
+// columns at a time.
 //
 // TMEM: 128 columns for lo <= 128, else 256. Shared memory never drops below
 // tmem_smem_floor of that count (and kFloor), so the SM's 512 TMEM columns are
