@@ -177,78 +177,6 @@ __global__ void qkv_rows_post_kernel(float* qkv, int q_heads, int kv_heads, int 
     }
 }
 
-// One CTA per (head, query row): scores in shared memory, two-pass softmax, P.V.
-// SRC 0: prefill rows over the KV cache, keys [0, past + m] (the causal -1e4
-// mask of make_decoder_mask removes later keys exactly: exp underflows to 0).
-// SRC 1: DiT rows over the qkv rows of the same 'seq'-row sequence, no mask.
-template <int SRC>
-__global__ void attn_rows_kernel(const float* qkv, int q_heads, int kv_heads, int d, int past,
-                                 int seq, const float* k_cache, const float* v_cache, int cap,
-                                 float scale, float* out, StreamCtl* ctl) {
-    extern __shared__ float sm[];
-    __shared__ float red[32];
-    pdl_launch_dependents();
-    pdl_wait();
-    if (SRC == 1 && ctl && ctl->stopped) return;
-    const int hh = blockIdx.x, m = blockIdx.y;
-    const int G = q_heads / kv_heads, kvh = hh / G;
-    const int width = (q_heads + 2 * kv_heads) * d;
-    float* qs = sm;       // [d]
-    float* sc = sm + d;   // [T]
-    for (int e = threadIdx.x; e < d; e += blockDim.x) qs[e] = qkv[static_cast<size_t>(m) * width + hh * d + e] * scale;
-    __syncthreads();
-    int T, key0;
-    if (SRC == 0) {
-        T = past + m + 1;
-        key0 = 0;
-    } else {
-        T = seq;
-        key0 = (m / seq) * seq;
-    }
-    for (int t = threadIdx.x; t < T; t += blockDim.x) {
-        float s = 0.f;
-        if (SRC == 0) {
-            const float* kp = k_cache + (static_cast<size_t>(kvh) * cap + t) * d;
-            for (int e = 0; e < d; ++e) s = fmaf(qs[e], kp[e], s);
-        } else {
-            const float* kp = qkv + static_cast<size_t>(key0 + t) * width + q_heads * d + kvh * d;
-            for (int e = 0; e < d; ++e) s = fmaf(qs[e], kp[e], s);
-        }
-        sc[t] = s;
-    }
-    __syncthreads();
-    float mx = -FLT_MAX;
-    for (int t = threadIdx.x; t < T; t += blockDim.x) mx = fmaxf(mx, sc[t]);
-    mx = warp_max(mx);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
-    __syncthreads();
-    mx = -FLT_MAX;
-    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) mx = fmaxf(mx, red[w]);
-    __syncthreads();
-    float l = 0.f;
-    for (int t = threadIdx.x; t < T; t += blockDim.x) {
-        const float p = __expf(sc[t] - mx);
-        sc[t] = p;
-        l += p;
-    }
-    l = warp_sum(l);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = l;
-    __syncthreads();
-    l = 0.f;
-    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) l += red[w];
-    const float inv = 1.f / l;
-    for (int e = threadIdx.x; e < d; e += blockDim.x) {
-        float acc = 0.f;
-        if (SRC == 0) {
-            const float* vp = v_cache + static_cast<size_t>(kvh) * cap * d + e;
-            for (int t = 0; t < T; ++t) acc = fmaf(sc[t], vp[static_cast<size_t>(t) * d], acc);
-        } else {
-            const float* vp = qkv + static_cast<size_t>(key0) * width + (q_heads + kv_heads) * d + kvh * d + e;
-            for (int t = 0; t < T; ++t) acc = fmaf(sc[t], vp[static_cast<size_t>(t) * width], acc);
-        }
-        out[static_cast<size_t>(m) * q_heads * d + hh * d + e] = acc * inv;
-    }
-}
 
 // Prefill attention over the cached keys (the rows' own K/V already appended by
 // qkv_rows_post): query row m sees keys 0 .. past + m (causal, kvcache.cpp:216-230).
@@ -974,7 +902,6 @@ __global__ void concat_kv_kernel(const float* past, const float* cur, int past_l
 
 void init_batched_attributes() {
     constexpr int kMax = 200 * 1024;
-    check_launch(cudaFuncSetAttribute(attn_rows_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax));
     check_launch(cudaFuncSetAttribute(dit_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax));
     check_launch(cudaFuncSetAttribute(dit_embed_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax));
     check_launch(cudaFuncSetAttribute(sdpa_rows_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax));
@@ -1029,15 +956,6 @@ void launch_attn_rows_cache(const float* qkv, int M, int q_heads, int kv_heads, 
                                     scale, out, rb));
 }
 
-void launch_dit_attention(const float* qkv, int nseq, int seq, int q_heads, int kv_heads, int d,
-                          float scale, float* out, StreamCtl* ctl, cudaStream_t s, bool pdl) {
-    const size_t smem = static_cast<size_t>(d + seq) * sizeof(float);
-    cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = make_cfg(dim3(q_heads, nseq * seq), dim3(64), smem, s, pdl, attr);
-    check_launch(cudaLaunchKernelEx(&cfg, attn_rows_kernel<1>, qkv, q_heads, kv_heads, d, 0, seq,
-                                    static_cast<const float*>(nullptr), static_cast<const float*>(nullptr), 0,
-                                    scale, out, ctl));
-}
 
 void launch_rmsnorm_rows_split(const float* x, int ldx, const __half* g, float eps, int K, int M, __half* xb,
                                StreamCtl* ctl, cudaStream_t s, bool pdl, int lo) {

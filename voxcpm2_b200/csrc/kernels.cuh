@@ -175,10 +175,6 @@ void launch_attn_rows_cache(const float* qkv, int M, int q_heads, int kv_heads, 
                             const float* k_cache, const float* v_cache, int cap, float scale,
                             float* out, cudaStream_t s, bool pdl);
 
-// DiT: full (non-causal, unmasked) attention within each sequence of 'seq'
-// rows of an already-rotated qkv buffer [nseq*seq][(hq+2hkv)d].
-void launch_dit_attention(const float* qkv, int nseq, int seq, int q_heads, int kv_heads, int d,
-                          float scale, float* out, StreamCtl* ctl, cudaStream_t s, bool pdl);
 
 // DiT, tensor-core operand producers. Both write the next tcgen05 linear's B
 // operand: split fp16 rows [48][ld] (row m = fp16(v), row 24 + m = fp16(v - fp16(v))).
