@@ -181,11 +181,11 @@ __global__ void qkv_rows_post_kernel(float* qkv, int q_heads, int kv_heads, int 
 // Prefill attention over the cached keys (the rows' own K/V already appended by
 // qkv_rows_post): query row m sees keys 0 .. past + m (causal, kvcache.cpp:216-230).
 // One CTA per (KV head, block of rb query rows): its rb x G query vectors (at most
-// 32) spread over 8 warps. Keys are walked in 32-key tiles staged by cp.async into
+// 16) spread over 8 warps. Keys are walked in 32-key tiles staged by cp.async into
 // two buffers; lane j holds key j's row in registers and scores it against each of
 // its warp's vectors; each vector keeps an online softmax (running max and sum) and
 // two output columns per lane, the probabilities broadcast by shuffles.
-constexpr int kPfThreads = 256, kPfWarps = 8, kPfVectors = 32, kPfPer = kPfVectors / kPfWarps, kPfMaxGroup = 16;
+constexpr int kPfThreads = 256, kPfWarps = 8, kPfVectors = 16, kPfPer = kPfVectors / kPfWarps, kPfMaxGroup = 16;
 constexpr int kPfKeys = 32, kPfKRow = 68;
 
 __device__ __forceinline__ void pf_cp_async16(void* smem_dst, const void* gsrc) {
