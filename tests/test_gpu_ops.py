@@ -338,9 +338,15 @@ def test_small_graphs(rt, models, name):
 # ---------------------------------------------------------------------- DiT ---
 @pytest.mark.parametrize("name", ["tiny", "bench"])
 @pytest.mark.parametrize("generic", [False, True])
-def test_dit_estimator(rt, models, name, generic):
+@pytest.mark.parametrize("plan", ["throughput", "latency"])
+def test_dit_estimator(rt, models, name, generic, plan):
+    """One estimator evaluation against the oracle. The latency plan gives the bench
+    model's down projection a 16-CTA K split, so its residual epilogue leaves 128
+    sums-of-squares parts for the next layer's q/k/v row scale."""
     cfg, blobs, dev, orc = models(name)
     s = rt.Stream(dev, kv_capacity=16)
+    if plan == "latency":
+        s.set_plan(rt.PLAN_LATENCY)
     rng = np.random.default_rng(21)
     x = rng.standard_normal((2, cfg.latent), dtype=np.float32)
     cond = rng.standard_normal((2, cfg.latent), dtype=np.float32)

@@ -619,19 +619,25 @@ void enqueue_decoder_step(vxc_stream* s, int which, float* out, float* out2, int
 // K split (cluster size) of a tensor-core linear: about 'target' CTAs per launch
 // (one per SM for a single stream; fewer when many streams share the GPU, which
 // saves each CTA's fixed setup and split-K exchange).
-int choose_splits(int tiles, int k, int target = 148) {
+int choose_splits(int tiles, int k, int target = 148, int most = 8) {
     const int chunks = k / 64;
     const int want = std::max(1, (target + tiles / 2) / tiles);
-    return std::max(1, std::min({8, chunks, want}));
+    return std::max(1, std::min({most, chunks, want}));
 }
 
-// The tensor-core kernels split K over 1, 2, 4 or 8 CTAs.
-int pow2_floor(int v) { return v >= 8 ? 8 : v >= 4 ? 4 : v >= 2 ? 2 : 1; }
+// The tensor-core kernels split K over 1, 2, 4, 8 or 16 CTAs.
+int pow2_floor(int v) { return v >= 16 ? 16 : v >= 8 ? 8 : v >= 4 ? 4 : v >= 2 ? 2 : 1; }
 
 // K split and ring depth of one tensor-core launch: about tc_target CTAs per launch.
-TcLinearArgs tc_plan(const vxc_stream* s, int tiles, int K) {
+// 'most' caps the split: 16 for the down projection only (K = 4096). There a 16-CTA
+// cluster gives the latency plan 128 CTAs of 4 weight chunks each instead of 64 CTAs
+// of 8, so a 3-stage ring refills once after the dependency wait instead of five
+// times (one estimator evaluation 364 -> 339 us on B200). The o projection (K = 1024)
+// measured slower at 16 (one chunk per CTA: the exchange outweighs the bytes); q/k/v
+// and gate/up keep 8.
+TcLinearArgs tc_plan(const vxc_stream* s, int tiles, int K, int most) {
     TcLinearArgs a;
-    a.splits = pow2_floor(choose_splits(tiles, K, s->tc_target));
+    a.splits = pow2_floor(choose_splits(tiles, K, s->tc_target, most));
     a.max_stages = s->tc_stages;
     a.recv_shared = s->recv_shared ? 1 : 0;
     return a;
@@ -656,7 +662,7 @@ void enqueue_dit_layers(vxc_stream* s, StreamCtl* ctl) {
     for (size_t l = 0; l < dev->dit.size(); ++l) {
         const LayerW& L = dev->dit[l];
         const std::array<CUtensorMap, 4>& maps = dev->dit_maps[l];
-        TcLinearArgs qa = tc_plan(s, W / 128, Hd);
+        TcLinearArgs qa = tc_plan(s, W / 128, Hd, 8);
         qa.K = Hd;
         qa.M = M;
         qa.rows = W;
@@ -672,7 +678,7 @@ void enqueue_dit_layers(vxc_stream* s, StreamCtl* ctl) {
             qa.eps = d.rms_eps;
         }
         launch_tc_linear(maps[0], s->map_xb_n, qa, s->cs, s->pdl);
-        TcLinearArgs oa = tc_plan(s, Hd / 128, hq * hd);
+        TcLinearArgs oa = tc_plan(s, Hd / 128, hq * hd, 8);
         oa.K = hq * hd;
         oa.M = M;
         oa.rows = Hd;
@@ -692,7 +698,7 @@ void enqueue_dit_layers(vxc_stream* s, StreamCtl* ctl) {
         }
         launch_tc_linear(maps[1], s->map_xb_a, oa, s->cs, s->pdl);
         const int o_parts = (Hd / 128) * oa.splits;
-        TcLinearArgs ga = tc_plan(s, F / 64, Hd);
+        TcLinearArgs ga = tc_plan(s, F / 64, Hd, 8);
         ga.K = Hd;
         ga.M = M;
         ga.rows = F;
@@ -709,7 +715,7 @@ void enqueue_dit_layers(vxc_stream* s, StreamCtl* ctl) {
             ga.eps = d.rms_eps;
         }
         launch_tc_linear(maps[2], s->map_xb_n, ga, s->cs, s->pdl);
-        TcLinearArgs da = tc_plan(s, Hd / 128, F);
+        TcLinearArgs da = tc_plan(s, Hd / 128, F, 16);
         da.K = F;
         da.M = M;
         da.rows = Hd;
@@ -1895,8 +1901,8 @@ VXC_API int32_t vxc_stream_create(vxc_device* dev, int32_t kv_capacity, vxc_stre
             if (s->tc_stages < 1 || s->tc_stages > 8) throw std::invalid_argument("VXC_TC_STAGES must be in [1, 8]");
         }
         // row sums of squares of dh, by slice: the embedding's Hd / 32 parts or a residual
-        // epilogue's (Hd / 128 tiles) x (K split <= 8) parts
-        const size_t ssq_n = static_cast<size_t>(Hd / 16 + Hd / 32 + 1) * kSsqStride;
+        // epilogue's (Hd / 128 tiles) x (K split <= 16) parts
+        const size_t ssq_n = static_cast<size_t>(Hd / 8 + Hd / 32 + 1) * kSsqStride;
         s->dssq = dev_alloc<float>(ssq_n);
         ck(cudaMemset(s->dssq, 0, ssq_n * sizeof(float)), "cudaMemset");
         for (__half** xb : {&s->xb_n, &s->xb_a, &s->xb_act}) {
@@ -2673,7 +2679,7 @@ std::vector<std::function<void(bool)>> profile_launches(vxc_stream* s, int kerne
     for (size_t l = 0; l < nl; ++l) {
         switch (kernel) {
             case VXC_PROF_DIT_GATEUP: {
-                TcLinearArgs a = tc_plan(s, Fd / 64, Hd);
+                TcLinearArgs a = tc_plan(s, Fd / 64, Hd, 8);
                 a.K = Hd; a.M = M; a.rows = Fd; a.gateup = 1;
                 a.yb = s->xb_act; a.ldyb = Fd; a.ctl = s->ctl;
                 bytes = 2.0 * 2 * Fd * Hd + 2.0 * 48 * Hd + 2.0 * 48 * Fd;
@@ -2682,7 +2688,7 @@ std::vector<std::function<void(bool)>> profile_launches(vxc_stream* s, int kerne
                 break;
             }
             case VXC_PROF_DIT_DOWN: {
-                TcLinearArgs a = tc_plan(s, Hd / 128, Fd);
+                TcLinearArgs a = tc_plan(s, Hd / 128, Fd, 16);
                 a.K = Fd; a.M = M; a.rows = Hd; a.resid = 1;
                 a.y = s->dxn; a.ldy = Hd; a.ctl = s->ctl;
                 bytes = 2.0 * Hd * Fd + 2.0 * 48 * Fd + 8.0 * M * Hd;
@@ -2691,7 +2697,7 @@ std::vector<std::function<void(bool)>> profile_launches(vxc_stream* s, int kerne
                 break;
             }
             case VXC_PROF_DIT_QKV: {
-                TcLinearArgs a = tc_plan(s, Wd / 128, Hd);
+                TcLinearArgs a = tc_plan(s, Wd / 128, Hd, 8);
                 a.K = Hd; a.M = M; a.rows = Wd;
                 a.y = s->dqkv; a.ldy = Wd; a.ctl = s->ctl;
                 bytes = 2.0 * Wd * Hd + 2.0 * 48 * Hd + 4.0 * M * Wd;
@@ -2700,7 +2706,7 @@ std::vector<std::function<void(bool)>> profile_launches(vxc_stream* s, int kerne
                 break;
             }
             case VXC_PROF_DIT_O: {
-                TcLinearArgs a = tc_plan(s, Hd / 128, dq * 64);
+                TcLinearArgs a = tc_plan(s, Hd / 128, dq * 64, 8);
                 a.K = dq * 64; a.M = M; a.rows = Hd; a.resid = 1;
                 a.y = s->dxn; a.ldy = Hd; a.ctl = s->ctl;
                 bytes = 2.0 * Hd * dq * 64 + 2.0 * 48 * dq * 64 + 8.0 * M * Hd;

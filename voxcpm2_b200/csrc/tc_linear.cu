@@ -50,7 +50,7 @@ constexpr int kMaxStages = 8;
 // conflicts on the owner's reads instead of eight)
 constexpr int kRecvStride = 28;
 constexpr int kRecvFloats = kTileRows * kRecvStride;
-constexpr int kMaxSsqParts = 64;  // sums-of-squares parts read in one batch (more: a serial loop)
+constexpr int kMaxSsqParts = 128;  // sums-of-squares parts read in one batch (more: a serial loop)
 constexpr int kSqFloats = kTileRows * kLoOffset;    // squares of the updated rows (at most 128 x 24)
 
 // A split launch can receive in its stage area when the area holds the partials and,
@@ -69,7 +69,8 @@ __host__ __device__ constexpr bool recv_in_stage_area(bool b_tma, int splits, bo
     return b_tma && splits == 1 && !ssq_out;
 }
 
-// S: the K split (cluster size, 1, 2, 4 or 8), a template parameter so that the
+// S: the K split (cluster size, 1, 2, 4, 8, or 16 for a non-gate/up linear: a
+// non-portable cluster), a template parameter so that the
 // rank-order sums of the partials unroll and their loads issue together.
 template <int S>
 __global__ void __launch_bounds__(kTcThreads, 1)
@@ -333,33 +334,35 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // the stage area is idle now: squares of updated rows (behind the partials when those share it)
         float* sq = reinterpret_cast<float*>(smem) + (shared ? kRecvFloats : 0);
         if (a.gateup) {
-            constexpr int kBatch = 4;
-            for (int mb = m0; mb < a.M; mb += per * kBatch) {
-                float g[kBatch][S], up[kBatch][S];
+            if constexpr (S <= 8) {  // the host gives gate/up at most an 8-way split
+                constexpr int kBatch = 4;
+                for (int mb = m0; mb < a.M; mb += per * kBatch) {
+                    float g[kBatch][S], up[kBatch][S];
 #pragma unroll
-                for (int j = 0; j < kBatch; ++j) {
-                    const int mc = min(mb + j * per, a.M - 1);
-#pragma unroll
-                    for (int p = 0; p < S; ++p) {
-                        g[j][p] = recv[static_cast<size_t>((p * 2 + 0) * nu + lu) * kRecvStride + mc];
-                        up[j][p] = recv[static_cast<size_t>((p * 2 + 1) * nu + lu) * kRecvStride + mc];
-                    }
-                }
-#pragma unroll
-                for (int j = 0; j < kBatch; ++j) {
-                    const int m = mb + j * per;
-                    if (m < a.M) {
-                        float gs = 0.f, us = 0.f;
+                    for (int j = 0; j < kBatch; ++j) {
+                        const int mc = min(mb + j * per, a.M - 1);
 #pragma unroll
                         for (int p = 0; p < S; ++p) {
-                            gs += g[j][p];
-                            us += up[j][p];
+                            g[j][p] = recv[static_cast<size_t>((p * 2 + 0) * nu + lu) * kRecvStride + mc];
+                            up[j][p] = recv[static_cast<size_t>((p * 2 + 1) * nu + lu) * kRecvStride + mc];
                         }
-                        if (a.row_scale) {
-                            gs *= inv_s[m];
-                            us *= inv_s[m];
+                    }
+#pragma unroll
+                    for (int j = 0; j < kBatch; ++j) {
+                        const int m = mb + j * per;
+                        if (m < a.M) {
+                            float gs = 0.f, us = 0.f;
+#pragma unroll
+                            for (int p = 0; p < S; ++p) {
+                                gs += g[j][p];
+                                us += up[j][p];
+                            }
+                            if (a.row_scale) {
+                                gs *= inv_s[m];
+                                us *= inv_s[m];
+                            }
+                            store_split(a.yb, a.ldyb, m, tile * 64 + col, silu(gs) * us);
                         }
-                        store_split(a.yb, a.ldyb, m, tile * 64 + col, silu(gs) * us);
                     }
                 }
             }
@@ -419,14 +422,16 @@ cudaError_t launch_split(cudaLaunchConfig_t& cfg, const CUtensorMap& map_a, cons
         case 1: return cudaLaunchKernelEx(&cfg, tc_linear_kernel<1>, map_a, map_b, a);
         case 2: return cudaLaunchKernelEx(&cfg, tc_linear_kernel<2>, map_a, map_b, a);
         case 4: return cudaLaunchKernelEx(&cfg, tc_linear_kernel<4>, map_a, map_b, a);
-        default: return cudaLaunchKernelEx(&cfg, tc_linear_kernel<8>, map_a, map_b, a);
+        case 8: return cudaLaunchKernelEx(&cfg, tc_linear_kernel<8>, map_a, map_b, a);
+        default: return cudaLaunchKernelEx(&cfg, tc_linear_kernel<16>, map_a, map_b, a);
     }
 }
 
 // every instantiation (one per K split)
 std::vector<const void*> tc_linear_kernels() {
     return {reinterpret_cast<const void*>(tc_linear_kernel<1>), reinterpret_cast<const void*>(tc_linear_kernel<2>),
-            reinterpret_cast<const void*>(tc_linear_kernel<4>), reinterpret_cast<const void*>(tc_linear_kernel<8>)};
+            reinterpret_cast<const void*>(tc_linear_kernel<4>), reinterpret_cast<const void*>(tc_linear_kernel<8>),
+            reinterpret_cast<const void*>(tc_linear_kernel<16>)};
 }
 
 size_t dyn_limit() {
@@ -447,8 +452,9 @@ void launch_tc_linear(const CUtensorMap& map_a, const CUtensorMap& map_b, const 
                       bool pdl) {
     if (a.K % kKChunk != 0 || a.K <= 0) throw std::invalid_argument("tc_linear: K must be a multiple of 64");
     if (a.M <= 0 || a.M > kLoOffset) throw std::invalid_argument("tc_linear: at most 24 token rows");
-    if ((a.splits != 1 && a.splits != 2 && a.splits != 4 && a.splits != 8) || a.splits > a.K / kKChunk)
-        throw std::invalid_argument("tc_linear: splits must be 1, 2, 4 or 8 and at most K / 64");
+    if ((a.splits != 1 && a.splits != 2 && a.splits != 4 && a.splits != 8 && a.splits != 16) ||
+        a.splits > a.K / kKChunk || (a.gateup && a.splits > 8))
+        throw std::invalid_argument("tc_linear: splits must be 1, 2, 4, 8 or 16 (gate/up: at most 8) and at most K / 64");
     const int n_tiles = a.gateup ? a.rows / 64 : a.rows / kTileRows;
     if ((a.gateup ? a.rows % 64 : a.rows % kTileRows) != 0) throw std::invalid_argument("tc_linear: rows");
     if (a.ssq_out && (a.gateup || a.M > kSsqStride)) throw std::invalid_argument("tc_linear: bad ssq_out");
@@ -485,6 +491,10 @@ void init_tc_attributes() {
                                                    static_cast<int>(dyn_limit()));
         if (e != cudaSuccess) throw std::runtime_error(std::string("tc_linear attribute: ") + cudaGetErrorString(e));
     }
+    // the 16-way K split is a cluster of 16 CTAs, beyond the portable 8
+    const cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(tc_linear_kernel<16>),
+                                               cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) throw std::runtime_error(std::string("tc_linear cluster attribute: ") + cudaGetErrorString(e));
 }
 
 // ------------------------------------------------------------ tensor maps ---
