@@ -322,7 +322,8 @@ struct TcLinearArgs {
 };
 constexpr int kSsqStride = 24;  // floats per part in a sums-of-squares buffer
 CUtensorMap make_tensor_map_f16(const void* base, int rows, int cols, int box_rows);
-size_t tc_linear_smem_bytes(int K, int splits, int max_stages = 8, bool ssq_out = false, bool recv_shared = false);
+size_t tc_linear_smem_bytes(int K, int splits, int max_stages = 8, bool ssq_out = false, bool recv_shared = false,
+                            int row_scale_parts = 0);
 void launch_tc_linear(const CUtensorMap& map_a, const CUtensorMap& map_b, const TcLinearArgs& a, cudaStream_t s,
                       bool pdl);
 void init_tc_attributes();

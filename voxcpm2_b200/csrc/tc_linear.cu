@@ -51,6 +51,17 @@ constexpr int kMaxStages = 8;
 constexpr int kRecvStride = 28;
 constexpr int kRecvFloats = kTileRows * kRecvStride;
 constexpr int kMaxSsqParts = 128;  // sums-of-squares parts read in one batch (more: a serial loop)
+// parts held in static shared memory; a launch reading more (a 16-way split producer)
+// gets them behind its dynamic area, so the common launch keeps its smaller footprint
+// (static shared memory counts against every CTA's residency)
+constexpr int kStaticSsqParts = 64;
+
+// Dynamic shared memory behind the stage area and the receive buffer for the row
+// scale's parts, when there are more than kStaticSsqParts (at most kMaxSsqParts).
+__host__ __device__ constexpr size_t ssq_tail_bytes(int row_scale, int parts) {
+    return row_scale && parts > kStaticSsqParts && parts <= kMaxSsqParts
+               ? static_cast<size_t>(parts) * kSsqStride * sizeof(float) : 0;
+}
 constexpr int kSqFloats = kTileRows * kLoOffset;    // squares of the updated rows (at most 128 x 24)
 
 // A split launch can receive in its stage area when the area holds the partials and,
@@ -82,7 +93,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __shared__ uint32_t tmem_base_s;
     __shared__ int failed_s;
     __shared__ float inv_s[kLoOffset];
-    __shared__ __align__(16) float ssq_s[kMaxSsqParts * kSsqStride];
+    __shared__ __align__(16) float ssq_static[kStaticSsqParts * kSsqStride];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int split = blockIdx.x, tile = blockIdx.y;
@@ -226,6 +237,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // shared memory; lane m of warp 2 then sums row m's parts in order.
     if (a.row_scale && warp >= 2) {
         if (a.ssq_parts <= kMaxSsqParts) {
+            float* ssq_s = ssq_static;
+            if (a.ssq_parts > kStaticSsqParts) {  // behind the stage area and the receive buffer
+                const bool rin = recv_in_stage_area(b_tma, S, a.ssq_out != nullptr) ||
+                                 shared_recv_fits(b_tma, S, a.recv_shared, static_cast<size_t>(stage_area) * kStageBytes);
+                ssq_s = reinterpret_cast<float*>(smem + static_cast<size_t>(stage_area) * kStageBytes +
+                                                 (rin ? 0 : static_cast<size_t>(kRecvFloats) * sizeof(float)));
+            }
             const int n4 = a.ssq_parts * kSsqStride / 4, t = tid - 64;
             const float4* src = reinterpret_cast<const float4*>(a.ssq_in);
             constexpr int kL = kMaxSsqParts * kSsqStride / 4 / 64;
@@ -405,15 +423,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
 }  // namespace
 
-size_t tc_linear_smem_bytes(int K, int splits, int max_stages, bool ssq_out, bool recv_shared) {
+size_t tc_linear_smem_bytes(int K, int splits, int max_stages, bool ssq_out, bool recv_shared, int row_scale_parts) {
     const int nch = K / kKChunk;
     const int cs = (nch + splits - 1) / splits;
     const int stages = std::min(std::min(max_stages, kMaxStages), std::max(cs, 1));
     const size_t stage_bytes = static_cast<size_t>(stages) * kStageBytes;
+    const size_t tail = ssq_tail_bytes(row_scale_parts > 0, row_scale_parts);
     if (recv_in_stage_area(true, splits, ssq_out) || shared_recv_fits(true, splits, recv_shared, stage_bytes))
-        return stage_bytes + 1024;  // + alignment slack
+        return stage_bytes + tail + 1024;  // + alignment slack
     const size_t recv_bytes = static_cast<size_t>(kRecvFloats) * sizeof(float);
-    return stage_bytes + recv_bytes + 1024;  // + alignment slack
+    return stage_bytes + recv_bytes + tail + 1024;  // + alignment slack
 }
 
 cudaError_t launch_split(cudaLaunchConfig_t& cfg, const CUtensorMap& map_a, const CUtensorMap& map_b,
@@ -467,7 +486,7 @@ void launch_tc_linear(const CUtensorMap& map_a, const CUtensorMap& map_b, const 
     cfg.blockDim = dim3(kTcThreads);
     if (a.max_stages < 1 || a.max_stages > kMaxStages) throw std::invalid_argument("tc_linear: max_stages in [1, 8]");
     cfg.dynamicSmemBytes = std::max(tc_linear_smem_bytes(a.K, a.splits, a.max_stages, a.ssq_out != nullptr,
-                                                         a.recv_shared != 0),
+                                                         a.recv_shared != 0, a.row_scale ? a.ssq_parts : 0),
                                     tmem_smem_floor(kTmemCols));
     if (cfg.dynamicSmemBytes > dyn_limit()) throw std::invalid_argument("tc_linear: shared memory over 227 KB");
     cfg.stream = s;
