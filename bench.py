@@ -46,10 +46,11 @@ def parse():
     p.add_argument("--group-members", type=int, default=4, help="streams per group (1..8)")
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--cpu-sample-patches", type=int, default=6)
-    p.add_argument("--range", choices=["stream", "group", "sdpa"], default=None,
-                   help="run a small case and exit, for ncu: 'stream' = 3 patches of one lone stream, 'group' = 3 "
-                        "patches of one stream group (--group-members), 'sdpa' = 8 calls of the VoxCPM2SDPA op at "
-                        "config 1's shape (q [16][1][64], K/V [2][511 + 1][64])")
+    p.add_argument("--range", choices=["stream", "stream-latency", "group", "sdpa"], default=None,
+                   help="run a small case and exit, for ncu: 'stream' = 3 patches of one lone stream, "
+                        "'stream-latency' = the same with VXC_PLAN_LATENCY, 'group' = 3 patches of one stream group "
+                        "(--group-members), 'sdpa' = 8 calls of the VoxCPM2SDPA op at config 1's shape (q [16][1][64], "
+                        "K/V [2][511 + 1][64])")
     return p.parse_args()
 
 
@@ -894,12 +895,14 @@ def run_range(args):
         g.close()
     else:
         st = rt.Stream(dev, kv_capacity=512)
+        if args.range == "stream-latency":
+            st.set_plan(rt.PLAN_LATENCY)
         st.prefill(synthetic.token_ids(BENCH, TEXT_TOKENS, seed=13))
         st.upload_noise(synthetic.normal((4, BENCH.latent), seed=14))
         for _ in range(3):
             st.patch_step_async(MIN_PATCHES, CFG, TIMESTEPS)
         st.synchronize()
-        print(json.dumps({"range": "stream", "kernels_per_patch": st.state().graph_kernels}))
+        print(json.dumps({"range": args.range, "kernels_per_patch": st.state().graph_kernels}))
         st.close()
     dev.close()
     return 0
