@@ -157,8 +157,9 @@ VXC_API void vxc_stream_destroy(vxc_stream* s);
 /* How a stream's estimator linears spread over the GPU (no counterpart in the
  * reference, which runs the estimator on the CPU). VXC_PLAN_THROUGHPUT, the default:
  * ~32 CTAs and a 2-stage shared-memory ring per tcgen05 linear, the highest rate when
- * many streams share the GPU. VXC_PLAN_LATENCY: ~296 CTAs and a 3-stage ring, the
- * lowest per-patch latency for a stream that runs alone. The plans split the linears'
+ * many streams share the GPU. VXC_PLAN_LATENCY: ~296 CTAs and a 3-stage ring (the
+ * down projection as 16-CTA clusters), the lowest per-patch latency for a stream
+ * that runs alone. The plans split the linears'
  * K range differently, so latents differ in the last bits between them. Takes effect
  * at the next patch (its graph is captured again); INVALID_STATE while a submitted
  * patch has not been collected. */
