@@ -574,8 +574,18 @@ __global__ void __launch_bounds__(kEmbedThreads) dit_embed_kernel(const DitEmbed
         const int kind = o & 1, b = (o >> 1) & 1, p = o >> 2;
         const float* src = (kind == 0 ? xs : cs) + b * DP + p;
         const float* w = wr + kind * D;
-        float acc = 0.f;
-        for (int e = 0; e < D; ++e) acc = fmaf(w[e], src[e * P], acc);  // frame p of a d-major [D][P] patch
+        float acc;
+        if ((D & 3) == 0) {  // four independent chains
+            float c4[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int e = 0; e < D; e += 4) {
+#pragma unroll
+                for (int u = 0; u < 4; ++u) c4[u] = fmaf(w[e + u], src[(e + u) * P], c4[u]);  // frame p of [D][P]
+            }
+            acc = (c4[0] + c4[1]) + (c4[2] + c4[3]);
+        } else {
+            acc = 0.f;
+            for (int e = 0; e < D; ++e) acc = fmaf(w[e], src[e * P], acc);  // frame p of a d-major [D][P] patch
+        }
         const int tok = kind == 0 ? 3 + P + p : 3 + p;
         const float v = live ? acc + __half2float(kind == 0 ? a.in_b[f] : a.cond_b[f]) : 0.f;
         if (live) a.hidden[static_cast<size_t>(b * seq + tok) * a.Hd + f] = v;
@@ -618,10 +628,12 @@ __global__ void timestep_embedding_kernel(const float* t_rows, float t_val, int 
 }
 
 // final norm of the x rows, out_proj, then CFG-zero* and the Euler step
-// (synthesizer.cpp:147-161). Each CTA normalises the 2P x rows into shared
-// memory and computes kOutFeatures output features of both CFG rows; the last
-// CTA to arrive reads the whole [2][D*P] estimate back and runs the CFG-zero*
-// scale (double, fixed summation order) and the Euler update.
+// (synthesizer.cpp:147-161). Each CTA computes kOutFeatures output features of
+// both CFG rows: warp r normalises x row r in registers and dots it with the CTA's
+// out_proj rows (staged in shared memory before the dependency wait), 16
+// independent accumulators per lane; the last CTA to arrive reads the whole
+// [2][D*P] estimate back and runs the CFG-zero* scale (double, fixed summation
+// order) and the Euler update.
 constexpr int kOutFeatures = 4;
 constexpr int kOutThreads = 256;
 
@@ -678,13 +690,15 @@ __global__ void __launch_bounds__(kOutThreads) dit_out_kernel(const DitOutArgs a
             wsm[i] = e0 + el < a.D ? __half2float(a.out_w[static_cast<size_t>(e0 + el) * a.Hd + k]) : 0.f;
         }
     }
+    __syncthreads();  // this CTA's out_proj rows are staged (before the dependency wait)
     pdl_wait();
     const bool stop = a.ctl && a.ctl->stopped;  // read beside the rows; nothing is written before the check
-    // warp r normalises row r (the row read once, as float4, into registers)
-    for (int r = warp; r < R; r += nw) {
-        const int b = r / a.P, p = r - b * a.P;
-        const float* h = a.hidden + (static_cast<size_t>(b) * a.seq + 3 + a.P + p) * a.Hd;
-        if (vec) {
+    if (vec && R <= nw) {
+        // warp r: row r normalised in registers, then its dot products with this CTA's
+        // kOutFeatures out_proj rows, 16 independent accumulators per lane
+        if (warp < R && !stop) {
+            const int r = warp, b = r / a.P, p = r - b * a.P;
+            const float* h = a.hidden + (static_cast<size_t>(b) * a.seq + 3 + a.P + p) * a.Hd;
             constexpr int kR = 1024 / 4 / 32;  // float4 per lane, Hd <= 1024
             const int n4 = a.Hd / 4;
             float4 hv[kR];
@@ -700,35 +714,85 @@ __global__ void __launch_bounds__(kOutThreads) dit_out_kernel(const DitOutArgs a
             for (int j = 0; j < kR; ++j) ss += hv[j].x * hv[j].x + hv[j].y * hv[j].y + hv[j].z * hv[j].z + hv[j].w * hv[j].w;
             ss = warp_sum(ss);
             const float inv = rsqrtf(ss / static_cast<float>(a.Hd) + a.eps);
+            float4 acc[kOutFeatures];
+#pragma unroll
+            for (int el = 0; el < kOutFeatures; ++el) acc[el] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
             for (int j = 0; j < kR; ++j) {
                 const int i = lane + j * 32;
                 if (i >= n4) continue;
                 const float2 g01 = __half22float2(*reinterpret_cast<const __half2*>(&gv[j].x));
                 const float2 g23 = __half22float2(*reinterpret_cast<const __half2*>(&gv[j].y));
-                reinterpret_cast<float4*>(xn + r * a.Hd)[i] =
-                    make_float4(hv[j].x * inv * g01.x, hv[j].y * inv * g01.y, hv[j].z * inv * g23.x, hv[j].w * inv * g23.y);
+                const float4 xv = make_float4(hv[j].x * inv * g01.x, hv[j].y * inv * g01.y, hv[j].z * inv * g23.x,
+                                              hv[j].w * inv * g23.y);
+#pragma unroll
+                for (int el = 0; el < kOutFeatures; ++el) {
+                    const float4 w4 = reinterpret_cast<const float4*>(wsm + el * a.Hd)[i];
+                    acc[el].x = fmaf(w4.x, xv.x, acc[el].x);
+                    acc[el].y = fmaf(w4.y, xv.y, acc[el].y);
+                    acc[el].z = fmaf(w4.z, xv.z, acc[el].z);
+                    acc[el].w = fmaf(w4.w, xv.w, acc[el].w);
+                }
             }
-        } else {
-            float ss = 0.f;
-            for (int k = lane; k < a.Hd; k += 32) ss = fmaf(h[k], h[k], ss);
-            ss = warp_sum(ss);
-            const float inv = rsqrtf(ss / static_cast<float>(a.Hd) + a.eps);
-            for (int k = lane; k < a.Hd; k += 32) xn[r * a.Hd + k] = h[k] * inv * __half2float(a.norm_g[k]);
+#pragma unroll
+            for (int el = 0; el < kOutFeatures; ++el) {
+                const float t = warp_sum((acc[el].x + acc[el].y) + (acc[el].z + acc[el].w));
+                const int e = e0 + el;
+                if (lane == 0 && e < a.D) a.est_buf[b * L + e * a.P + p] = t + __half2float(a.out_b[e]);  // [2][D][P]
+            }
         }
-    }
-    if (stop) return;
-    __syncthreads();
-    // (feature, row) pairs: warp w takes pairs w, w + 8, ...
-    for (int q = warp; q < kOutFeatures * R; q += nw) {
-        const int el = q / R, r = q - el * R, e = e0 + el;
-        if (e >= a.D) continue;
-        float acc = 0.f;
-        for (int k = lane; k < a.Hd; k += 32) acc = fmaf(wsm[el * a.Hd + k], xn[r * a.Hd + k], acc);
-        acc = warp_sum(acc);
-        if (lane == 0) {
+        if (stop) return;
+    } else {
+        // warp r normalises row r into shared memory (the row read once, as float4)
+        for (int r = warp; r < R; r += nw) {
             const int b = r / a.P, p = r - b * a.P;
-            a.est_buf[b * L + e * a.P + p] = acc + __half2float(a.out_b[e]);  // [2][D][P]
+            const float* h = a.hidden + (static_cast<size_t>(b) * a.seq + 3 + a.P + p) * a.Hd;
+            if (vec) {
+                constexpr int kR = 1024 / 4 / 32;  // float4 per lane, Hd <= 1024
+                const int n4 = a.Hd / 4;
+                float4 hv[kR];
+                uint2 gv[kR];
+#pragma unroll
+                for (int j = 0; j < kR; ++j) {
+                    const int i = lane + j * 32;
+                    hv[j] = i < n4 ? reinterpret_cast<const float4*>(h)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+                    gv[j] = i < n4 ? reinterpret_cast<const uint2*>(a.norm_g)[i] : make_uint2(0u, 0u);
+                }
+                float ss = 0.f;
+#pragma unroll
+                for (int j = 0; j < kR; ++j) ss += hv[j].x * hv[j].x + hv[j].y * hv[j].y + hv[j].z * hv[j].z + hv[j].w * hv[j].w;
+                ss = warp_sum(ss);
+                const float inv = rsqrtf(ss / static_cast<float>(a.Hd) + a.eps);
+#pragma unroll
+                for (int j = 0; j < kR; ++j) {
+                    const int i = lane + j * 32;
+                    if (i >= n4) continue;
+                    const float2 g01 = __half22float2(*reinterpret_cast<const __half2*>(&gv[j].x));
+                    const float2 g23 = __half22float2(*reinterpret_cast<const __half2*>(&gv[j].y));
+                    reinterpret_cast<float4*>(xn + r * a.Hd)[i] =
+                        make_float4(hv[j].x * inv * g01.x, hv[j].y * inv * g01.y, hv[j].z * inv * g23.x, hv[j].w * inv * g23.y);
+                }
+            } else {
+                float ss = 0.f;
+                for (int k = lane; k < a.Hd; k += 32) ss = fmaf(h[k], h[k], ss);
+                ss = warp_sum(ss);
+                const float inv = rsqrtf(ss / static_cast<float>(a.Hd) + a.eps);
+                for (int k = lane; k < a.Hd; k += 32) xn[r * a.Hd + k] = h[k] * inv * __half2float(a.norm_g[k]);
+            }
+        }
+        if (stop) return;
+        __syncthreads();
+        // (feature, row) pairs: warp w takes pairs w, w + 8, ...
+        for (int q = warp; q < kOutFeatures * R; q += nw) {
+            const int el = q / R, r = q - el * R, e = e0 + el;
+            if (e >= a.D) continue;
+            float acc = 0.f;
+            for (int k = lane; k < a.Hd; k += 32) acc = fmaf(wsm[el * a.Hd + k], xn[r * a.Hd + k], acc);
+            acc = warp_sum(acc);
+            if (lane == 0) {
+                const int b = r / a.P, p = r - b * a.P;
+                a.est_buf[b * L + e * a.P + p] = acc + __half2float(a.out_b[e]);  // [2][D][P]
+            }
         }
     }
     __threadfence();
