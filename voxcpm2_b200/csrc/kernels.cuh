@@ -286,7 +286,7 @@ struct TcLinearArgs {
     int K = 0;           // multiple of 64
     int M = 0;           // token rows (<= 24)
     int rows = 0;        // output features (GATEUP: gate/up pairs)
-    int splits = 1;      // K split = cluster size (<= 8)
+    int splits = 1;      // K split = cluster size (<= 16; gate/up <= 8)
     int gateup = 0;      // tile = 64 gate rows + the matching 64 up rows; out = SiLU(g) * u
     int resid = 0;       // y += rscale * out (else y = out)
     float rscale = 1.0f;
