@@ -300,6 +300,7 @@ struct vxc_device {
     const __half *base_norm = nullptr, *res_norm = nullptr, *dit_norm = nullptr;
     float *dit_rope_cos = nullptr, *dit_rope_sin = nullptr;  // positions 0..seq-1
     float* temb_freq = nullptr;  // the DiT timestep embedding's frequencies [dit_hidden / 2]
+    std::atomic<int> live_groups{0};  // stream groups on this device (sets their wide linears' CTA target)
     // per DiT layer: TMA maps of W_qkv, W_o, W_gate|up, W_down (A operands)
     std::vector<std::array<CUtensorMap, 4>> dit_maps;
     // per decoder layer: TMA maps of W_qkv, W_o, W_gate|up, W_down for the prefill's row-block linears
@@ -1374,8 +1375,10 @@ struct vxc_group {
     int lo = 0;  // the split operands' row block: 22 rows per member rounded up to 16
     __half *xw_n = nullptr, *xw_a = nullptr, *xw_act = nullptr;  // [2 lo][K] split operands
     CUtensorMap map_xw_n{}, map_xw_a{}, map_xw_act{};
-    int tc_target = 32;              // CTAs aimed at per wide linear (VXC_GROUP_TC_TARGET; 32 suits
-                                     // several groups at once, 148 a lone group's latency)
+    int tc_target = 32;              // CTAs aimed at per wide linear: group_tc_target(), or a fixed
+                                     // VXC_GROUP_TC_TARGET
+    bool target_fixed = false;       // VXC_GROUP_TC_TARGET was given
+    int graph_target = -1;           // the target the captured graph was built with
     int tc_stages = 2;               // TMA ring depth of the wide linears (VXC_GROUP_TC_STAGES)
     bool recv_shared = true;         // split wide linears receive in their stage area (VXC_GROUP_RECV_SHARED=0: not)
     bool bulk_gemv = false;          // decoder GEMVs: register-streaming batch form (0, the faster), or
@@ -1645,10 +1648,27 @@ void group_join(vxc_group* g, int k) {
     }
 }
 
+// CTAs per wide linear for a group: 256 over the device's groups, clamped to 16..32.
+// For the benchmark model that splits the o and down projections 4 ways up to 9 groups
+// and 2 ways from 10, so many groups do not crowd each other's CTAs off the SMs and a
+// few keep their latency. Measured per device (patches/s): 12 x 4 streams 2096-2112 at
+// 32 and 2136-2177 at 16 (1881 at 8); 12 x 8 1969 at 32 and 2133-2147 at 16; 8 x 4 1931
+// at 32 and 1883-1892 at 16-24; 4 x 4 1334 at 32 and 1200 at 16.
+int group_tc_target(const vxc_group* g) {
+    if (g->target_fixed) return g->tc_target;
+    const int n = std::max(1, g->dev->live_groups.load());
+    return std::max(16, std::min(32, 256 / n));
+}
+
 void capture_group_graph(vxc_group* g, int T, float cfg) {
     time_table(g->members[0], T);  // the graph reads it; keep it current before every replay
-    if (g->graph && g->graph_T == T && g->graph_cfg == cfg) return;
+    const int target = group_tc_target(g);
+    if (g->graph && g->graph_T == T && g->graph_cfg == cfg && g->graph_target == target) return;
+    g->tc_target = target;
     if (g->graph) {
+        // a patch of the old graph may still run (the target changes when another group
+        // is created or destroyed between this group's asynchronous patches)
+        ck(cudaStreamSynchronize(g->members[0]->cs), "cudaStreamSynchronize");
         cudaGraphExecDestroy(g->graph);
         g->graph = nullptr;
     }
@@ -1692,6 +1712,7 @@ void capture_group_graph(vxc_group* g, int T, float cfg) {
     ck(e, "cudaGraphInstantiate");
     g->graph_T = T;
     g->graph_cfg = cfg;
+    g->graph_target = target;
 }
 
 void free_group(vxc_group* g) {
@@ -2904,6 +2925,7 @@ VXC_API int32_t vxc_group_create(vxc_device* dev, int32_t n_streams, int32_t kv_
         if (const char* tt = std::getenv("VXC_GROUP_TC_TARGET")) {
             grp->tc_target = std::atoi(tt);
             require(grp->tc_target >= 1 && grp->tc_target <= 4096, "VXC_GROUP_TC_TARGET must be in [1, 4096]");
+            grp->target_fixed = true;
         }
         if (const char* bg = std::getenv("VXC_GROUP_BULK_GEMV")) grp->bulk_gemv = std::string(bg) == "1";
         if (const char* rs = std::getenv("VXC_GROUP_RECV_SHARED")) grp->recv_shared = std::string(rs) != "0";
@@ -2945,6 +2967,7 @@ VXC_API int32_t vxc_group_create(vxc_device* dev, int32_t n_streams, int32_t kv_
             for (vxc_stream* s : grp->members) vxc_stream_destroy(s);
             throw;
         }
+        dev->live_groups.fetch_add(1);
         *out = grp.release();
     });
 }
@@ -2957,6 +2980,7 @@ VXC_API void vxc_group_destroy(vxc_group* g) {
         if (!g->members.empty()) cudaStreamSynchronize(g->members[0]->cs);
         free_group(g);
     }
+    g->dev->live_groups.fetch_sub(1);
     for (vxc_stream* s : g->members) vxc_stream_destroy(s);
     delete g;
 }
