@@ -41,7 +41,7 @@ def parse():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--streams", type=int, default=16, help="independent batch-1 streams per GPU")
-    p.add_argument("--groups", type=int, default=12,
+    p.add_argument("--groups", type=int, default=16,
                    help="stream groups per GPU for the group measurement (0 skips it)")
     p.add_argument("--group-members", type=int, default=4, help="streams per group (1..8)")
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
